@@ -1,0 +1,62 @@
+# ugdr-b200 native build: libugdr.so (client API + daemon core + sm_100a executor), the daemon,
+# the smoke client, the native test and benchmark binaries.  `make -j` from the repo root;
+# outputs land in ugdr_b200/_lib/ (in-tree, so they travel with the source tree).
+CUDA_HOME ?= /usr/local/cuda
+NVCC      := $(CUDA_HOME)/bin/nvcc
+CXX       ?= g++
+OUT       := ugdr_b200/_lib
+OBJ       := build/obj
+ARCH      := -gencode arch=compute_100a,code=sm_100a
+
+CPPFLAGS  := -Icsrc -Iinclude -I$(CUDA_HOME)/include
+CXXFLAGS  := -std=c++20 -O2 -g -fPIC -Wall -Wextra -Wno-unused-parameter -pthread
+NVFLAGS   := -std=c++17 $(ARCH) -O3 -lineinfo -Xcompiler -fPIC -Xptxas -v
+LDLIBS    := -L$(CUDA_HOME)/lib64 -lcudart_static -ldl -lrt -lpthread
+
+LIB_CXX := \
+  csrc/common/shm.cpp csrc/queue/ring.cpp csrc/ipc/ipc.cpp \
+  csrc/control/rpc.cpp csrc/control/service.cpp csrc/control/client.cpp \
+  csrc/api/posting.cpp csrc/api/runtime.cpp csrc/api/memory_export.cpp \
+  csrc/engine/cpu_engine.cpp csrc/gpu/cuda_memory.cpp csrc/gpu/gpu_engine.cpp \
+  csrc/daemon/daemon.cpp
+LIB_CU  := csrc/gpu/executor.cu
+
+LIB_OBJS := $(LIB_CXX:csrc/%.cpp=$(OBJ)/%.o) $(LIB_CU:csrc/%.cu=$(OBJ)/%.cu.o)
+TEST_SRCS := $(wildcard tests/native/*.cpp)
+TEST_OBJS := $(TEST_SRCS:tests/native/%.cpp=$(OBJ)/tests/%.o)
+
+all: $(OUT)/libugdr.so $(OUT)/ugdr_daemon $(OUT)/ugdr_client
+
+$(OBJ)/%.o: csrc/%.cpp
+	@mkdir -p $(dir $@)
+	$(CXX) $(CPPFLAGS) $(CXXFLAGS) -MMD -MP -c $< -o $@
+
+$(OBJ)/%.cu.o: csrc/%.cu
+	@mkdir -p $(dir $@)
+	$(NVCC) $(CPPFLAGS) $(NVFLAGS) -MMD -MP -c $< -o $@ 2> $@.ptxas.log || (cat $@.ptxas.log; exit 1)
+
+$(OBJ)/tests/%.o: tests/native/%.cpp
+	@mkdir -p $(dir $@)
+	$(CXX) $(CPPFLAGS) $(CXXFLAGS) -MMD -MP -c $< -o $@
+
+$(OUT)/libugdr.so: $(LIB_OBJS)
+	@mkdir -p $(OUT)
+	$(NVCC) $(ARCH) -shared -o $@ $^ -Xlinker -soname=libugdr.so $(LDLIBS)
+
+$(OUT)/ugdr_daemon: $(OBJ)/daemon/main.o $(OUT)/libugdr.so
+	$(CXX) -o $@ $< -L$(OUT) -lugdr -Wl,-rpath,'$$ORIGIN' -pthread
+
+$(OUT)/ugdr_client: $(OBJ)/apps/client_main.o $(OUT)/libugdr.so
+	$(CXX) -o $@ $< -L$(OUT) -lugdr -Wl,-rpath,'$$ORIGIN' -pthread
+
+$(OUT)/ugdr_perf: $(OBJ)/bench/ugdr_perf.o $(OUT)/libugdr.so
+	$(CXX) -o $@ $< -L$(OUT) -lugdr -Wl,-rpath,'$$ORIGIN' $(LDLIBS)
+
+$(OUT)/ugdr_native_tests: $(TEST_OBJS) $(OUT)/libugdr.so
+	$(CXX) -o $@ $(TEST_OBJS) -L$(OUT) -lugdr -Wl,-rpath,'$$ORIGIN' $(LDLIBS)
+
+clean:
+	rm -rf build/obj $(OUT)/libugdr.so $(OUT)/ugdr_daemon $(OUT)/ugdr_client $(OUT)/ugdr_native_tests $(OUT)/ugdr_perf
+
+-include $(shell find build/obj -name '*.d' 2>/dev/null)
+.PHONY: all clean

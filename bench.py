@@ -1,0 +1,319 @@
+#!/usr/bin/env python
+"""Headline benchmark: all-pairs RDMA WRITE bandwidth through the ugdr verbs API.
+
+Workload (weak-scaled): every GPU holds one 256 MiB bf16 MR (N(0,1),
+seeded by rank) split in eight 32 MiB slots.  One step = every GPU RDMA_WRITEs its own slot
+(slot = rank) to 7 destinations over 7 QPs: WR k of rank r goes to GPU (r + 1 + k) % N into that
+GPU's slot (dst + 1 + k) % 8, which is never the destination's own source slot, so reads and
+writes never overlap.  With N = 8 this is exactly "a 32 MiB slice to each of its 7 peers"; with
+fewer GPUs the same 7 x 32 MiB per GPU cycle over the available peers (N = 1: loopback copies
+inside one GPU).  Per-GPU work is fixed, so scaling is weak.
+
+`value` is device-timed: the daemon launches every GPU's executor together for the K timed steps
+(all WRs of the K steps are queued first), brackets each launch with CUDA events on its
+launching stream, and the step time is the max over GPUs.  `e2e` runs the same steps through the
+public API with the persistent executors: per step each rank posts 7 WRs (the WQEs travel
+host->device from the pinned shared ring) and polls 7 CQEs (device->host).
+
+`--impl reference` runs the reference's own client->daemon benchmark binary, built unmodified
+from the reference sources into baseline/_ref (configure-time flags only), one process per GPU.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+SLOT_MIB = 32
+SLOTS = 8
+PEERS = 7
+BASELINE_GBPS = None  # BASELINE.json publishes no number for this config
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return world, rank, local
+
+
+class Comm:
+    """Host-side coordination between ranks (gloo): barriers, object exchange, max-reduce."""
+
+    def __init__(self, world: int, rank: int):
+        self.world, self.rank = world, rank
+        self.dist = None
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.init_process_group("gloo")
+            self.dist = dist
+
+    def barrier(self):
+        if self.dist:
+            self.dist.barrier()
+
+    def bcast(self, obj):
+        if not self.dist:
+            return obj
+        lst = [obj]
+        self.dist.broadcast_object_list(lst, src=0)
+        return lst[0]
+
+    def gather(self, obj):
+        if not self.dist:
+            return [obj]
+        out = [None] * self.world
+        self.dist.all_gather_object(out, obj)
+        return out
+
+    def max(self, x: float) -> float:
+        return max(self.gather(x))
+
+    def close(self):
+        if self.dist:
+            self.dist.destroy_process_group()
+
+
+def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None:
+    import torch
+
+    from ugdr_b200 import _native as N
+    from ugdr_b200 import verbs as V
+    from ugdr_b200.utils.clocks import ClockSampler
+
+    torch.cuda.set_device(local)
+    daemon = None
+    if rank == 0:
+        daemon = V.Daemon(gpus=world, cpu_device=False)
+        path = daemon.socket_path
+    else:
+        path = None
+    path = comm.bcast(path)
+    os.environ["UGDR_DAEMON_SOCKET"] = path
+
+    slot = SLOT_MIB << 20
+    total = SLOTS * slot
+    K, W = args.steps, args.warmup
+    depth = K + W + 4
+
+    ctx = V.Context(V.find_device(gpu=local))
+    pd = ctx.alloc_pd()
+    cq = ctx.create_cq(2 * PEERS * depth + 64)
+    gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    buf = torch.randn(total // 2, dtype=torch.bfloat16, device="cuda", generator=gen)
+    torch.cuda.synchronize()
+    acc = N.ACCESS_LOCAL_WRITE | N.ACCESS_REMOTE_WRITE
+    mr = pd.reg_mr(buf.data_ptr(), total, acc)
+    req = [pd.create_qp(cq, max_send_wr=depth) for _ in range(PEERS)]
+    rsp = [pd.create_qp(cq, max_send_wr=4) for _ in range(PEERS)]
+    for q in req + rsp:
+        q.to_init(N.ACCESS_REMOTE_WRITE)
+    info = comm.gather({"addr": buf.data_ptr(), "rkey": mr.rkey,
+                        "rsp": [q.qpn for q in rsp], "req": [q.qpn for q in req]})
+    for k in range(PEERS):
+        dst = (rank + 1 + k) % world
+        req[k].connect(info[dst]["rsp"][k])
+        src = (rank - 1 - k) % world
+        rsp[k].connect(info[src]["req"][k])
+    comm.barrier()
+
+    def post_step(step_id: int):
+        for k in range(PEERS):
+            dst = (rank + 1 + k) % world
+            dslot = (dst + 1 + k) % SLOTS
+            req[k].post_write((buf.data_ptr() + (rank % SLOTS) * slot, slot, mr.lkey),
+                              info[dst]["addr"] + dslot * slot, info[dst]["rkey"],
+                              wr_id=(step_id << 8) | k)
+
+    all_ctx = None
+    if rank == 0:
+        all_ctx = [V.Context(V.find_device(gpu=g)) for g in range(world)]
+
+    def drain(steps: int) -> float:
+        ctx.hold(True)
+        comm.barrier()
+        for s in range(steps):
+            post_step(s)
+        comm.barrier()
+        ms = None
+        if rank == 0:
+            ms = max(V.timed_drain(all_ctx, [PEERS * steps] * world, timeout_ms=300000))
+        ms = comm.bcast(ms)
+        wcs = cq.wait(PEERS * steps, timeout=120)
+        bad = [w for w in wcs if w.status != N.WC_SUCCESS]
+        if bad:
+            raise RuntimeError(f"rank {rank}: {len(bad)} failed completions, first {bad[0]}")
+        ctx.hold(False)
+        return ms
+
+    # Warm-up (untimed), then verify one destination slot per inbound WR.
+    drain(W)
+    comm.barrier()
+    torch.cuda.synchronize()
+    ok = True
+    bytes_view = buf.view(torch.uint8)
+    for k in range(PEERS):
+        src = (rank - 1 - k) % world
+        dslot = (rank + 1 + k) % SLOTS
+        g = torch.Generator(device="cuda").manual_seed(1234 + src)
+        ref = torch.randn(total // 2, dtype=torch.bfloat16, device="cuda", generator=g).view(torch.uint8)
+        sslot = src % SLOTS
+        ok &= torch.equal(bytes_view[dslot * slot:(dslot + 1) * slot], ref[sslot * slot:(sslot + 1) * slot])
+        del ref
+    ok = all(comm.gather(bool(ok)))
+
+    # Device-timed region.
+    sampler = ClockSampler(list(range(world))) if rank == 0 else None
+    if sampler:
+        sampler.__enter__()
+    t_ms = drain(K)
+    if sampler:
+        sampler.__exit__(None, None, None)
+    clocks = sampler.summary() if sampler else None
+
+    # End-to-end through the public API (persistent executors).
+    for s in range(W):
+        post_step(s)
+        cq.wait(PEERS, timeout=60)
+    comm.barrier()
+    t0 = time.perf_counter()
+    for s in range(K):
+        post_step(s)
+        wcs = cq.wait(PEERS, timeout=60)
+    t_e2e = time.perf_counter() - t0
+    t_e2e = comm.max(t_e2e)
+
+    step_bytes = world * PEERS * slot
+    value = step_bytes * K / (t_ms / 1e3) / 1e9
+    e2e = step_bytes * K / t_e2e / 1e9
+    stats = ctx.stats()
+    comm.barrier()
+    for q in req + rsp:
+        q.destroy()
+    mr.dereg()
+    cq.destroy()
+    pd.dealloc()
+    ctx.close()
+    if all_ctx:
+        for c in all_ctx:
+            c.close()
+    comm.barrier()
+    if daemon:
+        daemon.stop()
+    if rank != 0:
+        return None
+    wqe_bytes = 64  # one 64-byte send slot per WR (40 B header + 1 SGE, rounded)
+    cqe_bytes = 32
+    return {
+        "metric": "rdma_write_allpairs_aggregate_GBps",
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": K,
+        "warmup": W,
+        "ms_per_step": round(t_ms / K, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None if BASELINE_GBPS is None else round(value / BASELINE_GBPS, 3),
+        "dtype": "bf16",
+        "data": "synthetic: N(0,1) bf16 MR per GPU, seeded by rank; payload verified after warm-up",
+        "config": {
+            "model": "ugdr all-pairs RDMA_WRITE (BASELINE configs[2])",
+            "global_batch": world * PEERS,
+            "seq_len": slot,
+            "parallelism": f"{world} GPU(s) x {PEERS} QPs, 32 MiB per WR",
+            "mr_bytes_per_gpu": total,
+            "l2": "inputs larger than L2: 224 MiB read + 224 MiB written per GPU per step",
+            "timing": "CUDA events around each GPU's executor launch, max over GPUs",
+            "correct": bool(ok),
+        },
+        "clocks": clocks,
+        "e2e": {"value": round(e2e, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": world * PEERS * wqe_bytes,
+                "d2h_bytes_per_step": world * PEERS * cqe_bytes,
+                "path": "ugdr_post_send -> persistent executor -> ugdr_poll_cq, wall clock, max over ranks"},
+        "gpu_launches": world,
+        "executor_launches_rank0": int(stats.launches),
+    }
+
+
+def run_reference(args, comm: Comm, world: int, rank: int, local: int) -> dict | None:
+    exe = os.path.join(REPO, "baseline", "_ref", "build", "benchmarks", "ugdr_client_daemon_cuda_benchmark")
+    if not os.path.exists(exe):
+        out = {"impl": "reference", "unavailable": "reference benchmark binary not built in baseline/_ref"}
+        return out if rank == 0 else None
+    env = dict(os.environ)
+    env["CUDA_VISIBLE_DEVICES"] = str(local)
+    for k in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "MASTER_ADDR", "MASTER_PORT"):
+        env.pop(k, None)
+    wr = SLOT_MIB << 20
+    # The reference runs queue depth 64 per batch; size its batches to ~ the same bytes as ours.
+    batches = max(1, (args.steps * PEERS * wr) // (64 * wr))
+    cmd = [exe, "--wr-bytes", str(wr), "--warmup-batches", str(max(1, args.warmup // 4)),
+           "--bandwidth-batches", str(batches), "--latency-warmup", "2", "--latency-iterations", "20"]
+    comm.barrier()
+    res = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=1800)
+    gbps = None
+    for line in res.stdout.splitlines():
+        m = re.search(r"phase=bandwidth.*logical_payload_GB_per_s=([0-9.]+)", line)
+        if m:
+            gbps = float(m.group(1))
+    got = comm.gather(gbps)
+    if rank != 0:
+        return None
+    if any(g is None for g in got):
+        return {"impl": "reference", "unavailable": f"reference benchmark failed (rc={res.returncode}): "
+                f"{(res.stderr or res.stdout)[-300:]!r}"}
+    value = sum(got)
+    return {
+        "impl": "reference",
+        "metric": "rdma_write_allpairs_aggregate_GBps",
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (reference's own seeded payload)",
+        "config": {"model": "reference client->daemon CUDA benchmark, 32 MiB WRs, QD 64, same-GPU target",
+                   "per_gpu_GBps": got, "batches": batches,
+                   "timing": "reference's own wall clock (steady_clock) per process, summed over GPUs"},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ugdr", "reference"], default="ugdr")
+    args = ap.parse_args()
+    world, rank, local = dist_env()
+    if world != args.gpus and not (world == 1 and args.gpus == 1):
+        if world == 1:
+            raise SystemExit("--gpus N > 1 must be launched with torchrun (one rank per GPU)")
+    comm = Comm(world, rank)
+    try:
+        if args.impl == "reference":
+            out = run_reference(args, comm, world, rank, local)
+        else:
+            out = run_ugdr(args, comm, world, rank, local)
+    finally:
+        comm.close()
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

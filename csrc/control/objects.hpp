@@ -1,0 +1,169 @@
+// Daemon-side object model and the interfaces the control plane drives.
+//
+// The control plane (service.hpp) owns every object's lifetime and validates every request.
+// Two pluggable pieces sit below it:
+//  * MemoryBackend opens client memory inside the daemon (CUDA IPC for cudaMalloc ranges, a
+//    memfd mapping for ugdr host buffers); tests substitute a fake.
+//  * Engine executes the work queued on a device's QPs.  One engine per ugdr device: the
+//    host-memory CPU engine, and one sm_100a executor per GPU.  Each engine is told about
+//    every MR (any QP may name any MR by key), about CQs and QPs of its own device, and about
+//    state changes; it keeps whatever device-side mirror it needs.
+#pragma once
+
+#include "common/fd.hpp"
+#include "common/shm.hpp"
+#include "queue/ring.hpp"
+
+#include <array>
+#include <cstdint>
+#include <memory>
+#include <string>
+#include <vector>
+
+namespace ugdr::control {
+
+enum class DeviceKind : int { cpu = 0, gpu = 1 };
+
+struct DeviceInfo {
+    uint64_t identity = 0;
+    std::string name;
+    DeviceKind kind = DeviceKind::cpu;
+    int gpu_ordinal = -1;
+};
+
+// ---- memory --------------------------------------------------------------------------------
+
+enum class MemKind : uint8_t { cuda = 1, host = 2 };
+
+// What a client sends to register memory (decoded from the register-MR opaque).
+struct MemoryDescriptor {
+    MemKind kind = MemKind::cuda;
+    uint64_t client_address = 0;  // start of the registered range in the client
+    // cuda: allocation identity
+    std::array<uint8_t, 16> uuid{};
+    uint64_t allocation_bytes = 0;
+    uint64_t allocation_offset = 0;  // registered range start - allocation base
+    std::vector<uint8_t> ipc_handle;
+    // host: the memfd region holding the range
+    uint64_t region_bytes = 0;
+    uint64_t region_offset = 0;
+    Fd region_fd;
+};
+
+struct OpenedMemory {
+    void *address = nullptr;  // daemon address of the registered range start
+    void *device_address = nullptr;  // the same byte as seen by the GPU executors (0: unreachable)
+    int gpu = -1;             // owning CUDA ordinal, -1 for host memory
+    void *base = nullptr;     // what to close (IPC mapping base)
+    SharedMapping host;       // host regions stay mapped while registered
+};
+
+class MemoryBackend {
+  public:
+    virtual ~MemoryBackend() = default;
+    // Returns 0 or a positive errno (EOPNOTSUPP for memory kinds the backend cannot open).
+    virtual int open(MemoryDescriptor &desc, uint64_t length, OpenedMemory *out) = 0;
+    virtual void close(OpenedMemory &mem) noexcept = 0;
+};
+
+// ---- objects -------------------------------------------------------------------------------
+
+struct Context {
+    uint32_t device = 0;  // index into the daemon's device list
+    size_t children = 0;  // PDs + CQs
+};
+
+struct Pd {
+    uint64_t context_id = 0;
+    uint32_t pd_num = 0;  // daemon-unique, used for PD checks on the data path
+    size_t mrs = 0;
+    size_t qps = 0;
+};
+
+struct Mr {
+    uint64_t pd_id = 0;
+    uint32_t pd_num = 0;
+    uint32_t device = 0;  // device of the registering context
+    uint64_t client_address = 0;
+    uint64_t length = 0;
+    uint32_t access = 0;
+    uint32_t lkey = 0, rkey = 0;
+    uint32_t handle = 0;
+    uint32_t table_slot = 0;
+    OpenedMemory mem;
+};
+
+struct Cq {
+    uint64_t context_id = 0;
+    uint32_t device = 0;
+    uint32_t cq_num = 0;
+    queue::Ring ring;
+    size_t qp_refs = 0;
+    void *engine_block = nullptr;  // engine-private control block (e.g. device reservation counters)
+};
+
+struct QpCaps {
+    uint32_t max_send_wr = 0, max_recv_wr = 0, max_send_sge = 0, max_recv_sge = 0;
+};
+
+struct Qp {
+    uint64_t pd_id = 0;
+    uint32_t pd_num = 0;
+    uint32_t device = 0;
+    uint32_t qpn = 0;
+    uint64_t send_cq_id = 0, recv_cq_id = 0;
+    Cq *send_cq = nullptr;
+    Cq *recv_cq = nullptr;
+    QpCaps caps;
+    bool sq_sig_all = false;
+    queue::Ring sq, rq;
+    // verbs state
+    int state = 0;  // ugdr_qp_state
+    uint32_t access = 0;
+    uint8_t timeout = 0, retry_cnt = 0, rnr_retry = 0, min_rnr_timer = 0;
+    Qp *peer = nullptr;   // bound responder (after connect)
+    uint32_t peer_qpn = 0;
+    bool peer_lost = false;  // the bound responder was destroyed
+    void *engine_block = nullptr;  // engine-private per-QP state
+};
+
+// ---- engines -------------------------------------------------------------------------------
+
+struct EngineStats {
+    uint64_t wrs_completed = 0, bytes_moved = 0, error_completions = 0, launches = 0,
+             wait_timeouts = 0, first_start_ns = 0, last_end_ns = 0;
+};
+
+class Engine {
+  public:
+    virtual ~Engine() = default;
+    virtual DeviceInfo info() const = 0;
+
+    // MR table: every engine sees every MR.  attach may refuse memory it cannot reach only by
+    // leaving the entry unusable (the data path then reports an access error).
+    virtual int attach_mr(Mr &mr) = 0;
+    virtual void detach_mr(Mr &mr) noexcept = 0;
+    // CQs and QPs of this engine's device.
+    virtual int attach_cq(Cq &cq) = 0;
+    virtual void detach_cq(Cq &cq) noexcept = 0;
+    virtual int attach_qp(Qp &qp) = 0;
+    // The QP's verbs state, peer binding or retry attributes changed.
+    virtual void update_qp(Qp &qp) = 0;
+    virtual void detach_qp(Qp &qp) noexcept = 0;
+    // Stop executing and wait until nothing of this engine touches daemon objects.
+    virtual void quiesce() = 0;
+    // Allow execution again after quiesce().
+    virtual void resume() = 0;
+
+    virtual int stats(EngineStats *out, bool reset) = 0;
+    virtual int hold(bool on) = 0;
+    // Launch (held) executor for a timed drain; complete with finish_drain.
+    virtual int start_drain(uint64_t expected_wrs) { (void)expected_wrs; return EOPNOTSUPP; }
+    virtual int finish_drain(uint32_t timeout_ms, float *elapsed_ms) {
+        (void)timeout_ms;
+        (void)elapsed_ms;
+        return EOPNOTSUPP;
+    }
+};
+
+}  // namespace ugdr::control

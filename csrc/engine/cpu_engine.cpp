@@ -1,0 +1,321 @@
+#include "engine/cpu_engine.hpp"
+
+#include "control/service.hpp"
+#include "engine/semantics.hpp"
+#include "queue/layout.hpp"
+
+#include <chrono>
+#include <cstring>
+#include <time.h>
+
+namespace ugdr::engine {
+namespace {
+
+uint64_t now_ns() {
+    timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return uint64_t(ts.tv_sec) * 1000000000ull + uint64_t(ts.tv_nsec);
+}
+
+struct Seg {
+    uint8_t *local;
+    uint32_t length;
+};
+
+}  // namespace
+
+CpuEngine::CpuEngine(std::mutex &objects_mu, bool start_thread) : objects_mu_(objects_mu) {
+    if (start_thread) worker_ = std::thread([this] { run(); });
+}
+
+CpuEngine::~CpuEngine() {
+    stop_.store(true);
+    if (worker_.joinable()) worker_.join();
+}
+
+control::DeviceInfo CpuEngine::info() const {
+    control::DeviceInfo d;
+    d.name = "ugdr_cpu0";
+    d.kind = control::DeviceKind::cpu;
+    return d;
+}
+
+int CpuEngine::attach_mr(control::Mr &mr) {
+    MrView v;
+    if (mr.mem.gpu < 0) v.base = static_cast<uint8_t *>(mr.mem.address);  // host only
+    v.client_base = mr.client_address;
+    v.length = mr.length;
+    v.access = mr.access;
+    v.pd_num = mr.pd_num;
+    v.lkey = mr.lkey;
+    v.rkey = mr.rkey;
+    mrs_[mr.table_slot] = v;
+    return 0;
+}
+
+void CpuEngine::detach_mr(control::Mr &mr) noexcept { mrs_.erase(mr.table_slot); }
+
+int CpuEngine::attach_cq(control::Cq &) { return 0; }
+void CpuEngine::detach_cq(control::Cq &) noexcept {}
+
+int CpuEngine::attach_qp(control::Qp &qp) {
+    qps_.push_back(QpView{&qp, 0, 0});
+    return 0;
+}
+
+void CpuEngine::update_qp(control::Qp &qp) {
+    for (QpView &v : qps_)
+        if (v.qp == &qp) v.rnr_attempts = 0;
+}
+
+void CpuEngine::detach_qp(control::Qp &qp) noexcept {
+    for (size_t i = 0; i < qps_.size(); ++i) {
+        if (qps_[i].qp == &qp) {
+            qps_[i] = qps_.back();
+            qps_.pop_back();
+            return;
+        }
+    }
+}
+
+int CpuEngine::stats(control::EngineStats *out, bool reset) {
+    *out = stats_;
+    if (reset) stats_ = control::EngineStats{};
+    return 0;
+}
+
+int CpuEngine::hold(bool on) {
+    held_.store(on);
+    return 0;
+}
+
+const CpuEngine::MrView *CpuEngine::find(uint32_t key, bool remote) const {
+    auto it = mrs_.find(control::key_slot(key));
+    if (it == mrs_.end()) return nullptr;
+    if ((remote ? it->second.rkey : it->second.lkey) != key) return nullptr;
+    return &it->second;
+}
+
+bool CpuEngine::produce(control::Cq *cq, const void *cqe) {
+    queue::SlotRun run = cq->ring.reserve(1);
+    if (run.count() == 0) return false;
+    std::memcpy(run.first, cqe, sizeof(queue::Cqe));
+    cq->ring.publish(1);
+    return true;
+}
+
+void CpuEngine::enter_error(control::Qp &qp) {
+    qp.state = UGDR_QPS_ERR;
+    qp.sq.set_error_word(UGDR_QPS_ERR);
+}
+
+uint8_t *CpuEngine::resolve(const MrView *m, uint64_t addr, uint64_t len) {
+    if (m == nullptr || m->base == nullptr || addr < m->client_base || len > m->length ||
+        addr - m->client_base > m->length - len)
+        return nullptr;
+    return m->base + (addr - m->client_base);
+}
+
+size_t CpuEngine::progress_qp(QpView &v) {
+    control::Qp &qp = *v.qp;
+    size_t retired = 0;
+    if (qp.state == UGDR_QPS_ERR) {
+        // Flush: one FLUSH_ERR per outstanding SQ and RQ WR, signaled or not.
+        for (;;) {
+            queue::SlotRun run = qp.sq.peek(1);
+            if (run.count() == 0) break;
+            queue::SendWqe h;
+            std::memcpy(&h, run.first, sizeof(h));
+            queue::Cqe c{h.wr_id, UGDR_WC_WR_FLUSH_ERR, wc_opcode(h.opcode), 0, 0, qp.qpn, 0};
+            if (!produce(qp.send_cq, &c)) break;
+            qp.sq.release(1);
+            stats_.error_completions += 1;
+            ++retired;
+        }
+        for (;;) {
+            queue::SlotRun run = qp.rq.peek(1);
+            if (run.count() == 0) break;
+            queue::RecvWqe h;
+            std::memcpy(&h, run.first, sizeof(h));
+            queue::Cqe c{h.wr_id, UGDR_WC_WR_FLUSH_ERR, UGDR_WC_RECV_RDMA_WITH_IMM, 0, 0, qp.qpn, 0};
+            if (!produce(qp.recv_cq, &c)) break;
+            qp.rq.release(1);
+            stats_.error_completions += 1;
+        }
+        return retired;
+    }
+    if (qp.state != UGDR_QPS_RTS) return 0;
+
+    for (uint32_t budget = 0; budget < 64; ++budget) {
+        queue::SlotRun run = qp.sq.peek(1);
+        if (run.count() == 0) break;
+        const uint8_t *slot = run.first;
+        queue::SendWqe h;
+        std::memcpy(&h, slot, sizeof(h));
+        const uint32_t op = h.opcode;
+        const bool signaled = qp.sq_sig_all || (h.send_flags & UGDR_SEND_SIGNALED) != 0;
+        uint32_t status = UGDR_WC_SUCCESS;
+        uint64_t total = 0;
+        Seg segs[32];
+        uint32_t nseg = 0;
+
+        if (!op_known(op) || h.sge_count > qp.caps.max_send_sge || h.sge_count > 32 ||
+            (op_atomic(op) && h.sge_count != 1))
+            status = UGDR_WC_LOC_QP_OP_ERR;
+        for (uint32_t i = 0; status == UGDR_WC_SUCCESS && i < h.sge_count; ++i) {
+            queue::Sge sg;
+            std::memcpy(&sg, slot + queue::kSendSgeOffset + i * sizeof(queue::Sge), sizeof(sg));
+            total += sg.length;
+            if (total > 0x80000000ull) {
+                status = UGDR_WC_LOC_LEN_ERR;
+                break;
+            }
+            if (sg.length == 0) continue;
+            const MrView *m = find(sg.lkey, false);
+            uint8_t *p = (m != nullptr && m->pd_num == qp.pd_num) ? resolve(m, sg.address, sg.length)
+                                                                   : nullptr;
+            if (p == nullptr || (local_written(op) && (m->access & UGDR_ACCESS_LOCAL_WRITE) == 0)) {
+                status = UGDR_WC_LOC_PROT_ERR;
+                break;
+            }
+            segs[nseg++] = Seg{p, sg.length};
+        }
+        if (status == UGDR_WC_SUCCESS && op_atomic(op) && total != 8) status = UGDR_WC_LOC_LEN_ERR;
+
+        control::Qp *peer = qp.peer;
+        uint8_t *remote = nullptr;
+        if (status == UGDR_WC_SUCCESS) {
+            if (peer == nullptr || qp.peer_lost || peer->state == UGDR_QPS_RESET) {
+                status = UGDR_WC_RETRY_EXC_ERR;
+            } else if (peer->state == UGDR_QPS_ERR) {
+                status = UGDR_WC_REM_OP_ERR;
+            } else {
+                const uint32_t need = remote_access_for(op);
+                const MrView *m = find(h.rkey, true);
+                if (total != 0 || op_atomic(op)) {
+                    remote = (m != nullptr && m->pd_num == peer->pd_num && (m->access & need) != 0 &&
+                              (peer->access & need) != 0)
+                                 ? resolve(m, h.remote_address, op_atomic(op) ? 8 : total)
+                                 : nullptr;
+                    if (remote == nullptr) status = UGDR_WC_REM_ACCESS_ERR;
+                } else if ((peer->access & need) == 0) {
+                    status = UGDR_WC_REM_ACCESS_ERR;
+                }
+                if (status == UGDR_WC_SUCCESS && op_atomic(op) && (h.remote_address & 7) != 0)
+                    status = UGDR_WC_REM_INV_REQ_ERR;
+            }
+        }
+
+        // Responder resources for WRITE_WITH_IMM: one RQ WR and one recv-CQ slot.
+        uint64_t recv_wr_id = 0;
+        if (status == UGDR_WC_SUCCESS && op == UGDR_WR_RDMA_WRITE_WITH_IMM) {
+            queue::SlotRun rq = peer->rq.peek(1);
+            if (rq.count() == 0) {
+                if (qp.rnr_retry == kInfiniteRnrRetry) break;  // wait for a receive
+                const uint64_t now = now_ns();
+                if (v.rnr_next_ns == 0 || now >= v.rnr_next_ns) {
+                    if (v.rnr_next_ns != 0) v.rnr_attempts += 1;
+                    if (v.rnr_attempts >= qp.rnr_retry) {
+                        status = UGDR_WC_RNR_RETRY_EXC_ERR;
+                    } else {
+                        v.rnr_next_ns = now + rnr_timer_ns(peer->min_rnr_timer);
+                        break;
+                    }
+                } else {
+                    break;
+                }
+            } else {
+                queue::RecvWqe rh;
+                std::memcpy(&rh, rq.first, sizeof(rh));
+                recv_wr_id = rh.wr_id;
+                if (peer->recv_cq->ring.reserve(1).count() == 0) break;  // responder CQ full: wait
+            }
+        }
+        // Requester CQ slot (signaled successes and every error).
+        const bool need_cqe = signaled || status != UGDR_WC_SUCCESS;
+        if (need_cqe && qp.send_cq->ring.reserve(1).count() == 0) break;
+
+        if (status == UGDR_WC_SUCCESS) {
+            if (op == UGDR_WR_RDMA_WRITE || op == UGDR_WR_RDMA_WRITE_WITH_IMM) {
+                uint64_t off = 0;
+                for (uint32_t i = 0; i < nseg; ++i) {
+                    std::memcpy(remote + off, segs[i].local, segs[i].length);
+                    off += segs[i].length;
+                }
+            } else if (op == UGDR_WR_RDMA_READ) {
+                uint64_t off = 0;
+                for (uint32_t i = 0; i < nseg; ++i) {
+                    std::memcpy(segs[i].local, remote + off, segs[i].length);
+                    off += segs[i].length;
+                }
+            } else {
+                uint64_t compare_add = 0;
+                std::memcpy(&compare_add, slot + queue::kAtomicCompareOffset, 8);
+                const uint64_t swap = (uint64_t(h.reserved) << 32) | h.immediate_data;
+                auto *target = reinterpret_cast<uint64_t *>(remote);
+                uint64_t old;
+                if (op == UGDR_WR_ATOMIC_FETCH_AND_ADD) {
+                    old = __atomic_fetch_add(target, compare_add, __ATOMIC_ACQ_REL);
+                } else {
+                    old = compare_add;
+                    __atomic_compare_exchange_n(target, &old, swap, false, __ATOMIC_ACQ_REL,
+                                                __ATOMIC_ACQUIRE);
+                }
+                std::memcpy(segs[0].local, &old, 8);
+            }
+            std::atomic_thread_fence(std::memory_order_release);
+            if (op == UGDR_WR_RDMA_WRITE_WITH_IMM) {
+                peer->rq.peek(1);
+                peer->rq.release(1);
+                queue::Cqe rc{recv_wr_id, UGDR_WC_SUCCESS, UGDR_WC_RECV_RDMA_WITH_IMM,
+                              uint32_t(total), h.immediate_data, peer->qpn, UGDR_WC_WITH_IMM};
+                produce(peer->recv_cq, &rc);
+            }
+            v.rnr_attempts = 0;
+            v.rnr_next_ns = 0;
+            stats_.bytes_moved += op_atomic(op) ? 8 : total;
+        }
+        if (need_cqe) {
+            queue::Cqe c{h.wr_id, status, wc_opcode(op), uint32_t(total), 0, qp.qpn, 0};
+            if (status != UGDR_WC_SUCCESS) c.byte_length = 0;
+            produce(qp.send_cq, &c);
+        }
+        qp.sq.peek(1);
+        qp.sq.release(1);
+        ++retired;
+        stats_.wrs_completed += 1;
+        if (status != UGDR_WC_SUCCESS) {
+            stats_.error_completions += 1;
+            v.rnr_attempts = 0;
+            v.rnr_next_ns = 0;
+            enter_error(qp);
+            return retired + progress_qp(v);  // flush what remains
+        }
+    }
+    return retired;
+}
+
+size_t CpuEngine::progress_locked() {
+    size_t n = 0;
+    for (QpView &v : qps_) n += progress_qp(v);
+    return n;
+}
+
+void CpuEngine::run() {
+    uint32_t idle = 0;
+    while (!stop_.load(std::memory_order_relaxed)) {
+        size_t n = 0;
+        if (!held_.load(std::memory_order_relaxed)) {
+            std::lock_guard<std::mutex> lk(objects_mu_);
+            n = progress_locked();
+        }
+        if (n == 0) {
+            idle = idle < 64 ? idle + 1 : idle;
+            if (idle > 16) std::this_thread::sleep_for(std::chrono::microseconds(idle > 60 ? 50 : 2));
+        } else {
+            idle = 0;
+        }
+    }
+}
+
+}  // namespace ugdr::engine

@@ -1,0 +1,134 @@
+#include "gpu/cuda_memory.hpp"
+
+#include <cuda_runtime_api.h>
+
+#include <cerrno>
+#include <cstring>
+
+namespace ugdr::gpu {
+
+GpuInventory probe_gpus(int limit) {
+    GpuInventory inv;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return inv;
+    }
+    if (limit >= 0 && limit < n) n = limit;
+    for (int i = 0; i < n; ++i) {
+        cudaDeviceProp p{};
+        if (cudaGetDeviceProperties(&p, i) != cudaSuccess) break;
+        std::array<uint8_t, 16> u{};
+        std::memcpy(u.data(), p.uuid.bytes, 16);
+        inv.uuids.push_back(u);
+        inv.sm_count.push_back(p.multiProcessorCount);
+        inv.count += 1;
+    }
+    return inv;
+}
+
+int enable_all_peer_access(int n) {
+    int failures = 0;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    for (int a = 0; a < n; ++a) {
+        cudaSetDevice(a);
+        for (int b = 0; b < n; ++b) {
+            if (a == b) continue;
+            int can = 0;
+            cudaDeviceCanAccessPeer(&can, a, b);
+            if (!can) {
+                ++failures;
+                continue;
+            }
+            const cudaError_t e = cudaDeviceEnablePeerAccess(b, 0);
+            if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled) ++failures;
+            (void)cudaGetLastError();
+        }
+    }
+    cudaSetDevice(prev);
+    return failures;
+}
+
+int DaemonMemoryBackend::open(control::MemoryDescriptor &desc, uint64_t length,
+                              control::OpenedMemory *out) {
+    if (desc.kind == control::MemKind::host) {
+        if (int rc = map_shared_fd(desc.region_fd.release(), 0, &out->host); rc != 0) return rc;
+        if (desc.region_offset > out->host.bytes || length > out->host.bytes - desc.region_offset) {
+            out->host.unmap();
+            return EINVAL;
+        }
+        out->address = static_cast<uint8_t *>(out->host.address) + desc.region_offset;
+        out->gpu = -1;
+        out->device_address = nullptr;
+        if (inv_.count > 0) {
+            // Pin and map the whole region once, portable to every GPU the executors run on.
+            if (cudaHostRegister(out->host.address, out->host.bytes,
+                                 cudaHostRegisterMapped | cudaHostRegisterPortable) == cudaSuccess) {
+                void *dev = nullptr;
+                if (cudaHostGetDevicePointer(&dev, out->host.address, 0) == cudaSuccess)
+                    out->device_address = static_cast<uint8_t *>(dev) + desc.region_offset;
+                out->base = out->host.address;  // marks the registration for close()
+            }
+            (void)cudaGetLastError();
+        }
+        return 0;
+    }
+    if (desc.ipc_handle.size() != sizeof(cudaIpcMemHandle_t)) return EINVAL;
+    int gpu = -1;
+    for (int i = 0; i < inv_.count; ++i)
+        if (std::memcmp(inv_.uuids[i].data(), desc.uuid.data(), 16) == 0) gpu = i;
+    if (gpu < 0) return ENODEV;  // the allocation lives on a GPU this daemon does not own
+    std::lock_guard<std::mutex> lk(mu_);
+    auto it = open_.find(desc.ipc_handle);
+    if (it == open_.end()) {
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, desc.ipc_handle.data(), sizeof(h));
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaSetDevice(gpu);
+        void *base = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+        cudaSetDevice(prev);
+        if (e != cudaSuccess) {
+            (void)cudaGetLastError();
+            return EACCES;
+        }
+        it = open_.emplace(desc.ipc_handle, Mapping{base, gpu, 0}).first;
+    }
+    it->second.refs += 1;
+    out->base = it->second.base;
+    out->address = static_cast<uint8_t *>(it->second.base) + desc.allocation_offset;
+    out->device_address = out->address;  // UVA: the same pointer is valid on every peer GPU
+    out->gpu = gpu;
+    return 0;
+}
+
+void DaemonMemoryBackend::close(control::OpenedMemory &mem) noexcept {
+    if (mem.gpu < 0) {
+        if (mem.base != nullptr) cudaHostUnregister(mem.base);
+        mem.base = nullptr;
+        mem.device_address = nullptr;
+        mem.host.unmap();
+        mem.address = nullptr;
+        return;
+    }
+    std::lock_guard<std::mutex> lk(mu_);
+    for (auto it = open_.begin(); it != open_.end(); ++it) {
+        if (it->second.base == mem.base) {
+            if (--it->second.refs == 0) {
+                int prev = 0;
+                cudaGetDevice(&prev);
+                cudaSetDevice(it->second.gpu);
+                cudaIpcCloseMemHandle(it->second.base);
+                cudaSetDevice(prev);
+                open_.erase(it);
+            }
+            break;
+        }
+    }
+    mem.address = nullptr;
+    mem.base = nullptr;
+}
+
+}  // namespace ugdr::gpu

@@ -1,0 +1,182 @@
+// Structures shared by the GPU engine's host code and the sm_100a executor kernel.
+//
+// Every table lives in device memory of the GPU whose engine owns it and is reachable from the
+// other GPUs' executors through peer access (the daemon enables it for every pair), so a
+// requester on GPU a can consume the RQ and fill the receive CQ of a responder on GPU b.
+// Rings (SQ / RQ / CQ) stay in the memfd mappings clients already share with the daemon; the
+// daemon registers them with CUDA as mapped host memory so kernels read WQEs and write CQEs in
+// place, with .sys-scope acquire / release on the cursors.
+//
+// Host writes only `DevQpConfig`, `DevMr` and `DevCqConfig` (by copies on a side stream);
+// the `...State` halves belong to the kernel.
+#pragma once
+
+#include "queue/layout.hpp"
+
+#include <stdint.h>
+
+namespace ugdr::gpu {
+
+constexpr uint32_t kMaxMrs = 1u << 16;       // key slots (matches the control plane's keys)
+constexpr uint32_t kMaxQpsPerEngine = 4096;
+constexpr uint32_t kMaxCqsPerEngine = 4096;
+constexpr uint32_t kWindow = 4;              // in-flight WRs per QP
+constexpr uint32_t kMaxSge = 32;
+constexpr uint32_t kJobSlots = 1024;         // large-WR job ring per engine
+constexpr uint32_t kInlineBytes = 4096;      // WRs up to this size are copied by the owner warp
+
+struct DevMr {
+    uint64_t base;         // device-usable address of the first registered byte; 0 = unusable
+    uint64_t client_base;  // client address of that byte
+    uint64_t length;
+    uint32_t access;
+    uint32_t pd_num;
+    uint32_t lkey;
+    uint32_t rkey;
+    uint32_t valid;
+    uint32_t pad;
+};
+
+struct DevCqConfig {
+    queue::RingHeader *ring;  // device pointer of the mapped ring
+    uint8_t *slots;
+    uint32_t capacity;
+    uint32_t stride;
+    uint32_t valid;
+    uint32_t pad;
+};
+
+struct DevCqState {
+    unsigned long long reserve;    // next slot to hand out (CAS, .sys)
+    unsigned long long published;  // next slot to publish (in order)
+    unsigned long long head_seen;  // cached consumer cursor
+    unsigned long long pad[5];
+};
+
+struct DevCq {
+    DevCqConfig cfg;
+    DevCqState st;
+};
+
+struct DevQp;
+
+struct DevQpConfig {
+    queue::RingHeader *sq;
+    uint8_t *sq_slots;
+    queue::RingHeader *rq;
+    uint8_t *rq_slots;
+    DevCq *send_cq;
+    DevCq *recv_cq;
+    DevQp *peer;  // responder (may live on another GPU); null when unbound
+    uint32_t sq_cap, sq_stride, rq_cap, rq_stride;
+    uint32_t qpn, pd_num, access, max_send_sge;
+    uint32_t state;  // ugdr_qp_state as set by the control plane
+    uint32_t sq_sig_all;
+    uint32_t peer_lost;
+    uint32_t active;
+    uint8_t timeout, retry_cnt, rnr_retry, min_rnr_timer;
+    uint32_t pad[3];
+};
+
+struct DevSeg {
+    uint64_t local;  // device address
+    uint64_t length;
+};
+
+struct WrRec {
+    unsigned long long wr_id;
+    unsigned long long remote;  // device address of the remote range start
+    unsigned long long total;
+    unsigned long long recv_claim;  // RQ cursor claimed for WRITE_WITH_IMM
+    unsigned long long recv_wr_id;
+    unsigned int chunks_done;
+    unsigned int nchunks;
+    uint32_t opcode;
+    uint32_t status;
+    uint32_t signaled;
+    uint32_t imm;
+    uint32_t nseg;
+    uint32_t recv_cqe_done;
+    uint32_t pad[2];
+    DevSeg seg[kMaxSge];
+};
+
+struct DevQpState {
+    unsigned long long sq_head;   // next WQE to retire (== ring head)
+    unsigned long long sq_issue;  // next WQE to issue
+    unsigned long long rq_claim;  // RQ WRs handed out (CAS by requesters, .sys)
+    unsigned long long rq_released;  // RQ head published in order
+    unsigned long long rnr_next_ns;
+    uint32_t rnr_attempts;
+    uint32_t err;  // executor-detected error: the QP is in ERR
+    unsigned long long pad[2];
+    WrRec win[kWindow];
+};
+
+struct DevQp {
+    DevQpConfig cfg;
+    DevQpState st;
+};
+
+struct Job {
+    unsigned long long ctl;  // ticket (high 32) | next chunk (low 32)
+    WrRec *rec;
+    uint32_t nchunks;
+    uint32_t chunk_bytes;
+    unsigned long long seq;  // ticket for which the slot is free
+    unsigned long long pad[4];
+};
+
+struct JobRing {
+    unsigned long long tail;       // tickets handed out
+    unsigned long long head_hint;  // no unclaimed job below this ticket
+    unsigned long long pad[6];
+    Job slots[kJobSlots];
+};
+
+// Executor status / statistics, in device memory.  The counters (up to `retired`) reset
+// together; `qp_slots` is written by the host whenever a QP slot above the current bound is
+// activated, so a running kernel starts polling it.
+struct DevStats {
+    unsigned long long wrs_completed;
+    unsigned long long bytes_moved;
+    unsigned long long error_completions;
+    unsigned long long wait_timeouts;
+    unsigned long long first_start_ns;
+    unsigned long long last_end_ns;
+    unsigned long long last_work_ns;
+    unsigned long long retired;  // WRs retired since the last reset (drain mode exit test)
+    unsigned int exiting;
+    unsigned int error_code;  // first bounded wait that gave up (see ExecError)
+    unsigned int qp_slots;
+    unsigned int pad[13];
+};
+
+enum ExecError : uint32_t {
+    kErrNone = 0,
+    kErrCqPublishTimeout = 1,
+    kErrRqReleaseTimeout = 2,
+    kErrJobSlotTimeout = 3,
+};
+
+// Host-mapped control word the host flips while the kernel runs.
+struct HostCtrl {
+    volatile uint32_t stop;
+    uint32_t pad[15];
+};
+
+enum ExecMode : uint32_t { kPersistent = 0, kDrain = 1 };
+
+struct ExecParams {
+    DevMr *mrs;
+    DevQp *qps;
+    JobRing *jobs;
+    DevStats *stats;
+    HostCtrl *ctrl;
+    uint32_t mode;
+    unsigned long long expected;  // drain: exit once this many WRs retired
+    unsigned long long idle_exit_ns;
+    unsigned long long max_wait_ns;  // bound on every internal spin
+};
+
+}  // namespace ugdr::gpu

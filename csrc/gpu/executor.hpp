@@ -1,0 +1,19 @@
+// Host entry points of the executor translation unit (executor.cu).
+#pragma once
+
+#include "gpu/device_abi.hpp"
+
+#include <cuda_runtime_api.h>
+#include <stddef.h>
+
+namespace ugdr::gpu {
+
+// Bytes to allocate for the job ring (ring + its 1024-bit active bitmap).
+size_t job_ring_bytes();
+int executor_threads();
+// Launch the persistent executor; returns a cudaError_t value.
+int launch_executor(const ExecParams &p, int ctas, cudaStream_t stream);
+// One-warp copy-core test launch (alignment matrix).
+int launch_copy_test(void *dst, const void *src, uint64_t n, cudaStream_t stream);
+
+}  // namespace ugdr::gpu

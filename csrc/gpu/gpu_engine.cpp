@@ -1,0 +1,534 @@
+#include "gpu/gpu_engine.hpp"
+
+#include "control/service.hpp"
+#include "gpu/device_abi.hpp"
+#include "gpu/executor.hpp"
+#include "ugdr/api.hpp"
+
+#include <cuda_runtime_api.h>
+
+#include <atomic>
+#include <cerrno>
+#include <chrono>
+#include <condition_variable>
+#include <cstdio>
+#include <cstring>
+#include <thread>
+#include <vector>
+
+namespace ugdr::gpu {
+namespace {
+
+using Clock = std::chrono::steady_clock;
+
+// Register a daemon ring mapping with CUDA (portable, mapped); returns the device pointer.
+void *register_ring(queue::Ring &ring) {
+    if (cudaHostRegister(ring.mapping(), ring.bytes(),
+                         cudaHostRegisterMapped | cudaHostRegisterPortable) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return nullptr;
+    }
+    void *dev = nullptr;
+    if (cudaHostGetDevicePointer(&dev, ring.mapping(), 0) != cudaSuccess) {
+        (void)cudaGetLastError();
+        cudaHostUnregister(ring.mapping());
+        return nullptr;
+    }
+    return dev;
+}
+
+class GpuEngine final : public control::Engine {
+  public:
+    GpuEngine(const GpuEngineConfig &cfg) : cfg_(cfg) {}
+    ~GpuEngine() override;
+
+    int init();
+
+    control::DeviceInfo info() const override {
+        control::DeviceInfo d;
+        d.name = "ugdr_gpu" + std::to_string(cfg_.ordinal);
+        d.kind = control::DeviceKind::gpu;
+        d.gpu_ordinal = cfg_.ordinal;
+        return d;
+    }
+    int attach_mr(control::Mr &mr) override;
+    void detach_mr(control::Mr &mr) noexcept override;
+    int attach_cq(control::Cq &cq) override;
+    void detach_cq(control::Cq &cq) noexcept override;
+    int attach_qp(control::Qp &qp) override;
+    void update_qp(control::Qp &qp) override;
+    void detach_qp(control::Qp &qp) noexcept override;
+    void quiesce() override;
+    void resume() override;
+    int stats(control::EngineStats *out, bool reset) override;
+    int hold(bool on) override;
+    int start_drain(uint64_t expected) override;
+    int finish_drain(uint32_t timeout_ms, float *elapsed_ms) override;
+
+  private:
+    struct QpEntry {
+        control::Qp *qp = nullptr;
+        uint32_t slot = 0;
+        void *sq_dev = nullptr, *rq_dev = nullptr;
+        bool error = false;
+    };
+
+    void set_device() const { cudaSetDevice(cfg_.ordinal); }
+    int copy_to_device(void *dst, const void *src, size_t n);
+    int copy_from_device(void *dst, const void *src, size_t n);
+    bool has_work_locked();
+    int launch_locked(uint32_t mode, uint64_t expected, bool timed);
+    // Ask a running kernel to exit and wait (bounded); returns false if it did not stop.
+    bool stop_kernel_locked(uint32_t timeout_ms);
+    bool kernel_done_locked();
+    void monitor();
+    void fill_qp_config(control::Qp &qp, DevQpConfig *cfg);
+
+    GpuEngineConfig cfg_;
+    std::mutex mu_;
+    cudaStream_t exec_stream_ = nullptr, ctl_stream_ = nullptr;
+    cudaEvent_t ev_start_ = nullptr, ev_done_ = nullptr;
+    DevMr *mrs_ = nullptr;
+    DevQp *qps_ = nullptr;
+    DevCq *cqs_ = nullptr;
+    JobRing *jobs_ = nullptr;
+    DevStats *stats_ = nullptr;
+    HostCtrl *ctrl_ = nullptr;  // mapped pinned host memory
+    HostCtrl *ctrl_dev_ = nullptr;
+    std::vector<uint32_t> free_qp_slots_, free_cq_slots_;
+    uint32_t next_qp_slot_ = 0, next_cq_slot_ = 0, qp_slot_bound_ = 0;
+    std::vector<QpEntry> qps_host_;
+    bool running_ = false;
+    bool held_ = false;
+    int paused_ = 0;
+    uint64_t launches_ = 0;
+    std::atomic<bool> stop_monitor_{false};
+    std::thread monitor_;
+};
+
+GpuEngine::~GpuEngine() {
+    stop_monitor_.store(true);
+    if (monitor_.joinable()) monitor_.join();
+    std::lock_guard<std::mutex> lk(mu_);
+    set_device();
+    stop_kernel_locked(5000);
+    if (exec_stream_) cudaStreamDestroy(exec_stream_);
+    if (ctl_stream_) cudaStreamDestroy(ctl_stream_);
+    if (ev_start_) cudaEventDestroy(ev_start_);
+    if (ev_done_) cudaEventDestroy(ev_done_);
+    cudaFree(mrs_);
+    cudaFree(qps_);
+    cudaFree(cqs_);
+    cudaFree(jobs_);
+    cudaFree(stats_);
+    if (ctrl_) cudaFreeHost(ctrl_);
+}
+
+int GpuEngine::init() {
+    set_device();
+    auto ok = [](cudaError_t e) { return e == cudaSuccess; };
+    if (!ok(cudaStreamCreateWithFlags(&exec_stream_, cudaStreamNonBlocking)) ||
+        !ok(cudaStreamCreateWithFlags(&ctl_stream_, cudaStreamNonBlocking)) ||
+        !ok(cudaEventCreate(&ev_start_)) || !ok(cudaEventCreate(&ev_done_)) ||
+        !ok(cudaMalloc(reinterpret_cast<void **>(&mrs_), sizeof(DevMr) * kMaxMrs)) ||
+        !ok(cudaMalloc(reinterpret_cast<void **>(&qps_), sizeof(DevQp) * kMaxQpsPerEngine)) ||
+        !ok(cudaMalloc(reinterpret_cast<void **>(&cqs_), sizeof(DevCq) * kMaxCqsPerEngine)) ||
+        !ok(cudaMalloc(reinterpret_cast<void **>(&jobs_), job_ring_bytes())) ||
+        !ok(cudaMalloc(reinterpret_cast<void **>(&stats_), sizeof(DevStats))) ||
+        !ok(cudaHostAlloc(reinterpret_cast<void **>(&ctrl_), sizeof(HostCtrl), cudaHostAllocMapped | cudaHostAllocPortable)) ||
+        !ok(cudaHostGetDevicePointer(reinterpret_cast<void **>(&ctrl_dev_), ctrl_, 0))) {
+        (void)cudaGetLastError();
+        return ENODEV;
+    }
+    std::memset(ctrl_, 0, sizeof(HostCtrl));
+    cudaMemsetAsync(mrs_, 0, sizeof(DevMr) * kMaxMrs, ctl_stream_);
+    cudaMemsetAsync(qps_, 0, sizeof(DevQp) * kMaxQpsPerEngine, ctl_stream_);
+    cudaMemsetAsync(cqs_, 0, sizeof(DevCq) * kMaxCqsPerEngine, ctl_stream_);
+    cudaMemsetAsync(jobs_, 0, job_ring_bytes(), ctl_stream_);
+    cudaMemsetAsync(stats_, 0, sizeof(DevStats), ctl_stream_);
+    if (!ok(cudaStreamSynchronize(ctl_stream_))) return ENODEV;
+    monitor_ = std::thread([this] { monitor(); });
+    return 0;
+}
+
+int GpuEngine::copy_to_device(void *dst, const void *src, size_t n) {
+    set_device();
+    if (cudaMemcpyAsync(dst, src, n, cudaMemcpyHostToDevice, ctl_stream_) != cudaSuccess ||
+        cudaStreamSynchronize(ctl_stream_) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return EIO;
+    }
+    return 0;
+}
+
+int GpuEngine::copy_from_device(void *dst, const void *src, size_t n) {
+    set_device();
+    if (cudaMemcpyAsync(dst, src, n, cudaMemcpyDeviceToHost, ctl_stream_) != cudaSuccess ||
+        cudaStreamSynchronize(ctl_stream_) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return EIO;
+    }
+    return 0;
+}
+
+// ---- MRs --------------------------------------------------------------------------------------
+
+int GpuEngine::attach_mr(control::Mr &mr) {
+    DevMr d{};
+    d.base = reinterpret_cast<uint64_t>(mr.mem.device_address);
+    d.client_base = mr.client_address;
+    d.length = mr.length;
+    d.access = mr.access;
+    d.pd_num = mr.pd_num;
+    d.lkey = mr.lkey;
+    d.rkey = mr.rkey;
+    d.valid = 1;
+    return copy_to_device(&mrs_[mr.table_slot], &d, sizeof(d));
+}
+
+void GpuEngine::detach_mr(control::Mr &mr) noexcept {
+    quiesce();
+    DevMr d{};
+    copy_to_device(&mrs_[mr.table_slot], &d, sizeof(d));
+    resume();
+}
+
+// ---- CQs --------------------------------------------------------------------------------------
+
+int GpuEngine::attach_cq(control::Cq &cq) {
+    std::lock_guard<std::mutex> lk(mu_);
+    uint32_t slot;
+    if (!free_cq_slots_.empty()) {
+        slot = free_cq_slots_.back();
+        free_cq_slots_.pop_back();
+    } else {
+        if (next_cq_slot_ >= kMaxCqsPerEngine) return ENOSPC;
+        slot = next_cq_slot_++;
+    }
+    set_device();
+    void *dev = register_ring(cq.ring);
+    if (dev == nullptr) {
+        free_cq_slots_.push_back(slot);
+        return ENOMEM;
+    }
+    DevCq d{};
+    d.cfg.ring = static_cast<queue::RingHeader *>(dev);
+    d.cfg.slots = static_cast<uint8_t *>(dev) + queue::kRingHeaderBytes;
+    d.cfg.capacity = cq.ring.geometry().capacity;
+    d.cfg.stride = cq.ring.geometry().stride;
+    d.cfg.valid = 1;
+    if (int rc = copy_to_device(&cqs_[slot], &d, sizeof(d)); rc != 0) {
+        cudaHostUnregister(cq.ring.mapping());
+        free_cq_slots_.push_back(slot);
+        return rc;
+    }
+    cq.engine_block = &cqs_[slot];
+    return 0;
+}
+
+void GpuEngine::detach_cq(control::Cq &cq) noexcept {
+    if (cq.engine_block == nullptr) return;
+    quiesce();
+    {
+        std::lock_guard<std::mutex> lk(mu_);
+        DevCq *d = static_cast<DevCq *>(cq.engine_block);
+        DevCq zero{};
+        copy_to_device(d, &zero, sizeof(zero));
+        set_device();
+        cudaHostUnregister(cq.ring.mapping());
+        free_cq_slots_.push_back(uint32_t(d - cqs_));
+        cq.engine_block = nullptr;
+    }
+    resume();
+}
+
+// ---- QPs --------------------------------------------------------------------------------------
+
+void GpuEngine::fill_qp_config(control::Qp &qp, DevQpConfig *c) {
+    std::memset(c, 0, sizeof(*c));
+    for (const QpEntry &e : qps_host_) {
+        if (e.qp != &qp) continue;
+        c->sq = static_cast<queue::RingHeader *>(e.sq_dev);
+        c->sq_slots = static_cast<uint8_t *>(e.sq_dev) + queue::kRingHeaderBytes;
+        c->rq = static_cast<queue::RingHeader *>(e.rq_dev);
+        c->rq_slots = static_cast<uint8_t *>(e.rq_dev) + queue::kRingHeaderBytes;
+    }
+    c->send_cq = static_cast<DevCq *>(qp.send_cq->engine_block);
+    c->recv_cq = static_cast<DevCq *>(qp.recv_cq->engine_block);
+    c->peer = (qp.peer != nullptr) ? static_cast<DevQp *>(qp.peer->engine_block) : nullptr;
+    c->sq_cap = qp.sq.geometry().capacity;
+    c->sq_stride = qp.sq.geometry().stride;
+    c->rq_cap = qp.rq.geometry().capacity;
+    c->rq_stride = qp.rq.geometry().stride;
+    c->qpn = qp.qpn;
+    c->pd_num = qp.pd_num;
+    c->access = qp.access;
+    c->max_send_sge = qp.caps.max_send_sge;
+    c->state = uint32_t(qp.state);
+    c->sq_sig_all = qp.sq_sig_all ? 1u : 0u;
+    c->peer_lost = qp.peer_lost ? 1u : 0u;
+    c->active = 1;
+    c->timeout = qp.timeout;
+    c->retry_cnt = qp.retry_cnt;
+    c->rnr_retry = qp.rnr_retry;
+    c->min_rnr_timer = qp.min_rnr_timer;
+}
+
+int GpuEngine::attach_qp(control::Qp &qp) {
+    std::lock_guard<std::mutex> lk(mu_);
+    uint32_t slot;
+    if (!free_qp_slots_.empty()) {
+        slot = free_qp_slots_.back();
+        free_qp_slots_.pop_back();
+    } else {
+        if (next_qp_slot_ >= kMaxQpsPerEngine) return ENOSPC;
+        slot = next_qp_slot_++;
+    }
+    set_device();
+    QpEntry e;
+    e.qp = &qp;
+    e.slot = slot;
+    e.sq_dev = register_ring(qp.sq);
+    e.rq_dev = register_ring(qp.rq);
+    if (e.sq_dev == nullptr || e.rq_dev == nullptr) {
+        if (e.sq_dev) cudaHostUnregister(qp.sq.mapping());
+        if (e.rq_dev) cudaHostUnregister(qp.rq.mapping());
+        free_qp_slots_.push_back(slot);
+        return ENOMEM;
+    }
+    qps_host_.push_back(e);
+    qp.engine_block = &qps_[slot];
+    // Whole slot: config (inactive for now) and a zeroed device state.
+    std::unique_ptr<DevQp> d(new DevQp());
+    std::memset(d.get(), 0, sizeof(DevQp));
+    fill_qp_config(qp, &d->cfg);
+    d->cfg.active = 0;
+    int rc = copy_to_device(&qps_[slot], d.get(), sizeof(DevQp));
+    const uint32_t one = 1;
+    if (rc == 0) rc = copy_to_device(&qps_[slot].cfg.active, &one, sizeof(one));
+    if (rc == 0 && slot + 1 > qp_slot_bound_) {
+        qp_slot_bound_ = slot + 1;
+        rc = copy_to_device(&stats_->qp_slots, &qp_slot_bound_, sizeof(uint32_t));
+    }
+    if (rc != 0) {
+        qps_host_.pop_back();
+        cudaHostUnregister(qp.sq.mapping());
+        cudaHostUnregister(qp.rq.mapping());
+        free_qp_slots_.push_back(slot);
+        qp.engine_block = nullptr;
+    }
+    return rc;
+}
+
+void GpuEngine::update_qp(control::Qp &qp) {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (qp.engine_block == nullptr) return;
+    DevQp *d = static_cast<DevQp *>(qp.engine_block);
+    DevQpConfig c;
+    fill_qp_config(qp, &c);
+    // Everything but the state first, then the state word, so a running kernel never sees the
+    // new state with a half-written peer binding.
+    DevQpConfig staged = c;
+    uint32_t old_state = 0;
+    copy_from_device(&old_state, &d->cfg.state, sizeof(old_state));
+    staged.state = old_state;
+    copy_to_device(&d->cfg, &staged, sizeof(staged));
+    copy_to_device(&d->cfg.state, &c.state, sizeof(c.state));
+    for (QpEntry &e : qps_host_)
+        if (e.qp == &qp) e.error = qp.state == UGDR_QPS_ERR;
+}
+
+void GpuEngine::detach_qp(control::Qp &qp) noexcept {
+    if (qp.engine_block == nullptr) return;
+    quiesce();
+    {
+        std::lock_guard<std::mutex> lk(mu_);
+        DevQp *d = static_cast<DevQp *>(qp.engine_block);
+        const uint32_t zero = 0;
+        copy_to_device(&d->cfg.active, &zero, sizeof(zero));
+        set_device();
+        for (size_t i = 0; i < qps_host_.size(); ++i) {
+            if (qps_host_[i].qp != &qp) continue;
+            cudaHostUnregister(qp.sq.mapping());
+            cudaHostUnregister(qp.rq.mapping());
+            free_qp_slots_.push_back(qps_host_[i].slot);
+            qps_host_[i] = qps_host_.back();
+            qps_host_.pop_back();
+            break;
+        }
+        qp.engine_block = nullptr;
+    }
+    resume();
+}
+
+// ---- kernel life cycle ------------------------------------------------------------------------
+
+bool GpuEngine::kernel_done_locked() {
+    if (!running_) return true;
+    const cudaError_t e = cudaEventQuery(ev_done_);
+    if (e == cudaErrorNotReady) return false;
+    (void)cudaGetLastError();
+    running_ = false;
+    DevStats st{};
+    if (copy_from_device(&st, stats_, sizeof(st)) == 0 && st.error_code != 0) {
+        std::fprintf(stderr, "ugdr: GPU %d executor stopped a bounded wait (code %u)\n",
+                     cfg_.ordinal, st.error_code);
+        const uint32_t zero = 0;
+        copy_to_device(&stats_->error_code, &zero, sizeof(zero));
+    }
+    return true;
+}
+
+bool GpuEngine::stop_kernel_locked(uint32_t timeout_ms) {
+    if (!running_) return true;
+    set_device();
+    __atomic_store_n(&ctrl_->stop, 1u, __ATOMIC_RELEASE);
+    const auto deadline = Clock::now() + std::chrono::milliseconds(timeout_ms);
+    while (!kernel_done_locked()) {
+        if (Clock::now() > deadline) {
+            std::fprintf(stderr, "ugdr: GPU %d executor did not stop within %u ms\n", cfg_.ordinal,
+                         timeout_ms);
+            return false;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+    __atomic_store_n(&ctrl_->stop, 0u, __ATOMIC_RELEASE);
+    return true;
+}
+
+bool GpuEngine::has_work_locked() {
+    for (const QpEntry &e : qps_host_) {
+        const queue::Ring &sq = e.qp->sq;
+        if (sq.tail() != sq.head()) return true;
+        const bool err = e.error || sq.error_word() == UGDR_QPS_ERR;
+        if (err && e.qp->rq.tail() != e.qp->rq.head()) return true;
+    }
+    return false;
+}
+
+int GpuEngine::launch_locked(uint32_t mode, uint64_t expected, bool timed) {
+    set_device();
+    // Reset the per-launch words: exiting flag, and (drain) the retired counter.
+    const uint32_t zero = 0;
+    if (copy_to_device(&stats_->exiting, &zero, sizeof(zero)) != 0) return EIO;
+    if (mode == kDrain) {
+        const uint64_t z = 0;
+        if (copy_to_device(&stats_->retired, &z, sizeof(z)) != 0) return EIO;
+    }
+    ExecParams p{};
+    p.mrs = mrs_;
+    p.qps = qps_;
+    p.jobs = jobs_;
+    p.stats = stats_;
+    p.ctrl = ctrl_dev_;
+    p.mode = mode;
+    p.expected = expected;
+    p.idle_exit_ns = uint64_t(cfg_.idle_exit_us) * 1000ull;
+    p.max_wait_ns = uint64_t(cfg_.max_wait_ms) * 1000000ull;
+    if (timed) cudaEventRecord(ev_start_, exec_stream_);
+    const int rc = launch_executor(p, cfg_.ctas, exec_stream_);
+    if (rc != 0) {
+        std::fprintf(stderr, "ugdr: GPU %d executor launch failed: %s\n", cfg_.ordinal,
+                     cudaGetErrorString(cudaError_t(rc)));
+        return EIO;
+    }
+    cudaEventRecord(ev_done_, exec_stream_);
+    running_ = true;
+    launches_ += 1;
+    return 0;
+}
+
+void GpuEngine::monitor() {
+    set_device();
+    while (!stop_monitor_.load()) {
+        bool idle = true;
+        {
+            std::lock_guard<std::mutex> lk(mu_);
+            kernel_done_locked();
+            if (!running_ && !held_ && paused_ == 0 && has_work_locked()) {
+                launch_locked(kPersistent, 0, false);
+                idle = false;
+            }
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(idle ? 20 : 5));
+    }
+}
+
+void GpuEngine::quiesce() {
+    std::lock_guard<std::mutex> lk(mu_);
+    paused_ += 1;
+    stop_kernel_locked(cfg_.max_wait_ms * 4);
+}
+
+void GpuEngine::resume() {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (paused_ > 0) paused_ -= 1;
+}
+
+int GpuEngine::stats(control::EngineStats *out, bool reset) {
+    std::lock_guard<std::mutex> lk(mu_);
+    DevStats st{};
+    if (int rc = copy_from_device(&st, stats_, sizeof(st)); rc != 0) return rc;
+    out->wrs_completed = st.wrs_completed;
+    out->bytes_moved = st.bytes_moved;
+    out->error_completions = st.error_completions;
+    out->wait_timeouts = st.wait_timeouts;
+    out->first_start_ns = st.first_start_ns;
+    out->last_end_ns = st.last_end_ns;
+    out->launches = launches_;
+    if (reset) {
+        // Counters only (a running kernel may race a few increments into the fresh window).
+        cudaMemsetAsync(stats_, 0, offsetof(DevStats, last_work_ns), ctl_stream_);
+        cudaStreamSynchronize(ctl_stream_);
+        launches_ = 0;
+    }
+    return 0;
+}
+
+int GpuEngine::hold(bool on) {
+    std::lock_guard<std::mutex> lk(mu_);
+    held_ = on;
+    if (on) stop_kernel_locked(cfg_.max_wait_ms * 4);
+    return 0;
+}
+
+int GpuEngine::start_drain(uint64_t expected) {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (!stop_kernel_locked(cfg_.max_wait_ms * 4)) return EBUSY;
+    return launch_locked(kDrain, expected, true);
+}
+
+int GpuEngine::finish_drain(uint32_t timeout_ms, float *elapsed_ms) {
+    const auto deadline = Clock::now() + std::chrono::milliseconds(timeout_ms);
+    for (;;) {
+        {
+            std::lock_guard<std::mutex> lk(mu_);
+            if (kernel_done_locked()) break;
+            if (Clock::now() > deadline) {
+                stop_kernel_locked(cfg_.max_wait_ms * 4);
+                return ETIMEDOUT;
+            }
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(10));
+    }
+    std::lock_guard<std::mutex> lk(mu_);
+    set_device();
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, ev_start_, ev_done_) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return EIO;
+    }
+    *elapsed_ms = ms;
+    return 0;
+}
+
+}  // namespace
+
+int make_gpu_engine(const GpuEngineConfig &cfg, std::mutex &, std::unique_ptr<control::Engine> *out) {
+    auto e = std::make_unique<GpuEngine>(cfg);
+    if (int rc = e->init(); rc != 0) return rc;
+    *out = std::move(e);
+    return 0;
+}
+
+}  // namespace ugdr::gpu

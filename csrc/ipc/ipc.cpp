@@ -1,0 +1,268 @@
+#include "ipc/ipc.hpp"
+
+#include "common/bytes.hpp"
+
+#include <poll.h>
+#include <sys/socket.h>
+#include <sys/stat.h>
+#include <sys/un.h>
+#include <unistd.h>
+
+#include <cerrno>
+#include <cstring>
+#include <vector>
+
+namespace ugdr::ipc {
+
+void encode_envelope(const Envelope &e, uint8_t out[kEnvelopeBytes]) {
+    std::vector<std::byte> v;
+    v.reserve(kEnvelopeBytes);
+    ByteWriter w(&v);
+    w.be(e.magic).be(e.major).be(e.minor).be(e.method).be(e.flags).be(e.request_id);
+    w.be(uint32_t(e.status)).be(e.payload_length).be(e.fd_count);
+    std::memcpy(out, v.data(), kEnvelopeBytes);
+}
+
+Envelope decode_envelope(const uint8_t in[kEnvelopeBytes]) {
+    Envelope e;
+    ByteReader r(reinterpret_cast<const std::byte *>(in), kEnvelopeBytes);
+    uint32_t status = 0;
+    r.be(&e.magic);
+    r.be(&e.major);
+    r.be(&e.minor);
+    r.be(&e.method);
+    r.be(&e.flags);
+    r.be(&e.request_id);
+    r.be(&status);
+    r.be(&e.payload_length);
+    r.be(&e.fd_count);
+    e.status = int32_t(status);
+    return e;
+}
+
+int send_message(int sock, const Message &m) {
+    if (sock < 0 || m.payload.size() > kMaxPayload || m.fds.size() > kMaxFds) return EINVAL;
+    for (const Fd &f : m.fds)
+        if (!f.valid()) return EBADF;
+    Envelope e = m.env;
+    e.payload_length = uint32_t(m.payload.size());
+    e.fd_count = uint32_t(m.fds.size());
+    uint8_t head[kEnvelopeBytes];
+    encode_envelope(e, head);
+
+    iovec iov[2];
+    iov[0] = {head, kEnvelopeBytes};
+    iov[1] = {const_cast<std::byte *>(m.payload.data()), m.payload.size()};
+    msghdr mh{};
+    mh.msg_iov = iov;
+    mh.msg_iovlen = m.payload.empty() ? 1 : 2;
+    alignas(cmsghdr) char control[CMSG_SPACE(sizeof(int) * kMaxFds)];
+    if (!m.fds.empty()) {
+        const size_t len = sizeof(int) * m.fds.size();
+        std::memset(control, 0, sizeof(control));
+        mh.msg_control = control;
+        mh.msg_controllen = CMSG_SPACE(len);
+        cmsghdr *c = CMSG_FIRSTHDR(&mh);
+        c->cmsg_level = SOL_SOCKET;
+        c->cmsg_type = SCM_RIGHTS;
+        c->cmsg_len = CMSG_LEN(len);
+        int *dst = reinterpret_cast<int *>(CMSG_DATA(c));
+        for (size_t i = 0; i < m.fds.size(); ++i) dst[i] = m.fds[i].get();
+    }
+    for (;;) {
+        const ssize_t n = ::sendmsg(sock, &mh, MSG_NOSIGNAL);
+        if (n >= 0) return size_t(n) == kEnvelopeBytes + m.payload.size() ? 0 : EMSGSIZE;
+        if (errno != EINTR) return errno;
+    }
+}
+
+int recv_message(int sock, Message *m) {
+    if (sock < 0 || m == nullptr) return EINVAL;
+    std::vector<uint8_t> buf(kEnvelopeBytes + kMaxPayload + 1);
+    iovec iov{buf.data(), buf.size()};
+    msghdr mh{};
+    mh.msg_iov = &iov;
+    mh.msg_iovlen = 1;
+    alignas(cmsghdr) char control[CMSG_SPACE(sizeof(int) * kMaxFds)];
+    mh.msg_control = control;
+    mh.msg_controllen = sizeof(control);
+    ssize_t n;
+    for (;;) {
+        n = ::recvmsg(sock, &mh, MSG_CMSG_CLOEXEC);
+        if (n >= 0) break;
+        if (errno != EINTR) return errno;
+    }
+    // Adopt any descriptors first so an error path never leaks them.
+    std::vector<Fd> fds;
+    for (cmsghdr *c = CMSG_FIRSTHDR(&mh); c != nullptr; c = CMSG_NXTHDR(&mh, c)) {
+        if (c->cmsg_level == SOL_SOCKET && c->cmsg_type == SCM_RIGHTS) {
+            const size_t count = (c->cmsg_len - CMSG_LEN(0)) / sizeof(int);
+            const int *src = reinterpret_cast<const int *>(CMSG_DATA(c));
+            for (size_t i = 0; i < count; ++i) fds.emplace_back(src[i]);
+        }
+    }
+    if (n == 0) return ECONNRESET;
+    if ((mh.msg_flags & (MSG_TRUNC | MSG_CTRUNC)) != 0) return EMSGSIZE;
+    if (size_t(n) < kEnvelopeBytes) return EPROTO;
+    const Envelope e = decode_envelope(buf.data());
+    if (e.magic != kMagic || e.major != kVersionMajor || (e.flags & ~kFlagResponse) != 0 ||
+        e.payload_length != size_t(n) - kEnvelopeBytes || e.fd_count != fds.size() ||
+        e.payload_length > kMaxPayload) {
+        return EPROTO;
+    }
+    m->env = e;
+    m->payload.assign(reinterpret_cast<std::byte *>(buf.data() + kEnvelopeBytes),
+                      reinterpret_cast<std::byte *>(buf.data() + n));
+    m->fds = std::move(fds);
+    return 0;
+}
+
+namespace {
+
+int make_address(const std::string &path, sockaddr_un *addr) {
+    if (path.empty() || path.size() >= sizeof(addr->sun_path)) return ENAMETOOLONG;
+    std::memset(addr, 0, sizeof(*addr));
+    addr->sun_family = AF_UNIX;
+    std::memcpy(addr->sun_path, path.c_str(), path.size() + 1);
+    return 0;
+}
+
+}  // namespace
+
+int Client::connect(const std::string &path) {
+    sockaddr_un addr;
+    if (int rc = make_address(path, &addr); rc != 0) return rc;
+    Fd s(::socket(AF_UNIX, SOCK_SEQPACKET | SOCK_CLOEXEC, 0));
+    if (!s.valid()) return errno;
+    for (;;) {
+        if (::connect(s.get(), reinterpret_cast<sockaddr *>(&addr), sizeof(addr)) == 0) break;
+        if (errno != EINTR) return errno;
+    }
+    sock_ = std::move(s);
+    return 0;
+}
+
+int Client::call(uint32_t method, std::vector<std::byte> payload, std::vector<Fd> fds,
+                 Message *resp) {
+    if (!sock_.valid()) return ENOTCONN;
+    if (resp == nullptr) return EINVAL;
+    Message req;
+    req.env.method = method;
+    req.env.request_id = next_id_++;
+    req.payload = std::move(payload);
+    req.fds = std::move(fds);
+    if (int rc = send_message(sock_.get(), req); rc != 0) {
+        close();
+        return rc;
+    }
+    Message r;
+    if (int rc = recv_message(sock_.get(), &r); rc != 0) {
+        close();
+        return rc;
+    }
+    if ((r.env.flags & kFlagResponse) == 0 || r.env.request_id != req.env.request_id ||
+        r.env.method != method) {
+        close();
+        return EPROTO;
+    }
+    *resp = std::move(r);
+    return 0;
+}
+
+int Server::start(const std::string &path) {
+    if (listener_.valid()) return EALREADY;
+    sockaddr_un addr;
+    if (int rc = make_address(path, &addr); rc != 0) return rc;
+    Fd s(::socket(AF_UNIX, SOCK_SEQPACKET | SOCK_CLOEXEC | SOCK_NONBLOCK, 0));
+    if (!s.valid()) return errno;
+    if (::bind(s.get(), reinterpret_cast<sockaddr *>(&addr), sizeof(addr)) != 0) {
+        if (errno != EADDRINUSE) return errno;
+        // Replace only a stale socket: something that is a socket but refuses connections.
+        struct stat st {};
+        if (::lstat(path.c_str(), &st) != 0 || !S_ISSOCK(st.st_mode)) return EADDRINUSE;
+        Fd probe(::socket(AF_UNIX, SOCK_SEQPACKET | SOCK_CLOEXEC, 0));
+        if (probe.valid() &&
+            ::connect(probe.get(), reinterpret_cast<sockaddr *>(&addr), sizeof(addr)) == 0)
+            return EADDRINUSE;
+        ::unlink(path.c_str());
+        if (::bind(s.get(), reinterpret_cast<sockaddr *>(&addr), sizeof(addr)) != 0) return errno;
+    }
+    if (::listen(s.get(), 64) != 0) {
+        const int err = errno;
+        ::unlink(path.c_str());
+        return err;
+    }
+    struct stat st {};
+    if (::stat(path.c_str(), &st) == 0) {
+        sock_dev_ = st.st_dev;
+        sock_ino_ = st.st_ino;
+    }
+    listener_ = std::move(s);
+    path_ = path;
+    return 0;
+}
+
+void Server::drop(int fd) noexcept {
+    auto it = sessions_.find(fd);
+    if (it == sessions_.end()) return;
+    const SessionId id = it->second.id;
+    sessions_.erase(it);
+    handler_.on_disconnect(id);
+}
+
+int Server::poll_once(int timeout_ms) {
+    if (!listener_.valid()) return EBADF;
+    std::vector<pollfd> pfds;
+    pfds.reserve(sessions_.size() + 1);
+    pfds.push_back({listener_.get(), POLLIN, 0});
+    for (const auto &kv : sessions_) pfds.push_back({kv.first, POLLIN, 0});
+    int n = ::poll(pfds.data(), pfds.size(), timeout_ms);
+    if (n < 0) return errno == EINTR ? 0 : errno;
+    if (n == 0) return 0;
+    for (size_t i = 1; i < pfds.size(); ++i) {
+        const int fd = pfds[i].fd;
+        if (pfds[i].revents == 0) continue;
+        if ((pfds[i].revents & POLLIN) != 0) {
+            Message req;
+            const int rc = recv_message(fd, &req);
+            if (rc != 0 || (req.env.flags & kFlagResponse) != 0) {
+                drop(fd);
+                continue;
+            }
+            auto it = sessions_.find(fd);
+            if (it == sessions_.end()) continue;
+            const uint32_t method = req.env.method;
+            const uint64_t request_id = req.env.request_id;
+            Message resp = handler_.handle(it->second.id, std::move(req));
+            resp.env.method = method;
+            resp.env.request_id = request_id;
+            resp.env.flags = kFlagResponse;
+            if (send_message(fd, resp) != 0) drop(fd);
+        } else {
+            drop(fd);  // HUP / ERR without data
+        }
+    }
+    if ((pfds[0].revents & POLLIN) != 0) {
+        for (;;) {
+            int c = ::accept4(listener_.get(), nullptr, nullptr, SOCK_CLOEXEC);
+            if (c < 0) break;
+            sessions_.emplace(c, Session{Fd(c), next_session_++});
+        }
+    }
+    return 0;
+}
+
+void Server::close() noexcept {
+    std::vector<int> fds;
+    for (const auto &kv : sessions_) fds.push_back(kv.first);
+    for (int fd : fds) drop(fd);
+    if (listener_.valid()) {
+        listener_.reset();
+        struct stat st {};
+        if (!path_.empty() && ::stat(path_.c_str(), &st) == 0 && st.st_dev == sock_dev_ &&
+            st.st_ino == sock_ino_)
+            ::unlink(path_.c_str());
+    }
+}
+
+}  // namespace ugdr::ipc

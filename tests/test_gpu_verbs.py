@@ -1,0 +1,187 @@
+"""GPU data path through the public verbs API: the sm_100a executor against byte-exact
+expectations (the same checks the CPU engine passes in test_cpu_engine.py)."""
+from __future__ import annotations
+
+import pytest
+
+from conftest import gpu_count
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def gpu_env():
+    if gpu_count() < 1:
+        pytest.skip("no GPU")
+    from ugdr_b200 import verbs as V
+
+    torch.cuda.set_device(0)
+    d = V.Daemon(gpus=1)
+    yield V
+    d.stop()
+
+
+def _setup(V, N, depth=256, max_sge=1, access=None):
+    access = access or (N.ACCESS_REMOTE_WRITE | N.ACCESS_REMOTE_READ | N.ACCESS_REMOTE_ATOMIC)
+    ctx = V.Context(V.find_device(gpu=0))
+    pd = ctx.alloc_pd()
+    cq = ctx.create_cq(depth * 2)
+    a = pd.create_qp(cq, max_send_wr=depth, max_send_sge=max_sge, max_recv_wr=depth)
+    b = pd.create_qp(cq, max_send_wr=depth, max_send_sge=max_sge, max_recv_wr=depth)
+    V.connect_pair(a, b, access=access)
+    return ctx, pd, cq, a, b
+
+
+ACC_ALL = None
+
+
+def _acc(N):
+    return N.ACCESS_LOCAL_WRITE | N.ACCESS_REMOTE_WRITE | N.ACCESS_REMOTE_READ | N.ACCESS_REMOTE_ATOMIC
+
+
+@pytest.mark.parametrize("size,soff,doff", [(8, 0, 0), (1, 3, 5), (4096, 0, 0), (4097, 1, 1),
+                                            (65536, 16, 32), (1 << 20, 7, 3), ((32 << 20) + 5, 0, 16)])
+def test_write_read_sizes(gpu_env, size, soff, doff):
+    V = gpu_env
+    from ugdr_b200 import _native as N
+
+    ctx, pd, cq, a, b = _setup(V, N)
+    n = size + 64
+    g = torch.Generator(device="cuda").manual_seed(size)
+    src = torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda", generator=g)
+    dst = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    back = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    ms, md, mb = (pd.reg_mr(t.data_ptr(), n, _acc(N)) for t in (src, dst, back))
+    a.post_write((src.data_ptr() + soff, size, ms.lkey), dst.data_ptr() + doff, md.rkey, wr_id=7)
+    wc = cq.wait(1, 60)[0]
+    assert (wc.status, wc.wr_id, wc.opcode, wc.byte_len) == (N.WC_SUCCESS, 7, N.WC_RDMA_WRITE, size)
+    a.post_read((back.data_ptr() + soff, size, mb.lkey), dst.data_ptr() + doff, md.rkey, wr_id=8)
+    wc = cq.wait(1, 60)[0]
+    assert (wc.status, wc.opcode) == (N.WC_SUCCESS, N.WC_RDMA_READ)
+    torch.cuda.synchronize()
+    exp = torch.zeros_like(dst)
+    exp[doff:doff + size] = src[soff:soff + size]
+    assert torch.equal(dst, exp), "WRITE payload or guard bytes wrong"
+    exp2 = torch.zeros_like(back)
+    exp2[soff:soff + size] = src[soff:soff + size]
+    assert torch.equal(back, exp2), "READ payload or guard bytes wrong"
+
+
+def test_multi_sge_gather_and_imm(gpu_env):
+    V = gpu_env
+    from ugdr_b200 import _native as N
+
+    ctx, pd, cq, a, b = _setup(V, N, max_sge=16)
+    import random
+
+    rng = random.Random(3)
+    sizes = [int(2 ** rng.uniform(6, 16)) for _ in range(16)]
+    total = sum(sizes)
+    src = torch.randint(0, 256, (total + 4096 * 16,), dtype=torch.uint8, device="cuda")
+    dst = torch.zeros(total + 256, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    ms, md = pd.reg_mr(src.data_ptr(), src.numel(), _acc(N)), pd.reg_mr(dst.data_ptr(), dst.numel(), _acc(N))
+    sges, off, pieces = [], 0, []
+    for i, s in enumerate(sizes):
+        sges.append((src.data_ptr() + off, s, ms.lkey))
+        pieces.append(src[off:off + s])
+        off += s + 4096
+    b.post_recv(wr_id=555)
+    a.post_send(N.WR_RDMA_WRITE_WITH_IMM, sges, remote_addr=dst.data_ptr() + 128, rkey=md.rkey,
+                wr_id=9, imm=0xABCD1234)
+    wcs = cq.wait(2, 60)
+    by_op = {w.opcode: w for w in wcs}
+    send, recv = by_op[N.WC_RDMA_WRITE], by_op[N.WC_RECV_RDMA_WITH_IMM]
+    assert send.status == N.WC_SUCCESS and send.wr_id == 9
+    assert recv.status == N.WC_SUCCESS and recv.wr_id == 555 and recv.byte_len == total
+    assert recv.imm_data == 0xABCD1234 and recv.wc_flags & N.WC_WITH_IMM and recv.qp_num == b.qpn
+    torch.cuda.synchronize()
+    assert torch.equal(dst[128:128 + total], torch.cat(pieces))
+    assert int(dst[:128].sum()) == 0 and int(dst[128 + total:].sum()) == 0
+
+
+def test_atomics(gpu_env):
+    V = gpu_env
+    from ugdr_b200 import _native as N
+
+    ctx, pd, cq, a, b = _setup(V, N)
+    ctr = torch.zeros(4096, dtype=torch.int64, device="cuda")
+    ctr[5] = 100
+    old = torch.zeros(64, dtype=torch.int64, device="cuda")
+    torch.cuda.synchronize()
+    mc, mo = pd.reg_mr(ctr.data_ptr(), ctr.numel() * 8, _acc(N)), pd.reg_mr(old.data_ptr(), 512, _acc(N))
+    for i in range(10):
+        a.post_send(N.WR_ATOMIC_FETCH_AND_ADD, [(old.data_ptr() + 8 * i, 8, mo.lkey)],
+                    remote_addr=ctr.data_ptr() + 40, rkey=mc.rkey, compare_add=3, wr_id=i)
+    wcs = cq.wait(10, 60)
+    assert all(w.status == N.WC_SUCCESS and w.opcode == N.WC_FETCH_ADD for w in wcs)
+    torch.cuda.synchronize()
+    assert int(ctr[5]) == 130
+    assert old[:10].tolist() == [100 + 3 * i for i in range(10)]
+    # compare-and-swap: succeeds once, then fails (value already swapped)
+    for i, cmp in enumerate((130, 130)):
+        a.post_send(N.WR_ATOMIC_CMP_AND_SWP, [(old.data_ptr() + 8 * (20 + i), 8, mo.lkey)],
+                    remote_addr=ctr.data_ptr() + 40, rkey=mc.rkey, compare_add=cmp, swap=7, wr_id=50 + i)
+    wcs = cq.wait(2, 60)
+    assert all(w.status == N.WC_SUCCESS and w.opcode == N.WC_COMP_SWAP for w in wcs)
+    torch.cuda.synchronize()
+    assert int(ctr[5]) == 7 and old[20:22].tolist() == [130, 7]
+
+
+def test_remote_access_error_and_flush(gpu_env):
+    V = gpu_env
+    from ugdr_b200 import _native as N
+
+    ctx, pd, cq, a, b = _setup(V, N)
+    src = torch.ones(4096, dtype=torch.uint8, device="cuda")
+    dst = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    ms = pd.reg_mr(src.data_ptr(), 4096, _acc(N))
+    md = pd.reg_mr(dst.data_ptr(), 4096, N.ACCESS_LOCAL_WRITE)  # no remote write
+    b.post_recv(wr_id=77)
+    a.post_write((src.data_ptr(), 64, ms.lkey), dst.data_ptr(), md.rkey, wr_id=1)
+    a.post_write((src.data_ptr(), 64, ms.lkey), dst.data_ptr(), md.rkey, wr_id=2, signaled=False)
+    wcs = cq.wait(2, 60)
+    assert wcs[0].wr_id == 1 and wcs[0].status == N.WC_REM_ACCESS_ERR
+    assert wcs[1].wr_id == 2 and wcs[1].status == N.WC_WR_FLUSH_ERR
+    attr, _ = a.query()
+    assert attr.qp_state == N.QPS_ERR
+    b.to_error()
+    w = cq.wait(1, 60)[0]
+    assert w.wr_id == 77 and w.status == N.WC_WR_FLUSH_ERR
+    torch.cuda.synchronize()
+    assert int(dst.sum()) == 0
+
+
+def test_many_qps_queue_depth(gpu_env):
+    V = gpu_env
+    from ugdr_b200 import _native as N
+
+    ctx = V.Context(V.find_device(gpu=0))
+    pd = ctx.alloc_pd()
+    cq = ctx.create_cq(4096)
+    qps = [pd.create_qp(cq, max_send_wr=64) for _ in range(32)]
+    for i in range(0, 32, 2):
+        V.connect_pair(qps[i], qps[i + 1])
+    n = 1 << 16
+    src = torch.randint(0, 256, (n * 16,), dtype=torch.uint8, device="cuda")
+    dst = torch.zeros(n * 16 * 64, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    ms, md = pd.reg_mr(src.data_ptr(), src.numel(), _acc(N)), pd.reg_mr(dst.data_ptr(), dst.numel(), _acc(N))
+    k = 0
+    for d in range(64):
+        for q in range(0, 32, 2):
+            qps[q].post_write((src.data_ptr() + (q // 2) * n, n, ms.lkey),
+                              dst.data_ptr() + k * n, md.rkey, wr_id=k)
+            k += 1
+    wcs = cq.wait(k, 120)
+    assert sorted(w.wr_id for w in wcs) == list(range(k))
+    assert all(w.status == N.WC_SUCCESS for w in wcs)
+    torch.cuda.synchronize()
+    view = dst.view(k, n)
+    for i in (0, 1, 17, k - 1):
+        q = (i % 16)
+        assert torch.equal(view[i], src[q * n:(q + 1) * n])
