@@ -17,7 +17,7 @@ LIB_CXX := \
   csrc/common/shm.cpp csrc/queue/ring.cpp csrc/ipc/ipc.cpp \
   csrc/control/rpc.cpp csrc/control/service.cpp csrc/control/client.cpp \
   csrc/api/posting.cpp csrc/api/runtime.cpp csrc/api/memory_export.cpp \
-  csrc/engine/cpu_engine.cpp csrc/gpu/cuda_memory.cpp csrc/gpu/gpu_engine.cpp \
+  csrc/engine/cpu_engine.cpp csrc/gpu/cuda_memory.cpp csrc/gpu/gpu_engine.cpp csrc/gpu/diag.cpp \
   csrc/daemon/daemon.cpp
 LIB_CU  := csrc/gpu/executor.cu
 

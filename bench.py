@@ -2,12 +2,13 @@
 """Headline benchmark: all-pairs RDMA WRITE bandwidth through the ugdr verbs API.
 
 Workload (weak-scaled): every GPU holds one 256 MiB bf16 MR (N(0,1),
-seeded by rank) split in eight 32 MiB slots.  One step = every GPU RDMA_WRITEs its own slot
-(slot = rank) to 7 destinations over 7 QPs: WR k of rank r goes to GPU (r + 1 + k) % N into that
-GPU's slot (dst + 1 + k) % 8, which is never the destination's own source slot, so reads and
-writes never overlap.  With N = 8 this is exactly "a 32 MiB slice to each of its 7 peers"; with
-fewer GPUs the same 7 x 32 MiB per GPU cycle over the available peers (N = 1: loopback copies
-inside one GPU).  Per-GPU work is fixed, so scaling is weak.
+seeded by rank) of eight 32 MiB slices, plus a 256 MiB receive MR.  One step = every GPU
+RDMA_WRITEs 7 distinct slices over 7 QPs: WR k of rank r sends slice k to GPU (r + 1 + k) % N,
+into that GPU's receive slot (dst + 1 + k) % 8, so every inbound WR of a step lands in its own
+slot.  With N = 8 this is exactly "a 32 MiB slice to each of its 7 peers"; with fewer GPUs the
+same 7 x 32 MiB per GPU cycle over the available peers (N = 1: loopback copies inside one GPU).
+Per-GPU work is fixed, so scaling is weak; each step reads 224 MiB and writes 224 MiB per GPU,
+more than the 126 MB L2.
 
 `value` is device-timed: the daemon launches every GPU's executor together for the K timed steps
 (all WRs of the K steps are queued first), brackets each launch with CUDA events on its
@@ -107,16 +108,20 @@ def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None
     ctx = V.Context(V.find_device(gpu=local))
     pd = ctx.alloc_pd()
     cq = ctx.create_cq(2 * PEERS * depth + 64)
+    # Source MR: 256 MiB of N(0,1) bf16 seeded by rank; WR k reads its own slice k, so one step
+    # reads 7 distinct 32 MiB slices (224 MiB, larger than L2).  Receive MR: where peers write.
     gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
-    buf = torch.randn(total // 2, dtype=torch.bfloat16, device="cuda", generator=gen)
+    src_buf = torch.randn(total // 2, dtype=torch.bfloat16, device="cuda", generator=gen)
+    rcv_buf = torch.zeros(total // 2, dtype=torch.bfloat16, device="cuda")
     torch.cuda.synchronize()
     acc = N.ACCESS_LOCAL_WRITE | N.ACCESS_REMOTE_WRITE
-    mr = pd.reg_mr(buf.data_ptr(), total, acc)
+    src_mr = pd.reg_mr(src_buf.data_ptr(), total, acc)
+    rcv_mr = pd.reg_mr(rcv_buf.data_ptr(), total, acc)
     req = [pd.create_qp(cq, max_send_wr=depth) for _ in range(PEERS)]
     rsp = [pd.create_qp(cq, max_send_wr=4) for _ in range(PEERS)]
     for q in req + rsp:
         q.to_init(N.ACCESS_REMOTE_WRITE)
-    info = comm.gather({"addr": buf.data_ptr(), "rkey": mr.rkey,
+    info = comm.gather({"addr": rcv_buf.data_ptr(), "rkey": rcv_mr.rkey,
                         "rsp": [q.qpn for q in rsp], "req": [q.qpn for q in req]})
     for k in range(PEERS):
         dst = (rank + 1 + k) % world
@@ -129,7 +134,7 @@ def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None
         for k in range(PEERS):
             dst = (rank + 1 + k) % world
             dslot = (dst + 1 + k) % SLOTS
-            req[k].post_write((buf.data_ptr() + (rank % SLOTS) * slot, slot, mr.lkey),
+            req[k].post_write((src_buf.data_ptr() + k * slot, slot, src_mr.lkey),
                               info[dst]["addr"] + dslot * slot, info[dst]["rkey"],
                               wr_id=(step_id << 8) | k)
 
@@ -154,30 +159,38 @@ def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None
         ctx.hold(False)
         return ms
 
-    # Warm-up (untimed), then verify one destination slot per inbound WR.
+    # Warm-up (untimed), then verify every inbound slot against the sender's source slice.
     drain(W)
     comm.barrier()
     torch.cuda.synchronize()
     ok = True
-    bytes_view = buf.view(torch.uint8)
+    rcv_bytes = rcv_buf.view(torch.uint8)
     for k in range(PEERS):
         src = (rank - 1 - k) % world
         dslot = (rank + 1 + k) % SLOTS
         g = torch.Generator(device="cuda").manual_seed(1234 + src)
         ref = torch.randn(total // 2, dtype=torch.bfloat16, device="cuda", generator=g).view(torch.uint8)
-        sslot = src % SLOTS
-        ok &= torch.equal(bytes_view[dslot * slot:(dslot + 1) * slot], ref[sslot * slot:(sslot + 1) * slot])
+        ok &= torch.equal(rcv_bytes[dslot * slot:(dslot + 1) * slot], ref[k * slot:(k + 1) * slot])
         del ref
     ok = all(comm.gather(bool(ok)))
 
     # Device-timed region.
     sampler = ClockSampler(list(range(world))) if rank == 0 else None
+    if all_ctx:
+        for c in all_ctx:
+            c.stats(reset=True)
     if sampler:
         sampler.__enter__()
     t_ms = drain(K)
     if sampler:
         sampler.__exit__(None, None, None)
     clocks = sampler.summary() if sampler else None
+    diag = None
+    if all_ctx:
+        diag = []
+        for c in all_ctx:
+            st = c.stats()
+            diag.append({f: int(getattr(st, f)) for f, _ in st._fields_})
 
     # End-to-end through the public API (persistent executors).
     for s in range(W):
@@ -198,7 +211,8 @@ def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None
     comm.barrier()
     for q in req + rsp:
         q.destroy()
-    mr.dereg()
+    src_mr.dereg()
+    rcv_mr.dereg()
     cq.destroy()
     pd.dealloc()
     ctx.close()
@@ -206,8 +220,10 @@ def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None
         for c in all_ctx:
             c.close()
     comm.barrier()
+    daemon_log = ""
     if daemon:
         daemon.stop()
+        daemon_log = daemon.log_text()
     if rank != 0:
         return None
     wqe_bytes = 64  # one 64-byte send slot per WR (40 B header + 1 SGE, rounded)
@@ -231,7 +247,7 @@ def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None
             "seq_len": slot,
             "parallelism": f"{world} GPU(s) x {PEERS} QPs, 32 MiB per WR",
             "mr_bytes_per_gpu": total,
-            "l2": "inputs larger than L2: 224 MiB read + 224 MiB written per GPU per step",
+            "l2": "inputs larger than L2: 7 distinct 32 MiB source slices (224 MiB) read + 224 MiB written per GPU per step",
             "timing": "CUDA events around each GPU's executor launch, max over GPUs",
             "correct": bool(ok),
         },
@@ -242,6 +258,8 @@ def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None
                 "path": "ugdr_post_send -> persistent executor -> ugdr_poll_cq, wall clock, max over ranks"},
         "gpu_launches": world,
         "executor_launches_rank0": int(stats.launches),
+        "engine_stats_timed": diag,
+        "daemon_log_tail": daemon_log[-2000:] if daemon_log else "",
     }
 
 

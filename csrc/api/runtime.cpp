@@ -513,7 +513,9 @@ int ugdr_x_query_engine_stats(ugdr_context *ctx, ugdr_x_engine_stats *stats, int
     ByteReader rd(resp.opaque);
     if (!rd.be(&stats->wrs_completed) || !rd.be(&stats->bytes_moved) ||
         !rd.be(&stats->error_completions) || !rd.be(&stats->launches) ||
-        !rd.be(&stats->wait_timeouts) || !rd.be(&stats->first_start_ns) || !rd.be(&stats->last_end_ns))
+        !rd.be(&stats->wait_timeouts) || !rd.be(&stats->first_start_ns) || !rd.be(&stats->last_end_ns) ||
+        !rd.be(&stats->chunks_run) || !rd.be(&stats->claim_misses) || !rd.be(&stats->jobs_published) ||
+        !rd.be(&stats->inline_runs) || !rd.be(&stats->busy_ns))
         return EPROTO;
     return 0;
 }

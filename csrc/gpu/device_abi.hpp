@@ -118,12 +118,16 @@ struct DevQp {
     DevQpState st;
 };
 
-struct Job {
-    unsigned long long ctl;  // ticket (high 32) | next chunk (low 32)
-    WrRec *rec;
+// One chunked WR.  `ctl` = generation (high 32) | next unclaimed chunk (low 32); claims are
+// fetch-and-adds on it.  `seq` is even while the slot is free and odd while a job owns it; the
+// slot is freed only when every chunk is done, so the fields below never change under a worker
+// that holds an unfinished chunk.
+struct alignas(64) Job {
+    unsigned long long ctl;
+    unsigned long long seq;
+    WrRec *rec;  // 16-byte aligned with the two words after it: read as one vector
     uint32_t nchunks;
     uint32_t chunk_bytes;
-    unsigned long long seq;  // ticket for which the slot is free
     unsigned long long pad[4];
 };
 
@@ -144,6 +148,12 @@ struct DevStats {
     unsigned long long wait_timeouts;
     unsigned long long first_start_ns;
     unsigned long long last_end_ns;
+    unsigned long long chunks_run;      // chunked-job pieces copied
+    unsigned long long claim_misses;    // chunk-claim attempts that found nothing to take
+    unsigned long long jobs_published;  // WRs split into chunks
+    unsigned long long inline_runs;     // WRs copied by their owner warp
+    unsigned long long busy_ns;         // summed warp time inside chunk copies
+    unsigned long long launches_seen;   // kernel launches (block 0 thread 0)
     unsigned long long last_work_ns;
     unsigned long long retired;  // WRs retired since the last reset (drain mode exit test)
     unsigned int exiting;

@@ -38,8 +38,8 @@ namespace {
 constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
 constexpr uint32_t kWqeBytesMax = 576;  // roundup64(40 + 16 * 32)
-constexpr uint32_t kChunkMin = 4096;
-constexpr uint32_t kChunkMax = 65536;
+constexpr uint32_t kChunkMin = 16384;
+constexpr uint32_t kChunkMax = 262144;
 
 // ---- memory-model helpers --------------------------------------------------------------------
 
@@ -161,12 +161,14 @@ __device__ void copy_stream(const WrRec *rec, uint32_t nseg, uint64_t remote, bo
                             uint64_t off, uint64_t len, int lane) {
     uint64_t seg_start = 0;
     for (uint32_t i = 0; i < nseg && len > 0; ++i) {
-        const uint64_t sl = rec->seg[i].length;
+        const uint64_t sl = __ldcg(reinterpret_cast<const unsigned long long *>(&rec->seg[i].length));
         if (off < seg_start + sl) {
             const uint64_t in = off - seg_start;
             uint64_t take = sl - in;
             if (take > len) take = len;
-            uint8_t *local = reinterpret_cast<uint8_t *>(rec->seg[i].local) + in;
+            uint8_t *local = reinterpret_cast<uint8_t *>(
+                                 __ldcg(reinterpret_cast<const unsigned long long *>(&rec->seg[i].local))) +
+                             in;
             uint8_t *rem = reinterpret_cast<uint8_t *>(remote) + off;
             if (to_remote)
                 warp_copy(rem, local, take, lane);
@@ -188,6 +190,9 @@ struct Warp {
     uint32_t gwarp; // global warp index
     uint32_t rot;   // job-slot rotation seed
     bool abort;
+    // Private counters, folded into DevStats now and then (hot shared counters would serialise
+    // every warp of the grid on one L2 line).
+    uint64_t n_chunks, n_miss, bytes, busy;
 };
 
 __device__ void record_error(Warp &w, uint32_t code) {
@@ -298,7 +303,7 @@ __device__ bool publish_job(JobRing *jr, uint32_t *bitmap, WrRec *rec, uint32_t 
     for (uint32_t k = 0; k < 64; ++k) {
         const uint32_t s = (seed * 37u + k * 97u) % kJobSlots;
         Job *j = &jr->slots[s];
-        // slot free <=> its seq word is even; odd = in use (seq doubles as a generation).
+        // Slot free <=> seq even; taking it makes seq odd.  gen = (seq + 1) / 2 is new each time.
         const unsigned long long seq = ld_vol(&j->seq);
         if ((seq & 1ull) != 0) continue;
         if (atomicCAS(&j->seq, seq, seq + 1) != seq) continue;
@@ -315,75 +320,105 @@ __device__ bool publish_job(JobRing *jr, uint32_t *bitmap, WrRec *rec, uint32_t 
     return false;
 }
 
-// Claim one chunk from any active job (warp-wide).  Returns true with the chunk's record.
-__device__ bool claim_chunk(Warp &w, JobRing *jr, uint32_t *bitmap, WrRec **rec_out,
-                            uint32_t *chunk_out, uint32_t *cb_out) {
-    const uint32_t word = ld_vol32(&bitmap[w.lane]);
-    uint32_t nonzero = __ballot_sync(0xffffffffu, word != 0);
+struct Claim {
+    WrRec *rec;
+    Job *job;
+    uint32_t chunk, cb, n;
+};
+
+// Claim one chunk from any active job (warp-wide): a fetch-and-add on the job's counter, which
+// always yields a unique index (no CAS retry storms when thousands of warps contend).
+//  * The fields are read before the add; if the add returns the same generation, no recycle
+//    happened in between, so the fields belong to it (a slot is recycled only after all of its
+//    chunks are done, which cannot be while our index is below nchunks).
+//  * If the add lands in a newer generation, the index belongs to that job: re-read its fields
+//    (stable for the same reason) and run it, so no index is ever lost.
+// `mirror` is the CTA's shared copy of the active-job bitmap (refreshed by the CTA leader).
+__device__ bool claim_chunk(Warp &w, JobRing *jr, uint32_t *bitmap, const volatile uint32_t *mirror,
+                            Claim *out) {
+    const uint32_t word = mirror[w.lane];
+    const uint32_t nonzero = __ballot_sync(0xffffffffu, word != 0);
     if (nonzero == 0) return false;
-    bool got = false;
-    WrRec *rec = nullptr;
-    uint32_t chunk = 0, cb = 0;
+    int got = 0;
+    Claim cl{};
     if (w.lane == 0) {
         // Rotate the starting word / bit per warp so warps spread over active jobs.
-        for (int tries = 0; tries < 4 && !got; ++tries) {
-            const uint32_t rotw = (w.rot + tries) & 31;
-            const uint32_t nz = (nonzero >> rotw) | (nonzero << ((32 - rotw) & 31));
-            if (nz == 0) break;
-            const uint32_t wsel = (rotw + __ffs(nz) - 1) & 31;
-            uint32_t bits = ld_vol32(&bitmap[wsel]);
-            if (bits == 0) {
-                nonzero &= ~(1u << wsel);
-                continue;
-            }
+        const uint32_t rotw = w.rot & 31;
+        const uint32_t nz = (nonzero >> rotw) | (nonzero << ((32 - rotw) & 31));
+        const uint32_t wsel = (rotw + __ffs(nz) - 1) & 31;
+        const uint32_t bits = mirror[wsel];
+        if (bits != 0) {
             const uint32_t rb = (w.rot >> 5) & 31;
             const uint32_t rotated = (bits >> rb) | (bits << ((32 - rb) & 31));
             const uint32_t b = (rb + __ffs(rotated) - 1) & 31;
             Job *j = &jr->slots[wsel * 32 + b];
-            const unsigned long long v = ld_vol(&j->ctl);
-            const uint32_t n = ld_vol32(&j->nchunks);
-            const uint32_t c = uint32_t(v);
-            WrRec *r = reinterpret_cast<WrRec *>(ld_vol(&j->rec));
-            const uint32_t chb = ld_vol32(&j->chunk_bytes);
-            if (c >= n) continue;
-            if (atomicCAS(&j->ctl, v, v + 1) != v) continue;
-            got = true;
-            rec = r;
-            chunk = c;
-            cb = chb;
-            if (c + 1 == n) {
-                // Last chunk handed out: retire the slot.
-                atomicAnd(&bitmap[wsel], ~(1u << b));
-                __threadfence();
-                atomicAdd(&j->seq, 1ull);
+            const unsigned long long v0 = ld_vol(&j->ctl);
+            const uint4 f = ld_vol128(&j->rec);  // rec (x,y), nchunks (z), chunk_bytes (w)
+            if (uint32_t(v0) < f.z) {
+                const unsigned long long v = atomicAdd(&j->ctl, 1ull);
+                uint4 g = f;
+                if ((v >> 32) != (v0 >> 32)) g = ld_vol128(&j->rec);  // newer generation
+                const uint32_t c = uint32_t(v);
+                if (c < g.z) {
+                    got = 1;
+                    cl.rec = reinterpret_cast<WrRec *>((uint64_t(g.y) << 32) | g.x);
+                    cl.job = j;
+                    cl.chunk = c;
+                    cl.n = g.z;
+                    cl.cb = g.w;
+                    if (c + 1 == g.z) atomicAnd(&bitmap[wsel], ~(1u << b));  // all handed out
+                }
             }
         }
         w.rot = w.rot * 1664525u + 1013904223u;
     }
     w.rot = __shfl_sync(0xffffffffu, w.rot, 0);
-    got = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
-    if (!got) return false;
-    *rec_out = reinterpret_cast<WrRec *>(bcast64(reinterpret_cast<uint64_t>(rec)));
-    *chunk_out = bcast(chunk);
-    *cb_out = bcast(cb);
+    got = __shfl_sync(0xffffffffu, got, 0);
+    if (!got) {
+        w.n_miss += 1;
+        return false;
+    }
+    out->rec = reinterpret_cast<WrRec *>(bcast64(reinterpret_cast<uint64_t>(cl.rec)));
+    out->job = reinterpret_cast<Job *>(bcast64(reinterpret_cast<uint64_t>(cl.job)));
+    out->chunk = bcast(cl.chunk);
+    out->cb = bcast(cl.cb);
+    out->n = bcast(cl.n);
     return true;
 }
 
-__device__ void run_chunk(Warp &w, WrRec *rec, uint32_t chunk, uint32_t cb) {
+__device__ void run_chunk(Warp &w, const Claim &cl) {
+    WrRec *rec = cl.rec;
     const uint64_t total = ld_vol(&rec->total);
-    const uint64_t off = uint64_t(chunk) * cb;
+    const uint64_t off = uint64_t(cl.chunk) * cl.cb;
     uint64_t len = total - off;
-    if (len > cb) len = cb;
+    if (len > cl.cb) len = cl.cb;
     const uint32_t op = ld_vol32(&rec->opcode);
     const uint32_t nseg = ld_vol32(&rec->nseg);
     const uint64_t remote = ld_vol(&rec->remote);
+    const uint64_t t0 = gtime();
     copy_stream(rec, nseg, remote, op != UGDR_WR_RDMA_READ, off, len, w.lane);
     __syncwarp();
     if (w.lane == 0) {
-        __threadfence_system();
-        atomicAdd(&rec->chunks_done, 1u);
-        atomicAdd(&w.p->stats->bytes_moved, (unsigned long long)len);
+        // Device-scope release is enough here: the owner warp acquires chunks_done and issues
+        // the system-scope fence before it publishes the CQE, and causality is transitive.
+        __threadfence();
+        const uint32_t done = atomicAdd(&rec->chunks_done, 1u) + 1;
+        if (done == cl.n) atomicAdd(&cl.job->seq, 1ull);  // every chunk done: free the slot
     }
+    w.n_chunks += 1;
+    w.bytes += len;
+    w.busy += gtime() - t0;
+}
+
+// Fold the warp's private counters into DevStats (lane 0).
+__device__ void flush_counters(Warp &w) {
+    if (w.lane == 0) {
+        if (w.n_chunks) atomicAdd(&w.p->stats->chunks_run, (unsigned long long)w.n_chunks);
+        if (w.n_miss) atomicAdd(&w.p->stats->claim_misses, (unsigned long long)w.n_miss);
+        if (w.bytes) atomicAdd(&w.p->stats->bytes_moved, (unsigned long long)w.bytes);
+        if (w.busy) atomicAdd(&w.p->stats->busy_ns, (unsigned long long)w.busy);
+    }
+    w.n_chunks = w.n_miss = w.bytes = w.busy = 0;
 }
 
 // ---- per-QP service ----------------------------------------------------------------------------
@@ -728,9 +763,12 @@ __device__ uint32_t service_qp(Warp &w, DevQp *qp, uint8_t *wqe_smem, JobRing *j
         if (status == UGDR_WC_SUCCESS) {
             if (is_atomic(op) || total <= kInlineBytes) {
                 run_inline(w, rec, wqe_smem, op, total, remote);
+                if (w.lane == 0) atomicAdd(&w.p->stats->inline_runs, 1ull);
             } else {
-                // Chunk so one WR spreads over about every warp, within [4 KiB, 64 KiB].
-                uint64_t cb = total / nwarps;
+                // Chunk so one WR spreads over about half the warps, within [16 KiB, 256 KiB]:
+                // large enough that claims are rare next to the copy, small enough that a lone
+                // WR still reaches most SMs.
+                const uint64_t cb = total / (nwarps / 2 + 1);
                 uint32_t chunk = kChunkMin;
                 while (chunk < cb && chunk < kChunkMax) chunk <<= 1;
                 const uint32_t n = uint32_t((total + chunk - 1) / chunk);
@@ -740,6 +778,7 @@ __device__ uint32_t service_qp(Warp &w, DevQp *qp, uint8_t *wqe_smem, JobRing *j
                     __threadfence();
                     ok = publish_job(jr, bitmap, rec, n, chunk, w.gwarp + uint32_t(issue));
                     if (!ok) rec->nchunks = 0;
+                    else atomicAdd(&w.p->stats->jobs_published, 1ull);
                 }
                 issued = bcast(ok ? 1 : 0) != 0;
             }
@@ -756,8 +795,15 @@ __device__ uint32_t service_qp(Warp &w, DevQp *qp, uint8_t *wqe_smem, JobRing *j
     return work;
 }
 
+// Warp 0 of every CTA is its leader: it services its own QPs and, about every microsecond,
+// mirrors the global control words (job bitmap, QP-slot bound, exit / stop / drain state) into
+// shared memory.  Warps 1..15 service their QPs and copy chunks, reading only the mirror when
+// idle.  Without the mirror every warp of the grid polled the same few L2 lines and every
+// data access hashing to those slices queued behind the polls.
 __global__ void __launch_bounds__(kThreads, 1) executor_kernel(ExecParams p) {
     __shared__ __align__(16) uint8_t wqe_buf[kWarps][kWqeBytesMax];
+    __shared__ volatile uint32_t s_bits[32];
+    __shared__ volatile uint32_t s_slots, s_exit, s_work;
     Warp w;
     w.p = &p;
     w.lane = threadIdx.x & 31;
@@ -765,51 +811,95 @@ __global__ void __launch_bounds__(kThreads, 1) executor_kernel(ExecParams p) {
     w.gwarp = blockIdx.x * kWarps + w.wi;
     w.rot = w.gwarp * 2654435761u;
     w.abort = false;
+    w.n_chunks = w.n_miss = w.bytes = w.busy = 0;
     const uint32_t nwarps = gridDim.x * kWarps;
     JobRing *jr = p.jobs;
     // Active-job bitmap: 32 words right after the ring (see job_ring_bytes()).
     uint32_t *bits = reinterpret_cast<uint32_t *>(reinterpret_cast<uint8_t *>(p.jobs) +
                                                   sizeof(JobRing));
     const uint64_t t_launch = gtime();
+    const bool leader = w.wi == 0;
+    if (threadIdx.x < 32) s_bits[threadIdx.x] = ld_vol32(&bits[threadIdx.x]);
+    if (threadIdx.x == 0) {
+        s_slots = ld_vol32(&p.stats->qp_slots);
+        s_exit = 0;
+        s_work = 0;
+        if (blockIdx.x == 0) atomicAdd(&p.stats->launches_seen, 1ull);
+    }
+    __syncthreads();
+    uint64_t t_refresh = t_launch, t_host = t_launch, t_pub = 0;
     uint32_t idle_rounds = 0;
     for (uint64_t iter = 0;; ++iter) {
         uint32_t work = 0;
         // Owned QPs: q = cta + grid * (wi + warps * k).
-        const uint32_t slots = ld_vol32(&p.stats->qp_slots);
+        const uint32_t slots = s_slots;
+        const bool owner = blockIdx.x + gridDim.x * w.wi < slots;
         for (uint32_t q = blockIdx.x + gridDim.x * w.wi; q < slots; q += gridDim.x * kWarps) {
             work += service_qp(w, &p.qps[q], wqe_buf[w.wi], jr, bits, nwarps);
-            if (w.abort) return;
+            if (w.abort) {
+                s_exit = 1;
+                flush_counters(w);
+                return;
+            }
         }
-        // Help with chunked jobs.
-        for (int k = 0; k < 8; ++k) {
-            WrRec *rec;
-            uint32_t chunk, cb;
-            if (!claim_chunk(w, jr, bits, &rec, &chunk, &cb)) break;
-            run_chunk(w, rec, chunk, cb);
-            ++work;
-        }
-        // Exit checks.
-        int exit_now = 0;
-        if (w.lane == 0) {
+        if (!leader) {
+            for (int k = 0; k < 8; ++k) {
+                Claim cl;
+                if (!claim_chunk(w, jr, bits, s_bits, &cl)) break;
+                run_chunk(w, cl);
+                ++work;
+            }
+            if (work != 0 && w.lane == 0) s_work = 1;
+        } else {
             const uint64_t now = gtime();
-            if (work != 0) {
-                if (now - ld_vol(&p.stats->last_work_ns) > 20000)
-                    atomicMax(&p.stats->last_work_ns, (unsigned long long)now);
+            if (now - t_refresh >= 2000 || work != 0) {
+                t_refresh = now;
+                s_bits[w.lane] = ld_vol32(&bits[w.lane]);
+                int exit_now = 0;
+                if (w.lane == 0) {
+                    s_slots = ld_vol32(&p.stats->qp_slots);
+                    const bool busy = work != 0 || s_work != 0;
+                    s_work = 0;
+                    // Activity stamps are rare (one per CTA per 50 us) so the shared word
+                    // stays cold.
+                    if (busy && now - t_pub >= 50000) {
+                        t_pub = now;
+                        atomicMax(&p.stats->last_work_ns, (unsigned long long)now);
+                    }
+                    if (ld_vol32(&p.stats->exiting)) exit_now = 1;
+                    if (blockIdx.x == 0) {
+                        // The grid's control leader alone evaluates the exit conditions: the
+                        // host stop flag (a PCIe read), drain completion and idleness.
+                        if (now - t_host >= 10000) {
+                            t_host = now;
+                            if (ld_acq_sys32(const_cast<uint32_t *>(&p.ctrl->stop)) != 0) exit_now = 1;
+                            if (p.mode == kPersistent && !busy) {
+                                uint64_t last = ld_vol(&p.stats->last_work_ns);
+                                if (last < t_launch) last = t_launch;
+                                // Another CTA may have stamped a time later than `now`.
+                                if (now > last && now - last > p.idle_exit_ns) exit_now = 1;
+                            }
+                        }
+                        if (p.mode == kDrain && ld_vol(&p.stats->retired) >= p.expected) exit_now = 1;
+                    }
+                    if (exit_now) {
+                        atomicExch(&p.stats->exiting, 1u);
+                        s_exit = 1;
+                    }
+                }
+                __syncwarp();
             }
-            if (ld_vol32(&p.stats->exiting)) exit_now = 1;
-            if ((iter & 31) == 0 && ld_acq_sys32(const_cast<uint32_t *>(&p.ctrl->stop)) != 0) exit_now = 1;
-            if (p.mode == kDrain && ld_vol(&p.stats->retired) >= p.expected) exit_now = 1;
-            if (p.mode == kPersistent && work == 0) {
-                uint64_t last = ld_vol(&p.stats->last_work_ns);
-                if (last < t_launch) last = t_launch;
-                if (now - last > p.idle_exit_ns) exit_now = 1;
-            }
-            if (exit_now) atomicExch(&p.stats->exiting, 1u);
         }
-        if (bcast(exit_now)) return;
+        if (s_exit) {
+            flush_counters(w);
+            return;
+        }
+        if ((iter & 1023) == 0) flush_counters(w);
         if (work == 0) {
-            idle_rounds = idle_rounds < 16 ? idle_rounds + 1 : 16;
-            __nanosleep(32u << (idle_rounds >> 2));
+            // QP owners poll quickly (latency); pure workers back off a little further.
+            const uint32_t cap = owner ? 3u : 4u;
+            idle_rounds = idle_rounds < 2 * cap ? idle_rounds + 1 : 2 * cap;
+            __nanosleep(32u << (idle_rounds >> 1));
         } else {
             idle_rounds = 0;
         }
@@ -821,7 +911,27 @@ __global__ void copy_test_kernel(uint8_t *dst, const uint8_t *src, uint64_t n) {
     warp_copy(dst, src, n, threadIdx.x & 31);
 }
 
+// Copy-core ceiling: every warp of the grid copies one contiguous stripe with warp_copy, the
+// same routine the executor's chunk workers run (no queues, no claims).
+__global__ void __launch_bounds__(kThreads, 1) grid_copy_kernel(uint8_t *dst, const uint8_t *src,
+                                                                 uint64_t n, uint64_t stripe) {
+    const uint64_t gw = uint64_t(blockIdx.x) * kWarps + (threadIdx.x >> 5);
+    const uint64_t off = gw * stripe;
+    if (off >= n) return;
+    const uint64_t len = n - off < stripe ? n - off : stripe;
+    warp_copy(dst + off, src + off, len, threadIdx.x & 31);
+}
+
 }  // namespace
+
+int launch_grid_copy(void *dst, const void *src, uint64_t n, int ctas, cudaStream_t stream) {
+    const uint64_t warps = uint64_t(ctas) * kWarps;
+    uint64_t stripe = (n + warps - 1) / warps;
+    stripe = (stripe + 15) & ~uint64_t(15);
+    grid_copy_kernel<<<ctas, kThreads, 0, stream>>>(static_cast<uint8_t *>(dst),
+                                                    static_cast<const uint8_t *>(src), n, stripe);
+    return int(cudaGetLastError());
+}
 
 size_t job_ring_bytes() { return sizeof(JobRing) + 32 * sizeof(uint32_t); }
 int executor_threads() { return kThreads; }

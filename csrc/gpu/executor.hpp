@@ -15,5 +15,7 @@ int executor_threads();
 int launch_executor(const ExecParams &p, int ctas, cudaStream_t stream);
 // One-warp copy-core test launch (alignment matrix).
 int launch_copy_test(void *dst, const void *src, uint64_t n, cudaStream_t stream);
+// Whole-grid copy with the executor's copy core (bandwidth ceiling / profiling).
+int launch_grid_copy(void *dst, const void *src, uint64_t n, int ctas, cudaStream_t stream);
 
 }  // namespace ugdr::gpu

@@ -476,6 +476,11 @@ int GpuEngine::stats(control::EngineStats *out, bool reset) {
     out->first_start_ns = st.first_start_ns;
     out->last_end_ns = st.last_end_ns;
     out->launches = launches_;
+    out->chunks_run = st.chunks_run;
+    out->claim_misses = st.claim_misses;
+    out->jobs_published = st.jobs_published;
+    out->inline_runs = st.inline_runs;
+    out->busy_ns = st.busy_ns;
     if (reset) {
         // Counters only (a running kernel may race a few increments into the fresh window).
         cudaMemsetAsync(stats_, 0, offsetof(DevStats, last_work_ns), ctl_stream_);

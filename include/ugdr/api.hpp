@@ -256,6 +256,11 @@ typedef struct ugdr_x_engine_stats {
     uint64_t wait_timeouts;
     uint64_t first_start_ns; /* device clock of the first WR picked up since the last reset */
     uint64_t last_end_ns;    /* device clock of the last completion since the last reset */
+    uint64_t chunks_run;     /* large-WR pieces copied by the GPU executor */
+    uint64_t claim_misses;   /* chunk claims that found no free piece */
+    uint64_t jobs_published; /* WRs split across the grid */
+    uint64_t inline_runs;    /* WRs copied by their owner warp */
+    uint64_t busy_ns;        /* summed warp time spent copying chunks */
 } ugdr_x_engine_stats;
 
 int ugdr_x_query_engine_stats(ugdr_context *context, ugdr_x_engine_stats *stats,

@@ -11,7 +11,7 @@ import ctypes as C
 import os
 from pathlib import Path
 
-LIB_DIR = Path(__file__).resolve().parent / "_lib"
+LIB_DIR = Path(os.environ.get("UGDR_LIB_DIR") or Path(__file__).resolve().parent / "_lib")
 LIB_PATH = LIB_DIR / "libugdr.so"
 DAEMON_PATH = LIB_DIR / "ugdr_daemon"
 
@@ -186,6 +186,11 @@ class EngineStats(C.Structure):
         ("wait_timeouts", C.c_uint64),
         ("first_start_ns", C.c_uint64),
         ("last_end_ns", C.c_uint64),
+        ("chunks_run", C.c_uint64),
+        ("claim_misses", C.c_uint64),
+        ("jobs_published", C.c_uint64),
+        ("inline_runs", C.c_uint64),
+        ("busy_ns", C.c_uint64),
     ]
 
 

@@ -1,6 +1,7 @@
 """Sample GPU clocks and throttle reasons with nvidia-smi while a timed region runs."""
 from __future__ import annotations
 
+import os
 import statistics
 import subprocess
 import tempfile
@@ -28,6 +29,16 @@ class ClockSampler:
             self.proc = subprocess.Popen(cmd, stdout=self.out, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+        # nvidia-smi needs a moment before its first sample; wait for it so a short timed region
+        # is still covered.
+        import time
+
+        deadline = time.time() + 5.0
+        while self.proc is not None and time.time() < deadline:
+            self.out.flush()
+            if os.path.getsize(self.out.name) > 0:
+                break
+            time.sleep(0.05)
         return self
 
     def __exit__(self, *exc):

@@ -47,7 +47,7 @@ class Daemon:
 
     def __init__(self, gpus: int | None = None, socket_path: str | None = None,
                  ctas: int | None = None, idle_exit_us: int | None = None,
-                 cpu_device: bool = True, env: dict | None = None):
+                 cpu_device: bool = True, env: dict | None = None, log_path: str | None = None):
         self._dir = None
         if socket_path is None:
             self._dir = tempfile.mkdtemp(prefix="ugdr-")
@@ -56,6 +56,7 @@ class Daemon:
         args = [str(N.DAEMON_PATH), "--socket", socket_path]
         if gpus is not None:
             args += ["--gpus", str(gpus)]
+        ctas = ctas if ctas is not None else os.environ.get("UGDR_EXECUTOR_CTAS")
         if ctas is not None:
             args += ["--ctas", str(ctas)]
         if idle_exit_us is not None:
@@ -64,12 +65,15 @@ class Daemon:
             args += ["--no-cpu-device"]
         if not N.DAEMON_PATH.exists():
             raise RuntimeError(f"{N.DAEMON_PATH} missing: build the native tree first")
-        self.proc = subprocess.Popen(args, env=env, stderr=subprocess.PIPE, text=True)
+        # The daemon's stderr goes to a file (a pipe nobody drains could block its threads).
+        self.log_path = log_path or os.path.join(self._dir or tempfile.gettempdir(),
+                                                 f"ugdr-daemon-{os.getpid()}.log")
+        self._log = open(self.log_path, "w")
+        self.proc = subprocess.Popen(args, env=env, stderr=self._log, stdout=self._log)
         deadline = time.time() + 120
         while not os.path.exists(socket_path):
             if self.proc.poll() is not None:
-                err = self.proc.stderr.read() if self.proc.stderr else ""
-                raise RuntimeError(f"ugdr_daemon exited ({self.proc.returncode}): {err}")
+                raise RuntimeError(f"ugdr_daemon exited ({self.proc.returncode}): {self.log_text()}")
             if time.time() > deadline:
                 self.stop()
                 raise RuntimeError("ugdr_daemon did not create its socket")
@@ -84,6 +88,7 @@ class Daemon:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
                 self.proc.wait()
+        self._log.close()
         if self._dir:
             with contextlib.suppress(OSError):
                 os.unlink(self.socket_path)
@@ -91,10 +96,12 @@ class Daemon:
                 os.rmdir(self._dir)
         return self.proc.returncode
 
-    def stderr_text(self) -> str:
-        if self.proc.poll() is None or self.proc.stderr is None:
+    def log_text(self) -> str:
+        try:
+            with open(self.log_path) as f:
+                return f.read()
+        except OSError:
             return ""
-        return self.proc.stderr.read()
 
     def __enter__(self):
         return self
