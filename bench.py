@@ -3,10 +3,11 @@
 
 Workload (weak-scaled): every GPU holds one 256 MiB bf16 MR (N(0,1),
 seeded by rank) of eight 32 MiB slices, plus a 256 MiB receive MR.  One step = every GPU
-RDMA_WRITEs 7 distinct slices over 7 QPs: WR k of rank r sends slice k to GPU (r + 1 + k) % N,
-into that GPU's receive slot (dst + 1 + k) % 8, so every inbound WR of a step lands in its own
-slot.  With N = 8 this is exactly "a 32 MiB slice to each of its 7 peers"; with fewer GPUs the
-same 7 x 32 MiB per GPU cycle over the available peers (N = 1: loopback copies inside one GPU).
+RDMA_WRITEs 7 distinct slices over 7 QPs: WR k of rank r sends slice k to peer
+(r + 1 + k mod (N - 1)) % N, into that GPU's receive slot (dst + 1 + k) % 8, so every inbound WR
+of a step lands in its own slot.  With N = 8 this is exactly "a 32 MiB slice to each of its 7
+peers"; with fewer GPUs the same 7 x 32 MiB per GPU cycle over the N - 1 peers, so all traffic
+crosses NVLink (N = 1 has no peer: loopback copies inside the GPU).
 Per-GPU work is fixed, so scaling is weak; each step reads 224 MiB and writes 224 MiB per GPU,
 more than the 126 MB L2.
 
@@ -36,6 +37,21 @@ SLOT_MIB = 32
 SLOTS = 8
 PEERS = 7
 BASELINE_GBPS = None  # BASELINE.json publishes no number for this config
+_DAEMON = None  # rank 0's daemon, kept for its log when a run fails
+
+
+def peer_of(rank: int, k: int, world: int) -> int:
+    """Destination of WR k: the peers in turn (never the sender itself unless it is alone)."""
+    if world == 1:
+        return rank
+    return (rank + 1 + k % (world - 1)) % world
+
+
+def sender_of(rank: int, k: int, world: int) -> int:
+    """The rank whose WR k lands on `rank` (inverse of peer_of for a fixed k)."""
+    if world == 1:
+        return rank
+    return (rank - 1 - k % (world - 1)) % world
 
 
 def dist_env():
@@ -90,10 +106,11 @@ def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None
     from ugdr_b200 import verbs as V
     from ugdr_b200.utils.clocks import ClockSampler
 
+    global _DAEMON
     torch.cuda.set_device(local)
     daemon = None
     if rank == 0:
-        daemon = V.Daemon(gpus=world, cpu_device=False)
+        daemon = _DAEMON = V.Daemon(gpus=world, cpu_device=False)
         path = daemon.socket_path
     else:
         path = None
@@ -124,15 +141,13 @@ def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None
     info = comm.gather({"addr": rcv_buf.data_ptr(), "rkey": rcv_mr.rkey,
                         "rsp": [q.qpn for q in rsp], "req": [q.qpn for q in req]})
     for k in range(PEERS):
-        dst = (rank + 1 + k) % world
-        req[k].connect(info[dst]["rsp"][k])
-        src = (rank - 1 - k) % world
-        rsp[k].connect(info[src]["req"][k])
+        req[k].connect(info[peer_of(rank, k, world)]["rsp"][k])
+        rsp[k].connect(info[sender_of(rank, k, world)]["req"][k])
     comm.barrier()
 
     def post_step(step_id: int):
         for k in range(PEERS):
-            dst = (rank + 1 + k) % world
+            dst = peer_of(rank, k, world)
             dslot = (dst + 1 + k) % SLOTS
             req[k].post_write((src_buf.data_ptr() + k * slot, slot, src_mr.lkey),
                               info[dst]["addr"] + dslot * slot, info[dst]["rkey"],
@@ -166,7 +181,7 @@ def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None
     ok = True
     rcv_bytes = rcv_buf.view(torch.uint8)
     for k in range(PEERS):
-        src = (rank - 1 - k) % world
+        src = sender_of(rank, k, world)
         dslot = (rank + 1 + k) % SLOTS
         g = torch.Generator(device="cuda").manual_seed(1234 + src)
         ref = torch.randn(total // 2, dtype=torch.bfloat16, device="cuda", generator=g).view(torch.uint8)
@@ -327,6 +342,11 @@ def main():
             out = run_reference(args, comm, world, rank, local)
         else:
             out = run_ugdr(args, comm, world, rank, local)
+    except BaseException:
+        if _DAEMON is not None:
+            _DAEMON.stop()
+            print("---- ugdr_daemon log ----\n" + _DAEMON.log_text()[-4000:], file=sys.stderr)
+        raise
     finally:
         comm.close()
     if out is not None:

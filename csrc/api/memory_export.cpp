@@ -93,15 +93,22 @@ int export_memory(void *addr, size_t len, std::vector<std::byte> *opaque, std::v
     if (attr.type != cudaMemoryTypeDevice) return EOPNOTSUPP;
     GetRangeFn range = get_range_fn();
     if (range == nullptr) return EOPNOTSUPP;
-    CUdeviceptr base = 0;
-    size_t size = 0;
-    if (range(&base, &size, CUdeviceptr(a)) != CUDA_SUCCESS) return EOPNOTSUPP;
-    if (a + len > base + size || a + len < a) return EINVAL;
     cudaDeviceProp prop{};
     if (cudaGetDeviceProperties(&prop, attr.device) != cudaSuccess) return EOPNOTSUPP;
+    // The range query and the export run in the owning device's context.
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(attr.device);
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (range(&base, &size, CUdeviceptr(a)) != CUDA_SUCCESS) {
+        cudaSetDevice(prev);
+        return EOPNOTSUPP;
+    }
+    if (a + len > base + size || a + len < a) {
+        cudaSetDevice(prev);
+        return EINVAL;
+    }
     cudaIpcMemHandle_t h{};
     const cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void *>(base));
     cudaSetDevice(prev);

@@ -52,9 +52,13 @@ struct MemoryDescriptor {
 
 struct OpenedMemory {
     void *address = nullptr;  // daemon address of the registered range start
-    void *device_address = nullptr;  // the same byte as seen by the GPU executors (0: unreachable)
+    // The same byte as seen by the executor of each daemon GPU (index = CUDA ordinal; null:
+    // unreachable).  A CUDA IPC handle maps an allocation only into the context it is opened
+    // in, so device memory is opened once per GPU; pinned host memory has one portable address.
+    std::vector<void *> device_address;
     int gpu = -1;             // owning CUDA ordinal, -1 for host memory
-    void *base = nullptr;     // what to close (IPC mapping base)
+    std::vector<void *> bases;  // per-GPU IPC mapping bases to close (device memory)
+    void *host_registered = nullptr;  // pinned host region to unregister (host memory)
     SharedMapping host;       // host regions stay mapped while registered
 };
 

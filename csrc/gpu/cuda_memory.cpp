@@ -60,15 +60,15 @@ int DaemonMemoryBackend::open(control::MemoryDescriptor &desc, uint64_t length,
         }
         out->address = static_cast<uint8_t *>(out->host.address) + desc.region_offset;
         out->gpu = -1;
-        out->device_address = nullptr;
+        out->device_address.assign(size_t(inv_.count), nullptr);
         if (inv_.count > 0) {
             // Pin and map the whole region once, portable to every GPU the executors run on.
             if (cudaHostRegister(out->host.address, out->host.bytes,
                                  cudaHostRegisterMapped | cudaHostRegisterPortable) == cudaSuccess) {
                 void *dev = nullptr;
                 if (cudaHostGetDevicePointer(&dev, out->host.address, 0) == cudaSuccess)
-                    out->device_address = static_cast<uint8_t *>(dev) + desc.region_offset;
-                out->base = out->host.address;  // marks the registration for close()
+                    for (auto &d : out->device_address) d = static_cast<uint8_t *>(dev) + desc.region_offset;
+                out->host_registered = out->host.address;
             }
             (void)cudaGetLastError();
         }
@@ -82,53 +82,75 @@ int DaemonMemoryBackend::open(control::MemoryDescriptor &desc, uint64_t length,
     std::lock_guard<std::mutex> lk(mu_);
     auto it = open_.find(desc.ipc_handle);
     if (it == open_.end()) {
+        // Open the handle in every GPU's context: each executor stores / loads through a mapping
+        // of its own (the owner's is local memory, the others reach it over NVLink).
         cudaIpcMemHandle_t h;
         std::memcpy(&h, desc.ipc_handle.data(), sizeof(h));
         int prev = 0;
         cudaGetDevice(&prev);
-        cudaSetDevice(gpu);
-        void *base = nullptr;
-        const cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
-        cudaSetDevice(prev);
-        if (e != cudaSuccess) {
-            (void)cudaGetLastError();
+        Mapping m;
+        m.gpu = gpu;
+        m.bases.assign(size_t(inv_.count), nullptr);
+        bool ok = true;
+        for (int d = 0; d < inv_.count && ok; ++d) {
+            cudaSetDevice(d);
+            if (cudaIpcOpenMemHandle(&m.bases[d], h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                (void)cudaGetLastError();
+                m.bases[d] = nullptr;
+                ok = d != gpu;  // a peer that cannot map it only loses access; the owner must
+            }
+        }
+        if (!ok) {
+            for (int d = 0; d < inv_.count; ++d) {
+                if (m.bases[d] == nullptr) continue;
+                cudaSetDevice(d);
+                cudaIpcCloseMemHandle(m.bases[d]);
+            }
+            cudaSetDevice(prev);
             return EACCES;
         }
-        it = open_.emplace(desc.ipc_handle, Mapping{base, gpu, 0}).first;
+        cudaSetDevice(prev);
+        it = open_.emplace(desc.ipc_handle, std::move(m)).first;
     }
     it->second.refs += 1;
-    out->base = it->second.base;
-    out->address = static_cast<uint8_t *>(it->second.base) + desc.allocation_offset;
-    out->device_address = out->address;  // UVA: the same pointer is valid on every peer GPU
     out->gpu = gpu;
+    out->bases = it->second.bases;
+    out->device_address.assign(size_t(inv_.count), nullptr);
+    for (int d = 0; d < inv_.count; ++d)
+        if (it->second.bases[d] != nullptr)
+            out->device_address[d] = static_cast<uint8_t *>(it->second.bases[d]) + desc.allocation_offset;
+    out->address = out->device_address[gpu];
     return 0;
 }
 
 void DaemonMemoryBackend::close(control::OpenedMemory &mem) noexcept {
     if (mem.gpu < 0) {
-        if (mem.base != nullptr) cudaHostUnregister(mem.base);
-        mem.base = nullptr;
-        mem.device_address = nullptr;
+        if (mem.host_registered != nullptr) cudaHostUnregister(mem.host_registered);
+        mem.host_registered = nullptr;
+        mem.device_address.clear();
         mem.host.unmap();
         mem.address = nullptr;
         return;
     }
     std::lock_guard<std::mutex> lk(mu_);
     for (auto it = open_.begin(); it != open_.end(); ++it) {
-        if (it->second.base == mem.base) {
-            if (--it->second.refs == 0) {
-                int prev = 0;
-                cudaGetDevice(&prev);
-                cudaSetDevice(it->second.gpu);
-                cudaIpcCloseMemHandle(it->second.base);
-                cudaSetDevice(prev);
-                open_.erase(it);
+        if (it->second.bases != mem.bases) continue;
+        if (--it->second.refs == 0) {
+            int prev = 0;
+            cudaGetDevice(&prev);
+            for (size_t d = 0; d < it->second.bases.size(); ++d) {
+                if (it->second.bases[d] == nullptr) continue;
+                cudaSetDevice(int(d));
+                cudaIpcCloseMemHandle(it->second.bases[d]);
             }
-            break;
+            cudaSetDevice(prev);
+            open_.erase(it);
         }
+        break;
     }
     mem.address = nullptr;
-    mem.base = nullptr;
+    mem.bases.clear();
+    mem.device_address.clear();
 }
 
 }  // namespace ugdr::gpu

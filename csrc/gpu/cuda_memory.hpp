@@ -1,10 +1,11 @@
 // Daemon side of the CUDA-IPC memory-registration model.
 //
 // Parity: reference src/gpu/cuda_ipc_memory.cu:170-292 (per-UUID device table, open with
-// cudaIpcMemLazyEnablePeerAccess, close).  Differences: the opener enables peer access between
-// every pair of GPUs it owns at start-up (so an executor on GPU a can store into an MR that
-// lives on GPU b), and it reference-counts opened handles, because a client may register
-// several ranges of one allocation and a handle can be opened only once per process.
+// cudaIpcMemLazyEnablePeerAccess, close).  Differences: the daemon enables peer access between
+// every pair of GPUs it owns, and opens each handle once in every GPU's context, because an
+// IPC mapping exists only in the context that opened it: the executor on GPU a stores into an
+// MR on GPU b through GPU a's own mapping (NVLink).  Opened handles are reference-counted, since
+// a client may register several ranges of one allocation and a handle opens once per context.
 #pragma once
 
 #include "control/objects.hpp"
@@ -37,8 +38,8 @@ class DaemonMemoryBackend : public control::MemoryBackend {
 
   private:
     struct Mapping {
-        void *base = nullptr;
-        int gpu = -1;
+        std::vector<void *> bases;  // one mapping per daemon GPU (index = CUDA ordinal)
+        int gpu = -1;               // owner
         int refs = 0;
     };
     GpuInventory inv_;

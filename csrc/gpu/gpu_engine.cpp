@@ -175,7 +175,8 @@ int GpuEngine::copy_from_device(void *dst, const void *src, size_t n) {
 
 int GpuEngine::attach_mr(control::Mr &mr) {
     DevMr d{};
-    d.base = reinterpret_cast<uint64_t>(mr.mem.device_address);
+    const auto &addr = mr.mem.device_address;
+    d.base = size_t(cfg_.ordinal) < addr.size() ? reinterpret_cast<uint64_t>(addr[cfg_.ordinal]) : 0;
     d.client_base = mr.client_address;
     d.length = mr.length;
     d.access = mr.access;

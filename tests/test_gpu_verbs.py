@@ -185,3 +185,58 @@ def test_many_qps_queue_depth(gpu_env):
     for i in (0, 1, 17, k - 1):
         q = (i % 16)
         assert torch.equal(view[i], src[q * n:(q + 1) * n])
+
+
+@pytest.fixture(scope="module")
+def gpu2_env():
+    if gpu_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from ugdr_b200 import verbs as V
+
+    d = V.Daemon(gpus=2)
+    yield V
+    d.stop()
+
+
+def test_cross_gpu_write_read_imm_atomics(gpu2_env):
+    """Requester on GPU 0, responder memory / QP / CQ on GPU 1: the GPU 0 executor stores over
+    NVLink into GPU 1 memory, consumes GPU 1's RQ and fills GPU 1's receive CQ."""
+    V = gpu2_env
+    from ugdr_b200 import _native as N
+
+    acc = _acc(N)
+    c0, c1 = V.Context(V.find_device(gpu=0)), V.Context(V.find_device(gpu=1))
+    p0, p1 = c0.alloc_pd(), c1.alloc_pd()
+    q0c, q1c = c0.create_cq(256), c1.create_cq(256)
+    a = p0.create_qp(q0c, max_send_wr=64)
+    b = p1.create_qp(q1c, max_send_wr=64)
+    V.connect_pair(a, b, access=N.ACCESS_REMOTE_WRITE | N.ACCESS_REMOTE_READ | N.ACCESS_REMOTE_ATOMIC)
+    n = (8 << 20) + 3
+    src = torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda:0")
+    back = torch.zeros(n, dtype=torch.uint8, device="cuda:0")
+    dst = torch.zeros(n + 64, dtype=torch.uint8, device="cuda:1")
+    ctr = torch.zeros(16, dtype=torch.int64, device="cuda:1")
+    old = torch.zeros(16, dtype=torch.int64, device="cuda:0")
+    torch.cuda.synchronize(0)
+    torch.cuda.synchronize(1)
+    ms, mb, mo = (p0.reg_mr(t.data_ptr(), t.numel() * t.element_size(), acc) for t in (src, back, old))
+    md, mc = (p1.reg_mr(t.data_ptr(), t.numel() * t.element_size(), acc) for t in (dst, ctr))
+    b.post_recv(wr_id=42)
+    a.post_send(N.WR_RDMA_WRITE_WITH_IMM, [(src.data_ptr(), n, ms.lkey)], remote_addr=dst.data_ptr() + 32,
+                rkey=md.rkey, wr_id=1, imm=7)
+    w = q0c.wait(1, 60)[0]
+    assert (w.status, w.wr_id, w.byte_len) == (N.WC_SUCCESS, 1, n)
+    r = q1c.wait(1, 60)[0]
+    assert (r.status, r.wr_id, r.opcode, r.imm_data, r.byte_len) == (N.WC_SUCCESS, 42, N.WC_RECV_RDMA_WITH_IMM, 7, n)
+    a.post_read((back.data_ptr(), n, mb.lkey), dst.data_ptr() + 32, md.rkey, wr_id=2)
+    assert q0c.wait(1, 60)[0].status == N.WC_SUCCESS
+    for i in range(8):
+        a.post_send(N.WR_ATOMIC_FETCH_AND_ADD, [(old.data_ptr() + 8 * i, 8, mo.lkey)],
+                    remote_addr=ctr.data_ptr(), rkey=mc.rkey, compare_add=1 << i, wr_id=10 + i)
+    assert all(x.status == N.WC_SUCCESS for x in q0c.wait(8, 60))
+    torch.cuda.synchronize(0)
+    torch.cuda.synchronize(1)
+    assert torch.equal(dst[32:32 + n].cpu(), src.cpu()) and int(dst[:32].sum()) == 0
+    assert int(dst[32 + n:].sum()) == 0
+    assert torch.equal(back, src)
+    assert int(ctr[0]) == 255 and sorted(old[:8].tolist()) == sorted([sum(1 << j for j in range(i)) for i in range(8)])
