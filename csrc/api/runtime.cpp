@@ -97,10 +97,13 @@ class Runtime {
     // One control round trip.  Returns 0 / positive errno (transport or service status).
     int call(Request &&req, Response *resp) {
         std::lock_guard<std::mutex> lk(mu_);
-        if (!client_.connected()) {
-            const char *env = std::getenv("UGDR_DAEMON_SOCKET");
-            const std::string path = (env != nullptr && env[0] != '\0') ? env : kDefaultSocket;
+        const char *env = std::getenv("UGDR_DAEMON_SOCKET");
+        const std::string path = (env != nullptr && env[0] != '\0') ? env : kDefaultSocket;
+        // (Re)connect when there is no connection or the configured daemon changed; either way
+        // the epoch advances and proxies of the previous connection become stale.
+        if (!client_.connected() || path != path_) {
             if (int rc = client_.connect(path); rc != 0) return rc;
+            path_ = path;
         }
         if (int rc = client_.call(std::move(req), resp); rc != 0) return rc;
         return resp->status;
@@ -120,6 +123,7 @@ class Runtime {
   private:
     std::mutex mu_;
     ControlClient client_;
+    std::string path_;
 };
 
 Runtime &rt() { return Runtime::get(); }

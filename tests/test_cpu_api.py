@@ -1,0 +1,214 @@
+"""Public verbs API end to end against a real ugdr_daemon process, host-memory engine only (no
+GPU).  Mirrors the reference's integration suite (tests/integration/*_client_server_test.cpp,
+control_plane_acceptance_test.cpp) and adds the data path the reference only runs on a GPU."""
+from __future__ import annotations
+
+import ctypes as C
+import multiprocessing as mp
+import os
+import random
+import time
+
+import numpy as np
+import pytest
+
+from ugdr_b200 import _native as N
+from ugdr_b200 import verbs as V
+
+ACC = N.ACCESS_LOCAL_WRITE | N.ACCESS_REMOTE_WRITE | N.ACCESS_REMOTE_READ | N.ACCESS_REMOTE_ATOMIC
+REMOTE = N.ACCESS_REMOTE_WRITE | N.ACCESS_REMOTE_READ | N.ACCESS_REMOTE_ATOMIC
+
+
+def _pair(depth=128, max_sge=4, rnr_retry=7, min_rnr_timer=1, cq_depth=512):
+    ctx = V.Context(V.find_device(kind=0))
+    pd = ctx.alloc_pd()
+    cq = ctx.create_cq(cq_depth)
+    a = pd.create_qp(cq, max_send_wr=depth, max_recv_wr=depth, max_send_sge=max_sge, max_recv_sge=max_sge)
+    b = pd.create_qp(cq, max_send_wr=depth, max_recv_wr=depth, max_send_sge=max_sge, max_recv_sge=max_sge)
+    V.connect_pair(a, b, access=REMOTE, rnr_retry=rnr_retry, min_rnr_timer=min_rnr_timer)
+    return ctx, pd, cq, a, b
+
+
+def test_config0_cpu_plumbing_10k_writes(cpu_daemon):
+    """1 PD, 2 host MRs of 1 MiB, 1 QP of depth 128, 10,000 RDMA_WRITEs of
+    4 KiB at seeded random 4 KiB-aligned offsets, payload uniform uint8 from seed 0."""
+    ctx, pd, cq, a, b = _pair(depth=128, cq_depth=256)
+    n = 1 << 20
+    src, dst = V.HostBuffer(n), V.HostBuffer(n)
+    sv, dv = src.view(), dst.view()
+    sv[:] = np.random.default_rng(0).integers(0, 256, n, dtype=np.uint8)
+    ms, md = pd.reg_mr(src.addr, n, ACC), pd.reg_mr(dst.addr, n, ACC)
+    rng = random.Random(0)
+    expect = np.zeros(n, dtype=np.uint8)
+    done, posted, total = 0, 0, 10_000
+    t0 = time.perf_counter()
+    while done < total:
+        while posted < total and posted - done < 128:
+            so, do = rng.randrange(256) * 4096, rng.randrange(256) * 4096
+            a.post_write((src.addr + so, 4096, ms.lkey), dst.addr + do, md.rkey, wr_id=posted)
+            expect[do:do + 4096] = sv[so:so + 4096]
+            posted += 1
+        for w in cq.poll():
+            assert w.status == N.WC_SUCCESS and w.wr_id == done
+            done += 1
+    dt = time.perf_counter() - t0
+    assert np.array_equal(dv, expect)
+    print(f"config0: {total} x 4 KiB WRITEs in {dt * 1e3:.1f} ms ({total / dt / 1e6:.3f} MWR/s)")
+
+
+def test_write_with_imm_consumes_rq_in_order(cpu_daemon):
+    ctx, pd, cq, a, b = _pair()
+    buf = V.HostBuffer(1 << 16)
+    m = pd.reg_mr(buf.addr, 1 << 16, ACC)
+    for i in range(3):
+        b.post_recv(wr_id=100 + i)
+    for i in range(3):
+        a.post_send(N.WR_RDMA_WRITE_WITH_IMM, [(buf.addr, 64 * (i + 1), m.lkey)], remote_addr=buf.addr + 4096,
+                    rkey=m.rkey, wr_id=i, imm=0x10 + i, signaled=(i != 1))
+    wcs = cq.wait(5, 10)
+    recv = [w for w in wcs if w.opcode == N.WC_RECV_RDMA_WITH_IMM]
+    send = [w for w in wcs if w.opcode == N.WC_RDMA_WRITE]
+    assert [w.wr_id for w in recv] == [100, 101, 102]
+    assert [w.imm_data for w in recv] == [0x10, 0x11, 0x12]
+    assert [w.byte_len for w in recv] == [64, 128, 192]
+    assert all(w.wc_flags & N.WC_WITH_IMM and w.qp_num == b.qpn for w in recv)
+    assert [w.wr_id for w in send] == [0, 2]  # the unsignaled WR produces no send completion
+
+
+def test_rnr_retry_exhausted(cpu_daemon):
+    ctx, pd, cq, a, b = _pair(rnr_retry=2, min_rnr_timer=1)  # 10 us timer, 2 retries
+    buf = V.HostBuffer(8192)
+    m = pd.reg_mr(buf.addr, 8192, ACC)
+    a.post_send(N.WR_RDMA_WRITE_WITH_IMM, [(buf.addr, 8, m.lkey)], remote_addr=buf.addr + 64, rkey=m.rkey,
+                wr_id=5, imm=1, signaled=False)
+    a.post_write((buf.addr, 8, m.lkey), buf.addr + 128, m.rkey, wr_id=6)
+    wcs = cq.wait(2, 10)
+    assert (wcs[0].wr_id, wcs[0].status) == (5, N.WC_RNR_RETRY_EXC_ERR)  # error WCs ignore signaling
+    assert (wcs[1].wr_id, wcs[1].status) == (6, N.WC_WR_FLUSH_ERR)
+    assert a.query()[0].qp_state == N.QPS_ERR
+    # ERR refuses new sends.
+    rc, bad = a.post_send_raw([a.make_send_wr(N.WR_RDMA_WRITE, [(buf.addr, 8, m.lkey)], buf.addr, m.rkey)])
+    assert rc == 22 and bad == 0
+
+
+def test_infinite_rnr_waits_for_receive(cpu_daemon):
+    ctx, pd, cq, a, b = _pair(rnr_retry=7)
+    buf = V.HostBuffer(8192)
+    m = pd.reg_mr(buf.addr, 8192, ACC)
+    a.post_send(N.WR_RDMA_WRITE_WITH_IMM, [(buf.addr, 16, m.lkey)], remote_addr=buf.addr + 64, rkey=m.rkey,
+                wr_id=1, imm=9)
+    time.sleep(0.05)
+    assert cq.poll() == []  # stalled, not failed
+    b.post_recv(wr_id=2)
+    wcs = cq.wait(2, 10)
+    assert sorted((w.wr_id, w.status) for w in wcs) == [(1, 0), (2, 0)]
+
+
+def test_modify_to_err_flushes_sq_and_rq(cpu_daemon):
+    ctx, pd, cq, a, b = _pair()
+    for i in range(4):
+        b.post_recv(wr_id=i)
+    b.to_error()
+    wcs = cq.wait(4, 10)
+    assert [w.wr_id for w in wcs] == [0, 1, 2, 3]
+    assert all(w.status == N.WC_WR_FLUSH_ERR for w in wcs)
+    rc, _ = b.post_recv_raw([b.make_recv_wr(9, [])])
+    assert rc == 22
+
+
+def test_access_and_protection_errors(cpu_daemon):
+    ctx, pd, cq, a, b = _pair()
+    buf = V.HostBuffer(8192)
+    ro = pd.reg_mr(buf.addr, 4096, N.ACCESS_LOCAL_WRITE)  # no remote access
+    rw = pd.reg_mr(buf.addr + 4096, 4096, ACC)
+    a.post_write((buf.addr + 4096, 8, rw.lkey), buf.addr, ro.rkey, wr_id=1)
+    assert cq.wait(1, 10)[0].status == N.WC_REM_ACCESS_ERR
+    ctx2, pd2, cq2, c, d = _pair()
+    c.post_write((buf.addr + 4096, 8, rw.lkey), buf.addr + 4096, rw.rkey, wr_id=2)  # lkey of another PD
+    assert cq2.wait(1, 10)[0].status == N.WC_LOC_PROT_ERR
+    ctx3, pd3, cq3, e, f = _pair()
+    m3 = pd3.reg_mr(buf.addr + 4096, 4096, ACC)
+    e.post_write((buf.addr + 4096, 8, m3.lkey), buf.addr + 4096 + 4090, m3.rkey, wr_id=3)  # runs past the MR
+    assert cq3.wait(1, 10)[0].status == N.WC_REM_ACCESS_ERR
+
+
+def test_api_error_domains(cpu_daemon):
+    L = N.lib()
+    ctx = V.Context(V.find_device(kind=0))
+    pd = ctx.alloc_pd()
+    cq = ctx.create_cq(8)
+    assert L.ugdr_close_device(ctx.h) == -1 and N.errno() == 16  # EBUSY with live children
+    assert L.ugdr_poll_cq(None, 1, None) == -22
+    assert L.ugdr_create_cq(ctx.h, 0, None, None, 0) is None and N.errno() == 22
+    assert not L.ugdr_reg_mr(pd.h, C.c_void_p(12345), 8, 1)  # malloc-style host memory
+    assert N.errno() == 95
+    cq.destroy()
+    assert L.ugdr_destroy_cq(cq.h) == 22  # repeated destroy
+    pd.dealloc()
+    ctx.close()
+    assert L.ugdr_close_device(ctx.h) == -1 and N.errno() == 22
+
+
+def _client_b(path, q):
+    os.environ["UGDR_DAEMON_SOCKET"] = path
+    ctx = V.Context(V.find_device(kind=0))
+    pd = ctx.alloc_pd()
+    cq = ctx.create_cq(8)
+    qp = pd.create_qp(cq)
+    qp.to_init(N.ACCESS_REMOTE_WRITE)
+    q.put(qp.qpn)
+    q.get()  # wait for the peer to connect, then exit without cleanup (session reclaim)
+
+
+def test_two_clients_connect_and_disconnect_reclaim(cpu_daemon):
+    mpc = mp.get_context("spawn")
+    q = mpc.Queue()
+    p = mpc.Process(target=_client_b, args=(cpu_daemon.socket_path, q))
+    p.start()
+    remote_qpn = q.get(timeout=60)
+    ctx = V.Context(V.find_device(kind=0))
+    pd = ctx.alloc_pd()
+    cq = ctx.create_cq(8)
+    a = pd.create_qp(cq)
+    a.to_init(N.ACCESS_REMOTE_WRITE)
+    a.connect(remote_qpn)  # cross-session, same daemon
+    assert a.query()[0].qp_state == N.QPS_RTS
+    q.put("done")
+    p.join(30)
+    assert p.exitcode == 0
+    # The other client's QP was reclaimed with its session: a new connect cannot find it.
+    b = pd.create_qp(cq)
+    b.to_init(N.ACCESS_REMOTE_WRITE)
+    deadline = time.time() + 5
+    while True:
+        rc = N.lib().ugdr_connect_qp(b.h, C.byref(N.QpConnInfo(remote_qpn)),
+                                     C.byref(N.QpAttr(timeout=14, retry_cnt=7, rnr_retry=7, min_rnr_timer=1)),
+                                     N.CONNECT_MASK)
+        if rc == 2 or time.time() > deadline:
+            break
+        time.sleep(0.05)
+    assert rc == 2  # ENOENT
+
+
+def test_killed_client_does_not_take_the_daemon_down(cpu_daemon):
+    mpc = mp.get_context("spawn")
+    q = mpc.Queue()
+    p = mpc.Process(target=_client_b, args=(cpu_daemon.socket_path, q))
+    p.start()
+    q.get(timeout=60)
+    p.kill()
+    p.join(30)
+    assert cpu_daemon.proc.poll() is None
+    assert V.find_device(kind=0).name == "ugdr_cpu0"
+
+
+def test_engine_stats_count_work(cpu_daemon):
+    ctx, pd, cq, a, b = _pair()
+    buf = V.HostBuffer(1 << 16)
+    m = pd.reg_mr(buf.addr, 1 << 16, ACC)
+    ctx.stats(reset=True)
+    for i in range(10):
+        a.post_write((buf.addr, 1000, m.lkey), buf.addr + 8192, m.rkey, wr_id=i)
+    cq.wait(10, 10)
+    st = ctx.stats()
+    assert st.wrs_completed >= 10 and st.bytes_moved >= 10_000
