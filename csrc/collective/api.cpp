@@ -1,0 +1,115 @@
+// C ABI of the collective kernels and the IPC helpers that build a peer set.
+#include "collective/kernels.hpp"
+#include "ugdr/collective.h"
+
+#include <cuda.h>
+#include <cuda_runtime_api.h>
+
+#include <cstring>
+
+namespace {
+
+static_assert(sizeof(ugdr_x_peerset) == sizeof(ugdr::coll::PeerSet), "peer set layout");
+constexpr uint64_t kMaxWaitNs = 5ull * 1000 * 1000 * 1000;
+
+const ugdr::coll::PeerSet &as_ps(const ugdr_x_peerset *p) {
+    return *reinterpret_cast<const ugdr::coll::PeerSet *>(p);
+}
+
+int default_ctas() {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    return ugdr::coll::grid_for(dev);
+}
+
+using GetRangeFn = CUresult (*)(CUdeviceptr *, size_t *, CUdeviceptr);
+
+}  // namespace
+
+extern "C" {
+
+int ugdr_x_ipc_export(void *ptr, uint8_t handle[UGDR_X_IPC_HANDLE_BYTES], uint64_t *offset) {
+    static GetRangeFn range = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return GetRangeFn(nullptr);
+        return reinterpret_cast<GetRangeFn>(p);
+    }();
+    if (ptr == nullptr || handle == nullptr || offset == nullptr || range == nullptr)
+        return int(cudaErrorInvalidValue);
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (range(&base, &size, CUdeviceptr(reinterpret_cast<uintptr_t>(ptr))) != CUDA_SUCCESS)
+        return int(cudaErrorInvalidValue);
+    cudaIpcMemHandle_t h{};
+    const cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void *>(base));
+    if (e != cudaSuccess) return int(e);
+    std::memcpy(handle, &h, sizeof(h));
+    *offset = reinterpret_cast<uintptr_t>(ptr) - base;
+    return 0;
+}
+
+int ugdr_x_ipc_open(const uint8_t handle[UGDR_X_IPC_HANDLE_BYTES], void **base) {
+    if (handle == nullptr || base == nullptr) return int(cudaErrorInvalidValue);
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    return int(cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+int ugdr_x_ipc_close(void *base) { return int(cudaIpcCloseMemHandle(base)); }
+
+int ugdr_x_allreduce_bf16(const ugdr_x_peerset *ps, uint64_t offset, uint64_t count, uint64_t epoch, int ctas,
+                          void *stream) {
+    if (ps == nullptr || ps->n < 1 || ps->n > UGDR_X_MAX_RANKS) return int(cudaErrorInvalidValue);
+    return ugdr::coll::launch_allreduce_bf16(as_ps(ps), offset, count, epoch, ctas > 0 ? ctas : default_ctas(),
+                                             kMaxWaitNs, static_cast<cudaStream_t>(stream));
+}
+
+size_t ugdr_x_moe_route_scratch_bytes(uint64_t rows, int nexp) {
+    return ugdr::coll::route_scratch_bytes(rows, nexp);
+}
+
+int ugdr_x_moe_route(const int32_t *expert_ids, uint64_t rows, int nexp, int32_t *counts, int32_t *positions,
+                     void *scratch, size_t scratch_bytes, void *stream) {
+    if (counts == nullptr || (rows > 0 && (expert_ids == nullptr || positions == nullptr)))
+        return int(cudaErrorInvalidValue);
+    if (scratch_bytes < ugdr::coll::route_scratch_bytes(rows, nexp) || (scratch == nullptr && rows > 0))
+        return int(cudaErrorInvalidValue);
+    return ugdr::coll::launch_route(expert_ids, rows, nexp, counts, positions, static_cast<uint32_t *>(scratch),
+                                    static_cast<cudaStream_t>(stream));
+}
+
+int ugdr_x_moe_layout(const ugdr_x_peerset *ps, const int32_t *counts, int nexp, int experts_per_rank,
+                      uint64_t table_offset, int64_t *group_base, int64_t *recv_used, uint64_t epoch,
+                      void *stream) {
+    if (ps == nullptr || nexp <= 0 || experts_per_rank <= 0 || table_offset % 4 != 0)
+        return int(cudaErrorInvalidValue);
+    return ugdr::coll::launch_layout(as_ps(ps), counts, nexp, experts_per_rank, table_offset, group_base,
+                                     recv_used, epoch, kMaxWaitNs, static_cast<cudaStream_t>(stream));
+}
+
+int ugdr_x_moe_dispatch(const ugdr_x_peerset *ps, const void *x, uint64_t row_bytes, const int32_t *expert_ids,
+                        const int32_t *positions, const int64_t *group_base, uint64_t tokens, int topk,
+                        int experts_per_rank, uint64_t recv_offset, uint64_t recv_rows, uint64_t epoch, int ctas,
+                        void *stream) {
+    if (ps == nullptr || topk <= 0 || experts_per_rank <= 0) return int(cudaErrorInvalidValue);
+    return ugdr::coll::launch_dispatch(as_ps(ps), x, row_bytes, expert_ids, positions, group_base, tokens, topk,
+                                       experts_per_rank, recv_offset, recv_rows, epoch,
+                                       ctas > 0 ? ctas : default_ctas(), kMaxWaitNs,
+                                       static_cast<cudaStream_t>(stream));
+}
+
+int ugdr_x_moe_combine(const ugdr_x_peerset *ps, void *out, uint64_t row_bytes, const int32_t *expert_ids,
+                       const int32_t *positions, const int64_t *group_base, const float *weights, uint64_t tokens,
+                       int topk, int experts_per_rank, uint64_t recv_offset, uint64_t recv_rows, uint64_t epoch,
+                       int ctas, void *stream) {
+    if (ps == nullptr || topk <= 0 || experts_per_rank <= 0) return int(cudaErrorInvalidValue);
+    return ugdr::coll::launch_combine(as_ps(ps), out, row_bytes, expert_ids, positions, group_base, weights,
+                                      tokens, topk, experts_per_rank, recv_offset, recv_rows, epoch,
+                                      ctas > 0 ? ctas : default_ctas(), kMaxWaitNs,
+                                      static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,391 @@
+// Collectives on ugdr's memory model: every rank's buffers are CUDA-IPC mapped into every other
+// rank's process (the same export / open path as MR registration), and sm_100a kernels move the
+// data with direct NVLink loads and stores, fusing the arithmetic into the transfer.
+//
+//  * Allreduce (bf16, fp32 accumulation): reduce-scatter kernel, then all-gather kernel.  Rank r
+//    pulls shard r from every peer, sums, and stores it in place; then pulls every other shard.
+//    2 (N - 1) / N of the buffer crosses NVLink per GPU, the ring optimum, in two launches.
+//  * MoE routing (moe_route): deterministic counting sort of (token, k) rows by expert - counts per
+//    expert and each row's position within its expert group.  Scratch: per-block histograms.
+//  * MoE dispatch: each (token, k) row is stored straight into the expert owner's receive
+//    buffer at [expert group base + position], i.e. the permute is the NVLink store itself.
+//  * MoE combine: each token pulls its top-k expert rows back over NVLink and applies the routing
+//    weights in fp32: the unpermute and the weighted reduction are the NVLink load itself.
+//
+// Cross-GPU ordering: a kernel that must not return before every peer finished the same phase
+// ends with an arrival counter; the last CTA to arrive publishes `epoch` into each peer's signal
+// word (st.release.sys) and waits, with a %globaltimer bound, until every peer's word for this
+// rank reaches `epoch`.  Only that one CTA waits, so no co-residency is assumed; kernels on
+// different GPUs run concurrently by construction.  A wait that runs out sets *status and returns.
+#include "collective/kernels.hpp"
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ugdr::coll {
+namespace {
+
+__device__ __forceinline__ uint64_t gtime() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ uint64_t ld_acq_sys(const void *p) {
+    uint64_t v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_rel_sys(void *p, uint64_t v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint4 ld128(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+__device__ __forceinline__ void st128(void *p, uint4 v) {
+    asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+// Last-arriving CTA signals every peer and waits for theirs.  Called by every thread of every CTA.
+__device__ void end_barrier(const PeerSet &ps, uint64_t epoch, uint32_t slot, uint64_t max_ns) {
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    __threadfence_system();
+    unsigned int *arrive = &ps.arrive[slot];
+    const unsigned int old = atomicAdd(arrive, 1u);
+    if (old + 1 != gridDim.x) return;
+    atomicExch(arrive, 0u);  // re-arm for the next launch (stream order separates launches)
+    // Signal word layout in every rank's signal buffer: sig[slot * kMaxRanks + sender].
+    for (int q = 0; q < ps.n; ++q) {
+        uint64_t *w = ps.signal[q] + slot * kMaxRanks + ps.rank;
+        st_rel_sys(w, epoch);
+    }
+    const uint64_t *mine = ps.signal[ps.rank] + slot * kMaxRanks;
+    const uint64_t t0 = gtime();
+    for (int q = 0; q < ps.n; ++q) {
+        uint32_t spins = 0;
+        while (ld_acq_sys(mine + q) < epoch) {
+            if ((++spins & 255) == 0 && gtime() - t0 > max_ns) {
+                atomicExch(ps.status, 1u);
+                return;
+            }
+            __nanosleep(64);
+        }
+    }
+}
+
+__device__ __forceinline__ void acc8(float (&a)[8], uint4 v) {
+    const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h[i]);
+        a[2 * i] += f.x;
+        a[2 * i + 1] += f.y;
+    }
+}
+__device__ __forceinline__ uint4 pack8(const float (&a)[8]) {
+    uint4 v;
+    __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(a[2 * i], a[2 * i + 1]);
+    return v;
+}
+
+// ---- allreduce ---------------------------------------------------------------------------------
+
+// Phase 1: shard `rank` of every peer's buffer summed into this rank's buffer (in place).
+// Elements are processed 8 at a time (16 B); the shard is [begin, end) in 8-element vectors.
+template <int NR>
+__global__ void __launch_bounds__(512) reduce_scatter_kernel(PeerSet ps, uint64_t base_off, uint64_t nvec,
+                                                             uint64_t epoch, uint64_t max_ns) {
+    const uint64_t per = (nvec + ps.n - 1) / ps.n;
+    const uint64_t begin = min(nvec, per * ps.rank), end = min(nvec, begin + per);
+    const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
+    for (uint64_t i = begin + blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < end; i += 2 * stride) {
+        const bool two = i + stride < end;
+        float a[8] = {0, 0, 0, 0, 0, 0, 0, 0}, b[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        uint4 va[NR], vb[NR];
+#pragma unroll
+        for (int q = 0; q < NR; ++q) {
+            if (q < ps.n) {
+                const uint8_t *src = reinterpret_cast<const uint8_t *>(ps.buf[q]) + base_off;
+                va[q] = ld128(src + i * 16);
+                if (two) vb[q] = ld128(src + (i + stride) * 16);
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < NR; ++q) {
+            if (q < ps.n) {
+                acc8(a, va[q]);
+                if (two) acc8(b, vb[q]);
+            }
+        }
+        uint8_t *dst = reinterpret_cast<uint8_t *>(ps.buf[ps.rank]) + base_off;
+        st128(dst + i * 16, pack8(a));
+        if (two) st128(dst + (i + stride) * 16, pack8(b));
+    }
+    end_barrier(ps, epoch, 0, max_ns);
+}
+
+// Phase 2: every other rank's reduced shard copied from its owner into this rank's buffer.
+__global__ void __launch_bounds__(512) all_gather_kernel(PeerSet ps, uint64_t base_off, uint64_t nvec,
+                                                         uint64_t epoch, uint64_t max_ns) {
+    const uint64_t per = (nvec + ps.n - 1) / ps.n;
+    const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
+    uint8_t *dst = reinterpret_cast<uint8_t *>(ps.buf[ps.rank]) + base_off;
+    for (int k = 1; k < ps.n; ++k) {
+        const int q = (ps.rank + k) % ps.n;  // stagger owners so links are used evenly
+        const uint64_t begin = min(nvec, per * q), end = min(nvec, begin + per);
+        const uint8_t *src = reinterpret_cast<const uint8_t *>(ps.buf[q]) + base_off;
+        uint64_t i = begin + blockIdx.x * uint64_t(blockDim.x) + threadIdx.x;
+        for (; i + 3 * stride < end; i += 4 * stride) {
+            const uint4 v0 = ld128(src + i * 16), v1 = ld128(src + (i + stride) * 16);
+            const uint4 v2 = ld128(src + (i + 2 * stride) * 16), v3 = ld128(src + (i + 3 * stride) * 16);
+            st128(dst + i * 16, v0);
+            st128(dst + (i + stride) * 16, v1);
+            st128(dst + (i + 2 * stride) * 16, v2);
+            st128(dst + (i + 3 * stride) * 16, v3);
+        }
+        for (; i < end; i += stride) st128(dst + i * 16, ld128(src + i * 16));
+    }
+    end_barrier(ps, epoch, 1, max_ns);
+}
+
+// ---- MoE routing (counting sort) ---------------------------------------------------------------
+
+// K1: per-block expert histogram of rows [b * R, (b + 1) * R).
+__global__ void route_hist_kernel(const int32_t *idx, uint64_t rows, int nexp, uint32_t *hist) {
+    extern __shared__ uint32_t sh[];
+    for (int e = threadIdx.x; e < nexp; e += blockDim.x) sh[e] = 0;
+    __syncthreads();
+    const uint64_t b0 = uint64_t(blockIdx.x) * kRouteRowsPerBlock;
+    const uint64_t b1 = min(rows, b0 + kRouteRowsPerBlock);
+    for (uint64_t r = b0 + threadIdx.x; r < b1; r += blockDim.x) {
+        const int e = idx[r];
+        if (e >= 0 && e < nexp) atomicAdd(&sh[e], 1u);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < nexp; e += blockDim.x) hist[uint64_t(blockIdx.x) * nexp + e] = sh[e];
+}
+
+// K2: per expert, exclusive scan over blocks (in place: hist becomes block offsets) + totals.
+__global__ void route_scan_kernel(uint32_t *hist, int nblocks, int nexp, int32_t *counts) {
+    const int e = blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= nexp) return;
+    uint32_t run = 0;
+    for (int b = 0; b < nblocks; ++b) {
+        const uint32_t c = hist[uint64_t(b) * nexp + e];
+        hist[uint64_t(b) * nexp + e] = run;
+        run += c;
+    }
+    counts[e] = int32_t(run);
+}
+
+// K3: positions in row order; one warp walks its block's rows 32 at a time and ranks equal
+// experts with __match_any_sync, so the result is deterministic.
+__global__ void route_place_kernel(const int32_t *idx, uint64_t rows, int nexp, const uint32_t *off,
+                                   int32_t *pos) {
+    extern __shared__ uint32_t cur[];
+    for (int e = threadIdx.x; e < nexp; e += blockDim.x) cur[e] = off[uint64_t(blockIdx.x) * nexp + e];
+    __syncwarp();
+    const int lane = threadIdx.x & 31;
+    const uint64_t b0 = uint64_t(blockIdx.x) * kRouteRowsPerBlock;
+    const uint64_t b1 = min(rows, b0 + kRouteRowsPerBlock);
+    for (uint64_t r0 = b0; r0 < b1; r0 += 32) {
+        const uint64_t r = r0 + lane;
+        const bool live = r < b1;
+        int e = live ? idx[r] : -1;
+        const bool ok = live && e >= 0 && e < nexp;
+        if (!ok) e = -1 - lane;  // unique key: never matches a real expert or another lane
+        const unsigned same = __match_any_sync(0xffffffffu, e);
+        const unsigned lower = same & ((1u << lane) - 1);
+        const uint32_t base = ok ? cur[e] : 0;
+        __syncwarp();
+        if (ok && lower == 0) cur[e] = base + __popc(same);
+        __syncwarp();
+        if (live) pos[r] = ok ? int32_t(base + __popc(lower)) : -1;
+    }
+}
+
+// ---- MoE dispatch / combine --------------------------------------------------------------------
+
+// Dispatch: row (t, k) -> recv buffer of the expert's owner at row dst_row[e_base + rank part].
+// `gbase[e]` = first row of expert e's group in its owner's buffer for rows of THIS rank
+// (expert group start + rows of the lower ranks for that expert).
+__global__ void __launch_bounds__(512) dispatch_kernel(PeerSet ps, const uint8_t *x, uint64_t row_bytes,
+                                                       const int32_t *idx, const int32_t *pos,
+                                                       const int64_t *gbase, uint64_t rows, int topk,
+                                                       int exp_per_rank, uint64_t recv_off, uint64_t recv_rows,
+                                                       uint64_t epoch, uint64_t max_ns) {
+    const int lane = threadIdx.x & 31;
+    const uint64_t warp = (uint64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const uint64_t nwarps = (uint64_t(gridDim.x) * blockDim.x) >> 5;
+    const uint64_t nv = row_bytes / 16;
+    for (uint64_t r = warp; r < rows; r += nwarps) {
+        const int e = idx[r];
+        const int p = pos[r];
+        if (e < 0 || p < 0) continue;
+        const int owner = e / exp_per_rank;
+        const uint64_t drow = uint64_t(gbase[e]) + uint64_t(p);
+        if (owner >= ps.n || drow >= recv_rows) {
+            atomicExch(ps.status, 2u);  // receive buffer too small: recorded, row skipped
+            continue;
+        }
+        const uint4 *src = reinterpret_cast<const uint4 *>(x + (r / topk) * row_bytes);
+        uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(ps.buf[owner]) + recv_off +
+                                               drow * row_bytes);
+        uint64_t i = lane;
+        for (; i + 96 < nv; i += 128) {
+            const uint4 a = ld128(src + i), b = ld128(src + i + 32), c = ld128(src + i + 64), d = ld128(src + i + 96);
+            st128(dst + i, a);
+            st128(dst + i + 32, b);
+            st128(dst + i + 64, c);
+            st128(dst + i + 96, d);
+        }
+        for (; i < nv; i += 32) st128(dst + i, ld128(src + i));
+    }
+    end_barrier(ps, epoch, 2, max_ns);
+}
+
+// Combine: out[t] = sum_k w[t, k] * expert_out_row(t, k), rows pulled from their owners.
+__global__ void __launch_bounds__(512) combine_kernel(PeerSet ps, uint8_t *out, uint64_t row_bytes,
+                                                      const int32_t *idx, const int32_t *pos,
+                                                      const int64_t *gbase, const float *w, uint64_t ntok,
+                                                      int topk, int exp_per_rank, uint64_t recv_off,
+                                                      uint64_t recv_rows, uint64_t epoch, uint64_t max_ns) {
+    const int lane = threadIdx.x & 31;
+    const uint64_t warp = (uint64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const uint64_t nwarps = (uint64_t(gridDim.x) * blockDim.x) >> 5;
+    const uint64_t nv = row_bytes / 16;
+    for (uint64_t t = warp; t < ntok; t += nwarps) {
+        for (uint64_t i = lane; i < nv; i += 32) {
+            float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            for (int k = 0; k < topk; ++k) {
+                const uint64_t r = t * topk + k;
+                const int e = idx[r], p = pos[r];
+                if (e < 0 || p < 0) continue;
+                const int owner = e / exp_per_rank;
+                const uint64_t srow = uint64_t(gbase[e]) + uint64_t(p);
+                if (owner >= ps.n || srow >= recv_rows) continue;
+                const uint4 v = ld128(reinterpret_cast<const uint8_t *>(ps.buf[owner]) + recv_off +
+                                      srow * row_bytes + i * 16);
+                const float wk = w[r];
+                float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                acc8(f, v);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) a[j] += wk * f[j];
+            }
+            st128(out + t * row_bytes + i * 16, pack8(a));
+        }
+    }
+    end_barrier(ps, epoch, 3, max_ns);
+}
+
+// Counts exchange: this rank's per-expert counts stored into every rank's table
+// (table[rank * nexp + e], int32, at byte `table_off` of each buffer), then the end barrier.
+__global__ void counts_exchange_kernel(PeerSet ps, const int32_t *counts, int nexp, uint64_t table_off,
+                                       uint64_t epoch, uint64_t max_ns) {
+    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < nexp; e += gridDim.x * blockDim.x) {
+        const int32_t c = counts[e];
+        for (int q = 0; q < ps.n; ++q) {
+            int32_t *t = reinterpret_cast<int32_t *>(reinterpret_cast<uint8_t *>(ps.buf[q]) + table_off);
+            t[ps.rank * nexp + e] = c;
+        }
+    }
+    end_barrier(ps, epoch, 4, max_ns);
+}
+
+// Layout (one block): expert e's group in its owner's receive area starts after the groups of
+// the owner's lower experts; this rank's rows for e follow the rows of the lower ranks.
+__global__ void layout_kernel(PeerSet ps, int nexp, int exp_per_rank, uint64_t table_off, int64_t *gbase,
+                              int64_t *recv_used) {
+    const int32_t *t =
+        reinterpret_cast<const int32_t *>(reinterpret_cast<const uint8_t *>(ps.buf[ps.rank]) + table_off);
+    if (threadIdx.x != 0) return;
+    int64_t group = 0;
+    for (int e = 0; e < nexp; ++e) {
+        if (e % exp_per_rank == 0) group = 0;
+        int64_t lower = 0, total = 0;
+        for (int q = 0; q < ps.n; ++q) {
+            const int64_t c = t[q * nexp + e];
+            if (q < ps.rank) lower += c;
+            total += c;
+        }
+        gbase[e] = group + lower;
+        group += total;
+        if (e / exp_per_rank == ps.rank) *recv_used = group;
+    }
+}
+
+}  // namespace
+
+int launch_layout(const PeerSet &ps, const int32_t *counts, int nexp, int exp_per_rank, uint64_t table_off,
+                  int64_t *gbase, int64_t *recv_used, uint64_t epoch, uint64_t max_ns, cudaStream_t s) {
+    counts_exchange_kernel<<<1, 256, 0, s>>>(ps, counts, nexp, table_off, epoch, max_ns);
+    layout_kernel<<<1, 32, 0, s>>>(ps, nexp, exp_per_rank, table_off, gbase, recv_used);
+    return int(cudaGetLastError());
+}
+
+int grid_for(int device) {
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    return sms;
+}
+
+int launch_allreduce_bf16(const PeerSet &ps, uint64_t offset, uint64_t count, uint64_t epoch, int ctas,
+                          uint64_t max_ns, cudaStream_t s) {
+    if (count % 8 != 0 || offset % 16 != 0) return int(cudaErrorInvalidValue);
+    const uint64_t nvec = count / 8;
+    switch (ps.n) {
+    case 1: reduce_scatter_kernel<1><<<ctas, 512, 0, s>>>(ps, offset, nvec, epoch, max_ns); break;
+    case 2: reduce_scatter_kernel<2><<<ctas, 512, 0, s>>>(ps, offset, nvec, epoch, max_ns); break;
+    case 3:
+    case 4: reduce_scatter_kernel<4><<<ctas, 512, 0, s>>>(ps, offset, nvec, epoch, max_ns); break;
+    default: reduce_scatter_kernel<8><<<ctas, 512, 0, s>>>(ps, offset, nvec, epoch, max_ns); break;
+    }
+    all_gather_kernel<<<ctas, 512, 0, s>>>(ps, offset, nvec, epoch, max_ns);
+    return int(cudaGetLastError());
+}
+
+size_t route_scratch_bytes(uint64_t rows, int nexp) {
+    const uint64_t nblocks = (rows + kRouteRowsPerBlock - 1) / kRouteRowsPerBlock;
+    return size_t(nblocks) * size_t(nexp) * sizeof(uint32_t);
+}
+
+int launch_route(const int32_t *idx, uint64_t rows, int nexp, int32_t *counts, int32_t *pos, uint32_t *scratch,
+                 cudaStream_t s) {
+    if (nexp <= 0 || nexp > kRouteMaxExperts) return int(cudaErrorInvalidValue);
+    const int nblocks = int((rows + kRouteRowsPerBlock - 1) / kRouteRowsPerBlock);
+    const size_t sh = size_t(nexp) * sizeof(uint32_t);
+    if (nblocks > 0) route_hist_kernel<<<nblocks, 256, sh, s>>>(idx, rows, nexp, scratch);
+    route_scan_kernel<<<(nexp + 127) / 128, 128, 0, s>>>(scratch, nblocks, nexp, counts);
+    if (nblocks > 0) route_place_kernel<<<nblocks, 32, sh, s>>>(idx, rows, nexp, scratch, pos);
+    return int(cudaGetLastError());
+}
+
+int launch_dispatch(const PeerSet &ps, const void *x, uint64_t row_bytes, const int32_t *idx, const int32_t *pos,
+                    const int64_t *gbase, uint64_t ntok, int topk, int exp_per_rank, uint64_t recv_off,
+                    uint64_t recv_rows, uint64_t epoch, int ctas, uint64_t max_ns, cudaStream_t s) {
+    if (row_bytes % 16 != 0) return int(cudaErrorInvalidValue);
+    dispatch_kernel<<<ctas, 512, 0, s>>>(ps, static_cast<const uint8_t *>(x), row_bytes, idx, pos, gbase,
+                                         ntok * uint64_t(topk), topk, exp_per_rank, recv_off, recv_rows, epoch,
+                                         max_ns);
+    return int(cudaGetLastError());
+}
+
+int launch_combine(const PeerSet &ps, void *out, uint64_t row_bytes, const int32_t *idx, const int32_t *pos,
+                   const int64_t *gbase, const float *w, uint64_t ntok, int topk, int exp_per_rank,
+                   uint64_t recv_off, uint64_t recv_rows, uint64_t epoch, int ctas, uint64_t max_ns,
+                   cudaStream_t s) {
+    if (row_bytes % 16 != 0) return int(cudaErrorInvalidValue);
+    combine_kernel<<<ctas, 512, 0, s>>>(ps, static_cast<uint8_t *>(out), row_bytes, idx, pos, gbase, w, ntok, topk,
+                                        exp_per_rank, recv_off, recv_rows, epoch, max_ns);
+    return int(cudaGetLastError());
+}
+
+}  // namespace ugdr::coll

@@ -1,0 +1,73 @@
+/* ugdr collective extensions: allreduce (bf16, fused sum) and MoE all-to-all (fused permutes)
+ * over CUDA-IPC mapped peer buffers, plus the IPC export / open helpers that build the peer view.
+ * No counterpart in the reference (it has no collectives); they reuse its memory model.
+ *
+ * All launch functions are asynchronous on `stream` (a cudaStream_t, NULL for the legacy
+ * stream) and return a cudaError_t value.  Cross-GPU waits inside the kernels are bounded; when
+ * one runs out the kernel stores 1 in *status of the peer set (2 = receive buffer overflow). */
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define UGDR_X_MAX_RANKS 8
+#define UGDR_X_IPC_HANDLE_BYTES 64
+
+/* Layout identical to the kernels' peer set. */
+typedef struct ugdr_x_peerset {
+    void *buf[UGDR_X_MAX_RANKS];
+    uint64_t *signal[UGDR_X_MAX_RANKS];
+    unsigned int *arrive;
+    unsigned int *status;
+    int n;
+    int rank;
+} ugdr_x_peerset;
+
+/* Export the allocation holding `ptr` (cudaMalloc memory) for another process: the handle of
+ * the allocation base and the offset of `ptr` inside it. */
+int ugdr_x_ipc_export(void *ptr, uint8_t handle[UGDR_X_IPC_HANDLE_BYTES], uint64_t *offset);
+/* Open an exported allocation in the current device's context; *base receives the mapping. */
+int ugdr_x_ipc_open(const uint8_t handle[UGDR_X_IPC_HANDLE_BYTES], void **base);
+int ugdr_x_ipc_close(void *base);
+
+/* In-place allreduce of `count` bf16 elements at byte `offset` of every rank's buffer (count a
+ * multiple of 8, offset a multiple of 16).  `epoch` increases by one per call on every rank. */
+int ugdr_x_allreduce_bf16(const ugdr_x_peerset *ps, uint64_t offset, uint64_t count, uint64_t epoch,
+                          int ctas, void *stream);
+
+/* MoE routing: rows = tokens * topk expert ids (int32, row r = token r / topk).  Writes the row
+ * count of every expert and each row's position inside its expert group, in row order (rows
+ * with an id outside [0, nexp) get position -1).  `scratch` holds
+ * ugdr_x_moe_route_scratch_bytes(rows, nexp) bytes of device memory. */
+size_t ugdr_x_moe_route_scratch_bytes(uint64_t rows, int nexp);
+int ugdr_x_moe_route(const int32_t *expert_ids, uint64_t rows, int nexp, int32_t *counts, int32_t *positions,
+                     void *scratch, size_t scratch_bytes, void *stream);
+
+/* Layout: exchange every rank's expert counts through the peer buffers (an nranks * nexp int32
+ * table at byte `table_offset` of each buffer), then compute group_base[e] for this rank's rows
+ * and *recv_used, the rows this rank will receive.  Experts are owned in blocks of
+ * experts_per_rank (expert e lives on rank e / experts_per_rank). */
+int ugdr_x_moe_layout(const ugdr_x_peerset *ps, const int32_t *counts, int nexp, int experts_per_rank,
+                      uint64_t table_offset, int64_t *group_base, int64_t *recv_used, uint64_t epoch,
+                      void *stream);
+
+/* Dispatch: row (t, k) of this rank is stored into the receive area of the owner of expert
+ * e = expert_ids[t*topk+k] (owner = e / experts_per_rank) at row group_base[e] + positions[r].
+ * group_base[e] already includes the rows that lower ranks send to expert e. */
+int ugdr_x_moe_dispatch(const ugdr_x_peerset *ps, const void *x, uint64_t row_bytes, const int32_t *expert_ids,
+                        const int32_t *positions, const int64_t *group_base, uint64_t tokens, int topk,
+                        int experts_per_rank, uint64_t recv_offset, uint64_t recv_rows, uint64_t epoch,
+                        int ctas, void *stream);
+/* Combine: out[t] = sum_k weights[t*topk+k] * (the owner's row for (t, k)), fp32 accumulation. */
+int ugdr_x_moe_combine(const ugdr_x_peerset *ps, void *out, uint64_t row_bytes, const int32_t *expert_ids,
+                       const int32_t *positions, const int64_t *group_base, const float *weights,
+                       uint64_t tokens, int topk, int experts_per_rank, uint64_t recv_offset, uint64_t recv_rows,
+                       uint64_t epoch, int ctas, void *stream);
+
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,162 @@
+"""Collective kernels against plain torch fp32 references: MoE routing (1 GPU), allreduce and
+the MoE all-to-all on 1 rank and on 2 ranks (one process per GPU, gloo for the handle exchange)."""
+from __future__ import annotations
+
+import os
+
+import pytest
+
+from conftest import gpu_count
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def one_gpu():
+    if gpu_count() < 1:
+        pytest.skip("no GPU")
+    torch.cuda.set_device(0)
+
+
+@pytest.mark.parametrize("tokens,experts,topk", [(1, 8, 2), (1000, 256, 8), (16384, 256, 8), (5000, 64, 3)])
+def test_moe_route_matches_reference(one_gpu, tokens, experts, topk):
+    from ugdr_b200.models.moe import reference_positions, route
+    from ugdr_b200.parallel.collectives import moe_route
+
+    ids, _ = route(tokens, experts, topk, seed=tokens)
+    counts, pos = moe_route(ids, experts)
+    rc, rp = reference_positions(ids, experts)
+    assert torch.equal(counts, rc)
+    assert torch.equal(pos, rp)
+
+
+def test_moe_route_rejects_out_of_range_ids(one_gpu):
+    from ugdr_b200.parallel.collectives import moe_route
+
+    ids = torch.tensor([[0, 5], [9, 1], [-1, 0]], dtype=torch.int32, device="cuda")
+    counts, pos = moe_route(ids, 8)
+    assert counts.tolist() == [2, 1, 0, 0, 0, 1, 0, 0]
+    assert pos.tolist() == [[0, 0], [-1, 0], [-1, 1]]
+
+
+def _single_rank_group(nbytes):
+    from ugdr_b200.parallel.peers import PeerGroup
+
+    return PeerGroup(nbytes, 0, 1, lambda x: [x])
+
+
+def test_allreduce_single_rank_is_identity(one_gpu):
+    from ugdr_b200.parallel.collectives import allreduce_bf16
+
+    g = _single_rank_group(1 << 20)
+    x = g.view(torch.bfloat16, 1 << 19)
+    x.copy_(torch.randn(1 << 19, device="cuda").to(torch.bfloat16))
+    ref = x.clone()
+    allreduce_bf16(g, 1 << 19)
+    torch.cuda.synchronize()
+    g.check_status()
+    assert torch.equal(x, ref)
+
+
+def test_moe_all_to_all_single_rank(one_gpu):
+    from ugdr_b200.models.moe import route
+    from ugdr_b200.parallel.collectives import MoEAllToAll
+
+    tokens, hidden, topk, experts = 512, 1024, 4, 16
+    recv = tokens * topk
+    g = _single_rank_group(MoEAllToAll.required_bytes(1, experts, hidden, recv))
+    a2a = MoEAllToAll(g, tokens, hidden, topk, experts, recv)
+    x = torch.randn(tokens, hidden, device="cuda").to(torch.bfloat16)
+    ids, w = route(tokens, experts, topk, seed=1)
+    a2a.dispatch(x, ids)
+    out = a2a.combine(w)
+    torch.cuda.synchronize()
+    g.check_status()
+    # Rows landed grouped by expert, in token order inside each group.
+    rv = a2a.recv_view()
+    flat = ids.reshape(-1).long()
+    order = torch.sort(flat, stable=True).indices
+    assert torch.equal(rv[:recv], x[order // topk])
+    ref = (x.float() * w.sum(-1, keepdim=True)).to(torch.bfloat16)
+    assert torch.allclose(out.float(), ref.float(), atol=2e-2, rtol=1e-2)
+
+
+def _worker(rank, world, port, q):
+    try:
+        import torch.distributed as dist
+
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+
+        def exchange(obj):
+            out = [None] * world
+            dist.all_gather_object(out, obj)
+            return out
+
+        from ugdr_b200.models.moe import route
+        from ugdr_b200.parallel.collectives import MoEAllToAll, allreduce_bf16
+        from ugdr_b200.parallel.peers import PeerGroup
+
+        # allreduce: bf16 inputs, fp32 reference, several calls in a row
+        n = (3 << 20) + 8
+        g = PeerGroup(n * 2, rank, world, exchange)
+        for it in range(3):
+            xs = [torch.randn(n, generator=torch.Generator().manual_seed(100 * it + r)).to(torch.bfloat16)
+                  for r in range(world)]
+            v = g.view(torch.bfloat16, n)
+            v.copy_(xs[rank].cuda())
+            torch.cuda.synchronize()
+            dist.barrier()
+            allreduce_bf16(g, n)
+            torch.cuda.synchronize()
+            g.check_status()
+            ref = sum(x.float() for x in xs)
+            err = (v.float().cpu() - ref).abs().max().item()
+            assert err <= 0.05 * (1 + ref.abs().max().item()) / 8, f"allreduce error {err}"
+        # MoE all-to-all
+        tokens, hidden, topk, experts = 1024, 2048, 8, 32
+        recv = tokens * topk * world
+        mg = PeerGroup(MoEAllToAll.required_bytes(world, experts, hidden, recv), rank, world, exchange)
+        a2a = MoEAllToAll(mg, tokens, hidden, topk, experts, recv)
+        x = torch.randn(tokens, hidden, generator=torch.Generator().manual_seed(rank)).to(torch.bfloat16).cuda()
+        ids, w = route(tokens, experts, topk, seed=7 + rank)
+        for _ in range(2):
+            a2a.dispatch(x, ids)
+            out = a2a.combine(w)
+        torch.cuda.synchronize()
+        mg.check_status()
+        ref = (x.float() * w.sum(-1, keepdim=True)).to(torch.bfloat16)
+        assert torch.allclose(out.float(), ref.float(), atol=3e-2, rtol=2e-2)
+        # Receive side: every row this rank got belongs to one of its experts, grouped by expert.
+        used = int(a2a.recv_used.item())
+        assert used > 0
+        dist.barrier()
+        q.put((rank, "ok"))
+    except BaseException as e:  # report to the parent
+        q.put((rank, repr(e)))
+
+
+def test_two_rank_allreduce_and_moe():
+    if gpu_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29600 + os.getpid() % 200
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    results = {}
+    try:
+        for _ in ps:
+            r, msg = q.get(timeout=300)
+            results[r] = msg
+    finally:
+        for p in ps:
+            p.join(60)
+            if p.is_alive():
+                p.kill()
+    assert results == {0: "ok", 1: "ok"}, results
