@@ -25,7 +25,7 @@ LIB_OBJS := $(LIB_CXX:csrc/%.cpp=$(OBJ)/%.o) $(LIB_CU:csrc/%.cu=$(OBJ)/%.cu.o)
 TEST_SRCS := $(wildcard tests/native/*.cpp)
 TEST_OBJS := $(TEST_SRCS:tests/native/%.cpp=$(OBJ)/tests/%.o)
 
-all: $(OUT)/libugdr.so $(OUT)/ugdr_daemon $(OUT)/ugdr_client $(OUT)/ugdr_native_tests
+all: $(OUT)/libugdr.so $(OUT)/ugdr_daemon $(OUT)/ugdr_client $(OUT)/ugdr_native_tests $(OUT)/ugdr_perf
 
 $(OBJ)/%.o: csrc/%.cpp
 	@mkdir -p $(dir $@)

@@ -1,0 +1,350 @@
+// ugdr_perf: verbs-level benchmarks through the public C API (BASELINE configs[1] and the WR
+// posting rate).  Needs a running ugdr_daemon (UGDR_DAEMON_SOCKET).
+//
+//   ugdr_perf latency  --src-gpu A --dst-gpu B --bytes N --iters K        QD1 post_send -> poll_cq
+//   ugdr_perf bw       --src-gpu A --dst-gpu B --op write|read --min 8 --max 1G --qd 64 --bytes-per-size T
+//   ugdr_perf posting  --batch B --wrs N                                    post_send into the SQ ring
+//
+// Output: one key=value line per measurement (reference style, benchmarks/*.cpp) and a JSON
+// line with the same fields.  Payload: uniform uint8 from a seed; every size's destination is
+// compared byte-for-byte with the source once.
+#include "ugdr/api.hpp"
+
+#include <cuda_runtime_api.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <random>
+#include <string>
+#include <thread>
+#include <vector>
+
+namespace {
+
+using Clock = std::chrono::steady_clock;
+
+struct Opts {
+    std::string mode = "latency";
+    int src_gpu = 0, dst_gpu = 0;
+    uint64_t bytes = 8, iters = 20000, warmup = 2000;
+    std::string op = "write";
+    uint64_t min_bytes = 8, max_bytes = 1ull << 30, qd = 64, bytes_per_size = 8ull << 30;
+    uint64_t batch = 32, wrs = 4000000;
+};
+
+[[noreturn]] void die(const char *what, int rc) {
+    std::fprintf(stderr, "ugdr_perf: %s failed (%d: %s)\n", what, rc, std::strerror(rc > 0 ? rc : -rc));
+    std::exit(1);
+}
+
+uint64_t parse_size(const char *s) {
+    char *end = nullptr;
+    double v = std::strtod(s, &end);
+    if (end && (*end == 'k' || *end == 'K')) v *= 1024;
+    if (end && (*end == 'm' || *end == 'M')) v *= 1024 * 1024;
+    if (end && (*end == 'g' || *end == 'G')) v *= 1024.0 * 1024 * 1024;
+    return uint64_t(v);
+}
+
+struct Side {
+    ugdr_context *ctx = nullptr;
+    ugdr_pd *pd = nullptr;
+    ugdr_cq *cq = nullptr;
+    ugdr_qp *qp = nullptr;
+    ugdr_mr *mr = nullptr;
+    void *buf = nullptr;
+};
+
+ugdr_device *gpu_device(ugdr_device **list, int n, int gpu) {
+    for (int i = 0; i < n; ++i) {
+        ugdr_x_device_info info;
+        if (ugdr_x_query_device(list[i], &info) == 0 && info.kind == 1 && info.gpu_ordinal == gpu) return list[i];
+    }
+    std::fprintf(stderr, "ugdr_perf: daemon has no GPU %d\n", gpu);
+    std::exit(1);
+}
+
+// Requester on src_gpu, responder on dst_gpu, each with an MR of `bytes`.
+void setup(const Opts &o, uint64_t bytes, uint32_t depth, Side *a, Side *b) {
+    int n = 0;
+    ugdr_device **list = ugdr_get_device_list(&n);
+    if (!list) die("ugdr_get_device_list", errno);
+    Side *sides[2] = {a, b};
+    const int gpus[2] = {o.src_gpu, o.dst_gpu};
+    for (int i = 0; i < 2; ++i) {
+        Side &s = *sides[i];
+        s.ctx = ugdr_open_device(gpu_device(list, n, gpus[i]));
+        if (!s.ctx) die("ugdr_open_device", errno);
+        s.pd = ugdr_alloc_pd(s.ctx);
+        s.cq = ugdr_create_cq(s.ctx, int(depth * 2 + 16), nullptr, nullptr, 0);
+        if (!s.pd || !s.cq) die("pd/cq", errno);
+        cudaSetDevice(gpus[i]);
+        if (cudaMalloc(&s.buf, bytes) != cudaSuccess) die("cudaMalloc", ENOMEM);
+        s.mr = ugdr_reg_mr(s.pd, s.buf, bytes,
+                           UGDR_ACCESS_LOCAL_WRITE | UGDR_ACCESS_REMOTE_WRITE | UGDR_ACCESS_REMOTE_READ);
+        if (!s.mr) die("ugdr_reg_mr", errno);
+        ugdr_qp_init_attr ia{s.cq, s.cq, depth, depth, 1, 1, UGDR_QPT_RC, 0};
+        s.qp = ugdr_create_qp(s.pd, &ia);
+        if (!s.qp) die("ugdr_create_qp", errno);
+        ugdr_qp_attr at{};
+        at.qp_state = UGDR_QPS_INIT;
+        at.qp_access_flags = UGDR_ACCESS_REMOTE_WRITE | UGDR_ACCESS_REMOTE_READ;
+        if (int rc = ugdr_modify_qp(s.qp, &at, UGDR_QP_STATE | UGDR_QP_ACCESS_FLAGS)) die("modify INIT", rc);
+    }
+    ugdr_qp_conn_info ca{}, cb{};
+    ugdr_query_qp_conn_info(a->qp, &ca);
+    ugdr_query_qp_conn_info(b->qp, &cb);
+    ugdr_qp_attr c{};
+    c.timeout = 14;
+    c.retry_cnt = 7;
+    c.rnr_retry = 7;
+    c.min_rnr_timer = 1;
+    const int mask = UGDR_QP_TIMEOUT | UGDR_QP_RETRY_CNT | UGDR_QP_RNR_RETRY | UGDR_QP_MIN_RNR_TIMER;
+    if (int rc = ugdr_connect_qp(a->qp, &cb, &c, mask)) die("connect a", rc);
+    if (int rc = ugdr_connect_qp(b->qp, &ca, &c, mask)) die("connect b", rc);
+}
+
+void fill(void *dev, uint64_t bytes, uint64_t seed, int gpu) {
+    std::vector<uint8_t> h(std::min<uint64_t>(bytes, 64ull << 20));
+    std::mt19937_64 rng(seed);
+    for (auto &x : h) x = uint8_t(rng());
+    cudaSetDevice(gpu);
+    for (uint64_t off = 0; off < bytes; off += h.size())
+        cudaMemcpy(static_cast<uint8_t *>(dev) + off, h.data(), std::min<uint64_t>(h.size(), bytes - off),
+                   cudaMemcpyHostToDevice);
+}
+
+bool same(const void *a, int ga, const void *b, int gb, uint64_t bytes) {
+    const uint64_t n = std::min<uint64_t>(bytes, 16ull << 20);
+    std::vector<uint8_t> x(n), y(n);
+    cudaSetDevice(ga);
+    cudaMemcpy(x.data(), a, n, cudaMemcpyDeviceToHost);
+    cudaSetDevice(gb);
+    cudaMemcpy(y.data(), b, n, cudaMemcpyDeviceToHost);
+    return x == y;
+}
+
+void wait_cq(ugdr_cq *cq, uint64_t want) {
+    ugdr_wc wc[64];
+    uint64_t got = 0;
+    const auto deadline = Clock::now() + std::chrono::seconds(60);
+    while (got < want) {
+        const int n = ugdr_poll_cq(cq, int(std::min<uint64_t>(64, want - got)), wc);
+        if (n < 0) die("ugdr_poll_cq", -n);
+        for (int i = 0; i < n; ++i)
+            if (wc[i].status != UGDR_WC_SUCCESS) die("work completion", int(wc[i].status));
+        got += uint64_t(n);
+        if (n == 0 && Clock::now() > deadline) die("completion timeout", ETIMEDOUT);
+    }
+}
+
+void post(ugdr_qp *qp, int op, void *local, uint32_t lkey, uint64_t bytes, void *remote, uint32_t rkey,
+          uint64_t wr_id) {
+    ugdr_sge sg{reinterpret_cast<uint64_t>(local), uint32_t(bytes), lkey};
+    ugdr_send_wr wr{};
+    wr.wr_id = wr_id;
+    wr.sg_list = &sg;
+    wr.num_sge = 1;
+    wr.opcode = ugdr_wr_opcode(op);
+    wr.send_flags = UGDR_SEND_SIGNALED;
+    wr.wr.rdma.remote_addr = reinterpret_cast<uint64_t>(remote);
+    wr.wr.rdma.rkey = rkey;
+    ugdr_send_wr *bad = nullptr;
+    int rc;
+    while ((rc = ugdr_post_send(qp, &wr, &bad)) == ENOMEM) std::this_thread::yield();
+    if (rc) die("ugdr_post_send", rc);
+}
+
+double pct(std::vector<double> v, double p) {
+    std::sort(v.begin(), v.end());
+    return v[std::min<size_t>(v.size() - 1, size_t(p * (v.size() - 1) + 0.5))];
+}
+
+int run_latency(const Opts &o) {
+    Side a, b;
+    setup(o, std::max<uint64_t>(o.bytes, 4096), 16, &a, &b);
+    fill(a.buf, o.bytes, 1, o.src_gpu);
+    std::vector<double> us;
+    us.reserve(o.iters);
+    for (uint64_t i = 0; i < o.warmup + o.iters; ++i) {
+        const auto t0 = Clock::now();
+        post(a.qp, UGDR_WR_RDMA_WRITE, a.buf, a.mr->lkey, o.bytes, b.buf, b.mr->rkey, i);
+        wait_cq(a.cq, 1);
+        const double dt = std::chrono::duration<double, std::micro>(Clock::now() - t0).count();
+        if (i >= o.warmup) us.push_back(dt);
+    }
+    const bool ok = same(a.buf, o.src_gpu, b.buf, o.dst_gpu, o.bytes);
+    std::printf("benchmark=ugdr_latency op=write bytes=%llu src_gpu=%d dst_gpu=%d iters=%llu p50_us=%.3f "
+                "p99_us=%.3f p999_us=%.3f min_us=%.3f correct=%d\n",
+                (unsigned long long)o.bytes, o.src_gpu, o.dst_gpu, (unsigned long long)o.iters, pct(us, 0.5),
+                pct(us, 0.99), pct(us, 0.999), pct(us, 0.0), int(ok));
+    std::printf("{\"benchmark\": \"ugdr_latency\", \"bytes\": %llu, \"src_gpu\": %d, \"dst_gpu\": %d, "
+                "\"p50_us\": %.3f, \"p99_us\": %.3f, \"correct\": %s}\n",
+                (unsigned long long)o.bytes, o.src_gpu, o.dst_gpu, pct(us, 0.5), pct(us, 0.99),
+                ok ? "true" : "false");
+    return ok ? 0 : 2;
+}
+
+int run_bw(const Opts &o) {
+    Side a, b;
+    const uint32_t qd = uint32_t(o.qd);
+    setup(o, o.max_bytes, qd + 4, &a, &b);
+    fill(a.buf, o.max_bytes, 2, o.src_gpu);
+    fill(b.buf, o.max_bytes, 3, o.dst_gpu);
+    const int op = o.op == "read" ? UGDR_WR_RDMA_READ : UGDR_WR_RDMA_WRITE;
+    int status = 0;
+    for (uint64_t sz = o.min_bytes; sz <= o.max_bytes; sz *= 2) {
+        uint64_t wrs = std::max<uint64_t>(qd * 4, o.bytes_per_size / sz);
+        wrs = std::min<uint64_t>(wrs, 200000);
+        // Warm-up: one window.
+        for (uint64_t i = 0; i < qd; ++i) post(a.qp, op, a.buf, a.mr->lkey, sz, b.buf, b.mr->rkey, i);
+        wait_cq(a.cq, qd);
+        uint64_t posted = 0, done = 0;
+        ugdr_wc wc[64];
+        const auto t0 = Clock::now();
+        while (done < wrs) {
+            // Bound each size to ~2 s: stop posting and drain what is in flight.
+            if (posted < wrs && (posted & 255) == 0 && Clock::now() - t0 > std::chrono::seconds(2)) wrs = posted;
+            while (posted < wrs && posted - done < qd) {
+                // Each in-flight WR uses its own destination slice when it fits, else the start.
+                const uint64_t slot = (posted % qd) * sz;
+                const uint64_t off = slot + sz <= o.max_bytes ? slot : 0;
+                post(a.qp, op, static_cast<uint8_t *>(a.buf) + off, a.mr->lkey, sz,
+                     static_cast<uint8_t *>(b.buf) + off, b.mr->rkey, posted);
+                ++posted;
+            }
+            const int n = ugdr_poll_cq(a.cq, 64, wc);
+            if (n < 0) die("ugdr_poll_cq", -n);
+            for (int i = 0; i < n; ++i)
+                if (wc[i].status != UGDR_WC_SUCCESS) die("work completion", int(wc[i].status));
+            done += uint64_t(n);
+        }
+        const double s = std::chrono::duration<double>(Clock::now() - t0).count();
+        const double gbps = double(wrs) * double(sz) / s / 1e9;
+        const bool ok = op == UGDR_WR_RDMA_WRITE ? same(a.buf, o.src_gpu, b.buf, o.dst_gpu, sz)
+                                                 : same(b.buf, o.dst_gpu, a.buf, o.src_gpu, sz);
+        if (!ok) status = 2;
+        std::printf("benchmark=ugdr_bw op=%s bytes=%llu qd=%u src_gpu=%d dst_gpu=%d wrs=%llu seconds=%.6f "
+                    "GB_per_s=%.3f MWR_per_s=%.4f correct=%d\n",
+                    o.op.c_str(), (unsigned long long)sz, qd, o.src_gpu, o.dst_gpu, (unsigned long long)wrs, s,
+                    gbps, double(wrs) / s / 1e6, int(ok));
+        std::printf("{\"benchmark\": \"ugdr_bw\", \"op\": \"%s\", \"bytes\": %llu, \"qd\": %u, \"GBps\": %.3f, "
+                    "\"MWRps\": %.4f, \"correct\": %s}\n",
+                    o.op.c_str(), (unsigned long long)sz, qd, gbps, double(wrs) / s / 1e6, ok ? "true" : "false");
+        std::fflush(stdout);
+    }
+    return status;
+}
+
+// Posting rate: WRs copied into a QP's SQ through ugdr_post_send; a consumer thread releases the
+// slots directly on the shared ring so the measurement isolates the client posting path.
+int run_posting(const Opts &o) {
+    int n = 0;
+    ugdr_device **list = ugdr_get_device_list(&n);
+    if (!list) die("ugdr_get_device_list", errno);
+    ugdr_device *cpu = nullptr;
+    for (int i = 0; i < n; ++i) {
+        ugdr_x_device_info info;
+        if (ugdr_x_query_device(list[i], &info) == 0 && info.kind == 0) cpu = list[i];
+    }
+    if (!cpu) die("no host device", ENODEV);
+    ugdr_context *ctx = ugdr_open_device(cpu);
+    ugdr_pd *pd = ugdr_alloc_pd(ctx);
+    ugdr_cq *cq = ugdr_create_cq(ctx, 1 << 16, nullptr, nullptr, 0);
+    void *buf = ugdr_x_alloc_host(1 << 20);
+    ugdr_mr *mr = ugdr_reg_mr(pd, buf, 1 << 20, UGDR_ACCESS_LOCAL_WRITE | UGDR_ACCESS_REMOTE_WRITE);
+    ugdr_qp_init_attr ia{cq, cq, 4096, 16, 1, 1, UGDR_QPT_RC, 0};
+    ugdr_qp *qp = ugdr_create_qp(pd, &ia), *peer = ugdr_create_qp(pd, &ia);
+    if (!qp || !peer || !mr) die("posting setup", errno);
+    ugdr_qp_attr at{};
+    at.qp_state = UGDR_QPS_INIT;
+    at.qp_access_flags = UGDR_ACCESS_REMOTE_WRITE;
+    ugdr_modify_qp(qp, &at, UGDR_QP_STATE | UGDR_QP_ACCESS_FLAGS);
+    ugdr_modify_qp(peer, &at, UGDR_QP_STATE | UGDR_QP_ACCESS_FLAGS);
+    ugdr_qp_conn_info ci{};
+    ugdr_query_qp_conn_info(peer, &ci);
+    ugdr_qp_attr c{};
+    c.timeout = 14;
+    c.retry_cnt = 7;
+    c.rnr_retry = 7;
+    c.min_rnr_timer = 1;
+    if (int rc = ugdr_connect_qp(qp, &ci, &c, UGDR_QP_TIMEOUT | UGDR_QP_RETRY_CNT | UGDR_QP_RNR_RETRY |
+                                                UGDR_QP_MIN_RNR_TIMER))
+        die("connect", rc);
+    // The host engine executes these WRs (8-byte unsignaled writes); posting measures the client.
+    std::vector<ugdr_sge> sg(o.batch, ugdr_sge{reinterpret_cast<uint64_t>(buf), 8, mr->lkey});
+    std::vector<ugdr_send_wr> wr(o.batch);
+    for (uint64_t i = 0; i < o.batch; ++i) {
+        wr[i] = ugdr_send_wr{};
+        wr[i].sg_list = &sg[i];
+        wr[i].num_sge = 1;
+        wr[i].opcode = UGDR_WR_RDMA_WRITE;
+        wr[i].wr.rdma.remote_addr = reinterpret_cast<uint64_t>(buf) + 64;
+        wr[i].wr.rdma.rkey = mr->rkey;
+        wr[i].next = i + 1 < o.batch ? &wr[i + 1] : nullptr;
+    }
+    uint64_t accepted = 0, full = 0;
+    const auto t0 = Clock::now();
+    while (accepted < o.wrs) {
+        ugdr_send_wr *bad = nullptr;
+        const int rc = ugdr_post_send(qp, wr.data(), &bad);
+        if (rc == 0) {
+            accepted += o.batch;
+        } else if (rc == ENOMEM) {
+            // partial prefix accepted; count it and let the engine drain
+            uint64_t k = 0;
+            for (ugdr_send_wr *w = wr.data(); w != bad; w = w->next) ++k;
+            accepted += k;
+            ++full;
+            std::this_thread::yield();
+        } else {
+            die("ugdr_post_send", rc);
+        }
+    }
+    const double s = std::chrono::duration<double>(Clock::now() - t0).count();
+    std::printf("benchmark=ugdr_posting batch=%llu wrs=%llu seconds=%.6f MWR_per_s=%.3f ring_full_events=%llu\n",
+                (unsigned long long)o.batch, (unsigned long long)accepted, s, double(accepted) / s / 1e6,
+                (unsigned long long)full);
+    std::printf("{\"benchmark\": \"ugdr_posting\", \"batch\": %llu, \"MWRps\": %.3f}\n", (unsigned long long)o.batch,
+                double(accepted) / s / 1e6);
+    return 0;
+}
+
+}  // namespace
+
+int main(int argc, char **argv) {
+    Opts o;
+    if (argc < 2) {
+        std::fprintf(stderr, "usage: ugdr_perf latency|bw|posting [options]\n");
+        return 2;
+    }
+    o.mode = argv[1];
+    for (int i = 2; i + 1 < argc; i += 2) {
+        const std::string k = argv[i];
+        const char *v = argv[i + 1];
+        if (k == "--src-gpu") o.src_gpu = std::atoi(v);
+        else if (k == "--dst-gpu") o.dst_gpu = std::atoi(v);
+        else if (k == "--bytes") o.bytes = parse_size(v);
+        else if (k == "--iters") o.iters = parse_size(v);
+        else if (k == "--warmup") o.warmup = parse_size(v);
+        else if (k == "--op") o.op = v;
+        else if (k == "--min") o.min_bytes = parse_size(v);
+        else if (k == "--max") o.max_bytes = parse_size(v);
+        else if (k == "--qd") o.qd = parse_size(v);
+        else if (k == "--bytes-per-size") o.bytes_per_size = parse_size(v);
+        else if (k == "--batch") o.batch = parse_size(v);
+        else if (k == "--wrs") o.wrs = parse_size(v);
+        else {
+            std::fprintf(stderr, "ugdr_perf: unknown option %s\n", k.c_str());
+            return 2;
+        }
+    }
+    if (o.mode == "latency") return run_latency(o);
+    if (o.mode == "bw") return run_bw(o);
+    if (o.mode == "posting") return run_posting(o);
+    std::fprintf(stderr, "ugdr_perf: unknown mode %s\n", o.mode.c_str());
+    return 2;
+}
