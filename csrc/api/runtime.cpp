@@ -519,7 +519,9 @@ int ugdr_x_query_engine_stats(ugdr_context *ctx, ugdr_x_engine_stats *stats, int
         !rd.be(&stats->error_completions) || !rd.be(&stats->launches) ||
         !rd.be(&stats->wait_timeouts) || !rd.be(&stats->first_start_ns) || !rd.be(&stats->last_end_ns) ||
         !rd.be(&stats->chunks_run) || !rd.be(&stats->claim_misses) || !rd.be(&stats->jobs_published) ||
-        !rd.be(&stats->inline_runs) || !rd.be(&stats->busy_ns))
+        !rd.be(&stats->inline_runs) || !rd.be(&stats->busy_ns) || !rd.be(&stats->fast_batches) ||
+        !rd.be(&stats->fast_fetch_ns) || !rd.be(&stats->fast_exec_ns) || !rd.be(&stats->fast_reserve_ns) ||
+        !rd.be(&stats->fast_publish_ns))
         return EPROTO;
     return 0;
 }

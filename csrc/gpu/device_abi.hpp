@@ -20,7 +20,7 @@ namespace ugdr::gpu {
 constexpr uint32_t kMaxMrs = 1u << 16;       // key slots (matches the control plane's keys)
 constexpr uint32_t kMaxQpsPerEngine = 4096;
 constexpr uint32_t kMaxCqsPerEngine = 4096;
-constexpr uint32_t kWindow = 4;              // in-flight WRs per QP
+constexpr uint32_t kWindow = 16;             // in-flight WRs per QP
 constexpr uint32_t kMaxSge = 32;
 constexpr uint32_t kJobSlots = 1024;         // large-WR job ring per engine
 constexpr uint32_t kInlineBytes = 4096;      // WRs up to this size are copied by the owner warp
@@ -48,7 +48,7 @@ struct DevCqConfig {
 
 struct DevCqState {
     unsigned long long reserve;    // next slot to hand out (CAS, .sys)
-    unsigned long long published;  // next slot to publish (in order)
+    unsigned long long published;  // unused: the ring tail itself is the in-order publish cursor
     unsigned long long head_seen;  // cached consumer cursor
     unsigned long long pad[5];
 };
@@ -154,6 +154,8 @@ struct DevStats {
     unsigned long long inline_runs;     // WRs copied by their owner warp
     unsigned long long busy_ns;         // summed warp time inside chunk copies
     unsigned long long launches_seen;   // kernel launches (block 0 thread 0)
+    // Small-WR fast path, summed per batch: batches, WQE fetch, validate+copy, CQ reserve, publish.
+    unsigned long long fast_batches, fast_fetch_ns, fast_exec_ns, fast_reserve_ns, fast_publish_ns;
     unsigned long long last_work_ns;
     unsigned long long retired;  // WRs retired since the last reset (drain mode exit test)
     unsigned int exiting;

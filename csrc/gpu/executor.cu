@@ -37,7 +37,7 @@ namespace {
 
 constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
-constexpr uint32_t kWqeBytesMax = 576;  // roundup64(40 + 16 * 32)
+constexpr uint32_t kWqeStage = 1024;  // per-warp WQE staging: 16 slots of 64 B, or one of 576
 constexpr uint32_t kChunkMin = 16384;
 constexpr uint32_t kChunkMax = 262144;
 
@@ -83,6 +83,9 @@ __device__ __forceinline__ void st_vol128(void *p, uint4 v) {
     asm volatile("st.volatile.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
                  "r"(v.z), "r"(v.w)
                  : "memory");
+}
+__device__ __forceinline__ void st_vol64(void *p, uint64_t v) {
+    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 __device__ __forceinline__ uint4 ld128(const void *p) {
     uint4 v;
@@ -183,6 +186,35 @@ __device__ void copy_stream(const WrRec *rec, uint32_t nseg, uint64_t remote, bo
 
 // ---- per-launch warp context -------------------------------------------------------------------
 
+// A QP's configuration as one service pass sees it (read once per pass, in parallel).
+struct QpView {
+    queue::RingHeader *sq;
+    const uint8_t *sq_slots;
+    DevQp *peer;
+    DevCq *send_cq;
+    uint32_t sq_cap, sq_stride, qpn, state, pd, max_sge, sig_all, lost, err, retry_word;
+    // Responder configuration as of the last refresh (at most 20 us old).
+    uint32_t pstate, perr, pactive, pacc, ppd;
+};
+
+// Per-warp cache of the two MR entries the fast path used last.  MR table entries change only
+// while the executor is stopped (deregistration quiesces it), and a key's generation bits make a
+// reused slot miss, so a hit is always current within a launch.
+struct MrCacheEntry {
+    uint32_t key, pad[3];
+    uint4 part[3];
+};
+
+// A warp's cached view of the last CQ it produced into (configuration never changes while the
+// CQ is attached; the cursors are guesses that a failed CAS corrects).
+struct CqCache {
+    DevCq *cq;
+    queue::RingHeader *ring;
+    uint8_t *slots;
+    uint32_t cap, stride;
+    uint64_t reserve, head, published;
+};
+
 struct Warp {
     const ExecParams *p;
     int lane;
@@ -192,7 +224,14 @@ struct Warp {
     bool abort;
     // Private counters, folded into DevStats now and then (hot shared counters would serialise
     // every warp of the grid on one L2 line).
-    uint64_t n_chunks, n_miss, bytes, busy;
+    uint64_t n_chunks, n_miss, bytes, busy, n_inline;
+    bool started;  // this warp stamped first_start_ns in this launch
+    CqCache cq;
+    MrCacheEntry *mrc;  // this warp's two-entry MR cache (shared memory)
+    // Cached view of the QP this warp serviced last (see service_qp).
+    DevQp *vq;
+    uint64_t vt, vhead, vissue, t_reserved;
+    QpView vv;
 };
 
 __device__ void record_error(Warp &w, uint32_t code) {
@@ -215,41 +254,80 @@ __device__ bool wait_eq_sys(const unsigned long long *p, uint64_t want, uint64_t
     return true;
 }
 
-// Multi-producer CQE publish (lane 0 only).  Returns 0 = published, 1 = CQ full (retry later),
-// 2 = publish wait timed out.
-__device__ int produce_cqe(DevCq *cq, const queue::Cqe &e, uint64_t max_ns) {
-    const uint32_t cap = ld_vol32(&cq->cfg.capacity);
-    queue::RingHeader *ring = reinterpret_cast<queue::RingHeader *>(ld_vol(&cq->cfg.ring));
-    uint8_t *slots = reinterpret_cast<uint8_t *>(ld_vol(&cq->cfg.slots));
-    const uint32_t stride = ld_vol32(&cq->cfg.stride);
-    uint64_t r;
-    for (int attempt = 0;; ++attempt) {
-        r = ld_acq_sys(&cq->st.reserve);
-        uint64_t head = ld_acq_sys(&cq->st.head_seen);
-        if (r - head >= cap) {
-            head = ld_acq_sys(&ring->head.value);
-            atomicMax_system(&cq->st.head_seen, head);
-            if (r - head >= cap) return 1;
-        }
-        if (atomicCAS_system(&cq->st.reserve, r, r + 1) == r) break;
-        if (attempt > 1000) return 1;
+// Reserve up to `want` consecutive slots of a multi-producer CQ (lane 0).  Returns how many were
+// granted (0 when the CQ is full); *first receives the first slot's cursor.  The warp caches the
+// CQ's configuration and its last view of the cursors, so an uncontended reservation is one CAS.
+__device__ uint32_t reserve_cq(Warp &w, DevCq *cq, uint32_t want, uint64_t *first) {
+    CqCache &c = w.cq;
+    if (c.cq != cq) {
+        c.cq = cq;
+        c.cap = ld_vol32(&cq->cfg.capacity);
+        c.stride = ld_vol32(&cq->cfg.stride);
+        c.ring = reinterpret_cast<queue::RingHeader *>(ld_vol(&cq->cfg.ring));
+        c.slots = reinterpret_cast<uint8_t *>(ld_vol(&cq->cfg.slots));
+        c.reserve = ld_vol(&cq->st.reserve);
+        c.head = ld_vol(&cq->st.head_seen);
+        c.published = ~0ull;
     }
-    uint8_t *slot = slots + (r % cap) * stride;
-    const uint4 *src = reinterpret_cast<const uint4 *>(&e);
-    st_vol128(slot, src[0]);
-    st_vol128(slot + 16, src[1]);
-    if (!wait_eq_sys(&cq->st.published, r, max_ns)) return 2;
-    __threadfence_system();
-    st_rel_sys(&ring->tail.value, r + 1);
-    st_rel_sys(&cq->st.published, r + 1);
+    for (int attempt = 0; attempt < 256; ++attempt) {
+        const uint64_t r = c.reserve;
+        if (r - c.head + want > c.cap) {
+            const uint64_t head = ld_acq_sys(&c.ring->head.value);  // the consumer moved on
+            if (head > c.head) c.head = head;
+            atomicMax_system(&cq->st.head_seen, c.head);
+        }
+        const uint64_t used = r - c.head;
+        if (used >= c.cap) {
+            c.cq = nullptr;  // re-read everything next time
+            return 0;
+        }
+        const uint32_t k = uint32_t(want < c.cap - used ? want : c.cap - used);
+        const uint64_t old = atomicCAS_system(&cq->st.reserve, r, r + k);
+        if (old == r) {
+            c.reserve = r + k;
+            *first = r;
+            return k;
+        }
+        c.reserve = old;  // another producer got there first: retry from its cursor
+    }
+    c.cq = nullptr;
     return 0;
+}
+
+// Write k CQEs into reserved slots [first, first + k) and publish them in cursor order (lane 0).
+// Returns false when the in-order publish wait ran out.
+__device__ bool publish_cq(Warp &w, DevCq *cq, uint64_t first, const queue::Cqe *e, uint32_t k, uint64_t max_ns) {
+    CqCache &c = w.cq;
+    for (uint32_t i = 0; i < k; ++i) {
+        uint8_t *slot = c.slots + ((first + i) % c.cap) * c.stride;
+        const uint4 *src = reinterpret_cast<const uint4 *>(&e[i]);
+        st_vol128(slot, src[0]);
+        st_vol128(slot + 16, src[1]);
+    }
+    // The ring's tail is the in-order publish cursor: a producer publishes only after it has seen
+    // the tail reach its first slot, so the tail never moves backwards and the producer's fence is
+    // cumulative over every earlier producer's slots.  A warp that published the slots just below
+    // `first` itself (the common single-producer case) need not look.
+    if (c.published != first && !wait_eq_sys(reinterpret_cast<const unsigned long long *>(&c.ring->tail.value), first, max_ns)) return false;
+    // One system fence orders the WR payload stores and the CQE slots before the tail.
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    st_vol64(&c.ring->tail.value, first + k);
+    c.published = first + k;
+    return true;
+}
+
+// One CQE, reserved and published (lane 0): 0 published, 1 CQ full, 2 publish wait ran out.
+__device__ int produce_cqe(Warp &w, DevCq *cq, const queue::Cqe &e, uint64_t max_ns) {
+    uint64_t r = 0;
+    if (reserve_cq(w, cq, 1, &r) == 0) return 1;
+    return publish_cq(w, cq, r, &e, 1, max_ns) ? 0 : 2;
 }
 
 // Claim the next RQ WR of `qp` (lane 0).  Returns false when the RQ is empty.
 __device__ bool claim_rq(DevQp *qp, uint64_t *claim, uint64_t *wr_id) {
     queue::RingHeader *rq = reinterpret_cast<queue::RingHeader *>(ld_vol(&qp->cfg.rq));
     for (int attempt = 0; attempt < 64; ++attempt) {
-        const uint64_t c = ld_acq_sys(&qp->st.rq_claim);
+        const uint64_t c = ld_vol(&qp->st.rq_claim);
         const uint64_t tail = ld_acq_sys(&rq->tail.value);
         if (c >= tail) return false;
         if (atomicCAS_system(&qp->st.rq_claim, c, c + 1) == c) {
@@ -417,53 +495,64 @@ __device__ void flush_counters(Warp &w) {
         if (w.n_miss) atomicAdd(&w.p->stats->claim_misses, (unsigned long long)w.n_miss);
         if (w.bytes) atomicAdd(&w.p->stats->bytes_moved, (unsigned long long)w.bytes);
         if (w.busy) atomicAdd(&w.p->stats->busy_ns, (unsigned long long)w.busy);
+        if (w.n_inline) atomicAdd(&w.p->stats->inline_runs, (unsigned long long)w.n_inline);
     }
-    w.n_chunks = w.n_miss = w.bytes = w.busy = 0;
+    w.n_chunks = w.n_miss = w.bytes = w.busy = w.n_inline = 0;
 }
 
 // ---- per-QP service ----------------------------------------------------------------------------
 
-struct WqeView {
-    queue::SendWqe h;
-    uint64_t compare_add;
-};
+__device__ __forceinline__ uint4 ld_mr_part(const DevMr *m, int part) {
+    return ld_vol128(reinterpret_cast<const uint8_t *>(m) + 16 * part);
+}
 
-// Validate and stage one WQE (already in shared memory `wqe`) into `rec`.  Warp-wide.
-__device__ void stage_wr(Warp &w, DevQp *qp, const uint8_t *wqe, WrRec *rec, uint32_t *status_out,
+// Validate and stage one WQE (in shared memory) into `rec`.  Warp-wide.  Every global load the
+// checks need (local MRs by lane, the remote MR, the responder's configuration) is issued before
+// any of them is used, so the whole validation costs one memory round trip.
+__device__ void stage_wr(Warp &w, const QpView &v, const uint8_t *wqe, WrRec *rec, uint32_t *status_out,
                          uint64_t *total_out, uint64_t *remote_out) {
     const queue::SendWqe *h = reinterpret_cast<const queue::SendWqe *>(wqe);
     const uint32_t op = h->opcode;
     const uint32_t nsge = h->sge_count;
-    const uint32_t max_sge = ld_vol32(&qp->cfg.max_send_sge);
-    const uint32_t pd = ld_vol32(&qp->cfg.pd_num);
     uint32_t status = UGDR_WC_SUCCESS;
     const bool op_ok = op == UGDR_WR_RDMA_WRITE || op == UGDR_WR_RDMA_WRITE_WITH_IMM ||
                        op == UGDR_WR_RDMA_READ || is_atomic(op);
-    if (!op_ok || nsge > max_sge || nsge > kMaxSge || (is_atomic(op) && nsge != 1))
+    if (!op_ok || nsge > v.max_sge || nsge > kMaxSge || (is_atomic(op) && nsge != 1))
         status = UGDR_WC_LOC_QP_OP_ERR;
-    // Lane i resolves SGE i.
-    uint64_t len = 0, local = 0;
+    const bool mine = status == UGDR_WC_SUCCESS && uint32_t(w.lane) < nsge;
+    const queue::Sge *sg = reinterpret_cast<const queue::Sge *>(wqe + queue::kSendSgeOffset) + (mine ? w.lane : 0);
+    const uint64_t len = mine ? sg->length : 0;
+    // --- issue every load ---
+    uint4 l0{}, l1{}, l2{};
+    if (mine && len != 0) {
+        const DevMr *m = &w.p->mrs[(sg->lkey >> 1) & (kMaxMrs - 1)];
+        l0 = ld_mr_part(m, 0);  // base, client_base
+        l1 = ld_mr_part(m, 1);  // length, access, pd_num
+        l2 = ld_mr_part(m, 2);  // lkey, rkey, valid, pad
+    }
+    const DevMr *rm = &w.p->mrs[(h->rkey >> 1) & (kMaxMrs - 1)];
+    const uint4 r0 = ld_mr_part(rm, 0), r1 = ld_mr_part(rm, 1), r2 = ld_mr_part(rm, 2);
+    uint32_t pstate = 0, perr = 0, pactive = 0, pacc = 0, ppd = 0;
+    if (v.peer != nullptr) {
+        pstate = ld_vol32(&v.peer->cfg.state);
+        perr = ld_vol32(&v.peer->st.err);
+        pactive = ld_vol32(&v.peer->cfg.active);
+        pacc = ld_vol32(&v.peer->cfg.access);
+        ppd = ld_vol32(&v.peer->cfg.pd_num);
+    }
+    // --- then check ---
+    uint64_t local = 0;
     bool bad = false;
-    if (status == UGDR_WC_SUCCESS && uint32_t(w.lane) < nsge) {
-        const queue::Sge *sg =
-            reinterpret_cast<const queue::Sge *>(wqe + queue::kSendSgeOffset) + w.lane;
-        len = sg->length;
-        if (len != 0) {
-            const DevMr *m = &w.p->mrs[(sg->lkey >> 1) & (kMaxMrs - 1)];
-            const uint32_t valid = ld_vol32(&m->valid);
-            const uint32_t lkey = ld_vol32(&m->lkey);
-            const uint64_t cb = ld_vol(&m->client_base), ml = ld_vol(&m->length);
-            const uint64_t base = ld_vol(&m->base);
-            const uint32_t acc = ld_vol32(&m->access), mpd = ld_vol32(&m->pd_num);
-            const bool need_write = op == UGDR_WR_RDMA_READ || is_atomic(op);
-            if (!valid || lkey != sg->lkey || mpd != pd || base == 0 || sg->address < cb ||
-                len > ml || sg->address - cb > ml - len ||
-                (need_write && (acc & UGDR_ACCESS_LOCAL_WRITE) == 0)) {
-                bad = true;
-            } else {
-                local = base + (sg->address - cb);
-            }
-        }
+    if (mine && len != 0) {
+        const uint64_t base = (uint64_t(l0.y) << 32) | l0.x, cb = (uint64_t(l0.w) << 32) | l0.z;
+        const uint64_t ml = (uint64_t(l1.y) << 32) | l1.x;
+        const uint32_t acc = l1.z, mpd = l1.w, lkey = l2.x, valid = l2.z;
+        const bool need_write = op == UGDR_WR_RDMA_READ || is_atomic(op);
+        if (!valid || lkey != sg->lkey || mpd != v.pd || base == 0 || sg->address < cb || len > ml ||
+            sg->address - cb > ml - len || (need_write && (acc & UGDR_ACCESS_LOCAL_WRITE) == 0))
+            bad = true;
+        else
+            local = base + (sg->address - cb);
     }
     const bool any_bad = __any_sync(0xffffffffu, bad);
     uint64_t total = len;
@@ -473,7 +562,7 @@ __device__ void stage_wr(Warp &w, DevQp *qp, const uint8_t *wqe, WrRec *rec, uin
     if (status == UGDR_WC_SUCCESS && is_atomic(op) && total != 8) status = UGDR_WC_LOC_LEN_ERR;
 
     // Compact the non-empty segments: lane i keeps slot = prefix count of non-empty lanes.
-    const bool keep = uint32_t(w.lane) < nsge && len != 0;
+    const bool keep = mine && len != 0;
     const uint32_t keep_mask = __ballot_sync(0xffffffffu, keep);
     if (keep && status == UGDR_WC_SUCCESS) {
         const uint32_t idx = __popc(keep_mask & ((1u << w.lane) - 1));
@@ -481,36 +570,24 @@ __device__ void stage_wr(Warp &w, DevQp *qp, const uint8_t *wqe, WrRec *rec, uin
         rec->seg[idx].length = len;
     }
 
-    // Remote side (uniform).
     uint64_t remote = 0;
     if (status == UGDR_WC_SUCCESS) {
-        DevQp *peer = reinterpret_cast<DevQp *>(ld_vol(&qp->cfg.peer));
-        const uint32_t lost = ld_vol32(&qp->cfg.peer_lost);
-        uint32_t pstate = 0, perr = 0;
-        if (peer != nullptr) {
-            pstate = ld_acq_sys32(&peer->cfg.state);
-            perr = ld_acq_sys32(&peer->st.err);
-        }
-        if (peer == nullptr || lost || pstate == UGDR_QPS_RESET || !ld_acq_sys32(&peer->cfg.active)) {
+        if (v.peer == nullptr || v.lost || pstate == UGDR_QPS_RESET || !pactive) {
             status = UGDR_WC_RETRY_EXC_ERR;
         } else if (pstate == UGDR_QPS_ERR || perr) {
             status = UGDR_WC_REM_OP_ERR;
         } else {
             const uint32_t need = remote_need(op);
-            const uint32_t pacc = ld_acq_sys32(&peer->cfg.access);
-            const uint32_t ppd = ld_acq_sys32(&peer->cfg.pd_num);
             const uint64_t rlen = is_atomic(op) ? 8 : total;
             if ((pacc & need) == 0) {
                 status = UGDR_WC_REM_ACCESS_ERR;
             } else if (rlen != 0) {
-                const DevMr *m = &w.p->mrs[(h->rkey >> 1) & (kMaxMrs - 1)];
-                const uint32_t valid = ld_vol32(&m->valid), rkey = ld_vol32(&m->rkey);
-                const uint64_t cb = ld_vol(&m->client_base), ml = ld_vol(&m->length);
-                const uint64_t base = ld_vol(&m->base);
-                const uint32_t acc = ld_vol32(&m->access), mpd = ld_vol32(&m->pd_num);
+                const uint64_t base = (uint64_t(r0.y) << 32) | r0.x, cb = (uint64_t(r0.w) << 32) | r0.z;
+                const uint64_t ml = (uint64_t(r1.y) << 32) | r1.x;
+                const uint32_t acc = r1.z, mpd = r1.w, rkey = r2.y, valid = r2.z;
                 const uint64_t ra = h->remote_address;
-                if (!valid || rkey != h->rkey || mpd != ppd || base == 0 || (acc & need) == 0 ||
-                    ra < cb || rlen > ml || ra - cb > ml - rlen)
+                if (!valid || rkey != h->rkey || mpd != ppd || base == 0 || (acc & need) == 0 || ra < cb ||
+                    rlen > ml || ra - cb > ml - rlen)
                     status = UGDR_WC_REM_ACCESS_ERR;
                 else
                     remote = base + (ra - cb);
@@ -537,10 +614,10 @@ __device__ void stage_wr(Warp &w, DevQp *qp, const uint8_t *wqe, WrRec *rec, uin
     *remote_out = remote;
 }
 
-// Execute an inline WR (small payload or atomic) with the owner warp.
+// Execute an inline WR (small payload or atomic) with the owner warp.  No fence here: the issue
+// pass fences once for all the inline WRs it ran before any of them can retire.
 __device__ void run_inline(Warp &w, WrRec *rec, const uint8_t *wqe, uint32_t op, uint64_t total,
                            uint64_t remote) {
-    const uint32_t nseg = ld_vol32(&rec->nseg);
     if (is_atomic(op)) {
         if (w.lane == 0) {
             const queue::SendWqe *h = reinterpret_cast<const queue::SendWqe *>(wqe);
@@ -555,108 +632,362 @@ __device__ void run_inline(Warp &w, WrRec *rec, const uint8_t *wqe, uint32_t op,
                 old = atomicCAS_system(t, (unsigned long long)cmp, (unsigned long long)swap);
             uint8_t *dst = reinterpret_cast<uint8_t *>(rec->seg[0].local);
             memcpy(dst, &old, 8);
-            __threadfence_system();
-            atomicAdd(&w.p->stats->bytes_moved, 8ull);
         }
         __syncwarp();
+        w.bytes += 8;
         return;
     }
-    copy_stream(rec, nseg, remote, op != UGDR_WR_RDMA_READ, 0, total, w.lane);
-    __syncwarp();
-    if (w.lane == 0) {
-        __threadfence_system();
-        atomicAdd(&w.p->stats->bytes_moved, (unsigned long long)total);
+    const uint32_t nseg = rec->nseg;
+    if (nseg == 1 && total <= 16 && op != UGDR_WR_RDMA_READ) {
+        // Tiny payload: one lane per byte, no vector setup.
+        const uint8_t *src = reinterpret_cast<const uint8_t *>(rec->seg[0].local);
+        if (uint64_t(w.lane) < total) reinterpret_cast<uint8_t *>(remote)[w.lane] = src[w.lane];
+    } else {
+        copy_stream(rec, nseg, remote, op != UGDR_WR_RDMA_READ, 0, total, w.lane);
     }
+    __syncwarp();
+    w.bytes += total;
 }
 
-// Service one QP: retire finished WRs, then issue new ones.  Warp-wide; returns work done.
-__device__ uint32_t service_qp(Warp &w, DevQp *qp, uint8_t *wqe_smem, JobRing *jr, uint32_t *bitmap,
-                               uint32_t nwarps) {
-    if (!ld_vol32(&qp->cfg.active)) return 0;
+// Retire finished WRs in order.  Lane i inspects WR head + i, so the ready prefix, the CQE list
+// and its slot indices come out of one round of parallel loads and ballots; lane 0 then reserves
+// and publishes every send CQE at once.  Returns WRs retired, or -1 / -2 on a wait that ran out.
+// Commit the retirement of WRs [head, head + p): lane i (< p) holds WR head + i's completion
+// fields.  Send CQEs go out with one reservation and one publish; the head then moves past every
+// WR whose CQE found a slot.  Returns WRs retired (>= 0) or -1 when the publish wait ran out.
+__device__ int retire_commit(Warp &w, DevQp *qp, const QpView &v, queue::Cqe *cqe_buf, uint64_t head, uint32_t p,
+                             uint32_t err_mask, uint64_t wr_id, uint32_t status, uint32_t op, uint32_t signaled,
+                             uint64_t total) {
     const uint64_t max_ns = w.p->max_wait_ns;
-    queue::RingHeader *sq = reinterpret_cast<queue::RingHeader *>(ld_vol(&qp->cfg.sq));
-    const uint8_t *sq_slots = reinterpret_cast<const uint8_t *>(ld_vol(&qp->cfg.sq_slots));
-    const uint32_t sq_cap = ld_vol32(&qp->cfg.sq_cap), sq_stride = ld_vol32(&qp->cfg.sq_stride);
-    const uint32_t qpn = ld_vol32(&qp->cfg.qpn);
-    uint32_t work = 0;
+    int verdict = 0;
+    const bool need = uint32_t(w.lane) < p && (signaled || status != UGDR_WC_SUCCESS);
+    const uint32_t need_mask = __ballot_sync(0xffffffffu, need);
+    if (need) {
+        const uint32_t idx = __popc(need_mask & ((1u << w.lane) - 1));
+        cqe_buf[idx] = queue::Cqe{wr_id, status, wc_op(op), status == UGDR_WC_SUCCESS ? uint32_t(total) : 0u, 0u,
+                                  v.qpn, 0u};
+    }
+    __syncwarp();
+    const uint32_t ncqe = __popc(need_mask);
+    uint32_t retire_n = p;
+    if (w.lane == 0) {
+        uint32_t granted = 0;
+        uint64_t first = 0;
+        if (ncqe > 0) granted = reserve_cq(w, v.send_cq, ncqe, &first);
+        w.t_reserved = gtime();
+        if (granted < ncqe) {
+            // Retire only the WRs before the first CQE that found no slot.
+            uint32_t seen = 0;
+            retire_n = 0;
+            for (uint32_t i = 0; i < p; ++i) {
+                const bool needs = (need_mask >> i) & 1u;
+                if (needs && seen == granted) break;
+                seen += needs ? 1u : 0u;
+                ++retire_n;
+            }
+        }
+        if (granted > 0 && !publish_cq(w, v.send_cq, first, cqe_buf, granted, max_ns)) {
+            verdict = -1;
+        } else if (retire_n > 0) {
+            qp->st.sq_head = head + retire_n;
+            st_vol64(&v.sq->head.value, head + retire_n);  // slots may be reused by the client
+            atomicAdd(&w.p->stats->wrs_completed, (unsigned long long)retire_n);
+            atomicAdd(&w.p->stats->retired, (unsigned long long)retire_n);
+            atomicMax(&w.p->stats->last_end_ns, (unsigned long long)gtime());
+            if (err_mask && retire_n == p) {
+                atomicAdd(&w.p->stats->error_completions, 1ull);
+                qp->st.err = 1;
+                st_rel_sys(&v.sq->meta.reserved[queue::kQpErrorWordIndex], UGDR_QPS_ERR);
+            }
+            verdict = int(retire_n);
+        }
+    }
+    return bcast(verdict);
+}
 
-    // Retire in order.
-    for (;;) {
-        int verdict = 0;  // 0 stop, 1 retired one
+__device__ int retire(Warp &w, DevQp *qp, const QpView &v, queue::Cqe *cqe_buf) {
+    const uint64_t max_ns = w.p->max_wait_ns;
+    const uint64_t head = ld_vol(&qp->st.sq_head), issue = ld_vol(&qp->st.sq_issue);
+    const uint32_t m = uint32_t(issue - head);  // <= kWindow <= 32
+    if (m == 0) return 0;
+    const bool mine = uint32_t(w.lane) < m;
+    WrRec *rec = &qp->st.win[(head + (mine ? w.lane : 0)) % kWindow];
+    uint32_t n = 0, done = 0, status = 0, op = 0, signaled = 0, recv_done = 0;
+    unsigned long long wr_id = 0, total = 0;
+    if (mine) {
+        n = ld_vol32(&rec->nchunks);
+        done = ld_vol32(&rec->chunks_done);
+        status = ld_vol32(&rec->status);
+        op = ld_vol32(&rec->opcode);
+        signaled = ld_vol32(&rec->signaled);
+        recv_done = ld_vol32(&rec->recv_cqe_done);
+        wr_id = ld_vol(&rec->wr_id);
+        total = ld_vol(&rec->total);
+    }
+    const uint32_t ready_mask = __ballot_sync(0xffffffffu, mine && (n == 0 || done >= n));
+    uint32_t p = __ffs(~ready_mask) - 1;  // ready prefix length
+    if (p == 0) return 0;
+    const uint32_t err_mask = __ballot_sync(0xffffffffu, uint32_t(w.lane) < p && status != UGDR_WC_SUCCESS);
+    if (err_mask) p = __ffs(err_mask);  // retire up to and including the first error
+    __threadfence();  // chunk workers' payload stores happen-before what follows
+    // WRITE_WITH_IMM: responder completions first, in order, by lane 0.
+    const uint32_t imm_mask = __ballot_sync(0xffffffffu, uint32_t(w.lane) < p && status == UGDR_WC_SUCCESS &&
+                                                             op == UGDR_WR_RDMA_WRITE_WITH_IMM && !recv_done);
+    int verdict = 0;
+    if (imm_mask) {
+        uint32_t stop = p;
         if (w.lane == 0) {
-            const uint64_t head = qp->st.sq_head, issue = qp->st.sq_issue;
-            if (head < issue) {
-                WrRec *rec = &qp->st.win[head % kWindow];
-                const uint32_t n = ld_vol32(&rec->nchunks);
-                const uint32_t done = atomicAdd(&rec->chunks_done, 0u);
-                if (done >= n) {
-                    __threadfence();
-                    verdict = 1;
-                    const uint32_t op = rec->opcode, status = rec->status;
-                    if (status == UGDR_WC_SUCCESS && op == UGDR_WR_RDMA_WRITE_WITH_IMM &&
-                        !rec->recv_cqe_done) {
-                        DevQp *peer = reinterpret_cast<DevQp *>(ld_vol(&qp->cfg.peer));
-                        queue::Cqe rc{rec->recv_wr_id, UGDR_WC_SUCCESS, UGDR_WC_RECV_RDMA_WITH_IMM,
-                                      uint32_t(rec->total), rec->imm,
-                                      peer ? ld_acq_sys32(&peer->cfg.qpn) : 0u, UGDR_WC_WITH_IMM};
-                        DevCq *rcq = peer ? reinterpret_cast<DevCq *>(ld_vol(&peer->cfg.recv_cq)) : nullptr;
-                        const int prc = rcq ? produce_cqe(rcq, rc, max_ns) : 0;
-                        if (prc == 1) {
-                            verdict = 0;
-                        } else if (prc == 2) {
-                            verdict = -1;
-                        } else {
-                            if (peer && !release_rq(peer, rec->recv_claim, max_ns)) verdict = -2;
-                            rec->recv_cqe_done = 1;
-                        }
+            for (uint32_t i = 0; i < p; ++i) {
+                if (!(imm_mask & (1u << i))) continue;
+                WrRec *r = &qp->st.win[(head + i) % kWindow];
+                DevQp *peer = v.peer;
+                if (peer != nullptr) {
+                    DevCq *rcq = reinterpret_cast<DevCq *>(ld_vol(&peer->cfg.recv_cq));
+                    const queue::Cqe rc{r->recv_wr_id, UGDR_WC_SUCCESS, UGDR_WC_RECV_RDMA_WITH_IMM,
+                                        uint32_t(r->total), r->imm, ld_vol32(&peer->cfg.qpn), UGDR_WC_WITH_IMM};
+                    const int prc = produce_cqe(w, rcq, rc, max_ns);
+                    if (prc == 1) {  // responder CQ full: retry on a later pass
+                        stop = i;
+                        break;
                     }
-                    if (verdict == 1 && (rec->signaled || status != UGDR_WC_SUCCESS)) {
-                        queue::Cqe c{rec->wr_id, status, wc_op(op),
-                                     status == UGDR_WC_SUCCESS ? uint32_t(rec->total) : 0u, 0u, qpn, 0u};
-                        DevCq *scq = reinterpret_cast<DevCq *>(ld_vol(&qp->cfg.send_cq));
-                        const int prc = produce_cqe(scq, c, max_ns);
-                        if (prc == 1) verdict = 0;
-                        if (prc == 2) verdict = -1;
-                    }
-                    if (verdict == 1) {
-                        qp->st.sq_head = head + 1;
-                        st_rel_sys(&sq->head.value, head + 1);
-                        atomicAdd(&w.p->stats->wrs_completed, 1ull);
-                        atomicAdd(&w.p->stats->retired, 1ull);
-                        atomicMax(&w.p->stats->last_end_ns, (unsigned long long)gtime());
-                        if (status != UGDR_WC_SUCCESS) {
-                            atomicAdd(&w.p->stats->error_completions, 1ull);
-                            qp->st.err = 1;
-                            st_rel_sys(&sq->meta.reserved[queue::kQpErrorWordIndex], UGDR_QPS_ERR);
-                        }
+                    if (prc == 2 || !release_rq(peer, r->recv_claim, max_ns)) {
+                        verdict = prc == 2 ? -1 : -2;
+                        stop = i;
+                        break;
                     }
                 }
+                r->recv_cqe_done = 1;
             }
         }
         verdict = bcast(verdict);
-        if (verdict < 0) {
-            record_error(w, verdict == -1 ? kErrCqPublishTimeout : kErrRqReleaseTimeout);
+        if (verdict < 0) return verdict;
+        p = bcast(stop);
+        if (p == 0) return 0;
+    }
+    return retire_commit(w, qp, v, cqe_buf, head, p, err_mask, wr_id, status, op, signaled, total);
+}
+
+// Small-WR fast path: lane j validates and executes WQE j of the staged batch (single-SGE
+// WRITE / READ of at most kLaneBytes), so a batch of tiny WRs costs one round of parallel loads
+// and one of copies instead of one round trip per WR.  Processes the longest prefix of such WQEs
+// and returns its length (an erroring WQE ends the prefix and is included; nothing after it runs).
+constexpr uint32_t kLaneBytes = 64;
+
+struct LaneWr {
+    uint64_t wr_id, total;
+    uint32_t status, op, signaled;
+};
+
+__device__ uint32_t issue_fast(Warp &w, DevQp *qp, const QpView &v, const uint8_t *wqe_smem, uint64_t issue0,
+                               uint32_t avail, LaneWr *out) {
+    const uint32_t j = uint32_t(w.lane);
+    const bool in = j < avail;
+    const queue::SendWqe *h = reinterpret_cast<const queue::SendWqe *>(wqe_smem + (in ? j : 0) * v.sq_stride);
+    const queue::Sge *sg = reinterpret_cast<const queue::Sge *>(wqe_smem + (in ? j : 0) * v.sq_stride +
+                                                                queue::kSendSgeOffset);
+    const uint32_t op = h->opcode;
+    const bool fast = in && (op == UGDR_WR_RDMA_WRITE || op == UGDR_WR_RDMA_READ) && h->sge_count == 1 &&
+                      sg->length <= kLaneBytes && v.max_sge >= 1;
+    const uint32_t fast_mask = __ballot_sync(0xffffffffu, fast);
+    const uint32_t p = __ffs(~fast_mask) - 1;
+    if (p == 0) return 0;
+    const bool act = j < p;
+    const uint64_t len = act ? sg->length : 0;
+    // --- MR entries (warp cache, else one parallel round of loads); responder config from the
+    // QP view ---
+    uint4 l0{}, l1{}, l2{}, r0{}, r1{}, r2{};
+    const MrCacheEntry *lc = &w.mrc[0], *rc = &w.mrc[1];
+    const bool lhit = act && lc->key == sg->lkey && sg->lkey != 0;
+    const bool rhit = act && rc->key == h->rkey && h->rkey != 0;
+    if (act) {
+        if (lhit) {
+            l0 = lc->part[0];
+            l1 = lc->part[1];
+            l2 = lc->part[2];
+        } else {
+            const DevMr *lm = &w.p->mrs[(sg->lkey >> 1) & (kMaxMrs - 1)];
+            l0 = ld_mr_part(lm, 0);
+            l1 = ld_mr_part(lm, 1);
+            l2 = ld_mr_part(lm, 2);
+        }
+        if (rhit) {
+            r0 = rc->part[0];
+            r1 = rc->part[1];
+            r2 = rc->part[2];
+        } else {
+            const DevMr *rm = &w.p->mrs[(h->rkey >> 1) & (kMaxMrs - 1)];
+            r0 = ld_mr_part(rm, 0);
+            r1 = ld_mr_part(rm, 1);
+            r2 = ld_mr_part(rm, 2);
+        }
+    }
+    __syncwarp();
+    if (j == 0 && act) {  // remember lane 0's entries (only valid ones)
+        if (!lhit && l2.z && l2.x == sg->lkey) {
+            w.mrc[0].key = sg->lkey;
+            w.mrc[0].part[0] = l0;
+            w.mrc[0].part[1] = l1;
+            w.mrc[0].part[2] = l2;
+        }
+        if (!rhit && r2.z && r2.y == h->rkey) {
+            w.mrc[1].key = h->rkey;
+            w.mrc[1].part[0] = r0;
+            w.mrc[1].part[1] = r1;
+            w.mrc[1].part[2] = r2;
+        }
+    }
+    __syncwarp();
+    const uint32_t pstate = v.pstate, perr = v.perr, pactive = v.pactive, pacc = v.pacc, ppd = v.ppd;
+    // --- check ---
+    uint32_t status = UGDR_WC_SUCCESS;
+    uint64_t local = 0, remote = 0;
+    if (act && len != 0) {
+        const uint64_t base = (uint64_t(l0.y) << 32) | l0.x, cb = (uint64_t(l0.w) << 32) | l0.z;
+        const uint64_t ml = (uint64_t(l1.y) << 32) | l1.x;
+        const bool need_write = op == UGDR_WR_RDMA_READ;
+        if (!l2.z || l2.x != sg->lkey || l1.w != v.pd || base == 0 || sg->address < cb || len > ml ||
+            sg->address - cb > ml - len || (need_write && (l1.z & UGDR_ACCESS_LOCAL_WRITE) == 0))
+            status = UGDR_WC_LOC_PROT_ERR;
+        else
+            local = base + (sg->address - cb);
+    }
+    if (act && status == UGDR_WC_SUCCESS) {
+        if (v.peer == nullptr || v.lost || pstate == UGDR_QPS_RESET || !pactive) {
+            status = UGDR_WC_RETRY_EXC_ERR;
+        } else if (pstate == UGDR_QPS_ERR || perr) {
+            status = UGDR_WC_REM_OP_ERR;
+        } else {
+            const uint32_t need = remote_need(op);
+            if ((pacc & need) == 0) {
+                status = UGDR_WC_REM_ACCESS_ERR;
+            } else if (len != 0) {
+                const uint64_t base = (uint64_t(r0.y) << 32) | r0.x, cb = (uint64_t(r0.w) << 32) | r0.z;
+                const uint64_t ml = (uint64_t(r1.y) << 32) | r1.x;
+                const uint64_t ra = h->remote_address;
+                if (!r2.z || r2.y != h->rkey || r1.w != ppd || base == 0 || (r1.z & need) == 0 || ra < cb ||
+                    len > ml || ra - cb > ml - len)
+                    status = UGDR_WC_REM_ACCESS_ERR;
+                else
+                    remote = base + (ra - cb);
+            }
+        }
+    }
+    const uint32_t err_mask = __ballot_sync(0xffffffffu, act && status != UGDR_WC_SUCCESS);
+    const uint32_t count = err_mask ? __ffs(err_mask) : p;  // through the first error, inclusive
+    // --- execute (lanes before the first error only) ---
+    if (j < count && status == UGDR_WC_SUCCESS && len != 0) {
+        uint8_t *dst = reinterpret_cast<uint8_t *>(op == UGDR_WR_RDMA_READ ? local : remote);
+        const uint8_t *src = reinterpret_cast<const uint8_t *>(op == UGDR_WR_RDMA_READ ? remote : local);
+        if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src) | len) & 7) == 0) {
+            for (uint64_t o = 0; o < len; o += 8)
+                *reinterpret_cast<uint64_t *>(dst + o) = *reinterpret_cast<const uint64_t *>(src + o);
+        } else {
+            for (uint64_t o = 0; o < len; ++o) dst[o] = src[o];
+        }
+    }
+    if (j < count) {
+        WrRec *rec = &qp->st.win[(issue0 + j) % kWindow];
+        rec->wr_id = h->wr_id;
+        rec->opcode = op;
+        rec->total = len;
+        rec->remote = remote;
+        rec->status = status;
+        rec->imm = 0;
+        rec->nseg = len != 0 ? 1 : 0;
+        rec->seg[0].local = local;
+        rec->seg[0].length = len;
+        rec->recv_cqe_done = 0;
+        rec->chunks_done = 0;
+        rec->nchunks = 0;
+        rec->signaled = (v.sig_all || (h->send_flags & UGDR_SEND_SIGNALED) != 0) ? 1u : 0u;
+        w.bytes += len;
+        *out = LaneWr{h->wr_id, len, status, op, rec->signaled};
+    }
+    __syncwarp();
+    return count;
+}
+
+__device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_smem, queue::Cqe *cqe_smem,
+                                   JobRing *jr, uint32_t *bitmap, uint32_t nwarps);
+
+// Service one QP: retire, flush when in ERR, else issue a batch of WQEs and retire again.
+// Warp-wide; returns the work done.
+__device__ uint32_t service_qp(Warp &w, DevQp *qp, uint8_t *wqe_smem, queue::Cqe *cqe_smem, JobRing *jr,
+                               uint32_t *bitmap, uint32_t nwarps) {
+    const uint64_t max_ns = w.p->max_wait_ns;
+    // The configuration this pass needs: cached per warp for the QP it serviced last and re-read
+    // at least every 20 us (a host state change is seen within that; slots are only reused after
+    // the kernel was stopped, so a cache never outlives its QP).  The owner warp is the only
+    // writer of the QP's cursors, so the cached head / issue are authoritative.
+    const uint64_t now0 = gtime();
+    if (w.vq == qp && now0 - w.vt < 20000) {
+        return service_cached(w, qp, w.vv, wqe_smem, cqe_smem, jr, bitmap, nwarps);
+    }
+    if (!ld_vol32(&qp->cfg.active)) {
+        w.vq = nullptr;
+        return 0;
+    }
+    QpView v;
+    v.sq = reinterpret_cast<queue::RingHeader *>(ld_vol(&qp->cfg.sq));
+    v.sq_slots = reinterpret_cast<const uint8_t *>(ld_vol(&qp->cfg.sq_slots));
+    v.peer = reinterpret_cast<DevQp *>(ld_vol(&qp->cfg.peer));
+    v.send_cq = reinterpret_cast<DevCq *>(ld_vol(&qp->cfg.send_cq));
+    v.sq_cap = ld_vol32(&qp->cfg.sq_cap);
+    v.sq_stride = ld_vol32(&qp->cfg.sq_stride);
+    v.qpn = ld_vol32(&qp->cfg.qpn);
+    v.state = ld_vol32(&qp->cfg.state);
+    v.pd = ld_vol32(&qp->cfg.pd_num);
+    v.max_sge = ld_vol32(&qp->cfg.max_send_sge);
+    v.sig_all = ld_vol32(&qp->cfg.sq_sig_all);
+    v.lost = ld_vol32(&qp->cfg.peer_lost);
+    v.err = ld_vol32(&qp->st.err);
+    v.retry_word = ld_vol32(&qp->cfg.timeout);  // timeout, retry_cnt, rnr_retry, min_rnr_timer
+    v.pstate = v.perr = v.pactive = v.pacc = v.ppd = 0;
+    if (v.peer != nullptr) {
+        v.pstate = ld_vol32(&v.peer->cfg.state);
+        v.perr = ld_vol32(&v.peer->st.err);
+        v.pactive = ld_vol32(&v.peer->cfg.active);
+        v.pacc = ld_vol32(&v.peer->cfg.access);
+        v.ppd = ld_vol32(&v.peer->cfg.pd_num);
+    }
+    w.vhead = ld_vol(&qp->st.sq_head);
+    w.vissue = ld_vol(&qp->st.sq_issue);
+    w.vq = qp;
+    w.vv = v;
+    w.vt = now0;
+    return service_cached(w, qp, w.vv, wqe_smem, cqe_smem, jr, bitmap, nwarps);
+}
+
+__device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_smem, queue::Cqe *cqe_smem,
+                                   JobRing *jr, uint32_t *bitmap, uint32_t nwarps) {
+    const uint64_t max_ns = w.p->max_wait_ns;
+    uint32_t work = 0;
+
+    int r = 0;
+    if (w.vhead != w.vissue) {
+        r = retire(w, qp, v, cqe_smem);
+        if (r < 0) {
+            record_error(w, r == -1 ? kErrCqPublishTimeout : kErrRqReleaseTimeout);
             return work;
         }
-        if (verdict == 0) break;
-        ++work;
+        w.vhead += uint64_t(r);
+        work += uint32_t(r);
+        if (r > 0 && ld_vol32(&qp->st.err) != 0) v.err = 1;
     }
 
-    const uint32_t state = ld_vol32(&qp->cfg.state);
-    const bool in_error = state == UGDR_QPS_ERR || ld_vol32(&qp->st.err) != 0;
+    const bool in_error = v.state == UGDR_QPS_ERR || v.err != 0;
     if (in_error) {
         // Flush once nothing is in flight: every unissued SQ WR and every posted RQ WR.
         int flushed = 0;
         if (w.lane == 0 && qp->st.sq_head == qp->st.sq_issue) {
-            DevCq *scq = reinterpret_cast<DevCq *>(ld_vol(&qp->cfg.send_cq));
             DevCq *rcq = reinterpret_cast<DevCq *>(ld_vol(&qp->cfg.recv_cq));
-            const uint64_t tail = ld_acq_sys(&sq->tail.value);
+            const uint64_t tail = ld_acq_sys(&v.sq->tail.value);
             while (qp->st.sq_issue < tail && flushed >= 0) {
-                const uint8_t *slot = sq_slots + (qp->st.sq_issue % sq_cap) * sq_stride;
+                const uint8_t *slot = v.sq_slots + (qp->st.sq_issue % v.sq_cap) * v.sq_stride;
                 const uint64_t wr_id = ld_vol(slot);
                 const uint32_t op = ld_vol32(slot + 20);
-                queue::Cqe c{wr_id, UGDR_WC_WR_FLUSH_ERR, wc_op(op), 0u, 0u, qpn, 0u};
-                const int prc = produce_cqe(scq, c, max_ns);
+                const queue::Cqe c{wr_id, UGDR_WC_WR_FLUSH_ERR, wc_op(op), 0u, 0u, v.qpn, 0u};
+                const int prc = produce_cqe(w, v.send_cq, c, max_ns);
                 if (prc == 1) break;
                 if (prc == 2) {
                     flushed = -1;
@@ -664,18 +995,18 @@ __device__ uint32_t service_qp(Warp &w, DevQp *qp, uint8_t *wqe_smem, JobRing *j
                 }
                 qp->st.sq_issue += 1;
                 qp->st.sq_head = qp->st.sq_issue;
-                st_rel_sys(&sq->head.value, qp->st.sq_head);
+                st_rel_sys(&v.sq->head.value, qp->st.sq_head);
                 atomicAdd(&w.p->stats->error_completions, 1ull);
                 atomicAdd(&w.p->stats->retired, 1ull);
                 ++flushed;
             }
             uint64_t claim = 0, wr_id = 0;
             while (flushed >= 0 && claim_rq(qp, &claim, &wr_id)) {
-                queue::Cqe c{wr_id, UGDR_WC_WR_FLUSH_ERR, UGDR_WC_RECV_RDMA_WITH_IMM, 0u, 0u, qpn, 0u};
-                // Receive CQ full: the claim stays open and is retried by the next pass.
+                const queue::Cqe c{wr_id, UGDR_WC_WR_FLUSH_ERR, UGDR_WC_RECV_RDMA_WITH_IMM, 0u, 0u, v.qpn, 0u};
+                // Receive CQ full: wait (bounded) for the consumer; the claim is already taken.
                 int prc;
                 const uint64_t t0 = gtime();
-                while ((prc = produce_cqe(rcq, c, max_ns)) == 1 && gtime() - t0 < max_ns) __nanosleep(256);
+                while ((prc = produce_cqe(w, rcq, c, max_ns)) == 1 && gtime() - t0 < max_ns) __nanosleep(256);
                 if (prc != 0 || !release_rq(qp, claim, max_ns)) {
                     flushed = -2;
                     break;
@@ -686,45 +1017,64 @@ __device__ uint32_t service_qp(Warp &w, DevQp *qp, uint8_t *wqe_smem, JobRing *j
         }
         flushed = bcast(flushed);
         if (flushed < 0) record_error(w, flushed == -1 ? kErrCqPublishTimeout : kErrRqReleaseTimeout);
+        w.vhead = ld_vol(&qp->st.sq_head);
+        w.vissue = ld_vol(&qp->st.sq_issue);
         return work + (flushed > 0 ? flushed : 0);
     }
-    if (state != UGDR_QPS_RTS) return work;
+    if (v.state != UGDR_QPS_RTS) return work;
 
-    // Issue.
-    const uint32_t sig_all = ld_vol32(&qp->cfg.sq_sig_all);
+    // Issue: one tail read, one lane-parallel fetch of every WQE that fits the window and the
+    // staging buffer.
     uint64_t tail = 0;
-    if (w.lane == 0) tail = ld_acq_sys(&sq->tail.value);
+    if (w.lane == 0) tail = ld_acq_sys(&v.sq->tail.value);
     tail = bcast64(tail);
-    for (;;) {
-        const uint64_t head = ld_vol(&qp->st.sq_head), issue = ld_vol(&qp->st.sq_issue);
-        if (issue >= tail || issue - head >= kWindow) break;
-        // Fetch the WQE lane-parallel (16 B per lane) into shared memory.
-        const uint8_t *slot = sq_slots + (issue % sq_cap) * sq_stride;
-        for (uint32_t o = w.lane * 16; o < sq_stride && o < kWqeBytesMax; o += 32 * 16)
-            *reinterpret_cast<uint4 *>(wqe_smem + o) = ld_vol128(slot + o);
-        __syncwarp();
+    const uint64_t head = w.vhead, issue0 = w.vissue;
+    uint64_t avail = tail > issue0 ? tail - issue0 : 0;
+    if (avail > kWindow - (issue0 - head)) avail = kWindow - (issue0 - head);
+    if (avail > kWqeStage / v.sq_stride) avail = kWqeStage / v.sq_stride;
+    if (avail == 0) return work;
+    const uint64_t t_fetch0 = gtime();
+    const uint32_t nbytes = uint32_t(avail) * v.sq_stride;
+    for (uint32_t o = w.lane * 16; o < nbytes; o += 32 * 16) {
+        const uint64_t s = issue0 + o / v.sq_stride;
+        const uint8_t *src = v.sq_slots + (s % v.sq_cap) * v.sq_stride + (o % v.sq_stride);
+        *reinterpret_cast<uint4 *>(wqe_smem + o) = ld_vol128(src);
+    }
+    __syncwarp();
+    uint32_t inline_ran = 0;
+    const uint64_t t_fetch1 = gtime();
+    LaneWr lw{0, 0, 0, 0, 0};
+    uint64_t issued = issue_fast(w, qp, v, wqe_smem, issue0, uint32_t(avail), &lw);
+    const uint32_t fast_n = uint32_t(issued);
+    if (issued > 0) {
+        inline_ran += uint32_t(issued);
+        if (w.lane == 0 && !w.started) atomicCAS(&w.p->stats->first_start_ns, 0ull, (unsigned long long)gtime());
+        w.started = true;
+    }
+    const uint32_t fast_err = __ballot_sync(0xffffffffu, uint32_t(w.lane) < fast_n && lw.status != 0);
+    for (uint64_t j = fast_err ? avail : issued; j < avail; ++j) {
+        const uint64_t issue = issue0 + j;
+        const uint8_t *wqe = wqe_smem + j * v.sq_stride;
         WrRec *rec = &qp->st.win[issue % kWindow];
         uint32_t status;
         uint64_t total, remote;
-        stage_wr(w, qp, wqe_smem, rec, &status, &total, &remote);
-        const queue::SendWqe *h = reinterpret_cast<const queue::SendWqe *>(wqe_smem);
+        stage_wr(w, v, wqe, rec, &status, &total, &remote);
+        const queue::SendWqe *h = reinterpret_cast<const queue::SendWqe *>(wqe);
         const uint32_t op = h->opcode;
-        const bool signaled = sig_all || (h->send_flags & UGDR_SEND_SIGNALED) != 0;
+        const bool signaled = v.sig_all || (h->send_flags & UGDR_SEND_SIGNALED) != 0;
 
         // Responder RQ for WRITE_WITH_IMM (RNR when empty).
         int rnr = 0;  // 0 go, 1 wait, 2 retry budget exhausted
         if (status == UGDR_WC_SUCCESS && op == UGDR_WR_RDMA_WRITE_WITH_IMM) {
             if (w.lane == 0) {
-                DevQp *peer = reinterpret_cast<DevQp *>(ld_vol(&qp->cfg.peer));
                 uint64_t claim = 0, wr_id = 0;
-                if (claim_rq(peer, &claim, &wr_id)) {
+                if (claim_rq(v.peer, &claim, &wr_id)) {
                     rec->recv_claim = claim;
                     rec->recv_wr_id = wr_id;
                     qp->st.rnr_attempts = 0;
                     qp->st.rnr_next_ns = 0;
                 } else {
-                    // timeout, retry_cnt, rnr_retry, min_rnr_timer share one 32-bit word.
-                    const uint8_t rnr_retry = uint8_t(ld_vol32(&qp->cfg.timeout) >> 16);
+                    const uint8_t rnr_retry = uint8_t(v.retry_word >> 16);
                     if (rnr_retry == 7) {
                         rnr = 1;
                     } else {
@@ -734,7 +1084,7 @@ __device__ uint32_t service_qp(Warp &w, DevQp *qp, uint8_t *wqe_smem, JobRing *j
                             if (qp->st.rnr_attempts >= rnr_retry) {
                                 rnr = 2;
                             } else {
-                                const uint32_t code = ld_acq_sys32(&peer->cfg.timeout) >> 24;
+                                const uint32_t code = ld_vol32(&v.peer->cfg.timeout) >> 24;
                                 qp->st.rnr_next_ns = now + rnr_ns(code);
                                 rnr = 1;
                             }
@@ -757,13 +1107,14 @@ __device__ uint32_t service_qp(Warp &w, DevQp *qp, uint8_t *wqe_smem, JobRing *j
         }
         if (w.lane == 0) {
             rec->signaled = signaled ? 1u : 0u;
-            atomicCAS(&w.p->stats->first_start_ns, 0ull, (unsigned long long)gtime());
+            if (!w.started) atomicCAS(&w.p->stats->first_start_ns, 0ull, (unsigned long long)gtime());
         }
-        bool issued = true;
+        w.started = true;
+        bool ok = true;
         if (status == UGDR_WC_SUCCESS) {
             if (is_atomic(op) || total <= kInlineBytes) {
-                run_inline(w, rec, wqe_smem, op, total, remote);
-                if (w.lane == 0) atomicAdd(&w.p->stats->inline_runs, 1ull);
+                run_inline(w, rec, wqe, op, total, remote);
+                ++inline_ran;
             } else {
                 // Chunk so one WR spreads over about half the warps, within [16 KiB, 256 KiB]:
                 // large enough that claims are rare next to the copy, small enough that a lone
@@ -772,25 +1123,57 @@ __device__ uint32_t service_qp(Warp &w, DevQp *qp, uint8_t *wqe_smem, JobRing *j
                 uint32_t chunk = kChunkMin;
                 while (chunk < cb && chunk < kChunkMax) chunk <<= 1;
                 const uint32_t n = uint32_t((total + chunk - 1) / chunk);
-                bool ok = false;
+                bool pub = false;
                 if (w.lane == 0) {
                     rec->nchunks = n;
                     __threadfence();
-                    ok = publish_job(jr, bitmap, rec, n, chunk, w.gwarp + uint32_t(issue));
-                    if (!ok) rec->nchunks = 0;
-                    else atomicAdd(&w.p->stats->jobs_published, 1ull);
+                    pub = publish_job(jr, bitmap, rec, n, chunk, w.gwarp + uint32_t(issue));
+                    if (!pub) rec->nchunks = 0;
                 }
-                issued = bcast(ok ? 1 : 0) != 0;
+                ok = bcast(pub ? 1 : 0) != 0;
             }
         }
-        if (!issued) break;  // no job slot: retry next pass
+        if (!ok) break;  // no job slot: retry on a later pass
+        ++issued;
+        if (status != UGDR_WC_SUCCESS) break;  // stop issuing behind an error
+    }
+    if (issued > 0) {
+        __syncwarp();
         if (w.lane == 0) {
-            __threadfence();
-            qp->st.sq_issue = issue + 1;
+            // No fence: the issue cursor is private to this warp, and the publish path's system
+            // fence orders these inline payload stores before any of their CQEs.
+            qp->st.sq_issue = issue0 + issued;
         }
         __syncwarp();
-        ++work;
-        if (status != UGDR_WC_SUCCESS) break;  // stop issuing behind an error
+        w.vissue = issue0 + issued;
+        w.n_inline += inline_ran;
+        work += uint32_t(issued);
+        if (head == issue0 && issued == fast_n) {
+            // Only this fast batch is in flight and every lane still holds its WR: retire it
+            // without reading anything back.
+            const uint32_t err_mask = __ballot_sync(0xffffffffu, uint32_t(w.lane) < fast_n && lw.status != 0);
+            const uint64_t t_exec1 = gtime();
+            r = retire_commit(w, qp, v, cqe_smem, head, fast_n, err_mask, lw.wr_id, lw.status, lw.op, lw.signaled,
+                              lw.total);
+            if (w.lane == 0) {
+                const uint64_t t_end = gtime();
+                const uint64_t t_res = w.t_reserved > t_exec1 ? w.t_reserved : t_exec1;
+                atomicAdd(&w.p->stats->fast_batches, 1ull);
+                atomicAdd(&w.p->stats->fast_fetch_ns, (unsigned long long)(t_fetch1 - t_fetch0));
+                atomicAdd(&w.p->stats->fast_exec_ns, (unsigned long long)(t_exec1 - t_fetch1));
+                atomicAdd(&w.p->stats->fast_reserve_ns, (unsigned long long)(t_res - t_exec1));
+                atomicAdd(&w.p->stats->fast_publish_ns, (unsigned long long)(t_end - t_res));
+            }
+        } else {
+            r = retire(w, qp, v, cqe_smem);
+        }
+        if (r < 0) {
+            record_error(w, r == -1 ? kErrCqPublishTimeout : kErrRqReleaseTimeout);
+            return work;
+        }
+        w.vhead += uint64_t(r);
+        work += uint32_t(r);
+        if (r > 0 && ld_vol32(&qp->st.err) != 0) v.err = 1;
     }
     return work;
 }
@@ -801,7 +1184,9 @@ __device__ uint32_t service_qp(Warp &w, DevQp *qp, uint8_t *wqe_smem, JobRing *j
 // idle.  Without the mirror every warp of the grid polled the same few L2 lines and every
 // data access hashing to those slices queued behind the polls.
 __global__ void __launch_bounds__(kThreads, 1) executor_kernel(ExecParams p) {
-    __shared__ __align__(16) uint8_t wqe_buf[kWarps][kWqeBytesMax];
+    __shared__ __align__(16) uint8_t wqe_buf[kWarps][kWqeStage];
+    __shared__ __align__(16) queue::Cqe cqe_buf[kWarps][kWindow];
+    __shared__ __align__(16) MrCacheEntry mr_cache[kWarps][2];
     __shared__ volatile uint32_t s_bits[32];
     __shared__ volatile uint32_t s_slots, s_exit, s_work;
     Warp w;
@@ -811,7 +1196,12 @@ __global__ void __launch_bounds__(kThreads, 1) executor_kernel(ExecParams p) {
     w.gwarp = blockIdx.x * kWarps + w.wi;
     w.rot = w.gwarp * 2654435761u;
     w.abort = false;
-    w.n_chunks = w.n_miss = w.bytes = w.busy = 0;
+    w.n_chunks = w.n_miss = w.bytes = w.busy = w.n_inline = 0;
+    w.started = false;
+    w.cq.cq = nullptr;
+    w.vq = nullptr;
+    w.mrc = mr_cache[w.wi];
+    if (w.lane < 2) w.mrc[w.lane].key = 0;
     const uint32_t nwarps = gridDim.x * kWarps;
     JobRing *jr = p.jobs;
     // Active-job bitmap: 32 words right after the ring (see job_ring_bytes()).
@@ -835,7 +1225,7 @@ __global__ void __launch_bounds__(kThreads, 1) executor_kernel(ExecParams p) {
         const uint32_t slots = s_slots;
         const bool owner = blockIdx.x + gridDim.x * w.wi < slots;
         for (uint32_t q = blockIdx.x + gridDim.x * w.wi; q < slots; q += gridDim.x * kWarps) {
-            work += service_qp(w, &p.qps[q], wqe_buf[w.wi], jr, bits, nwarps);
+            work += service_qp(w, &p.qps[q], wqe_buf[w.wi], cqe_buf[w.wi], jr, bits, nwarps);
             if (w.abort) {
                 s_exit = 1;
                 flush_counters(w);

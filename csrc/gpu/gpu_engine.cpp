@@ -482,6 +482,11 @@ int GpuEngine::stats(control::EngineStats *out, bool reset) {
     out->jobs_published = st.jobs_published;
     out->inline_runs = st.inline_runs;
     out->busy_ns = st.busy_ns;
+    out->fast_batches = st.fast_batches;
+    out->fast_fetch_ns = st.fast_fetch_ns;
+    out->fast_exec_ns = st.fast_exec_ns;
+    out->fast_reserve_ns = st.fast_reserve_ns;
+    out->fast_publish_ns = st.fast_publish_ns;
     if (reset) {
         // Counters only (a running kernel may race a few increments into the fresh window).
         cudaMemsetAsync(stats_, 0, offsetof(DevStats, last_work_ns), ctl_stream_);

@@ -261,6 +261,8 @@ typedef struct ugdr_x_engine_stats {
     uint64_t jobs_published; /* WRs split across the grid */
     uint64_t inline_runs;    /* WRs copied by their owner warp */
     uint64_t busy_ns;        /* summed warp time spent copying chunks */
+    /* small-WR fast path (lane-parallel batches): batch count and summed phase times */
+    uint64_t fast_batches, fast_fetch_ns, fast_exec_ns, fast_reserve_ns, fast_publish_ns;
 } ugdr_x_engine_stats;
 
 int ugdr_x_query_engine_stats(ugdr_context *context, ugdr_x_engine_stats *stats,

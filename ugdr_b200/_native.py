@@ -191,6 +191,11 @@ class EngineStats(C.Structure):
         ("jobs_published", C.c_uint64),
         ("inline_runs", C.c_uint64),
         ("busy_ns", C.c_uint64),
+        ("fast_batches", C.c_uint64),
+        ("fast_fetch_ns", C.c_uint64),
+        ("fast_exec_ns", C.c_uint64),
+        ("fast_reserve_ns", C.c_uint64),
+        ("fast_publish_ns", C.c_uint64),
     ]
 
 
