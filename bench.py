@@ -7,7 +7,8 @@ RDMA_WRITEs 7 distinct slices over 7 QPs: WR k of rank r sends slice k to peer
 (r + 1 + k mod (N - 1)) % N, into that GPU's receive slot (dst + 1 + k) % 8, so every inbound WR
 of a step lands in its own slot.  With N = 8 this is exactly "a 32 MiB slice to each of its 7
 peers"; with fewer GPUs the same 7 x 32 MiB per GPU cycle over the N - 1 peers, so all traffic
-crosses NVLink (N = 1 has no peer: loopback copies inside the GPU).
+crosses NVLink.  N = 1 has no peer: the WRs are loopback copies inside the GPU, and each WR of
+the run gets its own source slice and destination slot so that no step is served from L2.
 Per-GPU work is fixed, so scaling is weak; each step reads 224 MiB and writes 224 MiB per GPU,
 more than the 126 MB L2.
 
@@ -118,9 +119,15 @@ def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None
     os.environ["UGDR_DAEMON_SOCKET"] = path
 
     slot = SLOT_MIB << 20
-    total = SLOTS * slot
     K, W = args.steps, args.warmup
     depth = K + W + 4
+    # N = 1 has no peer: every WR is a loopback copy inside the GPU.  The executor runs many
+    # queued steps at once, so with the 8-slice MR consecutive steps would re-read and re-write
+    # the same slices while they sit in L2; instead every WR of the run gets its own source slice
+    # and destination slot (capped at 448 slices, 14 GiB per MR), so each one moves HBM bytes.
+    loop = world == 1
+    nslices = min(PEERS * (K + W), 448) if loop else SLOTS
+    total = nslices * slot
 
     ctx = V.Context(V.find_device(gpu=local))
     pd = ctx.alloc_pd()
@@ -148,8 +155,11 @@ def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None
     def post_step(step_id: int):
         for k in range(PEERS):
             dst = peer_of(rank, k, world)
+            sidx = k
             dslot = (dst + 1 + k) % SLOTS
-            req[k].post_write((src_buf.data_ptr() + k * slot, slot, src_mr.lkey),
+            if loop:
+                sidx = dslot = (step_id * PEERS + k) % nslices
+            req[k].post_write((src_buf.data_ptr() + sidx * slot, slot, src_mr.lkey),
                               info[dst]["addr"] + dslot * slot, info[dst]["rkey"],
                               wr_id=(step_id << 8) | k)
 
@@ -157,11 +167,11 @@ def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None
     if rank == 0:
         all_ctx = [V.Context(V.find_device(gpu=g)) for g in range(world)]
 
-    def drain(steps: int) -> float:
+    def drain(steps: int, base: int) -> float:
         ctx.hold(True)
         comm.barrier()
         for s in range(steps):
-            post_step(s)
+            post_step(base + s)
         comm.barrier()
         ms = None
         if rank == 0:
@@ -175,12 +185,15 @@ def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None
         return ms
 
     # Warm-up (untimed), then verify every inbound slot against the sender's source slice.
-    drain(W)
+    drain(W, 0)
     comm.barrier()
     torch.cuda.synchronize()
     ok = True
     rcv_bytes = rcv_buf.view(torch.uint8)
-    for k in range(PEERS):
+    if loop:
+        n = min(PEERS * W, nslices) * slot
+        ok &= torch.equal(rcv_bytes[:n], src_buf.view(torch.uint8)[:n])
+    for k in range(PEERS if not loop else 0):
         src = sender_of(rank, k, world)
         dslot = (rank + 1 + k) % SLOTS
         g = torch.Generator(device="cuda").manual_seed(1234 + src)
@@ -196,7 +209,7 @@ def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None
             c.stats(reset=True)
     if sampler:
         sampler.__enter__()
-    t_ms = drain(K)
+    t_ms = drain(K, W)
     if sampler:
         sampler.__exit__(None, None, None)
     clocks = sampler.summary() if sampler else None
@@ -262,7 +275,9 @@ def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None
             "seq_len": slot,
             "parallelism": f"{world} GPU(s) x {PEERS} QPs, 32 MiB per WR",
             "mr_bytes_per_gpu": total,
-            "l2": "inputs larger than L2: 7 distinct 32 MiB source slices (224 MiB) read + 224 MiB written per GPU per step",
+            "l2": ("inputs larger than L2: every WR of the run has its own 32 MiB source slice and destination slot"
+                   if loop else
+                   "inputs larger than L2: 7 distinct 32 MiB source slices (224 MiB) read + 224 MiB written per GPU per step"),
             "timing": "CUDA events around each GPU's executor launch, max over GPUs",
             "correct": bool(ok),
         },

@@ -2,9 +2,9 @@
 // rank's process (the same export / open path as MR registration), and sm_100a kernels move the
 // data with direct NVLink loads and stores, fusing the arithmetic into the transfer.
 //
-//  * Allreduce (bf16, fp32 accumulation): reduce-scatter kernel, then all-gather kernel.  Rank r
-//    pulls shard r from every peer, sums, and stores it in place; then pulls every other shard.
-//    2 (N - 1) / N of the buffer crosses NVLink per GPU, the ring optimum, in two launches.
+//  * Allreduce (bf16, fp32 accumulation), one kernel: rank r pulls shard r from every rank, sums,
+//    and pushes the sum into every rank's buffer, vector by vector.  2 (N - 1) / N of the buffer
+//    crosses NVLink per GPU, the ring optimum, with both link directions busy throughout.
 //  * MoE routing (moe_route): deterministic counting sort of (token, k) rows by expert - counts per
 //    expert and each row's position within its expert group.  Scratch: per-block histograms.
 //  * MoE dispatch: each (token, k) row is stored straight into the expert owner's receive
@@ -98,26 +98,61 @@ __device__ __forceinline__ uint4 pack8(const float (&a)[8]) {
 
 // ---- allreduce ---------------------------------------------------------------------------------
 
-// Phase 1: shard `rank` of every peer's buffer summed into this rank's buffer (in place).
-// Elements are processed 8 at a time (16 B); the shard is [begin, end) in 8-element vectors.
+// Entry handshake: every CTA's thread 0 publishes `epoch` into each peer's entry word for this
+// rank and waits (bounded) until every peer's word in its own signal buffer reached `epoch`, i.e.
+// every rank has launched this call, so its input is in place and its previous call is over.
+// The waits read local memory only; peers' kernels run on other GPUs, so no co-residency is
+// assumed.
+__device__ void entry_barrier(const PeerSet &ps, uint64_t epoch, uint32_t slot, uint64_t max_ns) {
+    if (threadIdx.x == 0) {
+        for (int q = 0; q < ps.n; ++q) st_rel_sys(ps.signal[q] + slot * kMaxRanks + ps.rank, epoch);
+        const uint64_t *mine = ps.signal[ps.rank] + slot * kMaxRanks;
+        const uint64_t t0 = gtime();
+        for (int q = 0; q < ps.n; ++q) {
+            uint32_t spins = 0;
+            while (ld_acq_sys(mine + q) < epoch) {
+                if ((++spins & 255) == 0 && gtime() - t0 > max_ns) {
+                    atomicExch(ps.status, 1u);
+                    break;
+                }
+                __nanosleep(32);
+            }
+        }
+    }
+    __syncthreads();
+}
+
+// One-kernel allreduce.  Rank r owns shard r of the buffer; for each 16-byte vector of it a
+// thread loads the vector from every rank (NVLink loads), sums in fp32, rounds to bf16 once, and
+// stores the result into every rank's buffer (NVLink stores).  Shard r of a peer's buffer is
+// read and written only by rank r, and a thread reads an element before it overwrites it, so no
+// barrier is needed between the reduce and the broadcast: they overlap vector by vector, and
+// both link directions carry traffic for the whole kernel.  Per GPU, (N - 1) / N of the buffer
+// arrives by loads and (N - 1) / N by peers' stores: 2 (N - 1) / N in total, the ring optimum.
 template <int NR>
-__global__ void __launch_bounds__(512) reduce_scatter_kernel(PeerSet ps, uint64_t base_off, uint64_t nvec,
-                                                             uint64_t epoch, uint64_t max_ns) {
+__global__ void __launch_bounds__(512) allreduce_kernel(PeerSet ps, uint64_t base_off, uint64_t nvec,
+                                                        uint64_t epoch, uint64_t max_ns) {
+    entry_barrier(ps, epoch, kSlotArEntry, max_ns);
     const uint64_t per = (nvec + ps.n - 1) / ps.n;
     const uint64_t begin = min(nvec, per * ps.rank), end = min(nvec, begin + per);
     const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
+    uint8_t *bufs[NR];
+#pragma unroll
+    for (int q = 0; q < NR; ++q)
+        bufs[q] = q < ps.n ? reinterpret_cast<uint8_t *>(ps.buf[q]) + base_off : nullptr;
     for (uint64_t i = begin + blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < end; i += 2 * stride) {
         const bool two = i + stride < end;
-        float a[8] = {0, 0, 0, 0, 0, 0, 0, 0}, b[8] = {0, 0, 0, 0, 0, 0, 0, 0};
         uint4 va[NR], vb[NR];
 #pragma unroll
         for (int q = 0; q < NR; ++q) {
             if (q < ps.n) {
-                const uint8_t *src = reinterpret_cast<const uint8_t *>(ps.buf[q]) + base_off;
-                va[q] = ld128(src + i * 16);
-                if (two) vb[q] = ld128(src + (i + stride) * 16);
+                va[q] = ld128(bufs[q] + i * 16);
+                if (two) vb[q] = ld128(bufs[q] + (i + stride) * 16);
             }
         }
+        // Each vector is summed once, by its owner, in rank order, and the same bits go to every
+        // rank.
+        float a[8] = {0, 0, 0, 0, 0, 0, 0, 0}, b[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
         for (int q = 0; q < NR; ++q) {
             if (q < ps.n) {
@@ -125,35 +160,16 @@ __global__ void __launch_bounds__(512) reduce_scatter_kernel(PeerSet ps, uint64_
                 if (two) acc8(b, vb[q]);
             }
         }
-        uint8_t *dst = reinterpret_cast<uint8_t *>(ps.buf[ps.rank]) + base_off;
-        st128(dst + i * 16, pack8(a));
-        if (two) st128(dst + (i + stride) * 16, pack8(b));
-    }
-    end_barrier(ps, epoch, 0, max_ns);
-}
-
-// Phase 2: every other rank's reduced shard copied from its owner into this rank's buffer.
-__global__ void __launch_bounds__(512) all_gather_kernel(PeerSet ps, uint64_t base_off, uint64_t nvec,
-                                                         uint64_t epoch, uint64_t max_ns) {
-    const uint64_t per = (nvec + ps.n - 1) / ps.n;
-    const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
-    uint8_t *dst = reinterpret_cast<uint8_t *>(ps.buf[ps.rank]) + base_off;
-    for (int k = 1; k < ps.n; ++k) {
-        const int q = (ps.rank + k) % ps.n;  // stagger owners so links are used evenly
-        const uint64_t begin = min(nvec, per * q), end = min(nvec, begin + per);
-        const uint8_t *src = reinterpret_cast<const uint8_t *>(ps.buf[q]) + base_off;
-        uint64_t i = begin + blockIdx.x * uint64_t(blockDim.x) + threadIdx.x;
-        for (; i + 3 * stride < end; i += 4 * stride) {
-            const uint4 v0 = ld128(src + i * 16), v1 = ld128(src + (i + stride) * 16);
-            const uint4 v2 = ld128(src + (i + 2 * stride) * 16), v3 = ld128(src + (i + 3 * stride) * 16);
-            st128(dst + i * 16, v0);
-            st128(dst + (i + stride) * 16, v1);
-            st128(dst + (i + 2 * stride) * 16, v2);
-            st128(dst + (i + 3 * stride) * 16, v3);
+        const uint4 ra = pack8(a), rb = pack8(b);
+#pragma unroll
+        for (int q = 0; q < NR; ++q) {
+            if (q < ps.n) {
+                st128(bufs[q] + i * 16, ra);
+                if (two) st128(bufs[q] + (i + stride) * 16, rb);
+            }
         }
-        for (; i < end; i += stride) st128(dst + i * 16, ld128(src + i * 16));
     }
-    end_barrier(ps, epoch, 1, max_ns);
+    end_barrier(ps, epoch, kSlotArEnd, max_ns);
 }
 
 // ---- MoE routing (counting sort) ---------------------------------------------------------------
@@ -186,20 +202,24 @@ __global__ void route_scan_kernel(uint32_t *hist, int nblocks, int nexp, int32_t
     counts[e] = int32_t(run);
 }
 
-// K3: positions in row order; one warp walks its block's rows 32 at a time and ranks equal
-// experts with __match_any_sync, so the result is deterministic.
+// K3: positions in row order.  The block first stages its rows' expert ids in shared memory
+// (all threads, coalesced), then one warp walks them 32 at a time and ranks equal experts with
+// __match_any_sync, so the result is deterministic and the walk costs no global round trips.
 __global__ void route_place_kernel(const int32_t *idx, uint64_t rows, int nexp, const uint32_t *off,
                                    int32_t *pos) {
     extern __shared__ uint32_t cur[];
-    for (int e = threadIdx.x; e < nexp; e += blockDim.x) cur[e] = off[uint64_t(blockIdx.x) * nexp + e];
-    __syncwarp();
-    const int lane = threadIdx.x & 31;
+    __shared__ int32_t ids[kRouteRowsPerBlock];
     const uint64_t b0 = uint64_t(blockIdx.x) * kRouteRowsPerBlock;
     const uint64_t b1 = min(rows, b0 + kRouteRowsPerBlock);
-    for (uint64_t r0 = b0; r0 < b1; r0 += 32) {
-        const uint64_t r = r0 + lane;
-        const bool live = r < b1;
-        int e = live ? idx[r] : -1;
+    const int n = int(b1 - b0);
+    for (int e = threadIdx.x; e < nexp; e += blockDim.x) cur[e] = off[uint64_t(blockIdx.x) * nexp + e];
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ids[i] = idx[b0 + i];
+    __syncthreads();
+    const int lane = threadIdx.x;
+    for (int i0 = 0; threadIdx.x < 32 && i0 < n; i0 += 32) {
+        const int i = i0 + lane;
+        const bool live = i < n;
+        int e = live ? ids[i] : -1;
         const bool ok = live && e >= 0 && e < nexp;
         if (!ok) e = -1 - lane;  // unique key: never matches a real expert or another lane
         const unsigned same = __match_any_sync(0xffffffffu, e);
@@ -208,15 +228,46 @@ __global__ void route_place_kernel(const int32_t *idx, uint64_t rows, int nexp, 
         __syncwarp();
         if (ok && lower == 0) cur[e] = base + __popc(same);
         __syncwarp();
-        if (live) pos[r] = ok ? int32_t(base + __popc(lower)) : -1;
+        if (live) ids[i] = ok ? int32_t(base + __popc(lower)) : -1;
     }
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) pos[b0 + i] = ids[i];
 }
 
 // ---- MoE dispatch / combine --------------------------------------------------------------------
 
-// Dispatch: row (t, k) -> recv buffer of the expert's owner at row dst_row[e_base + rank part].
-// `gbase[e]` = first row of expert e's group in its owner's buffer for rows of THIS rank
-// (expert group start + rows of the lower ranks for that expert).
+// Row resolution shared by dispatch and combine: lane j of the warp resolves row r0 + j (its
+// expert, owner and row in the owner's receive area) in one round of parallel loads; the copy
+// loops then take the pointers by shuffle, so no dependent index loads sit between row copies.
+struct RowRef {
+    uint8_t *ptr;  // the row in its owner's receive area (null: skipped)
+    float w;
+};
+
+__device__ __forceinline__ RowRef resolve_row(const PeerSet &ps, const int32_t *idx, const int32_t *pos,
+                                              const int64_t *gbase, const float *w, uint64_t r, bool live,
+                                              int exp_per_rank, uint64_t recv_off, uint64_t recv_rows,
+                                              uint64_t row_bytes) {
+    RowRef ref{nullptr, 0.f};
+    if (!live) return ref;
+    const int e = idx[r];
+    const int p = pos[r];
+    if (w != nullptr) ref.w = w[r];
+    if (e < 0 || p < 0) return ref;
+    const int owner = e / exp_per_rank;
+    const uint64_t row = uint64_t(gbase[e]) + uint64_t(p);
+    if (owner >= ps.n || row >= recv_rows) {
+        atomicExch(ps.status, 2u);  // receive buffer too small: recorded, row skipped
+        return ref;
+    }
+    ref.ptr = reinterpret_cast<uint8_t *>(ps.buf[owner]) + recv_off + row * row_bytes;
+    return ref;
+}
+
+// Dispatch: row (t, k) -> recv buffer of the expert's owner at row gbase[e] + pos[(t, k)]
+// (`gbase[e]` = first row of expert e's group in its owner's buffer for rows of THIS rank).
+// A warp takes 32 consecutive rows at a time; each row is copied with 8 vectors in flight per
+// lane, so a 14 KiB row is 3.5 load rounds and the stores stream over NVLink behind them.
 __global__ void __launch_bounds__(512) dispatch_kernel(PeerSet ps, const uint8_t *x, uint64_t row_bytes,
                                                        const int32_t *idx, const int32_t *pos,
                                                        const int64_t *gbase, uint64_t rows, int topk,
@@ -226,33 +277,33 @@ __global__ void __launch_bounds__(512) dispatch_kernel(PeerSet ps, const uint8_t
     const uint64_t warp = (uint64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const uint64_t nwarps = (uint64_t(gridDim.x) * blockDim.x) >> 5;
     const uint64_t nv = row_bytes / 16;
-    for (uint64_t r = warp; r < rows; r += nwarps) {
-        const int e = idx[r];
-        const int p = pos[r];
-        if (e < 0 || p < 0) continue;
-        const int owner = e / exp_per_rank;
-        const uint64_t drow = uint64_t(gbase[e]) + uint64_t(p);
-        if (owner >= ps.n || drow >= recv_rows) {
-            atomicExch(ps.status, 2u);  // receive buffer too small: recorded, row skipped
-            continue;
+    for (uint64_t r0 = warp * 32; r0 < rows; r0 += nwarps * 32) {
+        const RowRef mine = resolve_row(ps, idx, pos, gbase, nullptr, r0 + lane, r0 + lane < rows, exp_per_rank,
+                                        recv_off, recv_rows, row_bytes);
+        const uint64_t nr = min(uint64_t(32), rows - r0);
+        for (uint64_t j = 0; j < nr; ++j) {
+            uint4 *dst = reinterpret_cast<uint4 *>(
+                __shfl_sync(0xffffffffu, reinterpret_cast<uint64_t>(mine.ptr), int(j)));
+            if (dst == nullptr) continue;
+            const uint4 *src = reinterpret_cast<const uint4 *>(x + ((r0 + j) / topk) * row_bytes);
+            uint64_t i = lane;
+            for (; i + 7 * 32 < nv; i += 8 * 32) {
+                uint4 v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v[u] = ld128(src + i + u * 32);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) st128(dst + i + u * 32, v[u]);
+            }
+            for (; i < nv; i += 32) st128(dst + i, ld128(src + i));
         }
-        const uint4 *src = reinterpret_cast<const uint4 *>(x + (r / topk) * row_bytes);
-        uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(ps.buf[owner]) + recv_off +
-                                               drow * row_bytes);
-        uint64_t i = lane;
-        for (; i + 96 < nv; i += 128) {
-            const uint4 a = ld128(src + i), b = ld128(src + i + 32), c = ld128(src + i + 64), d = ld128(src + i + 96);
-            st128(dst + i, a);
-            st128(dst + i + 32, b);
-            st128(dst + i + 64, c);
-            st128(dst + i + 96, d);
-        }
-        for (; i < nv; i += 32) st128(dst + i, ld128(src + i));
     }
-    end_barrier(ps, epoch, 2, max_ns);
+    end_barrier(ps, epoch, kSlotDispatch, max_ns);
 }
 
-// Combine: out[t] = sum_k w[t, k] * expert_out_row(t, k), rows pulled from their owners.
+// Combine: out[t] = sum_k w[t, k] * expert_out_row(t, k), rows pulled from their owners.  Lane
+// k (< topk) resolves row (t, k); every lane then streams its 16-byte columns with all top-k
+// loads of a column (two columns per step) in flight before the fp32 weighted sum.
+template <int TOPK>
 __global__ void __launch_bounds__(512) combine_kernel(PeerSet ps, uint8_t *out, uint64_t row_bytes,
                                                       const int32_t *idx, const int32_t *pos,
                                                       const int64_t *gbase, const float *w, uint64_t ntok,
@@ -263,27 +314,48 @@ __global__ void __launch_bounds__(512) combine_kernel(PeerSet ps, uint8_t *out, 
     const uint64_t nwarps = (uint64_t(gridDim.x) * blockDim.x) >> 5;
     const uint64_t nv = row_bytes / 16;
     for (uint64_t t = warp; t < ntok; t += nwarps) {
-        for (uint64_t i = lane; i < nv; i += 32) {
-            float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-            for (int k = 0; k < topk; ++k) {
-                const uint64_t r = t * topk + k;
-                const int e = idx[r], p = pos[r];
-                if (e < 0 || p < 0) continue;
-                const int owner = e / exp_per_rank;
-                const uint64_t srow = uint64_t(gbase[e]) + uint64_t(p);
-                if (owner >= ps.n || srow >= recv_rows) continue;
-                const uint4 v = ld128(reinterpret_cast<const uint8_t *>(ps.buf[owner]) + recv_off +
-                                      srow * row_bytes + i * 16);
-                const float wk = w[r];
-                float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                acc8(f, v);
+        const RowRef mine = resolve_row(ps, idx, pos, gbase, w, t * topk + lane, lane < topk, exp_per_rank,
+                                        recv_off, recv_rows, row_bytes);
+        const uint8_t *sp[TOPK];
+        float wk[TOPK];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) a[j] += wk * f[j];
+        for (int k = 0; k < TOPK; ++k) {
+            sp[k] = reinterpret_cast<const uint8_t *>(
+                __shfl_sync(0xffffffffu, reinterpret_cast<uint64_t>(mine.ptr), k));
+            wk[k] = __shfl_sync(0xffffffffu, mine.w, k);
+        }
+        uint8_t *orow = out + t * row_bytes;
+        constexpr uint64_t kStep = TOPK <= 8 ? 64 : 32;  // two columns per step while registers allow
+        for (uint64_t i = lane; i < nv; i += kStep) {
+            const bool two = kStep == 64 && i + 32 < nv;
+            uint4 va[TOPK], vb[TOPK];
+#pragma unroll
+            for (int k = 0; k < TOPK; ++k) {
+                if (sp[k] != nullptr) {
+                    va[k] = ld128(sp[k] + i * 16);
+                    if (two) vb[k] = ld128(sp[k] + (i + 32) * 16);
+                }
             }
-            st128(out + t * row_bytes + i * 16, pack8(a));
+            float a[8] = {0, 0, 0, 0, 0, 0, 0, 0}, b[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+            for (int k = 0; k < TOPK; ++k) {
+                if (sp[k] == nullptr) continue;
+                float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                acc8(f, va[k]);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) a[j] += wk[k] * f[j];
+                if (two) {
+                    float g[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                    acc8(g, vb[k]);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) b[j] += wk[k] * g[j];
+                }
+            }
+            st128(orow + i * 16, pack8(a));
+            if (two) st128(orow + (i + 32) * 16, pack8(b));
         }
     }
-    end_barrier(ps, epoch, 3, max_ns);
+    end_barrier(ps, epoch, kSlotCombine, max_ns);
 }
 
 // Counts exchange: this rank's per-expert counts stored into every rank's table
@@ -297,7 +369,7 @@ __global__ void counts_exchange_kernel(PeerSet ps, const int32_t *counts, int ne
             t[ps.rank * nexp + e] = c;
         }
     }
-    end_barrier(ps, epoch, 4, max_ns);
+    end_barrier(ps, epoch, kSlotCounts, max_ns);
 }
 
 // Layout (one block): expert e's group in its owner's receive area starts after the groups of
@@ -342,13 +414,15 @@ int launch_allreduce_bf16(const PeerSet &ps, uint64_t offset, uint64_t count, ui
     if (count % 8 != 0 || offset % 16 != 0) return int(cudaErrorInvalidValue);
     const uint64_t nvec = count / 8;
     switch (ps.n) {
-    case 1: reduce_scatter_kernel<1><<<ctas, 512, 0, s>>>(ps, offset, nvec, epoch, max_ns); break;
-    case 2: reduce_scatter_kernel<2><<<ctas, 512, 0, s>>>(ps, offset, nvec, epoch, max_ns); break;
-    case 3:
-    case 4: reduce_scatter_kernel<4><<<ctas, 512, 0, s>>>(ps, offset, nvec, epoch, max_ns); break;
-    default: reduce_scatter_kernel<8><<<ctas, 512, 0, s>>>(ps, offset, nvec, epoch, max_ns); break;
+    case 1: allreduce_kernel<1><<<ctas, 512, 0, s>>>(ps, offset, nvec, epoch, max_ns); break;
+    case 2: allreduce_kernel<2><<<ctas, 512, 0, s>>>(ps, offset, nvec, epoch, max_ns); break;
+    case 3: allreduce_kernel<3><<<ctas, 512, 0, s>>>(ps, offset, nvec, epoch, max_ns); break;
+    case 4: allreduce_kernel<4><<<ctas, 512, 0, s>>>(ps, offset, nvec, epoch, max_ns); break;
+    case 5: allreduce_kernel<5><<<ctas, 512, 0, s>>>(ps, offset, nvec, epoch, max_ns); break;
+    case 6: allreduce_kernel<6><<<ctas, 512, 0, s>>>(ps, offset, nvec, epoch, max_ns); break;
+    case 7: allreduce_kernel<7><<<ctas, 512, 0, s>>>(ps, offset, nvec, epoch, max_ns); break;
+    default: allreduce_kernel<8><<<ctas, 512, 0, s>>>(ps, offset, nvec, epoch, max_ns); break;
     }
-    all_gather_kernel<<<ctas, 512, 0, s>>>(ps, offset, nvec, epoch, max_ns);
     return int(cudaGetLastError());
 }
 
@@ -364,7 +438,7 @@ int launch_route(const int32_t *idx, uint64_t rows, int nexp, int32_t *counts, i
     const size_t sh = size_t(nexp) * sizeof(uint32_t);
     if (nblocks > 0) route_hist_kernel<<<nblocks, 256, sh, s>>>(idx, rows, nexp, scratch);
     route_scan_kernel<<<(nexp + 127) / 128, 128, 0, s>>>(scratch, nblocks, nexp, counts);
-    if (nblocks > 0) route_place_kernel<<<nblocks, 32, sh, s>>>(idx, rows, nexp, scratch, pos);
+    if (nblocks > 0) route_place_kernel<<<nblocks, 256, sh, s>>>(idx, rows, nexp, scratch, pos);
     return int(cudaGetLastError());
 }
 
@@ -383,8 +457,20 @@ int launch_combine(const PeerSet &ps, void *out, uint64_t row_bytes, const int32
                    uint64_t recv_off, uint64_t recv_rows, uint64_t epoch, int ctas, uint64_t max_ns,
                    cudaStream_t s) {
     if (row_bytes % 16 != 0) return int(cudaErrorInvalidValue);
-    combine_kernel<<<ctas, 512, 0, s>>>(ps, static_cast<uint8_t *>(out), row_bytes, idx, pos, gbase, w, ntok, topk,
-                                        exp_per_rank, recv_off, recv_rows, epoch, max_ns);
+    if (topk <= 0 || topk > 16) return int(cudaErrorInvalidValue);
+    uint8_t *o = static_cast<uint8_t *>(out);
+#define UGDR_COMBINE(K)                                                                                  \
+    combine_kernel<K><<<ctas, 512, 0, s>>>(ps, o, row_bytes, idx, pos, gbase, w, ntok, topk, exp_per_rank, \
+                                           recv_off, recv_rows, epoch, max_ns)
+    if (topk <= 2)
+        UGDR_COMBINE(2);
+    else if (topk <= 4)
+        UGDR_COMBINE(4);
+    else if (topk <= 8)
+        UGDR_COMBINE(8);
+    else
+        UGDR_COMBINE(16);
+#undef UGDR_COMBINE
     return int(cudaGetLastError());
 }
 

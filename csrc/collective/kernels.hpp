@@ -10,6 +10,9 @@ namespace ugdr::coll {
 constexpr int kMaxRanks = 8;
 constexpr int kRouteRowsPerBlock = 4096;  // fixed, so routing output never depends on the GPU
 constexpr int kRouteMaxExperts = 4096;
+// Signal slots (each kMaxRanks uint64 words per rank, plus one arrival counter per slot).
+constexpr uint32_t kSlotArEnd = 0, kSlotDispatch = 2, kSlotCombine = 3, kSlotCounts = 4, kSlotArEntry = 5;
+constexpr uint32_t kSignalSlots = 8;
 
 // One rank's view of a symmetric allocation: every rank's buffer and signal words mapped into
 // this process (CUDA IPC), plus this rank's own arrival counters and status word.

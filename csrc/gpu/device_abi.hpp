@@ -20,9 +20,9 @@ namespace ugdr::gpu {
 constexpr uint32_t kMaxMrs = 1u << 16;       // key slots (matches the control plane's keys)
 constexpr uint32_t kMaxQpsPerEngine = 4096;
 constexpr uint32_t kMaxCqsPerEngine = 4096;
-constexpr uint32_t kWindow = 16;             // in-flight WRs per QP
+constexpr uint32_t kWindow = 32;             // in-flight WRs per QP (one per lane of the owner warp)
 constexpr uint32_t kMaxSge = 32;
-constexpr uint32_t kJobSlots = 1024;         // large-WR job ring per engine
+constexpr uint32_t kJobSlots = 1024;         // chunked-job slots per engine
 constexpr uint32_t kInlineBytes = 4096;      // WRs up to this size are copied by the owner warp
 
 struct DevMr {
@@ -118,17 +118,23 @@ struct DevQp {
     DevQpState st;
 };
 
-// One chunked WR.  `ctl` = generation (high 32) | next unclaimed chunk (low 32); claims are
-// fetch-and-adds on it.  `seq` is even while the slot is free and odd while a job owns it; the
-// slot is freed only when every chunk is done, so the fields below never change under a worker
-// that holds an unfinished chunk.
+// One chunked job: WRs [first, first + nwr) of one QP's window (indices mod kWindow), cut into
+// `chunk_bytes` chunks numbered across the WRs (WR i owns chunks [start[i], start[i + 1])).
+// `ctl` = generation (high 32) | next unclaimed chunk (low 32); claims are fetch-and-adds on it.
+// `seq` is even while the slot is free and odd while a job owns it; the slot is freed when
+// `done` reaches `nchunks`, so no field changes under a worker that holds an unfinished chunk.
 struct alignas(64) Job {
     unsigned long long ctl;
     unsigned long long seq;
-    WrRec *rec;  // 16-byte aligned with the two words after it: read as one vector
+    WrRec *win;  // 16-byte aligned with the two words after it: read as one vector
     uint32_t nchunks;
     uint32_t chunk_bytes;
-    unsigned long long pad[4];
+    uint32_t first;
+    uint32_t nwr;
+    uint32_t done;
+    uint32_t pad0;
+    uint32_t pad1[4];
+    uint32_t start[kWindow];
 };
 
 struct JobRing {

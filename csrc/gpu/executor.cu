@@ -58,6 +58,16 @@ __device__ __forceinline__ uint32_t ld_acq_sys32(const void *p) {
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+__device__ __forceinline__ uint64_t ld_acq_gpu(const void *p) {
+    uint64_t v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint64_t add_acq_gpu(void *p, uint64_t v) {
+    uint64_t old;
+    asm volatile("atom.acquire.gpu.global.add.u64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
+    return old;
+}
 __device__ __forceinline__ void st_rel_sys(void *p, uint64_t v) {
     asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
@@ -228,6 +238,7 @@ struct Warp {
     bool started;  // this warp stamped first_start_ns in this launch
     CqCache cq;
     MrCacheEntry *mrc;  // this warp's two-entry MR cache (shared memory)
+    volatile uint32_t *mirror;  // the CTA's shared copy of the active-job bitmap
     // Cached view of the QP this warp serviced last (see service_qp).
     DevQp *vq;
     uint64_t vt, vhead, vissue, t_reserved;
@@ -375,9 +386,9 @@ __device__ uint64_t rnr_ns(uint32_t code) {
 
 // ---- jobs ------------------------------------------------------------------------------------
 
-// Publish `rec` as a chunked job (lane 0).  Returns false when no job slot is free.
-__device__ bool publish_job(JobRing *jr, uint32_t *bitmap, WrRec *rec, uint32_t nchunks,
-                            uint32_t chunk_bytes, uint32_t seed) {
+// Take a free job slot (lane 0).  Returns its index (and the job generation it starts), or -1
+// when none is free.
+__device__ int take_job_slot(JobRing *jr, uint32_t seed, unsigned long long *gen) {
     for (uint32_t k = 0; k < 64; ++k) {
         const uint32_t s = (seed * 37u + k * 97u) % kJobSlots;
         Job *j = &jr->slots[s];
@@ -385,32 +396,57 @@ __device__ bool publish_job(JobRing *jr, uint32_t *bitmap, WrRec *rec, uint32_t 
         const unsigned long long seq = ld_vol(&j->seq);
         if ((seq & 1ull) != 0) continue;
         if (atomicCAS(&j->seq, seq, seq + 1) != seq) continue;
-        j->rec = rec;
+        *gen = (seq + 1) >> 1;
+        return int(s);
+    }
+    return -1;
+}
+
+// Publish WRs [first, first + nwr) of a QP window as one job in a taken slot (warp-wide): lane
+// i (< nwr) passes WR i's first chunk index.  The WRs' records are complete before the call.
+// The CTA's own bitmap mirror is updated at once so its warps can start claiming immediately;
+// other CTAs see the job at their leader's next refresh.
+__device__ void publish_job(Warp &w, JobRing *jr, uint32_t *bitmap, int slot, unsigned long long gen,
+                            WrRec *win, uint32_t first, uint32_t nwr, uint32_t start, uint32_t nchunks,
+                            uint32_t chunk_bytes) {
+    Job *j = &jr->slots[slot];
+    if (uint32_t(w.lane) < nwr) j->start[w.lane] = start;
+    if (w.lane == 0) {
+        j->win = win;
         j->nchunks = nchunks;
         j->chunk_bytes = chunk_bytes;
-        const unsigned long long gen = (seq + 1) >> 1;
-        __threadfence();
-        atomicExch(&j->ctl, (gen << 32) | 0ull);
-        __threadfence();
-        atomicOr(&bitmap[s >> 5], 1u << (s & 31));
-        return true;
+        j->first = first;
+        j->nwr = nwr;
+        j->done = 0;
     }
-    return false;
+    __syncwarp();
+    if (w.lane == 0) {
+        __threadfence();
+        atomicExch(&j->ctl, gen << 32);
+        __threadfence();
+        const uint32_t bit = 1u << (slot & 31);
+        atomicOr(&bitmap[slot >> 5], bit);
+        atomicOr(const_cast<uint32_t *>(&w.mirror[slot >> 5]), bit);
+        atomicAdd(&w.p->stats->jobs_published, 1ull);
+    }
+    __syncwarp();
 }
 
 struct Claim {
     WrRec *rec;
     Job *job;
-    uint32_t chunk, cb, n;
+    uint64_t off;
+    uint32_t cb, n;
 };
 
 // Claim one chunk from any active job (warp-wide): a fetch-and-add on the job's counter, which
 // always yields a unique index (no CAS retry storms when thousands of warps contend).
-//  * The fields are read before the add; if the add returns the same generation, no recycle
-//    happened in between, so the fields belong to it (a slot is recycled only after all of its
-//    chunks are done, which cannot be while our index is below nchunks).
+//  * The fields are read after an acquiring load of the counter; if the add returns the same
+//    generation, no recycle happened in between, so the fields belong to it (a slot is recycled
+//    only after all of its chunks are done, which cannot be while our index is below nchunks).
 //  * If the add lands in a newer generation, the index belongs to that job: re-read its fields
 //    (stable for the same reason) and run it, so no index is ever lost.
+// The chunk's WR is found by a ballot over the job's per-WR start indices, one per lane.
 // `mirror` is the CTA's shared copy of the active-job bitmap (refreshed by the CTA leader).
 __device__ bool claim_chunk(Warp &w, JobRing *jr, uint32_t *bitmap, const volatile uint32_t *mirror,
                             Claim *out) {
@@ -418,7 +454,8 @@ __device__ bool claim_chunk(Warp &w, JobRing *jr, uint32_t *bitmap, const volati
     const uint32_t nonzero = __ballot_sync(0xffffffffu, word != 0);
     if (nonzero == 0) return false;
     int got = 0;
-    Claim cl{};
+    uint32_t c = 0, slot = 0;
+    uint4 g{};
     if (w.lane == 0) {
         // Rotate the starting word / bit per warp so warps spread over active jobs.
         const uint32_t rotw = w.rot & 31;
@@ -429,21 +466,17 @@ __device__ bool claim_chunk(Warp &w, JobRing *jr, uint32_t *bitmap, const volati
             const uint32_t rb = (w.rot >> 5) & 31;
             const uint32_t rotated = (bits >> rb) | (bits << ((32 - rb) & 31));
             const uint32_t b = (rb + __ffs(rotated) - 1) & 31;
-            Job *j = &jr->slots[wsel * 32 + b];
-            const unsigned long long v0 = ld_vol(&j->ctl);
-            const uint4 f = ld_vol128(&j->rec);  // rec (x,y), nchunks (z), chunk_bytes (w)
+            slot = wsel * 32 + b;
+            Job *j = &jr->slots[slot];
+            const unsigned long long v0 = ld_acq_gpu(&j->ctl);
+            const uint4 f = ld_vol128(&j->win);  // win (x,y), nchunks (z), chunk_bytes (w)
             if (uint32_t(v0) < f.z) {
-                const unsigned long long v = atomicAdd(&j->ctl, 1ull);
-                uint4 g = f;
-                if ((v >> 32) != (v0 >> 32)) g = ld_vol128(&j->rec);  // newer generation
-                const uint32_t c = uint32_t(v);
+                const unsigned long long v = add_acq_gpu(&j->ctl, 1ull);
+                g = f;
+                if ((v >> 32) != (v0 >> 32)) g = ld_vol128(&j->win);  // newer generation
+                c = uint32_t(v);
                 if (c < g.z) {
                     got = 1;
-                    cl.rec = reinterpret_cast<WrRec *>((uint64_t(g.y) << 32) | g.x);
-                    cl.job = j;
-                    cl.chunk = c;
-                    cl.n = g.z;
-                    cl.cb = g.w;
                     if (c + 1 == g.z) atomicAnd(&bitmap[wsel], ~(1u << b));  // all handed out
                 }
             }
@@ -456,18 +489,32 @@ __device__ bool claim_chunk(Warp &w, JobRing *jr, uint32_t *bitmap, const volati
         w.n_miss += 1;
         return false;
     }
-    out->rec = reinterpret_cast<WrRec *>(bcast64(reinterpret_cast<uint64_t>(cl.rec)));
-    out->job = reinterpret_cast<Job *>(bcast64(reinterpret_cast<uint64_t>(cl.job)));
-    out->chunk = bcast(cl.chunk);
-    out->cb = bcast(cl.cb);
-    out->n = bcast(cl.n);
+    __syncwarp();  // lane 0's acquire orders the other lanes' reads of the job below
+    c = bcast(c);
+    slot = bcast(slot);
+    g.x = bcast(g.x);
+    g.y = bcast(g.y);
+    g.z = bcast(g.z);
+    g.w = bcast(g.w);
+    Job *j = &jr->slots[slot];
+    const uint32_t first = ld_vol32(&j->first), nwr = ld_vol32(&j->nwr);
+    const uint32_t st = uint32_t(w.lane) < nwr ? ld_vol32(&j->start[w.lane]) : 0xffffffffu;
+    const uint32_t le = __ballot_sync(0xffffffffu, uint32_t(w.lane) < nwr && st <= c);
+    const int wr = le ? 31 - __clz(le) : 0;
+    const uint32_t s0 = __shfl_sync(0xffffffffu, st, wr);
+    WrRec *win = reinterpret_cast<WrRec *>((uint64_t(g.y) << 32) | g.x);
+    out->rec = win + (first + uint32_t(wr)) % kWindow;
+    out->job = j;
+    out->off = uint64_t(c - s0) * g.w;
+    out->cb = g.w;
+    out->n = g.z;
     return true;
 }
 
 __device__ void run_chunk(Warp &w, const Claim &cl) {
     WrRec *rec = cl.rec;
     const uint64_t total = ld_vol(&rec->total);
-    const uint64_t off = uint64_t(cl.chunk) * cl.cb;
+    const uint64_t off = cl.off;
     uint64_t len = total - off;
     if (len > cl.cb) len = cl.cb;
     const uint32_t op = ld_vol32(&rec->opcode);
@@ -480,8 +527,8 @@ __device__ void run_chunk(Warp &w, const Claim &cl) {
         // Device-scope release is enough here: the owner warp acquires chunks_done and issues
         // the system-scope fence before it publishes the CQE, and causality is transitive.
         __threadfence();
-        const uint32_t done = atomicAdd(&rec->chunks_done, 1u) + 1;
-        if (done == cl.n) atomicAdd(&cl.job->seq, 1ull);  // every chunk done: free the slot
+        atomicAdd(&rec->chunks_done, 1u);
+        if (atomicAdd(&cl.job->done, 1u) + 1 == cl.n) atomicAdd(&cl.job->seq, 1ull);  // free the slot
     }
     w.n_chunks += 1;
     w.bytes += len;
@@ -767,11 +814,23 @@ __device__ int retire(Warp &w, DevQp *qp, const QpView &v, queue::Cqe *cqe_buf) 
     return retire_commit(w, qp, v, cqe_buf, head, p, err_mask, wr_id, status, op, signaled, total);
 }
 
-// Small-WR fast path: lane j validates and executes WQE j of the staged batch (single-SGE
-// WRITE / READ of at most kLaneBytes), so a batch of tiny WRs costs one round of parallel loads
-// and one of copies instead of one round trip per WR.  Processes the longest prefix of such WQEs
-// and returns its length (an erroring WQE ends the prefix and is included; nothing after it runs).
+// Lane-parallel issue: lane j validates WQE j of the staged batch (single-SGE WRITE / READ of
+// any size), so a batch costs one round of parallel loads instead of one round trip per WR.
+// Payloads of at most kLaneBytes are copied by their lane on the spot; larger ones become one
+// chunked job for the whole batch (chunks numbered across its WRs), which every warp of the GPU
+// may claim.  Processes the longest prefix of such WQEs and returns its length (an erroring WQE
+// ends the prefix and is included; nothing after it runs).  *chunked_out tells whether any WR
+// of the prefix went to a job (then it completes later, through retire()).
 constexpr uint32_t kLaneBytes = 64;
+
+// Chunk size for a job whose largest WR is `max_len`: about half the warps get a chunk of a
+// lone WR, within [kChunkMin, kChunkMax], so claims stay rare next to the copies.
+__device__ __forceinline__ uint32_t chunk_for(uint64_t max_len, uint32_t nwarps) {
+    const uint64_t cb = max_len / (nwarps / 2 + 1);
+    uint32_t chunk = kChunkMin;
+    while (chunk < cb && chunk < kChunkMax) chunk <<= 1;
+    return chunk;
+}
 
 struct LaneWr {
     uint64_t wr_id, total;
@@ -779,7 +838,9 @@ struct LaneWr {
 };
 
 __device__ uint32_t issue_fast(Warp &w, DevQp *qp, const QpView &v, const uint8_t *wqe_smem, uint64_t issue0,
-                               uint32_t avail, LaneWr *out) {
+                               uint32_t avail, LaneWr *out, JobRing *jr, uint32_t *bitmap, uint32_t nwarps,
+                               bool *chunked_out) {
+    *chunked_out = false;
     const uint32_t j = uint32_t(w.lane);
     const bool in = j < avail;
     const queue::SendWqe *h = reinterpret_cast<const queue::SendWqe *>(wqe_smem + (in ? j : 0) * v.sq_stride);
@@ -787,7 +848,7 @@ __device__ uint32_t issue_fast(Warp &w, DevQp *qp, const QpView &v, const uint8_
                                                                 queue::kSendSgeOffset);
     const uint32_t op = h->opcode;
     const bool fast = in && (op == UGDR_WR_RDMA_WRITE || op == UGDR_WR_RDMA_READ) && h->sge_count == 1 &&
-                      sg->length <= kLaneBytes && v.max_sge >= 1;
+                      sg->length <= 0x80000000u && v.max_sge >= 1;
     const uint32_t fast_mask = __ballot_sync(0xffffffffu, fast);
     const uint32_t p = __ffs(~fast_mask) - 1;
     if (p == 0) return 0;
@@ -873,9 +934,42 @@ __device__ uint32_t issue_fast(Warp &w, DevQp *qp, const QpView &v, const uint8_
         }
     }
     const uint32_t err_mask = __ballot_sync(0xffffffffu, act && status != UGDR_WC_SUCCESS);
-    const uint32_t count = err_mask ? __ffs(err_mask) : p;  // through the first error, inclusive
+    uint32_t count = err_mask ? __ffs(err_mask) : p;  // through the first error, inclusive
+    // --- chunked WRs: one job for the batch; its slot is taken before anything runs ---
+    bool chunked = j < count && status == UGDR_WC_SUCCESS && len > kLaneBytes;
+    uint32_t chunk_mask = __ballot_sync(0xffffffffu, chunked);
+    int slot = -1;
+    unsigned long long gen = 0;
+    uint32_t cb = 0;
+    if (chunk_mask) {
+        if (w.lane == 0) slot = take_job_slot(jr, w.gwarp + uint32_t(issue0), &gen);
+        slot = bcast(slot);
+        if (slot < 0) {
+            // No free slot: only the WRs before the first chunked one run now.
+            count = __ffs(chunk_mask) - 1;
+            chunk_mask = 0;
+            chunked = false;
+            if (count == 0) return 0;
+        } else {
+            gen = bcast64(gen);
+            uint64_t mx = chunked ? len : 0;
+            for (int o = 16; o > 0; o >>= 1) {
+                const uint64_t t = __shfl_xor_sync(0xffffffffu, mx, o);
+                mx = t > mx ? t : mx;
+            }
+            cb = chunk_for(mx, nwarps);
+        }
+    }
+    const uint32_t nch = chunked ? uint32_t((len + cb - 1) / cb) : 0u;
+    uint32_t start = nch;  // inclusive scan, then made exclusive
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, start, o);
+        if (w.lane >= o) start += t;
+    }
+    const uint32_t total_chunks = __shfl_sync(0xffffffffu, start, 31);
+    start -= nch;
     // --- execute (lanes before the first error only) ---
-    if (j < count && status == UGDR_WC_SUCCESS && len != 0) {
+    if (j < count && !chunked && status == UGDR_WC_SUCCESS && len != 0) {
         uint8_t *dst = reinterpret_cast<uint8_t *>(op == UGDR_WR_RDMA_READ ? local : remote);
         const uint8_t *src = reinterpret_cast<const uint8_t *>(op == UGDR_WR_RDMA_READ ? remote : local);
         if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src) | len) & 7) == 0) {
@@ -898,12 +992,16 @@ __device__ uint32_t issue_fast(Warp &w, DevQp *qp, const QpView &v, const uint8_
         rec->seg[0].length = len;
         rec->recv_cqe_done = 0;
         rec->chunks_done = 0;
-        rec->nchunks = 0;
+        rec->nchunks = nch;
         rec->signaled = (v.sig_all || (h->send_flags & UGDR_SEND_SIGNALED) != 0) ? 1u : 0u;
-        w.bytes += len;
+        if (!chunked) w.bytes += len;
         *out = LaneWr{h->wr_id, len, status, op, rec->signaled};
     }
     __syncwarp();
+    if (chunk_mask) {
+        publish_job(w, jr, bitmap, slot, gen, qp->st.win, uint32_t(issue0 % kWindow), count, start, total_chunks, cb);
+        *chunked_out = true;
+    }
     return count;
 }
 
@@ -1044,7 +1142,8 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
     uint32_t inline_ran = 0;
     const uint64_t t_fetch1 = gtime();
     LaneWr lw{0, 0, 0, 0, 0};
-    uint64_t issued = issue_fast(w, qp, v, wqe_smem, issue0, uint32_t(avail), &lw);
+    bool fast_chunked = false;
+    uint64_t issued = issue_fast(w, qp, v, wqe_smem, issue0, uint32_t(avail), &lw, jr, bitmap, nwarps, &fast_chunked);
     const uint32_t fast_n = uint32_t(issued);
     if (issued > 0) {
         inline_ran += uint32_t(issued);
@@ -1116,21 +1215,19 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
                 run_inline(w, rec, wqe, op, total, remote);
                 ++inline_ran;
             } else {
-                // Chunk so one WR spreads over about half the warps, within [16 KiB, 256 KiB]:
-                // large enough that claims are rare next to the copy, small enough that a lone
-                // WR still reaches most SMs.
-                const uint64_t cb = total / (nwarps / 2 + 1);
-                uint32_t chunk = kChunkMin;
-                while (chunk < cb && chunk < kChunkMax) chunk <<= 1;
+                const uint32_t chunk = chunk_for(total, nwarps);
                 const uint32_t n = uint32_t((total + chunk - 1) / chunk);
-                bool pub = false;
+                int slot = -1;
+                unsigned long long gen = 0;
                 if (w.lane == 0) {
-                    rec->nchunks = n;
-                    __threadfence();
-                    pub = publish_job(jr, bitmap, rec, n, chunk, w.gwarp + uint32_t(issue));
-                    if (!pub) rec->nchunks = 0;
+                    slot = take_job_slot(jr, w.gwarp + uint32_t(issue), &gen);
+                    rec->nchunks = slot >= 0 ? n : 0u;
                 }
-                ok = bcast(pub ? 1 : 0) != 0;
+                slot = bcast(slot);
+                gen = bcast64(gen);
+                if (slot >= 0)
+                    publish_job(w, jr, bitmap, slot, gen, qp->st.win, uint32_t(issue % kWindow), 1u, 0u, n, chunk);
+                ok = slot >= 0;
             }
         }
         if (!ok) break;  // no job slot: retry on a later pass
@@ -1148,7 +1245,7 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
         w.vissue = issue0 + issued;
         w.n_inline += inline_ran;
         work += uint32_t(issued);
-        if (head == issue0 && issued == fast_n) {
+        if (head == issue0 && issued == fast_n && !fast_chunked) {
             // Only this fast batch is in flight and every lane still holds its WR: retire it
             // without reading anything back.
             const uint32_t err_mask = __ballot_sync(0xffffffffu, uint32_t(w.lane) < fast_n && lw.status != 0);
@@ -1201,6 +1298,7 @@ __global__ void __launch_bounds__(kThreads, 1) executor_kernel(ExecParams p) {
     w.cq.cq = nullptr;
     w.vq = nullptr;
     w.mrc = mr_cache[w.wi];
+    w.mirror = s_bits;
     if (w.lane < 2) w.mrc[w.lane].key = 0;
     const uint32_t nwarps = gridDim.x * kWarps;
     JobRing *jr = p.jobs;

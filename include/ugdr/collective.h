@@ -17,7 +17,10 @@ extern "C" {
 #define UGDR_X_MAX_RANKS 8
 #define UGDR_X_IPC_HANDLE_BYTES 64
 
-/* Layout identical to the kernels' peer set. */
+/* Layout identical to the kernels' peer set.  signal[q] is rank q's signal buffer (mapped here):
+ * UGDR_X_SIGNAL_SLOTS x UGDR_X_MAX_RANKS zero-initialised uint64 words; arrive points at
+ * UGDR_X_SIGNAL_SLOTS zero-initialised counters of this rank; status at one word of this rank. */
+#define UGDR_X_SIGNAL_SLOTS 8
 typedef struct ugdr_x_peerset {
     void *buf[UGDR_X_MAX_RANKS];
     uint64_t *signal[UGDR_X_MAX_RANKS];

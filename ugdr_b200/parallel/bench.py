@@ -152,6 +152,8 @@ def main():
     ap.add_argument("--op", default="all", choices=["all", "allreduce", "moe"])
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--ar-mib", type=int, default=1024, help="allreduce bytes per rank, MiB")
+    ap.add_argument("--tokens", type=int, default=MoEConfig().tokens, help="MoE tokens per rank")
     args = ap.parse_args()
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -160,9 +162,9 @@ def main():
     _GLOO = dist.new_group(backend="gloo")
     results = []
     if args.op in ("all", "allreduce"):
-        results.append(bench_allreduce(rank, world, args.iters, args.warmup))
+        results.append(bench_allreduce(rank, world, args.iters, args.warmup, args.ar_mib << 20))
     if args.op in ("all", "moe"):
-        results.append(bench_moe(rank, world, args.iters, args.warmup, MoEConfig()))
+        results.append(bench_moe(rank, world, args.iters, args.warmup, MoEConfig(tokens=args.tokens)))
     if rank == 0:
         for r in results:
             print(json.dumps(r), flush=True)

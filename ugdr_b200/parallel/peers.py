@@ -14,7 +14,7 @@ import torch
 from .. import _native as N
 
 MAX_RANKS = 8
-SLOTS = 8  # signal slots: 0 reduce-scatter, 1 all-gather, 2 dispatch, 3 combine, 4 counts
+SLOTS = 8  # signal slots: 0 allreduce end, 2 dispatch, 3 combine, 4 counts, 5 allreduce entry
 
 
 class PeerSet(C.Structure):
