@@ -18,7 +18,8 @@ LIB_CXX := \
   csrc/control/rpc.cpp csrc/control/service.cpp csrc/control/client.cpp \
   csrc/api/posting.cpp csrc/api/runtime.cpp csrc/api/memory_export.cpp \
   csrc/engine/cpu_engine.cpp csrc/gpu/cuda_memory.cpp csrc/gpu/gpu_engine.cpp csrc/gpu/diag.cpp \
-  csrc/daemon/daemon.cpp csrc/collective/api.cpp
+  csrc/gpu/visibility.cpp \
+  csrc/daemon/daemon.cpp csrc/collective/api.cpp csrc/collective/nvls.cpp
 LIB_CU  := csrc/gpu/executor.cu csrc/collective/kernels.cu csrc/collective/route_noalloc.cu
 
 LIB_OBJS := $(LIB_CXX:csrc/%.cpp=$(OBJ)/%.o) $(LIB_CU:csrc/%.cu=$(OBJ)/%.cu.o)

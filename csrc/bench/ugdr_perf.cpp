@@ -4,6 +4,12 @@
 //   ugdr_perf latency  --src-gpu A --dst-gpu B --bytes N --iters K        QD1 post_send -> poll_cq
 //   ugdr_perf bw       --src-gpu A --dst-gpu B --op write|read --min 8 --max 1G --qd 64 --bytes-per-size T
 //   ugdr_perf posting  --batch B --wrs N                                    post_send into the SQ ring
+//   ugdr_perf stress   --src-gpu A --dst-gpu B --qps 64 --depth 128 --sges 16 --rounds R
+//                      verbs-feature stress: per QP an interleave of
+//                      16-SGE WRITE and WRITE_WITH_IMM (SGE sizes log-uniform in 64 B..64 KiB,
+//                      gathered into a contiguous remote range), FETCH_ADD and CMP_AND_SWP on a
+//                      4096-entry uint64 counter array; checks every byte, immediate, and
+//                      atomic result; reports posting and completion rates.
 //
 // Output: one key=value line per measurement (reference style, benchmarks/*.cpp) and a JSON
 // line with the same fields.  Payload: uniform uint8 from a seed; every size's destination is
@@ -13,6 +19,7 @@
 #include <cuda_runtime_api.h>
 
 #include <algorithm>
+#include <cmath>
 #include <chrono>
 #include <cstdio>
 #include <cstdlib>
@@ -33,6 +40,7 @@ struct Opts {
     std::string op = "write";
     uint64_t min_bytes = 8, max_bytes = 1ull << 30, qd = 64, bytes_per_size = 8ull << 30;
     uint64_t batch = 32, wrs = 4000000;
+    uint64_t qps = 64, depth = 128, sges = 16, rounds = 3, seed = 7;
 };
 
 [[noreturn]] void die(const char *what, int rc) {
@@ -313,6 +321,259 @@ int run_posting(const Opts &o) {
     return 0;
 }
 
+
+// ---- verbs-feature stress ------------------------------------------------------------------------
+
+constexpr uint64_t kCounters = 4096;
+constexpr uint64_t kFaaCounters = 2048;  // [0, 2048): fetch-add from every QP
+                                          // [2048, 4096): compare-swap chains, owned per QP
+
+struct StressSide {
+    ugdr_context *ctx = nullptr;
+    ugdr_pd *pd = nullptr;
+    ugdr_cq *cq = nullptr;
+};
+
+StressSide open_side(ugdr_device **list, int n, int gpu, int cqe) {
+    StressSide s;
+    s.ctx = ugdr_open_device(gpu_device(list, n, gpu));
+    if (!s.ctx) die("ugdr_open_device", errno);
+    s.pd = ugdr_alloc_pd(s.ctx);
+    s.cq = ugdr_create_cq(s.ctx, cqe, nullptr, nullptr, 0);
+    if (!s.pd || !s.cq) die("pd/cq", errno);
+    return s;
+}
+
+ugdr_mr *dev_mr(ugdr_pd *pd, int gpu, uint64_t bytes, int access, void **buf) {
+    cudaSetDevice(gpu);
+    if (cudaMalloc(buf, bytes) != cudaSuccess) die("cudaMalloc", ENOMEM);
+    cudaMemset(*buf, 0, bytes);
+    ugdr_mr *mr = ugdr_reg_mr(pd, *buf, bytes, access);
+    if (!mr) die("ugdr_reg_mr", errno);
+    return mr;
+}
+
+int run_stress(const Opts &o) {
+    const uint32_t nq = uint32_t(o.qps), depth = uint32_t(o.depth), nsge = uint32_t(o.sges);
+    if (nq == 0 || nq > 64 || depth == 0 || nsge == 0 || nsge > 32) die("stress options", EINVAL);
+    const uint64_t per_round = uint64_t(nq) * depth;
+    int n = 0;
+    ugdr_device **list = ugdr_get_device_list(&n);
+    if (!list) die("ugdr_get_device_list", errno);
+    StressSide rq = open_side(list, n, o.src_gpu, int(per_round + 64));
+    StressSide rs = open_side(list, n, o.dst_gpu, int(per_round + 64));
+    // Requester memory: gather source (seeded bytes) and atomic results.
+    const uint64_t src_bytes = 64ull << 20;
+    void *src = nullptr, *res = nullptr, *dst = nullptr, *ctr = nullptr;
+    ugdr_mr *src_mr = dev_mr(rq.pd, o.src_gpu, src_bytes, UGDR_ACCESS_LOCAL_WRITE, &src);
+    ugdr_mr *res_mr = dev_mr(rq.pd, o.src_gpu, per_round * 8, UGDR_ACCESS_LOCAL_WRITE, &res);
+    fill(src, src_bytes, o.seed, o.src_gpu);
+    std::vector<uint8_t> host_src(src_bytes);
+    cudaSetDevice(o.src_gpu);
+    cudaMemcpy(host_src.data(), src, src_bytes, cudaMemcpyDeviceToHost);
+    // Responder memory: gather destination (sized for the largest possible round) and counters.
+    const uint64_t dst_bytes = per_round * nsge * 65536ull / 2 + (1 << 20);
+    ugdr_mr *dst_mr = dev_mr(rs.pd, o.dst_gpu, dst_bytes, UGDR_ACCESS_LOCAL_WRITE | UGDR_ACCESS_REMOTE_WRITE, &dst);
+    ugdr_mr *ctr_mr = dev_mr(rs.pd, o.dst_gpu, kCounters * 8,
+                             UGDR_ACCESS_LOCAL_WRITE | UGDR_ACCESS_REMOTE_WRITE | UGDR_ACCESS_REMOTE_ATOMIC, &ctr);
+    // QP pairs.
+    std::vector<ugdr_qp *> req(nq), rsp(nq);
+    ugdr_qp_attr c{};
+    c.timeout = 14;
+    c.retry_cnt = 7;
+    c.rnr_retry = 7;
+    c.min_rnr_timer = 1;
+    const int cmask = UGDR_QP_TIMEOUT | UGDR_QP_RETRY_CNT | UGDR_QP_RNR_RETRY | UGDR_QP_MIN_RNR_TIMER;
+    for (uint32_t q = 0; q < nq; ++q) {
+        ugdr_qp_init_attr a{rq.cq, rq.cq, depth, 4, nsge, 1, UGDR_QPT_RC, 0};
+        ugdr_qp_init_attr b{rs.cq, rs.cq, 4, depth, 1, 1, UGDR_QPT_RC, 0};
+        req[q] = ugdr_create_qp(rq.pd, &a);
+        rsp[q] = ugdr_create_qp(rs.pd, &b);
+        if (!req[q] || !rsp[q]) die("ugdr_create_qp", errno);
+        ugdr_qp_attr at{};
+        at.qp_state = UGDR_QPS_INIT;
+        at.qp_access_flags = UGDR_ACCESS_REMOTE_WRITE | UGDR_ACCESS_REMOTE_ATOMIC;
+        if (int rc = ugdr_modify_qp(req[q], &at, UGDR_QP_STATE | UGDR_QP_ACCESS_FLAGS)) die("modify", rc);
+        if (int rc = ugdr_modify_qp(rsp[q], &at, UGDR_QP_STATE | UGDR_QP_ACCESS_FLAGS)) die("modify", rc);
+        ugdr_qp_conn_info ia{}, ib{};
+        ugdr_query_qp_conn_info(req[q], &ia);
+        ugdr_query_qp_conn_info(rsp[q], &ib);
+        if (int rc = ugdr_connect_qp(req[q], &ib, &c, cmask)) die("connect", rc);
+        if (int rc = ugdr_connect_qp(rsp[q], &ia, &c, cmask)) die("connect", rc);
+    }
+
+    std::mt19937_64 rng(o.seed * 1000003ull + 17);
+    auto log_uniform = [&](uint64_t lo, uint64_t hi) {
+        const double u = std::uniform_real_distribution<double>(std::log(double(lo)), std::log(double(hi) + 1))(rng);
+        return std::min<uint64_t>(hi, std::max<uint64_t>(lo, uint64_t(std::exp(u))));
+    };
+    std::vector<uint64_t> faa_expect(kCounters, 0), cas_seen(kCounters, 0);
+    bool ok = true;
+    uint64_t bad_bytes = 0, bad_imm = 0, bad_cas = 0, bad_wc = 0, total_wrs = 0, total_bytes = 0;
+    double post_s = 0, run_s = 0;
+    std::vector<ugdr_sge> sges(per_round * nsge);
+    std::vector<ugdr_send_wr> wrs(per_round);
+    std::vector<ugdr_recv_wr> rwrs(per_round);
+    std::vector<uint64_t> cas_expect(per_round, ~0ull);
+    std::vector<uint8_t> expect;
+    for (uint64_t round = 0; round < o.rounds; ++round) {
+        // ---- build the round ----
+        uint64_t dst_off = 0;
+        expect.clear();
+        struct Span { uint64_t dst, len; };
+        std::vector<Span> spans;
+        std::vector<uint64_t> imm_of(per_round, 0);
+        uint64_t nimm = 0;
+        for (uint32_t q = 0; q < nq; ++q) {
+            for (uint32_t i = 0; i < depth; ++i) {
+                const uint64_t w = uint64_t(q) * depth + i;
+                ugdr_send_wr &wr = wrs[w];
+                wr = ugdr_send_wr{};
+                wr.wr_id = (round << 40) | w;
+                wr.send_flags = UGDR_SEND_SIGNALED;
+                wr.next = i + 1 < depth ? &wrs[w + 1] : nullptr;
+                ugdr_sge *sg = &sges[w * nsge];
+                const uint32_t kind = (q + i) % 4;
+                if (kind <= 1) {  // 16-SGE gather: WRITE, or WRITE_WITH_IMM
+                    const uint64_t start = dst_off;
+                    for (uint32_t k = 0; k < nsge; ++k) {
+                        const uint64_t len = log_uniform(64, 65536);
+                        const uint64_t off = std::uniform_int_distribution<uint64_t>(0, src_bytes - len)(rng);
+                        sg[k] = ugdr_sge{reinterpret_cast<uint64_t>(src) + off, uint32_t(len), src_mr->lkey};
+                        expect.insert(expect.end(), host_src.begin() + off, host_src.begin() + off + len);
+                        dst_off += len;
+                    }
+                    spans.push_back({start, dst_off - start});
+                    dst_off = (dst_off + 63) & ~63ull;  // next WR's range starts on a fresh line
+                    expect.resize(dst_off, 0);
+                    wr.sg_list = sg;
+                    wr.num_sge = int(nsge);
+                    wr.opcode = kind == 0 ? UGDR_WR_RDMA_WRITE : UGDR_WR_RDMA_WRITE_WITH_IMM;
+                    wr.wr.rdma.remote_addr = reinterpret_cast<uint64_t>(dst) + start;
+                    wr.wr.rdma.rkey = dst_mr->rkey;
+                    if (kind == 1) {
+                        wr.imm_data = uint32_t(rng());
+                        imm_of[w] = wr.imm_data | (1ull << 32);
+                        ++nimm;
+                    }
+                    total_bytes += dst_off - start;
+                } else {
+                    sg[0] = ugdr_sge{reinterpret_cast<uint64_t>(res) + w * 8, 8, res_mr->lkey};
+                    wr.sg_list = sg;
+                    wr.num_sge = 1;
+                    uint64_t idx;
+                    if (kind == 2) {
+                        idx = rng() % kFaaCounters;
+                        const uint64_t add = 1 + rng() % 7;
+                        faa_expect[idx] += add;
+                        wr.opcode = UGDR_WR_ATOMIC_FETCH_AND_ADD;
+                        wr.wr.atomic.compare_add = add;
+                    } else {
+                        // QP q owns counters [2048 + 32 q, 2048 + 32 q + 32): its CAS chain on each
+                        // is in posting order, so every old value is known in advance.
+                        idx = kFaaCounters + (uint64_t(q) * 32 + rng() % 32) % (kCounters - kFaaCounters);
+                        wr.opcode = UGDR_WR_ATOMIC_CMP_AND_SWP;
+                        wr.wr.atomic.compare_add = cas_seen[idx];
+                        wr.wr.atomic.swap = cas_seen[idx] + 1;
+                        cas_expect[w] = cas_seen[idx];
+                        cas_seen[idx] += 1;
+                    }
+                    wr.wr.atomic.remote_addr = reinterpret_cast<uint64_t>(ctr) + idx * 8;
+                    wr.wr.atomic.rkey = ctr_mr->rkey;
+                }
+            }
+        }
+        if (dst_off > dst_bytes) die("stress destination too small", ENOMEM);
+        // Receive WRs for the immediates (no SGE: WRITE_WITH_IMM lands at its remote address).
+        for (uint32_t q = 0; q < nq; ++q) {
+            uint32_t k = 0;
+            for (uint32_t i = 0; i < depth; ++i)
+                if ((q + i) % 4 == 1) {
+                    ugdr_recv_wr &r = rwrs[uint64_t(q) * depth + k];
+                    r = ugdr_recv_wr{};
+                    r.wr_id = (round << 40) | (uint64_t(q) * depth + i);
+                    r.num_sge = 0;
+                    r.next = nullptr;
+                    if (k > 0) rwrs[uint64_t(q) * depth + k - 1].next = &r;
+                    ++k;
+                }
+            ugdr_recv_wr *bad = nullptr;
+            if (k > 0)
+                if (int rc = ugdr_post_recv(rsp[q], &rwrs[uint64_t(q) * depth], &bad)) die("ugdr_post_recv", rc);
+        }
+        cudaSetDevice(o.dst_gpu);
+        cudaMemset(dst, 0, dst_off);
+        cudaDeviceSynchronize();
+        // ---- post (timed: the posting rate) and complete (timed: the completion rate) ----
+        const auto t0 = Clock::now();
+        for (uint32_t q = 0; q < nq; ++q) {
+            ugdr_send_wr *bad = nullptr;
+            if (int rc = ugdr_post_send(req[q], &wrs[uint64_t(q) * depth], &bad)) die("ugdr_post_send", rc);
+        }
+        const auto t1 = Clock::now();
+        ugdr_wc wc[64];
+        uint64_t got = 0, got_recv = 0;
+        const auto deadline = t1 + std::chrono::seconds(120);
+        while (got < per_round || got_recv < nimm) {
+            int k = ugdr_poll_cq(rq.cq, 64, wc);
+            if (k < 0) die("ugdr_poll_cq", -k);
+            for (int j = 0; j < k; ++j) {
+                if (wc[j].status != UGDR_WC_SUCCESS) ++bad_wc;
+            }
+            got += uint64_t(k);
+            k = ugdr_poll_cq(rs.cq, 64, wc);
+            if (k < 0) die("ugdr_poll_cq", -k);
+            for (int j = 0; j < k; ++j) {
+                const uint64_t w = wc[j].wr_id & ((1ull << 40) - 1);
+                if (wc[j].status != UGDR_WC_SUCCESS || wc[j].opcode != UGDR_WC_RECV_RDMA_WITH_IMM ||
+                    !(wc[j].wc_flags & UGDR_WC_WITH_IMM) || w >= per_round || imm_of[w] != (wc[j].imm_data | (1ull << 32)))
+                    ++bad_imm;
+            }
+            got_recv += uint64_t(k);
+            if (Clock::now() > deadline) die("stress completion timeout", ETIMEDOUT);
+        }
+        const auto t2 = Clock::now();
+        post_s += std::chrono::duration<double>(t1 - t0).count();
+        run_s += std::chrono::duration<double>(t2 - t0).count();
+        total_wrs += per_round;
+        // Compare-swap results: each old value is the chain position known at build time.
+        std::vector<uint64_t> olds(per_round);
+        cudaSetDevice(o.src_gpu);
+        cudaMemcpy(olds.data(), res, per_round * 8, cudaMemcpyDeviceToHost);
+        for (uint64_t w = 0; w < per_round; ++w)
+            if (cas_expect[w] != ~0ull && olds[w] != cas_expect[w]) ++bad_cas;
+        std::fill(cas_expect.begin(), cas_expect.end(), ~0ull);
+        // ---- verify every gathered byte ----
+        std::vector<uint8_t> got_dst(dst_off);
+        cudaSetDevice(o.dst_gpu);
+        cudaMemcpy(got_dst.data(), dst, dst_off, cudaMemcpyDeviceToHost);
+        for (const Span &sp : spans)
+            if (std::memcmp(got_dst.data() + sp.dst, expect.data() + sp.dst, sp.len) != 0) bad_bytes += 1;
+    }
+    // Counters: fetch-add sums and compare-swap chain lengths.
+    std::vector<uint64_t> ctr_host(kCounters);
+    cudaSetDevice(o.dst_gpu);
+    cudaMemcpy(ctr_host.data(), ctr, kCounters * 8, cudaMemcpyDeviceToHost);
+    uint64_t bad_ctr = 0;
+    for (uint64_t i = 0; i < kCounters; ++i)
+        if (ctr_host[i] != (i < kFaaCounters ? faa_expect[i] : cas_seen[i])) ++bad_ctr;
+    ok = bad_bytes == 0 && bad_imm == 0 && bad_cas == 0 && bad_wc == 0 && bad_ctr == 0;
+    const double post_mops = double(total_wrs) / post_s / 1e6, run_mops = double(total_wrs) / run_s / 1e6;
+    std::printf("benchmark=ugdr_stress src_gpu=%d dst_gpu=%d qps=%u depth=%u sges=%u rounds=%llu wrs=%llu "
+                "post_MWR_per_s=%.3f complete_MWR_per_s=%.3f GB_per_s=%.3f bad_wrs=%llu bad_imm=%llu bad_cas=%llu "
+                "bad_counters=%llu bad_wc=%llu correct=%d\n",
+                o.src_gpu, o.dst_gpu, nq, depth, nsge, (unsigned long long)o.rounds, (unsigned long long)total_wrs,
+                post_mops, run_mops, double(total_bytes) / run_s / 1e9, (unsigned long long)bad_bytes,
+                (unsigned long long)bad_imm, (unsigned long long)bad_cas, (unsigned long long)bad_ctr,
+                (unsigned long long)bad_wc, int(ok));
+    std::printf("{\"benchmark\": \"ugdr_stress\", \"src_gpu\": %d, \"dst_gpu\": %d, \"qps\": %u, \"depth\": %u, "
+                "\"sges\": %u, \"wrs\": %llu, \"post_MWRps\": %.3f, \"complete_MWRps\": %.3f, \"GBps\": %.3f, "
+                "\"correct\": %s}\n",
+                o.src_gpu, o.dst_gpu, nq, depth, nsge, (unsigned long long)total_wrs, post_mops, run_mops,
+                double(total_bytes) / run_s / 1e9, ok ? "true" : "false");
+    return ok ? 0 : 2;
+}
+
 }  // namespace
 
 int main(int argc, char **argv) {
@@ -337,6 +598,11 @@ int main(int argc, char **argv) {
         else if (k == "--bytes-per-size") o.bytes_per_size = parse_size(v);
         else if (k == "--batch") o.batch = parse_size(v);
         else if (k == "--wrs") o.wrs = parse_size(v);
+        else if (k == "--qps") o.qps = parse_size(v);
+        else if (k == "--depth") o.depth = parse_size(v);
+        else if (k == "--sges") o.sges = parse_size(v);
+        else if (k == "--rounds") o.rounds = parse_size(v);
+        else if (k == "--seed") o.seed = parse_size(v);
         else {
             std::fprintf(stderr, "ugdr_perf: unknown option %s\n", k.c_str());
             return 2;
@@ -345,6 +611,7 @@ int main(int argc, char **argv) {
     if (o.mode == "latency") return run_latency(o);
     if (o.mode == "bw") return run_bw(o);
     if (o.mode == "posting") return run_posting(o);
+    if (o.mode == "stress") return run_stress(o);
     std::fprintf(stderr, "ugdr_perf: unknown mode %s\n", o.mode.c_str());
     return 2;
 }

@@ -5,12 +5,14 @@
 #include <cuda.h>
 #include <cuda_runtime_api.h>
 
+#include <atomic>
 #include <cstring>
 
 namespace {
 
 static_assert(sizeof(ugdr_x_peerset) == sizeof(ugdr::coll::PeerSet), "peer set layout");
-constexpr uint64_t kMaxWaitNs = 5ull * 1000 * 1000 * 1000;
+// Bound on every cross-GPU wait inside the collective kernels (ugdr_x_set_collective_wait_ns).
+std::atomic<uint64_t> g_wait_ns{5ull * 1000 * 1000 * 1000};
 
 const ugdr::coll::PeerSet &as_ps(const ugdr_x_peerset *p) {
     return *reinterpret_cast<const ugdr::coll::PeerSet *>(p);
@@ -27,6 +29,10 @@ using GetRangeFn = CUresult (*)(CUdeviceptr *, size_t *, CUdeviceptr);
 }  // namespace
 
 extern "C" {
+
+uint64_t ugdr_x_set_collective_wait_ns(uint64_t ns) {
+    return g_wait_ns.exchange(ns == 0 ? 5ull * 1000 * 1000 * 1000 : ns);
+}
 
 int ugdr_x_ipc_export(void *ptr, uint8_t handle[UGDR_X_IPC_HANDLE_BYTES], uint64_t *offset) {
     static GetRangeFn range = [] {
@@ -64,7 +70,17 @@ int ugdr_x_allreduce_bf16(const ugdr_x_peerset *ps, uint64_t offset, uint64_t co
                           void *stream) {
     if (ps == nullptr || ps->n < 1 || ps->n > UGDR_X_MAX_RANKS) return int(cudaErrorInvalidValue);
     return ugdr::coll::launch_allreduce_bf16(as_ps(ps), offset, count, epoch, ctas > 0 ? ctas : default_ctas(),
-                                             kMaxWaitNs, static_cast<cudaStream_t>(stream));
+                                             g_wait_ns.load(std::memory_order_relaxed), static_cast<cudaStream_t>(stream));
+}
+
+int ugdr_x_allreduce_bf16_nvls(const ugdr_x_peerset *ps, const ugdr_x_nvls *h, uint64_t offset, uint64_t count,
+                               uint64_t epoch, int ctas, void *stream) {
+    if (ps == nullptr || h == nullptr || ps->n < 1 || ps->n > UGDR_X_MAX_RANKS || h->mc == nullptr ||
+        offset + count * 2 > h->bytes)
+        return int(cudaErrorInvalidValue);
+    return ugdr::coll::launch_allreduce_bf16_nvls(as_ps(ps), h->mc, offset, count, epoch,
+                                                  ctas > 0 ? ctas : default_ctas(), g_wait_ns.load(std::memory_order_relaxed),
+                                                  static_cast<cudaStream_t>(stream));
 }
 
 size_t ugdr_x_moe_route_scratch_bytes(uint64_t rows, int nexp) {
@@ -87,7 +103,7 @@ int ugdr_x_moe_layout(const ugdr_x_peerset *ps, const int32_t *counts, int nexp,
     if (ps == nullptr || nexp <= 0 || experts_per_rank <= 0 || table_offset % 4 != 0)
         return int(cudaErrorInvalidValue);
     return ugdr::coll::launch_layout(as_ps(ps), counts, nexp, experts_per_rank, table_offset, group_base,
-                                     recv_used, epoch, kMaxWaitNs, static_cast<cudaStream_t>(stream));
+                                     recv_used, epoch, g_wait_ns.load(std::memory_order_relaxed), static_cast<cudaStream_t>(stream));
 }
 
 int ugdr_x_moe_dispatch(const ugdr_x_peerset *ps, const void *x, uint64_t row_bytes, const int32_t *expert_ids,
@@ -97,7 +113,7 @@ int ugdr_x_moe_dispatch(const ugdr_x_peerset *ps, const void *x, uint64_t row_by
     if (ps == nullptr || topk <= 0 || experts_per_rank <= 0) return int(cudaErrorInvalidValue);
     return ugdr::coll::launch_dispatch(as_ps(ps), x, row_bytes, expert_ids, positions, group_base, tokens, topk,
                                        experts_per_rank, recv_offset, recv_rows, epoch,
-                                       ctas > 0 ? ctas : default_ctas(), kMaxWaitNs,
+                                       ctas > 0 ? ctas : default_ctas(), g_wait_ns.load(std::memory_order_relaxed),
                                        static_cast<cudaStream_t>(stream));
 }
 
@@ -108,7 +124,7 @@ int ugdr_x_moe_combine(const ugdr_x_peerset *ps, void *out, uint64_t row_bytes, 
     if (ps == nullptr || topk <= 0 || experts_per_rank <= 0) return int(cudaErrorInvalidValue);
     return ugdr::coll::launch_combine(as_ps(ps), out, row_bytes, expert_ids, positions, group_base, weights,
                                       tokens, topk, experts_per_rank, recv_offset, recv_rows, epoch,
-                                      ctas > 0 ? ctas : default_ctas(), kMaxWaitNs,
+                                      ctas > 0 ? ctas : default_ctas(), g_wait_ns.load(std::memory_order_relaxed),
                                       static_cast<cudaStream_t>(stream));
 }
 

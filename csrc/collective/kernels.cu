@@ -172,6 +172,48 @@ __global__ void __launch_bounds__(512) allreduce_kernel(PeerSet ps, uint64_t bas
     end_barrier(ps, epoch, kSlotArEnd, max_ns);
 }
 
+// NVLS allreduce: rank r owns shard r; for each 16-byte vector of it, one multimem.ld_reduce
+// through the multicast view has the NVSwitch read the vector from every GPU and return the
+// fp32-accumulated bf16 sum, and one multimem.st writes the sum to every GPU.  Per GPU about
+// (1 + 1/N) of the buffer crosses each link direction instead of 2 (N - 1) / N.  Peer data is
+// read only through the multicast alias, so a proxy fence after the entry handshake orders the
+// peers' unicast writes of their inputs before the reads, and one before the exit barrier orders
+// the multicast stores before the peers' unicast reads of the result.
+__device__ __forceinline__ uint4 mm_ld_add_bf16x8(const uint8_t *p) {
+    uint4 v;
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ void mm_st_bf16x8(uint8_t *p, uint4 v) {
+    asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
+                 "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+__global__ void __launch_bounds__(512) allreduce_nvls_kernel(PeerSet ps, uint8_t *mc, uint64_t nvec, uint64_t epoch,
+                                                             uint64_t max_ns) {
+    entry_barrier(ps, epoch, kSlotArEntry, max_ns);
+    asm volatile("fence.proxy.alias;" ::: "memory");
+    const uint64_t per = (nvec + ps.n - 1) / ps.n;
+    const uint64_t begin = min(nvec, per * ps.rank), end = min(nvec, begin + per);
+    const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
+    constexpr int U = 4;
+    for (uint64_t i = begin + blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < end; i += U * stride) {
+        uint4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (i + u * stride < end) v[u] = mm_ld_add_bf16x8(mc + (i + u * stride) * 16);
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (i + u * stride < end) mm_st_bf16x8(mc + (i + u * stride) * 16, v[u]);
+    }
+    asm volatile("fence.proxy.alias;" ::: "memory");
+    end_barrier(ps, epoch, kSlotArEnd, max_ns);
+}
+
 // ---- MoE routing (counting sort) ---------------------------------------------------------------
 
 // K1: per-block expert histogram of rows [b * R, (b + 1) * R).
@@ -423,6 +465,13 @@ int launch_allreduce_bf16(const PeerSet &ps, uint64_t offset, uint64_t count, ui
     case 7: allreduce_kernel<7><<<ctas, 512, 0, s>>>(ps, offset, nvec, epoch, max_ns); break;
     default: allreduce_kernel<8><<<ctas, 512, 0, s>>>(ps, offset, nvec, epoch, max_ns); break;
     }
+    return int(cudaGetLastError());
+}
+
+int launch_allreduce_bf16_nvls(const PeerSet &ps, void *mc, uint64_t offset, uint64_t count, uint64_t epoch,
+                               int ctas, uint64_t max_ns, cudaStream_t s) {
+    if (mc == nullptr || count % 8 != 0 || offset % 16 != 0) return int(cudaErrorInvalidValue);
+    allreduce_nvls_kernel<<<ctas, 512, 0, s>>>(ps, static_cast<uint8_t *>(mc) + offset, count / 8, epoch, max_ns);
     return int(cudaGetLastError());
 }
 

@@ -28,6 +28,8 @@ struct PeerSet {
 int grid_for(int device);
 int launch_allreduce_bf16(const PeerSet &ps, uint64_t offset, uint64_t count, uint64_t epoch, int ctas,
                           uint64_t max_ns, cudaStream_t s);
+int launch_allreduce_bf16_nvls(const PeerSet &ps, void *mc, uint64_t offset, uint64_t count, uint64_t epoch,
+                               int ctas, uint64_t max_ns, cudaStream_t s);
 size_t route_scratch_bytes(uint64_t rows, int nexp);
 int launch_route(const int32_t *idx, uint64_t rows, int nexp, int32_t *counts, int32_t *pos, uint32_t *scratch,
                  cudaStream_t s);

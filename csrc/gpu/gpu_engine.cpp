@@ -3,6 +3,7 @@
 #include "control/service.hpp"
 #include "gpu/device_abi.hpp"
 #include "gpu/executor.hpp"
+#include "gpu/visibility.hpp"
 #include "ugdr/api.hpp"
 
 #include <cuda_runtime_api.h>
@@ -104,6 +105,8 @@ class GpuEngine final : public control::Engine {
     uint64_t launches_ = 0;
     std::atomic<bool> stop_monitor_{false};
     std::thread monitor_;
+    CudaVisibilitySource vis_src_;
+    VisibilityGate vis_{vis_src_};
 };
 
 GpuEngine::~GpuEngine() {
@@ -147,6 +150,9 @@ int GpuEngine::init() {
     cudaMemsetAsync(jobs_, 0, job_ring_bytes(), ctl_stream_);
     cudaMemsetAsync(stats_, 0, sizeof(DevStats), ctl_stream_);
     if (!ok(cudaStreamSynchronize(ctl_stream_))) return ENODEV;
+    // Third-party (GPUDirect RDMA) writes into this GPU's MRs are visible to the executor in
+    // order only with owner ordering; otherwise every launch is preceded by a host flush.
+    vis_.init(cfg_.ordinal);
     monitor_ = std::thread([this] { monitor(); });
     return 0;
 }
@@ -426,6 +432,7 @@ int GpuEngine::launch_locked(uint32_t mode, uint64_t expected, bool timed) {
     p.expected = expected;
     p.idle_exit_ns = uint64_t(cfg_.idle_exit_us) * 1000ull;
     p.max_wait_ns = uint64_t(cfg_.max_wait_ms) * 1000000ull;
+    if (vis_.mode() == VisibilityGate::Mode::kFlush && vis_.before_publish() != 0) return EIO;
     if (timed) cudaEventRecord(ev_start_, exec_stream_);
     const int rc = launch_executor(p, cfg_.ctas, exec_stream_);
     if (rc != 0) {

@@ -30,6 +30,10 @@ typedef struct ugdr_x_peerset {
     int rank;
 } ugdr_x_peerset;
 
+/* Bound (ns) on every cross-GPU wait of the collective kernels launched after the call; 0
+ * restores the default (5 s).  Returns the previous bound. */
+uint64_t ugdr_x_set_collective_wait_ns(uint64_t ns);
+
 /* Export the allocation holding `ptr` (cudaMalloc memory) for another process: the handle of
  * the allocation base and the offset of `ptr` inside it. */
 int ugdr_x_ipc_export(void *ptr, uint8_t handle[UGDR_X_IPC_HANDLE_BYTES], uint64_t *offset);
@@ -41,6 +45,36 @@ int ugdr_x_ipc_close(void *base);
  * multiple of 8, offset a multiple of 16).  `epoch` increases by one per call on every rank. */
 int ugdr_x_allreduce_bf16(const ugdr_x_peerset *ps, uint64_t offset, uint64_t count, uint64_t epoch,
                           int ctas, void *stream);
+
+/* NVLink SHARP (NVLS) multicast memory.  Every rank's GPU binds `bytes` of its own memory to one
+ * multicast object; `uc` is this GPU's memory (ordinary access), `mc` the multicast view that
+ * only multimem instructions use.  Set-up order across the ranks:
+ *   rank 0: ugdr_x_nvls_create (gives a POSIX fd to pass to the others over a Unix socket);
+ *   others: ugdr_x_nvls_import(fd);
+ *   every rank: ugdr_x_nvls_add_device; then, once every rank has added its GPU, ugdr_x_nvls_bind.
+ * Sizes are rounded up to the multicast granularity (h->bytes).  All calls act on the current
+ * CUDA device and return 0 or a CUDA error value. */
+typedef struct ugdr_x_nvls {
+    uint64_t mc_handle;  /* multicast object (driver allocation handle) */
+    uint64_t mem_handle; /* this GPU's memory bound to it */
+    void *uc;            /* this GPU's memory, unicast mapping */
+    void *mc;            /* multicast mapping of the same bytes */
+    uint64_t bytes;
+    int device;
+} ugdr_x_nvls;
+int ugdr_x_nvls_supported(int device);
+int ugdr_x_nvls_create(int ndev, uint64_t bytes, ugdr_x_nvls *h, int *fd);
+int ugdr_x_nvls_import(int fd, int ndev, uint64_t bytes, ugdr_x_nvls *h);
+int ugdr_x_nvls_add_device(ugdr_x_nvls *h);
+int ugdr_x_nvls_bind(ugdr_x_nvls *h);
+int ugdr_x_nvls_release(ugdr_x_nvls *h);
+
+/* In-place allreduce of `count` bf16 elements at byte `offset` of the NVLS memory `h` (count a
+ * multiple of 8, offset a multiple of 16): rank r reduces shard r in the switch
+ * (multimem.ld_reduce, fp32 accumulation) and stores the sum to every GPU (multimem.st).  `ps`
+ * supplies the entry / exit signals (its buffers are not touched). */
+int ugdr_x_allreduce_bf16_nvls(const ugdr_x_peerset *ps, const ugdr_x_nvls *h, uint64_t offset, uint64_t count,
+                               uint64_t epoch, int ctas, void *stream);
 
 /* MoE routing: rows = tokens * topk expert ids (int32, row r = token r / topk).  Writes the row
  * count of every expert and each row's position inside its expert group, in row order (rows

@@ -59,6 +59,47 @@ def test_allreduce_single_rank_is_identity(one_gpu):
     assert torch.equal(x, ref)
 
 
+def test_missing_peer_times_out_with_status(one_gpu):
+    """A bounded cross-GPU wait that runs out: a 2-rank peer set in one process whose "peer"
+    buffers are local allocations that nothing signals.  The allreduce's waits give up after the
+    configured bound, the kernel reports status 1 and returns, and the GPU stays usable."""
+    import ctypes as C
+    import time
+
+    from ugdr_b200.parallel.collectives import allreduce_bf16
+    from ugdr_b200.parallel.peers import MAX_RANKS, SLOTS, lib
+
+    L = lib()
+    L.ugdr_x_set_collective_wait_ns.restype = C.c_uint64
+    L.ugdr_x_set_collective_wait_ns.argtypes = [C.c_uint64]
+    g = _single_rank_group(1 << 20)
+    fake_buf = torch.zeros(1 << 20, dtype=torch.uint8, device="cuda")
+    fake_sig = torch.zeros(SLOTS * MAX_RANKS, dtype=torch.int64, device="cuda")
+    g.ps.n = 2
+    g.ps.buf[1] = fake_buf.data_ptr()
+    g.ps.signal[1] = fake_sig.data_ptr()
+    old = L.ugdr_x_set_collective_wait_ns(2_000_000)  # 2 ms
+    try:
+        torch.cuda.synchronize()
+        t0 = time.monotonic()
+        allreduce_bf16(g, 1 << 19)
+        torch.cuda.synchronize()
+        elapsed = time.monotonic() - t0
+    finally:
+        L.ugdr_x_set_collective_wait_ns(old)
+    assert int(g.status.item()) == 1
+    assert elapsed < 2.0
+    # The context is intact: an ordinary single-rank call still works.
+    g.status.zero_()
+    g.ps.n = 1
+    x = g.view(torch.bfloat16, 1024)
+    x.fill_(1.5)
+    allreduce_bf16(g, 1024)
+    torch.cuda.synchronize()
+    g.check_status()
+    assert torch.all(x == 1.5)
+
+
 def test_moe_all_to_all_single_rank(one_gpu):
     from ugdr_b200.models.moe import route
     from ugdr_b200.parallel.collectives import MoEAllToAll
@@ -115,6 +156,31 @@ def _worker(rank, world, port, q):
             ref = sum(x.float() for x in xs)
             err = (v.float().cpu() - ref).abs().max().item()
             assert err <= 0.05 * (1 + ref.abs().max().item()) / 8, f"allreduce error {err}"
+        # The same through NVLS multicast memory (reduction inside the NVSwitch), when available.
+        from ugdr_b200.parallel import nvls
+
+        if nvls.supported():
+            sig = PeerGroup(4096, rank, world, exchange)
+            buf = nvls.NvlsBuffer(n * 2, rank, world, exchange)
+            errs = []
+            try:
+                for it in range(3):
+                    xs = [torch.randn(n, generator=torch.Generator().manual_seed(500 + 100 * it + r)).to(
+                        torch.bfloat16) for r in range(world)]
+                    v = buf.view(torch.bfloat16, n)
+                    v.copy_(xs[rank].cuda())
+                    torch.cuda.synchronize()
+                    dist.barrier()
+                    nvls.allreduce_bf16_nvls(sig, buf, n)
+                    torch.cuda.synchronize()
+                    sig.check_status()
+                    ref = sum(x.float() for x in xs)
+                    errs.append((v.float().cpu() - ref).abs().max().item() / (1 + ref.abs().max().item()))
+                    del v
+            finally:
+                buf.close()  # collective, before any rank can leave with memory bound
+            sig.close()
+            assert max(errs) <= 0.05 / 8, f"NVLS allreduce errors {errs}"
         # MoE all-to-all
         tokens, hidden, topk, experts = 1024, 2048, 8, 32
         recv = tokens * topk * world

@@ -240,3 +240,18 @@ def test_cross_gpu_write_read_imm_atomics(gpu2_env):
     assert int(dst[32 + n:].sum()) == 0
     assert torch.equal(back, src)
     assert int(ctr[0]) == 255 and sorted(old[:8].tolist()) == sorted([sum(1 << j for j in range(i)) for i in range(8)])
+
+
+@pytest.mark.parametrize("dst_gpu", [0, 1])
+def test_verbs_stress_16sge_imm_atomics(dst_gpu):
+    """BASELINE configs[3] at reduced size: per QP an interleave of 16-SGE WRITE / WRITE_WITH_IMM
+    (SGE sizes log-uniform 64 B..64 KiB, random offsets) and fetch-add / compare-swap on a
+    4096-entry counter array; ugdr_perf checks every gathered byte, immediate, CAS result and
+    final counter value."""
+    if gpu_count() < dst_gpu + 1:
+        pytest.skip(f"needs {dst_gpu + 1} GPU(s)")
+    from ugdr_b200.utils.perf import run
+
+    out = run(["stress", "--src-gpu", "0", "--dst-gpu", str(dst_gpu), "--qps", "16", "--depth", "64",
+               "--sges", "16", "--rounds", "2"], timeout=600)
+    assert out and out[-1]["correct"], out

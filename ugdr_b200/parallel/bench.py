@@ -23,6 +23,7 @@ import torch.distributed as dist
 
 from ..models.moe import MoEConfig, route
 from .collectives import MoEAllToAll, allreduce_bf16
+from . import nvls
 from .peers import PeerGroup
 
 
@@ -75,11 +76,35 @@ def bench_allreduce(rank, world, iters, warmup, nbytes=1 << 30) -> dict:
     ok = err <= tol
     t_ugdr = _timed(lambda: allreduce_bf16(g, count), iters, warmup)
     g.check_status()
+    g.close()
+    del x
+    # NVLS variant: the same data in multicast-bound memory, reduced inside the NVSwitch.
+    nv = {}
+    if nvls.supported():
+        sig = PeerGroup(4096, rank, world, exchange)
+        buf = nvls.NvlsBuffer(nbytes, rank, world, exchange)
+        try:
+            xn = buf.view(torch.bfloat16, count)
+            xn.copy_(torch.randn(count, generator=torch.Generator(device="cuda").manual_seed(rank), device="cuda",
+                                 dtype=torch.float32).to(torch.bfloat16))
+            torch.cuda.synchronize()
+            dist.barrier()
+            nvls.allreduce_bf16_nvls(sig, buf, count)
+            torch.cuda.synchronize()
+            sig.check_status()
+            err_n = (xn[lo:lo + (1 << 20)].float() - ref).abs().max().item()
+            t_n = _timed(lambda: nvls.allreduce_bf16_nvls(sig, buf, count), iters, warmup)
+            sig.check_status()
+            del xn
+        finally:
+            buf.close()  # collective, before any rank can leave with memory bound
+        sig.close()
+        nv = {"ugdr_nvls_ms": round(t_n, 4), "ugdr_nvls_algbw_GBps": round(nbytes / t_n / 1e6, 1),
+              "nvls_correct": bool(err_n <= tol), "nvls_max_err": err_n}
     y = torch.randn(count, device="cuda").to(torch.bfloat16)
     t_nccl = _timed(lambda: dist.all_reduce(y), iters, warmup)
-    g.close()
     bus = 2 * (world - 1) / world if world > 1 else 1.0
-    return {"op": "allreduce_bf16", "n_gpus": world, "bytes": nbytes,
+    return {"op": "allreduce_bf16", "n_gpus": world, "bytes": nbytes, **nv,
             "ugdr_ms": round(t_ugdr, 4), "nccl_ms": round(t_nccl, 4),
             "ugdr_algbw_GBps": round(nbytes / t_ugdr / 1e6, 1), "nccl_algbw_GBps": round(nbytes / t_nccl / 1e6, 1),
             "ugdr_busbw_GBps": round(bus * nbytes / t_ugdr / 1e6, 1),
