@@ -22,6 +22,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 namespace ugdr::coll {
 namespace {
@@ -193,6 +194,7 @@ __device__ __forceinline__ void mm_st_bf16x8(uint8_t *p, uint4 v) {
                  : "memory");
 }
 
+template <int U>
 __global__ void __launch_bounds__(512) allreduce_nvls_kernel(PeerSet ps, uint8_t *mc, uint64_t nvec, uint64_t epoch,
                                                              uint64_t max_ns) {
     entry_barrier(ps, epoch, kSlotArEntry, max_ns);
@@ -200,7 +202,6 @@ __global__ void __launch_bounds__(512) allreduce_nvls_kernel(PeerSet ps, uint8_t
     const uint64_t per = (nvec + ps.n - 1) / ps.n;
     const uint64_t begin = min(nvec, per * ps.rank), end = min(nvec, begin + per);
     const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
-    constexpr int U = 4;
     for (uint64_t i = begin + blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < end; i += U * stride) {
         uint4 v[U];
 #pragma unroll
@@ -471,7 +472,17 @@ int launch_allreduce_bf16(const PeerSet &ps, uint64_t offset, uint64_t count, ui
 int launch_allreduce_bf16_nvls(const PeerSet &ps, void *mc, uint64_t offset, uint64_t count, uint64_t epoch,
                                int ctas, uint64_t max_ns, cudaStream_t s) {
     if (mc == nullptr || count % 8 != 0 || offset % 16 != 0) return int(cudaErrorInvalidValue);
-    allreduce_nvls_kernel<<<ctas, 512, 0, s>>>(ps, static_cast<uint8_t *>(mc) + offset, count / 8, epoch, max_ns);
+    static const int unroll = [] {
+        const char *e = getenv("UGDR_NVLS_UNROLL");
+        return e ? atoi(e) : 4;
+    }();
+    uint8_t *base = static_cast<uint8_t *>(mc) + offset;
+    if (unroll >= 8)
+        allreduce_nvls_kernel<8><<<ctas, 512, 0, s>>>(ps, base, count / 8, epoch, max_ns);
+    else if (unroll <= 2)
+        allreduce_nvls_kernel<2><<<ctas, 512, 0, s>>>(ps, base, count / 8, epoch, max_ns);
+    else
+        allreduce_nvls_kernel<4><<<ctas, 512, 0, s>>>(ps, base, count / 8, epoch, max_ns);
     return int(cudaGetLastError());
 }
 

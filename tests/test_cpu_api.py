@@ -212,3 +212,11 @@ def test_engine_stats_count_work(cpu_daemon):
     cq.wait(10, 10)
     st = ctx.stats()
     assert st.wrs_completed >= 10 and st.bytes_moved >= 10_000
+
+
+def test_cli_doctor_reports_the_build():
+    from ugdr_b200.cli import doctor
+
+    rep = doctor()
+    assert rep["libugdr"] and rep["daemon"]
+    assert "gpus" in rep or "torch_error" in rep

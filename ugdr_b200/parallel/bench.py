@@ -47,7 +47,7 @@ def _timed(fn, iters: int, warmup: int) -> float:
 _GLOO = None
 
 
-def bench_allreduce(rank, world, iters, warmup, nbytes=1 << 30) -> dict:
+def bench_allreduce(rank, world, iters, warmup, nbytes=1 << 30, impl="all", ctas=0) -> dict:
     count = nbytes // 2
 
     def exchange(obj):
@@ -74,13 +74,13 @@ def bench_allreduce(rank, world, iters, warmup, nbytes=1 << 30) -> dict:
     err = (x[lo:lo + (1 << 20)].float() - ref).abs().max().item()
     tol = 2 ** -7 * ref.abs().max().item() + 1e-2
     ok = err <= tol
-    t_ugdr = _timed(lambda: allreduce_bf16(g, count), iters, warmup)
+    t_ugdr = _timed(lambda: allreduce_bf16(g, count, ctas=ctas), iters, warmup) if impl in ("all", "ring") else None
     g.check_status()
     g.close()
     del x
     # NVLS variant: the same data in multicast-bound memory, reduced inside the NVSwitch.
     nv = {}
-    if nvls.supported():
+    if impl in ("all", "nvls") and nvls.supported():
         sig = PeerGroup(4096, rank, world, exchange)
         buf = nvls.NvlsBuffer(nbytes, rank, world, exchange)
         try:
@@ -93,7 +93,7 @@ def bench_allreduce(rank, world, iters, warmup, nbytes=1 << 30) -> dict:
             torch.cuda.synchronize()
             sig.check_status()
             err_n = (xn[lo:lo + (1 << 20)].float() - ref).abs().max().item()
-            t_n = _timed(lambda: nvls.allreduce_bf16_nvls(sig, buf, count), iters, warmup)
+            t_n = _timed(lambda: nvls.allreduce_bf16_nvls(sig, buf, count, ctas=ctas), iters, warmup)
             sig.check_status()
             del xn
         finally:
@@ -102,14 +102,43 @@ def bench_allreduce(rank, world, iters, warmup, nbytes=1 << 30) -> dict:
         nv = {"ugdr_nvls_ms": round(t_n, 4), "ugdr_nvls_algbw_GBps": round(nbytes / t_n / 1e6, 1),
               "nvls_correct": bool(err_n <= tol), "nvls_max_err": err_n}
     y = torch.randn(count, device="cuda").to(torch.bfloat16)
-    t_nccl = _timed(lambda: dist.all_reduce(y), iters, warmup)
+    t_nccl = _timed(lambda: dist.all_reduce(y), iters, warmup) if impl == "all" else None
     bus = 2 * (world - 1) / world if world > 1 else 1.0
-    return {"op": "allreduce_bf16", "n_gpus": world, "bytes": nbytes, **nv,
-            "ugdr_ms": round(t_ugdr, 4), "nccl_ms": round(t_nccl, 4),
-            "ugdr_algbw_GBps": round(nbytes / t_ugdr / 1e6, 1), "nccl_algbw_GBps": round(nbytes / t_nccl / 1e6, 1),
-            "ugdr_busbw_GBps": round(bus * nbytes / t_ugdr / 1e6, 1),
-            "nccl_busbw_GBps": round(bus * nbytes / t_nccl / 1e6, 1),
-            "speedup_vs_nccl": round(t_nccl / t_ugdr, 3), "correct": bool(ok), "max_err": err}
+    out = {"op": "allreduce_bf16", "n_gpus": world, "bytes": nbytes, **nv, "correct": bool(ok), "max_err": err}
+    if t_ugdr is not None:
+        out.update({"ugdr_ring_ms": round(t_ugdr, 4), "ugdr_ring_algbw_GBps": round(nbytes / t_ugdr / 1e6, 1),
+                    "ugdr_ring_busbw_GBps": round(bus * nbytes / t_ugdr / 1e6, 1)})
+    best = min(t for t in (t_ugdr, nv.get("ugdr_nvls_ms")) if t is not None)
+    out["ugdr_best_ms"] = round(best, 4)
+    out["ugdr_best_path"] = "nvls" if nv and best == nv["ugdr_nvls_ms"] else "ring"
+    if t_nccl is not None:
+        out.update({"nccl_ms": round(t_nccl, 4), "nccl_algbw_GBps": round(nbytes / t_nccl / 1e6, 1),
+                    "nccl_busbw_GBps": round(bus * nbytes / t_nccl / 1e6, 1),
+                    "speedup_vs_nccl": round(t_nccl / best, 3)})
+    return out
+
+
+def bench_p2p_nccl(rank, world, sizes, iters, warmup) -> list[dict]:
+    """NCCL send/recv baseline for the point-to-point sweep: rank 0 sends
+    `size` bytes to rank 1, `iters` transfers back to back, device-timed, max over the pair."""
+    out = []
+    if world < 2:
+        return out
+    for size in sizes:
+        buf = torch.empty(max(size, 1), dtype=torch.uint8, device="cuda")
+
+        def step():
+            if rank == 0:
+                dist.send(buf, 1)
+            elif rank == 1:
+                dist.recv(buf, 0)
+
+        n = max(4, min(2000, (8 << 30) // max(size, 1)))
+        t = _timed(step, n, warmup)
+        out.append({"op": "p2p_nccl", "bytes": size, "us_per_transfer": round(t * 1e3, 3),
+                    "GBps": round(size / t / 1e6, 3)})
+        del buf
+    return out
 
 
 def bench_moe(rank, world, iters, warmup, cfg: MoEConfig) -> dict:
@@ -174,11 +203,14 @@ def bench_moe(rank, world, iters, warmup, cfg: MoEConfig) -> dict:
 def main():
     global _GLOO
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", default="all", choices=["all", "allreduce", "moe"])
+    ap.add_argument("--op", default="all", choices=["all", "allreduce", "moe", "p2p"])
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--ar-mib", type=int, default=1024, help="allreduce bytes per rank, MiB")
     ap.add_argument("--tokens", type=int, default=MoEConfig().tokens, help="MoE tokens per rank")
+    ap.add_argument("--ar-impl", default="all", choices=["all", "ring", "nvls"],
+                    help="allreduce paths to time (all: ring, NVLS when available, and NCCL)")
+    ap.add_argument("--ctas", type=int, default=0, help="allreduce grid size (0: one CTA per SM)")
     args = ap.parse_args()
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -187,7 +219,11 @@ def main():
     _GLOO = dist.new_group(backend="gloo")
     results = []
     if args.op in ("all", "allreduce"):
-        results.append(bench_allreduce(rank, world, args.iters, args.warmup, args.ar_mib << 20))
+        results.append(bench_allreduce(rank, world, args.iters, args.warmup, args.ar_mib << 20, args.ar_impl,
+                                       args.ctas))
+    if args.op == "p2p":
+        sizes = [1 << k for k in range(3, 31, 2)]
+        results.extend(bench_p2p_nccl(rank, world, sizes, max(args.iters, 20), args.warmup))
     if args.op in ("all", "moe"):
         results.append(bench_moe(rank, world, args.iters, args.warmup, MoEConfig(tokens=args.tokens)))
     if rank == 0:

@@ -3,6 +3,7 @@
     python -m ugdr_b200.utils.perf latency --src-gpu 0 --dst-gpu 1 --bytes 8
     python -m ugdr_b200.utils.perf bw --src-gpu 0 --dst-gpu 1 --op read --min 8 --max 1G
     python -m ugdr_b200.utils.perf posting --batch 32
+    python -m ugdr_b200.utils.perf stress-all --gpus 8 --qps 64 --depth 128 --rounds 2
 
 Prints the binary's key=value and JSON lines.  `--gpus N` sets how many GPUs the daemon owns
 (default: every GPU named by --src-gpu / --dst-gpu; 0 for `posting`).
@@ -38,6 +39,37 @@ def run(args: list[str], gpus: int | None = None, timeout: float = 1800) -> list
     return [json.loads(line) for line in lines if line.startswith("{")]
 
 
+def stress_all(gpus: int, extra: list[str], timeout: float = 1800) -> dict:
+    """BASELINE configs[3] on every ordered GPU pair at once: one daemon owning `gpus` GPUs and
+    one ugdr_perf stress client per (src, dst) pair, all running concurrently.  Returns the
+    per-pair JSON results and the aggregate rates."""
+    exe = N.LIB_DIR / "ugdr_perf"
+    pairs = [(a, b) for a in range(gpus) for b in range(gpus) if a != b] or [(0, 0)]
+    results = []
+    with V.Daemon(gpus=gpus) as d:
+        env = dict(os.environ, UGDR_DAEMON_SOCKET=d.socket_path)
+        procs = [subprocess.Popen([str(exe), "stress", "--src-gpu", str(a), "--dst-gpu", str(b), *extra,
+                                   "--seed", str(1 + a * 16 + b)], env=env, stdout=subprocess.PIPE,
+                                  stderr=subprocess.PIPE, text=True) for a, b in pairs]
+        failed = []
+        for (a, b), p in zip(pairs, procs):
+            out, err = p.communicate(timeout=timeout)
+            js = [json.loads(line) for line in out.splitlines() if line.startswith("{")]
+            if p.returncode != 0 or not js:
+                failed.append((a, b, p.returncode, err[-300:]))
+            results.extend(js)
+        if failed:
+            sys.stderr.write(d.log_text())
+    agg = {"benchmark": "ugdr_stress_all", "gpus": gpus, "pairs": len(pairs),
+           "wrs": sum(r["wrs"] for r in results),
+           "complete_MWRps_sum": round(sum(r["complete_MWRps"] for r in results), 3),
+           "post_MWRps_sum": round(sum(r["post_MWRps"] for r in results), 3),
+           "GBps_sum": round(sum(r["GBps"] for r in results), 3),
+           "correct": bool(results) and not failed and all(r["correct"] for r in results),
+           "failed": failed}
+    return {"pairs": results, "aggregate": agg}
+
+
 if __name__ == "__main__":
     argv = sys.argv[1:]
     g = None
@@ -45,4 +77,10 @@ if __name__ == "__main__":
         i = argv.index("--gpus")
         g = int(argv[i + 1])
         del argv[i:i + 2]
+    if argv and argv[0] == "stress-all":
+        res = stress_all(g or 2, argv[1:])
+        for r in res["pairs"]:
+            print(json.dumps(r))
+        print(json.dumps(res["aggregate"]))
+        sys.exit(0 if res["aggregate"]["correct"] else 2)
     run(argv, gpus=g)
