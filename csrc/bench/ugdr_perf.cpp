@@ -530,7 +530,12 @@ int run_stress(const Opts &o) {
                     ++bad_imm;
             }
             got_recv += uint64_t(k);
-            if (Clock::now() > deadline) die("stress completion timeout", ETIMEDOUT);
+            if (Clock::now() > deadline) {
+                std::fprintf(stderr, "ugdr_perf: stress round %llu: %llu of %llu send and %llu of %llu receive "
+                             "completions\n", (unsigned long long)round, (unsigned long long)got,
+                             (unsigned long long)per_round, (unsigned long long)got_recv, (unsigned long long)nimm);
+                die("stress completion timeout", ETIMEDOUT);
+            }
         }
         const auto t2 = Clock::now();
         post_s += std::chrono::duration<double>(t1 - t0).count();

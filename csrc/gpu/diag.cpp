@@ -1,6 +1,7 @@
 // Diagnostic entry points into the executor's copy core, callable through the C ABI (tests
 // and benchmarks pass torch tensors' device pointers and a CUDA stream).
 #include "gpu/executor.hpp"
+#include "ugdr/api.hpp"
 
 #include <cuda_runtime_api.h>
 
@@ -9,14 +10,14 @@
 extern "C" {
 
 // One warp copies n bytes (alignment-matrix tests).  Returns a cudaError_t value.
-int ugdr_x_copy_core_test(void *dst, const void *src, uint64_t n, void *stream) {
+int ugdr_x_copy_core_test(void *dst, const void *src, uint64_t n, void *stream) noexcept {
     return ugdr::gpu::launch_copy_test(dst, src, n, static_cast<cudaStream_t>(stream));
 }
 
 // Time `iters` whole-grid copies of n bytes with CUDA events on `stream`; writes the mean
 // milliseconds per copy.  Returns a cudaError_t value.
 int ugdr_x_grid_copy_bench(void *dst, const void *src, uint64_t n, int ctas, int iters, void *stream,
-                           float *ms_per_copy) {
+                           float *ms_per_copy) noexcept {
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaEvent_t a, b;
     cudaEventCreate(&a);

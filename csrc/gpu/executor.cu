@@ -119,13 +119,54 @@ __device__ __forceinline__ uint64_t bcast64(uint64_t v) {
 }
 
 // ---- warp copy core ----------------------------------------------------------------------------
-// Copies n bytes, never touching bytes outside [dst, dst + n) / [src, src + n).  16-byte vector
-// body when both pointers share their offset mod 16 (8 vectors in flight per lane), 4-byte body
-// when they share it mod 4, bytes otherwise.
+// Copies n bytes, never touching bytes outside [dst, dst + n) / [src, src + n).  32-byte vector
+// body (sm_100 256-bit loads / stores, 4 in flight per lane) when both pointers share their
+// offset mod 32 and the range is long; 16-byte body (8 in flight) when they share it mod 16;
+// 4-byte body when mod 4; bytes otherwise.
+
+struct alignas(32) V256 {
+    uint32_t w[8];
+};
+__device__ __forceinline__ V256 ld256(const void *p) {
+    V256 v;
+    asm volatile("ld.global.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3]), "=r"(v.w[4]), "=r"(v.w[5]),
+                   "=r"(v.w[6]), "=r"(v.w[7])
+                 : "l"(p));
+    return v;
+}
+__device__ __forceinline__ void st256(void *p, const V256 &v) {
+    asm volatile("st.global.v8.u32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(v.w[0]), "r"(v.w[1]),
+                 "r"(v.w[2]), "r"(v.w[3]), "r"(v.w[4]), "r"(v.w[5]), "r"(v.w[6]), "r"(v.w[7])
+                 : "memory");
+}
 
 __device__ void warp_copy(uint8_t *dst, const uint8_t *src, uint64_t n, int lane) {
     if (n == 0) return;
     const uintptr_t d = reinterpret_cast<uintptr_t>(dst), s = reinterpret_cast<uintptr_t>(src);
+    if (((d ^ s) & 31) == 0 && n >= 4096) {
+        const uint64_t head = (32 - (d & 31)) & 31;  // < 32 <= n
+        if (uint64_t(lane) < head) dst[lane] = src[lane];
+        dst += head;
+        src += head;
+        n -= head;
+        const uint64_t nvec = n >> 5;
+        V256 *dv = reinterpret_cast<V256 *>(dst);
+        const V256 *sv = reinterpret_cast<const V256 *>(src);
+        constexpr int U = 4;
+        uint64_t i = lane;
+        for (; i + (U - 1) * 32 < nvec; i += U * 32) {
+            V256 r[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) r[u] = ld256(sv + i + u * 32);
+#pragma unroll
+            for (int u = 0; u < U; ++u) st256(dv + i + u * 32, r[u]);
+        }
+        for (; i < nvec; i += 32) st256(dv + i, ld256(sv + i));
+        const uint64_t done = nvec << 5;
+        if (uint64_t(lane) < n - done) dst[done + lane] = src[done + lane];
+        return;
+    }
     if (((d ^ s) & 15) == 0 && n >= 64) {
         uint64_t head = (16 - (d & 15)) & 15;
         if (head > n) head = n;
@@ -1162,6 +1203,18 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
         const uint32_t op = h->opcode;
         const bool signaled = v.sig_all || (h->send_flags & UGDR_SEND_SIGNALED) != 0;
 
+        // A WR that becomes a job takes its job slot first: with no slot free the WR waits for a
+        // later pass before anything (an RQ claim, a copy) has been done for it.
+        int slot = -1;
+        unsigned long long gen = 0;
+        const bool needs_job = status == UGDR_WC_SUCCESS && !is_atomic(op) && total > kInlineBytes;
+        if (needs_job) {
+            if (w.lane == 0) slot = take_job_slot(jr, w.gwarp + uint32_t(issue), &gen);
+            slot = bcast(slot);
+            gen = bcast64(gen);
+            if (slot < 0) break;  // no job slot: retry on a later pass
+        }
+
         // Responder RQ for WRITE_WITH_IMM (RNR when empty).
         int rnr = 0;  // 0 go, 1 wait, 2 retry budget exhausted
         if (status == UGDR_WC_SUCCESS && op == UGDR_WR_RDMA_WRITE_WITH_IMM) {
@@ -1194,6 +1247,11 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
                 }
             }
             rnr = bcast(rnr);
+            if (rnr != 0 && slot >= 0) {
+                // No job after all: hand the taken slot back (its sequence becomes even again).
+                if (w.lane == 0) atomicAdd(&jr->slots[slot].seq, 1ull);
+                slot = -1;
+            }
             if (rnr == 1) break;
             if (rnr == 2) {
                 status = UGDR_WC_RNR_RETRY_EXC_ERR;
@@ -1209,28 +1267,17 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
             if (!w.started) atomicCAS(&w.p->stats->first_start_ns, 0ull, (unsigned long long)gtime());
         }
         w.started = true;
-        bool ok = true;
         if (status == UGDR_WC_SUCCESS) {
-            if (is_atomic(op) || total <= kInlineBytes) {
+            if (slot < 0) {
                 run_inline(w, rec, wqe, op, total, remote);
                 ++inline_ran;
             } else {
                 const uint32_t chunk = chunk_for(total, nwarps);
                 const uint32_t n = uint32_t((total + chunk - 1) / chunk);
-                int slot = -1;
-                unsigned long long gen = 0;
-                if (w.lane == 0) {
-                    slot = take_job_slot(jr, w.gwarp + uint32_t(issue), &gen);
-                    rec->nchunks = slot >= 0 ? n : 0u;
-                }
-                slot = bcast(slot);
-                gen = bcast64(gen);
-                if (slot >= 0)
-                    publish_job(w, jr, bitmap, slot, gen, qp->st.win, uint32_t(issue % kWindow), 1u, 0u, n, chunk);
-                ok = slot >= 0;
+                if (w.lane == 0) rec->nchunks = n;
+                publish_job(w, jr, bitmap, slot, gen, qp->st.win, uint32_t(issue % kWindow), 1u, 0u, n, chunk);
             }
         }
-        if (!ok) break;  // no job slot: retry on a later pass
         ++issued;
         if (status != UGDR_WC_SUCCESS) break;  // stop issuing behind an error
     }

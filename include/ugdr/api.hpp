@@ -280,6 +280,14 @@ int ugdr_x_engine_hold(ugdr_context *context, int hold) UGDR_NOEXCEPT;
 int ugdr_x_timed_drain(ugdr_context **contexts, int num_contexts, const uint64_t *expected_wrs,
                        uint32_t timeout_ms, float *elapsed_ms) UGDR_NOEXCEPT;
 
+/* Diagnostics on the current CUDA device (no daemon involved).  ugdr_x_copy_core_test runs the
+ * executor's warp copy core once (one warp) over [src, src + n) -> dst, for alignment-matrix
+ * tests; ugdr_x_grid_copy_bench times `iters` whole-grid copies with CUDA events on `stream` and
+ * writes the mean milliseconds per copy.  Both return a cudaError_t value. */
+int ugdr_x_copy_core_test(void *dst, const void *src, uint64_t n, void *stream) UGDR_NOEXCEPT;
+int ugdr_x_grid_copy_bench(void *dst, const void *src, uint64_t n, int ctas, int iters, void *stream,
+                           float *ms_per_copy) UGDR_NOEXCEPT;
+
 #ifdef __cplusplus
 }
 #endif

@@ -42,7 +42,8 @@ def _acc(N):
 
 
 @pytest.mark.parametrize("size,soff,doff", [(8, 0, 0), (1, 3, 5), (4096, 0, 0), (4097, 1, 1),
-                                            (65536, 16, 32), (1 << 20, 7, 3), ((32 << 20) + 5, 0, 16)])
+                                            (65536, 16, 32), (1 << 20, 7, 3), ((32 << 20) + 5, 0, 16),
+                                            ((1 << 20) + 3, 32, 0), (100003, 5, 37)])
 def test_write_read_sizes(gpu_env, size, soff, doff):
     V = gpu_env
     from ugdr_b200 import _native as N
@@ -255,3 +256,36 @@ def test_verbs_stress_16sge_imm_atomics(dst_gpu):
     out = run(["stress", "--src-gpu", "0", "--dst-gpu", str(dst_gpu), "--qps", "16", "--depth", "64",
                "--sges", "16", "--rounds", "2"], timeout=600)
     assert out and out[-1]["correct"], out
+
+
+def test_copy_core_alignment_matrix():
+    """The executor's warp copy core (reference parity: the copy-core alignment matrix of
+    tests/integration/persistent_copy_test.cpp): every (source offset, destination offset, size)
+    copies exactly its bytes - guard bytes on both sides of the destination stay untouched - for
+    the byte, 4-byte, 16-byte and 32-byte bodies."""
+    if gpu_count() < 1:
+        pytest.skip("no GPU")
+    import ctypes as C
+
+    from ugdr_b200 import _native as N
+
+    L = N.lib()
+    L.ugdr_x_copy_core_test.restype = C.c_int
+    L.ugdr_x_copy_core_test.argtypes = [C.c_void_p, C.c_void_p, C.c_uint64, C.c_void_p]
+    torch.cuda.set_device(0)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    src = torch.randint(0, 256, (1 << 20,), dtype=torch.uint8, device="cuda", generator=g)
+    dst = torch.empty((1 << 20) + 256, dtype=torch.uint8, device="cuda")
+    sizes = [0, 1, 3, 15, 16, 17, 31, 32, 33, 63, 64, 65, 255, 4095, 4096, 4097, 4127, 65536 + 7, 300001]
+    offs = [0, 1, 4, 15, 16, 17, 31, 32, 33]
+    for n in sizes:
+        for so in offs:
+            for do in offs:
+                dst.fill_(0xD3)
+                base = 64 + do
+                rc = L.ugdr_x_copy_core_test(C.c_void_p(dst.data_ptr() + base), C.c_void_p(src.data_ptr() + so), n,
+                                             None)
+                assert rc == 0
+                torch.cuda.synchronize()
+                assert torch.equal(dst[base:base + n], src[so:so + n]), (n, so, do)
+                assert bool((dst[:base] == 0xD3).all()) and bool((dst[base + n:] == 0xD3).all()), (n, so, do)

@@ -80,7 +80,7 @@ def bench_allreduce(rank, world, iters, warmup, nbytes=1 << 30, impl="all", ctas
     del x
     # NVLS variant: the same data in multicast-bound memory, reduced inside the NVSwitch.
     nv = {}
-    if impl in ("all", "nvls") and nvls.supported():
+    if impl in ("all", "nvls") and world >= 2 and nvls.supported():
         sig = PeerGroup(4096, rank, world, exchange)
         buf = nvls.NvlsBuffer(nbytes, rank, world, exchange)
         try:
