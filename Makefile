@@ -56,8 +56,37 @@ $(OUT)/ugdr_perf: $(OBJ)/bench/ugdr_perf.o $(OUT)/libugdr.so
 $(OUT)/ugdr_native_tests: $(TEST_OBJS) $(OUT)/libugdr.so
 	$(CXX) -o $@ $(TEST_OBJS) -L$(OUT) -lugdr -Wl,-rpath,'$$ORIGIN' $(LDLIBS)
 
+# Sanitizer builds of the native test suite (host code instrumented; the CUDA objects are the
+# regular ones): `make asan` / `make tsan`, then run build/san/<kind>/ugdr_native_tests.
+SAN       := build/san
+SAN_CXX   ?= /usr/bin/g++
+ASAN_FLAGS := -fsanitize=address,undefined -fno-omit-frame-pointer -fno-sanitize-recover=undefined
+TSAN_FLAGS := -fsanitize=thread
+
+$(SAN)/asan/%.o: csrc/%.cpp
+	@mkdir -p $(dir $@)
+	$(SAN_CXX) $(CPPFLAGS) $(CXXFLAGS) $(ASAN_FLAGS) -c $< -o $@
+$(SAN)/asan/tests/%.o: tests/native/%.cpp
+	@mkdir -p $(dir $@)
+	$(SAN_CXX) $(CPPFLAGS) $(CXXFLAGS) $(ASAN_FLAGS) -c $< -o $@
+$(SAN)/tsan/%.o: csrc/%.cpp
+	@mkdir -p $(dir $@)
+	$(SAN_CXX) $(CPPFLAGS) $(CXXFLAGS) $(TSAN_FLAGS) -c $< -o $@
+$(SAN)/tsan/tests/%.o: tests/native/%.cpp
+	@mkdir -p $(dir $@)
+	$(SAN_CXX) $(CPPFLAGS) $(CXXFLAGS) $(TSAN_FLAGS) -c $< -o $@
+
+CU_OBJS := $(LIB_CU:csrc/%.cu=$(OBJ)/%.cu.o)
+$(SAN)/asan/ugdr_native_tests: $(LIB_CXX:csrc/%.cpp=$(SAN)/asan/%.o) $(TEST_SRCS:tests/native/%.cpp=$(SAN)/asan/tests/%.o) $(CU_OBJS)
+	$(SAN_CXX) $(ASAN_FLAGS) -o $@ $^ $(LDLIBS)
+$(SAN)/tsan/ugdr_native_tests: $(LIB_CXX:csrc/%.cpp=$(SAN)/tsan/%.o) $(TEST_SRCS:tests/native/%.cpp=$(SAN)/tsan/tests/%.o) $(CU_OBJS)
+	$(SAN_CXX) $(TSAN_FLAGS) -o $@ $^ $(LDLIBS)
+
+asan: $(SAN)/asan/ugdr_native_tests
+tsan: $(SAN)/tsan/ugdr_native_tests
+
 clean:
-	rm -rf build/obj $(OUT)/libugdr.so $(OUT)/ugdr_daemon $(OUT)/ugdr_client $(OUT)/ugdr_native_tests $(OUT)/ugdr_perf
+	rm -rf build/obj build/san $(OUT)/libugdr.so $(OUT)/ugdr_daemon $(OUT)/ugdr_client $(OUT)/ugdr_native_tests $(OUT)/ugdr_perf
 
 -include $(shell find build/obj -name '*.d' 2>/dev/null)
-.PHONY: all clean
+.PHONY: all clean asan tsan
