@@ -521,7 +521,8 @@ int ugdr_x_query_engine_stats(ugdr_context *ctx, ugdr_x_engine_stats *stats, int
         !rd.be(&stats->chunks_run) || !rd.be(&stats->claim_misses) || !rd.be(&stats->jobs_published) ||
         !rd.be(&stats->inline_runs) || !rd.be(&stats->busy_ns) || !rd.be(&stats->fast_batches) ||
         !rd.be(&stats->fast_fetch_ns) || !rd.be(&stats->fast_exec_ns) || !rd.be(&stats->fast_reserve_ns) ||
-        !rd.be(&stats->fast_publish_ns))
+        !rd.be(&stats->fast_publish_ns) || !rd.be(&stats->slow_wrs) || !rd.be(&stats->slow_issue_ns) ||
+        !rd.be(&stats->job_slot_misses) || !rd.be(&stats->publish_waits) || !rd.be(&stats->publish_wait_ns))
         return EPROTO;
     return 0;
 }

@@ -212,17 +212,46 @@ int run_bw(const Opts &o) {
         wait_cq(a.cq, qd);
         uint64_t posted = 0, done = 0;
         ugdr_wc wc[64];
+        std::vector<ugdr_send_wr> chain(qd);
+        std::vector<ugdr_sge> chain_sge(qd);
+        ugdr_x_engine_stats es{};
+        ugdr_x_query_engine_stats(a.ctx, &es, 1);
         const auto t0 = Clock::now();
         while (done < wrs) {
             // Bound each size to ~2 s: stop posting and drain what is in flight.
             if (posted < wrs && (posted & 255) == 0 && Clock::now() - t0 > std::chrono::seconds(2)) wrs = posted;
-            while (posted < wrs && posted - done < qd) {
+            // Post every free window slot as one chain (one ugdr_post_send call), as the
+            // reference's client benchmark does with its post chains.
+            uint32_t nchain = 0;
+            while (posted + nchain < wrs && posted + nchain - done < qd) {
                 // Each in-flight WR uses its own destination slice when it fits, else the start.
-                const uint64_t slot = (posted % qd) * sz;
+                const uint64_t w = posted + nchain;
+                const uint64_t slot = (w % qd) * sz;
                 const uint64_t off = slot + sz <= o.max_bytes ? slot : 0;
-                post(a.qp, op, static_cast<uint8_t *>(a.buf) + off, a.mr->lkey, sz,
-                     static_cast<uint8_t *>(b.buf) + off, b.mr->rkey, posted);
-                ++posted;
+                chain_sge[nchain] = ugdr_sge{reinterpret_cast<uint64_t>(static_cast<uint8_t *>(a.buf) + off),
+                                             uint32_t(sz), a.mr->lkey};
+                ugdr_send_wr &wr = chain[nchain];
+                wr = ugdr_send_wr{};
+                wr.wr_id = w;
+                wr.sg_list = &chain_sge[nchain];
+                wr.num_sge = 1;
+                wr.opcode = ugdr_wr_opcode(op);
+                wr.send_flags = UGDR_SEND_SIGNALED;
+                wr.wr.rdma.remote_addr = reinterpret_cast<uint64_t>(static_cast<uint8_t *>(b.buf) + off);
+                wr.wr.rdma.rkey = b.mr->rkey;
+                if (nchain > 0) chain[nchain - 1].next = &wr;
+                ++nchain;
+            }
+            if (nchain > 0) {
+                ugdr_send_wr *bad = nullptr;
+                const int rc = ugdr_post_send(a.qp, chain.data(), &bad);
+                if (rc != 0 && rc != ENOMEM) die("ugdr_post_send", rc);
+                uint32_t accepted = nchain;
+                if (rc == ENOMEM) {
+                    accepted = 0;
+                    for (ugdr_send_wr *x = chain.data(); x != bad; x = x->next) ++accepted;
+                }
+                posted += accepted;
             }
             const int n = ugdr_poll_cq(a.cq, 64, wc);
             if (n < 0) die("ugdr_poll_cq", -n);
@@ -235,6 +264,14 @@ int run_bw(const Opts &o) {
         const bool ok = op == UGDR_WR_RDMA_WRITE ? same(a.buf, o.src_gpu, b.buf, o.dst_gpu, sz)
                                                  : same(b.buf, o.dst_gpu, a.buf, o.src_gpu, sz);
         if (!ok) status = 2;
+        if (ugdr_x_query_engine_stats(a.ctx, &es, 0) == 0)
+            std::printf("engine bytes=%llu wrs=%llu jobs=%llu chunks=%llu claim_misses=%llu busy_us=%.1f "
+                        "fast_batches=%llu slow_wrs=%llu publish_waits=%llu\n",
+                        (unsigned long long)sz, (unsigned long long)es.wrs_completed,
+                        (unsigned long long)es.jobs_published, (unsigned long long)es.chunks_run,
+                        (unsigned long long)es.claim_misses, double(es.busy_ns) / 1e3,
+                        (unsigned long long)es.fast_batches, (unsigned long long)es.slow_wrs,
+                        (unsigned long long)es.publish_waits);
         std::printf("benchmark=ugdr_bw op=%s bytes=%llu qd=%u src_gpu=%d dst_gpu=%d wrs=%llu seconds=%.6f "
                     "GB_per_s=%.3f MWR_per_s=%.4f correct=%d\n",
                     o.op.c_str(), (unsigned long long)sz, qd, o.src_gpu, o.dst_gpu, (unsigned long long)wrs, s,
@@ -402,6 +439,8 @@ int run_stress(const Opts &o) {
         if (int rc = ugdr_connect_qp(rsp[q], &ia, &c, cmask)) die("connect", rc);
     }
 
+    ugdr_x_engine_stats es{};
+    ugdr_x_query_engine_stats(rq.ctx, &es, 1);  // reset the requester engine's counters
     std::mt19937_64 rng(o.seed * 1000003ull + 17);
     auto log_uniform = [&](uint64_t lo, uint64_t hi) {
         const double u = std::uniform_real_distribution<double>(std::log(double(lo)), std::log(double(hi) + 1))(rng);
@@ -563,6 +602,17 @@ int run_stress(const Opts &o) {
     for (uint64_t i = 0; i < kCounters; ++i)
         if (ctr_host[i] != (i < kFaaCounters ? faa_expect[i] : cas_seen[i])) ++bad_ctr;
     ok = bad_bytes == 0 && bad_imm == 0 && bad_cas == 0 && bad_wc == 0 && bad_ctr == 0;
+    if (ugdr_x_query_engine_stats(rq.ctx, &es, 0) == 0)
+        std::printf("engine src_gpu=%d wrs=%llu jobs=%llu chunks=%llu claim_misses=%llu inline=%llu slow_wrs=%llu "
+                    "slow_issue_us_avg=%.3f job_slot_misses=%llu publish_waits=%llu publish_wait_us_avg=%.3f "
+                    "launches=%llu wait_timeouts=%llu\n",
+                    o.src_gpu, (unsigned long long)es.wrs_completed, (unsigned long long)es.jobs_published,
+                    (unsigned long long)es.chunks_run, (unsigned long long)es.claim_misses,
+                    (unsigned long long)es.inline_runs, (unsigned long long)es.slow_wrs,
+                    es.slow_wrs ? double(es.slow_issue_ns) / es.slow_wrs / 1e3 : 0.0,
+                    (unsigned long long)es.job_slot_misses, (unsigned long long)es.publish_waits,
+                    es.publish_waits ? double(es.publish_wait_ns) / es.publish_waits / 1e3 : 0.0,
+                    (unsigned long long)es.launches, (unsigned long long)es.wait_timeouts);
     const double post_mops = double(total_wrs) / post_s / 1e6, run_mops = double(total_wrs) / run_s / 1e6;
     std::printf("benchmark=ugdr_stress src_gpu=%d dst_gpu=%d qps=%u depth=%u sges=%u rounds=%llu wrs=%llu "
                 "post_MWR_per_s=%.3f complete_MWR_per_s=%.3f GB_per_s=%.3f bad_wrs=%llu bad_imm=%llu bad_cas=%llu "

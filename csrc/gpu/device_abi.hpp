@@ -40,6 +40,7 @@ struct DevMr {
 struct DevCqConfig {
     queue::RingHeader *ring;  // device pointer of the mapped ring
     uint8_t *slots;
+    unsigned long long *ready;  // per slot: s + 1 once slot s's CQE is written (device memory)
     uint32_t capacity;
     uint32_t stride;
     uint32_t valid;
@@ -48,7 +49,7 @@ struct DevCqConfig {
 
 struct DevCqState {
     unsigned long long reserve;    // next slot to hand out (CAS, .sys)
-    unsigned long long published;  // unused: the ring tail itself is the in-order publish cursor
+    unsigned long long published;  // device mirror of the ring tail: slots below are visible
     unsigned long long head_seen;  // cached consumer cursor
     unsigned long long pad[5];
 };
@@ -162,6 +163,8 @@ struct DevStats {
     unsigned long long launches_seen;   // kernel launches (block 0 thread 0)
     // Small-WR fast path, summed per batch: batches, WQE fetch, validate+copy, CQ reserve, publish.
     unsigned long long fast_batches, fast_fetch_ns, fast_exec_ns, fast_reserve_ns, fast_publish_ns;
+    // One-per-round issue path and CQ publish waits (see ugdr_x_engine_stats).
+    unsigned long long slow_wrs, slow_issue_ns, job_slot_misses, publish_waits, publish_wait_ns;
     unsigned long long last_work_ns;
     unsigned long long retired;  // WRs retired since the last reset (drain mode exit test)
     unsigned int exiting;

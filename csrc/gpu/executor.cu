@@ -122,7 +122,8 @@ __device__ __forceinline__ uint64_t bcast64(uint64_t v) {
 // Copies n bytes, never touching bytes outside [dst, dst + n) / [src, src + n).  32-byte vector
 // body (sm_100 256-bit loads / stores, 4 in flight per lane) when both pointers share their
 // offset mod 32 and the range is long; 16-byte body (8 in flight) when they share it mod 16;
-// 4-byte body when mod 4; bytes otherwise.
+// otherwise, from 64 bytes on, 16-byte stores built from shifted aligned 16-byte loads; bytes
+// for short ranges.
 
 struct alignas(32) V256 {
     uint32_t w[8];
@@ -139,6 +140,32 @@ __device__ __forceinline__ void st256(void *p, const V256 &v) {
     asm volatile("st.global.v8.u32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(v.w[0]), "r"(v.w[1]),
                  "r"(v.w[2]), "r"(v.w[3]), "r"(v.w[4]), "r"(v.w[5]), "r"(v.w[6]), "r"(v.w[7])
                  : "memory");
+}
+
+// Bytes [r, r + 16) of the 32-byte concatenation a:b (0 < r < 16), as one 16-byte vector.
+__device__ __forceinline__ uint4 shift_join(const uint4 &a, const uint4 &b, uint32_t r) {
+    const uint32_t c[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    const uint32_t sh = (r & 3) * 8;
+    uint4 o;
+    switch (r >> 2) {  // uniform across the warp: one branch, static register indices
+    case 0:
+        o = make_uint4(__funnelshift_r(c[0], c[1], sh), __funnelshift_r(c[1], c[2], sh), __funnelshift_r(c[2], c[3], sh),
+                       __funnelshift_r(c[3], c[4], sh));
+        break;
+    case 1:
+        o = make_uint4(__funnelshift_r(c[1], c[2], sh), __funnelshift_r(c[2], c[3], sh), __funnelshift_r(c[3], c[4], sh),
+                       __funnelshift_r(c[4], c[5], sh));
+        break;
+    case 2:
+        o = make_uint4(__funnelshift_r(c[2], c[3], sh), __funnelshift_r(c[3], c[4], sh), __funnelshift_r(c[4], c[5], sh),
+                       __funnelshift_r(c[5], c[6], sh));
+        break;
+    default:
+        o = make_uint4(__funnelshift_r(c[3], c[4], sh), __funnelshift_r(c[4], c[5], sh), __funnelshift_r(c[5], c[6], sh),
+                       __funnelshift_r(c[6], c[7], sh));
+        break;
+    }
+    return o;
 }
 
 __device__ void warp_copy(uint8_t *dst, const uint8_t *src, uint64_t n, int lane) {
@@ -192,18 +219,47 @@ __device__ void warp_copy(uint8_t *dst, const uint8_t *src, uint64_t n, int lane
         if (uint64_t(lane) < tail) dst[done + lane] = src[done + lane];
         return;
     }
-    if (((d ^ s) & 3) == 0 && n >= 16) {
-        uint64_t head = (4 - (d & 3)) & 3;
-        if (head > n) head = n;
+    if (n >= 64) {
+        // Source and destination disagree mod 16: align the destination, then build every
+        // 16-byte destination vector from the two aligned source vectors that cover it (the
+        // lane's own and its neighbour's, by shuffle), shifted by the constant misalignment r.
+        // Loads stay 16-byte vectors with U steps in flight; an aligned source vector always
+        // holds at least one byte of the range, so no load leaves the range's pages.
+        const uint64_t head = (16 - (d & 15)) & 15;
         if (uint64_t(lane) < head) dst[lane] = src[lane];
         dst += head;
         src += head;
         n -= head;
-        const uint64_t nw = n >> 2;
-        uint32_t *dw = reinterpret_cast<uint32_t *>(dst);
-        const uint32_t *sw = reinterpret_cast<const uint32_t *>(src);
-        for (uint64_t i = lane; i < nw; i += 32) dw[i] = sw[i];
-        const uint64_t done = nw << 2;
+        const uint32_t r = uint32_t(reinterpret_cast<uintptr_t>(src) & 15);  // != 0
+        const uint4 *sa = reinterpret_cast<const uint4 *>(src - r);
+        uint4 *dv = reinterpret_cast<uint4 *>(dst);
+        const uint64_t nvec = n >> 4;
+        constexpr int U = 2;
+        for (uint64_t j0 = 0; j0 < nvec; j0 += 32 * U) {
+            uint4 v[U], nx[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const uint64_t j = j0 + uint64_t(u) * 32 + lane;
+                const uint64_t base = j0 + uint64_t(u) * 32;
+                const uint64_t last = base + 31 < nvec ? base + 31 : nvec - 1;  // last vector of this step
+                if (j < nvec) v[u] = ld128(sa + j);
+                if (j == last) nx[u] = ld128(sa + j + 1);  // the step's last lane fetches its own next
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const uint64_t j = j0 + uint64_t(u) * 32 + lane;
+                const uint64_t base = j0 + uint64_t(u) * 32;
+                const uint64_t last = base + 31 < nvec ? base + 31 : nvec - 1;
+                uint4 t;
+                t.x = __shfl_down_sync(0xffffffffu, v[u].x, 1);
+                t.y = __shfl_down_sync(0xffffffffu, v[u].y, 1);
+                t.z = __shfl_down_sync(0xffffffffu, v[u].z, 1);
+                t.w = __shfl_down_sync(0xffffffffu, v[u].w, 1);
+                if (j == last) t = nx[u];
+                if (j < nvec) st128(dv + j, shift_join(v[u], t, r));
+            }
+        }
+        const uint64_t done = nvec << 4;
         if (uint64_t(lane) < n - done) dst[done + lane] = src[done + lane];
         return;
     }
@@ -211,7 +267,7 @@ __device__ void warp_copy(uint8_t *dst, const uint8_t *src, uint64_t n, int lane
 }
 
 // Copy stream bytes [off, off + len) of a WR: local segments <-> contiguous remote range.
-__device__ void copy_stream(const WrRec *rec, uint32_t nseg, uint64_t remote, bool to_remote,
+__device__ __noinline__ void copy_stream(const WrRec *rec, uint32_t nseg, uint64_t remote, bool to_remote,
                             uint64_t off, uint64_t len, int lane) {
     uint64_t seg_start = 0;
     for (uint32_t i = 0; i < nseg && len > 0; ++i) {
@@ -224,10 +280,7 @@ __device__ void copy_stream(const WrRec *rec, uint32_t nseg, uint64_t remote, bo
                                  __ldcg(reinterpret_cast<const unsigned long long *>(&rec->seg[i].local))) +
                              in;
             uint8_t *rem = reinterpret_cast<uint8_t *>(remote) + off;
-            if (to_remote)
-                warp_copy(rem, local, take, lane);
-            else
-                warp_copy(local, rem, take, lane);
+            warp_copy(to_remote ? rem : local, to_remote ? local : rem, take, lane);
             off += take;
             len -= take;
         }
@@ -263,7 +316,14 @@ struct CqCache {
     queue::RingHeader *ring;
     uint8_t *slots;
     uint32_t cap, stride;
+    unsigned long long *ready;
     uint64_t reserve, head, published;
+};
+
+// A warp's private statistics, folded into DevStats now and then (hot shared counters would
+// serialise every warp of the grid on one L2 line).  Kept in shared memory, not registers.
+struct WarpCounters {
+    unsigned long long n_chunks, n_miss, bytes, busy, n_inline, n_slow, t_slow, n_slot_miss, n_pub_wait, t_pub_wait;
 };
 
 struct Warp {
@@ -275,15 +335,15 @@ struct Warp {
     bool abort;
     // Private counters, folded into DevStats now and then (hot shared counters would serialise
     // every warp of the grid on one L2 line).
-    uint64_t n_chunks, n_miss, bytes, busy, n_inline;
+    WarpCounters *ctr;  // this warp's counters (shared memory, updated by lane 0)
     bool started;  // this warp stamped first_start_ns in this launch
-    CqCache cq;
+    CqCache *cq;  // lane 0's cache of the last CQ it produced into (shared memory)
     MrCacheEntry *mrc;  // this warp's two-entry MR cache (shared memory)
     volatile uint32_t *mirror;  // the CTA's shared copy of the active-job bitmap
     // Cached view of the QP this warp serviced last (see service_qp).
     DevQp *vq;
-    uint64_t vt, vhead, vissue, t_reserved;
-    QpView vv;
+    uint64_t vt, vhead, vissue, vtail, t_reserved;
+    QpView *vv;  // cached view of the QP serviced last (shared memory)
 };
 
 __device__ void record_error(Warp &w, uint32_t code) {
@@ -310,13 +370,14 @@ __device__ bool wait_eq_sys(const unsigned long long *p, uint64_t want, uint64_t
 // granted (0 when the CQ is full); *first receives the first slot's cursor.  The warp caches the
 // CQ's configuration and its last view of the cursors, so an uncontended reservation is one CAS.
 __device__ uint32_t reserve_cq(Warp &w, DevCq *cq, uint32_t want, uint64_t *first) {
-    CqCache &c = w.cq;
+    CqCache &c = *w.cq;
     if (c.cq != cq) {
         c.cq = cq;
         c.cap = ld_vol32(&cq->cfg.capacity);
         c.stride = ld_vol32(&cq->cfg.stride);
         c.ring = reinterpret_cast<queue::RingHeader *>(ld_vol(&cq->cfg.ring));
         c.slots = reinterpret_cast<uint8_t *>(ld_vol(&cq->cfg.slots));
+        c.ready = reinterpret_cast<unsigned long long *>(ld_vol(&cq->cfg.ready));
         c.reserve = ld_vol(&cq->st.reserve);
         c.head = ld_vol(&cq->st.head_seen);
         c.published = ~0ull;
@@ -346,25 +407,59 @@ __device__ uint32_t reserve_cq(Warp &w, DevCq *cq, uint32_t want, uint64_t *firs
     return 0;
 }
 
-// Write k CQEs into reserved slots [first, first + k) and publish them in cursor order (lane 0).
-// Returns false when the in-order publish wait ran out.
+// ---- CQ publication ---------------------------------------------------------------------------
+// A CQ may have many producers (warps on this and other GPUs).  Slots are reserved in order
+// (reserve_cq) but written by whoever reserved them; the ring tail must advance in slot order and
+// only over written slots.  DevCqState::published is a device-memory hint of the tail, and the
+// producer that owns slot `published` is the only one that may move the tail ("its turn"):
+//  * a producer writes its CQEs, fences them (system scope) and tags each of its slots s with
+//    s + 1 in the device-memory `ready` array;
+//  * it polls `published` (GPU memory, not the host ring over PCIe) until it reaches its slots;
+//    if a predecessor already moved the tail past them it is done;
+//  * on its turn it first reads the host tail until the predecessor's tail store has landed
+//    (usually at once), so tail stores are coherence-ordered and the tail never moves back; then
+//    it extends its range over every consecutively tagged slot after its own - waiting
+//    successors - and stores the host tail and the hint once for the whole batch.
+// A producer that stored the tail last and reserved the next slots (one producer streaming into
+// its CQ) skips the tags and both polls: fence, tail store, hint store.
 __device__ bool publish_cq(Warp &w, DevCq *cq, uint64_t first, const queue::Cqe *e, uint32_t k, uint64_t max_ns) {
-    CqCache &c = w.cq;
+    CqCache &c = *w.cq;
     for (uint32_t i = 0; i < k; ++i) {
         uint8_t *slot = c.slots + ((first + i) % c.cap) * c.stride;
         const uint4 *src = reinterpret_cast<const uint4 *>(&e[i]);
         st_vol128(slot, src[0]);
         st_vol128(slot + 16, src[1]);
     }
-    // The ring's tail is the in-order publish cursor: a producer publishes only after it has seen
-    // the tail reach its first slot, so the tail never moves backwards and the producer's fence is
-    // cumulative over every earlier producer's slots.  A warp that published the slots just below
-    // `first` itself (the common single-producer case) need not look.
-    if (c.published != first && !wait_eq_sys(reinterpret_cast<const unsigned long long *>(&c.ring->tail.value), first, max_ns)) return false;
-    // One system fence orders the WR payload stores and the CQE slots before the tail.
+    // One system fence orders the WR payload stores and the CQE slots before the tail (or the
+    // tags another producer publishes them by).
     asm volatile("fence.acq_rel.sys;" ::: "memory");
-    st_vol64(&c.ring->tail.value, first + k);
-    c.published = first + k;
+    uint64_t from = first;
+    if (c.published != first) {
+        for (uint32_t i = 0; i < k; ++i) st_vol64(&c.ready[(first + i) % c.cap], first + i + 1);
+        const uint64_t t0 = gtime();
+        uint32_t spins = 0;
+        uint64_t p;
+        while ((p = ld_acq_sys(&cq->st.published)) < first) {
+            if ((++spins & 63) == 0 && gtime() - t0 > max_ns) return false;
+            __nanosleep(32);
+        }
+        if (p >= first + k) {
+            if (w.lane == 0) w.ctr->n_pub_wait += 1;
+            if (w.lane == 0) w.ctr->t_pub_wait += gtime() - t0;
+            c.published = p;  // a predecessor published these slots
+            return true;
+        }
+        from = p;  // our turn (part of our range may already be out)
+        if (!wait_eq_sys(reinterpret_cast<const unsigned long long *>(&c.ring->tail.value), from, max_ns))
+            return false;
+        if (w.lane == 0) w.ctr->n_pub_wait += 1;
+        if (w.lane == 0) w.ctr->t_pub_wait += gtime() - t0;
+    }
+    uint64_t end = first + k;
+    while (end - from < c.cap && ld_acq_sys(&c.ready[end % c.cap]) == end + 1) ++end;
+    st_vol64(&c.ring->tail.value, end);
+    st_vol64(&cq->st.published, end);
+    c.published = end;
     return true;
 }
 
@@ -521,13 +616,16 @@ __device__ bool claim_chunk(Warp &w, JobRing *jr, uint32_t *bitmap, const volati
                     if (c + 1 == g.z) atomicAnd(&bitmap[wsel], ~(1u << b));  // all handed out
                 }
             }
+            // Every chunk of this job is handed out: drop it from the CTA's mirror so the other
+            // warps here stop trying it before the leader's next refresh.
+            if (!got) atomicAnd(const_cast<uint32_t *>(&w.mirror[wsel]), ~(1u << b));
         }
         w.rot = w.rot * 1664525u + 1013904223u;
     }
     w.rot = __shfl_sync(0xffffffffu, w.rot, 0);
     got = __shfl_sync(0xffffffffu, got, 0);
     if (!got) {
-        w.n_miss += 1;
+        if (w.lane == 0) w.ctr->n_miss += 1;
         return false;
     }
     __syncwarp();  // lane 0's acquire orders the other lanes' reads of the job below
@@ -571,21 +669,27 @@ __device__ void run_chunk(Warp &w, const Claim &cl) {
         atomicAdd(&rec->chunks_done, 1u);
         if (atomicAdd(&cl.job->done, 1u) + 1 == cl.n) atomicAdd(&cl.job->seq, 1ull);  // free the slot
     }
-    w.n_chunks += 1;
-    w.bytes += len;
-    w.busy += gtime() - t0;
+    if (w.lane == 0) w.ctr->n_chunks += 1;
+    if (w.lane == 0) w.ctr->bytes += len;
+    if (w.lane == 0) w.ctr->busy += gtime() - t0;
 }
 
 // Fold the warp's private counters into DevStats (lane 0).
 __device__ void flush_counters(Warp &w) {
     if (w.lane == 0) {
-        if (w.n_chunks) atomicAdd(&w.p->stats->chunks_run, (unsigned long long)w.n_chunks);
-        if (w.n_miss) atomicAdd(&w.p->stats->claim_misses, (unsigned long long)w.n_miss);
-        if (w.bytes) atomicAdd(&w.p->stats->bytes_moved, (unsigned long long)w.bytes);
-        if (w.busy) atomicAdd(&w.p->stats->busy_ns, (unsigned long long)w.busy);
-        if (w.n_inline) atomicAdd(&w.p->stats->inline_runs, (unsigned long long)w.n_inline);
+        WarpCounters &c = *w.ctr;
+        unsigned long long *dst[10] = {&w.p->stats->chunks_run, &w.p->stats->claim_misses, &w.p->stats->bytes_moved,
+                                       &w.p->stats->busy_ns, &w.p->stats->inline_runs, &w.p->stats->slow_wrs,
+                                       &w.p->stats->slow_issue_ns, &w.p->stats->job_slot_misses,
+                                       &w.p->stats->publish_waits, &w.p->stats->publish_wait_ns};
+        const unsigned long long val[10] = {c.n_chunks, c.n_miss, c.bytes, c.busy, c.n_inline,
+                                            c.n_slow, c.t_slow, c.n_slot_miss, c.n_pub_wait, c.t_pub_wait};
+#pragma unroll
+        for (int i = 0; i < 10; ++i)
+            if (val[i]) atomicAdd(dst[i], val[i]);
+        c = WarpCounters{};
     }
-    w.n_chunks = w.n_miss = w.bytes = w.busy = w.n_inline = 0;
+    __syncwarp();
 }
 
 // ---- per-QP service ----------------------------------------------------------------------------
@@ -722,7 +826,7 @@ __device__ void run_inline(Warp &w, WrRec *rec, const uint8_t *wqe, uint32_t op,
             memcpy(dst, &old, 8);
         }
         __syncwarp();
-        w.bytes += 8;
+        if (w.lane == 0) w.ctr->bytes += 8;
         return;
     }
     const uint32_t nseg = rec->nseg;
@@ -734,7 +838,7 @@ __device__ void run_inline(Warp &w, WrRec *rec, const uint8_t *wqe, uint32_t op,
         copy_stream(rec, nseg, remote, op != UGDR_WR_RDMA_READ, 0, total, w.lane);
     }
     __syncwarp();
-    w.bytes += total;
+    if (w.lane == 0) w.ctr->bytes += total;
 }
 
 // Retire finished WRs in order.  Lane i inspects WR head + i, so the ready prefix, the CQE list
@@ -987,6 +1091,7 @@ __device__ uint32_t issue_fast(Warp &w, DevQp *qp, const QpView &v, const uint8_
         slot = bcast(slot);
         if (slot < 0) {
             // No free slot: only the WRs before the first chunked one run now.
+            if (w.lane == 0) w.ctr->n_slot_miss += 1;
             count = __ffs(chunk_mask) - 1;
             chunk_mask = 0;
             chunked = false;
@@ -1020,6 +1125,7 @@ __device__ uint32_t issue_fast(Warp &w, DevQp *qp, const QpView &v, const uint8_
             for (uint64_t o = 0; o < len; ++o) dst[o] = src[o];
         }
     }
+    uint64_t lane_bytes = 0;
     if (j < count) {
         WrRec *rec = &qp->st.win[(issue0 + j) % kWindow];
         rec->wr_id = h->wr_id;
@@ -1035,10 +1141,12 @@ __device__ uint32_t issue_fast(Warp &w, DevQp *qp, const QpView &v, const uint8_
         rec->chunks_done = 0;
         rec->nchunks = nch;
         rec->signaled = (v.sig_all || (h->send_flags & UGDR_SEND_SIGNALED) != 0) ? 1u : 0u;
-        if (!chunked) w.bytes += len;
+        lane_bytes = chunked ? 0 : len;
         *out = LaneWr{h->wr_id, len, status, op, rec->signaled};
     }
     __syncwarp();
+    for (int o = 16; o > 0; o >>= 1) lane_bytes += __shfl_xor_sync(0xffffffffu, lane_bytes, o);
+    if (w.lane == 0) w.ctr->bytes += lane_bytes;
     if (chunk_mask) {
         publish_job(w, jr, bitmap, slot, gen, qp->st.win, uint32_t(issue0 % kWindow), count, start, total_chunks, cb);
         *chunked_out = true;
@@ -1060,7 +1168,7 @@ __device__ uint32_t service_qp(Warp &w, DevQp *qp, uint8_t *wqe_smem, queue::Cqe
     // writer of the QP's cursors, so the cached head / issue are authoritative.
     const uint64_t now0 = gtime();
     if (w.vq == qp && now0 - w.vt < 20000) {
-        return service_cached(w, qp, w.vv, wqe_smem, cqe_smem, jr, bitmap, nwarps);
+        return service_cached(w, qp, *w.vv, wqe_smem, cqe_smem, jr, bitmap, nwarps);
     }
     if (!ld_vol32(&qp->cfg.active)) {
         w.vq = nullptr;
@@ -1091,10 +1199,13 @@ __device__ uint32_t service_qp(Warp &w, DevQp *qp, uint8_t *wqe_smem, queue::Cqe
     }
     w.vhead = ld_vol(&qp->st.sq_head);
     w.vissue = ld_vol(&qp->st.sq_issue);
+    w.vtail = w.vissue;
     w.vq = qp;
-    w.vv = v;
+    __syncwarp();
+    if (w.lane == 0) *w.vv = v;
+    __syncwarp();
     w.vt = now0;
-    return service_cached(w, qp, w.vv, wqe_smem, cqe_smem, jr, bitmap, nwarps);
+    return service_cached(w, qp, *w.vv, wqe_smem, cqe_smem, jr, bitmap, nwarps);
 }
 
 __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_smem, queue::Cqe *cqe_smem,
@@ -1162,15 +1273,21 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
     }
     if (v.state != UGDR_QPS_RTS) return work;
 
-    // Issue: one tail read, one lane-parallel fetch of every WQE that fits the window and the
-    // staging buffer.
-    uint64_t tail = 0;
-    if (w.lane == 0) tail = ld_acq_sys(&v.sq->tail.value);
-    tail = bcast64(tail);
+    // Issue: one lane-parallel fetch of every WQE that fits the window and the staging buffer.
+    // The SQ tail (a PCIe read) is read only when the window has room and the tail seen last
+    // does not already cover it: WQEs below a tail acquired earlier are as valid now.
     const uint64_t head = w.vhead, issue0 = w.vissue;
+    uint64_t room = kWindow - (issue0 - head);
+    if (room > kWqeStage / v.sq_stride) room = kWqeStage / v.sq_stride;
+    if (room == 0) return work;
+    if (w.vtail < issue0 + room) {
+        uint64_t tail = 0;
+        if (w.lane == 0) tail = ld_acq_sys(&v.sq->tail.value);
+        w.vtail = bcast64(tail);
+    }
+    const uint64_t tail = w.vtail;
     uint64_t avail = tail > issue0 ? tail - issue0 : 0;
-    if (avail > kWindow - (issue0 - head)) avail = kWindow - (issue0 - head);
-    if (avail > kWqeStage / v.sq_stride) avail = kWqeStage / v.sq_stride;
+    if (avail > room) avail = room;
     if (avail == 0) return work;
     const uint64_t t_fetch0 = gtime();
     const uint32_t nbytes = uint32_t(avail) * v.sq_stride;
@@ -1198,6 +1315,7 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
         WrRec *rec = &qp->st.win[issue % kWindow];
         uint32_t status;
         uint64_t total, remote;
+        const uint64_t t_stage = gtime();
         stage_wr(w, v, wqe, rec, &status, &total, &remote);
         const queue::SendWqe *h = reinterpret_cast<const queue::SendWqe *>(wqe);
         const uint32_t op = h->opcode;
@@ -1212,7 +1330,10 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
             if (w.lane == 0) slot = take_job_slot(jr, w.gwarp + uint32_t(issue), &gen);
             slot = bcast(slot);
             gen = bcast64(gen);
-            if (slot < 0) break;  // no job slot: retry on a later pass
+            if (slot < 0) {  // no job slot: retry on a later pass
+                if (w.lane == 0) w.ctr->n_slot_miss += 1;
+                break;
+            }
         }
 
         // Responder RQ for WRITE_WITH_IMM (RNR when empty).
@@ -1278,6 +1399,8 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
                 publish_job(w, jr, bitmap, slot, gen, qp->st.win, uint32_t(issue % kWindow), 1u, 0u, n, chunk);
             }
         }
+        if (w.lane == 0) w.ctr->n_slow += 1;
+        if (w.lane == 0) w.ctr->t_slow += gtime() - t_stage;
         ++issued;
         if (status != UGDR_WC_SUCCESS) break;  // stop issuing behind an error
     }
@@ -1290,7 +1413,7 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
         }
         __syncwarp();
         w.vissue = issue0 + issued;
-        w.n_inline += inline_ran;
+        if (w.lane == 0) w.ctr->n_inline += inline_ran;
         work += uint32_t(issued);
         if (head == issue0 && issued == fast_n && !fast_chunked) {
             // Only this fast batch is in flight and every lane still holds its WR: retire it
@@ -1331,6 +1454,9 @@ __global__ void __launch_bounds__(kThreads, 1) executor_kernel(ExecParams p) {
     __shared__ __align__(16) uint8_t wqe_buf[kWarps][kWqeStage];
     __shared__ __align__(16) queue::Cqe cqe_buf[kWarps][kWindow];
     __shared__ __align__(16) MrCacheEntry mr_cache[kWarps][2];
+    __shared__ WarpCounters counters[kWarps];
+    __shared__ CqCache cq_cache[kWarps];
+    __shared__ QpView qp_view[kWarps];
     __shared__ volatile uint32_t s_bits[32];
     __shared__ volatile uint32_t s_slots, s_exit, s_work;
     Warp w;
@@ -1340,9 +1466,12 @@ __global__ void __launch_bounds__(kThreads, 1) executor_kernel(ExecParams p) {
     w.gwarp = blockIdx.x * kWarps + w.wi;
     w.rot = w.gwarp * 2654435761u;
     w.abort = false;
-    w.n_chunks = w.n_miss = w.bytes = w.busy = w.n_inline = 0;
+    w.ctr = &counters[w.wi];
+    if (w.lane == 0) counters[w.wi] = WarpCounters{};
     w.started = false;
-    w.cq.cq = nullptr;
+    w.cq = &cq_cache[w.wi];
+    w.vv = &qp_view[w.wi];
+    if (w.lane == 0) w.cq->cq = nullptr;
     w.vq = nullptr;
     w.mrc = mr_cache[w.wi];
     w.mirror = s_bits;

@@ -97,6 +97,7 @@ class GpuEngine final : public control::Engine {
     HostCtrl *ctrl_ = nullptr;  // mapped pinned host memory
     HostCtrl *ctrl_dev_ = nullptr;
     std::vector<uint32_t> free_qp_slots_, free_cq_slots_;
+    std::vector<unsigned long long *> cq_ready_ = std::vector<unsigned long long *>(kMaxCqsPerEngine, nullptr);
     uint32_t next_qp_slot_ = 0, next_cq_slot_ = 0, qp_slot_bound_ = 0;
     std::vector<QpEntry> qps_host_;
     bool running_ = false;
@@ -122,6 +123,8 @@ GpuEngine::~GpuEngine() {
     cudaFree(mrs_);
     cudaFree(qps_);
     cudaFree(cqs_);
+    for (unsigned long long *r : cq_ready_)
+        if (r) cudaFree(r);
     cudaFree(jobs_);
     cudaFree(stats_);
     if (ctrl_) cudaFreeHost(ctrl_);
@@ -219,16 +222,29 @@ int GpuEngine::attach_cq(control::Cq &cq) {
         return ENOMEM;
     }
     DevCq d{};
+    const uint32_t cap = cq.ring.geometry().capacity;
+    if (cudaMalloc(reinterpret_cast<void **>(&d.cfg.ready), sizeof(unsigned long long) * cap) != cudaSuccess ||
+        cudaMemset(d.cfg.ready, 0, sizeof(unsigned long long) * cap) != cudaSuccess) {
+        (void)cudaGetLastError();
+        if (d.cfg.ready) cudaFree(d.cfg.ready);
+        cudaHostUnregister(cq.ring.mapping());
+        free_cq_slots_.push_back(slot);
+        return ENOMEM;
+    }
     d.cfg.ring = static_cast<queue::RingHeader *>(dev);
     d.cfg.slots = static_cast<uint8_t *>(dev) + queue::kRingHeaderBytes;
     d.cfg.capacity = cq.ring.geometry().capacity;
     d.cfg.stride = cq.ring.geometry().stride;
     d.cfg.valid = 1;
+    d.st.reserve = d.st.published = cq.ring.tail();
+    d.st.head_seen = cq.ring.head();
     if (int rc = copy_to_device(&cqs_[slot], &d, sizeof(d)); rc != 0) {
+        cudaFree(d.cfg.ready);
         cudaHostUnregister(cq.ring.mapping());
         free_cq_slots_.push_back(slot);
         return rc;
     }
+    cq_ready_[slot] = d.cfg.ready;
     cq.engine_block = &cqs_[slot];
     return 0;
 }
@@ -243,7 +259,10 @@ void GpuEngine::detach_cq(control::Cq &cq) noexcept {
         copy_to_device(d, &zero, sizeof(zero));
         set_device();
         cudaHostUnregister(cq.ring.mapping());
-        free_cq_slots_.push_back(uint32_t(d - cqs_));
+        const uint32_t slot = uint32_t(d - cqs_);
+        cudaFree(cq_ready_[slot]);
+        cq_ready_[slot] = nullptr;
+        free_cq_slots_.push_back(slot);
         cq.engine_block = nullptr;
     }
     resume();
@@ -494,6 +513,11 @@ int GpuEngine::stats(control::EngineStats *out, bool reset) {
     out->fast_exec_ns = st.fast_exec_ns;
     out->fast_reserve_ns = st.fast_reserve_ns;
     out->fast_publish_ns = st.fast_publish_ns;
+    out->slow_wrs = st.slow_wrs;
+    out->slow_issue_ns = st.slow_issue_ns;
+    out->job_slot_misses = st.job_slot_misses;
+    out->publish_waits = st.publish_waits;
+    out->publish_wait_ns = st.publish_wait_ns;
     if (reset) {
         // Counters only (a running kernel may race a few increments into the fresh window).
         cudaMemsetAsync(stats_, 0, offsetof(DevStats, last_work_ns), ctl_stream_);

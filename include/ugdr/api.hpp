@@ -263,6 +263,10 @@ typedef struct ugdr_x_engine_stats {
     uint64_t busy_ns;        /* summed warp time spent copying chunks */
     /* small-WR fast path (lane-parallel batches): batch count and summed phase times */
     uint64_t fast_batches, fast_fetch_ns, fast_exec_ns, fast_reserve_ns, fast_publish_ns;
+    /* WRs staged one per warp round (multi-SGE, WRITE_WITH_IMM, atomics) and their summed issue
+     * time; issue attempts that found no free job slot; CQ publishes that had to wait for their turn
+     * behind other producers of the same CQ, and the summed wait */
+    uint64_t slow_wrs, slow_issue_ns, job_slot_misses, publish_waits, publish_wait_ns;
 } ugdr_x_engine_stats;
 
 int ugdr_x_query_engine_stats(ugdr_context *context, ugdr_x_engine_stats *stats,

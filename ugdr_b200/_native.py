@@ -196,6 +196,11 @@ class EngineStats(C.Structure):
         ("fast_exec_ns", C.c_uint64),
         ("fast_reserve_ns", C.c_uint64),
         ("fast_publish_ns", C.c_uint64),
+        ("slow_wrs", C.c_uint64),
+        ("slow_issue_ns", C.c_uint64),
+        ("job_slot_misses", C.c_uint64),
+        ("publish_waits", C.c_uint64),
+        ("publish_wait_ns", C.c_uint64),
     ]
 
 
