@@ -307,10 +307,57 @@ __device__ __forceinline__ RowRef resolve_row(const PeerSet &ps, const int32_t *
     return ref;
 }
 
+// 32-byte vector loads / stores (sm_100 256-bit global accesses).
+struct alignas(32) V256 {
+    uint32_t w[8];
+};
+__device__ __forceinline__ V256 ld256(const void *p) {
+    V256 v;
+    asm volatile("ld.global.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3]), "=r"(v.w[4]), "=r"(v.w[5]),
+                   "=r"(v.w[6]), "=r"(v.w[7])
+                 : "l"(p));
+    return v;
+}
+__device__ __forceinline__ void st256(void *p, const V256 &v) {
+    asm volatile("st.global.v8.u32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(v.w[0]), "r"(v.w[1]),
+                 "r"(v.w[2]), "r"(v.w[3]), "r"(v.w[4]), "r"(v.w[5]), "r"(v.w[6]), "r"(v.w[7])
+                 : "memory");
+}
+
+// One row copied by a warp: 32-byte vectors (4 in flight per lane) when both ends and the length
+// are 32-byte aligned, else 16-byte vectors (8 in flight).
+__device__ __forceinline__ void warp_copy_row(uint8_t *dst, const uint8_t *src, uint64_t bytes, int lane) {
+    if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src) | bytes) & 31) == 0) {
+        const uint64_t nv = bytes / 32;
+        uint64_t i = lane;
+        for (; i + 3 * 32 < nv; i += 4 * 32) {
+            V256 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = ld256(src + (i + u * 32) * 32);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) st256(dst + (i + u * 32) * 32, v[u]);
+        }
+        for (; i < nv; i += 32) st256(dst + i * 32, ld256(src + i * 32));
+        return;
+    }
+    const uint64_t nv = bytes / 16;
+    uint64_t i = lane;
+    for (; i + 7 * 32 < nv; i += 8 * 32) {
+        uint4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = ld128(src + (i + u * 32) * 16);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) st128(dst + (i + u * 32) * 16, v[u]);
+    }
+    for (; i < nv; i += 32) st128(dst + i * 16, ld128(src + i * 16));
+}
+
 // Dispatch: row (t, k) -> recv buffer of the expert's owner at row gbase[e] + pos[(t, k)]
 // (`gbase[e]` = first row of expert e's group in its owner's buffer for rows of THIS rank).
-// A warp takes 32 consecutive rows at a time; each row is copied with 8 vectors in flight per
-// lane, so a 14 KiB row is 3.5 load rounds and the stores stream over NVLink behind them.
+// Rows are interleaved over all warps of the grid (warp w takes rows w, w + W, ...), so work
+// stays balanced whatever the row count; each warp resolves its next 32 rows lane-parallel in
+// one round of loads, then copies them one by one.
 __global__ void __launch_bounds__(512) dispatch_kernel(PeerSet ps, const uint8_t *x, uint64_t row_bytes,
                                                        const int32_t *idx, const int32_t *pos,
                                                        const int64_t *gbase, uint64_t rows, int topk,
@@ -319,25 +366,17 @@ __global__ void __launch_bounds__(512) dispatch_kernel(PeerSet ps, const uint8_t
     const int lane = threadIdx.x & 31;
     const uint64_t warp = (uint64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const uint64_t nwarps = (uint64_t(gridDim.x) * blockDim.x) >> 5;
-    const uint64_t nv = row_bytes / 16;
-    for (uint64_t r0 = warp * 32; r0 < rows; r0 += nwarps * 32) {
-        const RowRef mine = resolve_row(ps, idx, pos, gbase, nullptr, r0 + lane, r0 + lane < rows, exp_per_rank,
+    for (uint64_t base = warp; base < rows; base += 32 * nwarps) {
+        const uint64_t mine_row = base + uint64_t(lane) * nwarps;
+        const RowRef mine = resolve_row(ps, idx, pos, gbase, nullptr, mine_row, mine_row < rows, exp_per_rank,
                                         recv_off, recv_rows, row_bytes);
-        const uint64_t nr = min(uint64_t(32), rows - r0);
-        for (uint64_t j = 0; j < nr; ++j) {
-            uint4 *dst = reinterpret_cast<uint4 *>(
-                __shfl_sync(0xffffffffu, reinterpret_cast<uint64_t>(mine.ptr), int(j)));
+        for (int j = 0; j < 32; ++j) {
+            const uint64_t r = base + uint64_t(j) * nwarps;
+            if (r >= rows) break;
+            uint8_t *dst = reinterpret_cast<uint8_t *>(
+                __shfl_sync(0xffffffffu, reinterpret_cast<uint64_t>(mine.ptr), j));
             if (dst == nullptr) continue;
-            const uint4 *src = reinterpret_cast<const uint4 *>(x + ((r0 + j) / topk) * row_bytes);
-            uint64_t i = lane;
-            for (; i + 7 * 32 < nv; i += 8 * 32) {
-                uint4 v[8];
-#pragma unroll
-                for (int u = 0; u < 8; ++u) v[u] = ld128(src + i + u * 32);
-#pragma unroll
-                for (int u = 0; u < 8; ++u) st128(dst + i + u * 32, v[u]);
-            }
-            for (; i < nv; i += 32) st128(dst + i, ld128(src + i));
+            warp_copy_row(dst, x + (r / topk) * row_bytes, row_bytes, lane);
         }
     }
     end_barrier(ps, epoch, kSlotDispatch, max_ns);
