@@ -18,6 +18,9 @@
 
 #include <cuda_runtime_api.h>
 
+#include <dirent.h>
+#include <unistd.h>
+
 #include <algorithm>
 #include <cmath>
 #include <chrono>
@@ -41,6 +44,8 @@ struct Opts {
     uint64_t min_bytes = 8, max_bytes = 1ull << 30, qd = 64, bytes_per_size = 8ull << 30;
     uint64_t batch = 32, wrs = 4000000;
     uint64_t qps = 64, depth = 128, sges = 16, rounds = 3, seed = 7;
+    std::string sync_dir;  // stress: start / finish barrier shared by concurrent clients
+    uint64_t sync_n = 0;
 };
 
 [[noreturn]] void die(const char *what, int rc) {
@@ -371,9 +376,81 @@ struct StressSide {
     ugdr_cq *cq = nullptr;
 };
 
+ugdr_device *any_device(ugdr_device **list, int n, int gpu) {
+    if (gpu >= 0) return gpu_device(list, n, gpu);
+    for (int i = 0; i < n; ++i) {
+        ugdr_x_device_info info;
+        if (ugdr_x_query_device(list[i], &info) == 0 && info.kind == 0) return list[i];
+    }
+    std::fprintf(stderr, "ugdr_perf: daemon has no host-memory device\n");
+    std::exit(1);
+}
+
+// Memory of one side: device memory of GPU `gpu`, or (gpu < 0) a ugdr host buffer served by the
+// daemon's CPU engine.
+void *mem_alloc(int gpu, uint64_t bytes) {
+    void *p = nullptr;
+    if (gpu < 0) {
+        p = ugdr_x_alloc_host(bytes);
+        if (!p) die("ugdr_x_alloc_host", errno);
+        std::memset(p, 0, bytes);
+        return p;
+    }
+    cudaSetDevice(gpu);
+    if (cudaMalloc(&p, bytes) != cudaSuccess) die("cudaMalloc", ENOMEM);
+    cudaMemset(p, 0, bytes);
+    return p;
+}
+void mem_zero(int gpu, void *p, uint64_t bytes) {
+    if (gpu < 0) {
+        std::memset(p, 0, bytes);
+        return;
+    }
+    cudaSetDevice(gpu);
+    cudaMemset(p, 0, bytes);
+    cudaDeviceSynchronize();
+}
+void mem_read(int gpu, void *host, const void *p, uint64_t bytes) {
+    if (gpu < 0) {
+        std::memcpy(host, p, bytes);
+        return;
+    }
+    cudaSetDevice(gpu);
+    cudaMemcpy(host, p, bytes, cudaMemcpyDeviceToHost);
+}
+void mem_write(int gpu, void *p, const void *host, uint64_t bytes) {
+    if (gpu < 0) {
+        std::memcpy(p, host, bytes);
+        return;
+    }
+    cudaSetDevice(gpu);
+    cudaMemcpy(p, host, bytes, cudaMemcpyHostToDevice);
+}
+
+// Cross-process start / finish barrier for concurrent stress clients: every process creates
+// <dir>/<phase>.<pid> and waits (bounded) until `n` such files exist.
+void sync_phase(const std::string &dir, uint64_t n, const char *phase) {
+    if (dir.empty() || n <= 1) return;
+    const std::string mine = dir + "/" + phase + "." + std::to_string(getpid());
+    if (FILE *f = std::fopen(mine.c_str(), "w")) std::fclose(f);
+    const auto deadline = Clock::now() + std::chrono::seconds(600);
+    for (;;) {
+        uint64_t seen = 0;
+        if (DIR *d = opendir(dir.c_str())) {
+            const size_t pl = std::strlen(phase);
+            while (dirent *e = readdir(d))
+                if (std::strncmp(e->d_name, phase, pl) == 0 && e->d_name[pl] == '.') ++seen;
+            closedir(d);
+        }
+        if (seen >= n) return;
+        if (Clock::now() > deadline) die("stress sync barrier", ETIMEDOUT);
+        std::this_thread::sleep_for(std::chrono::milliseconds(2));
+    }
+}
+
 StressSide open_side(ugdr_device **list, int n, int gpu, int cqe) {
     StressSide s;
-    s.ctx = ugdr_open_device(gpu_device(list, n, gpu));
+    s.ctx = ugdr_open_device(any_device(list, n, gpu));
     if (!s.ctx) die("ugdr_open_device", errno);
     s.pd = ugdr_alloc_pd(s.ctx);
     s.cq = ugdr_create_cq(s.ctx, cqe, nullptr, nullptr, 0);
@@ -382,9 +459,7 @@ StressSide open_side(ugdr_device **list, int n, int gpu, int cqe) {
 }
 
 ugdr_mr *dev_mr(ugdr_pd *pd, int gpu, uint64_t bytes, int access, void **buf) {
-    cudaSetDevice(gpu);
-    if (cudaMalloc(buf, bytes) != cudaSuccess) die("cudaMalloc", ENOMEM);
-    cudaMemset(*buf, 0, bytes);
+    *buf = mem_alloc(gpu, bytes);
     ugdr_mr *mr = ugdr_reg_mr(pd, *buf, bytes, access);
     if (!mr) die("ugdr_reg_mr", errno);
     return mr;
@@ -404,10 +479,12 @@ int run_stress(const Opts &o) {
     void *src = nullptr, *res = nullptr, *dst = nullptr, *ctr = nullptr;
     ugdr_mr *src_mr = dev_mr(rq.pd, o.src_gpu, src_bytes, UGDR_ACCESS_LOCAL_WRITE, &src);
     ugdr_mr *res_mr = dev_mr(rq.pd, o.src_gpu, per_round * 8, UGDR_ACCESS_LOCAL_WRITE, &res);
-    fill(src, src_bytes, o.seed, o.src_gpu);
     std::vector<uint8_t> host_src(src_bytes);
-    cudaSetDevice(o.src_gpu);
-    cudaMemcpy(host_src.data(), src, src_bytes, cudaMemcpyDeviceToHost);
+    {
+        std::mt19937_64 fr(o.seed);
+        for (auto &x : host_src) x = uint8_t(fr());
+    }
+    mem_write(o.src_gpu, src, host_src.data(), src_bytes);
     // Responder memory: gather destination (sized for the largest possible round) and counters.
     const uint64_t dst_bytes = per_round * nsge * 65536ull / 2 + (1 << 20);
     ugdr_mr *dst_mr = dev_mr(rs.pd, o.dst_gpu, dst_bytes, UGDR_ACCESS_LOCAL_WRITE | UGDR_ACCESS_REMOTE_WRITE, &dst);
@@ -540,9 +617,8 @@ int run_stress(const Opts &o) {
             if (k > 0)
                 if (int rc = ugdr_post_recv(rsp[q], &rwrs[uint64_t(q) * depth], &bad)) die("ugdr_post_recv", rc);
         }
-        cudaSetDevice(o.dst_gpu);
-        cudaMemset(dst, 0, dst_off);
-        cudaDeviceSynchronize();
+        mem_zero(o.dst_gpu, dst, dst_off);
+        if (round == 0) sync_phase(o.sync_dir, o.sync_n, "ready");
         // ---- post (timed: the posting rate) and complete (timed: the completion rate) ----
         const auto t0 = Clock::now();
         for (uint32_t q = 0; q < nq; ++q) {
@@ -582,22 +658,19 @@ int run_stress(const Opts &o) {
         total_wrs += per_round;
         // Compare-swap results: each old value is the chain position known at build time.
         std::vector<uint64_t> olds(per_round);
-        cudaSetDevice(o.src_gpu);
-        cudaMemcpy(olds.data(), res, per_round * 8, cudaMemcpyDeviceToHost);
+        mem_read(o.src_gpu, olds.data(), res, per_round * 8);
         for (uint64_t w = 0; w < per_round; ++w)
             if (cas_expect[w] != ~0ull && olds[w] != cas_expect[w]) ++bad_cas;
         std::fill(cas_expect.begin(), cas_expect.end(), ~0ull);
         // ---- verify every gathered byte ----
         std::vector<uint8_t> got_dst(dst_off);
-        cudaSetDevice(o.dst_gpu);
-        cudaMemcpy(got_dst.data(), dst, dst_off, cudaMemcpyDeviceToHost);
+        mem_read(o.dst_gpu, got_dst.data(), dst, dst_off);
         for (const Span &sp : spans)
             if (std::memcmp(got_dst.data() + sp.dst, expect.data() + sp.dst, sp.len) != 0) bad_bytes += 1;
     }
     // Counters: fetch-add sums and compare-swap chain lengths.
     std::vector<uint64_t> ctr_host(kCounters);
-    cudaSetDevice(o.dst_gpu);
-    cudaMemcpy(ctr_host.data(), ctr, kCounters * 8, cudaMemcpyDeviceToHost);
+    mem_read(o.dst_gpu, ctr_host.data(), ctr, kCounters * 8);
     uint64_t bad_ctr = 0;
     for (uint64_t i = 0; i < kCounters; ++i)
         if (ctr_host[i] != (i < kFaaCounters ? faa_expect[i] : cas_seen[i])) ++bad_ctr;
@@ -626,6 +699,8 @@ int run_stress(const Opts &o) {
                 "\"correct\": %s}\n",
                 o.src_gpu, o.dst_gpu, nq, depth, nsge, (unsigned long long)total_wrs, post_mops, run_mops,
                 double(total_bytes) / run_s / 1e9, ok ? "true" : "false");
+    std::fflush(stdout);
+    sync_phase(o.sync_dir, o.sync_n, "done");  // nobody tears down while others still run
     return ok ? 0 : 2;
 }
 
@@ -658,6 +733,8 @@ int main(int argc, char **argv) {
         else if (k == "--sges") o.sges = parse_size(v);
         else if (k == "--rounds") o.rounds = parse_size(v);
         else if (k == "--seed") o.seed = parse_size(v);
+        else if (k == "--sync-dir") o.sync_dir = v;
+        else if (k == "--sync-n") o.sync_n = parse_size(v);
         else {
             std::fprintf(stderr, "ugdr_perf: unknown option %s\n", k.c_str());
             return 2;

@@ -220,3 +220,25 @@ def test_cli_doctor_reports_the_build():
     rep = doctor()
     assert rep["libugdr"] and rep["daemon"]
     assert "gpus" in rep or "torch_error" in rep
+
+
+def test_config3_stress_on_the_host_engine():
+    """BASELINE configs[3] semantics on the host-memory engine: 16-SGE WRITE / WRITE_WITH_IMM with
+    log-uniform SGE sizes, fetch-add and compare-swap on a 4096-entry counter array; every byte,
+    immediate, CAS result and counter is checked by ugdr_perf."""
+    from ugdr_b200.utils.perf import run
+
+    out = run(["stress", "--src-gpu", "-1", "--dst-gpu", "-1", "--qps", "16", "--depth", "64", "--sges", "16",
+               "--rounds", "2"], gpus=0, timeout=300)
+    assert out and out[-1]["correct"] and out[-1]["wrs"] == 2048, out
+
+
+def test_concurrent_stress_clients_meet_at_the_barriers():
+    """Two stress clients against one daemon run their rounds between a shared start and finish
+    barrier (the stress-all launcher's protocol) and both verify."""
+    from ugdr_b200.utils.perf import stress_all
+
+    res = stress_all(0, ["--qps", "8", "--depth", "32", "--sges", "16", "--rounds", "2"], timeout=300,
+                     host_clients=2)
+    agg = res["aggregate"]
+    assert agg["correct"] and agg["clients"] == 2 and agg["wrs"] == 2 * 2 * 8 * 32, agg

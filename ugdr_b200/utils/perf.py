@@ -39,18 +39,28 @@ def run(args: list[str], gpus: int | None = None, timeout: float = 1800) -> list
     return [json.loads(line) for line in lines if line.startswith("{")]
 
 
-def stress_all(gpus: int, extra: list[str], timeout: float = 1800) -> dict:
+def stress_all(gpus: int, extra: list[str], timeout: float = 1800, host_clients: int = 2) -> dict:
     """BASELINE configs[3] on every ordered GPU pair at once: one daemon owning `gpus` GPUs and
-    one ugdr_perf stress client per (src, dst) pair, all running concurrently.  Returns the
-    per-pair JSON results and the aggregate rates."""
+    one ugdr_perf stress client per (src, dst) pair, all running concurrently.  The clients meet
+    at a start barrier after their set-up and at a finish barrier before their tear-down, so the
+    timed rounds overlap and no client's tear-down (which quiesces executors) lands inside
+    another's rounds.  With gpus == 0 the `host_clients` clients use the host-memory engine.
+    Returns the per-pair JSON results and aggregates: WRs and bytes over the slowest client's
+    time, and the summed posting rate."""
+    import tempfile
+
     exe = N.LIB_DIR / "ugdr_perf"
-    pairs = [(a, b) for a in range(gpus) for b in range(gpus) if a != b] or [(0, 0)]
+    if gpus > 0:
+        pairs = [(a, b) for a in range(gpus) for b in range(gpus) if a != b] or [(0, 0)]
+    else:
+        pairs = [(-1, -1)] * host_clients
     results = []
-    with V.Daemon(gpus=gpus) as d:
+    with tempfile.TemporaryDirectory(prefix="ugdr-stress-") as sync, V.Daemon(gpus=gpus) as d:
         env = dict(os.environ, UGDR_DAEMON_SOCKET=d.socket_path)
         procs = [subprocess.Popen([str(exe), "stress", "--src-gpu", str(a), "--dst-gpu", str(b), *extra,
-                                   "--seed", str(1 + a * 16 + b)], env=env, stdout=subprocess.PIPE,
-                                  stderr=subprocess.PIPE, text=True) for a, b in pairs]
+                                   "--seed", str(1 + i), "--sync-dir", sync, "--sync-n", str(len(pairs))],
+                                  env=env, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)
+                 for i, (a, b) in enumerate(pairs)]
         failed = []
         for (a, b), p in zip(pairs, procs):
             out, err = p.communicate(timeout=timeout)
@@ -60,11 +70,14 @@ def stress_all(gpus: int, extra: list[str], timeout: float = 1800) -> dict:
             results.extend(js)
         if failed:
             sys.stderr.write(d.log_text())
-    agg = {"benchmark": "ugdr_stress_all", "gpus": gpus, "pairs": len(pairs),
+    secs = [r["wrs"] / (r["complete_MWRps"] * 1e6) for r in results if r["complete_MWRps"] > 0]
+    slowest = max(secs) if secs else float("nan")
+    agg = {"benchmark": "ugdr_stress_all", "gpus": gpus, "clients": len(pairs),
            "wrs": sum(r["wrs"] for r in results),
-           "complete_MWRps_sum": round(sum(r["complete_MWRps"] for r in results), 3),
+           "complete_MWRps": round(sum(r["wrs"] for r in results) / slowest / 1e6, 3) if secs else None,
+           "GBps": round(sum(r["GBps"] * t for r, t in zip(results, secs)) / slowest, 3) if secs else None,
            "post_MWRps_sum": round(sum(r["post_MWRps"] for r in results), 3),
-           "GBps_sum": round(sum(r["GBps"] for r in results), 3),
+           "slowest_client_s": round(slowest, 4) if secs else None,
            "correct": bool(results) and not failed and all(r["correct"] for r in results),
            "failed": failed}
     return {"pairs": results, "aggregate": agg}
@@ -78,7 +91,7 @@ if __name__ == "__main__":
         g = int(argv[i + 1])
         del argv[i:i + 2]
     if argv and argv[0] == "stress-all":
-        res = stress_all(g or 2, argv[1:])
+        res = stress_all(2 if g is None else g, argv[1:])
         for r in res["pairs"]:
             print(json.dumps(r))
         print(json.dumps(res["aggregate"]))
