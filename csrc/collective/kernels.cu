@@ -22,7 +22,6 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
-#include <stdlib.h>
 
 namespace ugdr::coll {
 namespace {
@@ -511,17 +510,10 @@ int launch_allreduce_bf16(const PeerSet &ps, uint64_t offset, uint64_t count, ui
 int launch_allreduce_bf16_nvls(const PeerSet &ps, void *mc, uint64_t offset, uint64_t count, uint64_t epoch,
                                int ctas, uint64_t max_ns, cudaStream_t s) {
     if (mc == nullptr || count % 8 != 0 || offset % 16 != 0) return int(cudaErrorInvalidValue);
-    static const int unroll = [] {
-        const char *e = getenv("UGDR_NVLS_UNROLL");
-        return e ? atoi(e) : 4;
-    }();
-    uint8_t *base = static_cast<uint8_t *>(mc) + offset;
-    if (unroll >= 8)
-        allreduce_nvls_kernel<8><<<ctas, 512, 0, s>>>(ps, base, count / 8, epoch, max_ns);
-    else if (unroll <= 2)
-        allreduce_nvls_kernel<2><<<ctas, 512, 0, s>>>(ps, base, count / 8, epoch, max_ns);
-    else
-        allreduce_nvls_kernel<4><<<ctas, 512, 0, s>>>(ps, base, count / 8, epoch, max_ns);
+    // Four 16-byte vectors in flight per thread, one CTA per SM: the fastest of the measured
+    // settings on 8 B200, 1 GiB (unroll 4: 2.27 ms at 148 CTAs, 3.26 ms at 296; unroll 8:
+    // 2.46 ms at 148, 2.98 ms at 296).
+    allreduce_nvls_kernel<4><<<ctas, 512, 0, s>>>(ps, static_cast<uint8_t *>(mc) + offset, count / 8, epoch, max_ns);
     return int(cudaGetLastError());
 }
 
