@@ -4,6 +4,7 @@
 //   ugdr_perf latency  --src-gpu A --dst-gpu B --bytes N --iters K        QD1 post_send -> poll_cq
 //   ugdr_perf bw       --src-gpu A --dst-gpu B --op write|read --min 8 --max 1G --qd 64 --bytes-per-size T
 //   ugdr_perf posting  --batch B --wrs N                                    post_send into the SQ ring
+//   ugdr_perf plumbing --wrs 10000                                          BASELINE configs[0] (host engine)
 //   ugdr_perf stress   --src-gpu A --dst-gpu B --qps 64 --depth 128 --sges 16 --rounds R
 //                      verbs-feature stress: per QP an interleave of
 //                      16-SGE WRITE and WRITE_WITH_IMM (SGE sizes log-uniform in 64 B..64 KiB,
@@ -474,6 +475,80 @@ ugdr_mr *dev_mr(ugdr_pd *pd, int gpu, uint64_t bytes, int access, void **buf) {
     return mr;
 }
 
+// ---- CPU-only plumbing -------------------------------------------------------
+
+// One client and the daemon's host-memory engine: 1 PD, two 1 MiB host MRs, one QP of depth
+// 128, one CQ; `wrs` RDMA_WRITEs of one 4 KiB SGE at seeded random 4 KiB-aligned offsets, with
+// payload bytes uniform from seed 0; the CQ is polled until every completion arrives and the
+// destination is checked against a host model of the same writes.
+int run_plumbing(const Opts &o) {
+    int n = 0;
+    ugdr_device **list = ugdr_get_device_list(&n);
+    if (!list) die("ugdr_get_device_list", errno);
+    ugdr_context *ctx = ugdr_open_device(any_device(list, n, -1));
+    ugdr_pd *pd = ugdr_alloc_pd(ctx);
+    ugdr_cq *cq = ugdr_create_cq(ctx, 256, nullptr, nullptr, 0);
+    constexpr uint64_t kMr = 1 << 20, kWr = 4096;
+    uint8_t *src = static_cast<uint8_t *>(ugdr_x_alloc_host(kMr));
+    uint8_t *dst = static_cast<uint8_t *>(ugdr_x_alloc_host(kMr));
+    if (!ctx || !pd || !cq || !src || !dst) die("plumbing setup", errno);
+    std::mt19937_64 rng(0);
+    for (uint64_t i = 0; i < kMr; ++i) src[i] = uint8_t(rng());
+    std::memset(dst, 0, kMr);
+    ugdr_mr *smr = ugdr_reg_mr(pd, src, kMr, UGDR_ACCESS_LOCAL_WRITE);
+    ugdr_mr *dmr = ugdr_reg_mr(pd, dst, kMr, UGDR_ACCESS_LOCAL_WRITE | UGDR_ACCESS_REMOTE_WRITE);
+    ugdr_qp_init_attr ia{cq, cq, 128, 16, 1, 1, UGDR_QPT_RC, 0};
+    ugdr_qp *qp = ugdr_create_qp(pd, &ia), *peer = ugdr_create_qp(pd, &ia);
+    if (!smr || !dmr || !qp || !peer) die("plumbing setup", errno);
+    ugdr_qp_attr at{};
+    at.qp_state = UGDR_QPS_INIT;
+    at.qp_access_flags = UGDR_ACCESS_REMOTE_WRITE;
+    ugdr_modify_qp(qp, &at, UGDR_QP_STATE | UGDR_QP_ACCESS_FLAGS);
+    ugdr_modify_qp(peer, &at, UGDR_QP_STATE | UGDR_QP_ACCESS_FLAGS);
+    ugdr_qp_conn_info ci{}, cj{};
+    ugdr_query_qp_conn_info(peer, &ci);
+    ugdr_query_qp_conn_info(qp, &cj);
+    ugdr_qp_attr c{};
+    c.timeout = 14;
+    c.retry_cnt = 7;
+    c.rnr_retry = 7;
+    c.min_rnr_timer = 1;
+    const int cm = UGDR_QP_TIMEOUT | UGDR_QP_RETRY_CNT | UGDR_QP_RNR_RETRY | UGDR_QP_MIN_RNR_TIMER;
+    if (ugdr_connect_qp(qp, &ci, &c, cm) || ugdr_connect_qp(peer, &cj, &c, cm)) die("connect", EINVAL);
+    const uint64_t total = o.wrs;
+    std::vector<uint64_t> soff(total), doff(total);
+    std::vector<uint8_t> model(kMr, 0);
+    std::mt19937_64 pick(1);
+    for (uint64_t i = 0; i < total; ++i) {
+        soff[i] = (pick() % (kMr / kWr)) * kWr;
+        doff[i] = (pick() % (kMr / kWr)) * kWr;
+        std::memcpy(model.data() + doff[i], src + soff[i], kWr);
+    }
+    uint64_t posted = 0, done = 0;
+    ugdr_wc wc[64];
+    const auto t0 = Clock::now();
+    while (done < total) {
+        while (posted < total && posted - done < 128) {
+            post(qp, UGDR_WR_RDMA_WRITE, src + soff[posted], smr->lkey, kWr, dst + doff[posted], dmr->rkey, posted);
+            ++posted;
+        }
+        const int k = ugdr_poll_cq(cq, 64, wc);
+        if (k < 0) die("ugdr_poll_cq", -k);
+        for (int i = 0; i < k; ++i)
+            if (wc[i].status != UGDR_WC_SUCCESS) die("work completion", int(wc[i].status));
+        done += uint64_t(k);
+    }
+    const double sec = std::chrono::duration<double>(Clock::now() - t0).count();
+    const bool ok = std::memcmp(model.data(), dst, kMr) == 0;
+    std::printf("benchmark=ugdr_plumbing wrs=%llu wr_bytes=4096 qd=128 seconds=%.6f MWR_per_s=%.4f GB_per_s=%.3f "
+                "correct=%d\n", (unsigned long long)total, sec, double(total) / sec / 1e6,
+                double(total) * kWr / sec / 1e9, int(ok));
+    std::printf("{\"benchmark\": \"ugdr_plumbing\", \"wrs\": %llu, \"MWRps\": %.4f, \"GBps\": %.3f, "
+                "\"correct\": %s}\n", (unsigned long long)total, double(total) / sec / 1e6,
+                double(total) * kWr / sec / 1e9, ok ? "true" : "false");
+    return ok ? 0 : 2;
+}
+
 int run_stress(const Opts &o) {
     const uint32_t nq = uint32_t(o.qps), depth = uint32_t(o.depth), nsge = uint32_t(o.sges);
     if (nq == 0 || nq > 64 || depth == 0 || nsge == 0 || nsge > 32) die("stress options", EINVAL);
@@ -753,6 +828,7 @@ int main(int argc, char **argv) {
     if (o.mode == "bw") return run_bw(o);
     if (o.mode == "posting") return run_posting(o);
     if (o.mode == "stress") return run_stress(o);
+    if (o.mode == "plumbing") return run_plumbing(o);
     std::fprintf(stderr, "ugdr_perf: unknown mode %s\n", o.mode.c_str());
     return 2;
 }
