@@ -242,3 +242,44 @@ def test_concurrent_stress_clients_meet_at_the_barriers():
                      host_clients=2)
     agg = res["aggregate"]
     assert agg["correct"] and agg["clients"] == 2 and agg["wrs"] == 2 * 2 * 8 * 32, agg
+
+
+def test_daemon_death_is_reported_and_a_restarted_daemon_serves_new_objects(tmp_path):
+    """Failure detection on the host (reference: stale handles fail with EINVAL after a
+    reconnect, src/api/api.cpp connection epoch).  A daemon killed with SIGKILL leaves the client
+    with errors, not hangs: control calls on its objects fail promptly.  A new daemon on the same
+    socket path serves new objects, and handles from the dead daemon stay invalid."""
+    import signal
+
+    sock = str(tmp_path / "ugdr.sock")
+    d = V.Daemon(gpus=0, socket_path=sock)
+    ctx, pd, cq, a, b = _pair(depth=16, cq_depth=64)
+    buf = V.HostBuffer(1 << 16)
+    mr = pd.reg_mr(buf.addr, 1 << 16, ACC)
+    a.post_write((buf.addr, 8, mr.lkey), buf.addr + 4096, mr.rkey, wr_id=1)
+    assert cq.wait(1, timeout=10)[0].status == N.WC_SUCCESS
+    d.proc.send_signal(signal.SIGKILL)
+    d.proc.wait(10)
+    t0 = time.perf_counter()
+    with pytest.raises(V.UgdrError):
+        a.to_error()  # a control call on an object of the dead daemon
+    with pytest.raises(V.UgdrError):
+        ctx.alloc_pd()
+    assert time.perf_counter() - t0 < 5.0
+    # A restarted daemon on the same path: new objects work, old handles stay invalid.
+    os.unlink(sock)
+    d2 = V.Daemon(gpus=0, socket_path=sock)
+    try:
+        ctx2, pd2, cq2, a2, b2 = _pair(depth=16, cq_depth=64)
+        buf2 = V.HostBuffer(1 << 16)
+        mr2 = pd2.reg_mr(buf2.addr, 1 << 16, ACC)
+        buf2.view()[:8] = np.arange(8, dtype=np.uint8)
+        a2.post_write((buf2.addr, 8, mr2.lkey), buf2.addr + 4096, mr2.rkey, wr_id=7)
+        wc = cq2.wait(1, timeout=10)[0]
+        assert wc.status == N.WC_SUCCESS and wc.wr_id == 7
+        assert np.array_equal(buf2.view()[4096:4104], np.arange(8, dtype=np.uint8))
+        with pytest.raises(V.UgdrError):
+            pd.reg_mr(buf.addr, 4096, ACC)  # a PD of the dead daemon
+    finally:
+        d2.stop()
+        d.stop()  # reaps the killed process and closes its log
