@@ -1,5 +1,7 @@
 #include "control/service.hpp"
 
+#include "common/trace.hpp"
+
 #include "common/bytes.hpp"
 #include "ugdr/api.hpp"
 
@@ -96,7 +98,26 @@ ipc::Message ControlPlane::handle(ipc::SessionId session, ipc::Message &&msg) {
     return out;
 }
 
+namespace {
+const char *method_range(uint32_t m) {
+    static const char *names[] = {"ugdr.rpc.unknown",        "ugdr.rpc.list_devices",    "ugdr.rpc.create_context",
+                                  "ugdr.rpc.destroy_context", "ugdr.rpc.create_pd",       "ugdr.rpc.destroy_pd",
+                                  "ugdr.rpc.register_mr",    "ugdr.rpc.deregister_mr",   "ugdr.rpc.create_cq",
+                                  "ugdr.rpc.destroy_cq",     "ugdr.rpc.create_qp",       "ugdr.rpc.destroy_qp",
+                                  "ugdr.rpc.query_qp",       "ugdr.rpc.modify_qp",       "ugdr.rpc.query_conn_info",
+                                  "ugdr.rpc.connect_qp"};
+    if (m < sizeof(names) / sizeof(names[0])) return names[m];
+    switch (m) {
+    case kEngineStats: return "ugdr.rpc.engine_stats";
+    case kEngineHold: return "ugdr.rpc.engine_hold";
+    case kTimedDrain: return "ugdr.rpc.timed_drain";
+    default: return names[0];
+    }
+}
+}  // namespace
+
 Response ControlPlane::dispatch(ipc::SessionId s, Request &&r) {
+    TraceRange range(method_range(r.method));
     switch (r.method) {
     case kListDevices: return list_devices();
     case kCreateContext: return create_context(s, r);

@@ -4,6 +4,7 @@
 #include "gpu/device_abi.hpp"
 #include "gpu/executor.hpp"
 #include "gpu/visibility.hpp"
+#include "common/trace.hpp"
 #include "ugdr/api.hpp"
 
 #include <cuda_runtime_api.h>
@@ -433,6 +434,7 @@ bool GpuEngine::has_work_locked() {
 }
 
 int GpuEngine::launch_locked(uint32_t mode, uint64_t expected, bool timed) {
+    TraceRange range(mode == kDrain ? "ugdr.executor.launch_drain" : "ugdr.executor.launch");
     set_device();
     // Reset the per-launch words: exiting flag, and (drain) the retired counter.
     const uint32_t zero = 0;
@@ -482,6 +484,7 @@ void GpuEngine::monitor() {
 }
 
 void GpuEngine::quiesce() {
+    TraceRange range("ugdr.engine.quiesce");
     std::lock_guard<std::mutex> lk(mu_);
     paused_ += 1;
     stop_kernel_locked(cfg_.max_wait_ms * 4);
@@ -541,6 +544,7 @@ int GpuEngine::start_drain(uint64_t expected) {
 }
 
 int GpuEngine::finish_drain(uint32_t timeout_ms, float *elapsed_ms) {
+    TraceRange range("ugdr.engine.drain_wait");
     const auto deadline = Clock::now() + std::chrono::milliseconds(timeout_ms);
     for (;;) {
         {
