@@ -283,3 +283,19 @@ def test_daemon_death_is_reported_and_a_restarted_daemon_serves_new_objects(tmp_
     finally:
         d2.stop()
         d.stop()  # reaps the killed process and closes its log
+
+
+def test_smoke_binaries(tmp_path):
+    """Reference smoke checks (tests/smoke): the client without a daemon reports an errno and
+    fails; the daemon prints its usage; with a daemon, the client lists its devices."""
+    import subprocess
+
+    env = dict(os.environ, UGDR_DAEMON_SOCKET=str(tmp_path / "none.sock"))
+    r = subprocess.run([str(N.LIB_DIR / "ugdr_client")], env=env, capture_output=True, text=True, timeout=30)
+    assert r.returncode != 0 and "no daemon" in r.stderr
+    r = subprocess.run([str(N.DAEMON_PATH), "--help"], capture_output=True, text=True, timeout=30)
+    assert r.returncode == 0 and "usage: ugdr_daemon" in r.stdout
+    with V.Daemon(gpus=0, socket_path=str(tmp_path / "d.sock")):
+        env = dict(os.environ, UGDR_DAEMON_SOCKET=str(tmp_path / "d.sock"))
+        r = subprocess.run([str(N.LIB_DIR / "ugdr_client")], env=env, capture_output=True, text=True, timeout=30)
+        assert r.returncode == 0 and "kind=cpu" in r.stdout, r.stdout + r.stderr
