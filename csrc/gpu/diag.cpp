@@ -19,6 +19,13 @@ int ugdr_x_copy_core_test(void *dst, const void *src, uint64_t n, void *stream) 
 int ugdr_x_grid_copy_bench(void *dst, const void *src, uint64_t n, int ctas, int iters, void *stream,
                            float *ms_per_copy) noexcept {
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (dst == nullptr || src == nullptr) return int(cudaErrorInvalidValue);
+    if (ctas <= 0) {  // one CTA per SM
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&ctas, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || ctas <= 0)
+            return int(cudaErrorInvalidValue);
+    }
     cudaEvent_t a, b;
     cudaEventCreate(&a);
     cudaEventCreate(&b);

@@ -1,1 +1,67 @@
-"""ugdr_b200.ops"""
+"""Device kernels callable from Python on tensors of the current CUDA device.
+
+* copy_core(dst, src)      the executor's warp copy core over one range (one warp; for tests)
+* grid_copy_ms(dst, src)   mean ms of a whole-grid copy with the executor's copy core
+* moe_route(ids, nexp)     deterministic counting sort of (token, k) rows by expert
+* register(pd, tensor)     a verbs MR over a tensor's bytes (local write + remote read / write)
+
+The collectives themselves live in ugdr_b200.parallel (they need a peer group).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from .. import _native as N
+from ..parallel.collectives import moe_route  # noqa: F401  (re-exported)
+
+
+def _lib():
+    L = N.lib()
+    if not getattr(L, "_ops_sigs", False):
+        L.ugdr_x_copy_core_test.restype = C.c_int
+        L.ugdr_x_copy_core_test.argtypes = [C.c_void_p, C.c_void_p, C.c_uint64, C.c_void_p]
+        L.ugdr_x_grid_copy_bench.restype = C.c_int
+        L.ugdr_x_grid_copy_bench.argtypes = [C.c_void_p, C.c_void_p, C.c_uint64, C.c_int, C.c_int, C.c_void_p,
+                                             C.POINTER(C.c_float)]
+        L._ops_sigs = True
+    return L
+
+
+def _stream(stream: torch.cuda.Stream | None) -> C.c_void_p:
+    return C.c_void_p((stream or torch.cuda.current_stream()).cuda_stream)
+
+
+def copy_core(dst: torch.Tensor, src: torch.Tensor, nbytes: int | None = None,
+              stream: torch.cuda.Stream | None = None) -> None:
+    """Copy `nbytes` (default: all of src) from src's storage to dst's with one warp of the
+    executor's copy core, on `stream`."""
+    n = src.numel() * src.element_size() if nbytes is None else nbytes
+    if n > dst.numel() * dst.element_size() or n > src.numel() * src.element_size():
+        raise ValueError("copy larger than a tensor")
+    rc = _lib().ugdr_x_copy_core_test(C.c_void_p(dst.data_ptr()), C.c_void_p(src.data_ptr()), n, _stream(stream))
+    if rc != 0:
+        raise RuntimeError(f"ugdr_x_copy_core_test failed: cudaError {rc}")
+
+
+def grid_copy_ms(dst: torch.Tensor, src: torch.Tensor, ctas: int = 0, iters: int = 10,
+                 stream: torch.cuda.Stream | None = None) -> float:
+    """Mean milliseconds of a whole-grid copy of src into dst (CUDA events on `stream`)."""
+    n = src.numel() * src.element_size()
+    if n > dst.numel() * dst.element_size():
+        raise ValueError("destination smaller than source")
+    ms = C.c_float()
+    rc = _lib().ugdr_x_grid_copy_bench(C.c_void_p(dst.data_ptr()), C.c_void_p(src.data_ptr()), n, ctas, iters,
+                                      _stream(stream), C.byref(ms))
+    if rc != 0:
+        raise RuntimeError(f"ugdr_x_grid_copy_bench failed: cudaError {rc}")
+    return float(ms.value)
+
+
+def register(pd, tensor: torch.Tensor, access: int | None = None):
+    """A memory region over `tensor`'s bytes (contiguous CUDA or ugdr host memory)."""
+    if not tensor.is_contiguous():
+        raise ValueError("register() needs a contiguous tensor")
+    acc = access if access is not None else (N.ACCESS_LOCAL_WRITE | N.ACCESS_REMOTE_WRITE | N.ACCESS_REMOTE_READ)
+    return pd.reg_mr(tensor.data_ptr(), tensor.numel() * tensor.element_size(), acc)
