@@ -11,15 +11,18 @@
 //  * Ownership.  QP slot q belongs to exactly one warp of the grid (CTA q % grid, warp
 //    (q / grid) % warps), so each QP's WRs are fetched, validated and retired in posting order by
 //    one warp, and QPs spread over all SMs.
-//  * Issue.  The owner warp reads the WQE (host-mapped ring) lane-parallel into shared memory,
-//    resolves every SGE's lkey and the rkey against the device MR table, and either copies the
-//    payload itself (<= 4 KiB, atomics) or publishes it as a job whose fixed-size chunks any
-//    warp on the GPU may claim (CAS on a generation-tagged counter), so a single large WR
-//    spreads over every SM.
-//  * Retire.  When all chunks of the oldest in-flight WR are done the owner produces the receive
-//    CQE (WRITE_WITH_IMM), the send CQE (signaled or error), and advances the ring head.  CQs
-//    are multi-producer (several warps, several GPUs): slots are reserved by CAS against the
-//    consumer cursor and published strictly in order.
+//  * Issue.  The owner warp reads up to 16 WQEs (host-mapped ring) lane-parallel into shared
+//    memory.  Single-SGE WRITE / READ are validated lane-parallel (lane j checks WQE j against
+//    the device MR table); payloads up to 64 B are copied by their lane, larger ones become one
+//    chunked job for the whole batch.  Other WRs (multi-SGE, WRITE_WITH_IMM, atomics) are staged
+//    one per round and run inline (<= 4 KiB, atomics) or as a one-WR job.  Any warp of the GPU
+//    claims job chunks with a fetch-and-add on the job's counter, so one large WR spreads over
+//    every SM.
+//  * Retire.  When all chunks of the oldest in-flight WRs are done the owner produces the
+//    receive CQEs (WRITE_WITH_IMM), the send CQEs (signaled or error) and advances the ring
+//    head.  CQs are multi-producer (several warps, several GPUs): slots are reserved by CAS and
+//    the tail moves in slot order, by turns passed through a device-memory tail hint (see
+//    publish_cq), never by polling the host ring.
 //  * Bounded waits.  Every spin carries a %globaltimer deadline; on expiry the kernel records
 //    the reason in DevStats::error_code and every warp exits.  There is no __trap, assert or
 //    unbounded loop.  The kernel also exits after `idle_exit_ns` without work, on a host stop

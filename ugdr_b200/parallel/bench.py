@@ -1,10 +1,14 @@
 """Collectives benchmark - launch one rank per GPU:
 
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \\
-        -m ugdr_b200.parallel.bench [--op allreduce|moe|all] [--iters K] [--warmup W]
+        -m ugdr_b200.parallel.bench [--op allreduce|moe|p2p|all] [--iters K] [--warmup W]
 
-* allreduce: 1 GiB bf16 per rank, N(0,1) seeded by rank; ugdr's fused-sum kernels vs NCCL
-  all_reduce on the same tensor size.  Reports algbw (bytes / time) and busbw (x 2(N-1)/N).
+* allreduce: 1 GiB bf16 per rank, N(0,1) seeded by rank; ugdr's one-kernel fused-sum allreduce
+  over peer memory and (N >= 2, when the GPUs support multicast) its NVLS allreduce that sums in
+  the NVSwitch, vs NCCL all_reduce on the same tensor size.  Reports both, the faster as
+  `ugdr_best_ms`, algbw (bytes / time) and busbw (x 2(N-1)/N).
+* p2p: NCCL send / recv from rank 0 to rank 1 for 8 B .. 1 GiB (the baseline of the verbs
+  WRITE / READ sweep, which ugdr_b200.utils.perf runs).
 * moe: 16,384 tokens x 7,168 bf16 per rank, top-8 of 256 experts from uniform router logits;
   one step = dispatch + combine (experts are the identity).  ugdr fuses the permutes into the
   NVLink stores / loads; the NCCL baseline is all_to_all_single with the permutes as separate
