@@ -299,3 +299,23 @@ def test_smoke_binaries(tmp_path):
         env = dict(os.environ, UGDR_DAEMON_SOCKET=str(tmp_path / "d.sock"))
         r = subprocess.run([str(N.LIB_DIR / "ugdr_client")], env=env, capture_output=True, text=True, timeout=30)
         assert r.returncode == 0 and "kind=cpu" in r.stdout, r.stdout + r.stderr
+
+
+def test_c_example_client(tmp_path):
+    """examples/write_read.c builds as C11 against the public header and runs WRITE, READ and
+    FETCH_ADD through a daemon's host-memory engine."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    exe = str(tmp_path / "write_read")
+    subprocess.run([cc, "-std=c11", "-Wall", "-Wextra", "-Werror", "-pedantic", "-I", os.path.join(repo, "include"),
+                    os.path.join(repo, "examples", "write_read.c"), "-L", str(N.LIB_DIR), "-lugdr",
+                    f"-Wl,-rpath,{N.LIB_DIR}", "-o", exe], check=True, capture_output=True, text=True)
+    with V.Daemon(gpus=0, socket_path=str(tmp_path / "d.sock")):
+        env = dict(os.environ, UGDR_DAEMON_SOCKET=str(tmp_path / "d.sock"))
+        r = subprocess.run([exe, "ugdr_cpu0"], env=env, capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
