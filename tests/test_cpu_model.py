@@ -47,6 +47,8 @@ def wr_stream(draw):
         fault = draw(st.sampled_from([None] * 12 + ["lkey", "range", "align"]))
         if kind in ("faa", "cas"):
             ctr = draw(st.integers(0, 31))
+            if fault == "align":
+                ctr = min(ctr, 30)  # the misaligned 8 bytes stay inside the MR (else: access error first)
             wrs.append(dict(kind=kind, signaled=signaled, fault=fault if fault != "range" else None,
                             ctr=ctr, local=draw(st.integers(0, 255)) * 8,
                             operand=draw(st.integers(0, 5)), swap=draw(st.integers(0, 1 << 40))))
@@ -76,7 +78,8 @@ def model(wrs, loc0: np.ndarray, rem0: np.ndarray):
             send.append((i, N.WC_WR_FLUSH_ERR, WC_OP[op], 0))
             continue
         status = N.WC_SUCCESS
-        if w["fault"] == "lkey":
+        # Zero-length SGEs touch no memory, so their lkey is not checked (as on an HCA).
+        if w["fault"] == "lkey" and (w["kind"] in ("faa", "cas") or any(ln for _, ln in w["sges"])):
             status = N.WC_LOC_PROT_ERR
         elif w["fault"] == "range":
             status = N.WC_REM_ACCESS_ERR
@@ -159,9 +162,14 @@ def test_host_engine_matches_the_model(daemon, wrs, seed):
                     w["sges"][0] = (w["sges"][0][0], 64)
                 raw.append(V.QueuePair.make_send_wr(op, sges, remote_addr=rb.addr + roff, rkey=rm.rkey, wr_id=i,
                                                     signaled=w["signaled"], imm=w["imm"]))
+        # A signaled zero-length WRITE closes the stream, so there is always a completion that
+        # comes after every WR above has run (or been flushed).
+        raw.append(V.QueuePair.make_send_wr(N.WR_RDMA_WRITE, [], remote_addr=rb.addr, rkey=rm.rkey,
+                                            wr_id=len(wrs), signaled=True))
         rc, bad = a.post_send_raw(raw)
         assert rc == 0 and bad == -1
         loc, rem, send, recv, err = model(wrs, loc0, rem0)
+        send.append((len(wrs), N.WC_WR_FLUSH_ERR if err else N.WC_SUCCESS, N.WC_RDMA_WRITE, 0))
         got = cq.wait(len(send) + len(recv), timeout=30)
         got_send = [(w.wr_id, w.status, w.opcode, w.byte_len) for w in got if w.opcode != N.WC_RECV_RDMA_WITH_IMM]
         got_recv = [(w.wr_id, w.byte_len, w.imm_data) for w in got
