@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Headline benchmark: all-pairs RDMA WRITE bandwidth through the ugdr verbs API.
 
-Workload (weak-scaled): every GPU holds one 256 MiB bf16 MR (N(0,1),
+Workload (the all-pairs configuration, weak-scaled): every GPU holds one 256 MiB bf16 MR (N(0,1),
 seeded by rank) of eight 32 MiB slices, plus a 256 MiB receive MR.  One step = every GPU
 RDMA_WRITEs 7 distinct slices over 7 QPs: WR k of rank r sends slice k to peer
 (r + 1 + k mod (N - 1)) % N, into that GPU's receive slot (dst + 1 + k) % 8, so every inbound WR
@@ -37,7 +37,7 @@ sys.path.insert(0, REPO)
 SLOT_MIB = 32
 SLOTS = 8
 PEERS = 7
-BASELINE_GBPS = None  # BASELINE.json publishes no number for this config
+BASELINE_GBPS = None  # no published number exists for this configuration
 _DAEMON = None  # rank 0's daemon, kept for its log when a run fails
 
 

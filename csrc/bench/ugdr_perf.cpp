@@ -1,12 +1,12 @@
-// ugdr_perf: verbs-level benchmarks through the public C API (BASELINE configs[1] and the WR
+// ugdr_perf: verbs-level benchmarks through the public C API (the point-to-point sweep and the WR
 // posting rate).  Needs a running ugdr_daemon (UGDR_DAEMON_SOCKET).
 //
 //   ugdr_perf latency  --src-gpu A --dst-gpu B --bytes N --iters K        QD1 post_send -> poll_cq
 //   ugdr_perf bw       --src-gpu A --dst-gpu B --op write|read --min 8 --max 1G --qd 64 --bytes-per-size T
 //   ugdr_perf posting  --batch B --wrs N                                    post_send into the SQ ring
-//   ugdr_perf plumbing --wrs 10000                                          BASELINE configs[0] (host engine)
+//   ugdr_perf plumbing --wrs 10000                                          CPU-only plumbing (host engine)
 //   ugdr_perf stress   --src-gpu A --dst-gpu B --qps 64 --depth 128 --sges 16 --rounds R
-//                      verbs-feature stress (BASELINE configs[3]): per QP an interleave of
+//                      verbs-feature stress: per QP an interleave of
 //                      16-SGE WRITE and WRITE_WITH_IMM (SGE sizes log-uniform in 64 B..64 KiB,
 //                      gathered into a contiguous remote range), FETCH_ADD and CMP_AND_SWP on a
 //                      4096-entry uint64 counter array; checks every byte, immediate, and
@@ -475,7 +475,7 @@ ugdr_mr *dev_mr(ugdr_pd *pd, int gpu, uint64_t bytes, int access, void **buf) {
     return mr;
 }
 
-// ---- CPU-only plumbing -------------------------------------------------------
+// ---- CPU-only plumbing workload -------------------------------------------------------
 
 // One client and the daemon's host-memory engine: 1 PD, two 1 MiB host MRs, one QP of depth
 // 128, one CQ; `wrs` RDMA_WRITEs of one 4 KiB SGE at seeded random 4 KiB-aligned offsets, with

@@ -30,7 +30,7 @@ def _pair(depth=128, max_sge=4, rnr_retry=7, min_rnr_timer=1, cq_depth=512):
 
 
 def test_config0_cpu_plumbing_10k_writes(cpu_daemon):
-    """1 PD, 2 host MRs of 1 MiB, 1 QP of depth 128, 10,000 RDMA_WRITEs of
+    """CPU-only plumbing workload: 1 PD, 2 host MRs of 1 MiB, 1 QP of depth 128, 10,000 RDMA_WRITEs of
     4 KiB at seeded random 4 KiB-aligned offsets, payload uniform uint8 from seed 0."""
     ctx, pd, cq, a, b = _pair(depth=128, cq_depth=256)
     n = 1 << 20
@@ -223,7 +223,7 @@ def test_cli_doctor_reports_the_build():
 
 
 def test_config3_stress_on_the_host_engine():
-    """BASELINE configs[3] semantics on the host-memory engine: 16-SGE WRITE / WRITE_WITH_IMM with
+    """Verbs-feature stress semantics on the host-memory engine: 16-SGE WRITE / WRITE_WITH_IMM with
     log-uniform SGE sizes, fetch-add and compare-swap on a 4096-entry counter array; every byte,
     immediate, CAS result and counter is checked by ugdr_perf."""
     from ugdr_b200.utils.perf import run

@@ -245,7 +245,7 @@ def test_cross_gpu_write_read_imm_atomics(gpu2_env):
 
 @pytest.mark.parametrize("dst_gpu", [0, 1])
 def test_verbs_stress_16sge_imm_atomics(dst_gpu):
-    """BASELINE configs[3] at reduced size: per QP an interleave of 16-SGE WRITE / WRITE_WITH_IMM
+    """The verbs-feature stress workload at reduced size: per QP an interleave of 16-SGE WRITE / WRITE_WITH_IMM
     (SGE sizes log-uniform 64 B..64 KiB, random offsets) and fetch-add / compare-swap on a
     4096-entry counter array; ugdr_perf checks every gathered byte, immediate, CAS result and
     final counter value."""

@@ -1,4 +1,4 @@
-"""Collectives benchmark (BASELINE configs[4]) - launch one rank per GPU:
+"""Collectives benchmark - launch one rank per GPU:
 
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \\
         -m ugdr_b200.parallel.bench [--op allreduce|moe|p2p|all] [--iters K] [--warmup W]
@@ -123,7 +123,7 @@ def bench_allreduce(rank, world, iters, warmup, nbytes=1 << 30, impl="all", ctas
 
 
 def bench_p2p_nccl(rank, world, sizes, iters, warmup) -> list[dict]:
-    """NCCL send/recv baseline for the point-to-point sweep: rank 0 sends
+    """NCCL send/recv baseline for the point-to-point WRITE / READ sweep: rank 0 sends
     `size` bytes to rank 1, `iters` transfers back to back, device-timed, max over the pair."""
     out = []
     if world < 2:

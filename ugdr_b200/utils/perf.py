@@ -40,7 +40,7 @@ def run(args: list[str], gpus: int | None = None, timeout: float = 1800) -> list
 
 
 def stress_all(gpus: int, extra: list[str], timeout: float = 1800, host_clients: int = 2) -> dict:
-    """BASELINE configs[3] on every ordered GPU pair at once: one daemon owning `gpus` GPUs and
+    """The verbs-feature stress workload on every ordered GPU pair at once: one daemon owning `gpus` GPUs and
     one ugdr_perf stress client per (src, dst) pair, all running concurrently.  The clients meet
     at a start barrier after their set-up and at a finish barrier before their tear-down, so the
     timed rounds overlap and no client's tear-down (which quiesces executors) lands inside
