@@ -14,6 +14,7 @@
 #include <cstring>
 #include <memory>
 #include <mutex>
+#include <random>
 #include <vector>
 
 using namespace ugdr;
@@ -393,4 +394,76 @@ TEST(cqe_to_wc_fields) {
     CHECK_EQ(wc.qp_num, 9u);
     CHECK_EQ(wc.wc_flags, unsigned(UGDR_WC_WITH_IMM));
     CHECK_EQ(wc.vendor_err, 0u);
+}
+
+// A client that bypasses the library and writes arbitrary bytes into its SQ ring must not crash
+// the host engine or make it touch memory outside registered ranges: every WQE either runs
+// inside an MR, or fails with an error completion that moves the QP to ERR.
+TEST(cpu_engine_survives_garbage_wqes) {
+    Fixture f;
+    const uint64_t c = f.ctx(), p = f.pd(c);
+    const uint64_t cq = f.cq(c, 8192).identity;
+    SharedMapping region;
+    constexpr size_t kRegion = 512 << 10, kOff = 64 << 10, kLen = 256 << 10;
+    Response m = f.mr(p, &region, kRegion, kOff, kLen, kAllAccess);
+    CHECK_EQ(m.status, 0);
+    const Keys k = keys_of(m);
+    uint8_t *base = static_cast<uint8_t *>(region.address);
+    for (size_t i = 0; i < kRegion; ++i) base[i] = uint8_t(i * 7 + 3);
+    std::vector<uint8_t> before(base, base + kRegion);
+    const uint64_t lo = reinterpret_cast<uintptr_t>(base) + kOff;
+    std::mt19937_64 rng(5);
+    auto pick_addr = [&]() -> uint64_t {
+        switch (rng() % 4) {
+        case 0: return lo + rng() % kLen;                  // inside the MR
+        case 1: return lo + kLen - rng() % 64;             // at its end
+        case 2: return reinterpret_cast<uintptr_t>(base) + rng() % kRegion;  // possibly outside
+        default: return rng();                              // anywhere
+        }
+    };
+    auto pick_key = [&](uint32_t good) -> uint32_t { return rng() % 4 ? good : uint32_t(rng()); };
+    const uint32_t stride = queue::send_stride(4);
+    for (int iter = 0; iter < 200; ++iter) {
+        Response qx = f.qp(p, cq, cq), qy = f.qp(p, cq, cq);
+        CHECK_EQ(f.modify(qx.identity, UGDR_QP_STATE | UGDR_QP_ACCESS_FLAGS, UGDR_QPS_INIT, kRemoteAll), 0);
+        CHECK_EQ(f.modify(qy.identity, UGDR_QP_STATE | UGDR_QP_ACCESS_FLAGS, UGDR_QPS_INIT, kRemoteAll), 0);
+        CHECK_EQ(f.connect(qx.identity, qpn_of(qy)), 0);
+        CHECK_EQ(f.connect(qy.identity, qpn_of(qx)), 0);
+        queue::Ring sq;
+        CHECK_EQ(queue::Ring::attach(qx.fds[0].release(), {queue::kSendRing, 16, stride}, &sq), 0);
+        queue::SlotRun run = sq.reserve(8);
+        CHECK_EQ(run.count(), 8u);
+        for (uint32_t i = 0; i < run.count(); ++i) {
+            uint8_t *slot = i < run.first_count ? run.first + uint64_t(i) * stride
+                                                : run.second + uint64_t(i - run.first_count) * stride;
+            for (uint32_t b = 0; b < stride; ++b) slot[b] = uint8_t(rng());
+            if (rng() % 8 == 0) continue;  // pure noise
+            queue::SendWqe h;
+            std::memcpy(&h, slot, sizeof(h));
+            const uint32_t ops[] = {UGDR_WR_RDMA_WRITE, UGDR_WR_RDMA_READ, UGDR_WR_ATOMIC_FETCH_AND_ADD,
+                                    UGDR_WR_ATOMIC_CMP_AND_SWP, uint32_t(rng())};
+            h.opcode = ops[rng() % 5];
+            h.sge_count = uint32_t(rng() % 6);
+            h.send_flags = UGDR_SEND_SIGNALED;
+            h.remote_address = pick_addr();
+            h.rkey = pick_key(k.rkey);
+            std::memcpy(slot, &h, sizeof(h));
+            for (uint32_t s = 0; s < h.sge_count && s < 4; ++s) {
+                queue::Sge sg{pick_addr(), uint32_t(rng() % 3 ? rng() % 4096 : rng()), pick_key(k.lkey)};
+                if (h.opcode == UGDR_WR_ATOMIC_FETCH_AND_ADD || h.opcode == UGDR_WR_ATOMIC_CMP_AND_SWP)
+                    sg.length = rng() % 4 ? 8 : sg.length;
+                std::memcpy(slot + queue::kSendSgeOffset + s * sizeof(queue::Sge), &sg, sizeof(sg));
+            }
+        }
+        sq.publish(run.count());
+        {
+            std::lock_guard<std::mutex> lk(f.mu);
+            for (int k2 = 0; k2 < 16; ++k2) f.eng.progress_locked();
+        }
+        CHECK_EQ(f.call(kDestroyQp, qx.identity).status, 0);
+        CHECK_EQ(f.call(kDestroyQp, qy.identity).status, 0);
+    }
+    // Bytes outside the registered range were never written.
+    CHECK(std::memcmp(base, before.data(), kOff) == 0);
+    CHECK(std::memcmp(base + kOff + kLen, before.data() + kOff + kLen, kRegion - kOff - kLen) == 0);
 }
