@@ -12,6 +12,8 @@ sys.path.insert(0, REPO)
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200); run with -m gpu")
+    config.addinivalue_line("markers", "gpu_extended: long GPU property tests; run with -m gpu_extended "
+                            "(skipped without a GPU, not part of -m gpu)")
 
 
 @pytest.fixture(scope="session", autouse=True)
