@@ -4,6 +4,7 @@
 //   ugdr_perf latency  --src-gpu A --dst-gpu B --bytes N --iters K        QD1 post_send -> poll_cq
 //   ugdr_perf bw       --src-gpu A --dst-gpu B --op write|read --min 8 --max 1G --qd 64 --bytes-per-size T
 //   ugdr_perf posting  --batch B --wrs N                                    post_send into the SQ ring
+//   ugdr_perf ring     --batch B --wrs N                                    shared SPSC ring alone (2 threads)
 //   ugdr_perf plumbing --wrs 10000                                          CPU-only plumbing (host engine)
 //   ugdr_perf stress   --src-gpu A --dst-gpu B --qps 64 --depth 128 --sges 16 --rounds R
 //                      verbs-feature stress: per QP an interleave of
@@ -15,6 +16,8 @@
 // Output: one key=value line per measurement (reference style, benchmarks/*.cpp) and a JSON
 // line with the same fields.  Payload: uniform uint8 from a seed; every size's destination is
 // compared byte-for-byte with the source once.
+#include "queue/layout.hpp"
+#include "queue/ring.hpp"
 #include "ugdr/api.hpp"
 
 #include <cuda_runtime_api.h>
@@ -23,6 +26,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <chrono>
 #include <cstdio>
@@ -475,6 +479,61 @@ ugdr_mr *dev_mr(ugdr_pd *pd, int gpu, uint64_t bytes, int access, void **buf) {
     return mr;
 }
 
+// ---- shared ring alone -------------------------------------------------------------------------
+
+// Descriptor rate of the shared SPSC ring with no daemon: a producer thread reserves, writes (the
+// first 16 bytes of every 64-byte slot) and publishes `batch` slots at a time; a consumer thread
+// peeks, reads and releases them.  Reference counterpart: benchmarks/shared_ring_benchmark.cpp
+// (descriptors per second at batch 1 and 32).
+int run_ring(const Opts &o) {
+    ugdr::queue::Ring prod, cons;
+    const ugdr::queue::RingGeometry g{ugdr::queue::kSendRing, 4096, 64};
+    if (int rc = ugdr::queue::Ring::create(g, &prod)) die("ring create", rc);
+    if (int rc = ugdr::queue::Ring::attach(::dup(prod.fd()), g, &cons)) die("ring attach", rc);
+    const uint32_t batch = uint32_t(std::max<uint64_t>(1, std::min<uint64_t>(o.batch, 4096)));
+    const uint64_t total = o.wrs;
+    std::atomic<uint64_t> checksum{0};
+    const auto t0 = Clock::now();
+    std::thread consumer([&] {
+        uint64_t got = 0, sum = 0;
+        while (got < total) {
+            ugdr::queue::SlotRun r = cons.peek(batch);
+            const uint32_t n = r.count();
+            for (uint32_t i = 0; i < n; ++i) {
+                const uint8_t *slot = i < r.first_count ? r.first + uint64_t(i) * 64 : r.second + uint64_t(i - r.first_count) * 64;
+                uint64_t v;
+                std::memcpy(&v, slot, 8);
+                sum += v;
+            }
+            cons.release(n);
+            got += n;
+        }
+        checksum.store(sum);
+    });
+    uint64_t sent = 0;
+    while (sent < total) {
+        const uint32_t want = uint32_t(std::min<uint64_t>(batch, total - sent));
+        ugdr::queue::SlotRun r = prod.reserve(want);
+        const uint32_t n = r.count();
+        for (uint32_t i = 0; i < n; ++i) {
+            uint8_t *slot = i < r.first_count ? r.first + uint64_t(i) * 64 : r.second + uint64_t(i - r.first_count) * 64;
+            const uint64_t v = sent + i;
+            std::memcpy(slot, &v, 8);
+            std::memcpy(slot + 8, &v, 8);
+        }
+        prod.publish(n);
+        sent += n;
+    }
+    consumer.join();
+    const double sec = std::chrono::duration<double>(Clock::now() - t0).count();
+    const bool ok = checksum.load() == total * (total - 1) / 2;
+    std::printf("benchmark=ugdr_ring batch=%u descriptors=%llu seconds=%.6f M_per_s=%.3f correct=%d\n", batch,
+                (unsigned long long)total, sec, double(total) / sec / 1e6, int(ok));
+    std::printf("{\"benchmark\": \"ugdr_ring\", \"batch\": %u, \"M_per_s\": %.3f, \"correct\": %s}\n", batch,
+                double(total) / sec / 1e6, ok ? "true" : "false");
+    return ok ? 0 : 2;
+}
+
 // ---- CPU-only plumbing workload -------------------------------------------------------
 
 // One client and the daemon's host-memory engine: 1 PD, two 1 MiB host MRs, one QP of depth
@@ -829,6 +888,7 @@ int main(int argc, char **argv) {
     if (o.mode == "posting") return run_posting(o);
     if (o.mode == "stress") return run_stress(o);
     if (o.mode == "plumbing") return run_plumbing(o);
+    if (o.mode == "ring") return run_ring(o);
     std::fprintf(stderr, "ugdr_perf: unknown mode %s\n", o.mode.c_str());
     return 2;
 }

@@ -319,3 +319,16 @@ def test_c_example_client(tmp_path):
         env = dict(os.environ, UGDR_DAEMON_SOCKET=str(tmp_path / "d.sock"))
         r = subprocess.run([exe, "ugdr_cpu0"], env=env, capture_output=True, text=True, timeout=60)
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
+
+
+def test_ring_benchmark_moves_every_descriptor():
+    """ugdr_perf ring: producer and consumer threads over one shared ring, batch 1 and 32; the
+    consumer's checksum proves every descriptor arrived once and in order."""
+    import json
+    import subprocess
+
+    for batch in (1, 32):
+        r = subprocess.run([str(N.LIB_DIR / "ugdr_perf"), "ring", "--batch", str(batch), "--wrs", "200000"],
+                           capture_output=True, text=True, timeout=120)
+        out = [json.loads(line) for line in r.stdout.splitlines() if line.startswith("{")]
+        assert r.returncode == 0 and out and out[-1]["correct"], r.stdout + r.stderr

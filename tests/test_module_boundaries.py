@@ -21,7 +21,7 @@ ALLOWED = {
     "collective": {"collective", "ugdr"},
     "daemon": {"common", "queue", "ipc", "control", "engine", "gpu", "daemon", "ugdr"},
     "apps": {"ugdr"},
-    "bench": {"ugdr"},
+    "bench": {"ugdr", "queue", "common"},  # the ring benchmark drives the queue layer directly
 }
 # Files of a layer that need no CUDA headers at all (wire formats and the control plane run in
 # processes and tests without a GPU stack).
