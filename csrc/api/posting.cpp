@@ -10,15 +10,14 @@ bool is_atomic(uint32_t op) {
     return op == UGDR_WR_ATOMIC_CMP_AND_SWP || op == UGDR_WR_ATOMIC_FETCH_AND_ADD;
 }
 
-bool send_ok(const ugdr_send_wr &wr, uint32_t max_sge) {
-    switch (wr.opcode) {
-    case UGDR_WR_RDMA_WRITE:
-    case UGDR_WR_RDMA_WRITE_WITH_IMM:
-    case UGDR_WR_RDMA_READ:
-    case UGDR_WR_ATOMIC_CMP_AND_SWP:
-    case UGDR_WR_ATOMIC_FETCH_AND_ADD: break;
-    default: return false;
-    }
+// Opcodes a send WQE may carry, as a bit mask over the opcode value.
+constexpr uint32_t kSendOpMask = (1u << UGDR_WR_RDMA_WRITE) | (1u << UGDR_WR_RDMA_WRITE_WITH_IMM) |
+                                 (1u << UGDR_WR_RDMA_READ) | (1u << UGDR_WR_ATOMIC_CMP_AND_SWP) |
+                                 (1u << UGDR_WR_ATOMIC_FETCH_AND_ADD);
+
+inline bool send_ok(const ugdr_send_wr &wr, uint32_t max_sge) {
+    const uint32_t op = uint32_t(wr.opcode);
+    if (op >= 32 || ((kSendOpMask >> op) & 1u) == 0) return false;
     if ((wr.send_flags & ~unsigned(UGDR_SEND_SIGNALED)) != 0) return false;
     if (wr.num_sge < 0 || uint32_t(wr.num_sge) > max_sge) return false;
     if (wr.num_sge > 0 && wr.sg_list == nullptr) return false;
@@ -38,34 +37,46 @@ int post_chain(queue::Ring &ring, Wr *wr, Wr **bad_wr, Ok ok, Enc enc) {
         if (bad_wr) *bad_wr = wr;
         return EINVAL;
     }
-    // Count the chain up to the first invalid WR, then reserve once.
-    uint32_t want = 0;
-    Wr *stop = nullptr;
+    // One pass: take the slots known to be free, validate and encode WRs into them in order,
+    // publish the encoded prefix once.  The consumer cursor (a line the consumer writes) is
+    // re-read only when those slots run out.
+    queue::SlotRun run = ring.reserve_free(false);
+    uint32_t room = run.count();
+    const uint32_t stride = ring.geometry().stride;
+    uint8_t *slot = run.first;
+    uint32_t left_in_span = run.first_count;
+    uint32_t n = 0;
     int err = 0;
-    for (Wr *w = wr; w != nullptr; w = w->next) {
+    Wr *w = wr;
+    for (; w != nullptr; w = w->next) {
         if (!ok(*w)) {
-            stop = w;
             err = EINVAL;
             break;
         }
-        ++want;
-    }
-    queue::SlotRun run = ring.reserve(want);
-    const uint32_t got = run.count();
-    Wr *w = wr;
-    const uint32_t stride = ring.geometry().stride;
-    for (uint32_t i = 0; i < got; ++i, w = w->next) {
-        uint8_t *slot = i < run.first_count ? run.first + uint64_t(i) * stride
-                                            : run.second + uint64_t(i - run.first_count) * stride;
+        if (n == room) {
+            ring.publish(n);
+            run = ring.reserve_free(true);
+            room = run.count();
+            slot = run.first;
+            left_in_span = run.first_count;
+            n = 0;
+            if (room == 0) {
+                err = ENOMEM;
+                break;
+            }
+        }
+        if (left_in_span == 0) {  // wrapped into the second span
+            slot = run.second;
+            left_in_span = run.second_count;
+        }
         enc(slot, *w);
+        slot += stride;
+        --left_in_span;
+        ++n;
     }
-    ring.publish(got);
-    if (got < want) {
-        *bad_wr = w;
-        return ENOMEM;
-    }
+    ring.publish(n);
     if (err != 0) {
-        *bad_wr = stop;
+        *bad_wr = w;
         return err;
     }
     return 0;
@@ -74,28 +85,26 @@ int post_chain(queue::Ring &ring, Wr *wr, Wr **bad_wr, Ok ok, Enc enc) {
 }  // namespace
 
 void encode_send(uint8_t *slot, const ugdr_send_wr &wr) {
-    queue::SendWqe h;
-    h.wr_id = wr.wr_id;
-    h.opcode = uint32_t(wr.opcode);
-    h.send_flags = wr.send_flags;
-    h.sge_count = uint32_t(wr.num_sge);
+    // Slots are 64-byte aligned, so the header is written in place, field by field.
+    auto *h = reinterpret_cast<queue::SendWqe *>(slot);
+    h->wr_id = wr.wr_id;
+    h->opcode = uint32_t(wr.opcode);
+    h->send_flags = wr.send_flags;
+    h->sge_count = uint32_t(wr.num_sge);
     if (is_atomic(wr.opcode)) {
-        h.remote_address = wr.wr.atomic.remote_addr;
-        h.rkey = wr.wr.atomic.rkey;
-        h.immediate_data = uint32_t(wr.wr.atomic.swap);
-        h.reserved = uint32_t(wr.wr.atomic.swap >> 32);
+        h->remote_address = wr.wr.atomic.remote_addr;
+        h->rkey = wr.wr.atomic.rkey;
+        h->immediate_data = uint32_t(wr.wr.atomic.swap);
+        h->reserved = uint32_t(wr.wr.atomic.swap >> 32);
         std::memcpy(slot + queue::kAtomicCompareOffset, &wr.wr.atomic.compare_add, 8);
     } else {
-        h.remote_address = wr.wr.rdma.remote_addr;
-        h.rkey = wr.wr.rdma.rkey;
-        h.immediate_data = wr.opcode == UGDR_WR_RDMA_WRITE_WITH_IMM ? wr.imm_data : 0;
-        h.reserved = 0;
+        h->remote_address = wr.wr.rdma.remote_addr;
+        h->rkey = wr.wr.rdma.rkey;
+        h->immediate_data = wr.opcode == UGDR_WR_RDMA_WRITE_WITH_IMM ? wr.imm_data : 0;
+        h->reserved = 0;
     }
-    std::memcpy(slot, &h, sizeof(h));
-    for (int i = 0; i < wr.num_sge; ++i) {
-        queue::Sge s{wr.sg_list[i].addr, wr.sg_list[i].length, wr.sg_list[i].lkey};
-        std::memcpy(slot + queue::kSendSgeOffset + i * sizeof(queue::Sge), &s, sizeof(s));
-    }
+    auto *sg = reinterpret_cast<queue::Sge *>(slot + queue::kSendSgeOffset);
+    for (int i = 0; i < wr.num_sge; ++i) sg[i] = queue::Sge{wr.sg_list[i].addr, wr.sg_list[i].length, wr.sg_list[i].lkey};
 }
 
 void encode_recv(uint8_t *slot, const ugdr_recv_wr &wr) {

@@ -1,7 +1,8 @@
 // The public C ABI (include/ugdr/api.hpp), implemented as a process-global client runtime.
 //
 // Parity: reference src/api/api.cpp:26-976 (proxy records, lazy daemon connect from
-// UGDR_DAEMON_SOCKET, per-CQ poll mutex, per-QP posting mutex, extern "C" surface).
+// UGDR_DAEMON_SOCKET, per-CQ poll mutex, per-QP posting mutex, extern "C" surface).  Here the
+// per-QP and per-CQ locks are spin locks: their critical sections are a few slot copies.
 //
 // Design here: every proxy starts with a magic word and the connection epoch it was created
 // under.  A destroyed proxy keeps its (small) shell with a dead magic, so a repeated destroy or
@@ -11,6 +12,7 @@
 #include "api/memory_export.hpp"
 #include "api/posting.hpp"
 #include "common/bytes.hpp"
+#include "common/spinlock.hpp"
 #include "control/client.hpp"
 #include "control/rpc.hpp"
 #include "queue/ring.hpp"
@@ -71,7 +73,7 @@ struct MrProxy {
 struct ugdr_cq : ProxyBase {
     ugdr_context *context = nullptr;
     ugdr::queue::Ring ring;
-    std::mutex poll_mu;
+    ugdr::SpinLock poll_mu;
 };
 
 struct ugdr_qp : ProxyBase {
@@ -79,7 +81,7 @@ struct ugdr_qp : ProxyBase {
     uint32_t qpn = 0;
     ugdr_qp_init_attr init{};
     ugdr::queue::Ring sq, rq;
-    std::mutex post_mu;
+    ugdr::SpinLock post_mu;
     std::atomic<int> state{UGDR_QPS_RESET};
     int access = 0;
     uint8_t timeout = 0, retry_cnt = 0, rnr_retry = 0, min_rnr_timer = 0;
@@ -338,7 +340,7 @@ int ugdr_destroy_cq(ugdr_cq *cq) noexcept {
     if (!rt().live(cq)) return EINVAL;
     Response resp;
     if (int rc = rt().call(make(kDestroyCq, cq->identity), &resp); rc != 0) return rc;
-    std::lock_guard<std::mutex> lk(cq->poll_mu);
+    std::lock_guard<ugdr::SpinLock> lk(cq->poll_mu);
     kill(cq);
     cq->ring = ugdr::queue::Ring();
     return 0;
@@ -347,7 +349,7 @@ int ugdr_destroy_cq(ugdr_cq *cq) noexcept {
 int ugdr_poll_cq(ugdr_cq *cq, int num_entries, ugdr_wc *wc) noexcept {
     if (cq == nullptr || cq->magic != kLive || num_entries < 0 || (num_entries > 0 && wc == nullptr))
         return -EINVAL;
-    std::lock_guard<std::mutex> lk(cq->poll_mu);
+    std::lock_guard<ugdr::SpinLock> lk(cq->poll_mu);
     if (cq->magic != kLive) return -EINVAL;
     ugdr::queue::SlotRun run = cq->ring.peek(uint32_t(num_entries));
     const uint32_t n = run.count();
@@ -408,7 +410,7 @@ int ugdr_destroy_qp(ugdr_qp *qp) noexcept {
     if (!rt().live(qp)) return EINVAL;
     Response resp;
     if (int rc = rt().call(make(kDestroyQp, qp->identity), &resp); rc != 0) return rc;
-    std::lock_guard<std::mutex> lk(qp->post_mu);
+    std::lock_guard<ugdr::SpinLock> lk(qp->post_mu);
     kill(qp);
     qp->sq = ugdr::queue::Ring();
     qp->rq = ugdr::queue::Ring();
@@ -482,7 +484,7 @@ int ugdr_post_send(ugdr_qp *qp, ugdr_send_wr *wr, ugdr_send_wr **bad_wr) noexcep
         if (bad_wr) *bad_wr = wr;
         return EINVAL;
     }
-    std::lock_guard<std::mutex> lk(qp->post_mu);
+    std::lock_guard<ugdr::SpinLock> lk(qp->post_mu);
     if (qp->magic != kLive || qp_state(qp) != UGDR_QPS_RTS) {
         if (bad_wr) *bad_wr = wr;
         return EINVAL;
@@ -495,7 +497,7 @@ int ugdr_post_recv(ugdr_qp *qp, ugdr_recv_wr *wr, ugdr_recv_wr **bad_wr) noexcep
         if (bad_wr) *bad_wr = wr;
         return EINVAL;
     }
-    std::lock_guard<std::mutex> lk(qp->post_mu);
+    std::lock_guard<ugdr::SpinLock> lk(qp->post_mu);
     const int st = qp_state(qp);
     if (qp->magic != kLive || (st != UGDR_QPS_INIT && st != UGDR_QPS_RTR && st != UGDR_QPS_RTS)) {
         if (bad_wr) *bad_wr = wr;

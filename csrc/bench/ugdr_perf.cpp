@@ -5,6 +5,7 @@
 //   ugdr_perf bw       --src-gpu A --dst-gpu B --op write|read --min 8 --max 1G --qd 64 --bytes-per-size T
 //   ugdr_perf posting  --batch B --wrs N                                    post_send into the SQ ring
 //   ugdr_perf ring     --batch B --wrs N                                    shared SPSC ring alone (2 threads)
+//   ugdr_perf postcore --batch B --wrs N                                    WR encode + publish path alone
 //   ugdr_perf plumbing --wrs 10000                                          CPU-only plumbing (host engine)
 //   ugdr_perf stress   --src-gpu A --dst-gpu B --qps 64 --depth 128 --sges 16 --rounds R
 //                      verbs-feature stress: per QP an interleave of
@@ -16,6 +17,7 @@
 // Output: one key=value line per measurement (reference style, benchmarks/*.cpp) and a JSON
 // line with the same fields.  Payload: uniform uint8 from a seed; every size's destination is
 // compared byte-for-byte with the source once.
+#include "api/posting.hpp"
 #include "queue/layout.hpp"
 #include "queue/ring.hpp"
 #include "ugdr/api.hpp"
@@ -534,6 +536,39 @@ int run_ring(const Opts &o) {
     return ok ? 0 : 2;
 }
 
+// Posting core without the public API's per-call checks: chains of `batch` zero-SGE RDMA WRITEs
+// encoded by the library's posting routine into a 64-slot send ring, consumed in the same thread
+// right after each chain (the ring stays in L1).  Same setup as the reference's
+// benchmarks/wr_posting_benchmark.cpp, so the two numbers compare directly.
+int run_postcore(const Opts &o) {
+    ugdr::queue::Ring prod, cons;
+    const ugdr::queue::RingGeometry g{ugdr::queue::kSendRing, 64, ugdr::queue::send_stride(1)};
+    if (int rc = ugdr::queue::Ring::create(g, &prod)) die("ring create", rc);
+    if (int rc = ugdr::queue::Ring::attach(::dup(prod.fd()), g, &cons)) die("ring attach", rc);
+    const uint32_t batch = uint32_t(std::max<uint64_t>(1, std::min<uint64_t>(o.batch, 64)));
+    std::vector<ugdr_send_wr> wr(batch);
+    for (uint32_t i = 0; i < batch; ++i) {
+        wr[i] = ugdr_send_wr{};
+        wr[i].wr_id = i;
+        wr[i].opcode = UGDR_WR_RDMA_WRITE;
+        wr[i].next = i + 1 < batch ? &wr[i + 1] : nullptr;
+    }
+    const uint64_t iters = std::max<uint64_t>(1, o.wrs / batch);
+    const auto t0 = Clock::now();
+    for (uint64_t it = 0; it < iters; ++it) {
+        ugdr_send_wr *bad = nullptr;
+        if (ugdr::api::post_send_chain(prod, 1, wr.data(), &bad) != 0) die("post_send_chain", EIO);
+        if (cons.peek(batch).count() != batch) die("ring peek", EIO);
+        cons.release(batch);
+    }
+    const double sec = std::chrono::duration<double>(Clock::now() - t0).count();
+    const double rate = double(iters * batch) / sec / 1e6;
+    std::printf("benchmark=ugdr_postcore batch=%u wrs=%llu seconds=%.6f MWR_per_s=%.3f\n", batch,
+                (unsigned long long)(iters * batch), sec, rate);
+    std::printf("{\"benchmark\": \"ugdr_postcore\", \"batch\": %u, \"MWRps\": %.3f}\n", batch, rate);
+    return 0;
+}
+
 // ---- CPU-only plumbing workload -------------------------------------------------------
 
 // One client and the daemon's host-memory engine: 1 PD, two 1 MiB host MRs, one QP of depth
@@ -889,6 +924,7 @@ int main(int argc, char **argv) {
     if (o.mode == "stress") return run_stress(o);
     if (o.mode == "plumbing") return run_plumbing(o);
     if (o.mode == "ring") return run_ring(o);
+    if (o.mode == "postcore") return run_postcore(o);
     std::fprintf(stderr, "ugdr_perf: unknown mode %s\n", o.mode.c_str());
     return 2;
 }

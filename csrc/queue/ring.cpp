@@ -106,6 +106,17 @@ SlotRun Ring::reserve(uint32_t want) {
     return run_at(prod_tail_, n);
 }
 
+SlotRun Ring::reserve_free(bool refresh) {
+    uint64_t used = prod_tail_ - prod_head_seen_;
+    if (refresh || used >= geom_.capacity) {
+        prod_head_seen_ = head();
+        used = prod_tail_ - prod_head_seen_;
+    }
+    const uint32_t n = used >= geom_.capacity ? 0u : uint32_t(geom_.capacity - used);
+    reserved_ = n;
+    return run_at(prod_tail_, n);
+}
+
 void Ring::publish(uint32_t n) {
     n = std::min(n, reserved_);
     reserved_ = 0;

@@ -61,6 +61,9 @@ class Ring {
 
     // Producer: claim up to `want` free slots (never more than are free).  Returns the run.
     SlotRun reserve(uint32_t want);
+    // Producer: claim every slot that is free according to the consumer cursor seen last; the
+    // shared cursor is re-read only when that shows none free, or when `refresh` is set.
+    SlotRun reserve_free(bool refresh);
     // Producer: make `n` previously reserved slots visible to the consumer.
     void publish(uint32_t n);
     // Consumer: look at up to `want` published slots without consuming them.
