@@ -9,7 +9,7 @@ OBJ       := build/obj
 ARCH      := -gencode arch=compute_100a,code=sm_100a
 
 CPPFLAGS  := -Icsrc -Iinclude -I$(CUDA_HOME)/include
-CXXFLAGS  := -std=c++20 -O2 -g -fPIC -Wall -Wextra -Wno-unused-parameter -pthread
+CXXFLAGS  := -std=c++20 -O2 -g -fPIC -fno-semantic-interposition -Wall -Wextra -Wno-unused-parameter -pthread
 NVFLAGS   := -std=c++17 $(ARCH) -O3 -lineinfo -Xcompiler -fPIC -Xptxas -v
 LDLIBS    := -L$(CUDA_HOME)/lib64 -lcudart_static -ldl -lrt -lpthread
 
@@ -65,16 +65,16 @@ TSAN_FLAGS := -fsanitize=thread
 
 $(SAN)/asan/%.o: csrc/%.cpp
 	@mkdir -p $(dir $@)
-	$(SAN_CXX) $(CPPFLAGS) $(CXXFLAGS) $(ASAN_FLAGS) -c $< -o $@
+	$(SAN_CXX) $(CPPFLAGS) $(CXXFLAGS) $(ASAN_FLAGS) -MMD -MP -c $< -o $@
 $(SAN)/asan/tests/%.o: tests/native/%.cpp
 	@mkdir -p $(dir $@)
-	$(SAN_CXX) $(CPPFLAGS) $(CXXFLAGS) $(ASAN_FLAGS) -c $< -o $@
+	$(SAN_CXX) $(CPPFLAGS) $(CXXFLAGS) $(ASAN_FLAGS) -MMD -MP -c $< -o $@
 $(SAN)/tsan/%.o: csrc/%.cpp
 	@mkdir -p $(dir $@)
-	$(SAN_CXX) $(CPPFLAGS) $(CXXFLAGS) $(TSAN_FLAGS) -c $< -o $@
+	$(SAN_CXX) $(CPPFLAGS) $(CXXFLAGS) $(TSAN_FLAGS) -MMD -MP -c $< -o $@
 $(SAN)/tsan/tests/%.o: tests/native/%.cpp
 	@mkdir -p $(dir $@)
-	$(SAN_CXX) $(CPPFLAGS) $(CXXFLAGS) $(TSAN_FLAGS) -c $< -o $@
+	$(SAN_CXX) $(CPPFLAGS) $(CXXFLAGS) $(TSAN_FLAGS) -MMD -MP -c $< -o $@
 
 CU_OBJS := $(LIB_CU:csrc/%.cu=$(OBJ)/%.cu.o)
 $(SAN)/asan/ugdr_native_tests: $(LIB_CXX:csrc/%.cpp=$(SAN)/asan/%.o) $(TEST_SRCS:tests/native/%.cpp=$(SAN)/asan/tests/%.o) $(CU_OBJS)
@@ -88,5 +88,5 @@ tsan: $(SAN)/tsan/ugdr_native_tests
 clean:
 	rm -rf build/obj build/san $(OUT)/libugdr.so $(OUT)/ugdr_daemon $(OUT)/ugdr_client $(OUT)/ugdr_native_tests $(OUT)/ugdr_perf
 
--include $(shell find build/obj -name '*.d' 2>/dev/null)
+-include $(shell find build/obj build/san -name '*.d' 2>/dev/null)
 .PHONY: all clean asan tsan

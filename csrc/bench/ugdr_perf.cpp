@@ -484,11 +484,17 @@ ugdr_mr *dev_mr(ugdr_pd *pd, int gpu, uint64_t bytes, int access, void **buf) {
 // ---- shared ring alone -------------------------------------------------------------------------
 
 // Descriptor rate of the shared SPSC ring with no daemon: a producer thread reserves, writes (the
-// first 16 bytes of every 64-byte slot) and publishes `batch` slots at a time; a consumer thread
-// peeks, reads and releases them.  Reference counterpart: benchmarks/shared_ring_benchmark.cpp
+// first 16 bytes of every 64-byte slot) and publishes whole batches of `batch` slots; a consumer
+// thread peeks, reads and releases whole batches.  Reference counterpart: benchmarks/shared_ring_benchmark.cpp
 // (descriptors per second at batch 1 and 32).
 int run_ring(const Opts &o) {
-    ugdr::queue::Ring prod, cons;
+    // Each side's ring view (its private cursor copies) on its own cache lines, as in real use
+    // where producer and consumer are different processes.
+    struct alignas(128) Side {
+        ugdr::queue::Ring r;
+    };
+    Side ps, cs;
+    ugdr::queue::Ring &prod = ps.r, &cons = cs.r;
     const ugdr::queue::RingGeometry g{ugdr::queue::kSendRing, 4096, 64};
     if (int rc = ugdr::queue::Ring::create(g, &prod)) die("ring create", rc);
     if (int rc = ugdr::queue::Ring::attach(::dup(prod.fd()), g, &cons)) die("ring attach", rc);
@@ -499,8 +505,11 @@ int run_ring(const Opts &o) {
     std::thread consumer([&] {
         uint64_t got = 0, sum = 0;
         while (got < total) {
-            ugdr::queue::SlotRun r = cons.peek(batch);
+            // Whole batches only (as the reference's benchmark consumes): a short peek is retried.
+            const uint32_t want = uint32_t(std::min<uint64_t>(batch, total - got));
+            ugdr::queue::SlotRun r = cons.peek(want);
             const uint32_t n = r.count();
+            if (n < want) continue;
             for (uint32_t i = 0; i < n; ++i) {
                 const uint8_t *slot = i < r.first_count ? r.first + uint64_t(i) * 64 : r.second + uint64_t(i - r.first_count) * 64;
                 uint64_t v;
@@ -517,6 +526,7 @@ int run_ring(const Opts &o) {
         const uint32_t want = uint32_t(std::min<uint64_t>(batch, total - sent));
         ugdr::queue::SlotRun r = prod.reserve(want);
         const uint32_t n = r.count();
+        if (n < want) continue;  // whole batches only
         for (uint32_t i = 0; i < n; ++i) {
             uint8_t *slot = i < r.first_count ? r.first + uint64_t(i) * 64 : r.second + uint64_t(i - r.first_count) * 64;
             const uint64_t v = sent + i;

@@ -78,13 +78,14 @@ uint64_t Ring::head() const { return cursor_ref(header()->head.value).load(std::
 void Ring::resync() {
     prod_tail_ = cons_tail_seen_ = tail();
     cons_head_ = prod_head_seen_ = head();
+    prod_index_ = uint32_t(prod_tail_ % geom_.capacity);
+    cons_index_ = uint32_t(cons_head_ % geom_.capacity);
     reserved_ = peeked_ = 0;
 }
 
-SlotRun Ring::run_at(uint64_t cursor, uint32_t count) const {
+SlotRun Ring::run_at(uint32_t index, uint32_t count) const {
     SlotRun run;
     if (count == 0) return run;
-    const uint32_t index = uint32_t(cursor % geom_.capacity);
     const uint32_t first = std::min(count, geom_.capacity - index);
     run.first = slots() + uint64_t(index) * geom_.stride;
     run.first_count = first;
@@ -103,7 +104,7 @@ SlotRun Ring::reserve(uint32_t want) {
     }
     const uint32_t n = uint32_t(std::min<uint64_t>(want, geom_.capacity - used));
     reserved_ = n;
-    return run_at(prod_tail_, n);
+    return run_at(prod_index_, n);
 }
 
 SlotRun Ring::reserve_free(bool refresh) {
@@ -114,7 +115,7 @@ SlotRun Ring::reserve_free(bool refresh) {
     }
     const uint32_t n = used >= geom_.capacity ? 0u : uint32_t(geom_.capacity - used);
     reserved_ = n;
-    return run_at(prod_tail_, n);
+    return run_at(prod_index_, n);
 }
 
 void Ring::publish(uint32_t n) {
@@ -122,6 +123,8 @@ void Ring::publish(uint32_t n) {
     reserved_ = 0;
     if (n == 0) return;
     prod_tail_ += n;
+    prod_index_ += n;
+    if (prod_index_ >= geom_.capacity) prod_index_ -= geom_.capacity;
     cursor_ref(header()->tail.value).store(prod_tail_, std::memory_order_release);
 }
 
@@ -134,7 +137,7 @@ SlotRun Ring::peek(uint32_t want) {
     }
     const uint32_t n = uint32_t(std::min<uint64_t>(want, avail));
     peeked_ = n;
-    return run_at(cons_head_, n);
+    return run_at(cons_index_, n);
 }
 
 void Ring::release(uint32_t n) {
@@ -142,6 +145,8 @@ void Ring::release(uint32_t n) {
     peeked_ = 0;
     if (n == 0) return;
     cons_head_ += n;
+    cons_index_ += n;
+    if (cons_index_ >= geom_.capacity) cons_index_ -= geom_.capacity;
     cursor_ref(header()->head.value).store(cons_head_, std::memory_order_release);
 }
 

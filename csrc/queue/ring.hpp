@@ -82,12 +82,15 @@ class Ring {
     void set_error_word(uint64_t v);
 
   private:
-    SlotRun run_at(uint64_t cursor, uint32_t count) const;
+    SlotRun run_at(uint32_t index, uint32_t count) const;
 
     SharedMapping map_;
     RingGeometry geom_;
     uint64_t prod_tail_ = 0, prod_head_seen_ = 0;
     uint64_t cons_head_ = 0, cons_tail_seen_ = 0;
+    // prod_tail_ % capacity and cons_head_ % capacity, kept up to date by publish / release so
+    // the fast paths never divide (capacity need not be a power of two).
+    uint32_t prod_index_ = 0, cons_index_ = 0;
     uint32_t reserved_ = 0, peeked_ = 0;
 };
 

@@ -111,8 +111,14 @@ class Echo : public ipc::Handler {
         r.payload = req.payload;
         return r;
     }
-    void on_disconnect(ipc::SessionId) noexcept override { disconnects++; }
+    void on_disconnect(ipc::SessionId s) noexcept override {
+        last_gone.store(int64_t(s));
+        if (watch.load() == int64_t(s)) watched_gone.store(true);
+        disconnects++;
+    }
     std::atomic<int> disconnects{0};
+    std::atomic<int64_t> last_gone{-1}, watch{-1};
+    std::atomic<bool> watched_gone{false};
 };
 }  // namespace
 
@@ -137,9 +143,13 @@ TEST(ipc_client_server_sessions) {
     CHECK(ra.payload == pa && rb.payload == pb);
     CHECK(ra.env.status != rb.env.status);  // distinct session ids
     CHECK_EQ(ra.env.flags, ipc::kFlagResponse);
+    // The second server's liveness probe is also a session (it connects and leaves), so watch
+    // for client a's session id specifically.
+    h.watch.store(int64_t(ra.env.status));
     a.close();
-    for (int i = 0; i < 200 && h.disconnects.load() < 1; ++i) usleep(1000);
-    CHECK_EQ(h.disconnects.load(), 1);
+    for (int i = 0; i < 5000 && !h.watched_gone.load(); ++i) usleep(1000);  // bounded: 5 s
+    CHECK(h.watched_gone.load());
+    CHECK(h.disconnects.load() <= 2);  // a, and possibly the probe; b is still connected
     stop.store(true);
     loop.join();
     srv.close();
