@@ -332,3 +332,15 @@ def test_ring_benchmark_moves_every_descriptor():
                            capture_output=True, text=True, timeout=120)
         out = [json.loads(line) for line in r.stdout.splitlines() if line.startswith("{")]
         assert r.returncode == 0 and out and out[-1]["correct"], r.stdout + r.stderr
+
+
+def test_python_example_runs():
+    """examples/host_rdma.py runs end to end (gather WRITE, WRITE_WITH_IMM, FETCH_ADD)."""
+    import subprocess
+    import sys
+
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = {k: v for k, v in os.environ.items() if k != "UGDR_DAEMON_SOCKET"}
+    r = subprocess.run([sys.executable, os.path.join(repo, "examples", "host_rdma.py")], capture_output=True,
+                       text=True, timeout=120, env=env)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
