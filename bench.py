@@ -152,16 +152,31 @@ def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None
         rsp[k].connect(info[sender_of(rank, k, world)]["req"][k])
     comm.barrier()
 
-    def post_step(step_id: int):
-        for k in range(PEERS):
+    # Work requests are built once per distinct (step pattern, QP) and reused: a step's WRs differ
+    # only in their slices, which repeat with period 1 (N > 1) or nslices / 7 (N = 1).
+    period = nslices // PEERS if loop else 1
+    wr_cache: dict[tuple[int, int], object] = {}
+
+    def step_wr(step_id: int, k: int):
+        key = (step_id % period, k)
+        w = wr_cache.get(key)
+        if w is None:
             dst = peer_of(rank, k, world)
             sidx = k
             dslot = (dst + 1 + k) % SLOTS
             if loop:
                 sidx = dslot = (step_id * PEERS + k) % nslices
-            req[k].post_write((src_buf.data_ptr() + sidx * slot, slot, src_mr.lkey),
-                              info[dst]["addr"] + dslot * slot, info[dst]["rkey"],
-                              wr_id=(step_id << 8) | k)
+            w = V.QueuePair.make_send_wr(N.WR_RDMA_WRITE, [(src_buf.data_ptr() + sidx * slot, slot, src_mr.lkey)],
+                                         remote_addr=info[dst]["addr"] + dslot * slot, rkey=info[dst]["rkey"],
+                                         wr_id=k)
+            wr_cache[key] = w
+        return w
+
+    def post_step(step_id: int):
+        for k in range(PEERS):
+            rc, _ = req[k].post_send_raw([step_wr(step_id, k)])
+            if rc != 0:
+                raise RuntimeError(f"rank {rank}: ugdr_post_send failed ({rc})")
 
     all_ctx = None
     if rank == 0:
@@ -225,16 +240,18 @@ def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None
         post_step(s)
         cq.wait(PEERS, timeout=60)
     comm.barrier()
-    # Two steps in flight: step s + 1 is posted before step s's completions are polled, as a
-    # streaming client would; every step still posts its 7 WQEs and reads its 7 CQEs.
+    # Up to four steps in flight: new steps are posted before older steps' completions are
+    # polled, as a streaming client would; every step still posts its 7 WQEs and reads its 7 CQEs.
+    inflight = 4
     e2e_bad = 0
     t0 = time.perf_counter()
-    post_step(0)
+    for s in range(min(inflight, K)):
+        post_step(s)
     for s in range(K):
-        if s + 1 < K:
-            post_step(s + 1)
         wcs = cq.wait(PEERS, timeout=60)
         e2e_bad += sum(1 for w in wcs if w.status != N.WC_SUCCESS)
+        if s + inflight < K:
+            post_step(s + inflight)
     t_e2e = time.perf_counter() - t0
     t_e2e = comm.max(t_e2e)
     if e2e_bad:
@@ -293,7 +310,7 @@ def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None
         "e2e": {"value": round(e2e, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": world * PEERS * wqe_bytes,
                 "d2h_bytes_per_step": world * PEERS * cqe_bytes,
-                "path": "ugdr_post_send -> persistent executor -> ugdr_poll_cq, two steps in flight, wall clock, "
+                "path": "ugdr_post_send -> persistent executor -> ugdr_poll_cq, four steps in flight, wall clock, "
                         "max over ranks"},
         "gpu_launches": world,
         "executor_launches_rank0": int(stats.launches),
