@@ -82,8 +82,15 @@ $(SAN)/asan/ugdr_native_tests: $(LIB_CXX:csrc/%.cpp=$(SAN)/asan/%.o) $(TEST_SRCS
 $(SAN)/tsan/ugdr_native_tests: $(LIB_CXX:csrc/%.cpp=$(SAN)/tsan/%.o) $(TEST_SRCS:tests/native/%.cpp=$(SAN)/tsan/tests/%.o) $(CU_OBJS)
 	$(SAN_CXX) $(TSAN_FLAGS) -o $@ $^ $(LDLIBS)
 
-asan: $(SAN)/asan/ugdr_native_tests
-tsan: $(SAN)/tsan/ugdr_native_tests
+# Whole daemons with instrumented host code (linked statically against the instrumented objects),
+# for running the Python API suites against them via UGDR_DAEMON_BIN.
+$(SAN)/asan/ugdr_daemon: $(LIB_CXX:csrc/%.cpp=$(SAN)/asan/%.o) $(SAN)/asan/daemon/main.o $(CU_OBJS)
+	$(SAN_CXX) $(ASAN_FLAGS) -o $@ $^ $(LDLIBS)
+$(SAN)/tsan/ugdr_daemon: $(LIB_CXX:csrc/%.cpp=$(SAN)/tsan/%.o) $(SAN)/tsan/daemon/main.o $(CU_OBJS)
+	$(SAN_CXX) $(TSAN_FLAGS) -o $@ $^ $(LDLIBS)
+
+asan: $(SAN)/asan/ugdr_native_tests $(SAN)/asan/ugdr_daemon
+tsan: $(SAN)/tsan/ugdr_native_tests $(SAN)/tsan/ugdr_daemon
 
 clean:
 	rm -rf build/obj build/san $(OUT)/libugdr.so $(OUT)/ugdr_daemon $(OUT)/ugdr_client $(OUT)/ugdr_native_tests $(OUT)/ugdr_perf

@@ -22,6 +22,7 @@
 #include <cerrno>
 #include <cstdlib>
 #include <cstring>
+#include <deque>
 #include <memory>
 #include <mutex>
 #include <string>
@@ -122,10 +123,35 @@ class Runtime {
     std::mutex lists_mu;
     std::unordered_set<ugdr_device **> lists;
 
+    // Destroyed proxies keep a dead magic for a while: a repeated destroy, or a use shortly
+    // after destroy, finds kDead instead of freed memory.  The shells wait in a bounded
+    // quarantine and the oldest is freed once it holds kQuarantine of them, so a client that
+    // creates and destroys objects forever keeps a fixed amount of memory.
+    template <typename T> void retire(T *obj, ProxyBase *base) {
+        base->magic = kDead;
+        Shell victim{nullptr, nullptr};
+        {
+            std::lock_guard<std::mutex> lk(quarantine_mu_);
+            quarantine_.push_back(Shell{obj, [](void *o) { delete static_cast<T *>(o); }});
+            if (quarantine_.size() > kQuarantine) {
+                victim = quarantine_.front();
+                quarantine_.pop_front();
+            }
+        }
+        if (victim.obj != nullptr) victim.del(victim.obj);
+    }
+
   private:
+    struct Shell {
+        void *obj;
+        void (*del)(void *);
+    };
+    static constexpr size_t kQuarantine = 4096;
     std::mutex mu_;
     ControlClient client_;
     std::string path_;
+    std::mutex quarantine_mu_;
+    std::deque<Shell> quarantine_;
 };
 
 Runtime &rt() { return Runtime::get(); }
@@ -142,7 +168,6 @@ Request make(uint32_t method, uint64_t identity = 0) {
     return r;
 }
 
-void kill(ProxyBase *p) { p->magic = kDead; }
 
 int qp_state(ugdr_qp *qp) {
     if (qp->sq.valid() && qp->sq.error_word() == UGDR_QPS_ERR) return UGDR_QPS_ERR;
@@ -205,7 +230,7 @@ void ugdr_free_device_list(ugdr_device **list) noexcept {
         return;
     }
     rt().lists.erase(it);
-    for (ugdr_device **p = list; *p != nullptr; ++p) kill(*p);  // shells stay valid memory
+    for (ugdr_device **p = list; *p != nullptr; ++p) rt().retire(*p, *p);
     delete[] list;
 }
 
@@ -243,7 +268,7 @@ int ugdr_close_device(ugdr_context *ctx) noexcept {
         errno = rc;
         return -1;
     }
-    kill(ctx);
+    rt().retire(ctx, ctx);
     return 0;
 }
 
@@ -262,7 +287,7 @@ int ugdr_dealloc_pd(ugdr_pd *pd) noexcept {
     if (!rt().live(pd)) return EINVAL;
     Response resp;
     if (int rc = rt().call(make(kDestroyPd, pd->identity), &resp); rc != 0) return rc;
-    kill(pd);
+    rt().retire(pd, pd);
     return 0;
 }
 
@@ -303,7 +328,7 @@ int ugdr_dereg_mr(ugdr_mr *mr) noexcept {
     if (!rt().live(&p->b)) return EINVAL;
     Response resp;
     if (int rc = rt().call(make(kDeregisterMr, p->b.identity), &resp); rc != 0) return rc;
-    kill(&p->b);
+    rt().retire(p, &p->b);
     return 0;
 }
 
@@ -340,9 +365,12 @@ int ugdr_destroy_cq(ugdr_cq *cq) noexcept {
     if (!rt().live(cq)) return EINVAL;
     Response resp;
     if (int rc = rt().call(make(kDestroyCq, cq->identity), &resp); rc != 0) return rc;
-    std::lock_guard<ugdr::SpinLock> lk(cq->poll_mu);
-    kill(cq);
-    cq->ring = ugdr::queue::Ring();
+    {
+        std::lock_guard<ugdr::SpinLock> lk(cq->poll_mu);
+        cq->magic = kDead;
+        cq->ring = ugdr::queue::Ring();
+    }
+    rt().retire(cq, cq);
     return 0;
 }
 
@@ -410,10 +438,13 @@ int ugdr_destroy_qp(ugdr_qp *qp) noexcept {
     if (!rt().live(qp)) return EINVAL;
     Response resp;
     if (int rc = rt().call(make(kDestroyQp, qp->identity), &resp); rc != 0) return rc;
-    std::lock_guard<ugdr::SpinLock> lk(qp->post_mu);
-    kill(qp);
-    qp->sq = ugdr::queue::Ring();
-    qp->rq = ugdr::queue::Ring();
+    {
+        std::lock_guard<ugdr::SpinLock> lk(qp->post_mu);
+        qp->magic = kDead;
+        qp->sq = ugdr::queue::Ring();
+        qp->rq = ugdr::queue::Ring();
+    }
+    rt().retire(qp, qp);
     return 0;
 }
 

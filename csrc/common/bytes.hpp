@@ -41,6 +41,7 @@ class ByteReader {
     }
     bool raw(void *dst, size_t n) {
         if (n_ - off_ < n) return false;
+        if (n == 0) return true;  // an empty read: dst and p_ may be null
         std::memcpy(dst, p_ + off_, n);
         off_ += n;
         return true;

@@ -275,13 +275,15 @@ size_t CpuEngine::progress_qp(QpView &v) {
             v.rnr_next_ns = 0;
             stats_.bytes_moved += op_atomic(op) ? 8 : total;
         }
+        // The SQ slot is returned before the completion is visible: a client that sees the CQE
+        // may post into that slot at once (an HCA retires the WQE before it reports it).
+        qp.sq.peek(1);
+        qp.sq.release(1);
         if (need_cqe) {
             queue::Cqe c{h.wr_id, status, wc_opcode(op), uint32_t(total), 0, qp.qpn, 0};
             if (status != UGDR_WC_SUCCESS) c.byte_length = 0;
             produce(qp.send_cq, &c);
         }
-        qp.sq.peek(1);
-        qp.sq.release(1);
         ++retired;
         stats_.wrs_completed += 1;
         if (status != UGDR_WC_SUCCESS) {

@@ -881,11 +881,16 @@ __device__ int retire_commit(Warp &w, DevQp *qp, const QpView &v, queue::Cqe *cq
                 ++retire_n;
             }
         }
+        if (retire_n > 0) {
+            // Return the SQ slots before the completions become visible: a client that polls a
+            // CQE may post into its slot at once.  The WRs' fields are already in registers and
+            // their payloads are done; the publish below is a release, so it orders this store.
+            qp->st.sq_head = head + retire_n;
+            st_vol64(&v.sq->head.value, head + retire_n);
+        }
         if (granted > 0 && !publish_cq(w, v.send_cq, first, cqe_buf, granted, max_ns)) {
             verdict = -1;
         } else if (retire_n > 0) {
-            qp->st.sq_head = head + retire_n;
-            st_vol64(&v.sq->head.value, head + retire_n);  // slots may be reused by the client
             atomicAdd(&w.p->stats->wrs_completed, (unsigned long long)retire_n);
             atomicAdd(&w.p->stats->retired, (unsigned long long)retire_n);
             atomicMax(&w.p->stats->last_end_ns, (unsigned long long)gtime());

@@ -56,6 +56,35 @@ def test_config0_cpu_plumbing_10k_writes(cpu_daemon):
     print(f"config0: {total} x 4 KiB WRITEs in {dt * 1e3:.1f} ms ({total / dt / 1e6:.3f} MWR/s)")
 
 
+def test_a_polled_completion_frees_its_send_slot(cpu_daemon):
+    """A full SQ: once a completion has been polled, the next post must find its slot free at once
+    (the engine returns the SQ slot before it publishes the CQE, as an HCA retires a WQE first)."""
+    ctx, pd, cq, a, b = _pair(depth=4, cq_depth=64)
+    buf = V.HostBuffer(1 << 16)
+    mr = pd.reg_mr(buf.addr, 1 << 16, ACC)
+    try:
+        posted = done = 0
+        while posted < 4:  # fill the SQ
+            a.post_write((buf.addr, 8, mr.lkey), buf.addr + 4096, mr.rkey, wr_id=posted)
+            posted += 1
+        while done < 2000:
+            got = cq.wait(1, timeout=10)
+            assert got and all(w.status == N.WC_SUCCESS for w in got)
+            done += len(got)
+            for _ in got:  # every polled completion is a slot that must take a new WR at once
+                a.post_write((buf.addr, 8, mr.lkey), buf.addr + 4096, mr.rkey, wr_id=posted)
+                posted += 1
+        assert len(cq.wait(posted - done, timeout=10)) == posted - done
+    finally:
+        a.destroy()
+        b.destroy()
+        mr.dereg()
+        cq.destroy()
+        pd.dealloc()
+        ctx.close()
+        buf.free()
+
+
 def test_write_with_imm_consumes_rq_in_order(cpu_daemon):
     ctx, pd, cq, a, b = _pair()
     buf = V.HostBuffer(1 << 16)

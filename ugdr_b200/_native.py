@@ -13,7 +13,8 @@ from pathlib import Path
 
 LIB_DIR = Path(os.environ.get("UGDR_LIB_DIR") or Path(__file__).resolve().parent / "_lib")
 LIB_PATH = LIB_DIR / "libugdr.so"
-DAEMON_PATH = LIB_DIR / "ugdr_daemon"
+# UGDR_DAEMON_BIN selects another daemon build (e.g. the sanitizer one) for the launcher.
+DAEMON_PATH = Path(os.environ.get("UGDR_DAEMON_BIN") or LIB_DIR / "ugdr_daemon")
 
 # ---- enums (numeric values are libibverbs') -------------------------------------------------
 QPT_RC = 2

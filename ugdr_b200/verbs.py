@@ -66,8 +66,9 @@ class Daemon:
         if not N.DAEMON_PATH.exists():
             raise RuntimeError(f"{N.DAEMON_PATH} missing: build the native tree first")
         # The daemon's stderr goes to a file (a pipe nobody drains could block its threads).
-        self.log_path = log_path or os.path.join(self._dir or tempfile.gettempdir(),
-                                                 f"ugdr-daemon-{os.getpid()}.log")
+        log_dir = os.environ.get("UGDR_DAEMON_LOG_DIR") or self._dir or tempfile.gettempdir()
+        self.log_path = log_path or tempfile.mkstemp(prefix=f"ugdr-daemon-{os.getpid()}-", suffix=".log",
+                                                     dir=log_dir)[1]
         self._log = open(self.log_path, "w")
         self.proc = subprocess.Popen(args, env=env, stderr=self._log, stdout=self._log)
         deadline = time.time() + 120
