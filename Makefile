@@ -26,7 +26,8 @@ LIB_OBJS := $(LIB_CXX:csrc/%.cpp=$(OBJ)/%.o) $(LIB_CU:csrc/%.cu=$(OBJ)/%.cu.o)
 TEST_SRCS := $(wildcard tests/native/*.cpp)
 TEST_OBJS := $(TEST_SRCS:tests/native/%.cpp=$(OBJ)/tests/%.o)
 
-all: $(OUT)/libugdr.so $(OUT)/ugdr_daemon $(OUT)/ugdr_client $(OUT)/ugdr_native_tests $(OUT)/ugdr_perf
+all: $(OUT)/libugdr.so $(OUT)/ugdr_daemon $(OUT)/ugdr_client $(OUT)/ugdr_native_tests $(OUT)/ugdr_perf \
+     $(OUT)/ugdr_engine_bench
 
 $(OBJ)/%.o: csrc/%.cpp
 	@mkdir -p $(dir $@)
@@ -51,6 +52,9 @@ $(OUT)/ugdr_client: $(OBJ)/apps/client_main.o $(OUT)/libugdr.so
 	$(CXX) -o $@ $< -L$(OUT) -lugdr -Wl,-rpath,'$$ORIGIN' -pthread
 
 $(OUT)/ugdr_perf: $(OBJ)/bench/ugdr_perf.o $(OUT)/libugdr.so
+	$(CXX) -o $@ $< -L$(OUT) -lugdr -Wl,-rpath,'$$ORIGIN' $(LDLIBS)
+
+$(OUT)/ugdr_engine_bench: $(OBJ)/bench/engine_bench.o $(OUT)/libugdr.so
 	$(CXX) -o $@ $< -L$(OUT) -lugdr -Wl,-rpath,'$$ORIGIN' $(LDLIBS)
 
 $(OUT)/ugdr_native_tests: $(TEST_OBJS) $(OUT)/libugdr.so
@@ -93,7 +97,7 @@ asan: $(SAN)/asan/ugdr_native_tests $(SAN)/asan/ugdr_daemon
 tsan: $(SAN)/tsan/ugdr_native_tests $(SAN)/tsan/ugdr_daemon
 
 clean:
-	rm -rf build/obj build/san $(OUT)/libugdr.so $(OUT)/ugdr_daemon $(OUT)/ugdr_client $(OUT)/ugdr_native_tests $(OUT)/ugdr_perf
+	rm -rf build/obj build/san $(OUT)/libugdr.so $(OUT)/ugdr_daemon $(OUT)/ugdr_client $(OUT)/ugdr_native_tests $(OUT)/ugdr_perf $(OUT)/ugdr_engine_bench
 
 -include $(shell find build/obj build/san -name '*.d' 2>/dev/null)
 .PHONY: all clean asan tsan

@@ -53,7 +53,10 @@ int CpuEngine::attach_mr(control::Mr &mr) {
     return 0;
 }
 
-void CpuEngine::detach_mr(control::Mr &mr) noexcept { mrs_.erase(mr.table_slot); }
+void CpuEngine::detach_mr(control::Mr &mr) noexcept {
+    mrs_.erase(mr.table_slot);
+    for (QpView &v : qps_) v.lm = v.rm = nullptr;
+}
 
 int CpuEngine::attach_cq(control::Cq &) { return 0; }
 void CpuEngine::detach_cq(control::Cq &) noexcept {}
@@ -94,6 +97,18 @@ const CpuEngine::MrView *CpuEngine::find(uint32_t key, bool remote) const {
     if (it == mrs_.end()) return nullptr;
     if ((remote ? it->second.rkey : it->second.lkey) != key) return nullptr;
     return &it->second;
+}
+
+const CpuEngine::MrView *CpuEngine::find_cached(QpView &v, uint32_t key, bool remote) const {
+    const MrView *&slot = remote ? v.rm : v.lm;
+    uint32_t &cached = remote ? v.rkey : v.lkey;
+    if (slot != nullptr && cached == key) return slot;
+    const MrView *m = find(key, remote);
+    if (m != nullptr) {
+        slot = m;
+        cached = key;
+    }
+    return m;
 }
 
 bool CpuEngine::produce(control::Cq *cq, const void *cqe) {
@@ -171,7 +186,7 @@ size_t CpuEngine::progress_qp(QpView &v) {
                 break;
             }
             if (sg.length == 0) continue;
-            const MrView *m = find(sg.lkey, false);
+            const MrView *m = find_cached(v, sg.lkey, false);
             uint8_t *p = (m != nullptr && m->pd_num == qp.pd_num) ? resolve(m, sg.address, sg.length)
                                                                    : nullptr;
             if (p == nullptr || (local_written(op) && (m->access & UGDR_ACCESS_LOCAL_WRITE) == 0)) {
@@ -191,7 +206,7 @@ size_t CpuEngine::progress_qp(QpView &v) {
                 status = UGDR_WC_REM_OP_ERR;
             } else {
                 const uint32_t need = remote_access_for(op);
-                const MrView *m = find(h.rkey, true);
+                const MrView *m = find_cached(v, h.rkey, true);
                 if (total != 0 || op_atomic(op)) {
                     remote = (m != nullptr && m->pd_num == peer->pd_num && (m->access & need) != 0 &&
                               (peer->access & need) != 0)

@@ -53,8 +53,13 @@ class CpuEngine : public control::Engine {
         control::Qp *qp = nullptr;
         uint32_t rnr_attempts = 0;
         uint64_t rnr_next_ns = 0;
+        // Last local and remote key this QP resolved (WRs of one QP mostly reuse one MR pair);
+        // cleared whenever an MR is detached.
+        const MrView *lm = nullptr, *rm = nullptr;
+        uint32_t lkey = 0, rkey = 0;
     };
     const MrView *find(uint32_t key, bool remote) const;
+    const MrView *find_cached(QpView &v, uint32_t key, bool remote) const;
     static uint8_t *resolve(const MrView *m, uint64_t addr, uint64_t len);
     size_t progress_qp(QpView &v);
     bool produce(control::Cq *cq, const void *cqe);

@@ -373,3 +373,23 @@ def test_python_example_runs():
     r = subprocess.run([sys.executable, os.path.join(repo, "examples", "host_rdma.py")], capture_output=True,
                        text=True, timeout=120, env=env)
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
+
+
+def test_engine_bench_runs_every_case():
+    """ugdr_engine_bench (in-process host engine): the eight metadata cases and the four payload
+    cases run to completion, move the payload (the binary byte-checks it) and report rates."""
+    import subprocess
+
+    exe = str(N.LIB_DIR / "ugdr_engine_bench")
+    r = subprocess.run([exe, "metadata", "--wr-bytes", "64"], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("benchmark=engine_metadata")]
+    assert len(lines) == 8
+    for ln in lines:
+        f = dict(kv.split("=", 1) for kv in ln.split())
+        assert f["completed_wr"] == "262144" and float(f["MWR_per_s"]) > 0
+        assert int(f["wc"]) == (262144 if f["signaling"] == "every_wr" else 262144 // 32)
+    r = subprocess.run([exe, "payload", "--iters", "2000"], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("benchmark=engine_payload")]
+    assert len(lines) == 4 and all("parent_MWR_per_s=" in ln for ln in lines)

@@ -21,7 +21,7 @@ ALLOWED = {
     "collective": {"collective", "ugdr"},
     "daemon": {"common", "queue", "ipc", "control", "engine", "gpu", "daemon", "ugdr"},
     "apps": {"ugdr"},
-    "bench": {"ugdr", "queue", "common", "api"},  # ring / posting-core benchmarks drive those layers
+    "bench": {"ugdr", "queue", "common", "api", "control", "engine"},  # in-process benchmarks drive those layers
 }
 # Files of a layer that need no CUDA headers at all (wire formats and the control plane run in
 # processes and tests without a GPU stack).
