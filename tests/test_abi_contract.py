@@ -121,3 +121,40 @@ def test_binding_constants_match_the_header(probe):
              "ACCESS_REMOTE_ATOMIC": "UGDR_ACCESS_REMOTE_ATOMIC", "QPS_ERR": "UGDR_QPS_ERR"}
     for py, c in pairs.items():
         assert getattr(N, py) == probe[c], py
+
+
+# The reference's public function set (its client-contract list: tools/client-contracts.json).
+REFERENCE_SYMBOLS = [
+    "ugdr_get_device_list", "ugdr_free_device_list", "ugdr_open_device", "ugdr_close_device", "ugdr_alloc_pd",
+    "ugdr_dealloc_pd", "ugdr_reg_mr", "ugdr_dereg_mr", "ugdr_create_cq", "ugdr_destroy_cq", "ugdr_poll_cq",
+    "ugdr_create_qp", "ugdr_destroy_qp", "ugdr_modify_qp", "ugdr_query_qp", "ugdr_query_qp_conn_info",
+    "ugdr_connect_qp", "ugdr_post_send", "ugdr_post_recv",
+]
+
+
+def _declared_functions() -> set[str]:
+    import re
+
+    names = set()
+    for h in ("api.hpp", "collective.h"):
+        with open(os.path.join(REPO, "include", "ugdr", h)) as f:
+            text = re.sub(r"/\*.*?\*/|//[^\n]*", "", f.read(), flags=re.S)
+        names |= set(re.findall(r"\b(ugdr_[a-z0-9_]+)\s*\([^;{]*\)\s*(?:noexcept\s*)?(?:UGDR_NOEXCEPT\s*)?;", text))
+    return names
+
+
+def test_every_declared_function_is_exported_with_c_linkage():
+    """Each `ugdr_*` function declared in the public headers is a defined, unmangled dynamic
+    symbol of libugdr.so, and the reference's whole public set is among them."""
+    nm = shutil.which("nm")
+    if nm is None:
+        pytest.skip("nm not available")
+    from ugdr_b200 import _native as N
+
+    out = subprocess.run([nm, "-D", "--defined-only", str(N.LIB_PATH)], check=True, capture_output=True,
+                         text=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if ln.split()[-2:-1] == ["T"]}
+    declared = _declared_functions()
+    assert set(REFERENCE_SYMBOLS) <= declared
+    missing = sorted(declared - exported)
+    assert not missing, missing

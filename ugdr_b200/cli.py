@@ -4,6 +4,9 @@
     python -m ugdr_b200.cli build       make -j (libugdr.so, daemon, client, perf, native tests)
     python -m ugdr_b200.cli test [-m "not gpu"]   pytest over tests/
     python -m ugdr_b200.cli smoke       one WRITE + READ through a private daemon on cuda:0
+    python -m ugdr_b200.cli lint        layering, public ABI/exports, Python byte-compile
+                                        (parity: the reference's tools/check_module_boundaries.py and
+                                        tools/check_client_contracts.py)
 """
 from __future__ import annotations
 
@@ -56,6 +59,7 @@ def main(argv: list[str] | None = None) -> int:
     t = sub.add_parser("test")
     t.add_argument("-m", default="not gpu")
     sub.add_parser("smoke")
+    sub.add_parser("lint")
     args = ap.parse_args(argv)
     if args.cmd == "doctor":
         print(json.dumps(doctor(), indent=1))
@@ -71,6 +75,13 @@ def main(argv: list[str] | None = None) -> int:
         __graft_entry__.smoke()
         print("smoke ok")
         return 0
+    if args.cmd == "lint":
+        import compileall
+
+        ok = all(compileall.compile_dir(os.path.join(REPO, d), quiet=1) for d in ("ugdr_b200", "tests"))
+        rc = subprocess.run([sys.executable, "-m", "pytest", "-q", "-p", "no:cacheprovider",
+                             "tests/test_module_boundaries.py", "tests/test_abi_contract.py"], cwd=REPO).returncode
+        return 0 if ok and rc == 0 else 1
     return 2
 
 
