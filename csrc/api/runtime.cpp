@@ -560,6 +560,19 @@ int ugdr_x_query_engine_stats(ugdr_context *ctx, ugdr_x_engine_stats *stats, int
     return 0;
 }
 
+int ugdr_x_query_qp_stats(ugdr_qp *qp, ugdr_x_qp_stats *stats) noexcept {
+    if (!rt().live(qp) || stats == nullptr) return EINVAL;
+    Response resp;
+    if (int rc = rt().call(make(kQpStats, qp->identity), &resp); rc != 0) return rc;
+    ByteReader rd(resp.opaque);
+    if (!rd.be(&stats->send_posted) || !rd.be(&stats->send_retired) || !rd.be(&stats->recv_posted) ||
+        !rd.be(&stats->recv_consumed) || !rd.be(&stats->bytes) || !rd.be(&stats->error_completions) ||
+        !rd.be(&stats->rnr_waits) || !rd.be(&stats->state))
+        return EPROTO;
+    stats->reserved = 0;
+    return 0;
+}
+
 int ugdr_x_engine_hold(ugdr_context *ctx, int hold) noexcept {
     if (!rt().live(ctx)) return EINVAL;
     Request req = make(kEngineHold, ctx->identity);

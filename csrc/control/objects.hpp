@@ -141,6 +141,13 @@ struct EngineStats {
              job_slot_misses = 0, publish_waits = 0, publish_wait_ns = 0;
 };
 
+// Per-QP counters an engine keeps on top of the ring cursors (which the control plane reads
+// itself): payload bytes moved by the QP's successful send WRs, its error completions (flushes
+// included), and receiver-not-ready waits it entered.
+struct QpCounters {
+    uint64_t bytes = 0, error_completions = 0, rnr_waits = 0;
+};
+
 class Engine {
   public:
     virtual ~Engine() = default;
@@ -163,6 +170,11 @@ class Engine {
     virtual void resume() = 0;
 
     virtual int stats(EngineStats *out, bool reset) = 0;
+    virtual int qp_counters(Qp &qp, QpCounters *out) {
+        (void)qp;
+        (void)out;
+        return EOPNOTSUPP;
+    }
     virtual int hold(bool on) = 0;
     // Launch (held) executor for a timed drain; complete with finish_drain.
     virtual int start_drain(uint64_t expected_wrs) { (void)expected_wrs; return EOPNOTSUPP; }

@@ -41,6 +41,7 @@ enum Method : uint32_t {
     kEngineStats = 32,
     kEngineHold = 33,
     kTimedDrain = 34,
+    kQpStats = 35,
 };
 
 struct Request {

@@ -111,6 +111,7 @@ const char *method_range(uint32_t m) {
     case kEngineStats: return "ugdr.rpc.engine_stats";
     case kEngineHold: return "ugdr.rpc.engine_hold";
     case kTimedDrain: return "ugdr.rpc.timed_drain";
+    case kQpStats: return "ugdr.rpc.qp_stats";
     default: return names[0];
     }
 }
@@ -137,6 +138,7 @@ Response ControlPlane::dispatch(ipc::SessionId s, Request &&r) {
     case kEngineStats: return engine_stats(s, r);
     case kEngineHold: return engine_hold(s, r);
     case kTimedDrain: return timed_drain(s, r);
+    case kQpStats: return qp_stats(s, r);
     default: return status(EOPNOTSUPP);
     }
 }
@@ -538,6 +540,22 @@ Response ControlPlane::engine_stats(uint64_t s, const Request &r) {
     w.be(st.chunks_run).be(st.claim_misses).be(st.jobs_published).be(st.inline_runs).be(st.busy_ns);
     w.be(st.fast_batches).be(st.fast_fetch_ns).be(st.fast_exec_ns).be(st.fast_reserve_ns).be(st.fast_publish_ns);
     w.be(st.slow_wrs).be(st.slow_issue_ns).be(st.job_slot_misses).be(st.publish_waits).be(st.publish_wait_ns);
+    return out;
+}
+
+// Ring cursors give the WR counts for every engine: the SQ and RQ tails are what the client
+// posted, their heads what the engine retired or consumed.  The engine adds its own counters
+// (zero when it keeps none).
+Response ControlPlane::qp_stats(uint64_t s, const Request &r) {
+    Qp *qp = qps_.find(s, r.identity);
+    if (qp == nullptr) return status(EINVAL);
+    QpCounters c;
+    if (int rc = engines_[qp->device]->qp_counters(*qp, &c); rc != 0 && rc != EOPNOTSUPP) return status(rc);
+    if (qp->state != UGDR_QPS_ERR && qp->sq.error_word() == UGDR_QPS_ERR) qp->state = UGDR_QPS_ERR;
+    Response out;
+    ByteWriter w(&out.opaque);
+    w.be(qp->sq.tail()).be(qp->sq.head()).be(qp->rq.tail()).be(qp->rq.head());
+    w.be(c.bytes).be(c.error_completions).be(c.rnr_waits).be(uint32_t(qp->state));
     return out;
 }
 

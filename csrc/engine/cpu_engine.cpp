@@ -62,7 +62,9 @@ int CpuEngine::attach_cq(control::Cq &) { return 0; }
 void CpuEngine::detach_cq(control::Cq &) noexcept {}
 
 int CpuEngine::attach_qp(control::Qp &qp) {
-    qps_.push_back(QpView{&qp, 0, 0});
+    QpView v;
+    v.qp = &qp;
+    qps_.push_back(v);
     return 0;
 }
 
@@ -85,6 +87,16 @@ int CpuEngine::stats(control::EngineStats *out, bool reset) {
     *out = stats_;
     if (reset) stats_ = control::EngineStats{};
     return 0;
+}
+
+int CpuEngine::qp_counters(control::Qp &qp, control::QpCounters *out) {
+    for (const QpView &v : qps_) {
+        if (v.qp == &qp) {
+            *out = v.c;
+            return 0;
+        }
+    }
+    return ENOENT;
 }
 
 int CpuEngine::hold(bool on) {
@@ -142,9 +154,11 @@ size_t CpuEngine::progress_qp(QpView &v) {
             queue::SendWqe h;
             std::memcpy(&h, run.first, sizeof(h));
             queue::Cqe c{h.wr_id, UGDR_WC_WR_FLUSH_ERR, wc_opcode(h.opcode), 0, 0, qp.qpn, 0};
-            if (!produce(qp.send_cq, &c)) break;
-            qp.sq.release(1);
+            if (qp.send_cq->ring.reserve(1).count() == 0) break;
+            qp.sq.release(1);  // the slot is free before its completion is visible
+            produce(qp.send_cq, &c);
             stats_.error_completions += 1;
+            v.c.error_completions += 1;
             ++retired;
         }
         for (;;) {
@@ -153,9 +167,11 @@ size_t CpuEngine::progress_qp(QpView &v) {
             queue::RecvWqe h;
             std::memcpy(&h, run.first, sizeof(h));
             queue::Cqe c{h.wr_id, UGDR_WC_WR_FLUSH_ERR, UGDR_WC_RECV_RDMA_WITH_IMM, 0, 0, qp.qpn, 0};
-            if (!produce(qp.recv_cq, &c)) break;
+            if (qp.recv_cq->ring.reserve(1).count() == 0) break;
             qp.rq.release(1);
+            produce(qp.recv_cq, &c);
             stats_.error_completions += 1;
+            v.c.error_completions += 1;
         }
         return retired;
     }
@@ -226,6 +242,10 @@ size_t CpuEngine::progress_qp(QpView &v) {
         if (status == UGDR_WC_SUCCESS && op == UGDR_WR_RDMA_WRITE_WITH_IMM) {
             queue::SlotRun rq = peer->rq.peek(1);
             if (rq.count() == 0) {
+                if (!v.rnr_waiting) {
+                    v.rnr_waiting = true;
+                    v.c.rnr_waits += 1;
+                }
                 if (qp.rnr_retry == kInfiniteRnrRetry) break;  // wait for a receive
                 const uint64_t now = now_ns();
                 if (v.rnr_next_ns == 0 || now >= v.rnr_next_ns) {
@@ -288,7 +308,9 @@ size_t CpuEngine::progress_qp(QpView &v) {
             }
             v.rnr_attempts = 0;
             v.rnr_next_ns = 0;
+            v.rnr_waiting = false;
             stats_.bytes_moved += op_atomic(op) ? 8 : total;
+            v.c.bytes += op_atomic(op) ? 8 : total;
         }
         // The SQ slot is returned before the completion is visible: a client that sees the CQE
         // may post into that slot at once (an HCA retires the WQE before it reports it).
@@ -303,6 +325,7 @@ size_t CpuEngine::progress_qp(QpView &v) {
         stats_.wrs_completed += 1;
         if (status != UGDR_WC_SUCCESS) {
             stats_.error_completions += 1;
+            v.c.error_completions += 1;
             v.rnr_attempts = 0;
             v.rnr_next_ns = 0;
             enter_error(qp);

@@ -36,6 +36,7 @@ class CpuEngine : public control::Engine {
     void quiesce() override {}
     void resume() override {}
     int stats(control::EngineStats *out, bool reset) override;
+    int qp_counters(control::Qp &qp, control::QpCounters *out) override;
     int hold(bool on) override;
 
     // One pass over every QP; caller holds the object lock.  Returns WRs retired.  Public so
@@ -57,6 +58,8 @@ class CpuEngine : public control::Engine {
         // cleared whenever an MR is detached.
         const MrView *lm = nullptr, *rm = nullptr;
         uint32_t lkey = 0, rkey = 0;
+        control::QpCounters c;
+        bool rnr_waiting = false;  // an RNR wait episode is open (counted once)
     };
     const MrView *find(uint32_t key, bool remote) const;
     const MrView *find_cached(QpView &v, uint32_t key, bool remote) const;

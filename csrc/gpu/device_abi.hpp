@@ -110,7 +110,8 @@ struct DevQpState {
     unsigned long long rnr_next_ns;
     uint32_t rnr_attempts;
     uint32_t err;  // executor-detected error: the QP is in ERR
-    unsigned long long pad[2];
+    unsigned long long bytes;   // payload bytes of retired successful send WRs (owner warp writes)
+    unsigned long long errors;  // error and flush completions of this QP (owner warp writes)
     WrRec win[kWindow];
 };
 

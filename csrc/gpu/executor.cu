@@ -896,13 +896,22 @@ __device__ int retire_commit(Warp &w, DevQp *qp, const QpView &v, queue::Cqe *cq
             atomicMax(&w.p->stats->last_end_ns, (unsigned long long)gtime());
             if (err_mask && retire_n == p) {
                 atomicAdd(&w.p->stats->error_completions, 1ull);
+                qp->st.errors += 1;
                 qp->st.err = 1;
                 st_rel_sys(&v.sq->meta.reserved[queue::kQpErrorWordIndex], UGDR_QPS_ERR);
             }
             verdict = int(retire_n);
         }
     }
-    return bcast(verdict);
+    verdict = bcast(verdict);
+    if (verdict > 0) {
+        // Per-QP byte count: the successful WRs among the retired prefix, summed over the warp.
+        unsigned long long b =
+            uint32_t(w.lane) < uint32_t(verdict) && status == UGDR_WC_SUCCESS ? (unsigned long long)total : 0ull;
+        for (int o = 16; o > 0; o >>= 1) b += __shfl_xor_sync(0xffffffffu, b, o);
+        if (w.lane == 0) qp->st.bytes += b;
+    }
+    return verdict;
 }
 
 __device__ int retire(Warp &w, DevQp *qp, const QpView &v, queue::Cqe *cqe_buf) {
@@ -1255,6 +1264,7 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
                 qp->st.sq_head = qp->st.sq_issue;
                 st_rel_sys(&v.sq->head.value, qp->st.sq_head);
                 atomicAdd(&w.p->stats->error_completions, 1ull);
+                qp->st.errors += 1;
                 atomicAdd(&w.p->stats->retired, 1ull);
                 ++flushed;
             }
@@ -1270,6 +1280,7 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
                     break;
                 }
                 atomicAdd(&w.p->stats->error_completions, 1ull);
+                qp->st.errors += 1;
                 ++flushed;
             }
         }

@@ -63,6 +63,7 @@ class GpuEngine final : public control::Engine {
     void quiesce() override;
     void resume() override;
     int stats(control::EngineStats *out, bool reset) override;
+    int qp_counters(control::Qp &qp, control::QpCounters *out) override;
     int hold(bool on) override;
     int start_drain(uint64_t expected) override;
     int finish_drain(uint32_t timeout_ms, float *elapsed_ms) override;
@@ -493,6 +494,21 @@ void GpuEngine::quiesce() {
 void GpuEngine::resume() {
     std::lock_guard<std::mutex> lk(mu_);
     if (paused_ > 0) paused_ -= 1;
+}
+
+// The owner warp keeps each QP's byte and error counts in its device state; RNR waits are not
+// counted per QP on the device (the engine-wide wait counters cover them).
+int GpuEngine::qp_counters(control::Qp &qp, control::QpCounters *out) {
+    std::lock_guard<std::mutex> lk(mu_);
+    const auto *d = static_cast<const DevQp *>(qp.engine_block);
+    if (d == nullptr) return ENOENT;
+    unsigned long long v[2] = {0, 0};
+    static_assert(offsetof(DevQpState, errors) == offsetof(DevQpState, bytes) + sizeof(unsigned long long));
+    if (int rc = copy_from_device(v, &d->st.bytes, sizeof(v)); rc != 0) return rc;
+    out->bytes = v[0];
+    out->error_completions = v[1];
+    out->rnr_waits = 0;
+    return 0;
 }
 
 int GpuEngine::stats(control::EngineStats *out, bool reset) {

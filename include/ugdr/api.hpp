@@ -277,6 +277,20 @@ int ugdr_x_query_engine_stats(ugdr_context *context, ugdr_x_engine_stats *stats,
  * across drains until released. */
 int ugdr_x_engine_hold(ugdr_context *context, int hold) UGDR_NOEXCEPT;
 
+/* Per-QP counters.  The WR counts are the QP's ring cursors since creation: send WRs posted and
+ * retired (completed, flushed or silently retired when unsignaled), receive WRs posted and
+ * consumed.  `bytes` sums the payload of retired successful send WRs; `error_completions`
+ * counts this QP's error and flush completions; `rnr_waits` counts the times a WRITE_WITH_IMM
+ * found no receive posted (host engine; 0 on a GPU).  `state` is the current ugdr_qp_state. */
+typedef struct ugdr_x_qp_stats {
+    uint64_t send_posted, send_retired, recv_posted, recv_consumed;
+    uint64_t bytes, error_completions, rnr_waits;
+    uint32_t state;
+    uint32_t reserved;
+} ugdr_x_qp_stats;
+
+int ugdr_x_query_qp_stats(ugdr_qp *qp, ugdr_x_qp_stats *stats) UGDR_NOEXCEPT;
+
 /* Timed drain (benchmarks): the daemon launches the device executors of `num_contexts`
  * contexts together, each bracketed by CUDA events on its launching stream, and returns once
  * every executor has retired `expected_wrs[i]` send WRs or `timeout_ms` passed.  `elapsed_ms[i]`

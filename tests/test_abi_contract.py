@@ -78,6 +78,8 @@ def _probe() -> dict:
             lines.append(f'    printf("offsetof.{st}.{fd} %zu\\n", offsetof(struct {st}, {fd}));')
     lines.append('    printf("sizeof.ugdr_x_peerset %zu\\n", sizeof(ugdr_x_peerset));')
     lines.append('    printf("sizeof.ugdr_x_nvls %zu\\n", sizeof(ugdr_x_nvls));')
+    lines.append('    printf("sizeof.ugdr_x_qp_stats %zu\\n", sizeof(ugdr_x_qp_stats));')
+    lines.append('    printf("sizeof.ugdr_x_engine_stats %zu\\n", sizeof(ugdr_x_engine_stats));')
     lines += ["    return 0;", "}"]
     out = {}
     for line in _compile_and_run("\n".join(lines) + "\n").splitlines():
@@ -109,6 +111,8 @@ def test_python_binding_layouts_match_the_header(probe):
             assert getattr(cls, fd).offset == probe[f"offsetof.{st}.{fd}"], f"{st}.{fd}"
     assert C.sizeof(PeerSet) == probe["sizeof.ugdr_x_peerset"]
     assert C.sizeof(Nvls) == probe["sizeof.ugdr_x_nvls"]
+    assert C.sizeof(N.QpStats) == probe["sizeof.ugdr_x_qp_stats"]
+    assert C.sizeof(N.EngineStats) == probe["sizeof.ugdr_x_engine_stats"]
 
 
 def test_binding_constants_match_the_header(probe):

@@ -85,6 +85,50 @@ def test_a_polled_completion_frees_its_send_slot(cpu_daemon):
         buf.free()
 
 
+def test_qp_stats_count_wrs_bytes_rnr_and_errors(cpu_daemon):
+    """ugdr_x_query_qp_stats: ring cursors, payload bytes, one RNR wait episode, and the error plus
+    flush completions of a QP that went to ERR."""
+    ctx, pd, cq, a, b = _pair(depth=32, cq_depth=128)  # rnr_retry 7: wait for a receive forever
+    buf = V.HostBuffer(1 << 16)
+    mr = pd.reg_mr(buf.addr, 1 << 16, ACC)
+    try:
+        for i in range(10):
+            a.post_write((buf.addr, 100, mr.lkey), buf.addr + 4096, mr.rkey, wr_id=i)
+        assert len(cq.wait(10, timeout=10)) == 10
+        st = a.stats()
+        assert (st.send_posted, st.send_retired, st.bytes, st.error_completions) == (10, 10, 1000, 0)
+        assert st.state == N.QPS_RTS
+        a.post_send(N.WR_RDMA_WRITE_WITH_IMM, [(buf.addr, 64, mr.lkey)], remote_addr=buf.addr + 8192, rkey=mr.rkey,
+                    wr_id=50, imm=7)
+        deadline = time.time() + 10
+        while a.stats().rnr_waits == 0 and time.time() < deadline:
+            time.sleep(0.001)
+        assert a.stats().rnr_waits == 1 and a.stats().send_retired == 10
+        b.post_recv(900)
+        got = cq.wait(2, timeout=10)
+        assert sorted(w.wr_id for w in got) == [50, 900]
+        sa, sb = a.stats(), b.stats()
+        assert (sa.send_retired, sa.bytes, sa.rnr_waits) == (11, 1064, 1)
+        assert (sb.recv_posted, sb.recv_consumed, sb.send_posted) == (1, 1, 0)
+        # A bad lkey moves the QP to ERR; the two WRs behind it are flushed.
+        a.post_write((buf.addr, 8, mr.lkey ^ 2), buf.addr, mr.rkey, wr_id=60)
+        a.post_write((buf.addr, 8, mr.lkey), buf.addr, mr.rkey, wr_id=61)
+        a.post_write((buf.addr, 8, mr.lkey), buf.addr, mr.rkey, wr_id=62)
+        got = cq.wait(3, timeout=10)
+        assert [w.status for w in got] == [N.WC_LOC_PROT_ERR, N.WC_WR_FLUSH_ERR, N.WC_WR_FLUSH_ERR]
+        sa = a.stats()
+        assert (sa.send_posted, sa.send_retired, sa.error_completions, sa.bytes) == (14, 14, 3, 1064)
+        assert sa.state == N.QPS_ERR
+    finally:
+        a.destroy()
+        b.destroy()
+        mr.dereg()
+        cq.destroy()
+        pd.dealloc()
+        ctx.close()
+        buf.free()
+
+
 def test_write_with_imm_consumes_rq_in_order(cpu_daemon):
     ctx, pd, cq, a, b = _pair()
     buf = V.HostBuffer(1 << 16)

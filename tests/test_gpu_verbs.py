@@ -289,3 +289,29 @@ def test_copy_core_alignment_matrix():
                 torch.cuda.synchronize()
                 assert torch.equal(dst[base:base + n], src[so:so + n]), (n, so, do)
                 assert bool((dst[:base] == 0xD3).all()) and bool((dst[base + n:] == 0xD3).all()), (n, so, do)
+
+
+def test_qp_stats_on_the_executor(gpu_env):
+    """Per-QP counters kept by the executor: bytes of retired successful WRs (inline, lane-parallel
+    and chunked sizes) and the error plus flush completions of a QP that went to ERR."""
+    V = gpu_env
+    from ugdr_b200 import _native as N
+
+    ctx, pd, cq, a, b = _setup(V, N)
+    n = 2 << 20
+    src = torch.ones(n, dtype=torch.uint8, device="cuda")
+    dst = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    ms, md = pd.reg_mr(src.data_ptr(), n, _acc(N)), pd.reg_mr(dst.data_ptr(), n, _acc(N))
+    sizes = [8, 100, 4097, 65536, 1 << 20]
+    for i, sz in enumerate(sizes):
+        a.post_write((src.data_ptr(), sz, ms.lkey), dst.data_ptr(), md.rkey, wr_id=i)
+    assert all(w.status == N.WC_SUCCESS for w in cq.wait(len(sizes), 60))
+    st = a.stats()
+    assert (st.send_posted, st.send_retired, st.bytes, st.error_completions) == (5, 5, sum(sizes), 0)
+    a.post_write((src.data_ptr(), 64, ms.lkey), dst.data_ptr(), md.rkey ^ 2, wr_id=10)
+    a.post_write((src.data_ptr(), 64, ms.lkey), dst.data_ptr(), md.rkey, wr_id=11)
+    wcs = cq.wait(2, 60)
+    assert [w.status for w in wcs] == [N.WC_REM_ACCESS_ERR, N.WC_WR_FLUSH_ERR]
+    st = a.stats()
+    assert (st.send_retired, st.bytes, st.error_completions, st.state) == (7, sum(sizes), 2, N.QPS_ERR)

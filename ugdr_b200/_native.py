@@ -178,6 +178,20 @@ class DeviceInfo(C.Structure):
     ]
 
 
+class QpStats(C.Structure):
+    _fields_ = [
+        ("send_posted", C.c_uint64),
+        ("send_retired", C.c_uint64),
+        ("recv_posted", C.c_uint64),
+        ("recv_consumed", C.c_uint64),
+        ("bytes", C.c_uint64),
+        ("error_completions", C.c_uint64),
+        ("rnr_waits", C.c_uint64),
+        ("state", C.c_uint32),
+        ("reserved", C.c_uint32),
+    ]
+
+
 class EngineStats(C.Structure):
     _fields_ = [
         ("wrs_completed", C.c_uint64),
@@ -244,6 +258,7 @@ def lib() -> C.CDLL:
         "ugdr_x_alloc_host": (vp, [sz]),
         "ugdr_x_free_host": (i, [vp]),
         "ugdr_x_query_engine_stats": (i, [vp, C.POINTER(EngineStats), i]),
+        "ugdr_x_query_qp_stats": (i, [vp, C.POINTER(QpStats)]),
         "ugdr_x_engine_hold": (i, [vp, i]),
         "ugdr_x_timed_drain": (i, [C.POINTER(vp), i, C.POINTER(u64), u32, C.POINTER(C.c_float)]),
     }

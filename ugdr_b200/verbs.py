@@ -291,6 +291,13 @@ class QueuePair:
         _check(N.lib().ugdr_query_qp(self.h, C.byref(a), mask, C.byref(ia)), "ugdr_query_qp")
         return a, ia
 
+    def stats(self) -> N.QpStats:
+        """Per-QP counters: ring cursors (posted / retired / consumed) and the engine's byte,
+        error and RNR counts."""
+        st = N.QpStats()
+        _check(N.lib().ugdr_x_query_qp_stats(self.h, C.byref(st)), "ugdr_x_query_qp_stats")
+        return st
+
     # -- posting --
     def post_send_raw(self, wrs: list[N.SendWr]) -> tuple[int, int]:
         """Post a chain; returns (rc, index of bad_wr or -1)."""
