@@ -26,9 +26,41 @@ int default_ctas() {
 
 using GetRangeFn = CUresult (*)(CUdeviceptr *, size_t *, CUdeviceptr);
 
+// Fills `out` for one kernel: resources from cudaFuncGetAttributes, residency from the
+// occupancy calculator at the kernel's launch block size.
+template <typename Ref> int fill_kernel_attr(const Ref &k, ugdr_x_kernel_attr *out) {
+    cudaFuncAttributes a{};
+    if (cudaError_t e = cudaFuncGetAttributes(&a, k.fn); e != cudaSuccess) {
+        (void)cudaGetLastError();
+        return int(e);
+    }
+    int blocks = 0;
+    if (cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, k.fn, k.threads, 0); e != cudaSuccess) {
+        (void)cudaGetLastError();
+        return int(e);
+    }
+    std::memset(out, 0, sizeof(*out));
+    std::strncpy(out->name, k.name, sizeof(out->name) - 1);
+    out->threads_per_block = k.threads;
+    out->registers_per_thread = a.numRegs;
+    out->local_bytes_per_thread = int(a.localSizeBytes);
+    out->static_smem_bytes = int(a.sharedSizeBytes);
+    out->max_threads_per_block = a.maxThreadsPerBlock;
+    out->blocks_per_sm = blocks;
+    return 0;
+}
+
 }  // namespace
 
 extern "C" {
+
+int ugdr_x_collective_kernel_attributes(int index, ugdr_x_kernel_attr *out) {
+    const ugdr::coll::KernelRef *refs = nullptr;
+    const int n = ugdr::coll::collective_kernels(&refs);
+    if (out == nullptr || index < 0) return int(cudaErrorInvalidValue);
+    if (index >= n) return -1;
+    return fill_kernel_attr(refs[index], out);
+}
 
 uint64_t ugdr_x_set_collective_wait_ns(uint64_t ns) {
     return g_wait_ns.exchange(ns == 0 ? 5ull * 1000 * 1000 * 1000 : ns);

@@ -517,6 +517,23 @@ int launch_allreduce_bf16_nvls(const PeerSet &ps, void *mc, uint64_t offset, uin
     return int(cudaGetLastError());
 }
 
+int collective_kernels(const KernelRef **out) {
+    static const KernelRef refs[] = {
+        {"allreduce_kernel<8>", reinterpret_cast<const void *>(&allreduce_kernel<8>), 512},
+        {"allreduce_kernel<2>", reinterpret_cast<const void *>(&allreduce_kernel<2>), 512},
+        {"allreduce_nvls_kernel<4>", reinterpret_cast<const void *>(&allreduce_nvls_kernel<4>), 512},
+        {"route_hist_kernel", reinterpret_cast<const void *>(&route_hist_kernel), 256},
+        {"route_scan_kernel", reinterpret_cast<const void *>(&route_scan_kernel), 128},
+        {"route_place_kernel", reinterpret_cast<const void *>(&route_place_kernel), 256},
+        {"counts_exchange_kernel", reinterpret_cast<const void *>(&counts_exchange_kernel), 256},
+        {"layout_kernel", reinterpret_cast<const void *>(&layout_kernel), 32},
+        {"dispatch_kernel", reinterpret_cast<const void *>(&dispatch_kernel), 512},
+        {"combine_kernel<8>", reinterpret_cast<const void *>(&combine_kernel<8>), 512},
+    };
+    *out = refs;
+    return int(sizeof(refs) / sizeof(refs[0]));
+}
+
 size_t route_scratch_bytes(uint64_t rows, int nexp) {
     const uint64_t nblocks = (rows + kRouteRowsPerBlock - 1) / kRouteRowsPerBlock;
     return size_t(nblocks) * size_t(nexp) * sizeof(uint32_t);

@@ -26,6 +26,14 @@ struct PeerSet {
 };
 
 int grid_for(int device);
+
+// The collective kernels with the block size they are launched with (resource reports).
+struct KernelRef {
+    const char *name;
+    const void *fn;
+    int threads;
+};
+int collective_kernels(const KernelRef **out);
 int launch_allreduce_bf16(const PeerSet &ps, uint64_t offset, uint64_t count, uint64_t epoch, int ctas,
                           uint64_t max_ns, cudaStream_t s);
 int launch_allreduce_bf16_nvls(const PeerSet &ps, void *mc, uint64_t offset, uint64_t count, uint64_t epoch,

@@ -1624,6 +1624,16 @@ int launch_executor(const ExecParams &p, int ctas, cudaStream_t stream) {
     return int(cudaGetLastError());
 }
 
+int executor_kernels(const KernelRef **out) {
+    static const KernelRef refs[] = {
+        {"executor_kernel", reinterpret_cast<const void *>(&executor_kernel), kThreads},
+        {"grid_copy_kernel", reinterpret_cast<const void *>(&grid_copy_kernel), kThreads},
+        {"copy_test_kernel", reinterpret_cast<const void *>(&copy_test_kernel), 32},
+    };
+    *out = refs;
+    return int(sizeof(refs) / sizeof(refs[0]));
+}
+
 int launch_copy_test(void *dst, const void *src, uint64_t n, cudaStream_t stream) {
     copy_test_kernel<<<1, 32, 0, stream>>>(static_cast<uint8_t *>(dst),
                                            static_cast<const uint8_t *>(src), n);

@@ -18,4 +18,12 @@ int launch_copy_test(void *dst, const void *src, uint64_t n, cudaStream_t stream
 // Whole-grid copy with the executor's copy core (bandwidth ceiling / profiling).
 int launch_grid_copy(void *dst, const void *src, uint64_t n, int ctas, cudaStream_t stream);
 
+// The translation unit's kernels with the block size they are launched with (resource reports).
+struct KernelRef {
+    const char *name;
+    const void *fn;
+    int threads;
+};
+int executor_kernels(const KernelRef **out);
+
 }  // namespace ugdr::gpu

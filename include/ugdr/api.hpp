@@ -303,6 +303,26 @@ int ugdr_x_timed_drain(ugdr_context **contexts, int num_contexts, const uint64_t
  * tests; ugdr_x_grid_copy_bench times `iters` whole-grid copies with CUDA events on `stream` and
  * writes the mean milliseconds per copy.  Both return a cudaError_t value. */
 int ugdr_x_copy_core_test(void *dst, const void *src, uint64_t n, void *stream) UGDR_NOEXCEPT;
+#ifndef UGDR_X_KERNEL_ATTR_DEFINED
+#define UGDR_X_KERNEL_ATTR_DEFINED
+/* Compiled resources of one kernel on the current CUDA device, with the block size it is
+ * launched with and the resident blocks per SM that gives (cudaFuncGetAttributes and the
+ * occupancy calculator; static shared memory only). */
+typedef struct ugdr_x_kernel_attr {
+    char name[48];
+    int threads_per_block;
+    int registers_per_thread;
+    int local_bytes_per_thread; /* spill and stack */
+    int static_smem_bytes;
+    int max_threads_per_block;
+    int blocks_per_sm;
+} ugdr_x_kernel_attr;
+#endif
+
+/* Kernel `index` of the executor translation unit (executor, whole-grid copy, copy-core test).
+ * Returns 0, -1 past the last kernel, or a cudaError_t value. */
+int ugdr_x_kernel_attributes(int index, ugdr_x_kernel_attr *out) UGDR_NOEXCEPT;
+
 int ugdr_x_grid_copy_bench(void *dst, const void *src, uint64_t n, int ctas, int iters, void *stream,
                            float *ms_per_copy) UGDR_NOEXCEPT;
 

@@ -34,6 +34,26 @@ typedef struct ugdr_x_peerset {
  * restores the default (5 s).  Returns the previous bound. */
 uint64_t ugdr_x_set_collective_wait_ns(uint64_t ns);
 
+#ifndef UGDR_X_KERNEL_ATTR_DEFINED
+#define UGDR_X_KERNEL_ATTR_DEFINED
+/* Compiled resources of one kernel on the current CUDA device, with the block size it is
+ * launched with and the resident blocks per SM that gives (cudaFuncGetAttributes and the
+ * occupancy calculator; static shared memory only). */
+typedef struct ugdr_x_kernel_attr {
+    char name[48];
+    int threads_per_block;
+    int registers_per_thread;
+    int local_bytes_per_thread; /* spill and stack */
+    int static_smem_bytes;
+    int max_threads_per_block;
+    int blocks_per_sm;
+} ugdr_x_kernel_attr;
+#endif
+
+/* Kernel `index` of the collective kernels.  Returns 0, -1 past the last kernel, or a
+ * cudaError_t value. */
+int ugdr_x_collective_kernel_attributes(int index, ugdr_x_kernel_attr *out);
+
 /* Export the allocation holding `ptr` (cudaMalloc memory) for another process: the handle of
  * the allocation base and the offset of `ptr` inside it. */
 int ugdr_x_ipc_export(void *ptr, uint8_t handle[UGDR_X_IPC_HANDLE_BYTES], uint64_t *offset);

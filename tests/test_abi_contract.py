@@ -80,6 +80,7 @@ def _probe() -> dict:
     lines.append('    printf("sizeof.ugdr_x_nvls %zu\\n", sizeof(ugdr_x_nvls));')
     lines.append('    printf("sizeof.ugdr_x_qp_stats %zu\\n", sizeof(ugdr_x_qp_stats));')
     lines.append('    printf("sizeof.ugdr_x_engine_stats %zu\\n", sizeof(ugdr_x_engine_stats));')
+    lines.append('    printf("sizeof.ugdr_x_kernel_attr %zu\\n", sizeof(ugdr_x_kernel_attr));')
     lines += ["    return 0;", "}"]
     out = {}
     for line in _compile_and_run("\n".join(lines) + "\n").splitlines():
@@ -113,6 +114,9 @@ def test_python_binding_layouts_match_the_header(probe):
     assert C.sizeof(Nvls) == probe["sizeof.ugdr_x_nvls"]
     assert C.sizeof(N.QpStats) == probe["sizeof.ugdr_x_qp_stats"]
     assert C.sizeof(N.EngineStats) == probe["sizeof.ugdr_x_engine_stats"]
+    from ugdr_b200.ops import KernelAttr
+
+    assert C.sizeof(KernelAttr) == probe["sizeof.ugdr_x_kernel_attr"]
 
 
 def test_binding_constants_match_the_header(probe):

@@ -315,3 +315,20 @@ def test_qp_stats_on_the_executor(gpu_env):
     assert [w.status for w in wcs] == [N.WC_REM_ACCESS_ERR, N.WC_WR_FLUSH_ERR]
     st = a.stats()
     assert (st.send_retired, st.bytes, st.error_completions, st.state) == (7, sum(sizes), 2, N.QPS_ERR)
+
+
+def test_kernel_attributes_report_every_kernel():
+    """cudaFuncGetAttributes + occupancy for every kernel of the library: each fits its launch
+    block size; the persistent executor keeps one 512-thread CTA per SM without spilling more than
+    the ptxas report allows."""
+    if gpu_count() < 1:
+        pytest.skip("no GPU")
+    from ugdr_b200 import ops
+
+    torch.cuda.set_device(0)
+    attrs = {a["name"]: a for a in ops.kernel_attributes()}
+    assert {"executor_kernel", "allreduce_nvls_kernel<4>", "dispatch_kernel", "combine_kernel<8>"} <= set(attrs)
+    for a in attrs.values():
+        assert a["blocks_per_sm"] >= 1 and a["threads_per_block"] <= a["max_threads_per_block"], a
+    ex = attrs["executor_kernel"]
+    assert ex["threads_per_block"] == 512 and ex["registers_per_thread"] <= 128 and ex["blocks_per_sm"] == 1

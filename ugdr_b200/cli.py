@@ -46,6 +46,9 @@ def doctor() -> dict:
             from .parallel import nvls
 
             rep["nvls_multicast"] = [nvls.supported(i) for i in range(n)]
+            from . import ops
+
+            rep["kernels"] = ops.kernel_attributes()
     except Exception as e:  # a report, not a failure
         rep["torch_error"] = repr(e)
     return rep

@@ -4,6 +4,8 @@
 * grid_copy_ms(dst, src)   mean ms of a whole-grid copy with the executor's copy core
 * moe_route(ids, nexp)     deterministic counting sort of (token, k) rows by expert
 * register(pd, tensor)     a verbs MR over a tensor's bytes (local write + remote read / write)
+* kernel_attributes()      registers, spills, static shared memory and blocks per SM of every
+                           kernel of the library on the current device
 
 The collectives themselves live in ugdr_b200.parallel (they need a peer group).
 """
@@ -17,6 +19,12 @@ from .. import _native as N
 from ..parallel.collectives import moe_route  # noqa: F401  (re-exported)
 
 
+class KernelAttr(C.Structure):
+    _fields_ = [("name", C.c_char * 48), ("threads_per_block", C.c_int), ("registers_per_thread", C.c_int),
+                ("local_bytes_per_thread", C.c_int), ("static_smem_bytes", C.c_int),
+                ("max_threads_per_block", C.c_int), ("blocks_per_sm", C.c_int)]
+
+
 def _lib():
     L = N.lib()
     if not getattr(L, "_ops_sigs", False):
@@ -25,6 +33,9 @@ def _lib():
         L.ugdr_x_grid_copy_bench.restype = C.c_int
         L.ugdr_x_grid_copy_bench.argtypes = [C.c_void_p, C.c_void_p, C.c_uint64, C.c_int, C.c_int, C.c_void_p,
                                              C.POINTER(C.c_float)]
+        for fn in ("ugdr_x_kernel_attributes", "ugdr_x_collective_kernel_attributes"):
+            getattr(L, fn).restype = C.c_int
+            getattr(L, fn).argtypes = [C.c_int, C.POINTER(KernelAttr)]
         L._ops_sigs = True
     return L
 
@@ -65,3 +76,22 @@ def register(pd, tensor: torch.Tensor, access: int | None = None):
         raise ValueError("register() needs a contiguous tensor")
     acc = access if access is not None else (N.ACCESS_LOCAL_WRITE | N.ACCESS_REMOTE_WRITE | N.ACCESS_REMOTE_READ)
     return pd.reg_mr(tensor.data_ptr(), tensor.numel() * tensor.element_size(), acc)
+
+
+def kernel_attributes() -> list[dict]:
+    """One dict per kernel of libugdr.so (executor translation unit first, then the collective
+    kernels): compiled resources and resident blocks per SM at the launch block size."""
+    L = _lib()
+    out = []
+    for fn in (L.ugdr_x_kernel_attributes, L.ugdr_x_collective_kernel_attributes):
+        i = 0
+        while True:
+            a = KernelAttr()
+            rc = fn(i, C.byref(a))
+            if rc == -1:
+                break
+            if rc != 0:
+                raise RuntimeError(f"kernel attributes failed: cudaError {rc}")
+            out.append({f: (getattr(a, f).decode() if f == "name" else getattr(a, f)) for f, _ in KernelAttr._fields_})
+            i += 1
+    return out
