@@ -110,10 +110,11 @@ def test_qp_stats_count_wrs_bytes_rnr_and_errors(cpu_daemon):
         sa, sb = a.stats(), b.stats()
         assert (sa.send_retired, sa.bytes, sa.rnr_waits) == (11, 1064, 1)
         assert (sb.recv_posted, sb.recv_consumed, sb.send_posted) == (1, 1, 0)
-        # A bad lkey moves the QP to ERR; the two WRs behind it are flushed.
-        a.post_write((buf.addr, 8, mr.lkey ^ 2), buf.addr, mr.rkey, wr_id=60)
-        a.post_write((buf.addr, 8, mr.lkey), buf.addr, mr.rkey, wr_id=61)
-        a.post_write((buf.addr, 8, mr.lkey), buf.addr, mr.rkey, wr_id=62)
+        # A bad lkey moves the QP to ERR; the two WRs behind it (same chain: posting on an ERR QP
+        # is refused) are flushed.
+        raw = [V.QueuePair.make_send_wr(N.WR_RDMA_WRITE, [(buf.addr, 8, mr.lkey ^ (2 if i == 0 else 0))],
+                                        remote_addr=buf.addr, rkey=mr.rkey, wr_id=60 + i) for i in range(3)]
+        assert a.post_send_raw(raw) == (0, -1)
         got = cq.wait(3, timeout=10)
         assert [w.status for w in got] == [N.WC_LOC_PROT_ERR, N.WC_WR_FLUSH_ERR, N.WC_WR_FLUSH_ERR]
         sa = a.stats()

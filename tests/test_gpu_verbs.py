@@ -143,8 +143,9 @@ def test_remote_access_error_and_flush(gpu_env):
     ms = pd.reg_mr(src.data_ptr(), 4096, _acc(N))
     md = pd.reg_mr(dst.data_ptr(), 4096, N.ACCESS_LOCAL_WRITE)  # no remote write
     b.post_recv(wr_id=77)
-    a.post_write((src.data_ptr(), 64, ms.lkey), dst.data_ptr(), md.rkey, wr_id=1)
-    a.post_write((src.data_ptr(), 64, ms.lkey), dst.data_ptr(), md.rkey, wr_id=2, signaled=False)
+    raw = [V.QueuePair.make_send_wr(N.WR_RDMA_WRITE, [(src.data_ptr(), 64, ms.lkey)], remote_addr=dst.data_ptr(),
+                                    rkey=md.rkey, wr_id=1 + i, signaled=i == 0) for i in range(2)]
+    assert a.post_send_raw(raw) == (0, -1)  # one chain: posting on a QP already in ERR is refused
     wcs = cq.wait(2, 60)
     assert wcs[0].wr_id == 1 and wcs[0].status == N.WC_REM_ACCESS_ERR
     assert wcs[1].wr_id == 2 and wcs[1].status == N.WC_WR_FLUSH_ERR
@@ -309,8 +310,9 @@ def test_qp_stats_on_the_executor(gpu_env):
     assert all(w.status == N.WC_SUCCESS for w in cq.wait(len(sizes), 60))
     st = a.stats()
     assert (st.send_posted, st.send_retired, st.bytes, st.error_completions) == (5, 5, sum(sizes), 0)
-    a.post_write((src.data_ptr(), 64, ms.lkey), dst.data_ptr(), md.rkey ^ 2, wr_id=10)
-    a.post_write((src.data_ptr(), 64, ms.lkey), dst.data_ptr(), md.rkey, wr_id=11)
+    raw = [V.QueuePair.make_send_wr(N.WR_RDMA_WRITE, [(src.data_ptr(), 64, ms.lkey)], remote_addr=dst.data_ptr(),
+                                    rkey=md.rkey ^ (2 if i == 0 else 0), wr_id=10 + i) for i in range(2)]
+    assert a.post_send_raw(raw) == (0, -1)  # one chain: posting on a QP already in ERR is refused
     wcs = cq.wait(2, 60)
     assert [w.status for w in wcs] == [N.WC_REM_ACCESS_ERR, N.WC_WR_FLUSH_ERR]
     st = a.stats()
