@@ -414,15 +414,24 @@ Response ControlPlane::create_qp(uint64_t s, const Request &r) {
 void ControlPlane::erase_qp(uint64_t id) noexcept {
     Qp *qp = qps_.find_any(id);
     if (qp == nullptr) return;
-    engines_[qp->device]->detach_qp(*qp);
-    // Requesters bound to this QP lose their peer: later WRs fail with RETRY_EXC.
+    // Requesters bound to this QP lose their peer (later WRs fail with RETRY_EXC).  Their
+    // engines may be on other GPUs and may be executing a WRITE_WITH_IMM into this QP's receive
+    // ring at this moment, so each is stopped before the binding changes and stays stopped until
+    // this QP's rings are gone from its own engine.
+    std::vector<Engine *> held;
     qps_.for_each([&](uint64_t, uint64_t, Qp &other) {
-        if (other.peer == qp) {
-            other.peer = nullptr;
-            other.peer_lost = true;
-            engines_[other.device]->update_qp(other);
+        if (other.peer != qp) return;
+        Engine *e = engines_[other.device];
+        if (std::find(held.begin(), held.end(), e) == held.end()) {
+            e->quiesce();
+            held.push_back(e);
         }
+        other.peer = nullptr;
+        other.peer_lost = true;
+        e->update_qp(other);
     });
+    engines_[qp->device]->detach_qp(*qp);
+    for (Engine *e : held) e->resume();
     qpn_index_.erase(qp->qpn);
     if (Pd *pd = pds_.find_any(qp->pd_id)) pd->qps -= 1;
     if (qp->send_cq) qp->send_cq->qp_refs -= 1;

@@ -105,6 +105,10 @@ class GpuEngine final : public control::Engine {
     bool running_ = false;
     bool held_ = false;
     int paused_ = 0;
+    // Set when quiesce() could not stop the executor: host memory it may still read stays
+    // registered (leaked) instead of being unregistered under a running kernel.
+    bool wedged_ = false;
+    std::vector<queue::Ring> graveyard_;  // rings of objects destroyed while wedged (kept mapped)
     uint64_t launches_ = 0;
     std::atomic<bool> stop_monitor_{false};
     std::thread monitor_;
@@ -260,11 +264,15 @@ void GpuEngine::detach_cq(control::Cq &cq) noexcept {
         DevCq zero{};
         copy_to_device(d, &zero, sizeof(zero));
         set_device();
-        cudaHostUnregister(cq.ring.mapping());
         const uint32_t slot = uint32_t(d - cqs_);
-        cudaFree(cq_ready_[slot]);
-        cq_ready_[slot] = nullptr;
-        free_cq_slots_.push_back(slot);
+        if (!wedged_) {
+            cudaHostUnregister(cq.ring.mapping());
+            cudaFree(cq_ready_[slot]);
+            cq_ready_[slot] = nullptr;
+            free_cq_slots_.push_back(slot);
+        } else {
+            graveyard_.push_back(std::move(cq.ring));
+        }
         cq.engine_block = nullptr;
     }
     resume();
@@ -377,9 +385,14 @@ void GpuEngine::detach_qp(control::Qp &qp) noexcept {
         set_device();
         for (size_t i = 0; i < qps_host_.size(); ++i) {
             if (qps_host_[i].qp != &qp) continue;
-            cudaHostUnregister(qp.sq.mapping());
-            cudaHostUnregister(qp.rq.mapping());
-            free_qp_slots_.push_back(qps_host_[i].slot);
+            if (!wedged_) {
+                cudaHostUnregister(qp.sq.mapping());
+                cudaHostUnregister(qp.rq.mapping());
+                free_qp_slots_.push_back(qps_host_[i].slot);
+            } else {
+                graveyard_.push_back(std::move(qp.sq));
+                graveyard_.push_back(std::move(qp.rq));
+            }
             qps_host_[i] = qps_host_.back();
             qps_host_.pop_back();
             break;
@@ -488,7 +501,14 @@ void GpuEngine::quiesce() {
     TraceRange range("ugdr.engine.quiesce");
     std::lock_guard<std::mutex> lk(mu_);
     paused_ += 1;
-    stop_kernel_locked(cfg_.max_wait_ms * 4);
+    // Every device wait is bounded by max_wait_ms and the kernel checks the stop flag between
+    // waits, so one round normally suffices; a few more cover a pass that chains several waits.
+    bool stopped = false;
+    for (int round = 0; round < 4 && !stopped; ++round) stopped = stop_kernel_locked(cfg_.max_wait_ms * 4);
+    wedged_ = !stopped;
+    if (wedged_)
+        std::fprintf(stderr, "ugdr: GPU %d executor did not stop; ring memory of destroyed objects stays registered\n",
+                     cfg_.ordinal);
 }
 
 void GpuEngine::resume() {

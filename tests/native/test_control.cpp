@@ -15,6 +15,7 @@
 #include <memory>
 #include <mutex>
 #include <random>
+#include <string>
 #include <vector>
 
 using namespace ugdr;
@@ -466,4 +467,92 @@ TEST(cpu_engine_survives_garbage_wqes) {
     // Bytes outside the registered range were never written.
     CHECK(std::memcmp(base, before.data(), kOff) == 0);
     CHECK(std::memcmp(base + kOff + kLen, before.data() + kOff + kLen, kRegion - kOff - kLen) == 0);
+}
+
+namespace {
+
+// An engine that records the calls the control plane makes, for ordering checks.
+class RecordingEngine : public Engine {
+  public:
+    RecordingEngine(std::vector<std::string> *log, std::string name) : log_(log), name_(std::move(name)) {}
+    DeviceInfo info() const override {
+        DeviceInfo d;
+        d.name = name_;
+        d.kind = DeviceKind::gpu;
+        return d;
+    }
+    int attach_mr(Mr &) override { return 0; }
+    void detach_mr(Mr &) noexcept override {}
+    int attach_cq(Cq &) override { return 0; }
+    void detach_cq(Cq &) noexcept override {}
+    int attach_qp(Qp &) override { return 0; }
+    void update_qp(Qp &q) override { log_->push_back(name_ + ".update_qp(" + std::to_string(q.qpn) + ")"); }
+    void detach_qp(Qp &q) noexcept override { log_->push_back(name_ + ".detach_qp(" + std::to_string(q.qpn) + ")"); }
+    void quiesce() override { log_->push_back(name_ + ".quiesce"); }
+    void resume() override { log_->push_back(name_ + ".resume"); }
+    int stats(EngineStats *, bool) override { return 0; }
+    int hold(bool) override { return 0; }
+
+  private:
+    std::vector<std::string> *log_;
+    std::string name_;
+};
+
+}  // namespace
+
+TEST(control_destroying_a_qp_stops_its_peers_engine_first) {
+    // QP a on GPU engine 1 is bound to QP b on GPU engine 2.  Destroying b must stop engine 1
+    // (which may be writing into b's receive ring), unbind a, drop b from engine 2, then let
+    // engine 1 run again.
+    std::vector<std::string> log;
+    RecordingEngine e1(&log, "e1"), e2(&log, "e2");
+    HostBackend mem;
+    ControlPlane cp{{&e1, &e2}, mem};
+    auto call = [&](uint32_t method, uint64_t id, uint64_t length = 0, uint32_t access = 0,
+                    std::vector<std::byte> opaque = {}) {
+        Request r;
+        r.method = method;
+        r.identity = id;
+        r.length = length;
+        r.access = access;
+        r.opaque = std::move(opaque);
+        return cp.dispatch(1, std::move(r));
+    };
+    uint64_t qp[2];
+    uint32_t qpn[2];
+    for (int i = 0; i < 2; ++i) {
+        const uint64_t ctx = call(kCreateContext, uint64_t(i + 1)).identity;
+        const uint64_t pd = call(kCreatePd, ctx).identity;
+        const uint64_t cq = call(kCreateCq, ctx, 16).identity;
+        std::vector<std::byte> o;
+        ByteWriter w(&o);
+        w.be(cq).be(cq).be(uint32_t(16)).be(uint32_t(16)).be(uint32_t(1)).be(uint32_t(1)).be(uint32_t(UGDR_QPT_RC));
+        w.be(uint32_t(0));
+        Response q = call(kCreateQp, pd, 0, 0, std::move(o));
+        CHECK_EQ(q.status, 0);
+        qp[i] = q.identity;
+        qpn[i] = qpn_of(q);
+        std::vector<std::byte> m;
+        ByteWriter mw(&m);
+        mw.be(uint32_t(UGDR_QPS_INIT)).be(uint32_t(0)).be(uint32_t(UGDR_ACCESS_REMOTE_WRITE));
+        mw.be(uint8_t(14)).be(uint8_t(7)).be(uint8_t(7)).be(uint8_t(12));
+        CHECK_EQ(call(kModifyQp, qp[i], 0, UGDR_QP_STATE | UGDR_QP_ACCESS_FLAGS, std::move(m)).status, 0);
+    }
+    for (int i = 0; i < 2; ++i) {
+        std::vector<std::byte> o;
+        ByteWriter w(&o);
+        w.be(qpn[1 - i]).be(uint32_t(0)).be(uint32_t(0)).be(uint32_t(0)).be(uint8_t(14)).be(uint8_t(7));
+        w.be(uint8_t(7)).be(uint8_t(1));
+        CHECK_EQ(call(kConnectQp, qp[i], 0,
+                      UGDR_QP_TIMEOUT | UGDR_QP_RETRY_CNT | UGDR_QP_RNR_RETRY | UGDR_QP_MIN_RNR_TIMER, std::move(o))
+                     .status,
+                 0);
+    }
+    log.clear();
+    CHECK_EQ(call(kDestroyQp, qp[1]).status, 0);
+    const std::vector<std::string> want = {"e1.quiesce", "e1.update_qp(" + std::to_string(qpn[0]) + ")",
+                                           "e2.detach_qp(" + std::to_string(qpn[1]) + ")", "e1.resume"};
+    CHECK(log == want);
+    if (log != want)
+        for (const std::string &l : log) std::fprintf(stderr, "    got %s\n", l.c_str());
 }
