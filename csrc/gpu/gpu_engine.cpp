@@ -84,6 +84,10 @@ class GpuEngine final : public control::Engine {
     // Ask a running kernel to exit and wait (bounded); returns false if it did not stop.
     bool stop_kernel_locked(uint32_t timeout_ms);
     bool kernel_done_locked();
+    // True while some chunked copy still has pieces nobody has claimed (job bitmap non-zero).
+    // A stopped kernel has finished every piece it claimed, so with the bitmap clear no copy
+    // into any MR is left half done.
+    bool copies_pending_locked();
     void monitor();
     void fill_qp_config(control::Qp &qp, DevQpConfig *cfg);
 
@@ -203,9 +207,22 @@ int GpuEngine::attach_mr(control::Mr &mr) {
 }
 
 void GpuEngine::detach_mr(control::Mr &mr) noexcept {
+    // Clear the entry's `valid` word first (one aligned 4-byte store, so a running warp sees
+    // either the whole old entry or an invalid one): a kernel that quiesce() restarts to finish
+    // pending copies then resolves no new WR against this MR.  Warps of the running kernel may
+    // still hold it in their MR caches, which the stop clears.  The rest of the entry is zeroed
+    // once the kernel is stopped.
+    {
+        std::lock_guard<std::mutex> lk(mu_);
+        const uint32_t invalid = 0;
+        copy_to_device(&mrs_[mr.table_slot].valid, &invalid, sizeof(invalid));
+    }
     quiesce();
-    DevMr d{};
-    copy_to_device(&mrs_[mr.table_slot], &d, sizeof(d));
+    {
+        std::lock_guard<std::mutex> lk(mu_);
+        DevMr d{};
+        copy_to_device(&mrs_[mr.table_slot], &d, sizeof(d));
+    }
     resume();
 }
 
@@ -420,6 +437,15 @@ bool GpuEngine::kernel_done_locked() {
     return true;
 }
 
+bool GpuEngine::copies_pending_locked() {
+    uint32_t words[32] = {};
+    if (copy_from_device(words, reinterpret_cast<uint8_t *>(jobs_) + sizeof(JobRing), sizeof(words)) != 0)
+        return false;
+    for (uint32_t x : words)
+        if (x != 0) return true;
+    return false;
+}
+
 bool GpuEngine::stop_kernel_locked(uint32_t timeout_ms) {
     if (!running_) return true;
     set_device();
@@ -505,6 +531,17 @@ void GpuEngine::quiesce() {
     // waits, so one round normally suffices; a few more cover a pass that chains several waits.
     bool stopped = false;
     for (int round = 0; round < 4 && !stopped; ++round) stopped = stop_kernel_locked(cfg_.max_wait_ms * 4);
+    // The caller is about to take memory away (an MR, a ring).  A stop can leave chunked copies
+    // with unclaimed pieces whose resolved addresses point into it, so run the executor on until
+    // none is left (bounded; a held engine is not restarted).
+    const auto deadline = Clock::now() + std::chrono::milliseconds(cfg_.max_wait_ms);
+    while (stopped && !held_ && copies_pending_locked() && Clock::now() < deadline) {
+        if (launch_locked(kPersistent, 0, false) != 0) break;
+        std::this_thread::sleep_for(std::chrono::microseconds(200));
+        stopped = stop_kernel_locked(cfg_.max_wait_ms * 4);
+    }
+    if (stopped && copies_pending_locked())
+        std::fprintf(stderr, "ugdr: GPU %d stopped with chunked copies still pending\n", cfg_.ordinal);
     wedged_ = !stopped;
     if (wedged_)
         std::fprintf(stderr, "ugdr: GPU %d executor did not stop; ring memory of destroyed objects stays registered\n",
