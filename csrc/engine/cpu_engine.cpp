@@ -17,6 +17,14 @@ uint64_t now_ns() {
     return uint64_t(ts.tv_sec) * 1000000000ull + uint64_t(ts.tv_nsec);
 }
 
+inline void cpu_relax() {
+#if defined(__x86_64__) || defined(__i386__)
+    __builtin_ia32_pause();
+#elif defined(__aarch64__)
+    asm volatile("yield" ::: "memory");
+#endif
+}
+
 struct Seg {
     uint8_t *local;
     uint32_t length;
@@ -341,19 +349,31 @@ size_t CpuEngine::progress_locked() {
     return n;
 }
 
+// Idle policy: spin (with a pause hint) for the first 50 us without work, then yield the CPU
+// between passes for up to 2 ms, then sleep 50 us per pass.  Yielding keeps the engine
+// responsive while letting a client that shares its core run; a sleep costs tens of
+// microseconds however short it is asked to be.
 void CpuEngine::run() {
-    uint32_t idle = 0;
+    uint64_t idle_since = 0;
     while (!stop_.load(std::memory_order_relaxed)) {
         size_t n = 0;
         if (!held_.load(std::memory_order_relaxed)) {
             std::lock_guard<std::mutex> lk(objects_mu_);
             n = progress_locked();
         }
-        if (n == 0) {
-            idle = idle < 64 ? idle + 1 : idle;
-            if (idle > 16) std::this_thread::sleep_for(std::chrono::microseconds(idle > 60 ? 50 : 2));
+        if (n != 0) {
+            idle_since = 0;
+            continue;
+        }
+        const uint64_t now = now_ns();
+        if (idle_since == 0) idle_since = now;
+        const uint64_t idle = now - idle_since;
+        if (idle < 50000) {
+            for (int i = 0; i < 16; ++i) cpu_relax();
+        } else if (idle < 2000000) {
+            std::this_thread::yield();
         } else {
-            idle = 0;
+            std::this_thread::sleep_for(std::chrono::microseconds(50));
         }
     }
 }
