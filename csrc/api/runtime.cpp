@@ -573,6 +573,36 @@ int ugdr_x_query_qp_stats(ugdr_qp *qp, ugdr_x_qp_stats *stats) noexcept {
     return 0;
 }
 
+int ugdr_x_engine_trace(ugdr_context *ctx, uint32_t records_per_cta) noexcept {
+    if (!rt().live(ctx)) return EINVAL;
+    Request req = make(kEngineTrace, ctx->identity);
+    req.length = records_per_cta;
+    req.access = 0;
+    Response resp;
+    return rt().call(std::move(req), &resp);
+}
+
+int ugdr_x_engine_trace_dump(ugdr_context *ctx, const char *path, uint64_t *kept, uint64_t *dropped) noexcept {
+    if (!rt().live(ctx) || path == nullptr || path[0] == '\0') return EINVAL;
+    try {
+        Request req = make(kEngineTrace, ctx->identity);
+        req.access = 1;
+        const size_t n = std::strlen(path);
+        req.opaque.resize(n);
+        std::memcpy(req.opaque.data(), path, n);
+        Response resp;
+        if (int rc = rt().call(std::move(req), &resp); rc != 0) return rc;
+        ByteReader rd(resp.opaque);
+        uint64_t k = 0, d = 0;
+        if (!rd.be(&k) || !rd.be(&d)) return EPROTO;
+        if (kept) *kept = k;
+        if (dropped) *dropped = d;
+        return 0;
+    } catch (...) {
+        return ENOMEM;
+    }
+}
+
 int ugdr_x_engine_hold(ugdr_context *ctx, int hold) noexcept {
     if (!rt().live(ctx)) return EINVAL;
     Request req = make(kEngineHold, ctx->identity);

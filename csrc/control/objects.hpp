@@ -170,6 +170,19 @@ class Engine {
     virtual void resume() = 0;
 
     virtual int stats(EngineStats *out, bool reset) = 0;
+    // Device trace: keep up to `records_per_unit` events per execution unit from the next launch
+    // on (0 turns tracing off and frees the buffer); trace_dump writes what was kept, as Chrome
+    // trace-event JSON, to `path`.
+    virtual int trace(uint32_t records_per_unit) {
+        (void)records_per_unit;
+        return EOPNOTSUPP;
+    }
+    virtual int trace_dump(const std::string &path, uint64_t *kept, uint64_t *dropped) {
+        (void)path;
+        (void)kept;
+        (void)dropped;
+        return EOPNOTSUPP;
+    }
     virtual int qp_counters(Qp &qp, QpCounters *out) {
         (void)qp;
         (void)out;

@@ -42,6 +42,7 @@ enum Method : uint32_t {
     kEngineHold = 33,
     kTimedDrain = 34,
     kQpStats = 35,
+    kEngineTrace = 36,
 };
 
 struct Request {

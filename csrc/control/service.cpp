@@ -112,6 +112,7 @@ const char *method_range(uint32_t m) {
     case kEngineHold: return "ugdr.rpc.engine_hold";
     case kTimedDrain: return "ugdr.rpc.timed_drain";
     case kQpStats: return "ugdr.rpc.qp_stats";
+    case kEngineTrace: return "ugdr.rpc.engine_trace";
     default: return names[0];
     }
 }
@@ -139,6 +140,7 @@ Response ControlPlane::dispatch(ipc::SessionId s, Request &&r) {
     case kEngineHold: return engine_hold(s, r);
     case kTimedDrain: return timed_drain(s, r);
     case kQpStats: return qp_stats(s, r);
+    case kEngineTrace: return engine_trace(s, r);
     default: return status(EOPNOTSUPP);
     }
 }
@@ -565,6 +567,27 @@ Response ControlPlane::qp_stats(uint64_t s, const Request &r) {
     ByteWriter w(&out.opaque);
     w.be(qp->sq.tail()).be(qp->sq.head()).be(qp->rq.tail()).be(qp->rq.head());
     w.be(c.bytes).be(c.error_completions).be(c.rnr_waits).be(uint32_t(qp->state));
+    return out;
+}
+
+// access 0: keep r.length trace records per execution unit from now on (0 = off);
+// access 1: write the kept records to the file named by the payload (the daemon's file system).
+Response ControlPlane::engine_trace(uint64_t s, const Request &r) {
+    Context *ctx = contexts_.find(s, r.identity);
+    if (ctx == nullptr || r.access > 1) return status(EINVAL);
+    Engine *e = engines_[ctx->device];
+    if (r.access == 0) {
+        if (r.length > 0xffffffffull) return status(EINVAL);
+        return status(e->trace(uint32_t(r.length)));
+    }
+    if (r.opaque.empty() || r.opaque.size() > 4096) return status(EINVAL);
+    const std::string path(reinterpret_cast<const char *>(r.opaque.data()), r.opaque.size());
+    if (path.find('\0') != std::string::npos) return status(EINVAL);
+    uint64_t kept = 0, dropped = 0;
+    if (int rc = e->trace_dump(path, &kept, &dropped); rc != 0) return status(rc);
+    Response out;
+    ByteWriter w(&out.opaque);
+    w.be(kept).be(dropped);
     return out;
 }
 

@@ -189,6 +189,24 @@ struct HostCtrl {
 
 enum ExecMode : uint32_t { kPersistent = 0, kDrain = 1 };
 
+// Optional device trace: one 32-byte record per event, appended by lane 0 of the warp that saw
+// it into its CTA's segment of the trace buffer (`trace_cap` records per CTA; later events are
+// only counted).  Times are %globaltimer nanoseconds.
+enum TraceEvent : uint32_t {
+    kTraceFastBatch = 1,  // lane-parallel batch: fetch .. CQ publish; value = WRs
+    kTraceRetire = 2,     // in-order retire of staged / chunked WRs; value = WRs retired
+    kTraceChunk = 3,      // one chunk copied by a worker warp; value = bytes
+    kTraceError = 4,      // a bounded wait ran out; value = error code
+};
+
+struct TraceRec {
+    unsigned long long t0, t1;
+    uint32_t event;  // TraceEvent << 16 | global warp index & 0xffff
+    uint32_t qp;     // QP slot (0xffffffff when none)
+    uint32_t value;
+    uint32_t cta;
+};
+
 struct ExecParams {
     DevMr *mrs;
     DevQp *qps;
@@ -199,6 +217,9 @@ struct ExecParams {
     unsigned long long expected;  // drain: exit once this many WRs retired
     unsigned long long idle_exit_ns;
     unsigned long long max_wait_ns;  // bound on every internal spin
+    TraceRec *trace;             // null: tracing off
+    unsigned int *trace_count;   // one append counter per CTA
+    uint32_t trace_cap;          // records per CTA
 };
 
 }  // namespace ugdr::gpu

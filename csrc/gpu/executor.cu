@@ -349,8 +349,24 @@ struct Warp {
     QpView *vv;  // cached view of the QP serviced last (shared memory)
 };
 
+// Appends one trace record (lane 0 only; the caller checks that tracing is on).  Not inlined:
+// the hot paths keep only the null test of p->trace.
+__device__ __noinline__ void trace_event(const ExecParams *p, uint32_t ev, uint32_t gwarp, uint32_t qp,
+                                         uint32_t value, uint64_t t0, uint64_t t1) {
+    const uint32_t i = atomicAdd(&p->trace_count[blockIdx.x], 1u);
+    if (i >= p->trace_cap) return;
+    TraceRec *r = p->trace + size_t(blockIdx.x) * p->trace_cap + i;
+    r->t0 = t0;
+    r->t1 = t1;
+    r->event = (ev << 16) | (gwarp & 0xffffu);
+    r->qp = qp;
+    r->value = value;
+    r->cta = blockIdx.x;
+}
+
 __device__ void record_error(Warp &w, uint32_t code) {
     if (w.lane == 0) {
+        if (w.p->trace != nullptr) trace_event(w.p, kTraceError, w.gwarp, 0xffffffffu, code, gtime(), gtime());
         atomicCAS(&w.p->stats->error_code, 0u, code);
         atomicAdd(&w.p->stats->wait_timeouts, 1ull);
         atomicExch(&w.p->stats->exiting, 1u);
@@ -672,9 +688,13 @@ __device__ void run_chunk(Warp &w, const Claim &cl) {
         atomicAdd(&rec->chunks_done, 1u);
         if (atomicAdd(&cl.job->done, 1u) + 1 == cl.n) atomicAdd(&cl.job->seq, 1ull);  // free the slot
     }
-    if (w.lane == 0) w.ctr->n_chunks += 1;
-    if (w.lane == 0) w.ctr->bytes += len;
-    if (w.lane == 0) w.ctr->busy += gtime() - t0;
+    if (w.lane == 0) {
+        const uint64_t t1 = gtime();
+        w.ctr->n_chunks += 1;
+        w.ctr->bytes += len;
+        w.ctr->busy += t1 - t0;
+        if (w.p->trace != nullptr) trace_event(w.p, kTraceChunk, w.gwarp, 0xffffffffu, uint32_t(len), t0, t1);
+    }
 }
 
 // Fold the warp's private counters into DevStats (lane 0).
@@ -1232,7 +1252,10 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
 
     int r = 0;
     if (w.vhead != w.vissue) {
+        const uint64_t t_r0 = gtime();
         r = retire(w, qp, v, cqe_smem);
+        if (r > 0 && w.lane == 0 && w.p->trace != nullptr)
+            trace_event(w.p, kTraceRetire, w.gwarp, uint32_t(qp - w.p->qps), uint32_t(r), t_r0, gtime());
         if (r < 0) {
             record_error(w, r == -1 ? kErrCqPublishTimeout : kErrRqReleaseTimeout);
             return work;
@@ -1449,9 +1472,14 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
                 atomicAdd(&w.p->stats->fast_exec_ns, (unsigned long long)(t_exec1 - t_fetch1));
                 atomicAdd(&w.p->stats->fast_reserve_ns, (unsigned long long)(t_res - t_exec1));
                 atomicAdd(&w.p->stats->fast_publish_ns, (unsigned long long)(t_end - t_res));
+                if (w.p->trace != nullptr)
+                    trace_event(w.p, kTraceFastBatch, w.gwarp, uint32_t(qp - w.p->qps), fast_n, t_fetch0, t_end);
             }
         } else {
+            const uint64_t t_r0 = gtime();
             r = retire(w, qp, v, cqe_smem);
+            if (r > 0 && w.lane == 0 && w.p->trace != nullptr)
+                trace_event(w.p, kTraceRetire, w.gwarp, uint32_t(qp - w.p->qps), uint32_t(r), t_r0, gtime());
         }
         if (r < 0) {
             record_error(w, r == -1 ? kErrCqPublishTimeout : kErrRqReleaseTimeout);

@@ -9,6 +9,7 @@
 
 #include <cuda_runtime_api.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cerrno>
 #include <chrono>
@@ -64,6 +65,8 @@ class GpuEngine final : public control::Engine {
     void resume() override;
     int stats(control::EngineStats *out, bool reset) override;
     int qp_counters(control::Qp &qp, control::QpCounters *out) override;
+    int trace(uint32_t records_per_unit) override;
+    int trace_dump(const std::string &path, uint64_t *kept, uint64_t *dropped) override;
     int hold(bool on) override;
     int start_drain(uint64_t expected) override;
     int finish_drain(uint32_t timeout_ms, float *elapsed_ms) override;
@@ -112,6 +115,9 @@ class GpuEngine final : public control::Engine {
     // Set when quiesce() could not stop the executor: host memory it may still read stays
     // registered (leaked) instead of being unregistered under a running kernel.
     bool wedged_ = false;
+    TraceRec *trace_ = nullptr;          // device trace buffer (ctas x trace_cap_ records)
+    unsigned int *trace_count_ = nullptr;
+    uint32_t trace_cap_ = 0;
     std::vector<queue::Ring> graveyard_;  // rings of objects destroyed while wedged (kept mapped)
     uint64_t launches_ = 0;
     std::atomic<bool> stop_monitor_{false};
@@ -137,6 +143,8 @@ GpuEngine::~GpuEngine() {
         if (r) cudaFree(r);
     cudaFree(jobs_);
     cudaFree(stats_);
+    cudaFree(trace_);
+    cudaFree(trace_count_);
     if (ctrl_) cudaFreeHost(ctrl_);
 }
 
@@ -493,6 +501,9 @@ int GpuEngine::launch_locked(uint32_t mode, uint64_t expected, bool timed) {
     p.expected = expected;
     p.idle_exit_ns = uint64_t(cfg_.idle_exit_us) * 1000ull;
     p.max_wait_ns = uint64_t(cfg_.max_wait_ms) * 1000000ull;
+    p.trace = trace_;
+    p.trace_count = trace_count_;
+    p.trace_cap = trace_cap_;
     if (vis_.mode() == VisibilityGate::Mode::kFlush && vis_.before_publish() != 0) return EIO;
     if (timed) cudaEventRecord(ev_start_, exec_stream_);
     const int rc = launch_executor(p, cfg_.ctas, exec_stream_);
@@ -551,6 +562,100 @@ void GpuEngine::quiesce() {
 void GpuEngine::resume() {
     std::lock_guard<std::mutex> lk(mu_);
     if (paused_ > 0) paused_ -= 1;
+}
+
+int GpuEngine::trace(uint32_t records_per_unit) {
+    if (records_per_unit > (1u << 20)) return EINVAL;
+    quiesce();
+    int rc = 0;
+    {
+        std::lock_guard<std::mutex> lk(mu_);
+        set_device();
+        cudaFree(trace_);
+        cudaFree(trace_count_);
+        trace_ = nullptr;
+        trace_count_ = nullptr;
+        trace_cap_ = 0;
+        if (records_per_unit > 0) {
+            const size_t n = size_t(cfg_.ctas) * records_per_unit;
+            if (cudaMalloc(reinterpret_cast<void **>(&trace_), n * sizeof(TraceRec)) != cudaSuccess ||
+                cudaMalloc(reinterpret_cast<void **>(&trace_count_), size_t(cfg_.ctas) * sizeof(unsigned int)) !=
+                    cudaSuccess ||
+                cudaMemsetAsync(trace_count_, 0, size_t(cfg_.ctas) * sizeof(unsigned int), ctl_stream_) !=
+                    cudaSuccess ||
+                cudaStreamSynchronize(ctl_stream_) != cudaSuccess) {
+                (void)cudaGetLastError();
+                cudaFree(trace_);
+                cudaFree(trace_count_);
+                trace_ = nullptr;
+                trace_count_ = nullptr;
+                rc = ENOMEM;
+            } else {
+                trace_cap_ = records_per_unit;
+            }
+        }
+    }
+    resume();
+    return rc;
+}
+
+// Chrome trace-event JSON ("X" events, microseconds from the first record): one row per warp,
+// grouped by CTA.  The counters restart, so each dump holds the events since the last one.
+int GpuEngine::trace_dump(const std::string &path, uint64_t *kept, uint64_t *dropped) {
+    quiesce();
+    int rc = 0;
+    std::vector<unsigned int> counts;
+    std::vector<TraceRec> recs;
+    {
+        std::lock_guard<std::mutex> lk(mu_);
+        if (trace_ == nullptr) {
+            rc = EINVAL;
+        } else {
+            counts.resize(size_t(cfg_.ctas));
+            recs.resize(size_t(cfg_.ctas) * trace_cap_);
+            if (copy_from_device(counts.data(), trace_count_, counts.size() * sizeof(unsigned int)) != 0 ||
+                copy_from_device(recs.data(), trace_, recs.size() * sizeof(TraceRec)) != 0) {
+                rc = EIO;
+            } else {
+                cudaMemsetAsync(trace_count_, 0, counts.size() * sizeof(unsigned int), ctl_stream_);
+                cudaStreamSynchronize(ctl_stream_);
+            }
+        }
+    }
+    resume();
+    if (rc != 0) return rc;
+    static const char *names[] = {"?", "fast_batch", "retire", "chunk", "error"};
+    uint64_t t_min = ~0ull, n_kept = 0, n_drop = 0;
+    for (size_t c = 0; c < counts.size(); ++c) {
+        const uint32_t k = counts[c] < trace_cap_ ? counts[c] : trace_cap_;
+        n_kept += k;
+        n_drop += counts[c] - k;
+        for (uint32_t i = 0; i < k; ++i) t_min = std::min<uint64_t>(t_min, recs[c * trace_cap_ + i].t0);
+    }
+    FILE *f = std::fopen(path.c_str(), "w");
+    if (f == nullptr) return errno != 0 ? errno : EIO;
+    std::fprintf(f, "{\"traceEvents\": [");
+    bool first = true;
+    for (size_t c = 0; c < counts.size(); ++c) {
+        const uint32_t k = counts[c] < trace_cap_ ? counts[c] : trace_cap_;
+        for (uint32_t i = 0; i < k; ++i) {
+            const TraceRec &r = recs[c * trace_cap_ + i];
+            const uint32_t ev = r.event >> 16;
+            std::fprintf(f,
+                         "%s\n{\"name\": \"%s\", \"ph\": \"X\", \"pid\": %u, \"tid\": %u, \"ts\": %.3f, "
+                         "\"dur\": %.3f, \"args\": {\"qp\": %d, \"value\": %u}}",
+                         first ? "" : ",", ev < 5 ? names[ev] : "?", r.cta, r.event & 0xffffu,
+                         double(r.t0 - t_min) / 1000.0, double(r.t1 - r.t0) / 1000.0,
+                         r.qp == 0xffffffffu ? -1 : int(r.qp), r.value);
+            first = false;
+        }
+    }
+    std::fprintf(f, "\n], \"displayTimeUnit\": \"ns\", \"otherData\": {\"gpu\": %d, \"dropped\": %llu}}\n",
+                 cfg_.ordinal, (unsigned long long)n_drop);
+    const bool ok = std::fclose(f) == 0;
+    if (kept) *kept = n_kept;
+    if (dropped) *dropped = n_drop;
+    return ok ? 0 : EIO;
 }
 
 // The owner warp keeps each QP's byte and error counts in its device state; RNR waits are not

@@ -291,6 +291,16 @@ typedef struct ugdr_x_qp_stats {
 
 int ugdr_x_query_qp_stats(ugdr_qp *qp, ugdr_x_qp_stats *stats) UGDR_NOEXCEPT;
 
+/* Device trace of a GPU context's executor.  ugdr_x_engine_trace keeps up to
+ * `records_per_cta` events per CTA from the next launch on (0 turns it off): lane-parallel
+ * batches, in-order retires, chunk copies and bounded-wait errors, each with %globaltimer start
+ * and end.  ugdr_x_engine_trace_dump has the daemon write the events kept since the last dump to
+ * `path` (on the daemon's file system) as Chrome trace-event JSON, and returns how many were
+ * kept and dropped.  EOPNOTSUPP on the host-memory device. */
+int ugdr_x_engine_trace(ugdr_context *context, uint32_t records_per_cta) UGDR_NOEXCEPT;
+int ugdr_x_engine_trace_dump(ugdr_context *context, const char *path, uint64_t *kept,
+                             uint64_t *dropped) UGDR_NOEXCEPT;
+
 /* Timed drain (benchmarks): the daemon launches the device executors of `num_contexts`
  * contexts together, each bracketed by CUDA events on its launching stream, and returns once
  * every executor has retired `expected_wrs[i]` send WRs or `timeout_ms` passed.  `elapsed_ms[i]`

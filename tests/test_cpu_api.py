@@ -130,6 +130,20 @@ def test_qp_stats_count_wrs_bytes_rnr_and_errors(cpu_daemon):
         buf.free()
 
 
+def test_engine_trace_is_a_gpu_feature(cpu_daemon):
+    """The device trace exists on GPU contexts only: the host-memory device answers EOPNOTSUPP."""
+    import errno
+
+    ctx = V.Context(V.find_device(kind=0))
+    try:
+        for call in (lambda: ctx.trace(16), lambda: ctx.trace_dump("/nonexistent/trace.json")):
+            with pytest.raises(V.UgdrError) as e:
+                call()
+            assert e.value.errno == errno.EOPNOTSUPP
+    finally:
+        ctx.close()
+
+
 def test_write_with_imm_consumes_rq_in_order(cpu_daemon):
     ctx, pd, cq, a, b = _pair()
     buf = V.HostBuffer(1 << 16)

@@ -171,6 +171,17 @@ class Context:
         _check(N.lib().ugdr_x_query_engine_stats(self.h, C.byref(st), int(reset)), "engine stats")
         return st
 
+    def trace(self, records_per_cta: int) -> None:
+        """Keep up to `records_per_cta` executor events per CTA from the next launch on (0: off)."""
+        _check(N.lib().ugdr_x_engine_trace(self.h, records_per_cta), "ugdr_x_engine_trace")
+
+    def trace_dump(self, path: str) -> tuple[int, int]:
+        """Write the kept events (Chrome trace JSON) to `path`; returns (kept, dropped)."""
+        k, d = C.c_uint64(), C.c_uint64()
+        _check(N.lib().ugdr_x_engine_trace_dump(self.h, path.encode(), C.byref(k), C.byref(d)),
+               "ugdr_x_engine_trace_dump")
+        return k.value, d.value
+
     def hold(self, on: bool) -> None:
         _check(N.lib().ugdr_x_engine_hold(self.h, int(on)), "engine hold")
 
