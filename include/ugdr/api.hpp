@@ -333,6 +333,11 @@ typedef struct ugdr_x_kernel_attr {
  * Returns 0, -1 past the last kernel, or a cudaError_t value. */
 int ugdr_x_kernel_attributes(int index, ugdr_x_kernel_attr *out) UGDR_NOEXCEPT;
 
+/* The same timing for the TMA bulk-copy kernel (cp.async.bulk global -> shared -> global;
+ * src, dst and n multiples of 16).  *status: 0, or 1 if a bounded wait ran out. */
+int ugdr_x_bulk_copy_bench(void *dst, const void *src, uint64_t n, int ctas, int iters, void *stream,
+                           float *ms_per_copy, unsigned int *status) UGDR_NOEXCEPT;
+
 int ugdr_x_grid_copy_bench(void *dst, const void *src, uint64_t n, int ctas, int iters, void *stream,
                            float *ms_per_copy) UGDR_NOEXCEPT;
 

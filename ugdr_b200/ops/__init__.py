@@ -2,6 +2,7 @@
 
 * copy_core(dst, src)      the executor's warp copy core over one range (one warp; for tests)
 * grid_copy_ms(dst, src)   mean ms of a whole-grid copy with the executor's copy core
+* bulk_copy_ms(dst, src)   the same copy staged through shared memory by the TMA bulk engine
 * moe_route(ids, nexp)     deterministic counting sort of (token, k) rows by expert
 * register(pd, tensor)     a verbs MR over a tensor's bytes (local write + remote read / write)
 * kernel_attributes()      registers, spills, static shared memory and blocks per SM of every
@@ -36,6 +37,9 @@ def _lib():
         for fn in ("ugdr_x_kernel_attributes", "ugdr_x_collective_kernel_attributes"):
             getattr(L, fn).restype = C.c_int
             getattr(L, fn).argtypes = [C.c_int, C.POINTER(KernelAttr)]
+        L.ugdr_x_bulk_copy_bench.restype = C.c_int
+        L.ugdr_x_bulk_copy_bench.argtypes = [C.c_void_p, C.c_void_p, C.c_uint64, C.c_int, C.c_int, C.c_void_p,
+                                             C.POINTER(C.c_float), C.POINTER(C.c_uint)]
         L._ops_sigs = True
     return L
 
@@ -67,6 +71,23 @@ def grid_copy_ms(dst: torch.Tensor, src: torch.Tensor, ctas: int = 0, iters: int
                                       _stream(stream), C.byref(ms))
     if rc != 0:
         raise RuntimeError(f"ugdr_x_grid_copy_bench failed: cudaError {rc}")
+    return float(ms.value)
+
+
+def bulk_copy_ms(dst: torch.Tensor, src: torch.Tensor, ctas: int = 0, iters: int = 10,
+                 stream: torch.cuda.Stream | None = None) -> float:
+    """Mean milliseconds of a whole-grid copy of src into dst through the TMA bulk-copy engine
+    (global -> shared -> global); both tensors and the size must be 16-byte aligned."""
+    n = src.numel() * src.element_size()
+    if n > dst.numel() * dst.element_size():
+        raise ValueError("destination smaller than source")
+    ms, st = C.c_float(), C.c_uint()
+    rc = _lib().ugdr_x_bulk_copy_bench(C.c_void_p(dst.data_ptr()), C.c_void_p(src.data_ptr()), n, ctas, iters,
+                                      _stream(stream), C.byref(ms), C.byref(st))
+    if rc != 0:
+        raise RuntimeError(f"ugdr_x_bulk_copy_bench failed: cudaError {rc}")
+    if st.value != 0:
+        raise RuntimeError("bulk copy: a bounded wait ran out")
     return float(ms.value)
 
 
