@@ -1,5 +1,6 @@
-// Whole-grid local copy through the TMA bulk-copy engine: global -> shared -> global with
-// cp.async.bulk (untiled, no tensor map, no multicast), one issuing thread per CTA and a
+// Whole-grid local copy through the TMA bulk-copy engine: global -> shared::cta -> global with
+// cp.async.bulk (untiled, no tensor map, this CTA's own shared memory only), one issuing thread
+// per CTA and a
 // kStages-deep ring of shared-memory buffers tracked by mbarriers.  It is the staged
 // counterpart of the executor's load/store copy core (grid_copy_kernel), kept as a diagnostic so
 // the two can be timed against each other on the same buffers.
@@ -56,7 +57,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64
 
 __device__ __forceinline__ void bulk_load(void *smem, const void *gmem, uint32_t bytes, uint64_t *bar) {
     asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+        "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
             smem_addr(smem)),
         "l"(gmem), "r"(bytes), "r"(smem_addr(bar))
         : "memory");

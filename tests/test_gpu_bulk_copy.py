@@ -1,5 +1,5 @@
-"""The TMA bulk-copy diagnostic kernel (cp.async.bulk global -> shared -> global, no multicast)
-against torch's copy: byte-exact over sizes that end mid-stage and mid-chunk, guard bytes
+"""The TMA bulk-copy diagnostic kernel (global -> this CTA's shared memory -> global) against
+torch's copy: byte-exact over sizes that end mid-stage and mid-chunk, guard bytes
 untouched, misaligned requests refused.  It also times the copy against the load/store copy
 core on one buffer larger than L2.
 
