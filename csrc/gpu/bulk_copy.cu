@@ -1,7 +1,6 @@
 // Whole-grid local copy through the TMA bulk-copy engine: global -> shared::cta -> global with
 // cp.async.bulk (untiled, no tensor map, this CTA's own shared memory only), one issuing thread
-// per CTA and a
-// kStages-deep ring of shared-memory buffers tracked by mbarriers.  It is the staged
+// per CTA and a kStages-deep ring of shared-memory buffers tracked by mbarriers.  It is the staged
 // counterpart of the executor's load/store copy core (grid_copy_kernel), kept as a diagnostic so
 // the two can be timed against each other on the same buffers.
 //
