@@ -19,6 +19,7 @@
 #include "ugdr/api.hpp"
 
 #include <atomic>
+#include <chrono>
 #include <cerrno>
 #include <cstdlib>
 #include <cstring>
@@ -391,6 +392,23 @@ int ugdr_poll_cq(ugdr_cq *cq, int num_entries, ugdr_wc *wc) noexcept {
     }
     cq->ring.release(n);
     return int(n);
+}
+
+int ugdr_x_poll_cq_wait(ugdr_cq *cq, int min_entries, int max_entries, ugdr_wc *wc, uint64_t timeout_ns) noexcept {
+    if (min_entries < 0 || max_entries < min_entries || (max_entries > 0 && wc == nullptr)) return -EINVAL;
+    int got = 0;
+    const auto deadline = std::chrono::steady_clock::now() + std::chrono::nanoseconds(timeout_ns);
+    for (uint32_t spins = 0;; ++spins) {
+        const int k = ugdr_poll_cq(cq, max_entries - got, wc + got);
+        if (k < 0) return k;
+        got += k;
+        if (got >= min_entries) return got;
+        // The clock is read now and then; a pause keeps the polling core's sibling responsive.
+        if ((spins & 255u) == 255u && std::chrono::steady_clock::now() >= deadline) return got;
+#if defined(__x86_64__) || defined(__i386__)
+        __builtin_ia32_pause();
+#endif
+    }
 }
 
 ugdr_qp *ugdr_create_qp(ugdr_pd *pd, ugdr_qp_init_attr *init) noexcept {

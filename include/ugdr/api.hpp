@@ -291,6 +291,12 @@ typedef struct ugdr_x_qp_stats {
 
 int ugdr_x_query_qp_stats(ugdr_qp *qp, ugdr_x_qp_stats *stats) UGDR_NOEXCEPT;
 
+/* Busy-polls `cq` until at least `min_entries` completions (at most `max_entries`) were taken
+ * into `wc`, or `timeout_ns` passed.  Returns the number taken (possibly fewer than min_entries
+ * on timeout) or a negative errno, like ugdr_poll_cq. */
+int ugdr_x_poll_cq_wait(ugdr_cq *cq, int min_entries, int max_entries, ugdr_wc *wc,
+                        uint64_t timeout_ns) UGDR_NOEXCEPT;
+
 /* Device trace of a GPU context's executor.  ugdr_x_engine_trace keeps up to
  * `records_per_cta` events per CTA from the next launch on (0 turns it off): lane-parallel
  * batches, in-order retires, chunk copies and bounded-wait errors, each with %globaltimer start

@@ -4,6 +4,7 @@ control_plane_acceptance_test.cpp) and adds the data path the reference only run
 from __future__ import annotations
 
 import ctypes as C
+import errno
 import multiprocessing as mp
 import os
 import random
@@ -142,6 +143,34 @@ def test_engine_trace_is_a_gpu_feature(cpu_daemon):
             assert e.value.errno == errno.EOPNOTSUPP
     finally:
         ctx.close()
+
+
+def test_poll_cq_wait_returns_on_count_or_timeout(cpu_daemon):
+    """ugdr_x_poll_cq_wait: returns as soon as the minimum is there, or with what it has once the
+    timeout passes; CompletionQueue.wait raises TimeoutError past its own deadline."""
+    ctx, pd, cq, a, b = _pair(depth=16, cq_depth=64)
+    buf = V.HostBuffer(8192)
+    mr = pd.reg_mr(buf.addr, 8192, ACC)
+    try:
+        wc = (N.Wc * 8)()
+        t0 = time.perf_counter()
+        assert N.lib().ugdr_x_poll_cq_wait(cq.h, 1, 8, wc, 5_000_000) == 0
+        assert time.perf_counter() - t0 >= 0.004
+        assert N.lib().ugdr_x_poll_cq_wait(cq.h, 2, 1, wc, 0) == -errno.EINVAL
+        for i in range(3):
+            a.post_write((buf.addr, 8, mr.lkey), buf.addr + 4096, mr.rkey, wr_id=i)
+        got = N.lib().ugdr_x_poll_cq_wait(cq.h, 3, 8, wc, 10_000_000_000)
+        assert got == 3 and [wc[i].wr_id for i in range(3)] == [0, 1, 2]
+        with pytest.raises(TimeoutError):
+            cq.wait(1, timeout=0.05)
+    finally:
+        a.destroy()
+        b.destroy()
+        mr.dereg()
+        cq.destroy()
+        pd.dealloc()
+        ctx.close()
+        buf.free()
 
 
 def test_write_with_imm_consumes_rq_in_order(cpu_daemon):

@@ -259,6 +259,7 @@ def lib() -> C.CDLL:
         "ugdr_x_free_host": (i, [vp]),
         "ugdr_x_query_engine_stats": (i, [vp, C.POINTER(EngineStats), i]),
         "ugdr_x_query_qp_stats": (i, [vp, C.POINTER(QpStats)]),
+        "ugdr_x_poll_cq_wait": (i, [vp, i, i, C.POINTER(Wc), C.c_uint64]),
         "ugdr_x_engine_trace": (i, [vp, C.c_uint32]),
         "ugdr_x_engine_trace_dump": (i, [vp, C.c_char_p, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
         "ugdr_x_engine_hold": (i, [vp, i]),

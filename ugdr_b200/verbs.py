@@ -255,10 +255,17 @@ class CompletionQueue:
                 for w in self._buf[:got]]
 
     def wait(self, count: int, timeout: float = 30.0) -> list[Completion]:
+        """At least `count` completions (the C library busy-polls; no Python loop per poll)."""
         out: list[Completion] = []
         deadline = time.time() + timeout
         while len(out) < count:
-            out += self.poll(count - len(out))
+            want = min(count - len(out), 256)
+            left_ns = max(0, int((deadline - time.time()) * 1e9))
+            got = N.lib().ugdr_x_poll_cq_wait(self.h, want, want, self._buf, left_ns)
+            if got < 0:
+                raise UgdrError(-got, f"ugdr_x_poll_cq_wait: {N.errname(-got)}")
+            out += [Completion(w.wr_id, w.status, w.opcode, w.byte_len, w.imm_data, w.qp_num, w.wc_flags)
+                    for w in self._buf[:got]]
             if len(out) < count and time.time() > deadline:
                 raise TimeoutError(f"got {len(out)} of {count} completions")
         return out
