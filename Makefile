@@ -46,19 +46,19 @@ $(OUT)/libugdr.so: $(LIB_OBJS)
 	$(NVCC) $(ARCH) -shared -o $@ $^ -Xlinker -soname=libugdr.so $(LDLIBS)
 
 $(OUT)/ugdr_daemon: $(OBJ)/daemon/main.o $(OUT)/libugdr.so
-	$(CXX) -o $@ $< -L$(OUT) -lugdr -Wl,-rpath,'$$ORIGIN' -pthread
+	$(CXX) -o $@ $< -L$(OUT) -lugdr -Wl,-rpath,'$$ORIGIN:$$ORIGIN/../lib' -pthread
 
 $(OUT)/ugdr_client: $(OBJ)/apps/client_main.o $(OUT)/libugdr.so
-	$(CXX) -o $@ $< -L$(OUT) -lugdr -Wl,-rpath,'$$ORIGIN' -pthread
+	$(CXX) -o $@ $< -L$(OUT) -lugdr -Wl,-rpath,'$$ORIGIN:$$ORIGIN/../lib' -pthread
 
 $(OUT)/ugdr_perf: $(OBJ)/bench/ugdr_perf.o $(OUT)/libugdr.so
-	$(CXX) -o $@ $< -L$(OUT) -lugdr -Wl,-rpath,'$$ORIGIN' $(LDLIBS)
+	$(CXX) -o $@ $< -L$(OUT) -lugdr -Wl,-rpath,'$$ORIGIN:$$ORIGIN/../lib' $(LDLIBS)
 
 $(OUT)/ugdr_engine_bench: $(OBJ)/bench/engine_bench.o $(OUT)/libugdr.so
-	$(CXX) -o $@ $< -L$(OUT) -lugdr -Wl,-rpath,'$$ORIGIN' $(LDLIBS)
+	$(CXX) -o $@ $< -L$(OUT) -lugdr -Wl,-rpath,'$$ORIGIN:$$ORIGIN/../lib' $(LDLIBS)
 
 $(OUT)/ugdr_native_tests: $(TEST_OBJS) $(OUT)/libugdr.so
-	$(CXX) -o $@ $(TEST_OBJS) -L$(OUT) -lugdr -Wl,-rpath,'$$ORIGIN' $(LDLIBS)
+	$(CXX) -o $@ $(TEST_OBJS) -L$(OUT) -lugdr -Wl,-rpath,'$$ORIGIN:$$ORIGIN/../lib' $(LDLIBS)
 
 # Sanitizer builds of the native test suite (host code instrumented; the CUDA objects are the
 # regular ones): `make asan` / `make tsan`, then run build/san/<kind>/ugdr_native_tests.
@@ -96,8 +96,19 @@ $(SAN)/tsan/ugdr_daemon: $(LIB_CXX:csrc/%.cpp=$(SAN)/tsan/%.o) $(SAN)/tsan/daemo
 asan: $(SAN)/asan/ugdr_native_tests $(SAN)/asan/ugdr_daemon
 tsan: $(SAN)/tsan/ugdr_native_tests $(SAN)/tsan/ugdr_daemon
 
+# Installed layout: $(PREFIX)/include/ugdr/*.h{,pp}, $(PREFIX)/lib/libugdr.so and ugdr.pc,
+# $(PREFIX)/bin/{ugdr_daemon,ugdr_client,ugdr_perf,ugdr_engine_bench} (their rpath also looks in
+# ../lib).  `make install PREFIX=/opt/ugdr`; then `pkg-config --cflags --libs ugdr`.
+PREFIX ?= /usr/local
+install: all
+	install -d $(DESTDIR)$(PREFIX)/include/ugdr $(DESTDIR)$(PREFIX)/lib/pkgconfig $(DESTDIR)$(PREFIX)/bin
+	install -m 644 include/ugdr/api.hpp include/ugdr/collective.h $(DESTDIR)$(PREFIX)/include/ugdr/
+	install -m 755 $(OUT)/libugdr.so $(DESTDIR)$(PREFIX)/lib/
+	install -m 755 $(OUT)/ugdr_daemon $(OUT)/ugdr_client $(OUT)/ugdr_perf $(OUT)/ugdr_engine_bench $(DESTDIR)$(PREFIX)/bin/
+	printf 'prefix=%s\nlibdir=$${prefix}/lib\nincludedir=$${prefix}/include\n\nName: ugdr\nDescription: Userspace GPU RDMA verbs over NVLink (libibverbs-shaped C API)\nVersion: 1.0.0\nCflags: -I$${includedir}\nLibs: -L$${libdir} -Wl,-rpath,$${libdir} -lugdr\n' '$(PREFIX)' > $(DESTDIR)$(PREFIX)/lib/pkgconfig/ugdr.pc
+
 clean:
 	rm -rf build/obj build/san $(OUT)/libugdr.so $(OUT)/ugdr_daemon $(OUT)/ugdr_client $(OUT)/ugdr_native_tests $(OUT)/ugdr_perf $(OUT)/ugdr_engine_bench
 
 -include $(shell find build/obj build/san -name '*.d' 2>/dev/null)
-.PHONY: all clean asan tsan
+.PHONY: all clean asan tsan install

@@ -481,3 +481,41 @@ def test_engine_bench_runs_every_case():
     assert r.returncode == 0, r.stderr
     lines = [ln for ln in r.stdout.splitlines() if ln.startswith("benchmark=engine_payload")]
     assert len(lines) == 4 and all("parent_MWR_per_s=" in ln for ln in lines)
+
+
+def test_make_install_layout_and_pkg_config(tmp_path):
+    """`make install PREFIX=...` gives headers, libugdr.so, ugdr.pc and the binaries; the C example
+    builds from pkg-config flags alone and runs against the installed daemon."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None or shutil.which("make") is None or shutil.which("pkg-config") is None:
+        pytest.skip("needs cc, make and pkg-config")
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    prefix = tmp_path / "usr"
+    r = subprocess.run(["make", "install", f"PREFIX={prefix}"], cwd=repo, capture_output=True, text=True,
+                       timeout=900)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    for rel in ("include/ugdr/api.hpp", "include/ugdr/collective.h", "lib/libugdr.so", "lib/pkgconfig/ugdr.pc",
+                "bin/ugdr_daemon", "bin/ugdr_client"):
+        assert (prefix / rel).exists(), rel
+    env = dict(os.environ, PKG_CONFIG_PATH=str(prefix / "lib" / "pkgconfig"))
+    flags = subprocess.run(["pkg-config", "--cflags", "--libs", "ugdr"], env=env, capture_output=True, text=True,
+                           check=True).stdout.split()
+    exe = str(tmp_path / "write_read")
+    subprocess.run([cc, "-std=c11", os.path.join(repo, "examples", "write_read.c"), "-o", exe, *flags], check=True,
+                   capture_output=True, text=True)
+    sock = str(tmp_path / "d.sock")
+    d = subprocess.Popen([str(prefix / "bin" / "ugdr_daemon"), "--socket", sock, "--gpus", "0"],
+                         stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+    try:
+        deadline = time.time() + 20
+        while not os.path.exists(sock) and time.time() < deadline:
+            time.sleep(0.02)
+        r = subprocess.run([exe, "ugdr_cpu0"], env=dict(os.environ, UGDR_DAEMON_SOCKET=sock), capture_output=True,
+                           text=True, timeout=60)
+        assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
+    finally:
+        d.terminate()
+        d.wait(timeout=30)
