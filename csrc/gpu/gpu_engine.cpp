@@ -3,6 +3,7 @@
 #include "control/service.hpp"
 #include "gpu/device_abi.hpp"
 #include "gpu/executor.hpp"
+#include "gpu/trace_writer.hpp"
 #include "gpu/visibility.hpp"
 #include "common/trace.hpp"
 #include "ugdr/api.hpp"
@@ -606,11 +607,13 @@ int GpuEngine::trace_dump(const std::string &path, uint64_t *kept, uint64_t *dro
     int rc = 0;
     std::vector<unsigned int> counts;
     std::vector<TraceRec> recs;
+    uint32_t cap = 0;
     {
         std::lock_guard<std::mutex> lk(mu_);
         if (trace_ == nullptr) {
             rc = EINVAL;
         } else {
+            cap = trace_cap_;
             counts.resize(size_t(cfg_.ctas));
             recs.resize(size_t(cfg_.ctas) * trace_cap_);
             if (copy_from_device(counts.data(), trace_count_, counts.size() * sizeof(unsigned int)) != 0 ||
@@ -624,38 +627,7 @@ int GpuEngine::trace_dump(const std::string &path, uint64_t *kept, uint64_t *dro
     }
     resume();
     if (rc != 0) return rc;
-    static const char *names[] = {"?", "fast_batch", "retire", "chunk", "error"};
-    uint64_t t_min = ~0ull, n_kept = 0, n_drop = 0;
-    for (size_t c = 0; c < counts.size(); ++c) {
-        const uint32_t k = counts[c] < trace_cap_ ? counts[c] : trace_cap_;
-        n_kept += k;
-        n_drop += counts[c] - k;
-        for (uint32_t i = 0; i < k; ++i) t_min = std::min<uint64_t>(t_min, recs[c * trace_cap_ + i].t0);
-    }
-    FILE *f = std::fopen(path.c_str(), "w");
-    if (f == nullptr) return errno != 0 ? errno : EIO;
-    std::fprintf(f, "{\"traceEvents\": [");
-    bool first = true;
-    for (size_t c = 0; c < counts.size(); ++c) {
-        const uint32_t k = counts[c] < trace_cap_ ? counts[c] : trace_cap_;
-        for (uint32_t i = 0; i < k; ++i) {
-            const TraceRec &r = recs[c * trace_cap_ + i];
-            const uint32_t ev = r.event >> 16;
-            std::fprintf(f,
-                         "%s\n{\"name\": \"%s\", \"ph\": \"X\", \"pid\": %u, \"tid\": %u, \"ts\": %.3f, "
-                         "\"dur\": %.3f, \"args\": {\"qp\": %d, \"value\": %u}}",
-                         first ? "" : ",", ev < 5 ? names[ev] : "?", r.cta, r.event & 0xffffu,
-                         double(r.t0 - t_min) / 1000.0, double(r.t1 - r.t0) / 1000.0,
-                         r.qp == 0xffffffffu ? -1 : int(r.qp), r.value);
-            first = false;
-        }
-    }
-    std::fprintf(f, "\n], \"displayTimeUnit\": \"ns\", \"otherData\": {\"gpu\": %d, \"dropped\": %llu}}\n",
-                 cfg_.ordinal, (unsigned long long)n_drop);
-    const bool ok = std::fclose(f) == 0;
-    if (kept) *kept = n_kept;
-    if (dropped) *dropped = n_drop;
-    return ok ? 0 : EIO;
+    return write_chrome_trace(path, recs, counts, cap, cfg_.ordinal, kept, dropped);
 }
 
 // The owner warp keeps each QP's byte and error counts in its device state; RNR waits are not
