@@ -1,0 +1,16 @@
+"""Packaging hook: `pip install .` first runs `make` so that libugdr.so, the daemon and the tools
+exist in ugdr_b200/_lib/, then ships them as package data (metadata lives in pyproject.toml)."""
+import os
+import subprocess
+
+from setuptools import setup
+from setuptools.command.build_py import build_py
+
+
+class BuildWithMake(build_py):
+    def run(self):
+        subprocess.check_call(["make", "-j"], cwd=os.path.dirname(os.path.abspath(__file__)))
+        super().run()
+
+
+setup(cmdclass={"build_py": BuildWithMake})

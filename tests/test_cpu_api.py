@@ -519,3 +519,28 @@ def test_make_install_layout_and_pkg_config(tmp_path):
     finally:
         d.terminate()
         d.wait(timeout=30)
+
+
+def test_pip_install_ships_the_native_build(tmp_path):
+    """`pip install .` (offline, no build isolation) runs make and ships libugdr.so and the daemon
+    as package data: the installed package starts its own daemon and lists the host device from
+    a directory outside the source tree."""
+    import subprocess
+    import sys
+
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    site = tmp_path / "site"
+    r = subprocess.run([sys.executable, "-m", "pip", "install", "--no-index", "--no-build-isolation", "--no-deps",
+                        "--target", str(site), repo], capture_output=True, text=True, timeout=900)
+    if r.returncode != 0 and "No module named pip" in r.stderr:
+        pytest.skip("pip not available")
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    code = ("from ugdr_b200 import verbs as V, _native as N\n"
+            "assert str(N.LIB_DIR).startswith(%r), N.LIB_DIR\n"
+            "with V.Daemon(gpus=0):\n"
+            "    print(sorted(d.name for d in V.get_devices()))\n") % str(site)
+    env = {k: v for k, v in os.environ.items() if not k.startswith("UGDR_")}
+    env["PYTHONPATH"] = str(site)
+    r = subprocess.run([sys.executable, "-c", code], cwd=str(tmp_path), env=env, capture_output=True, text=True,
+                       timeout=120)
+    assert r.returncode == 0 and "ugdr_cpu0" in r.stdout, r.stdout + r.stderr
