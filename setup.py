@@ -13,4 +13,6 @@ class BuildWithMake(build_py):
         super().run()
 
 
-setup(cmdclass={"build_py": BuildWithMake})
+# setuptools' own staging goes under build/py so it stays apart from the make objects (build/obj).
+setup(cmdclass={"build_py": BuildWithMake},
+      options={"build": {"build_base": "build/py"}, "egg_info": {"egg_base": "build/py"}})
