@@ -84,3 +84,94 @@ def test_daemon_survives_malformed_clients(daemon, msgs):
 def test_daemon_still_serves_after_fuzzing(daemon):
     assert daemon.proc.poll() is None
     assert _healthy(daemon)
+
+
+def _fd_count(pid: int) -> int:
+    return len(os.listdir(f"/proc/{pid}/fd"))
+
+
+def test_fds_sent_with_bad_requests_are_not_leaked(daemon):
+    """Descriptors attached (SCM_RIGHTS) to malformed or refused requests are closed by the daemon:
+    its descriptor count returns to where it was after many such requests."""
+    import array
+
+    assert _healthy(daemon)
+    before = _fd_count(daemon.proc.pid)
+    for i in range(200):
+        s = socket.socket(socket.AF_UNIX, socket.SOCK_SEQPACKET)
+        s.settimeout(2.0)
+        fds = [os.memfd_create(f"leak{i}_{k}") for k in range(3)]
+        try:
+            s.connect(daemon.socket_path)
+            kind = i % 4
+            if kind == 0:  # garbage bytes with descriptors
+                msg = os.urandom(40)
+            elif kind == 1:  # valid envelope, unknown method, descriptor count matching
+                msg = envelope(999, 0, i, 0, 0, 3)
+            elif kind == 2:  # register-MR method with a truncated body
+                msg = envelope(6, 0, i, 0, 8, 3) + b"\0" * 8
+            else:  # well-formed register-MR request for a PD that does not exist
+                opaque = struct.pack(">B3xQQQ", 1, 0x10000, 4096, 0)
+                body = struct.pack(">HHQQII", 1, 0, 0x0300000100000001, 4096, 1, len(opaque)) + opaque
+                msg = envelope(6, 0, i, 0, len(body), 3) + body
+            s.sendmsg([msg], [(socket.SOL_SOCKET, socket.SCM_RIGHTS, array.array("i", fds))])
+            try:
+                s.recv(1 << 16)
+            except (socket.timeout, OSError):
+                pass
+        except (ConnectionError, OSError):
+            pass
+        finally:
+            s.close()
+            for fd in fds:
+                os.close(fd)
+    assert daemon.proc.poll() is None
+    assert _healthy(daemon)
+    import time
+
+    deadline = time.time() + 5
+    while _fd_count(daemon.proc.pid) > before + 2 and time.time() < deadline:
+        time.sleep(0.05)
+    assert _fd_count(daemon.proc.pid) <= before + 2, (before, _fd_count(daemon.proc.pid))
+
+
+def test_objects_of_a_vanished_client_release_their_descriptors(daemon):
+    """A client that registers host MRs and creates CQs and QPs (each backed by a memfd the daemon
+    holds) and then exits without destroying anything: session reclaim closes every descriptor."""
+    import sys
+    import time
+
+    assert _healthy(daemon)
+    before = _fd_count(daemon.proc.pid)
+    code = (
+        "import os\n"
+        "from ugdr_b200 import verbs as V, _native as N\n"
+        "ctx = V.Context(V.find_device(kind=0))\n"
+        "pd = ctx.alloc_pd()\n"
+        "cqs = [ctx.create_cq(64) for _ in range(4)]\n"
+        "qps = [pd.create_qp(cqs[i % 4], max_send_wr=16, max_recv_wr=16) for i in range(8)]\n"
+        "bufs = [V.HostBuffer(1 << 16) for _ in range(4)]\n"
+        "mrs = [pd.reg_mr(b.addr, 1 << 16, N.ACCESS_LOCAL_WRITE) for b in bufs]\n"
+        "print('held', flush=True)\n"
+        "input()\n"
+        "os._exit(0)\n")
+    env = dict(os.environ, UGDR_DAEMON_SOCKET=daemon.socket_path,
+               PYTHONPATH=os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    p = subprocess.Popen([sys.executable, "-c", code], env=env, stdin=subprocess.PIPE, stdout=subprocess.PIPE,
+                         stderr=subprocess.PIPE, text=True)
+    try:
+        assert p.stdout.readline().strip() == "held", p.stderr.read()
+        # The daemon now holds the rings and MR regions (4 CQs + 8 x 2 QP rings + 4 MRs).
+        assert _fd_count(daemon.proc.pid) >= before + 20, (before, _fd_count(daemon.proc.pid))
+        p.stdin.write("\n")
+        p.stdin.flush()
+        assert p.wait(timeout=60) == 0
+    finally:
+        if p.poll() is None:
+            p.kill()
+            p.wait()
+    deadline = time.time() + 10
+    while _fd_count(daemon.proc.pid) > before + 2 and time.time() < deadline:
+        time.sleep(0.05)
+    assert _fd_count(daemon.proc.pid) <= before + 2, (before, _fd_count(daemon.proc.pid))
+    assert _healthy(daemon)
