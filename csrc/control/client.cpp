@@ -21,6 +21,9 @@ int ControlClient::call(Request &&req, Response *resp) {
     ipc::Message reply;
     if (int rc = ipc_.call(method, std::move(msg.payload), std::move(msg.fds), &reply); rc != 0)
         return rc;
+    // This process is at its descriptor limit: the reply's rings or regions were lost.  The
+    // connection is still in step; the call fails with EMFILE.
+    if (reply.fds_truncated) return EMFILE;
     if (int rc = decode_response(std::move(reply), resp); rc != 0) {
         ipc_.close();
         return rc;

@@ -83,7 +83,9 @@ ipc::Message ControlPlane::handle(ipc::SessionId session, ipc::Message &&msg) {
     const uint32_t method = msg.env.method;
     Request req;
     Response resp;
-    const int rc = decode_request(std::move(msg), &req);
+    // Descriptors lost on the way in (the daemon is at its descriptor limit): refuse the request
+    // instead of running it without them; the ones that arrived close with `msg`.
+    const int rc = msg.fds_truncated ? EMFILE : decode_request(std::move(msg), &req);
     if (rc != 0) {
         resp.status = rc;
     } else {

@@ -1,6 +1,8 @@
 // ugdr_daemon: serve the ugdr control plane and execute posted work on the host and the GPUs.
 #include "daemon/daemon.hpp"
 
+#include <sys/resource.h>
+
 #include <atomic>
 #include <csignal>
 #include <cstdio>
@@ -21,6 +23,12 @@ void usage(FILE *f) {
 }  // namespace
 
 int main(int argc, char **argv) {
+    // Every CQ holds one ring descriptor, every QP two, every host MR one: lift the soft
+    // descriptor limit to the hard one so thousands of QPs fit.
+    if (rlimit rl{}; ::getrlimit(RLIMIT_NOFILE, &rl) == 0 && rl.rlim_cur < rl.rlim_max) {
+        rl.rlim_cur = rl.rlim_max;
+        ::setrlimit(RLIMIT_NOFILE, &rl);
+    }
     ugdr::daemon::Options opt;
     const char *env = std::getenv("UGDR_DAEMON_SOCKET");
     opt.socket_path = (env != nullptr && env[0] != '\0') ? env : "/run/ugdr/ugdr.sock";

@@ -102,14 +102,18 @@ int recv_message(int sock, Message *m) {
         }
     }
     if (n == 0) return ECONNRESET;
-    if ((mh.msg_flags & (MSG_TRUNC | MSG_CTRUNC)) != 0) return EMSGSIZE;
+    if ((mh.msg_flags & MSG_TRUNC) != 0) return EMSGSIZE;
+    // A lost descriptor leaves the byte stream in step (one datagram per message), so the
+    // message is still delivered, marked, for the receiver to refuse with EMFILE.
+    const bool fds_truncated = (mh.msg_flags & MSG_CTRUNC) != 0;
     if (size_t(n) < kEnvelopeBytes) return EPROTO;
     const Envelope e = decode_envelope(buf.data());
     if (e.magic != kMagic || e.major != kVersionMajor || (e.flags & ~kFlagResponse) != 0 ||
-        e.payload_length != size_t(n) - kEnvelopeBytes || e.fd_count != fds.size() ||
-        e.payload_length > kMaxPayload) {
+        e.payload_length != size_t(n) - kEnvelopeBytes || e.payload_length > kMaxPayload ||
+        (fds_truncated ? e.fd_count <= fds.size() || e.fd_count > kMaxFds : e.fd_count != fds.size())) {
         return EPROTO;
     }
+    m->fds_truncated = fds_truncated;
     m->env = e;
     m->payload.assign(reinterpret_cast<std::byte *>(buf.data() + kEnvelopeBytes),
                       reinterpret_cast<std::byte *>(buf.data() + n));

@@ -42,6 +42,9 @@ struct Message {
     Envelope env;
     std::vector<std::byte> payload;
     std::vector<Fd> fds;
+    // The payload arrived whole but the kernel could not install every attached descriptor
+    // (the receiver is at its descriptor limit).  `fds` holds the ones that did arrive.
+    bool fds_truncated = false;
 };
 
 void encode_envelope(const Envelope &e, uint8_t out[kEnvelopeBytes]);

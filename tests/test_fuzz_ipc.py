@@ -175,3 +175,46 @@ def test_objects_of_a_vanished_client_release_their_descriptors(daemon):
         time.sleep(0.05)
     assert _fd_count(daemon.proc.pid) <= before + 2, (before, _fd_count(daemon.proc.pid))
     assert _healthy(daemon)
+
+
+def test_descriptor_exhaustion_refuses_the_request_and_keeps_the_session(tmp_path):
+    """At its descriptor limit the daemon answers EMFILE to a registration whose region
+    descriptor it could not receive; the client's session survives, and once MRs are freed
+    registration works again."""
+    import errno
+    import resource
+
+    d = V.Daemon(gpus=0, socket_path=str(tmp_path / "d.sock"))
+    try:
+        env_sock = os.environ.get("UGDR_DAEMON_SOCKET")
+        os.environ["UGDR_DAEMON_SOCKET"] = d.socket_path
+        ctx = V.Context(V.find_device(kind=0))
+        pd = ctx.alloc_pd()
+        buf = V.HostBuffer(1 << 16)
+        have = _fd_count(d.proc.pid)
+        resource.prlimit(d.proc.pid, resource.RLIMIT_NOFILE, (have + 40, have + 40))
+        mrs, err = [], None
+        for _ in range(200):
+            try:
+                mrs.append(pd.reg_mr(buf.addr, 4096, N.ACCESS_LOCAL_WRITE))
+            except V.UgdrError as e:
+                err = e
+                break
+        assert err is not None and err.errno == errno.EMFILE, err
+        assert 20 <= len(mrs) <= 40
+        for m in mrs[:8]:
+            m.dereg()
+        again = pd.reg_mr(buf.addr, 4096, N.ACCESS_LOCAL_WRITE)  # same session, still connected
+        again.dereg()
+        for m in mrs[8:]:
+            m.dereg()
+        pd.dealloc()
+        ctx.close()
+        buf.free()
+        assert d.proc.poll() is None
+    finally:
+        if env_sock is None:
+            os.environ.pop("UGDR_DAEMON_SOCKET", None)
+        else:
+            os.environ["UGDR_DAEMON_SOCKET"] = env_sock
+        d.stop()
