@@ -3,6 +3,7 @@
 #include "common/bytes.hpp"
 
 #include <poll.h>
+#include <fcntl.h>
 #include <sys/socket.h>
 #include <sys/stat.h>
 #include <sys/un.h>
@@ -202,6 +203,7 @@ int Server::start(const std::string &path) {
         sock_ino_ = st.st_ino;
     }
     listener_ = std::move(s);
+    reserve_ = Fd(::open("/dev/null", O_RDONLY | O_CLOEXEC));
     path_ = path;
     return 0;
 }
@@ -249,6 +251,13 @@ int Server::poll_once(int timeout_ms) {
     if ((pfds[0].revents & POLLIN) != 0) {
         for (;;) {
             int c = ::accept4(listener_.get(), nullptr, nullptr, SOCK_CLOEXEC);
+            if (c < 0 && (errno == EMFILE || errno == ENFILE) && reserve_.valid()) {
+                reserve_ = Fd();  // frees one descriptor
+                const int refused = ::accept4(listener_.get(), nullptr, nullptr, SOCK_CLOEXEC);
+                if (refused >= 0) ::close(refused);
+                reserve_ = Fd(::open("/dev/null", O_RDONLY | O_CLOEXEC));
+                if (refused >= 0) continue;
+            }
             if (c < 0) break;
             sessions_.emplace(c, Session{Fd(c), next_session_++});
         }

@@ -102,6 +102,9 @@ class Server {
 
     Handler &handler_;
     Fd listener_;
+    // A descriptor held back so that, at the descriptor limit, a pending connection can still be
+    // accepted and closed (the client sees the refusal) instead of keeping the listener readable.
+    Fd reserve_;
     std::string path_;
     uint64_t sock_dev_ = 0, sock_ino_ = 0;
     struct Session {

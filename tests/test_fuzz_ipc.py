@@ -202,6 +202,12 @@ def test_descriptor_exhaustion_refuses_the_request_and_keeps_the_session(tmp_pat
                 break
         assert err is not None and err.errno == errno.EMFILE, err
         assert 20 <= len(mrs) <= 40
+        # A new connection at the limit is accepted on a reserved descriptor and closed at once.
+        s = socket.socket(socket.AF_UNIX, socket.SOCK_SEQPACKET)
+        s.settimeout(5.0)
+        s.connect(d.socket_path)
+        assert s.recv(64) == b""
+        s.close()
         for m in mrs[:8]:
             m.dereg()
         again = pd.reg_mr(buf.addr, 4096, N.ACCESS_LOCAL_WRITE)  # same session, still connected
