@@ -1,5 +1,7 @@
 #include "control/client.hpp"
 
+#include "common/bytes.hpp"
+
 #include <cerrno>
 
 namespace ugdr::control {
@@ -21,9 +23,26 @@ int ControlClient::call(Request &&req, Response *resp) {
     ipc::Message reply;
     if (int rc = ipc_.call(method, std::move(msg.payload), std::move(msg.fds), &reply); rc != 0)
         return rc;
-    // This process is at its descriptor limit: the reply's rings or regions were lost.  The
-    // connection is still in step; the call fails with EMFILE.
-    if (reply.fds_truncated) return EMFILE;
+    // This process is at its descriptor limit: the reply's rings were lost.  The connection is
+    // still in step; the call fails with EMFILE, and an object the daemon created for it (a CQ
+    // or QP whose rings never arrived) is destroyed again rather than left to the session's end.
+    if (reply.fds_truncated) {
+        const uint32_t destroy = method == kCreateCq   ? uint32_t(kDestroyCq)
+                                 : method == kCreateQp ? uint32_t(kDestroyQp)
+                                                       : 0u;
+        ByteReader rd(reply.payload);
+        uint16_t version = 0, reserved = 0;
+        uint64_t identity = 0;
+        if (destroy != 0 && reply.env.status == 0 && rd.be(&version) && rd.be(&reserved) && rd.be(&identity) &&
+            identity != 0) {
+            Request undo;
+            undo.method = destroy;
+            undo.identity = identity;
+            Response ignored;
+            (void)call(std::move(undo), &ignored);
+        }
+        return EMFILE;
+    }
     if (int rc = decode_response(std::move(reply), resp); rc != 0) {
         ipc_.close();
         return rc;

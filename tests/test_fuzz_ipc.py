@@ -224,3 +224,49 @@ def test_descriptor_exhaustion_refuses_the_request_and_keeps_the_session(tmp_pat
         else:
             os.environ["UGDR_DAEMON_SOCKET"] = env_sock
         d.stop()
+
+
+def test_client_at_its_descriptor_limit_gets_emfile_and_leaves_no_orphan(daemon):
+    """A client at its own descriptor limit cannot receive a new CQ's ring: ugdr_create_cq fails
+    with EMFILE, the library destroys the CQ the daemon made for it, and the connection stays
+    usable."""
+    import sys
+    import time
+
+    code = (
+        "import os, resource\n"
+        "from ugdr_b200 import verbs as V\n"
+        "ctx = V.Context(V.find_device(kind=0))\n"
+        "n = len(os.listdir('/proc/self/fd'))\n"
+        "resource.setrlimit(resource.RLIMIT_NOFILE, (n + 6, resource.getrlimit(resource.RLIMIT_NOFILE)[1]))\n"
+        "cqs, err = [], None\n"
+        "while err is None and len(cqs) < 50:\n"
+        "    try:\n"
+        "        cqs.append(ctx.create_cq(16))\n"
+        "    except V.UgdrError as e:\n"
+        "        err = e.errno\n"
+        "print(len(cqs), err, flush=True)\n"
+        "input()\n"
+        "cqs[0].destroy()\n"
+        "print('ok', ctx.create_cq(16) is not None, flush=True)\n"
+        "os._exit(0)\n")
+    env = dict(os.environ, UGDR_DAEMON_SOCKET=daemon.socket_path,
+               PYTHONPATH=os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    before = _fd_count(daemon.proc.pid)
+    p = subprocess.Popen([sys.executable, "-c", code], env=env, stdin=subprocess.PIPE, stdout=subprocess.PIPE,
+                         stderr=subprocess.PIPE, text=True)
+    try:
+        made, err = p.stdout.readline().split()
+        assert err == str(__import__("errno").EMFILE) and 1 <= int(made) < 50
+        time.sleep(0.1)
+        # The daemon holds the client's session socket and one ring descriptor per CQ the client
+        # kept, none for the refused one.
+        assert _fd_count(daemon.proc.pid) == before + 1 + int(made), (before, made, _fd_count(daemon.proc.pid))
+        p.stdin.write("\n")
+        p.stdin.flush()
+        assert p.stdout.readline().strip() == "ok True"
+        assert p.wait(timeout=60) == 0
+    finally:
+        if p.poll() is None:
+            p.kill()
+            p.wait()
