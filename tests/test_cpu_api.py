@@ -544,3 +544,39 @@ def test_pip_install_ships_the_native_build(tmp_path):
     r = subprocess.run([sys.executable, "-c", code], cwd=str(tmp_path), env=env, capture_output=True, text=True,
                        timeout=120)
     assert r.returncode == 0 and "ugdr_cpu0" in r.stdout, r.stdout + r.stderr
+
+
+def test_object_churn_holds_memory_and_descriptors_flat(cpu_daemon):
+    """Thousands of create / connect / post / destroy cycles (CQ, two QPs, an MR): the daemon's
+    resident memory and descriptor count and this client's resident memory stay flat once warm
+    (destroyed proxies sit in a bounded quarantine; the daemon frees every object)."""
+    def rss_kb(pid: int) -> int:
+        with open(f"/proc/{pid}/status") as f:
+            return next(int(ln.split()[1]) for ln in f if ln.startswith("VmRSS"))
+
+    ctx = V.Context(V.find_device(kind=0))
+    pd = ctx.alloc_pd()
+    buf = V.HostBuffer(1 << 16)
+    dpid = cpu_daemon.proc.pid
+    try:
+        marks = {}
+        for it in range(3000):
+            cq = ctx.create_cq(64)
+            a = pd.create_qp(cq, max_send_wr=16, max_recv_wr=16)
+            b = pd.create_qp(cq, max_send_wr=16, max_recv_wr=16)
+            V.connect_pair(a, b, access=N.ACCESS_REMOTE_WRITE)
+            mr = pd.reg_mr(buf.addr, 4096, N.ACCESS_LOCAL_WRITE | N.ACCESS_REMOTE_WRITE)
+            a.post_write((buf.addr, 8, mr.lkey), buf.addr + 64, mr.rkey, wr_id=it)
+            assert cq.wait(1, 10)[0].status == N.WC_SUCCESS
+            a.destroy()
+            b.destroy()
+            mr.dereg()
+            cq.destroy()
+            if it in (1000, 2999):
+                marks[it] = (rss_kb(dpid), len(os.listdir(f"/proc/{dpid}/fd")), rss_kb(os.getpid()))
+        (d0, f0, c0), (d1, f1, c1) = marks[1000], marks[2999]
+        assert f1 <= f0 and d1 - d0 < 2048 and c1 - c0 < 4096, marks
+    finally:
+        pd.dealloc()
+        ctx.close()
+        buf.free()
