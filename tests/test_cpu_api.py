@@ -580,3 +580,13 @@ def test_object_churn_holds_memory_and_descriptors_flat(cpu_daemon):
         pd.dealloc()
         ctx.close()
         buf.free()
+
+
+def test_examples_byte_compile():
+    """Every Python example at least compiles (the GPU ones run on a B200 box)."""
+    import py_compile
+
+    root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "examples")
+    for name in sorted(os.listdir(root)):
+        if name.endswith(".py"):
+            py_compile.compile(os.path.join(root, name), doraise=True)
