@@ -11,6 +11,8 @@
 
 #include <cerrno>
 #include <cstring>
+#include <memory>
+#include <new>
 #include <vector>
 
 namespace ugdr::ipc {
@@ -79,8 +81,15 @@ int send_message(int sock, const Message &m) {
 
 int recv_message(int sock, Message *m) {
     if (sock < 0 || m == nullptr) return EINVAL;
-    std::vector<uint8_t> buf(kEnvelopeBytes + kMaxPayload + 1);
-    iovec iov{buf.data(), buf.size()};
+    // One receive buffer per thread, large enough for any datagram plus one byte (to detect an
+    // oversized one), reused and never cleared: a fresh zero-filled MiB per message cost more
+    // than the round trip itself.
+    constexpr size_t kBufBytes = kEnvelopeBytes + kMaxPayload + 1;
+    thread_local std::unique_ptr<uint8_t[]> tls_buf;
+    if (!tls_buf) tls_buf.reset(new (std::nothrow) uint8_t[kBufBytes]);
+    if (!tls_buf) return ENOMEM;
+    uint8_t *const buf = tls_buf.get();
+    iovec iov{buf, kBufBytes};
     msghdr mh{};
     mh.msg_iov = &iov;
     mh.msg_iovlen = 1;
@@ -108,7 +117,7 @@ int recv_message(int sock, Message *m) {
     // message is still delivered, marked, for the receiver to refuse with EMFILE.
     const bool fds_truncated = (mh.msg_flags & MSG_CTRUNC) != 0;
     if (size_t(n) < kEnvelopeBytes) return EPROTO;
-    const Envelope e = decode_envelope(buf.data());
+    const Envelope e = decode_envelope(buf);
     if (e.magic != kMagic || e.major != kVersionMajor || (e.flags & ~kFlagResponse) != 0 ||
         e.payload_length != size_t(n) - kEnvelopeBytes || e.payload_length > kMaxPayload ||
         (fds_truncated ? e.fd_count <= fds.size() || e.fd_count > kMaxFds : e.fd_count != fds.size())) {
@@ -116,8 +125,7 @@ int recv_message(int sock, Message *m) {
     }
     m->fds_truncated = fds_truncated;
     m->env = e;
-    m->payload.assign(reinterpret_cast<std::byte *>(buf.data() + kEnvelopeBytes),
-                      reinterpret_cast<std::byte *>(buf.data() + n));
+    m->payload.assign(reinterpret_cast<std::byte *>(buf + kEnvelopeBytes), reinterpret_cast<std::byte *>(buf + n));
     m->fds = std::move(fds);
     return 0;
 }
