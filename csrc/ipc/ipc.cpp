@@ -10,9 +10,9 @@
 #include <unistd.h>
 
 #include <cerrno>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
-#include <new>
 #include <vector>
 
 namespace ugdr::ipc {
@@ -85,8 +85,11 @@ int recv_message(int sock, Message *m) {
     // oversized one), reused and never cleared: a fresh zero-filled MiB per message cost more
     // than the round trip itself.
     constexpr size_t kBufBytes = kEnvelopeBytes + kMaxPayload + 1;
-    thread_local std::unique_ptr<uint8_t[]> tls_buf;
-    if (!tls_buf) tls_buf.reset(new (std::nothrow) uint8_t[kBufBytes]);
+    struct FreeBuf {
+        void operator()(uint8_t *p) const noexcept { std::free(p); }
+    };
+    thread_local std::unique_ptr<uint8_t, FreeBuf> tls_buf;
+    if (!tls_buf) tls_buf.reset(static_cast<uint8_t *>(std::malloc(kBufBytes)));
     if (!tls_buf) return ENOMEM;
     uint8_t *const buf = tls_buf.get();
     iovec iov{buf, kBufBytes};

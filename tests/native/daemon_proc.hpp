@@ -3,6 +3,7 @@
 #pragma once
 
 #include <signal.h>
+#include <sys/prctl.h>
 #include <sys/socket.h>
 #include <sys/stat.h>
 #include <sys/un.h>
@@ -52,6 +53,7 @@ struct DaemonProc {
         sock = dir + "/ugdr.sock";
         pid = ::fork();
         if (pid == 0) {
+            ::prctl(PR_SET_PDEATHSIG, SIGTERM);  // never outlive a test binary that aborted
             ::execl(bin.c_str(), bin.c_str(), "--socket", sock.c_str(), "--gpus", "0", static_cast<char *>(nullptr));
             ::_exit(127);
         }

@@ -575,7 +575,12 @@ def test_object_churn_holds_memory_and_descriptors_flat(cpu_daemon):
             if it in (1000, 2999):
                 marks[it] = (rss_kb(dpid), len(os.listdir(f"/proc/{dpid}/fd")), rss_kb(os.getpid()))
         (d0, f0, c0), (d1, f1, c1) = marks[1000], marks[2999]
-        assert f1 <= f0 and d1 - d0 < 2048 and c1 - c0 < 4096, marks
+        assert f1 <= f0 and c1 - c0 < 4096, marks
+        # An instrumented daemon (the sanitizer suite sets UGDR_DAEMON_BIN) keeps freed blocks in
+        # its allocator's quarantine, so its resident size grows by design; LeakSanitizer checks
+        # that daemon instead.
+        if not os.environ.get("UGDR_DAEMON_BIN"):
+            assert d1 - d0 < 2048, marks
     finally:
         pd.dealloc()
         ctx.close()
