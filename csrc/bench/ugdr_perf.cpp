@@ -7,6 +7,7 @@
 //   ugdr_perf ring     --batch B --wrs N                                    shared SPSC ring alone (2 threads)
 //   ugdr_perf postcore --batch B --wrs N                                    WR encode + publish path alone
 //   ugdr_perf plumbing --wrs 10000                                          CPU-only plumbing (host engine)
+//   ugdr_perf control  --src-gpu A|-1 --iters N                             control-plane op latencies
 //   ugdr_perf stress   --src-gpu A --dst-gpu B --qps 64 --depth 128 --sges 16 --rounds R
 //                      verbs-feature stress: per QP an interleave of
 //                      16-SGE WRITE and WRITE_WITH_IMM (SGE sizes log-uniform in 64 B..64 KiB,
@@ -579,6 +580,94 @@ int run_postcore(const Opts &o) {
     return 0;
 }
 
+// ---- control-plane operation costs ------------------------------------------------------------
+
+// Round trips of the object life cycle through the public API on one device (`--src-gpu`, -1 for
+// the host-memory device): CQ create / destroy, QP create / destroy, RESET->INIT->RTS (modify +
+// connect of a pair), MR register / deregister of a 64 KiB range, query_qp.  Each is timed
+// per call over `iters` repetitions after a warm-up; p50 / p99 in microseconds.
+int run_control(const Opts &o) {
+    int n = 0;
+    ugdr_device **list = ugdr_get_device_list(&n);
+    if (!list) die("ugdr_get_device_list", errno);
+    ugdr_context *ctx = ugdr_open_device(any_device(list, n, o.src_gpu));
+    ugdr_pd *pd = ugdr_alloc_pd(ctx);
+    ugdr_cq *cq = ugdr_create_cq(ctx, 256, nullptr, nullptr, 0);
+    const size_t bytes = 1 << 16;
+    void *buf = nullptr;
+    if (o.src_gpu < 0) {
+        buf = ugdr_x_alloc_host(bytes);
+    } else if (cudaSetDevice(o.src_gpu) != cudaSuccess || cudaMalloc(&buf, bytes) != cudaSuccess) {
+        buf = nullptr;
+    }
+    if (!ctx || !pd || !cq || !buf) die("control setup", errno);
+    const uint64_t iters = o.iters > 0 ? o.iters : 2000;
+    using Op = std::pair<const char *, std::vector<double>>;
+    std::vector<Op> ops = {{"cq_create", {}}, {"cq_destroy", {}}, {"qp_create", {}}, {"qp_destroy", {}},
+                           {"qp_connect_pair", {}}, {"mr_register", {}}, {"mr_deregister", {}}, {"query_qp", {}}};
+    auto timed = [](std::vector<double> &v, auto &&fn) {
+        const auto t0 = Clock::now();
+        fn();
+        v.push_back(std::chrono::duration<double, std::micro>(Clock::now() - t0).count());
+    };
+    const uint64_t warm = iters / 10 + 10;
+    for (uint64_t i = 0; i < warm + iters; ++i) {
+        const bool keep = i >= warm;
+        std::vector<double> sink;
+        auto sel = [&](size_t k) -> std::vector<double> & { return keep ? ops[k].second : sink; };
+        ugdr_cq *c = nullptr;
+        timed(sel(0), [&] { c = ugdr_create_cq(ctx, 256, nullptr, nullptr, 0); });
+        if (!c) die("ugdr_create_cq", errno);
+        timed(sel(1), [&] { ugdr_destroy_cq(c); });
+        ugdr_qp_init_attr ia{cq, cq, 128, 128, 1, 1, UGDR_QPT_RC, 0};
+        ugdr_qp *a = nullptr, *b = nullptr;
+        timed(sel(2), [&] { a = ugdr_create_qp(pd, &ia); });
+        b = ugdr_create_qp(pd, &ia);
+        if (!a || !b) die("ugdr_create_qp", errno);
+        timed(sel(4), [&] {
+            ugdr_qp_attr at{};
+            at.qp_state = UGDR_QPS_INIT;
+            at.qp_access_flags = UGDR_ACCESS_REMOTE_WRITE;
+            ugdr_modify_qp(a, &at, UGDR_QP_STATE | UGDR_QP_ACCESS_FLAGS);
+            ugdr_modify_qp(b, &at, UGDR_QP_STATE | UGDR_QP_ACCESS_FLAGS);
+            ugdr_qp_conn_info ca{}, cb{};
+            ugdr_query_qp_conn_info(a, &ca);
+            ugdr_query_qp_conn_info(b, &cb);
+            ugdr_qp_attr c2{};
+            c2.timeout = 14;
+            c2.retry_cnt = 7;
+            c2.rnr_retry = 7;
+            c2.min_rnr_timer = 1;
+            const int cm = UGDR_QP_TIMEOUT | UGDR_QP_RETRY_CNT | UGDR_QP_RNR_RETRY | UGDR_QP_MIN_RNR_TIMER;
+            if (ugdr_connect_qp(a, &cb, &c2, cm) != 0 || ugdr_connect_qp(b, &ca, &c2, cm) != 0) die("connect", EINVAL);
+        });
+        timed(sel(7), [&] {
+            ugdr_qp_attr qa{};
+            ugdr_qp_init_attr qi{};
+            ugdr_query_qp(a, &qa, UGDR_QP_STATE, &qi);
+        });
+        timed(sel(3), [&] { ugdr_destroy_qp(a); });
+        ugdr_destroy_qp(b);
+        ugdr_mr *m = nullptr;
+        timed(sel(5), [&] { m = ugdr_reg_mr(pd, buf, bytes, UGDR_ACCESS_LOCAL_WRITE | UGDR_ACCESS_REMOTE_WRITE); });
+        if (!m) die("ugdr_reg_mr", errno);
+        timed(sel(6), [&] { ugdr_dereg_mr(m); });
+    }
+    std::printf("{\"benchmark\": \"ugdr_control\", \"device\": %d, \"iters\": %llu", o.src_gpu,
+                (unsigned long long)iters);
+    for (auto &op : ops) {
+        std::sort(op.second.begin(), op.second.end());
+        const double p50 = op.second[op.second.size() / 2], p99 = op.second[op.second.size() * 99 / 100];
+        std::printf(", \"%s_p50_us\": %.2f, \"%s_p99_us\": %.2f", op.first, p50, op.first, p99);
+    }
+    std::printf("}\n");
+    ugdr_destroy_cq(cq);
+    ugdr_dealloc_pd(pd);
+    ugdr_close_device(ctx);
+    ugdr_free_device_list(list);
+    return 0;
+}
+
 // ---- CPU-only plumbing workload -------------------------------------------------------
 
 // One client and the daemon's host-memory engine: 1 PD, two 1 MiB host MRs, one QP of depth
@@ -933,6 +1022,7 @@ int main(int argc, char **argv) {
     if (o.mode == "posting") return run_posting(o);
     if (o.mode == "stress") return run_stress(o);
     if (o.mode == "plumbing") return run_plumbing(o);
+    if (o.mode == "control") return run_control(o);
     if (o.mode == "ring") return run_ring(o);
     if (o.mode == "postcore") return run_postcore(o);
     std::fprintf(stderr, "ugdr_perf: unknown mode %s\n", o.mode.c_str());

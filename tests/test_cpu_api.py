@@ -595,3 +595,15 @@ def test_examples_byte_compile():
     for name in sorted(os.listdir(root)):
         if name.endswith(".py"):
             py_compile.compile(os.path.join(root, name), doraise=True)
+
+
+def test_control_plane_latency_benchmark():
+    """ugdr_perf control on the host device: every life-cycle operation is timed and reported."""
+    from ugdr_b200.utils import perf
+
+    rows = [r for r in perf.run(["control", "--src-gpu", "-1", "--iters", "50"], gpus=0)
+            if r.get("benchmark") == "ugdr_control"]
+    assert len(rows) == 1
+    for op in ("cq_create", "cq_destroy", "qp_create", "qp_destroy", "qp_connect_pair", "mr_register",
+               "mr_deregister", "query_qp"):
+        assert 0 < rows[0][f"{op}_p50_us"] <= rows[0][f"{op}_p99_us"], op
