@@ -6,6 +6,7 @@
 #include "gpu/gpu_engine.hpp"
 #include "ipc/ipc.hpp"
 
+#include <chrono>
 #include <cerrno>
 #include <cstdio>
 
@@ -68,9 +69,16 @@ int Daemon::start() {
 
 int Daemon::poll_once(int timeout_ms) { return server_ ? server_->poll_once(timeout_ms) : EBADF; }
 
+// Clients send control requests in bursts (create, modify, connect, ...): for 200 us after a
+// request the loop polls without sleeping, so the next request is not delayed by a wake-up.
 int Daemon::run(const std::atomic<bool> &stop) {
     while (!stop.load()) {
-        if (int rc = server_->poll_once(50); rc != 0) return rc;
+        const uint64_t now = uint64_t(std::chrono::duration_cast<std::chrono::nanoseconds>(
+                                          std::chrono::steady_clock::now().time_since_epoch())
+                                          .count());
+        const uint64_t last = server_->last_served_ns();
+        const int timeout_ms = last != 0 && now - last < 200000 ? 0 : 50;
+        if (int rc = server_->poll_once(timeout_ms); rc != 0) return rc;
     }
     return 0;
 }

@@ -54,7 +54,8 @@ Envelope decode_envelope(const uint8_t in[kEnvelopeBytes]);
 int send_message(int sock, const Message &m);
 // Receive one message.  Returns 0, ECONNRESET on orderly EOF, or a positive errno (EPROTO for a
 // malformed envelope, EMSGSIZE for truncation).
-int recv_message(int sock, Message *m);
+// `nonblocking`: return EAGAIN at once when no message is waiting.
+int recv_message(int sock, Message *m, bool nonblocking = false);
 
 class Client {
   public:
@@ -94,6 +95,8 @@ class Server {
     int poll_once(int timeout_ms);
     void close() noexcept;
     size_t session_count() const { return sessions_.size(); }
+    // Steady-clock nanoseconds of the last request served (0 before the first).
+    uint64_t last_served_ns() const { return last_served_ns_; }
     bool running() const { return listener_.valid(); }
     const std::string &path() const { return path_; }
 
@@ -113,6 +116,7 @@ class Server {
     };
     std::unordered_map<int, Session> sessions_;
     SessionId next_session_ = 1;
+    uint64_t last_served_ns_ = 0;
 };
 
 }  // namespace ugdr::ipc
