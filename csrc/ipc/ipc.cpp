@@ -251,6 +251,7 @@ int Server::poll_once(int timeout_ms) {
         if ((pfds[i].revents & POLLIN) != 0) {
             Message req;
             const int rc = recv_message(fd, &req);
+            if (rc == EAGAIN || rc == EWOULDBLOCK) continue;  // nothing after all (sockets are non-blocking)
             if (rc != 0 || (req.env.flags & kFlagResponse) != 0) {
                 drop(fd);
                 continue;
@@ -263,6 +264,8 @@ int Server::poll_once(int timeout_ms) {
             resp.env.method = method;
             resp.env.request_id = request_id;
             resp.env.flags = kFlagResponse;
+            // Session sockets are non-blocking: a client whose unread replies fill its socket
+            // buffer (EAGAIN) is dropped rather than allowed to stall every other client.
             if (send_message(fd, resp) != 0) drop(fd);
             last_served_ns_ = uint64_t(std::chrono::duration_cast<std::chrono::nanoseconds>(
                                            std::chrono::steady_clock::now().time_since_epoch())
@@ -273,7 +276,7 @@ int Server::poll_once(int timeout_ms) {
     }
     if ((pfds[0].revents & POLLIN) != 0) {
         for (;;) {
-            int c = ::accept4(listener_.get(), nullptr, nullptr, SOCK_CLOEXEC);
+            int c = ::accept4(listener_.get(), nullptr, nullptr, SOCK_CLOEXEC | SOCK_NONBLOCK);
             if (c < 0 && (errno == EMFILE || errno == ENFILE) && reserve_.valid()) {
                 reserve_ = Fd();  // frees one descriptor
                 const int refused = ::accept4(listener_.get(), nullptr, nullptr, SOCK_CLOEXEC);

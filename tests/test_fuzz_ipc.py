@@ -270,3 +270,37 @@ def test_client_at_its_descriptor_limit_gets_emfile_and_leaves_no_orphan(daemon)
         if p.poll() is None:
             p.kill()
             p.wait()
+
+
+def test_a_client_that_never_reads_replies_cannot_stall_the_daemon(tmp_path):
+    """A client that floods requests and never reads the replies fills its socket's buffer; the
+    daemon drops that session instead of blocking on it, and keeps serving everyone else."""
+    import threading
+
+    d = V.Daemon(gpus=0, socket_path=str(tmp_path / "d.sock"))
+    try:
+        flood = socket.socket(socket.AF_UNIX, socket.SOCK_SEQPACKET)
+        flood.connect(d.socket_path)
+        flood.settimeout(0.5)
+        body = struct.pack(">HHQQII", 1, 0, 0, 0, 0, 0)
+        sent = 0
+        try:
+            for i in range(200000):  # list-devices requests; their replies pile up unread
+                flood.send(envelope(1, 0, i, 0, len(body), 0) + body)
+                sent += 1
+        except (socket.timeout, BlockingIOError, ConnectionError, OSError):
+            pass
+        assert sent > 100
+        ok = threading.Event()
+
+        def probe():
+            ok.set() if _healthy(d) else None
+
+        t = threading.Thread(target=probe)
+        t.start()
+        t.join(timeout=20)
+        assert ok.is_set(), "daemon stopped serving other clients"
+        flood.close()
+        assert d.proc.poll() is None
+    finally:
+        d.stop()
