@@ -6,6 +6,7 @@
 #include <fcntl.h>
 #include <sys/socket.h>
 #include <sys/stat.h>
+#include <sys/time.h>
 #include <sys/un.h>
 #include <unistd.h>
 
@@ -155,6 +156,19 @@ int Client::connect(const std::string &path) {
         if (::connect(s.get(), reinterpret_cast<sockaddr *>(&addr), sizeof(addr)) == 0) break;
         if (errno != EINTR) return errno;
     }
+    // A daemon that stops answering must not hang its clients: every reply has a deadline
+    // (UGDR_RPC_TIMEOUT_MS, default 120 s, 0 = wait forever), after which the call fails with
+    // ETIMEDOUT and the connection is closed.  The longest legitimate request (quiescing a GPU's
+    // executor around a destroy) is bounded well below the default.
+    uint64_t ms = 120000;
+    if (const char *e = std::getenv("UGDR_RPC_TIMEOUT_MS"); e != nullptr && e[0] != '\0')
+        ms = std::strtoull(e, nullptr, 10);
+    if (ms > 0) {
+        timeval tv{};
+        tv.tv_sec = time_t(ms / 1000);
+        tv.tv_usec = suseconds_t((ms % 1000) * 1000);
+        ::setsockopt(s.get(), SOL_SOCKET, SO_RCVTIMEO, &tv, sizeof(tv));
+    }
     sock_ = std::move(s);
     return 0;
 }
@@ -181,6 +195,7 @@ int Client::call(uint32_t method, std::vector<std::byte> payload, std::vector<Fd
         rc = recv_message(sock_.get(), &r, true);
     } while (rc == EAGAIN && std::chrono::steady_clock::now() < spin_until);
     if (rc == EAGAIN || rc == EWOULDBLOCK) rc = recv_message(sock_.get(), &r);
+    if (rc == EAGAIN || rc == EWOULDBLOCK) rc = ETIMEDOUT;  // SO_RCVTIMEO ran out
     if (rc != 0) {
         close();
         return rc;

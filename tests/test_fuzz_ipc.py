@@ -304,3 +304,23 @@ def test_a_client_that_never_reads_replies_cannot_stall_the_daemon(tmp_path):
         assert d.proc.poll() is None
     finally:
         d.stop()
+
+
+def test_a_daemon_that_never_answers_times_out_the_call(tmp_path):
+    """A listener that accepts and never replies: with UGDR_RPC_TIMEOUT_MS set, the client's first
+    call (ugdr_client lists the devices) fails quickly instead of hanging."""
+    import sys
+    import time
+
+    path = str(tmp_path / "mute.sock")
+    srv = socket.socket(socket.AF_UNIX, socket.SOCK_SEQPACKET)
+    srv.bind(path)
+    srv.listen(4)
+    try:
+        env = {k: v for k, v in os.environ.items() if not k.startswith("UGDR_")}
+        env.update(UGDR_DAEMON_SOCKET=path, UGDR_RPC_TIMEOUT_MS="300")
+        t0 = time.time()
+        r = subprocess.run([str(N.LIB_DIR / "ugdr_client")], env=env, capture_output=True, text=True, timeout=30)
+        assert r.returncode != 0 and time.time() - t0 < 10, (r.stdout, r.stderr)
+    finally:
+        srv.close()
