@@ -99,7 +99,7 @@ class Runtime {
     }
 
     // One control round trip.  Returns 0 / positive errno (transport or service status).
-    int call(Request &&req, Response *resp) {
+    int call(Request &&req, Response *resp, uint64_t min_wait_ms = 0) {
         std::lock_guard<std::mutex> lk(mu_);
         const char *env = std::getenv("UGDR_DAEMON_SOCKET");
         const std::string path = (env != nullptr && env[0] != '\0') ? env : kDefaultSocket;
@@ -109,7 +109,7 @@ class Runtime {
             if (int rc = client_.connect(path); rc != 0) return rc;
             path_ = path;
         }
-        if (int rc = client_.call(std::move(req), resp); rc != 0) return rc;
+        if (int rc = client_.call(std::move(req), resp, min_wait_ms); rc != 0) return rc;
         return resp->status;
     }
     uint64_t epoch() {
@@ -641,7 +641,8 @@ int ugdr_x_timed_drain(ugdr_context **contexts, int n, const uint64_t *expected,
         w.be(contexts[i]->identity).be(expected[i]);
     }
     Response resp;
-    const int rc = rt().call(std::move(req), &resp);
+    // The daemon answers at the latest `timeout_ms` after it starts the drain.
+    const int rc = rt().call(std::move(req), &resp, uint64_t(timeout_ms) + 30000);
     ByteReader rd(resp.opaque);
     for (int i = 0; i < n; ++i) {
         uint32_t bits = 0;

@@ -15,13 +15,13 @@ int ControlClient::connect(const std::string &path) {
 
 void ControlClient::close() { ipc_.close(); }
 
-int ControlClient::call(Request &&req, Response *resp) {
+int ControlClient::call(Request &&req, Response *resp, uint64_t min_wait_ms) {
     if (!ipc_.connected()) return ENOTCONN;
     ipc::Message msg;
     const uint32_t method = req.method;
     if (int rc = encode_request(std::move(req), &msg); rc != 0) return rc;
     ipc::Message reply;
-    if (int rc = ipc_.call(method, std::move(msg.payload), std::move(msg.fds), &reply); rc != 0)
+    if (int rc = ipc_.call(method, std::move(msg.payload), std::move(msg.fds), &reply, min_wait_ms); rc != 0)
         return rc;
     // This process is at its descriptor limit: the reply's rings were lost.  The connection is
     // still in step; the call fails with EMFILE, and an object the daemon created for it (a CQ

@@ -20,7 +20,7 @@ class ControlClient {
     uint64_t epoch() const { return epoch_; }
     // Transport failures close the channel (the epoch then changes on reconnect) and come back
     // as a positive errno; service failures come back in resp->status.
-    int call(Request &&req, Response *resp);
+    int call(Request &&req, Response *resp, uint64_t min_wait_ms = 0);
 
   private:
     ipc::Client ipc_;

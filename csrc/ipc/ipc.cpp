@@ -147,6 +147,17 @@ int make_address(const std::string &path, sockaddr_un *addr) {
 
 }  // namespace
 
+namespace {
+
+void set_recv_timeout(int sock, uint64_t ms) {
+    timeval tv{};  // zero: no deadline
+    tv.tv_sec = time_t(ms / 1000);
+    tv.tv_usec = suseconds_t((ms % 1000) * 1000);
+    ::setsockopt(sock, SOL_SOCKET, SO_RCVTIMEO, &tv, sizeof(tv));
+}
+
+}  // namespace
+
 int Client::connect(const std::string &path) {
     sockaddr_un addr;
     if (int rc = make_address(path, &addr); rc != 0) return rc;
@@ -163,18 +174,14 @@ int Client::connect(const std::string &path) {
     uint64_t ms = 120000;
     if (const char *e = std::getenv("UGDR_RPC_TIMEOUT_MS"); e != nullptr && e[0] != '\0')
         ms = std::strtoull(e, nullptr, 10);
-    if (ms > 0) {
-        timeval tv{};
-        tv.tv_sec = time_t(ms / 1000);
-        tv.tv_usec = suseconds_t((ms % 1000) * 1000);
-        ::setsockopt(s.get(), SOL_SOCKET, SO_RCVTIMEO, &tv, sizeof(tv));
-    }
+    set_recv_timeout(s.get(), ms);
+    timeout_ms_ = ms;
     sock_ = std::move(s);
     return 0;
 }
 
-int Client::call(uint32_t method, std::vector<std::byte> payload, std::vector<Fd> fds,
-                 Message *resp) {
+int Client::call(uint32_t method, std::vector<std::byte> payload, std::vector<Fd> fds, Message *resp,
+                 uint64_t min_wait_ms) {
     if (!sock_.valid()) return ENOTCONN;
     if (resp == nullptr) return EINVAL;
     Message req;
@@ -194,7 +201,10 @@ int Client::call(uint32_t method, std::vector<std::byte> payload, std::vector<Fd
     do {
         rc = recv_message(sock_.get(), &r, true);
     } while (rc == EAGAIN && std::chrono::steady_clock::now() < spin_until);
+    const bool longer = timeout_ms_ != 0 && min_wait_ms > timeout_ms_;
+    if (longer) set_recv_timeout(sock_.get(), min_wait_ms);
     if (rc == EAGAIN || rc == EWOULDBLOCK) rc = recv_message(sock_.get(), &r);
+    if (longer) set_recv_timeout(sock_.get(), timeout_ms_);
     if (rc == EAGAIN || rc == EWOULDBLOCK) rc = ETIMEDOUT;  // SO_RCVTIMEO ran out
     if (rc != 0) {
         close();

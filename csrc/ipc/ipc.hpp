@@ -62,13 +62,17 @@ class Client {
     int connect(const std::string &path);
     // Synchronous request / response; `resp` keeps the reply.  Returns 0 or a positive errno
     // for transport failures; the reply's env.status carries the service result.
-    int call(uint32_t method, std::vector<std::byte> payload, std::vector<Fd> fds, Message *resp);
+    // `min_wait_ms` raises the reply deadline for this call (requests that wait on purpose, such
+    // as a timed drain).
+    int call(uint32_t method, std::vector<std::byte> payload, std::vector<Fd> fds, Message *resp,
+             uint64_t min_wait_ms = 0);
     void close() { sock_.reset(); }
     bool connected() const { return sock_.valid(); }
 
   private:
     Fd sock_;
     uint64_t next_id_ = 1;
+    uint64_t timeout_ms_ = 0;  // reply deadline set at connect (0: none)
 };
 
 using SessionId = uint64_t;
