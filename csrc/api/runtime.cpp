@@ -18,6 +18,8 @@
 #include "queue/ring.hpp"
 #include "ugdr/api.hpp"
 
+#include <unistd.h>
+
 #include <atomic>
 #include <chrono>
 #include <cerrno>
@@ -103,11 +105,14 @@ class Runtime {
         std::lock_guard<std::mutex> lk(mu_);
         const char *env = std::getenv("UGDR_DAEMON_SOCKET");
         const std::string path = (env != nullptr && env[0] != '\0') ? env : kDefaultSocket;
-        // (Re)connect when there is no connection or the configured daemon changed; either way
-        // the epoch advances and proxies of the previous connection become stale.
-        if (!client_.connected() || path != path_) {
+        // (Re)connect when there is no connection, the configured daemon changed, or this is a
+        // forked child (the inherited socket is the parent's session); either way the epoch
+        // advances and proxies of the previous connection become stale in this process.
+        const pid_t pid = ::getpid();
+        if (!client_.connected() || path != path_ || pid != pid_) {
             if (int rc = client_.connect(path); rc != 0) return rc;
             path_ = path;
+            pid_ = pid;
         }
         if (int rc = client_.call(std::move(req), resp, min_wait_ms); rc != 0) return rc;
         return resp->status;
@@ -143,6 +148,7 @@ class Runtime {
     }
 
   private:
+    pid_t pid_ = 0;  // process that opened the current connection
     struct Shell {
         void *obj;
         void (*del)(void *);

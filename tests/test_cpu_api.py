@@ -607,3 +607,37 @@ def test_control_plane_latency_benchmark():
     for op in ("cq_create", "cq_destroy", "qp_create", "qp_destroy", "qp_connect_pair", "mr_register",
                "mr_deregister", "query_qp"):
         assert 0 < rows[0][f"{op}_p50_us"] <= rows[0][f"{op}_p99_us"], op
+
+
+def test_forked_child_gets_its_own_session(cpu_daemon):
+    """After fork the child does not talk over its parent's session: its first control call opens
+    a new connection, the parent's objects are stale there (EINVAL), and the parent keeps working."""
+    import errno
+
+    ctx = V.Context(V.find_device(kind=0))
+    pd = ctx.alloc_pd()
+    r, w = os.pipe()
+    pid = os.fork()
+    if pid == 0:  # child
+        code = 1
+        try:
+            os.close(r)
+            try:
+                ctx.alloc_pd()
+                code = 2  # the parent's context must be stale in the child
+            except V.UgdrError as e:
+                if e.errno == errno.EINVAL:
+                    names = [d.name for d in V.get_devices()]  # a fresh session works
+                    code = 0 if "ugdr_cpu0" in names else 3
+        finally:
+            os.write(w, bytes([code]))
+            os._exit(0)
+    os.close(w)
+    code = os.read(r, 1)
+    os.close(r)
+    os.waitpid(pid, 0)
+    assert code == b"\x00", code
+    pd2 = ctx.alloc_pd()  # the parent's session is intact
+    pd2.dealloc()
+    pd.dealloc()
+    ctx.close()
