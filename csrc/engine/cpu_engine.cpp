@@ -205,7 +205,7 @@ size_t CpuEngine::progress_qp(QpView &v) {
             queue::Sge sg;
             std::memcpy(&sg, slot + queue::kSendSgeOffset + i * sizeof(queue::Sge), sizeof(sg));
             total += sg.length;
-            if (total > 0x80000000ull) {
+            if (total > 0xffffffffull) {  // byte_len is 32 bits: up to 4 GiB - 1 per WR
                 status = UGDR_WC_LOC_LEN_ERR;
                 break;
             }

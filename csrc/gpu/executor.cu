@@ -773,7 +773,7 @@ __device__ void stage_wr(Warp &w, const QpView &v, const uint8_t *wqe, WrRec *re
     uint64_t total = len;
     for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
     if (status == UGDR_WC_SUCCESS && any_bad) status = UGDR_WC_LOC_PROT_ERR;
-    if (status == UGDR_WC_SUCCESS && total > 0x80000000ull) status = UGDR_WC_LOC_LEN_ERR;
+    if (status == UGDR_WC_SUCCESS && total > 0xffffffffull) status = UGDR_WC_LOC_LEN_ERR;  // 4 GiB - 1 max
     if (status == UGDR_WC_SUCCESS && is_atomic(op) && total != 8) status = UGDR_WC_LOC_LEN_ERR;
 
     // Compact the non-empty segments: lane i keeps slot = prefix count of non-empty lanes.

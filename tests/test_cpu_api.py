@@ -641,3 +641,35 @@ def test_forked_child_gets_its_own_session(cpu_daemon):
     pd2.dealloc()
     pd.dealloc()
     ctx.close()
+
+
+def test_wr_length_limit_is_four_gib_minus_one(cpu_daemon):
+    """A WR may gather up to 4 GiB - 1 bytes (byte_len is 32 bits; the reference's limit): 2.25 GiB
+    passes the length check (and then fails on the small remote MR), 4.25 GiB is LOC_LEN_ERR.
+    The SGEs repeat one untouched 300 MiB region, so nothing is copied."""
+    ctx = V.Context(V.find_device(kind=0))
+    pd = ctx.alloc_pd()
+    cq = ctx.create_cq(64)
+    mk = lambda: pd.create_qp(cq, max_send_wr=8, max_recv_wr=8, max_send_sge=32, max_recv_sge=1)  # noqa: E731
+    big, small = V.HostBuffer(300 << 20), V.HostBuffer(4096)
+    lm = pd.reg_mr(big.addr, 300 << 20, ACC)
+    rm = pd.reg_mr(small.addr, 4096, ACC)
+    try:
+        for nsge, want in ((9, N.WC_REM_ACCESS_ERR), (17, N.WC_LOC_LEN_ERR)):
+            a, b = mk(), mk()
+            V.connect_pair(a, b, access=REMOTE)
+            sges = [(big.addr, 256 << 20, lm.lkey)] * nsge
+            wr = V.QueuePair.make_send_wr(N.WR_RDMA_WRITE, sges, remote_addr=small.addr, rkey=rm.rkey, wr_id=nsge)
+            assert a.post_send_raw([wr]) == (0, -1)
+            w = cq.wait(1, 30)[0]
+            assert (w.wr_id, w.status) == (nsge, want)
+            a.destroy()
+            b.destroy()
+    finally:
+        lm.dereg()
+        rm.dereg()
+        cq.destroy()
+        pd.dealloc()
+        ctx.close()
+        big.free()
+        small.free()
