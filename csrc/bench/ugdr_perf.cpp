@@ -79,7 +79,12 @@ struct Side {
     void *buf = nullptr;
 };
 
+// `gpu` < 0 selects the host-memory device (buffers from ugdr_x_alloc_host).
 ugdr_device *gpu_device(ugdr_device **list, int n, int gpu) {
+    for (int i = 0; i < n; ++i) {
+        ugdr_x_device_info info;
+        if (gpu < 0 && ugdr_x_query_device(list[i], &info) == 0 && info.kind == 0) return list[i];
+    }
     for (int i = 0; i < n; ++i) {
         ugdr_x_device_info info;
         if (ugdr_x_query_device(list[i], &info) == 0 && info.kind == 1 && info.gpu_ordinal == gpu) return list[i];
@@ -102,8 +107,13 @@ void setup(const Opts &o, uint64_t bytes, uint32_t depth, Side *a, Side *b) {
         s.pd = ugdr_alloc_pd(s.ctx);
         s.cq = ugdr_create_cq(s.ctx, int(depth * 2 + 16), nullptr, nullptr, 0);
         if (!s.pd || !s.cq) die("pd/cq", errno);
-        cudaSetDevice(gpus[i]);
-        if (cudaMalloc(&s.buf, bytes) != cudaSuccess) die("cudaMalloc", ENOMEM);
+        if (gpus[i] < 0) {
+            s.buf = ugdr_x_alloc_host(bytes);
+            if (!s.buf) die("ugdr_x_alloc_host", ENOMEM);
+        } else {
+            cudaSetDevice(gpus[i]);
+            if (cudaMalloc(&s.buf, bytes) != cudaSuccess) die("cudaMalloc", ENOMEM);
+        }
         s.mr = ugdr_reg_mr(s.pd, s.buf, bytes,
                            UGDR_ACCESS_LOCAL_WRITE | UGDR_ACCESS_REMOTE_WRITE | UGDR_ACCESS_REMOTE_READ);
         if (!s.mr) die("ugdr_reg_mr", errno);
@@ -132,19 +142,29 @@ void fill(void *dev, uint64_t bytes, uint64_t seed, int gpu) {
     std::vector<uint8_t> h(std::min<uint64_t>(bytes, 64ull << 20));
     std::mt19937_64 rng(seed);
     for (auto &x : h) x = uint8_t(rng());
-    cudaSetDevice(gpu);
-    for (uint64_t off = 0; off < bytes; off += h.size())
-        cudaMemcpy(static_cast<uint8_t *>(dev) + off, h.data(), std::min<uint64_t>(h.size(), bytes - off),
-                   cudaMemcpyHostToDevice);
+    if (gpu >= 0) cudaSetDevice(gpu);
+    for (uint64_t off = 0; off < bytes; off += h.size()) {
+        const uint64_t k = std::min<uint64_t>(h.size(), bytes - off);
+        if (gpu < 0)
+            std::memcpy(static_cast<uint8_t *>(dev) + off, h.data(), k);
+        else
+            cudaMemcpy(static_cast<uint8_t *>(dev) + off, h.data(), k, cudaMemcpyHostToDevice);
+    }
 }
 
 bool same(const void *a, int ga, const void *b, int gb, uint64_t bytes) {
     const uint64_t n = std::min<uint64_t>(bytes, 16ull << 20);
     std::vector<uint8_t> x(n), y(n);
-    cudaSetDevice(ga);
-    cudaMemcpy(x.data(), a, n, cudaMemcpyDeviceToHost);
-    cudaSetDevice(gb);
-    cudaMemcpy(y.data(), b, n, cudaMemcpyDeviceToHost);
+    auto get = [](std::vector<uint8_t> &out, const void *p, int g, uint64_t k) {
+        if (g < 0) {
+            std::memcpy(out.data(), p, k);
+        } else {
+            cudaSetDevice(g);
+            cudaMemcpy(out.data(), p, k, cudaMemcpyDeviceToHost);
+        }
+    };
+    get(x, a, ga, n);
+    get(y, b, gb, n);
     return x == y;
 }
 

@@ -673,3 +673,16 @@ def test_wr_length_limit_is_four_gib_minus_one(cpu_daemon):
         ctx.close()
         big.free()
         small.free()
+
+
+def test_latency_and_bandwidth_sweeps_run_on_the_host_device():
+    """ugdr_perf latency / bw with --src-gpu -1 --dst-gpu -1 use the host-memory device and host
+    buffers end to end (byte-checked by the binary)."""
+    from ugdr_b200.utils import perf
+
+    lat = [r for r in perf.run(["latency", "--src-gpu", "-1", "--dst-gpu", "-1", "--bytes", "4096", "--iters", "500"],
+                               gpus=0) if r.get("benchmark") == "ugdr_latency"]
+    assert len(lat) == 1 and lat[0]["correct"] and lat[0]["p50_us"] > 0
+    bw = [r for r in perf.run(["bw", "--src-gpu", "-1", "--dst-gpu", "-1", "--min", "8", "--max", "64K", "--qd", "16",
+                               "--bytes-per-size", "4M"], gpus=0) if r.get("benchmark") == "ugdr_bw"]
+    assert len(bw) >= 2 and all(r["correct"] for r in bw)
