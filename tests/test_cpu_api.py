@@ -686,3 +686,17 @@ def test_latency_and_bandwidth_sweeps_run_on_the_host_device():
     bw = [r for r in perf.run(["bw", "--src-gpu", "-1", "--dst-gpu", "-1", "--min", "8", "--max", "64K", "--qd", "16",
                                "--bytes-per-size", "4M"], gpus=0) if r.get("benchmark") == "ugdr_bw"]
     assert len(bw) >= 2 and all(r["correct"] for r in bw)
+
+
+def test_python_objects_are_context_managers(cpu_daemon):
+    """Each verbs object releases itself at the end of a `with` block, innermost first."""
+    with V.Context(V.find_device(kind=0)) as ctx, ctx.alloc_pd() as pd, ctx.create_cq(64) as cq, \
+            V.HostBuffer(8192) as buf, pd.reg_mr(buf.addr, 8192, ACC) as mr, \
+            pd.create_qp(cq, max_send_wr=8, max_recv_wr=8) as a, pd.create_qp(cq, max_send_wr=8, max_recv_wr=8) as b:
+        V.connect_pair(a, b, access=REMOTE)
+        buf.view()[:8] = 7
+        a.post_write((buf.addr, 8, mr.lkey), buf.addr + 4096, mr.rkey, wr_id=1)
+        assert cq.wait(1, 10)[0].status == N.WC_SUCCESS
+        assert bytes(buf.view()[4096:4104]) == b"\x07" * 8
+    with pytest.raises(V.UgdrError):  # everything above is gone
+        pd.dealloc()

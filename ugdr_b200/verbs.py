@@ -155,6 +155,12 @@ class Context:
         self.device = device
         self.h = _check_ptr(N.lib().ugdr_open_device(device.handle), "ugdr_open_device")
 
+    def __enter__(self) -> "Context":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
     def close(self) -> None:
         if N.lib().ugdr_close_device(self.h) != 0:
             e = N.errno()
@@ -200,6 +206,12 @@ class Pd:
         self.ctx = ctx
         self.h = _check_ptr(N.lib().ugdr_alloc_pd(ctx.h), "ugdr_alloc_pd")
 
+    def __enter__(self) -> "Pd":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.dealloc()
+
     def dealloc(self) -> None:
         _check(N.lib().ugdr_dealloc_pd(self.h), "ugdr_dealloc_pd")
 
@@ -222,6 +234,12 @@ class MemoryRegion:
         self.lkey = self.p.contents.lkey
         self.rkey = self.p.contents.rkey
 
+    def __enter__(self) -> "MemoryRegion":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.dereg()
+
     def dereg(self) -> None:
         _check(N.lib().ugdr_dereg_mr(self.p), "ugdr_dereg_mr")
 
@@ -242,6 +260,12 @@ class CompletionQueue:
         self.ctx = ctx
         self.h = _check_ptr(N.lib().ugdr_create_cq(ctx.h, cqe, None, None, 0), "ugdr_create_cq")
         self._buf = (N.Wc * 256)()
+
+    def __enter__(self) -> "CompletionQueue":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.destroy()
 
     def destroy(self) -> None:
         _check(N.lib().ugdr_destroy_cq(self.h), "ugdr_destroy_cq")
@@ -281,6 +305,12 @@ class QueuePair:
         info = N.QpConnInfo()
         _check(N.lib().ugdr_query_qp_conn_info(self.h, C.byref(info)), "conn info")
         self.qpn = info.qp_num
+
+    def __enter__(self) -> "QueuePair":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.destroy()
 
     def destroy(self) -> None:
         _check(N.lib().ugdr_destroy_qp(self.h), "ugdr_destroy_qp")
@@ -410,6 +440,12 @@ class HostBuffer:
         import numpy as np
 
         return np.ctypeslib.as_array((C.c_uint8 * self.length).from_address(self.addr))
+
+    def __enter__(self) -> "HostBuffer":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.free()
 
     def free(self) -> None:
         _check(N.lib().ugdr_x_free_host(C.c_void_p(self.addr)), "ugdr_x_free_host")
