@@ -30,8 +30,7 @@ NO_CUDA = {"common", "queue", "ipc", "control"}
 INCLUDE = re.compile(r'^\s*#\s*include\s+[<"]([^>"]+)[>"]', re.M)
 
 
-def _sources():
-    root = os.path.join(REPO, "csrc")
+def _sources(root: str = os.path.join(REPO, "csrc")):
     for layer in sorted(os.listdir(root)):
         d = os.path.join(root, layer)
         if not os.path.isdir(d):
@@ -47,16 +46,34 @@ def test_every_layer_is_listed():
     assert layers <= set(ALLOWED), layers - set(ALLOWED)
 
 
-def test_includes_respect_the_layering():
+def layering_violations(root: str = os.path.join(REPO, "csrc")) -> list[str]:
     bad = []
-    for layer, name, incs in _sources():
+    for layer, name, incs in _sources(root):
         for inc in incs:
             if "/" not in inc:
                 continue  # system and toolkit headers
             top = inc.split("/")[0]
             if top in ALLOWED and top not in ALLOWED[layer] or top == "ugdr" and "ugdr" not in ALLOWED[layer]:
                 bad.append(f"csrc/{layer}/{name} includes {inc}")
+    return bad
+
+
+def test_includes_respect_the_layering():
+    bad = layering_violations()
     assert not bad, "\n".join(bad)
+
+
+def test_the_checker_rejects_a_forbidden_dependency(tmp_path):
+    """The checker itself is exercised on a fixture tree: the wire-format layer including the
+    control plane, and the client API including the GPU executor, must both be reported
+    (reference: tests/integration/forbidden_dependency/ against check_module_boundaries.py)."""
+    (tmp_path / "queue").mkdir()
+    (tmp_path / "api").mkdir()
+    (tmp_path / "queue" / "ring.cpp").write_text('#include "control/service.hpp"\n#include <vector>\n')
+    (tmp_path / "api" / "runtime.cpp").write_text('#include "gpu/executor.hpp"\n#include "queue/ring.hpp"\n')
+    bad = layering_violations(str(tmp_path))
+    assert sorted(bad) == ["csrc/api/runtime.cpp includes gpu/executor.hpp",
+                           "csrc/queue/ring.cpp includes control/service.hpp"]
 
 
 def test_wire_and_control_layers_do_not_include_cuda():
