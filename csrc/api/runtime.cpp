@@ -627,6 +627,17 @@ int ugdr_x_engine_trace_dump(ugdr_context *ctx, const char *path, uint64_t *kept
     }
 }
 
+int ugdr_x_query_daemon_stats(ugdr_x_daemon_stats *stats) noexcept {
+    if (stats == nullptr) return EINVAL;
+    Response resp;
+    if (int rc = rt().call(make(kDaemonStats), &resp); rc != 0) return rc;
+    ByteReader rd(resp.opaque);
+    if (!rd.be(&stats->devices) || !rd.be(&stats->contexts) || !rd.be(&stats->pds) || !rd.be(&stats->mrs) ||
+        !rd.be(&stats->cqs) || !rd.be(&stats->qps))
+        return EPROTO;
+    return 0;
+}
+
 int ugdr_x_engine_hold(ugdr_context *ctx, int hold) noexcept {
     if (!rt().live(ctx)) return EINVAL;
     Request req = make(kEngineHold, ctx->identity);

@@ -43,6 +43,7 @@ enum Method : uint32_t {
     kTimedDrain = 34,
     kQpStats = 35,
     kEngineTrace = 36,
+    kDaemonStats = 37,
 };
 
 struct Request {

@@ -115,6 +115,7 @@ const char *method_range(uint32_t m) {
     case kTimedDrain: return "ugdr.rpc.timed_drain";
     case kQpStats: return "ugdr.rpc.qp_stats";
     case kEngineTrace: return "ugdr.rpc.engine_trace";
+    case kDaemonStats: return "ugdr.rpc.daemon_stats";
     default: return names[0];
     }
 }
@@ -143,6 +144,7 @@ Response ControlPlane::dispatch(ipc::SessionId s, Request &&r) {
     case kTimedDrain: return timed_drain(s, r);
     case kQpStats: return qp_stats(s, r);
     case kEngineTrace: return engine_trace(s, r);
+    case kDaemonStats: return daemon_stats(s, r);
     default: return status(EOPNOTSUPP);
     }
 }
@@ -590,6 +592,15 @@ Response ControlPlane::engine_trace(uint64_t s, const Request &r) {
     Response out;
     ByteWriter w(&out.opaque);
     w.be(kept).be(dropped);
+    return out;
+}
+
+// Live objects of every session (operators' view of the daemon), and the device count.
+Response ControlPlane::daemon_stats(uint64_t, const Request &) {
+    Response out;
+    ByteWriter w(&out.opaque);
+    w.be(uint64_t(engines_.size())).be(uint64_t(contexts_.size())).be(uint64_t(pds_.size()));
+    w.be(uint64_t(mrs_.size())).be(uint64_t(cqs_.size())).be(uint64_t(qps_.size()));
     return out;
 }
 

@@ -61,6 +61,7 @@ class ControlPlane : public ipc::Handler {
     Response engine_hold(uint64_t s, const Request &r);
     Response qp_stats(uint64_t s, const Request &r);
     Response engine_trace(uint64_t s, const Request &r);
+    Response daemon_stats(uint64_t s, const Request &r);
     Response timed_drain(uint64_t s, const Request &r);
 
     void erase_qp(uint64_t id) noexcept;

@@ -291,6 +291,13 @@ typedef struct ugdr_x_qp_stats {
 
 int ugdr_x_query_qp_stats(ugdr_qp *qp, ugdr_x_qp_stats *stats) UGDR_NOEXCEPT;
 
+/* The daemon's live objects over all sessions, and its device count. */
+typedef struct ugdr_x_daemon_stats {
+    uint64_t devices, contexts, pds, mrs, cqs, qps;
+} ugdr_x_daemon_stats;
+
+int ugdr_x_query_daemon_stats(ugdr_x_daemon_stats *stats) UGDR_NOEXCEPT;
+
 /* Busy-polls `cq` until at least `min_entries` completions (at most `max_entries`) were taken
  * into `wc`, or `timeout_ns` passed.  Returns the number taken (possibly fewer than min_entries
  * on timeout) or a negative errno, like ugdr_poll_cq. */

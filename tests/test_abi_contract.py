@@ -81,6 +81,7 @@ def _probe() -> dict:
     lines.append('    printf("sizeof.ugdr_x_qp_stats %zu\\n", sizeof(ugdr_x_qp_stats));')
     lines.append('    printf("sizeof.ugdr_x_engine_stats %zu\\n", sizeof(ugdr_x_engine_stats));')
     lines.append('    printf("sizeof.ugdr_x_kernel_attr %zu\\n", sizeof(ugdr_x_kernel_attr));')
+    lines.append('    printf("sizeof.ugdr_x_daemon_stats %zu\\n", sizeof(ugdr_x_daemon_stats));')
     lines += ["    return 0;", "}"]
     out = {}
     for line in _compile_and_run("\n".join(lines) + "\n").splitlines():
@@ -117,6 +118,7 @@ def test_python_binding_layouts_match_the_header(probe):
     from ugdr_b200.ops import KernelAttr
 
     assert C.sizeof(KernelAttr) == probe["sizeof.ugdr_x_kernel_attr"]
+    assert C.sizeof(N.DaemonStats) == probe["sizeof.ugdr_x_daemon_stats"]
 
 
 def test_binding_constants_match_the_header(probe):

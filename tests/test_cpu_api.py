@@ -700,3 +700,38 @@ def test_python_objects_are_context_managers(cpu_daemon):
         assert bytes(buf.view()[4096:4104]) == b"\x07" * 8
     with pytest.raises(V.UgdrError):  # everything above is gone
         pd.dealloc()
+
+
+def test_daemon_stats_count_live_objects(tmp_path):
+    """ugdr_x_query_daemon_stats counts every session's live objects and follows creation,
+    destruction and the reclaim of a vanished client."""
+    import subprocess
+    import sys
+
+    with V.Daemon(gpus=0, socket_path=str(tmp_path / "d.sock")) as d:
+        old = os.environ.get("UGDR_DAEMON_SOCKET")
+        os.environ["UGDR_DAEMON_SOCKET"] = d.socket_path
+        try:
+            base = V.daemon_stats()
+            assert base["devices"] == 1 and base["qps"] == 0
+            with V.Context(V.find_device(kind=0)) as ctx, ctx.alloc_pd() as pd, ctx.create_cq(16) as cq:
+                with pd.create_qp(cq, max_send_wr=4, max_recv_wr=4):
+                    st = V.daemon_stats()
+                    assert (st["contexts"], st["pds"], st["cqs"], st["qps"]) == (1, 1, 1, 1)
+            code = ("from ugdr_b200 import verbs as V\n"
+                    "ctx = V.Context(V.find_device(kind=0)); pd = ctx.alloc_pd(); cq = ctx.create_cq(8)\n"
+                    "print(V.daemon_stats()['cqs'])\n")
+            env = dict(os.environ, PYTHONPATH=os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+            r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=60)
+            assert r.stdout.strip() == "1", r.stderr
+            import time
+
+            deadline = time.time() + 10
+            while V.daemon_stats()["cqs"] != 0 and time.time() < deadline:
+                time.sleep(0.02)
+            assert V.daemon_stats() == base  # the vanished client's objects were reclaimed
+        finally:
+            if old is None:
+                os.environ.pop("UGDR_DAEMON_SOCKET", None)
+            else:
+                os.environ["UGDR_DAEMON_SOCKET"] = old

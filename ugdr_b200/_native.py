@@ -178,6 +178,10 @@ class DeviceInfo(C.Structure):
     ]
 
 
+class DaemonStats(C.Structure):
+    _fields_ = [(f, C.c_uint64) for f in ("devices", "contexts", "pds", "mrs", "cqs", "qps")]
+
+
 class QpStats(C.Structure):
     _fields_ = [
         ("send_posted", C.c_uint64),
@@ -259,6 +263,7 @@ def lib() -> C.CDLL:
         "ugdr_x_free_host": (i, [vp]),
         "ugdr_x_query_engine_stats": (i, [vp, C.POINTER(EngineStats), i]),
         "ugdr_x_query_qp_stats": (i, [vp, C.POINTER(QpStats)]),
+        "ugdr_x_query_daemon_stats": (i, [C.POINTER(DaemonStats)]),
         "ugdr_x_poll_cq_wait": (i, [vp, i, i, C.POINTER(Wc), C.c_uint64]),
         "ugdr_x_engine_trace": (i, [vp, C.c_uint32]),
         "ugdr_x_engine_trace_dump": (i, [vp, C.c_char_p, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),

@@ -192,6 +192,13 @@ class Context:
         _check(N.lib().ugdr_x_engine_hold(self.h, int(on)), "engine hold")
 
 
+def daemon_stats() -> dict:
+    """Live objects in the daemon over all sessions, and its device count."""
+    st = N.DaemonStats()
+    _check(N.lib().ugdr_x_query_daemon_stats(C.byref(st)), "ugdr_x_query_daemon_stats")
+    return {f: int(getattr(st, f)) for f, _ in st._fields_}
+
+
 def timed_drain(contexts: list[Context], expected: list[int], timeout_ms: int = 60000) -> list[float]:
     n = len(contexts)
     arr = (C.c_void_p * n)(*[c.h for c in contexts])
