@@ -32,6 +32,14 @@ def doctor() -> dict:
     from . import _native as N
 
     rep["libugdr"] = str(N.LIB_PATH) if N.LIB_PATH.exists() else None
+    if os.environ.get("UGDR_DAEMON_SOCKET") and rep["libugdr"]:
+        from . import verbs as V
+
+        try:  # a running daemon: its devices and live objects
+            rep["daemon_stats"] = V.daemon_stats()
+            rep["daemon_devices"] = [d.name for d in V.get_devices()]
+        except Exception as e:  # a report, not a failure
+            rep["daemon_error"] = repr(e)
     rep["daemon"] = str(N.DAEMON_PATH) if N.DAEMON_PATH.exists() else None
     try:
         import torch
