@@ -25,6 +25,22 @@ inline void cpu_relax() {
 #endif
 }
 
+// Payload copy.  Short segments (descriptor-sized WRs, gathers of a few bytes each) skip the
+// library call: up to 16 bytes move as two possibly overlapping 8-byte words, or bytewise.
+inline void copy_bytes(uint8_t *dst, const uint8_t *src, uint32_t n) {
+    if (n >= 8 && n <= 16) {
+        uint64_t a, b;
+        std::memcpy(&a, src, 8);
+        std::memcpy(&b, src + n - 8, 8);
+        std::memcpy(dst, &a, 8);
+        std::memcpy(dst + n - 8, &b, 8);
+    } else if (n < 8) {
+        for (uint32_t i = 0; i < n; ++i) dst[i] = src[i];
+    } else {
+        std::memcpy(dst, src, n);
+    }
+}
+
 struct Seg {
     uint8_t *local;
     uint32_t length;
@@ -282,13 +298,13 @@ size_t CpuEngine::progress_qp(QpView &v) {
             if (op == UGDR_WR_RDMA_WRITE || op == UGDR_WR_RDMA_WRITE_WITH_IMM) {
                 uint64_t off = 0;
                 for (uint32_t i = 0; i < nseg; ++i) {
-                    std::memcpy(remote + off, segs[i].local, segs[i].length);
+                    copy_bytes(remote + off, segs[i].local, segs[i].length);
                     off += segs[i].length;
                 }
             } else if (op == UGDR_WR_RDMA_READ) {
                 uint64_t off = 0;
                 for (uint32_t i = 0; i < nseg; ++i) {
-                    std::memcpy(segs[i].local, remote + off, segs[i].length);
+                    copy_bytes(segs[i].local, remote + off, segs[i].length);
                     off += segs[i].length;
                 }
             } else {
