@@ -3,6 +3,8 @@
 // place:
 //
 //   ugdr_engine_bench metadata   post_send chain -> engine pass -> poll CQ, per batch
+//                                (--pass-lock 0: no object lock around the pass, as the
+//                                reference's lock-free mock worker)
 //                                (reference: benchmarks/queue_metadata_benchmark.cpp:70-176;
 //                                batch 1/32 x SGEs 1/4 x signal every WR / every 32nd WR).
 //   ugdr_engine_bench payload    up to `depth` WRs in flight on one QP, completion seen at the
@@ -166,7 +168,12 @@ struct Rig {
 
     uint64_t addr(const uint8_t *p) const { return reinterpret_cast<uintptr_t>(p); }
 
+    // With `pass_lock` each engine pass takes the control plane's object lock, as the daemon's
+    // engine thread does; without it this single thread holds no lock (nothing else runs here),
+    // which is the reference's mock-worker setting.
+    bool pass_lock = true;
     size_t progress() {
+        if (!pass_lock) return eng.progress_locked();
         std::lock_guard<std::mutex> lk(mu);
         return eng.progress_locked();
     }
@@ -209,10 +216,13 @@ void fill_sges(ugdr_sge *sg, uint32_t n, uint64_t base, uint32_t bytes, uint32_t
     }
 }
 
+bool g_pass_lock = true;
+
 void metadata_case(uint32_t batch, uint32_t nsge, bool every, uint32_t wr_bytes) {
     constexpr uint32_t kCap = 256;
     constexpr uint64_t kWrs = 262144;
     Rig r(kCap, nsge, kCap, uint64_t(wr_bytes) * batch);
+    r.pass_lock = g_pass_lock;
     std::vector<ugdr_send_wr> wr(batch);
     std::vector<ugdr_sge> sg(size_t(batch) * nsge);
     for (uint32_t i = 0; i < batch; ++i) {
@@ -257,9 +267,9 @@ void metadata_case(uint32_t batch, uint32_t nsge, bool every, uint32_t wr_bytes)
     const uint64_t c1 = cycles();
     const double wrs = double(iters * batch);
     if (std::memcmp(r.dst, r.src, size_t(wr_bytes) * batch) != 0) die("payload check", EIO);
-    std::printf("benchmark=engine_metadata batch=%u num_sge=%u signaling=%s wr_bytes=%u completed_wr=%llu wc=%llu "
+    std::printf("benchmark=engine_metadata pass_lock=%d batch=%u num_sge=%u signaling=%s wr_bytes=%u completed_wr=%llu wc=%llu "
                 "MWR_per_s=%.3f cycles_per_wr=%.1f latency_sample=batch p50_ns=%.0f p99_ns=%.0f\n",
-                batch, nsge, every ? "every_wr" : "every_32_wr", wr_bytes, (unsigned long long)(iters * batch),
+                int(g_pass_lock), batch, nsge, every ? "every_wr" : "every_32_wr", wr_bytes, (unsigned long long)(iters * batch),
                 (unsigned long long)wc, wrs / secs / 1e6, double(c1 - c0) / wrs, pct(lat, 0.5), pct(lat, 0.99));
 }
 
@@ -325,6 +335,7 @@ int main(int argc, char **argv) {
         const std::string k = argv[i];
         if (k == "--wr-bytes") wr_bytes = uint32_t(std::strtoul(argv[i + 1], nullptr, 0));
         else if (k == "--iters") iters = std::strtoull(argv[i + 1], nullptr, 0);
+        else if (k == "--pass-lock") g_pass_lock = std::strtoul(argv[i + 1], nullptr, 0) != 0;
         else die("unknown option", EINVAL);
     }
     if (mode == "metadata") {
