@@ -168,3 +168,15 @@ def test_every_declared_function_is_exported_with_c_linkage():
     assert set(REFERENCE_SYMBOLS) <= declared
     missing = sorted(declared - exported)
     assert not missing, missing
+
+
+def test_diagnostics_fail_cleanly_without_a_gpu():
+    """Without a CUDA device the kernel reports and copy diagnostics return a CUDA error code
+    (raised as RuntimeError by the binding) instead of crashing the process."""
+    torch = pytest.importorskip("torch")
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    from ugdr_b200 import ops
+
+    with pytest.raises(RuntimeError):
+        ops.kernel_attributes()
