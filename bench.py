@@ -363,6 +363,14 @@ def run_reference(args, comm: Comm, world: int, rank: int, local: int) -> dict |
         "config": {"model": "reference client->daemon CUDA benchmark, 32 MiB WRs, QD 64, same-GPU target",
                    "per_gpu_GBps": got, "batches": batches,
                    "timing": "reference's own wall clock (steady_clock) per process, summed over GPUs"},
+        # The reference's number is already end to end: its client posts WRs into the shared
+        # ring through the public API and polls their CQEs; the daemon's host worker feeds the
+        # copy kernel.  One WQE goes host->device and one CQE device->host per WR, as in ours.
+        "e2e": {"value": round(value, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": world * PEERS * 64,
+                "d2h_bytes_per_step": world * PEERS * 32,
+                "path": "reference ugdr_post_send -> daemon worker -> persistent copy kernel -> ugdr_poll_cq, "
+                        "QD 64, wall clock per process, summed over GPUs"},
     }
 
 

@@ -1,7 +1,7 @@
 // ugdr_x_moe_route_noalloc: the MoE routing kernels with their scratch in a fixed device array
-// (see route_noalloc.h for who needs it and its limits).  No counterpart in the reference.
+// (see include/ugdr/route_noalloc.h for who needs it and its limits).  No counterpart in the reference.
 #include "collective/kernels.hpp"
-#include "collective/route_noalloc.h"
+#include "ugdr/route_noalloc.h"
 
 #include <cuda_runtime.h>
 
@@ -53,4 +53,13 @@ extern "C" int ugdr_x_moe_route_noalloc(const int32_t *expert_ids, uint64_t rows
     if (cudaError_t e = scratch_for(device, &scratch); e != cudaSuccess) return int(e);
     return ugdr::coll::launch_route(expert_ids, rows, nexp, counts, positions, scratch,
                                     static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ugdr_x_moe_route_noalloc_reset(void) {
+    int device = 0;
+    if (cudaError_t e = cudaGetDevice(&device); e != cudaSuccess) return int(e);
+    if (device < 0 || device >= kMaxDevices) return int(cudaErrorInvalidDevice);
+    std::lock_guard<std::mutex> lk(g_mu);
+    g_scratch_ptr[device] = nullptr;
+    return int(cudaSuccess);
 }

@@ -1,7 +1,7 @@
 """ABI contract of the public headers (reference suite semantics: tests/unit/api_contract_c_test.c
 compiles the header as C11; libibverbs_alignment_test.cpp pins values and layouts).
 
-* include/ugdr/api.hpp and include/ugdr/collective.h compile as strict C11.
+* include/ugdr/api.hpp, include/ugdr/collective.h and include/ugdr/route_noalloc.h compile as strict C11.
 * Enum values are libibverbs' (ibv_wr_opcode, ibv_wc_status, ibv_wc_opcode, ibv_qp_state,
   ibv_access_flags, ibv_qp_attr_mask bits), written out here because <infiniband/verbs.h> is not
   installed on this machine.
@@ -69,7 +69,7 @@ def _compile_and_run(src: str) -> str:
 
 def _probe() -> dict:
     lines = ['#include <stddef.h>', '#include <stdio.h>', '#include "ugdr/api.hpp"', '#include "ugdr/collective.h"',
-             "int main(void) {"]
+             '#include "ugdr/route_noalloc.h"', "int main(void) {"]
     for name in IBV_VALUES:
         lines.append(f'    printf("{name} %lld\\n", (long long){name});')
     for st, fields in STRUCTS.items():
@@ -146,7 +146,7 @@ def _declared_functions() -> set[str]:
     import re
 
     names = set()
-    for h in ("api.hpp", "collective.h"):
+    for h in ("api.hpp", "collective.h", "route_noalloc.h"):
         with open(os.path.join(REPO, "include", "ugdr", h)) as f:
             text = re.sub(r"/\*.*?\*/|//[^\n]*", "", f.read(), flags=re.S)
         names |= set(re.findall(r"\b(ugdr_[a-z0-9_]+)\s*\([^;{]*\)\s*(?:noexcept\s*)?(?:UGDR_NOEXCEPT\s*)?;", text))

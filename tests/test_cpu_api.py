@@ -402,6 +402,32 @@ def test_daemon_death_is_reported_and_a_restarted_daemon_serves_new_objects(tmp_
         d.stop()  # reaps the killed process and closes its log
 
 
+def test_nested_daemon_leaves_the_outer_socket_in_place():
+    """A daemon started and stopped inside another's lifetime (as benchmark helpers do) puts
+    UGDR_DAEMON_SOCKET back when it stops, so clients of the outer daemon keep working; a daemon
+    started with export=False never touches the variable."""
+    outer = V.Daemon(gpus=0)
+    try:
+        assert os.environ["UGDR_DAEMON_SOCKET"] == outer.socket_path
+        assert any(d.kind == 0 for d in V.get_devices())
+        with V.Daemon(gpus=0) as inner:
+            assert os.environ["UGDR_DAEMON_SOCKET"] == inner.socket_path
+        assert os.environ["UGDR_DAEMON_SOCKET"] == outer.socket_path
+        with V.Daemon(gpus=0, export=False) as quiet:
+            assert os.environ["UGDR_DAEMON_SOCKET"] == outer.socket_path != quiet.socket_path
+        assert os.environ["UGDR_DAEMON_SOCKET"] == outer.socket_path
+        devs = V.get_devices()  # reaches the outer daemon, whose socket still exists
+        assert any(d.kind == 0 for d in devs)
+        ctx, pd, cq, a, b = _pair(depth=16, cq_depth=64)
+        buf = V.HostBuffer(1 << 16)
+        mr = pd.reg_mr(buf.addr, 1 << 16, ACC)
+        buf.view()[:8] = np.arange(8, dtype=np.uint8)
+        a.post_write((buf.addr, 8, mr.lkey), buf.addr + 4096, mr.rkey, wr_id=3)
+        assert cq.wait(1, timeout=10)[0].status == N.WC_SUCCESS
+    finally:
+        outer.stop()
+
+
 def test_smoke_binaries(tmp_path):
     """Reference smoke checks (tests/smoke): the client without a daemon reports an errno and
     fails; the daemon prints its usage; with a daemon, the client lists its devices."""

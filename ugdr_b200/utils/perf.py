@@ -25,7 +25,7 @@ def run(args: list[str], gpus: int | None = None, timeout: float = 1800) -> list
         gpus = 0 if args and args[0] == "posting" else (max(ids) + 1 if ids else 1)
     exe = N.LIB_DIR / "ugdr_perf"
     lines: list[str] = []
-    with V.Daemon(gpus=gpus) as d:
+    with V.Daemon(gpus=gpus, export=False) as d:
         env = dict(os.environ, UGDR_DAEMON_SOCKET=d.socket_path)
         proc = subprocess.Popen([str(exe), *args], env=env, stdout=subprocess.PIPE, text=True)
         for line in proc.stdout:  # stream: a run cut short still leaves its finished points
@@ -55,7 +55,7 @@ def stress_all(gpus: int, extra: list[str], timeout: float = 1800, host_clients:
     else:
         pairs = [(-1, -1)] * host_clients
     results = []
-    with tempfile.TemporaryDirectory(prefix="ugdr-stress-") as sync, V.Daemon(gpus=gpus) as d:
+    with tempfile.TemporaryDirectory(prefix="ugdr-stress-") as sync, V.Daemon(gpus=gpus, export=False) as d:
         env = dict(os.environ, UGDR_DAEMON_SOCKET=d.socket_path)
         procs = [subprocess.Popen([str(exe), "stress", "--src-gpu", str(a), "--dst-gpu", str(b), *extra,
                                    "--seed", str(1 + i), "--sync-dir", sync, "--sync-n", str(len(pairs))],

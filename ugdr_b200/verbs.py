@@ -41,14 +41,20 @@ def _check_ptr(p, what: str):
 class Daemon:
     """Run `ugdr_daemon` as a child process on a private socket.
 
-    `gpus`: how many GPUs it owns (None = all visible, 0 = host engine only).  The socket path is
-    exported as UGDR_DAEMON_SOCKET so this process's verbs calls reach it.
+    `gpus`: how many GPUs it owns (None = all visible, 0 = host engine only).  With `export`
+    (the default) the socket path is set as UGDR_DAEMON_SOCKET so this process's verbs calls reach
+    it, and `stop()` puts the variable back as it was, so a nested daemon (one a benchmark helper
+    starts and stops) leaves the outer daemon's clients pointing at the outer socket.  Helpers
+    that only hand the socket to child processes pass `export=False`.
     """
 
     def __init__(self, gpus: int | None = None, socket_path: str | None = None,
                  ctas: int | None = None, idle_exit_us: int | None = None,
-                 cpu_device: bool = True, env: dict | None = None, log_path: str | None = None):
+                 cpu_device: bool = True, env: dict | None = None, log_path: str | None = None,
+                 export: bool = True):
         self._dir = None
+        self._exported = False
+        self._prev_socket = None
         if socket_path is None:
             self._dir = tempfile.mkdtemp(prefix="ugdr-")
             socket_path = os.path.join(self._dir, "ugdr.sock")
@@ -79,7 +85,10 @@ class Daemon:
                 self.stop()
                 raise RuntimeError("ugdr_daemon did not create its socket")
             time.sleep(0.01)
-        os.environ["UGDR_DAEMON_SOCKET"] = socket_path
+        if export:
+            self._prev_socket = os.environ.get("UGDR_DAEMON_SOCKET")
+            os.environ["UGDR_DAEMON_SOCKET"] = socket_path
+            self._exported = True
 
     def stop(self, timeout: float = 30.0) -> int:
         if self.proc.poll() is None:
@@ -90,6 +99,12 @@ class Daemon:
                 self.proc.kill()
                 self.proc.wait()
         self._log.close()
+        if self._exported and os.environ.get("UGDR_DAEMON_SOCKET") == self.socket_path:
+            if self._prev_socket is None:
+                os.environ.pop("UGDR_DAEMON_SOCKET", None)
+            else:
+                os.environ["UGDR_DAEMON_SOCKET"] = self._prev_socket
+        self._exported = False
         if self._dir:
             with contextlib.suppress(OSError):
                 os.unlink(self.socket_path)
