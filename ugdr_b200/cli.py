@@ -4,7 +4,7 @@
     python -m ugdr_b200.cli build       make -j (libugdr.so, daemon, client, perf, native tests)
     python -m ugdr_b200.cli test [-m "not gpu"]   pytest over tests/
     python -m ugdr_b200.cli smoke       one WRITE + READ through a private daemon on cuda:0
-    python -m ugdr_b200.cli lint        layering, public ABI/exports, Python byte-compile
+    python -m ugdr_b200.cli lint        layering, public ABI/exports, client contracts, byte-compile
                                         (parity: the reference's tools/check_module_boundaries.py and
                                         tools/check_client_contracts.py)
 """
@@ -91,7 +91,8 @@ def main(argv: list[str] | None = None) -> int:
 
         ok = all(compileall.compile_dir(os.path.join(REPO, d), quiet=1) for d in ("ugdr_b200", "tests"))
         rc = subprocess.run([sys.executable, "-m", "pytest", "-q", "-p", "no:cacheprovider",
-                             "tests/test_module_boundaries.py", "tests/test_abi_contract.py"], cwd=REPO).returncode
+                             "tests/test_module_boundaries.py", "tests/test_abi_contract.py",
+                             "tests/test_contracts.py"], cwd=REPO).returncode
         return 0 if ok and rc == 0 else 1
     return 2
 
