@@ -2,10 +2,10 @@
 """Headline benchmark: all-pairs RDMA WRITE bandwidth through the ugdr verbs API.
 
 Workload (the all-pairs configuration, weak-scaled): every GPU holds one 256 MiB bf16 MR (N(0,1),
-seeded by rank) of eight 32 MiB slices, plus a 256 MiB receive MR.  One step = every GPU
-RDMA_WRITEs 7 distinct slices over 7 QPs: WR k of rank r sends slice k to peer
-(r + 1 + k mod (N - 1)) % N, into that GPU's receive slot (dst + 1 + k) % 8, so every inbound WR
-of a step lands in its own slot.  With N = 8 this is exactly "a 32 MiB slice to each of its 7
+seeded by rank) of eight 32 MiB slices, plus a 512 MiB receive MR (two sets of eight slots, used by
+alternate steps).  One step = every GPU RDMA_WRITEs 7 distinct slices over 7 QPs: WR k of rank r
+sends slice k to peer (r + 1 + k mod (N - 1)) % N, into that GPU's receive slot (dst + 1 + k) % 8
+of the step's set, so every inbound WR of a step lands in its own slot.  With N = 8 this is exactly "a 32 MiB slice to each of its 7
 peers"; with fewer GPUs the same 7 x 32 MiB per GPU cycle over the N - 1 peers, so all traffic
 crosses NVLink.  N = 1 has no peer: the WRs are loopback copies inside the GPU, and each WR of
 the run gets its own source slice and destination slot so that no step is served from L2.
@@ -128,6 +128,10 @@ def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None
     loop = world == 1
     nslices = min(PEERS * (K + W), 448) if loop else SLOTS
     total = nslices * slot
+    # Receive MR: with peers, two sets of 8 slots used by alternate steps.  A QP's WRs take effect
+    # in posting order, so a WR into the slot the previous step's WR on that QP is still writing
+    # would wait for it; alternating sets lets two steps per QP be in flight.
+    rcv_total = total if loop else 2 * total
 
     ctx = V.Context(V.find_device(gpu=local))
     pd = ctx.alloc_pd()
@@ -136,11 +140,11 @@ def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None
     # reads 7 distinct 32 MiB slices (224 MiB, larger than L2).  Receive MR: where peers write.
     gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
     src_buf = torch.randn(total // 2, dtype=torch.bfloat16, device="cuda", generator=gen)
-    rcv_buf = torch.zeros(total // 2, dtype=torch.bfloat16, device="cuda")
+    rcv_buf = torch.zeros(rcv_total // 2, dtype=torch.bfloat16, device="cuda")
     torch.cuda.synchronize()
     acc = N.ACCESS_LOCAL_WRITE | N.ACCESS_REMOTE_WRITE
     src_mr = pd.reg_mr(src_buf.data_ptr(), total, acc)
-    rcv_mr = pd.reg_mr(rcv_buf.data_ptr(), total, acc)
+    rcv_mr = pd.reg_mr(rcv_buf.data_ptr(), rcv_total, acc)
     req = [pd.create_qp(cq, max_send_wr=depth) for _ in range(PEERS)]
     rsp = [pd.create_qp(cq, max_send_wr=4) for _ in range(PEERS)]
     for q in req + rsp:
@@ -153,8 +157,8 @@ def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None
     comm.barrier()
 
     # Work requests are built once per distinct (step pattern, QP) and reused: a step's WRs differ
-    # only in their slices, which repeat with period 1 (N > 1) or nslices / 7 (N = 1).
-    period = nslices // PEERS if loop else 1
+    # only in their slices, which repeat with period 2 (N > 1) or nslices / 7 (N = 1).
+    period = nslices // PEERS if loop else 2
     wr_cache: dict[tuple[int, int], object] = {}
 
     def step_wr(step_id: int, k: int):
@@ -163,7 +167,7 @@ def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None
         if w is None:
             dst = peer_of(rank, k, world)
             sidx = k
-            dslot = (dst + 1 + k) % SLOTS
+            dslot = (dst + 1 + k) % SLOTS + SLOTS * (step_id % 2)
             if loop:
                 sidx = dslot = (step_id * PEERS + k) % nslices
             w = V.QueuePair.make_send_wr(N.WR_RDMA_WRITE, [(src_buf.data_ptr() + sidx * slot, slot, src_mr.lkey)],
@@ -300,6 +304,7 @@ def run_ugdr(args, comm: Comm, world: int, rank: int, local: int) -> dict | None
             "seq_len": slot,
             "parallelism": f"{world} GPU(s) x {PEERS} QPs, 32 MiB per WR",
             "mr_bytes_per_gpu": total,
+            "rcv_mr_bytes_per_gpu": rcv_total,
             "l2": ("inputs larger than L2: every WR of the run has its own 32 MiB source slice and destination slot"
                    if loop else
                    "inputs larger than L2: 7 distinct 32 MiB source slices (224 MiB) read + 224 MiB written per GPU per step"),

@@ -99,6 +99,10 @@ struct WrRec {
     uint32_t nseg;
     uint32_t recv_cqe_done;
     uint32_t pad[2];
+    // Device-address extent of the WR's local segments, [lo, hi) (empty when lo == hi): with
+    // `remote` and `total` it gives the ranges a later WR of the same QP must not touch while
+    // this one may still be moving bytes (see the ordering rule in executor.cu).
+    unsigned long long lo, hi;
     DevSeg seg[kMaxSge];
 };
 

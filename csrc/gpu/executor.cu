@@ -532,6 +532,140 @@ __device__ __forceinline__ uint32_t remote_need(uint32_t op) {
     if (is_atomic(op)) return UGDR_ACCESS_REMOTE_ATOMIC;
     return UGDR_ACCESS_REMOTE_WRITE;
 }
+// ---- ordering within a QP --------------------------------------------------------------------
+// The WRs of one QP take effect in posting order (RC semantics: the responder executes them in
+// order, so of two WRITEs to the same bytes the later one wins, and a READ sees every earlier
+// WRITE).  The executor runs a batch's WRs on different lanes at once, and large WRs as chunked
+// jobs that finish later, so a WR starts only when no earlier WR of its QP that may still be
+// moving bytes touches the same bytes with at least one of the two writing them.  Addresses are
+// device addresses in this GPU's mappings; every registered allocation is mapped once per GPU,
+// so the same bytes always have the same address here.
+
+// The bytes one WR touches: the remote range [rl, rh) and the extent of its local segments
+// [ll, lh); w bit 0: the remote range is written, bit 1: the local range is written.
+struct Span {
+    uint64_t rl, rh, ll, lh;
+    uint32_t w;
+};
+
+__device__ __forceinline__ Span span_of(uint32_t op, uint64_t remote, uint64_t total, uint64_t lo, uint64_t hi,
+                                        bool moves) {
+    Span s{0, 0, 0, 0, 0};
+    if (!moves) return s;
+    s.rl = remote;
+    s.rh = remote + (is_atomic(op) ? 8 : total);
+    s.ll = lo;
+    s.lh = hi;
+    s.w = op == UGDR_WR_RDMA_READ ? 2u : is_atomic(op) ? 3u : 1u;
+    return s;
+}
+
+__device__ __forceinline__ bool overlap(uint64_t al, uint64_t ah, uint64_t bl, uint64_t bh) {
+    return al < bh && bl < ah;
+}
+
+// True when a and b touch a common byte and at least one of them writes it.
+__device__ __forceinline__ bool clash(const Span &a, const Span &b) {
+    const bool awr = a.w & 1u, awl = a.w & 2u, bwr = b.w & 1u, bwl = b.w & 2u;
+    return (overlap(a.rl, a.rh, b.rl, b.rh) && (awr || bwr)) || (overlap(a.rl, a.rh, b.ll, b.lh) && (awr || bwl)) ||
+           (overlap(a.ll, a.lh, b.rl, b.rh) && (awl || bwr)) || (overlap(a.ll, a.lh, b.ll, b.lh) && (awl || bwl));
+}
+
+__device__ __forceinline__ Span shfl_span(const Span &s, int src) {
+    Span o;
+    o.rl = __shfl_sync(0xffffffffu, (unsigned long long)s.rl, src);
+    o.rh = __shfl_sync(0xffffffffu, (unsigned long long)s.rh, src);
+    o.ll = __shfl_sync(0xffffffffu, (unsigned long long)s.ll, src);
+    o.lh = __shfl_sync(0xffffffffu, (unsigned long long)s.lh, src);
+    o.w = __shfl_sync(0xffffffffu, s.w, src);
+    return o;
+}
+
+// Smallest and largest address any of the warp's spans touches (empty spans excluded).
+__device__ __forceinline__ void span_box(const Span &s, uint64_t *lo, uint64_t *hi) {
+    uint64_t a = ~0ull, b = 0;
+    if (s.rl < s.rh) {
+        a = s.rl;
+        b = s.rh;
+    }
+    if (s.ll < s.lh) {
+        a = s.ll < a ? s.ll : a;
+        b = s.lh > b ? s.lh : b;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const uint64_t ta = __shfl_xor_sync(0xffffffffu, (unsigned long long)a, o);
+        const uint64_t tb = __shfl_xor_sync(0xffffffffu, (unsigned long long)b, o);
+        a = ta < a ? ta : a;
+        b = tb > b ? tb : b;
+    }
+    *lo = a;
+    *hi = b;
+}
+
+// Warp-wide: true on the lanes whose span clashes with a WR of `qp` in [head, issue) (issued,
+// not yet retired; such a WR may still be copying).  Lane k loads WR head + k's record.
+__device__ bool clashes_in_flight(const Warp &w, DevQp *qp, uint64_t head, uint64_t issue, const Span &mine) {
+    const uint32_t m = uint32_t(issue - head);
+    if (m == 0 || __all_sync(0xffffffffu, mine.w == 0)) return false;
+    Span f{0, 0, 0, 0, 0};
+    if (uint32_t(w.lane) < m) {
+        const WrRec *r = &qp->st.win[(head + w.lane) % kWindow];
+        if (ld_vol32(&r->status) == UGDR_WC_SUCCESS)
+            f = span_of(ld_vol32(&r->opcode), ld_vol(&r->remote), ld_vol(&r->total), ld_vol(&r->lo), ld_vol(&r->hi),
+                        true);
+    }
+    // Cheap filter: nothing in flight reaches the addresses this warp's spans touch.
+    uint64_t blo, bhi;
+    span_box(f, &blo, &bhi);
+    const bool near = mine.w != 0 && (overlap(mine.rl, mine.rh, blo, bhi) || overlap(mine.ll, mine.lh, blo, bhi));
+    if (!__any_sync(0xffffffffu, near)) return false;
+    bool hit = false;
+    for (uint32_t k = 0; k < m; ++k) {
+        const Span s = shfl_span(f, int(k));
+        hit |= mine.w != 0 && clash(s, mine);
+    }
+    return hit;
+}
+
+// Warp-wide: true on lane j (< n) when its span clashes with the span of a lane i < j.
+__device__ bool clashes_in_batch(const Warp &w, uint32_t n, const Span &mine) {
+    if (n < 2) return false;
+    // Cheap filter: written ranges ascending and disjoint lane by lane, and the written and read
+    // ranges of the batch in disjoint address boxes.  Both hold for the usual streaming pattern.
+    const uint64_t wl = (mine.w & 1u) ? mine.rl : (mine.w & 2u) ? mine.ll : 0;
+    const uint64_t wh = (mine.w & 1u) ? mine.rh : (mine.w & 2u) ? mine.lh : 0;
+    const uint64_t rl = (mine.w & 1u) ? mine.ll : mine.rl, rh = (mine.w & 1u) ? mine.lh : mine.rh;
+    const bool two_writes = mine.w == 3u;
+    uint64_t pmax = wh;  // inclusive prefix max of written ends, then made exclusive
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint64_t t = __shfl_up_sync(0xffffffffu, (unsigned long long)pmax, o);
+        if (w.lane >= o && t > pmax) pmax = t;
+    }
+    uint64_t prev = __shfl_up_sync(0xffffffffu, (unsigned long long)pmax, 1);
+    if (w.lane == 0) prev = 0;
+    const bool in = uint32_t(w.lane) < n;
+    bool suspect = in && (two_writes || (wl < wh && wl < prev));
+    uint64_t wlo = in && wl < wh ? wl : ~0ull, whi = in && wl < wh ? wh : 0;
+    uint64_t rlo = in && rl < rh ? rl : ~0ull, rhi = in && rl < rh ? rh : 0;
+    for (int o = 16; o > 0; o >>= 1) {
+        uint64_t t = __shfl_xor_sync(0xffffffffu, (unsigned long long)wlo, o);
+        wlo = t < wlo ? t : wlo;
+        t = __shfl_xor_sync(0xffffffffu, (unsigned long long)whi, o);
+        whi = t > whi ? t : whi;
+        t = __shfl_xor_sync(0xffffffffu, (unsigned long long)rlo, o);
+        rlo = t < rlo ? t : rlo;
+        t = __shfl_xor_sync(0xffffffffu, (unsigned long long)rhi, o);
+        rhi = t > rhi ? t : rhi;
+    }
+    if (!__any_sync(0xffffffffu, suspect) && !overlap(wlo, whi, rlo, rhi)) return false;
+    bool hit = false;
+    for (uint32_t i = 0; i + 1 < n; ++i) {
+        const Span s = shfl_span(mine, int(i));
+        hit |= in && uint32_t(w.lane) > i && clash(s, mine);
+    }
+    return hit;
+}
+
 __device__ uint64_t rnr_ns(uint32_t code) {
     constexpr uint32_t t[32] = {65536, 1,    2,    3,    4,    6,    8,     12,    16,   24,   32,
                             48,    64,   96,   128,  192,  256,  384,   512,   768,  1024, 1536,
@@ -724,8 +858,26 @@ __device__ __forceinline__ uint4 ld_mr_part(const DevMr *m, int part) {
 // Validate and stage one WQE (in shared memory) into `rec`.  Warp-wide.  Every global load the
 // checks need (local MRs by lane, the remote MR, the responder's configuration) is issued before
 // any of them is used, so the whole validation costs one memory round trip.
+// Warp-wide minimum / maximum of the lanes' values where `on` holds (~0 / 0 when none).
+__device__ __forceinline__ uint64_t keep_lo(bool on, uint64_t v) {
+    uint64_t a = on ? v : ~0ull;
+    for (int o = 16; o > 0; o >>= 1) {
+        const uint64_t t = __shfl_xor_sync(0xffffffffu, (unsigned long long)a, o);
+        a = t < a ? t : a;
+    }
+    return a;
+}
+__device__ __forceinline__ uint64_t keep_hi(bool on, uint64_t v) {
+    uint64_t a = on ? v : 0;
+    for (int o = 16; o > 0; o >>= 1) {
+        const uint64_t t = __shfl_xor_sync(0xffffffffu, (unsigned long long)a, o);
+        a = t > a ? t : a;
+    }
+    return a;
+}
+
 __device__ void stage_wr(Warp &w, const QpView &v, const uint8_t *wqe, WrRec *rec, uint32_t *status_out,
-                         uint64_t *total_out, uint64_t *remote_out) {
+                         uint64_t *total_out, uint64_t *remote_out, uint64_t *lo_out, uint64_t *hi_out) {
     const queue::SendWqe *h = reinterpret_cast<const queue::SendWqe *>(wqe);
     const uint32_t op = h->opcode;
     const uint32_t nsge = h->sge_count;
@@ -776,6 +928,8 @@ __device__ void stage_wr(Warp &w, const QpView &v, const uint8_t *wqe, WrRec *re
     if (status == UGDR_WC_SUCCESS && total > 0xffffffffull) status = UGDR_WC_LOC_LEN_ERR;  // 4 GiB - 1 max
     if (status == UGDR_WC_SUCCESS && is_atomic(op) && total != 8) status = UGDR_WC_LOC_LEN_ERR;
 
+    // Extent of the local segments (for the ordering rule).
+    uint64_t lo = keep_lo(mine && len != 0 && !bad, local), hi = keep_hi(mine && len != 0 && !bad, local + len);
     // Compact the non-empty segments: lane i keeps slot = prefix count of non-empty lanes.
     const bool keep = mine && len != 0;
     const uint32_t keep_mask = __ballot_sync(0xffffffffu, keep);
@@ -822,11 +976,15 @@ __device__ void stage_wr(Warp &w, const QpView &v, const uint8_t *wqe, WrRec *re
         rec->recv_cqe_done = 0;
         rec->chunks_done = 0;
         rec->nchunks = 0;
+        rec->lo = lo < hi ? lo : 0;
+        rec->hi = lo < hi ? hi : 0;
     }
     __syncwarp();
     *status_out = status;
     *total_out = total;
     *remote_out = remote;
+    *lo_out = lo < hi ? lo : 0;
+    *hi_out = lo < hi ? hi : 0;
 }
 
 // Execute an inline WR (small payload or atomic) with the owner warp.  No fence here: the issue
@@ -1019,9 +1177,9 @@ struct LaneWr {
     uint32_t status, op, signaled;
 };
 
-__device__ uint32_t issue_fast(Warp &w, DevQp *qp, const QpView &v, const uint8_t *wqe_smem, uint64_t issue0,
-                               uint32_t avail, LaneWr *out, JobRing *jr, uint32_t *bitmap, uint32_t nwarps,
-                               bool *chunked_out) {
+__device__ uint32_t issue_fast(Warp &w, DevQp *qp, const QpView &v, const uint8_t *wqe_smem, uint64_t head,
+                               uint64_t issue0, uint32_t avail, LaneWr *out, JobRing *jr, uint32_t *bitmap,
+                               uint32_t nwarps, bool *chunked_out) {
     *chunked_out = false;
     const uint32_t j = uint32_t(w.lane);
     const bool in = j < avail;
@@ -1117,6 +1275,17 @@ __device__ uint32_t issue_fast(Warp &w, DevQp *qp, const QpView &v, const uint8_
     }
     const uint32_t err_mask = __ballot_sync(0xffffffffu, act && status != UGDR_WC_SUCCESS);
     uint32_t count = err_mask ? __ffs(err_mask) : p;  // through the first error, inclusive
+    // --- ordering: stop before the first WR that touches bytes an earlier one may still move ---
+    {
+        const Span sp = span_of(op, remote, len, local, local + len, j < count && status == UGDR_WC_SUCCESS && len != 0);
+        const bool c = clashes_in_batch(w, count, sp);
+        const bool f = clashes_in_flight(w, qp, head, issue0, sp);
+        const uint32_t clash_mask = __ballot_sync(0xffffffffu, j < count && (c || f));
+        if (clash_mask) {
+            count = __ffs(clash_mask) - 1;
+            if (count == 0) return 0;
+        }
+    }
     // --- chunked WRs: one job for the batch; its slot is taken before anything runs ---
     bool chunked = j < count && status == UGDR_WC_SUCCESS && len > kLaneBytes;
     uint32_t chunk_mask = __ballot_sync(0xffffffffu, chunked);
@@ -1174,6 +1343,8 @@ __device__ uint32_t issue_fast(Warp &w, DevQp *qp, const QpView &v, const uint8_
         rec->nseg = len != 0 ? 1 : 0;
         rec->seg[0].local = local;
         rec->seg[0].length = len;
+        rec->lo = len != 0 ? local : 0;
+        rec->hi = len != 0 ? local + len : 0;
         rec->recv_cqe_done = 0;
         rec->chunks_done = 0;
         rec->nchunks = nch;
@@ -1343,7 +1514,8 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
     const uint64_t t_fetch1 = gtime();
     LaneWr lw{0, 0, 0, 0, 0};
     bool fast_chunked = false;
-    uint64_t issued = issue_fast(w, qp, v, wqe_smem, issue0, uint32_t(avail), &lw, jr, bitmap, nwarps, &fast_chunked);
+    uint64_t issued = issue_fast(w, qp, v, wqe_smem, head, issue0, uint32_t(avail), &lw, jr, bitmap, nwarps,
+                                 &fast_chunked);
     const uint32_t fast_n = uint32_t(issued);
     if (issued > 0) {
         inline_ran += uint32_t(issued);
@@ -1356,12 +1528,17 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
         const uint8_t *wqe = wqe_smem + j * v.sq_stride;
         WrRec *rec = &qp->st.win[issue % kWindow];
         uint32_t status;
-        uint64_t total, remote;
+        uint64_t total, remote, lo, hi;
         const uint64_t t_stage = gtime();
-        stage_wr(w, v, wqe, rec, &status, &total, &remote);
+        stage_wr(w, v, wqe, rec, &status, &total, &remote, &lo, &hi);
         const queue::SendWqe *h = reinterpret_cast<const queue::SendWqe *>(wqe);
         const uint32_t op = h->opcode;
         const bool signaled = v.sig_all || (h->send_flags & UGDR_SEND_SIGNALED) != 0;
+        // Ordering: wait (a later pass) while an earlier WR still in flight touches its bytes.
+        if (__any_sync(0xffffffffu,
+                       clashes_in_flight(w, qp, head, issue,
+                                         span_of(op, remote, total, lo, hi, status == UGDR_WC_SUCCESS))))
+            break;
 
         // A WR that becomes a job takes its job slot first: with no slot free the WR waits for a
         // later pass before anything (an RQ claim, a copy) has been done for it.
