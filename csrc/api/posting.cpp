@@ -13,7 +13,7 @@ bool is_atomic(uint32_t op) {
 // Opcodes a send WQE may carry, as a bit mask over the opcode value.
 constexpr uint32_t kSendOpMask = (1u << UGDR_WR_RDMA_WRITE) | (1u << UGDR_WR_RDMA_WRITE_WITH_IMM) |
                                  (1u << UGDR_WR_RDMA_READ) | (1u << UGDR_WR_ATOMIC_CMP_AND_SWP) |
-                                 (1u << UGDR_WR_ATOMIC_FETCH_AND_ADD);
+                                 (1u << UGDR_WR_ATOMIC_FETCH_AND_ADD) | (1u << UGDR_X_WR_RDMA_WRITE_SUM_BF16);
 
 inline bool send_ok(const ugdr_send_wr &wr, uint32_t max_sge) {
     const uint32_t op = uint32_t(wr.opcode);

@@ -236,6 +236,18 @@ size_t CpuEngine::progress_qp(QpView &v) {
             segs[nseg++] = Seg{p, sg.length};
         }
         if (status == UGDR_WC_SUCCESS && op_atomic(op) && total != 8) status = UGDR_WC_LOC_LEN_ERR;
+        if (status == UGDR_WC_SUCCESS && op_sum(op) && h.sge_count > 0) {
+            // Every SGE has the same even length L; the WR moves L bytes.
+            queue::Sge first;
+            std::memcpy(&first, slot + queue::kSendSgeOffset, sizeof(first));
+            for (uint32_t i = 0; i < h.sge_count && status == UGDR_WC_SUCCESS; ++i) {
+                queue::Sge sg;
+                std::memcpy(&sg, slot + queue::kSendSgeOffset + i * sizeof(queue::Sge), sizeof(sg));
+                if (sg.length != first.length || (sg.length & 1u) != 0) status = UGDR_WC_LOC_LEN_ERR;
+                else if ((sg.address & 1u) != 0) status = UGDR_WC_LOC_PROT_ERR;
+            }
+            total = first.length;
+        }
 
         control::Qp *peer = qp.peer;
         uint8_t *remote = nullptr;
@@ -257,6 +269,8 @@ size_t CpuEngine::progress_qp(QpView &v) {
                     status = UGDR_WC_REM_ACCESS_ERR;
                 }
                 if (status == UGDR_WC_SUCCESS && op_atomic(op) && (h.remote_address & 7) != 0)
+                    status = UGDR_WC_REM_INV_REQ_ERR;
+                if (status == UGDR_WC_SUCCESS && op_sum(op) && (h.remote_address & 1) != 0)
                     status = UGDR_WC_REM_INV_REQ_ERR;
             }
         }
@@ -295,7 +309,20 @@ size_t CpuEngine::progress_qp(QpView &v) {
         if (need_cqe && qp.send_cq->ring.reserve(1).count() == 0) break;
 
         if (status == UGDR_WC_SUCCESS) {
-            if (op == UGDR_WR_RDMA_WRITE || op == UGDR_WR_RDMA_WRITE_WITH_IMM) {
+            if (op_sum(op)) {
+                // Element by element: every input element is read before its output is written,
+                // so the remote range may be one of the SGEs.
+                for (uint64_t e = 0; e < total / 2; ++e) {
+                    float acc = 0.f;
+                    for (uint32_t i = 0; i < nseg; ++i) {
+                        uint16_t x;
+                        std::memcpy(&x, segs[i].local + 2 * e, 2);
+                        acc += bf16_to_f32(x);
+                    }
+                    const uint16_t r = bf16_rne(acc);
+                    std::memcpy(remote + 2 * e, &r, 2);
+                }
+            } else if (op == UGDR_WR_RDMA_WRITE || op == UGDR_WR_RDMA_WRITE_WITH_IMM) {
                 uint64_t off = 0;
                 for (uint32_t i = 0; i < nseg; ++i) {
                     copy_bytes(remote + off, segs[i].local, segs[i].length);

@@ -15,7 +15,25 @@ namespace ugdr::engine {
 
 inline bool op_known(uint32_t op) {
     return op == UGDR_WR_RDMA_WRITE || op == UGDR_WR_RDMA_WRITE_WITH_IMM || op == UGDR_WR_RDMA_READ ||
-           op == UGDR_WR_ATOMIC_CMP_AND_SWP || op == UGDR_WR_ATOMIC_FETCH_AND_ADD;
+           op == UGDR_WR_ATOMIC_CMP_AND_SWP || op == UGDR_WR_ATOMIC_FETCH_AND_ADD ||
+           op == UGDR_X_WR_RDMA_WRITE_SUM_BF16;
+}
+inline bool op_sum(uint32_t op) { return op == UGDR_X_WR_RDMA_WRITE_SUM_BF16; }
+
+// fp32 -> bf16, round to nearest even (quiet NaN kept).  Plain IEEE-754 arithmetic on the bit
+// pattern: add half an ulp of the bf16 result (plus the tie-to-even bit) and truncate.
+inline uint16_t bf16_rne(float f) {
+    uint32_t u;
+    __builtin_memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return uint16_t((u >> 16) | 0x40u);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return uint16_t(u >> 16);
+}
+inline float bf16_to_f32(uint16_t h) {
+    const uint32_t u = uint32_t(h) << 16;
+    float f;
+    __builtin_memcpy(&f, &u, 4);
+    return f;
 }
 inline bool op_atomic(uint32_t op) {
     return op == UGDR_WR_ATOMIC_CMP_AND_SWP || op == UGDR_WR_ATOMIC_FETCH_AND_ADD;

@@ -32,6 +32,7 @@
 #include "gpu/executor.hpp"
 #include "ugdr/api.hpp"
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -288,6 +289,81 @@ __device__ __noinline__ void copy_stream(const WrRec *rec, uint32_t nseg, uint64
             len -= take;
         }
         seg_start += sl;
+    }
+}
+
+// ---- elementwise bf16 sum (UGDR_X_WR_RDMA_WRITE_SUM_BF16) ----------------------------------------
+// Bytes [off, off + len) of the destination get the fp32 sum, in SGE order, of the same bytes of
+// every segment (all segments have the WR's length), rounded to bf16.  Each lane reads all inputs
+// of its elements before it writes them, so the destination may be one of the segments.
+
+__device__ __forceinline__ void acc_bf16x2(float &lo, float &hi, uint32_t x) {
+    lo += __uint_as_float(x << 16);
+    hi += __uint_as_float(x & 0xffff0000u);
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&v);
+}
+
+__device__ __noinline__ void sum_stream(const WrRec *rec, uint32_t nseg, uint64_t remote, uint64_t off,
+                                        uint64_t len, int lane) {
+    // Lane i holds segment i's source address at `off`; the others come by shuffle.
+    const uint64_t mine =
+        uint32_t(lane) < nseg
+            ? uint64_t(__ldcg(reinterpret_cast<const unsigned long long *>(&rec->seg[lane].local))) + off
+            : 0;
+    uint8_t *dst = reinterpret_cast<uint8_t *>(remote) + off;
+    const uint32_t misaligned =
+        __ballot_sync(0xffffffffu, (uint32_t(lane) < nseg && (mine & 15) != 0) || (lane == 0 && (uintptr_t(dst) & 15)));
+    const uint64_t nvec = misaligned ? 0 : len >> 4;
+    uint64_t v = lane;
+    for (; v + 32 < nvec; v += 64) {  // two vectors per lane in flight
+        float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, b[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (uint32_t i = 0; i < nseg; ++i) {
+            const uint8_t *src = reinterpret_cast<const uint8_t *>(__shfl_sync(0xffffffffu, (unsigned long long)mine, i));
+            const uint4 x = ld128(src + v * 16), y = ld128(src + (v + 32) * 16);
+            acc_bf16x2(a[0], a[1], x.x);
+            acc_bf16x2(a[2], a[3], x.y);
+            acc_bf16x2(a[4], a[5], x.z);
+            acc_bf16x2(a[6], a[7], x.w);
+            acc_bf16x2(b[0], b[1], y.x);
+            acc_bf16x2(b[2], b[3], y.y);
+            acc_bf16x2(b[4], b[5], y.z);
+            acc_bf16x2(b[6], b[7], y.w);
+        }
+        st128(dst + v * 16, make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]), pack_bf16x2(a[4], a[5]),
+                                       pack_bf16x2(a[6], a[7])));
+        st128(dst + (v + 32) * 16, make_uint4(pack_bf16x2(b[0], b[1]), pack_bf16x2(b[2], b[3]),
+                                              pack_bf16x2(b[4], b[5]), pack_bf16x2(b[6], b[7])));
+    }
+    for (; v < nvec; v += 32) {
+        float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (uint32_t i = 0; i < nseg; ++i) {
+            const uint8_t *src = reinterpret_cast<const uint8_t *>(__shfl_sync(0xffffffffu, (unsigned long long)mine, i));
+            const uint4 x = ld128(src + v * 16);
+            acc_bf16x2(a[0], a[1], x.x);
+            acc_bf16x2(a[2], a[3], x.y);
+            acc_bf16x2(a[4], a[5], x.z);
+            acc_bf16x2(a[6], a[7], x.w);
+        }
+        st128(dst + v * 16, make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]), pack_bf16x2(a[4], a[5]),
+                                       pack_bf16x2(a[6], a[7])));
+    }
+    // Tail, or everything when an address is not 16-byte aligned: 2-byte elements.  The loop
+    // bound is uniform over the warp so every lane reaches each shuffle.
+    const uint64_t e0 = (nvec << 4) >> 1, ne = len >> 1;
+    for (uint64_t base = e0; base < ne; base += 32) {
+        const uint64_t e = base + lane;
+        float acc = 0.f;
+        for (uint32_t i = 0; i < nseg; ++i) {
+            const uint8_t *src = reinterpret_cast<const uint8_t *>(__shfl_sync(0xffffffffu, (unsigned long long)mine, i));
+            if (e < ne) acc += __uint_as_float(uint32_t(*reinterpret_cast<const uint16_t *>(src + 2 * e)) << 16);
+        }
+        if (e < ne) {
+            const __nv_bfloat16 r = __float2bfloat16_rn(acc);
+            *reinterpret_cast<__nv_bfloat16 *>(dst + 2 * e) = r;
+        }
     }
 }
 
@@ -813,7 +889,10 @@ __device__ void run_chunk(Warp &w, const Claim &cl) {
     const uint32_t nseg = ld_vol32(&rec->nseg);
     const uint64_t remote = ld_vol(&rec->remote);
     const uint64_t t0 = gtime();
-    copy_stream(rec, nseg, remote, op != UGDR_WR_RDMA_READ, off, len, w.lane);
+    if (op == UGDR_X_WR_RDMA_WRITE_SUM_BF16)
+        sum_stream(rec, nseg, remote, off, len, w.lane);
+    else
+        copy_stream(rec, nseg, remote, op != UGDR_WR_RDMA_READ, off, len, w.lane);
     __syncwarp();
     if (w.lane == 0) {
         // Device-scope release is enough here: the owner warp acquires chunks_done and issues
@@ -882,8 +961,9 @@ __device__ void stage_wr(Warp &w, const QpView &v, const uint8_t *wqe, WrRec *re
     const uint32_t op = h->opcode;
     const uint32_t nsge = h->sge_count;
     uint32_t status = UGDR_WC_SUCCESS;
+    const bool sum = op == UGDR_X_WR_RDMA_WRITE_SUM_BF16;
     const bool op_ok = op == UGDR_WR_RDMA_WRITE || op == UGDR_WR_RDMA_WRITE_WITH_IMM ||
-                       op == UGDR_WR_RDMA_READ || is_atomic(op);
+                       op == UGDR_WR_RDMA_READ || is_atomic(op) || sum;
     if (!op_ok || nsge > v.max_sge || nsge > kMaxSge || (is_atomic(op) && nsge != 1))
         status = UGDR_WC_LOC_QP_OP_ERR;
     const bool mine = status == UGDR_WC_SUCCESS && uint32_t(w.lane) < nsge;
@@ -927,6 +1007,15 @@ __device__ void stage_wr(Warp &w, const QpView &v, const uint8_t *wqe, WrRec *re
     if (status == UGDR_WC_SUCCESS && any_bad) status = UGDR_WC_LOC_PROT_ERR;
     if (status == UGDR_WC_SUCCESS && total > 0xffffffffull) status = UGDR_WC_LOC_LEN_ERR;  // 4 GiB - 1 max
     if (status == UGDR_WC_SUCCESS && is_atomic(op) && total != 8) status = UGDR_WC_LOC_LEN_ERR;
+    if (status == UGDR_WC_SUCCESS && sum && nsge > 0) {
+        // Every SGE has the same even length L, at a 2-byte aligned address; the WR moves L bytes.
+        const uint64_t l0 = __shfl_sync(0xffffffffu, len, 0);
+        const bool len_bad = mine && (len != l0 || (len & 1) != 0);
+        const bool addr_bad = mine && (sg->address & 1) != 0;
+        if (__any_sync(0xffffffffu, len_bad)) status = UGDR_WC_LOC_LEN_ERR;
+        else if (__any_sync(0xffffffffu, addr_bad)) status = UGDR_WC_LOC_PROT_ERR;
+        total = l0;
+    }
 
     // Extent of the local segments (for the ordering rule).
     uint64_t lo = keep_lo(mine && len != 0 && !bad, local), hi = keep_hi(mine && len != 0 && !bad, local + len);
@@ -962,6 +1051,7 @@ __device__ void stage_wr(Warp &w, const QpView &v, const uint8_t *wqe, WrRec *re
                     remote = base + (ra - cb);
                 if (status == UGDR_WC_SUCCESS && is_atomic(op) && (ra & 7) != 0)
                     status = UGDR_WC_REM_INV_REQ_ERR;
+                if (status == UGDR_WC_SUCCESS && sum && (ra & 1) != 0) status = UGDR_WC_REM_INV_REQ_ERR;
             }
         }
     }
@@ -1011,7 +1101,9 @@ __device__ void run_inline(Warp &w, WrRec *rec, const uint8_t *wqe, uint32_t op,
         return;
     }
     const uint32_t nseg = rec->nseg;
-    if (nseg == 1 && total <= 16 && op != UGDR_WR_RDMA_READ) {
+    if (op == UGDR_X_WR_RDMA_WRITE_SUM_BF16) {
+        sum_stream(rec, nseg, remote, 0, total, w.lane);
+    } else if (nseg == 1 && total <= 16 && op != UGDR_WR_RDMA_READ) {
         // Tiny payload: one lane per byte, no vector setup.
         const uint8_t *src = reinterpret_cast<const uint8_t *>(rec->seg[0].local);
         if (uint64_t(w.lane) < total) reinterpret_cast<uint8_t *>(remote)[w.lane] = src[w.lane];

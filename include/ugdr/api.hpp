@@ -69,6 +69,14 @@ typedef enum ugdr_wr_opcode {
     UGDR_WR_RDMA_READ = 4,
     UGDR_WR_ATOMIC_CMP_AND_SWP = 5,
     UGDR_WR_ATOMIC_FETCH_AND_ADD = 6,
+    /* Extension (no libibverbs counterpart): RDMA WRITE of an elementwise bf16 sum.  The WR's
+     * n >= 1 SGEs all have the same even length L; the remote range [remote_addr, +L) receives,
+     * element by element, the bf16 (round to nearest even) of the fp32 sum of the n SGEs' bf16
+     * elements, added in SGE order.  Every address is 2-byte aligned.  The remote range may be
+     * one of the SGEs (in place).  Needs REMOTE_WRITE; completes as UGDR_WC_RDMA_WRITE with
+     * byte_len L.  Unequal or odd lengths give UGDR_WC_LOC_LEN_ERR, a misaligned local address
+     * UGDR_WC_LOC_PROT_ERR, a misaligned remote address UGDR_WC_REM_INV_REQ_ERR. */
+    UGDR_X_WR_RDMA_WRITE_SUM_BF16 = 24,
 } ugdr_wr_opcode;
 
 typedef enum ugdr_send_flags {

@@ -33,6 +33,7 @@ WR_RDMA_WRITE_WITH_IMM = 1
 WR_RDMA_READ = 4
 WR_ATOMIC_CMP_AND_SWP = 5
 WR_ATOMIC_FETCH_AND_ADD = 6
+WR_X_RDMA_WRITE_SUM_BF16 = 24  # extension: WRITE of the elementwise bf16 sum of the SGEs
 SEND_SIGNALED = 1 << 1
 
 WC_SUCCESS = 0
