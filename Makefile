@@ -19,7 +19,8 @@ LIB_CXX := \
   csrc/api/posting.cpp csrc/api/runtime.cpp csrc/api/memory_export.cpp \
   csrc/engine/cpu_engine.cpp csrc/gpu/cuda_memory.cpp csrc/gpu/gpu_engine.cpp csrc/gpu/diag.cpp \
   csrc/gpu/visibility.cpp csrc/gpu/trace_writer.cpp \
-  csrc/daemon/daemon.cpp csrc/collective/api.cpp csrc/collective/nvls.cpp
+  csrc/daemon/daemon.cpp csrc/collective/api.cpp csrc/collective/nvls.cpp \
+  csrc/collective/verbs_allreduce.cpp
 LIB_CU  := csrc/gpu/executor.cu csrc/gpu/bulk_copy.cu csrc/collective/kernels.cu csrc/collective/route_noalloc.cu
 
 LIB_OBJS := $(LIB_CXX:csrc/%.cpp=$(OBJ)/%.o) $(LIB_CU:csrc/%.cu=$(OBJ)/%.cu.o)
@@ -102,7 +103,7 @@ tsan: $(SAN)/tsan/ugdr_native_tests $(SAN)/tsan/ugdr_daemon
 PREFIX ?= /usr/local
 install: all
 	install -d $(DESTDIR)$(PREFIX)/include/ugdr $(DESTDIR)$(PREFIX)/lib/pkgconfig $(DESTDIR)$(PREFIX)/bin
-	install -m 644 include/ugdr/api.hpp include/ugdr/collective.h include/ugdr/route_noalloc.h $(DESTDIR)$(PREFIX)/include/ugdr/
+	install -m 644 include/ugdr/api.hpp include/ugdr/collective.h include/ugdr/route_noalloc.h include/ugdr/verbs_collective.h $(DESTDIR)$(PREFIX)/include/ugdr/
 	install -m 755 $(OUT)/libugdr.so $(DESTDIR)$(PREFIX)/lib/
 	install -m 755 $(OUT)/ugdr_daemon $(OUT)/ugdr_client $(OUT)/ugdr_perf $(OUT)/ugdr_engine_bench $(DESTDIR)$(PREFIX)/bin/
 	printf 'prefix=%s\nlibdir=$${prefix}/lib\nincludedir=$${prefix}/include\n\nName: ugdr\nDescription: Userspace GPU RDMA verbs over NVLink (libibverbs-shaped C API)\nVersion: 1.0.0\nCflags: -I$${includedir}\nLibs: -L$${libdir} -Wl,-rpath,$${libdir} -lugdr\n' '$(PREFIX)' > $(DESTDIR)$(PREFIX)/lib/pkgconfig/ugdr.pc

@@ -1,0 +1,77 @@
+/* Collectives built on the ugdr verbs: every byte moves as an RDMA WRITE work request that the
+ * daemon's persistent executors run, the reduction is the UGDR_X_WR_RDMA_WRITE_SUM_BF16 opcode
+ * (the sum is done by the executor while it writes the result), and ranks signal each other with
+ * WRITE_WITH_IMM receive completions.  No counterpart in the reference (it has no collectives);
+ * they use only its public object model: registered MRs, connected RC QPs, one CQ.
+ *
+ * A group is wired by the caller (see ugdr_b200.parallel.verbs_collectives for a torch
+ * version): each rank opens a context on its GPU, creates one CQ, registers its data buffer and
+ * a staging buffer, creates per peer one QP that writes to that peer (`to`) and one that the
+ * peer writes through (`from`, whose receive queue takes the peer's immediates), plus a
+ * connected loopback pair on its own GPU (`self_to`), and exchanges addresses and rkeys.
+ *
+ * Sizes: the send queues of `to` and `self_to` hold at least 2 x pieces WRs, the receive queue
+ * of each `from` QP at least 2 x pieces WRs, max_send_sge of `self_to` is at least n, and the CQ
+ * has room for 2 x pieces x (n - 1) + pieces + n entries. */
+#pragma once
+
+#include "ugdr/api.hpp"
+
+#ifdef __cplusplus
+#define UGDR_VC_NOEXCEPT noexcept
+extern "C" {
+#else
+#define UGDR_VC_NOEXCEPT
+#endif
+
+#define UGDR_X_VGROUP_MAX_RANKS 8
+
+typedef struct ugdr_x_vgroup_peer {
+    ugdr_qp *to;         /* connected to this peer's `from` QP for our rank */
+    ugdr_qp *from;       /* connected to this peer's `to` QP for our rank */
+    uint64_t buf_addr;   /* the peer's data buffer */
+    uint32_t buf_rkey;
+    uint32_t stage_rkey;
+    uint64_t stage_addr; /* the peer's staging buffer */
+} ugdr_x_vgroup_peer;
+
+typedef struct ugdr_x_vgroup {
+    int rank;
+    int n;
+    ugdr_cq *cq;          /* send and receive CQ of every QP of the group */
+    ugdr_qp *self_to;     /* loopback QP on this rank's GPU (connected to a local peer QP) */
+    uint64_t buf_addr;    /* this rank's data buffer (registered as buf_lkey / buf_rkey) */
+    uint32_t buf_lkey;
+    uint32_t buf_rkey;
+    uint64_t stage_addr;  /* n x shard-size bytes (registered as stage_lkey) */
+    uint32_t stage_lkey;
+    uint32_t pad;
+    uint64_t stage_bytes;
+    uint32_t epoch;       /* calls made so far (tags the immediates); start at 0 */
+    uint32_t pad2;
+    ugdr_x_vgroup_peer peer[UGDR_X_VGROUP_MAX_RANKS]; /* index = peer rank; own entry unused */
+} ugdr_x_vgroup;
+
+/* Staging bytes an allreduce of `count` bf16 elements over n ranks needs. */
+uint64_t ugdr_x_verbs_allreduce_stage_bytes(uint64_t count, int n) UGDR_VC_NOEXCEPT;
+
+/* In-place sum of `count` bf16 elements at buf_addr over the group (fp32 accumulation), as a
+ * reduce-scatter and an all-gather of WRs, pipelined in `pieces` pieces per shard:
+ *   1. rank r WRITE_WITH_IMMs piece m of shard q into rank q's staging slot r;
+ *   2. once a piece of its shard arrived from every peer, rank r posts one WRITE_SUM_BF16 on
+ *      its loopback QP whose n SGEs are the ranks' pieces in rank order (its own in place, the
+ *      others staged), written in place over its own piece, so each element is the fp32 sum
+ *      x_0 + ... + x_{n-1} rounded to bf16 once;
+ *   3. when that sum completes, rank r WRITE_WITH_IMMs the piece to every peer's buffer.
+ * Every rank calls it with the same count and pieces.  Blocks until this rank's part is done
+ * (its buffer holds the sum and its WRs retired).  Each call first posts its own receives; a
+ * peer that runs ahead waits in RNR (the `to` QPs need rnr_retry 7) until they are posted, so
+ * no call's data lands in a buffer still in use by the previous one.  Returns 0, EINVAL,
+ * ETIMEDOUT (nothing for timeout_ns), EIO (an error completion) or an errno of the verbs calls. */
+int ugdr_x_verbs_allreduce_bf16(ugdr_x_vgroup *g, uint64_t count, int pieces,
+                                uint64_t timeout_ns) UGDR_VC_NOEXCEPT;
+
+#ifdef __cplusplus
+}
+#endif
+#undef UGDR_VC_NOEXCEPT

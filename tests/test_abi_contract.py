@@ -69,7 +69,7 @@ def _compile_and_run(src: str) -> str:
 
 def _probe() -> dict:
     lines = ['#include <stddef.h>', '#include <stdio.h>', '#include "ugdr/api.hpp"', '#include "ugdr/collective.h"',
-             '#include "ugdr/route_noalloc.h"', "int main(void) {"]
+             '#include "ugdr/route_noalloc.h"', '#include "ugdr/verbs_collective.h"', "int main(void) {"]
     for name in IBV_VALUES:
         lines.append(f'    printf("{name} %lld\\n", (long long){name});')
     for st, fields in STRUCTS.items():
@@ -146,10 +146,10 @@ def _declared_functions() -> set[str]:
     import re
 
     names = set()
-    for h in ("api.hpp", "collective.h", "route_noalloc.h"):
+    for h in ("api.hpp", "collective.h", "route_noalloc.h", "verbs_collective.h"):
         with open(os.path.join(REPO, "include", "ugdr", h)) as f:
             text = re.sub(r"/\*.*?\*/|//[^\n]*", "", f.read(), flags=re.S)
-        names |= set(re.findall(r"\b(ugdr_[a-z0-9_]+)\s*\([^;{]*\)\s*(?:noexcept\s*)?(?:UGDR_NOEXCEPT\s*)?;", text))
+        names |= set(re.findall(r"\b(ugdr_[a-z0-9_]+)\s*\([^;{]*\)\s*(?:noexcept\s*)?(?:UGDR_[A-Z_]*NOEXCEPT\s*)?;", text))
     return names
 
 

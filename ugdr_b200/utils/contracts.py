@@ -31,7 +31,7 @@ import sys
 from pathlib import Path
 
 FIELDS = {"schema_version", "library", "documentation", "compatible_symbols", "headers"}
-_DECL = re.compile(r"\b(ugdr_[a-z0-9_]+)\s*\([^;{]*\)\s*(?:noexcept\s*)?(?:UGDR_NOEXCEPT\s*)?;")
+_DECL = re.compile(r"\b(ugdr_[a-z0-9_]+)\s*\([^;{]*\)\s*(?:noexcept\s*)?(?:UGDR_[A-Z_]*NOEXCEPT\s*)?;")
 _COMMENT = re.compile(r"/\*.*?\*/|//[^\n]*", re.S)
 
 
