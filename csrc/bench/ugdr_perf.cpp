@@ -257,10 +257,12 @@ int run_bw(const Opts &o) {
             // reference's client benchmark does with its post chains.
             uint32_t nchain = 0;
             while (posted + nchain < wrs && posted + nchain - done < qd) {
-                // Each in-flight WR uses its own destination slice when it fits, else the start.
+                // WRs rotate over the buffer's sz-byte slices.  A QP's WRs take effect in posting
+                // order, so two in flight on the same slice would run one after the other; with
+                // at least 32 slices (the executor's per-QP window) none ever waits for another.
                 const uint64_t w = posted + nchain;
-                const uint64_t slot = (w % qd) * sz;
-                const uint64_t off = slot + sz <= o.max_bytes ? slot : 0;
+                const uint64_t nslices = std::max<uint64_t>(1, o.max_bytes / sz);
+                const uint64_t off = (w % nslices) * sz;
                 chain_sge[nchain] = ugdr_sge{reinterpret_cast<uint64_t>(static_cast<uint8_t *>(a.buf) + off),
                                              uint32_t(sz), a.mr->lkey};
                 ugdr_send_wr &wr = chain[nchain];

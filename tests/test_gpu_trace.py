@@ -52,6 +52,6 @@ def test_trace_records_batches_and_chunks(tmp_path):
         assert "chunk" in names and ({"fast_batch", "retire"} & names)
         assert all(e["dur"] >= 0 and e["ts"] >= 0 for e in ev)
         # Every WR above 64 B is copied in chunks: the 64 small ones and the large one.
-            assert sum(e["args"]["value"] for e in ev if e["name"] == "chunk") == n + 64 * 256
+        assert sum(e["args"]["value"] for e in ev if e["name"] == "chunk") == n + 64 * 256
         with pytest.raises(V.UgdrError):  # off again: nothing to dump
             ctx.trace_dump(str(path))

@@ -1,7 +1,7 @@
 """Collectives benchmark - launch one rank per GPU:
 
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \\
-        -m ugdr_b200.parallel.bench [--op allreduce|moe|p2p|all] [--iters K] [--warmup W]
+        -m ugdr_b200.parallel.bench [--op allreduce|moe|p2p|all] [--api peer|verbs|both] [--iters K]
 
 * allreduce: 1 GiB bf16 per rank, N(0,1) seeded by rank; ugdr's one-kernel fused-sum allreduce
   over peer memory and (N >= 2, when the GPUs support multicast) its NVLS allreduce that sums in
@@ -122,6 +122,74 @@ def bench_allreduce(rank, world, iters, warmup, nbytes=1 << 30, impl="all", ctas
     return out
 
 
+def bench_allreduce_verbs(rank, world, local, iters, warmup, nbytes=1 << 30, pieces=8) -> dict:
+    """The allreduce on the verbs API (ugdr_x_verbs_allreduce_bf16): every byte is a WR that the
+    daemon's executor on the rank's GPU runs, the sum is the executor's WRITE_SUM_BF16.  Checked
+    bit for bit on a 1 Mi-element window against the fp32 sum of the seeded inputs rounded once.
+    Timed two ways, max over ranks: the executor's own span on the GPU (from the last retire of
+    the call before the timed ones to the last retire of the last one, %globaltimer, from the
+    engine statistics) and the caller's wall clock per call."""
+    import time
+
+    from . import verbs_collectives as VC
+
+    count = nbytes // 2
+
+    def exchange(obj):
+        out = [None] * world
+        dist.all_gather_object(out, obj, group=_GLOO)
+        return out
+
+    def bcast(obj):
+        lst = [obj]
+        dist.broadcast_object_list(lst, src=0, group=_GLOO)
+        return lst[0]
+
+    daemon = VC.shared_daemon(rank, world, bcast)
+    g = VC.VerbsGroup(rank, world, local, count, exchange, pieces=pieces)
+    try:
+        gen = torch.Generator(device="cuda").manual_seed(rank)
+        g.buf.copy_(torch.randn(count, generator=gen, device="cuda", dtype=torch.float32).to(torch.bfloat16))
+        lo = (count // 3) // 8 * 8
+        ref = torch.zeros(1 << 20, dtype=torch.float32, device="cuda")
+        for r in range(world):
+            gr = torch.Generator(device="cuda").manual_seed(r)
+            ref += torch.randn(count, generator=gr, device="cuda", dtype=torch.float32).to(torch.bfloat16)[
+                lo:lo + (1 << 20)].float()
+        torch.cuda.synchronize()
+        dist.barrier(group=_GLOO)
+        g.allreduce()
+        exact = bool(torch.equal(g.buf[lo:lo + (1 << 20)], ref.to(torch.bfloat16)))
+        for _ in range(warmup):
+            g.allreduce()
+        dist.barrier(group=_GLOO)
+        g.allreduce()  # its last retire opens the timed span on the executor's clock
+        st0 = g.ctx.stats()
+        t0 = time.perf_counter()
+        for _ in range(iters):
+            g.allreduce()
+        wall = (time.perf_counter() - t0) / iters * 1e3
+        st = g.ctx.stats()
+        dev = (int(st.last_end_ns) - int(st0.last_end_ns)) / 1e6 / iters
+        t = torch.tensor([wall, dev], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=_GLOO)
+        wall, dev = float(t[0]), float(t[1])
+        dist.barrier(group=_GLOO)
+    finally:
+        g.close()
+        dist.barrier(group=_GLOO)
+        if daemon is not None:
+            daemon.stop()
+    bus = 2 * (world - 1) / world if world > 1 else 1.0
+    return {"op": "allreduce_bf16_verbs", "n_gpus": world, "bytes": nbytes, "pieces": pieces,
+            "ugdr_verbs_ms": round(dev, 4), "ugdr_verbs_wall_ms": round(wall, 4),
+            "ugdr_verbs_algbw_GBps": round(nbytes / dev / 1e6, 1),
+            "ugdr_verbs_busbw_GBps": round(bus * nbytes / dev / 1e6, 1),
+            "correct_exact": exact,
+            "timing": "executor span on the GPU (last retire of the previous call to last retire of the last "
+                      "call) per call, and wall clock per call; max over ranks"}
+
+
 def bench_p2p_nccl(rank, world, sizes, iters, warmup) -> list[dict]:
     """NCCL send/recv baseline for the point-to-point WRITE / READ sweep: rank 0 sends
     `size` bytes to rank 1, `iters` transfers back to back, device-timed, max over the pair."""
@@ -215,6 +283,10 @@ def main():
     ap.add_argument("--ar-impl", default="all", choices=["all", "ring", "nvls"],
                     help="allreduce paths to time (all: ring, NVLS when available, and NCCL)")
     ap.add_argument("--ctas", type=int, default=0, help="allreduce grid size (0: one CTA per SM)")
+    ap.add_argument("--api", default="peer", choices=["peer", "verbs", "both"],
+                    help="allreduce over peer-mapped buffers (one kernel), over the verbs (WRs run by the "
+                         "daemon's executors), or both")
+    ap.add_argument("--pieces", type=int, default=8, help="verbs allreduce: pipeline pieces per shard")
     args = ap.parse_args()
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -223,8 +295,18 @@ def main():
     _GLOO = dist.new_group(backend="gloo")
     results = []
     if args.op in ("all", "allreduce"):
-        results.append(bench_allreduce(rank, world, args.iters, args.warmup, args.ar_mib << 20, args.ar_impl,
-                                       args.ctas))
+        if args.api in ("peer", "both"):
+            results.append(bench_allreduce(rank, world, args.iters, args.warmup, args.ar_mib << 20, args.ar_impl,
+                                           args.ctas))
+        if args.api in ("verbs", "both"):
+            results.append(bench_allreduce_verbs(rank, world, local, args.iters, args.warmup, args.ar_mib << 20,
+                                                 args.pieces))
+            if args.api == "verbs":  # the NCCL figure beside it
+                y = torch.randn((args.ar_mib << 20) // 2, device="cuda").to(torch.bfloat16)
+                t_nccl = _timed(lambda: dist.all_reduce(y), args.iters, args.warmup)
+                results[-1]["nccl_ms"] = round(t_nccl, 4)
+                results[-1]["speedup_vs_nccl"] = round(t_nccl / results[-1]["ugdr_verbs_ms"], 3)
+                del y
     if args.op == "p2p":
         sizes = [1 << k for k in range(3, 31, 2)]
         results.extend(bench_p2p_nccl(rank, world, sizes, max(args.iters, 20), args.warmup))
