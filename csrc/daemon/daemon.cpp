@@ -49,6 +49,7 @@ int Daemon::start() {
         cfg.ordinal = g;
         cfg.ctas = opt_.executor_ctas > 0 ? opt_.executor_ctas : inv.sm_count[g];
         cfg.idle_exit_us = opt_.idle_exit_us;
+        if (opt_.bulk_min_bytes >= 0) cfg.bulk_min_bytes = uint32_t(opt_.bulk_min_bytes);
         std::unique_ptr<control::Engine> e;
         if (int rc = gpu::make_gpu_engine(cfg, objects_mu_, &e); rc != 0) {
             std::fprintf(stderr, "ugdr_daemon: GPU %d engine unavailable (%d)\n", g, rc);

@@ -27,6 +27,7 @@ struct Options {
     int gpus = -1;          // GPUs to own (-1: all visible)
     bool cpu_device = true; // expose the host-memory engine as a device
     int executor_ctas = 0;  // CTAs per GPU executor (0: one per SM)
+    int bulk_min_bytes = -1;  // TMA bulk-copy threshold of the executors (-1: engine default, 0: off)
     uint32_t idle_exit_us = 200000;  // executor exits after this long without work
 };
 

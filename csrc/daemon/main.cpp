@@ -17,7 +17,9 @@ extern "C" void on_signal(int) { g_stop.store(true); }
 void usage(FILE *f) {
     std::fprintf(f,
                  "usage: ugdr_daemon [--socket PATH] [--gpus N] [--no-cpu-device] [--ctas N]\n"
-                 "                   [--idle-exit-us N]\n"
+                 "                   [--idle-exit-us N] [--bulk-min BYTES]\n"
+                 "  --bulk-min: chunk pieces of at least BYTES (16-byte aligned) are copied by the\n"
+                 "    TMA bulk-copy engine (default 8192, 0 = never; also $UGDR_EXECUTOR_BULK_MIN)\n"
                  "  PATH defaults to $UGDR_DAEMON_SOCKET, then /run/ugdr/ugdr.sock\n");
 }
 }  // namespace
@@ -32,6 +34,8 @@ int main(int argc, char **argv) {
     ugdr::daemon::Options opt;
     const char *env = std::getenv("UGDR_DAEMON_SOCKET");
     opt.socket_path = (env != nullptr && env[0] != '\0') ? env : "/run/ugdr/ugdr.sock";
+    if (const char *b = std::getenv("UGDR_EXECUTOR_BULK_MIN"); b != nullptr && b[0] != '\0')
+        opt.bulk_min_bytes = std::atoi(b);
     for (int i = 1; i < argc; ++i) {
         const std::string a = argv[i];
         auto next = [&]() -> const char * {
@@ -52,6 +56,8 @@ int main(int argc, char **argv) {
             opt.cpu_device = false;
         } else if (a == "--ctas") {
             opt.executor_ctas = std::atoi(next());
+        } else if (a == "--bulk-min") {
+            opt.bulk_min_bytes = std::atoi(next());
         } else if (a == "--idle-exit-us") {
             opt.idle_exit_us = uint32_t(std::strtoul(next(), nullptr, 10));
         } else {

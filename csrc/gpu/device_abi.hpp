@@ -183,6 +183,7 @@ enum ExecError : uint32_t {
     kErrCqPublishTimeout = 1,
     kErrRqReleaseTimeout = 2,
     kErrJobSlotTimeout = 3,
+    kErrBulkCopyTimeout = 4,  // a TMA bulk copy of a chunk did not complete in time
 };
 
 // Host-mapped control word the host flips while the kernel runs.
@@ -224,6 +225,8 @@ struct ExecParams {
     TraceRec *trace;             // null: tracing off
     unsigned int *trace_count;   // one append counter per CTA
     uint32_t trace_cap;          // records per CTA
+    uint32_t bulk_min;           // chunk pieces of at least this many 16-byte aligned bytes go
+                                 // through the TMA bulk-copy engine (0: never)
 };
 
 }  // namespace ugdr::gpu

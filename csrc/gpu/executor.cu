@@ -270,9 +270,125 @@ __device__ void warp_copy(uint8_t *dst, const uint8_t *src, uint64_t n, int lane
     for (uint64_t i = lane; i < n; i += 32) dst[i] = src[i];
 }
 
+// ---- TMA bulk-copy path ----------------------------------------------------------------------
+// Long 16-byte aligned pieces of a chunk move through the TMA bulk-copy engine instead of the
+// load/store core: lane 0 of a chunk worker issues cp.async.bulk global -> shared (completion on
+// an mbarrier, expected bytes) and shared -> global (bulk groups) over kTmaStages 4 KiB stages of
+// its warp's own shared memory.  Untiled copies, no tensor map and no multicast: the source may be
+// local or a peer's memory (READ), the destination local or a peer's (WRITE).  A bulk copy keeps
+// far more bytes in flight per warp than the vector core, which is what an NVLink round trip
+// wants.  Every mbarrier wait is bounded; when one runs out the copy waits (bounded) for its other
+// loads, reports failure and the kernel exits with kErrBulkCopyTimeout.
+constexpr uint32_t kTmaStages = 3;
+constexpr uint32_t kTmaPiece = 4096;
+
+struct Tma {
+    uint8_t *buf;    // kTmaStages x kTmaPiece bytes of this warp's shared memory
+    uint64_t *bar;   // kTmaStages mbarriers, arrival count 1
+    uint32_t phase;  // bit s: parity of stage s's next completion (lane 0)
+    uint32_t min;    // pieces shorter than this stay on the load/store path
+    uint32_t failed;
+    uint64_t max_ns;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ bool mbar_wait_until(uint64_t *bar, uint32_t parity, uint64_t deadline) {
+    for (uint32_t spins = 0;; ++spins) {
+        uint32_t done = 0;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(smem_u32(bar)), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if ((spins & 15) == 15 && gtime() > deadline) return false;
+    }
+}
+__device__ __forceinline__ void tma_load(Tma *t, uint32_t s, const uint8_t *src, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&t->bar[s])), "r"(bytes)
+                 : "memory");
+    asm volatile(
+        "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(t->buf + size_t(s) * kTmaPiece)),
+        "l"(src), "r"(bytes), "r"(smem_u32(&t->bar[s]))
+        : "memory");
+}
+__device__ __forceinline__ void tma_store(uint8_t *dst, const uint8_t *smem, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_u32(smem)),
+                 "r"(bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Lane 0: copy n bytes (dst, src and n multiples of 16) through the stages.  Returns false when a
+// wait ran out (the stages are then left quiet, or as quiet as a second bounded wait allows).
+__device__ bool tma_copy(Tma *t, uint8_t *dst, const uint8_t *src, uint64_t n) {
+    // Generic-proxy writes to the source (earlier WRs) before the async proxy reads it.
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    const uint64_t pieces = (n + kTmaPiece - 1) / kTmaPiece;
+    auto piece_bytes = [&](uint64_t i) {
+        const uint64_t left = n - i * kTmaPiece;
+        return uint32_t(left < kTmaPiece ? left : kTmaPiece);
+    };
+    uint64_t loaded = 0;
+    for (; loaded < pieces && loaded < kTmaStages; ++loaded)
+        tma_load(t, uint32_t(loaded % kTmaStages), src + loaded * kTmaPiece, piece_bytes(loaded));
+    const uint64_t deadline = gtime() + t->max_ns;
+    bool ok = true;
+    uint64_t i = 0;
+    for (; i < pieces; ++i) {
+        const uint32_t s = uint32_t(i % kTmaStages);
+        if (!mbar_wait_until(&t->bar[s], (t->phase >> s) & 1u, deadline)) {
+            ok = false;
+            break;
+        }
+        t->phase ^= 1u << s;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        tma_store(dst + i * kTmaPiece, t->buf + size_t(s) * kTmaPiece, piece_bytes(i));
+        if (loaded < pieces) {
+            // Stage s is refilled only once the store just issued has read it.
+            asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+            tma_load(t, s, src + loaded * kTmaPiece, piece_bytes(loaded));
+            ++loaded;
+        }
+    }
+    if (!ok) {
+        const uint64_t d2 = gtime() + t->max_ns;
+        for (uint64_t j = i; j < loaded; ++j) {
+            const uint32_t s = uint32_t(j % kTmaStages);
+            if (mbar_wait_until(&t->bar[s], (t->phase >> s) & 1u, d2)) t->phase ^= 1u << s;
+        }
+    }
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    // The bulk stores are complete; order them before the generic-proxy release that follows.
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    return ok;
+}
+
+// Warp-wide copy of one range: the aligned body through the TMA when it is long enough, the rest
+// (or all of it) with the vector core.
+__device__ void range_copy(Tma *t, uint8_t *dst, const uint8_t *src, uint64_t n, int lane) {
+    if (t != nullptr && t->min != 0 && ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15) == 0 &&
+        n >= t->min) {
+        const uint64_t body = n & ~uint64_t(15);
+        int ok = 1;
+        if (lane == 0) ok = tma_copy(t, dst, src, body) ? 1 : 0;
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) t->failed = 1;
+        warp_copy(dst + body, src + body, n - body, lane);
+        return;
+    }
+    warp_copy(dst, src, n, lane);
+}
+
 // Copy stream bytes [off, off + len) of a WR: local segments <-> contiguous remote range.
+// `t` (null: none) is the calling warp's TMA staging.
 __device__ __noinline__ void copy_stream(const WrRec *rec, uint32_t nseg, uint64_t remote, bool to_remote,
-                            uint64_t off, uint64_t len, int lane) {
+                                         uint64_t off, uint64_t len, int lane, Tma *t) {
     uint64_t seg_start = 0;
     for (uint32_t i = 0; i < nseg && len > 0; ++i) {
         const uint64_t sl = __ldcg(reinterpret_cast<const unsigned long long *>(&rec->seg[i].length));
@@ -284,7 +400,7 @@ __device__ __noinline__ void copy_stream(const WrRec *rec, uint32_t nseg, uint64
                                  __ldcg(reinterpret_cast<const unsigned long long *>(&rec->seg[i].local))) +
                              in;
             uint8_t *rem = reinterpret_cast<uint8_t *>(remote) + off;
-            warp_copy(to_remote ? rem : local, to_remote ? local : rem, take, lane);
+            range_copy(t, to_remote ? rem : local, to_remote ? local : rem, take, lane);
             off += take;
             len -= take;
         }
@@ -423,6 +539,7 @@ struct Warp {
     DevQp *vq;
     uint64_t vt, vhead, vissue, vtail, t_reserved;
     QpView *vv;  // cached view of the QP serviced last (shared memory)
+    Tma *tma;    // this warp's TMA staging (null for the leader warp, which runs no chunks)
 };
 
 // Appends one trace record (lane 0 only; the caller checks that tracing is on).  Not inlined:
@@ -892,8 +1009,12 @@ __device__ void run_chunk(Warp &w, const Claim &cl) {
     if (op == UGDR_X_WR_RDMA_WRITE_SUM_BF16)
         sum_stream(rec, nseg, remote, off, len, w.lane);
     else
-        copy_stream(rec, nseg, remote, op != UGDR_WR_RDMA_READ, off, len, w.lane);
+        copy_stream(rec, nseg, remote, op != UGDR_WR_RDMA_READ, off, len, w.lane, w.tma);
     __syncwarp();
+    if (w.tma != nullptr && w.tma->failed) {
+        record_error(w, kErrBulkCopyTimeout);
+        return;  // the chunk stays unfinished: the kernel exits and reports the error
+    }
     if (w.lane == 0) {
         // Device-scope release is enough here: the owner warp acquires chunks_done and issues
         // the system-scope fence before it publishes the CQE, and causality is transitive.
@@ -1108,7 +1229,7 @@ __device__ void run_inline(Warp &w, WrRec *rec, const uint8_t *wqe, uint32_t op,
         const uint8_t *src = reinterpret_cast<const uint8_t *>(rec->seg[0].local);
         if (uint64_t(w.lane) < total) reinterpret_cast<uint8_t *>(remote)[w.lane] = src[w.lane];
     } else {
-        copy_stream(rec, nseg, remote, op != UGDR_WR_RDMA_READ, 0, total, w.lane);
+        copy_stream(rec, nseg, remote, op != UGDR_WR_RDMA_READ, 0, total, w.lane, nullptr);
     }
     __syncwarp();
     if (w.lane == 0) w.ctr->bytes += total;
@@ -1767,6 +1888,9 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
 // idle.  Without the mirror every warp of the grid polled the same few L2 lines and every
 // data access hashing to those slices queued behind the polls.
 __global__ void __launch_bounds__(kThreads, 1) executor_kernel(ExecParams p) {
+    extern __shared__ __align__(128) uint8_t tma_smem[];  // (kWarps - 1) x kTmaStages x kTmaPiece
+    __shared__ __align__(8) uint64_t tma_bar[kWarps][kTmaStages];
+    __shared__ Tma tma_state[kWarps];
     __shared__ __align__(16) uint8_t wqe_buf[kWarps][kWqeStage];
     __shared__ __align__(16) queue::Cqe cqe_buf[kWarps][kWindow];
     __shared__ __align__(16) MrCacheEntry mr_cache[kWarps][2];
@@ -1792,6 +1916,22 @@ __global__ void __launch_bounds__(kThreads, 1) executor_kernel(ExecParams p) {
     w.mrc = mr_cache[w.wi];
     w.mirror = s_bits;
     if (w.lane < 2) w.mrc[w.lane].key = 0;
+    w.tma = nullptr;
+    if (w.wi != 0) {  // chunk workers: TMA staging and its barriers, fresh for every launch
+        w.tma = &tma_state[w.wi];
+        if (w.lane == 0) {
+            Tma &t = tma_state[w.wi];
+            t.buf = tma_smem + size_t(w.wi - 1) * kTmaStages * kTmaPiece;
+            t.bar = tma_bar[w.wi];
+            t.phase = 0;
+            t.min = p.bulk_min < kTmaPiece && p.bulk_min != 0 ? kTmaPiece : p.bulk_min;
+            t.failed = 0;
+            t.max_ns = p.max_wait_ns;
+            for (uint32_t s = 0; s < kTmaStages; ++s)
+                asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&tma_bar[w.wi][s])) : "memory");
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        }
+    }
     const uint32_t nwarps = gridDim.x * kWarps;
     JobRing *jr = p.jobs;
     // Active-job bitmap: 32 words right after the ring (see job_ring_bytes()).
@@ -1916,8 +2056,16 @@ int launch_grid_copy(void *dst, const void *src, uint64_t n, int ctas, cudaStrea
 size_t job_ring_bytes() { return sizeof(JobRing) + 32 * sizeof(uint32_t); }
 int executor_threads() { return kThreads; }
 
+constexpr size_t kTmaSmemBytes = size_t(kWarps - 1) * kTmaStages * kTmaPiece;
+
 int launch_executor(const ExecParams &p, int ctas, cudaStream_t stream) {
-    executor_kernel<<<ctas, kThreads, 0, stream>>>(p);
+    // The dynamic shared memory (TMA staging) is above the 48 KiB default: opt in (cheap, and
+    // per device, so it is set on every launch).
+    if (cudaError_t e = cudaFuncSetAttribute(executor_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             int(kTmaSmemBytes));
+        e != cudaSuccess)
+        return int(e);
+    executor_kernel<<<ctas, kThreads, kTmaSmemBytes, stream>>>(p);
     return int(cudaGetLastError());
 }
 

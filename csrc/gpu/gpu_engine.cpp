@@ -505,6 +505,7 @@ int GpuEngine::launch_locked(uint32_t mode, uint64_t expected, bool timed) {
     p.trace = trace_;
     p.trace_count = trace_count_;
     p.trace_cap = trace_cap_;
+    p.bulk_min = cfg_.bulk_min_bytes;
     if (vis_.mode() == VisibilityGate::Mode::kFlush && vis_.before_publish() != 0) return EIO;
     if (timed) cudaEventRecord(ev_start_, exec_stream_);
     const int rc = launch_executor(p, cfg_.ctas, exec_stream_);

@@ -21,6 +21,7 @@ struct GpuEngineConfig {
     int ctas = 148;
     uint32_t idle_exit_us = 200000;
     uint32_t max_wait_ms = 2000;  // bound on every device-side spin
+    uint32_t bulk_min_bytes = 8192;  // TMA bulk-copy path for aligned chunk pieces this long (0: off)
 };
 
 // Build the engine for one GPU.  Returns 0 or a positive errno (ENODEV without CUDA).
