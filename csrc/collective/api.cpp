@@ -160,4 +160,11 @@ int ugdr_x_moe_combine(const ugdr_x_peerset *ps, void *out, uint64_t row_bytes, 
                                       static_cast<cudaStream_t>(stream));
 }
 
+int ugdr_x_moe_weighted_sum(void *out, const void *rows, const float *weights, uint64_t tokens, int topk,
+                            uint64_t row_bytes, int ctas, void *stream) {
+    if (out == nullptr || rows == nullptr || weights == nullptr) return int(cudaErrorInvalidValue);
+    return ugdr::coll::launch_weighted_rows(out, rows, weights, tokens, topk, row_bytes,
+                                            ctas > 0 ? ctas : default_ctas(), static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -439,6 +439,42 @@ __global__ void __launch_bounds__(512) combine_kernel(PeerSet ps, uint8_t *out, 
     end_barrier(ps, epoch, kSlotCombine, max_ns);
 }
 
+// Weighted sum of rows that are already local, in (token, k) order (the combine of the MoE
+// all-to-all on the verbs, whose READs brought the rows back): out[t] = sum_k w[t, k] * rows[t, k],
+// fp32 accumulation.  One warp per token; every lane keeps all top-k loads of its columns in
+// flight before the sum.
+template <int TOPK>
+__global__ void __launch_bounds__(512) weighted_rows_kernel(uint8_t *out, const uint8_t *rows, const float *w,
+                                                            uint64_t ntok, int topk, uint64_t row_bytes) {
+    const int lane = threadIdx.x & 31;
+    const uint64_t warp = (uint64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const uint64_t nwarps = (uint64_t(gridDim.x) * blockDim.x) >> 5;
+    const uint64_t nv = row_bytes / 16;
+    for (uint64_t t = warp; t < ntok; t += nwarps) {
+        float wk[TOPK];
+#pragma unroll
+        for (int k = 0; k < TOPK; ++k) wk[k] = k < topk ? __ldg(w + t * topk + k) : 0.f;
+        const uint8_t *base = rows + t * uint64_t(topk) * row_bytes;
+        uint8_t *orow = out + t * row_bytes;
+        for (uint64_t i = lane; i < nv; i += 32) {
+            uint4 v[TOPK];
+#pragma unroll
+            for (int k = 0; k < TOPK; ++k)
+                if (k < topk) v[k] = ld128(base + uint64_t(k) * row_bytes + i * 16);
+            float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+            for (int k = 0; k < TOPK; ++k) {
+                if (k >= topk) continue;
+                float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                acc8(f, v[k]);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) a[j] += wk[k] * f[j];
+            }
+            st128(orow + i * 16, pack8(a));
+        }
+    }
+}
+
 // Counts exchange: this rank's per-expert counts stored into every rank's table
 // (table[rank * nexp + e], int32, at byte `table_off` of each buffer), then the end barrier.
 __global__ void counts_exchange_kernel(PeerSet ps, const int32_t *counts, int nexp, uint64_t table_off,
@@ -529,6 +565,7 @@ int collective_kernels(const KernelRef **out) {
         {"layout_kernel", reinterpret_cast<const void *>(&layout_kernel), 32},
         {"dispatch_kernel", reinterpret_cast<const void *>(&dispatch_kernel), 512},
         {"combine_kernel<8>", reinterpret_cast<const void *>(&combine_kernel<8>), 512},
+        {"weighted_rows_kernel<8>", reinterpret_cast<const void *>(&weighted_rows_kernel<8>), 512},
     };
     *out = refs;
     return int(sizeof(refs) / sizeof(refs[0]));
@@ -579,6 +616,22 @@ int launch_combine(const PeerSet &ps, void *out, uint64_t row_bytes, const int32
     else
         UGDR_COMBINE(16);
 #undef UGDR_COMBINE
+    return int(cudaGetLastError());
+}
+
+int launch_weighted_rows(void *out, const void *rows, const float *w, uint64_t ntok, int topk, uint64_t row_bytes,
+                         int ctas, cudaStream_t s) {
+    if (row_bytes % 16 != 0 || topk <= 0 || topk > 16) return int(cudaErrorInvalidValue);
+    uint8_t *o = static_cast<uint8_t *>(out);
+    const uint8_t *r = static_cast<const uint8_t *>(rows);
+    if (topk <= 2)
+        weighted_rows_kernel<2><<<ctas, 512, 0, s>>>(o, r, w, ntok, topk, row_bytes);
+    else if (topk <= 4)
+        weighted_rows_kernel<4><<<ctas, 512, 0, s>>>(o, r, w, ntok, topk, row_bytes);
+    else if (topk <= 8)
+        weighted_rows_kernel<8><<<ctas, 512, 0, s>>>(o, r, w, ntok, topk, row_bytes);
+    else
+        weighted_rows_kernel<16><<<ctas, 512, 0, s>>>(o, r, w, ntok, topk, row_bytes);
     return int(cudaGetLastError());
 }
 

@@ -120,6 +120,11 @@ int ugdr_x_moe_dispatch(const ugdr_x_peerset *ps, const void *x, uint64_t row_by
                         int experts_per_rank, uint64_t recv_offset, uint64_t recv_rows, uint64_t epoch,
                         int ctas, void *stream);
 /* Combine: out[t] = sum_k weights[t*topk+k] * (the owner's row for (t, k)), fp32 accumulation. */
+/* out[t] = sum_k weights[t * topk + k] * rows[t * topk + k] over rows already on this GPU
+ * ([tokens * topk][row_bytes] bf16 in (token, k) order; fp32 accumulation): the last step of the
+ * MoE combine on the verbs, after its READs brought the rows back.  row_bytes a multiple of 16. */
+int ugdr_x_moe_weighted_sum(void *out, const void *rows, const float *weights, uint64_t tokens, int topk,
+                            uint64_t row_bytes, int ctas, void *stream);
 int ugdr_x_moe_combine(const ugdr_x_peerset *ps, void *out, uint64_t row_bytes, const int32_t *expert_ids,
                        const int32_t *positions, const int64_t *group_base, const float *weights,
                        uint64_t tokens, int topk, int experts_per_rank, uint64_t recv_offset, uint64_t recv_rows,

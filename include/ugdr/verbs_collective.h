@@ -71,6 +71,58 @@ uint64_t ugdr_x_verbs_allreduce_stage_bytes(uint64_t count, int n) UGDR_VC_NOEXC
 int ugdr_x_verbs_allreduce_bf16(ugdr_x_vgroup *g, uint64_t count, int pieces,
                                 uint64_t timeout_ns) UGDR_VC_NOEXCEPT;
 
+/* MoE all-to-all on the verbs.  Experts split evenly over the ranks (rank q owns experts
+ * [q * nexp / n, (q + 1) * nexp / n)).  The permutes are the SGE lists of the WRs: dispatch
+ * WRITEs gather each expert group's token rows (one SGE per row) into one contiguous range of
+ * the owner's receive area; combine READs each group back and scatters it (one SGE per row)
+ * into the (token, k) row order of `back`.  The group's `to` QPs and `self_to` need
+ * max_send_sge >= 32 and send queues of at least ugdr_x_verbs_moe_wrs(...) WRs; `from` QPs need
+ * 2 receives per call.  Counts travel as WRITE_WITH_IMM into every rank's count table (a host
+ * buffer), which also orders calls: a rank's next dispatch writes nothing before every rank has
+ * finished its combine. */
+typedef struct ugdr_x_vmoe {
+    int tokens;
+    int topk;
+    int nexp;
+    uint32_t row_bytes;
+    uint64_t x_addr;        /* [tokens][row_bytes] rows to send (registered: x_lkey) */
+    uint32_t x_lkey;
+    uint32_t recv_lkey;
+    uint64_t recv_addr;     /* receive area: recv_rows rows, grouped by expert then source rank */
+    uint32_t recv_rkey;
+    uint32_t back_lkey;
+    uint64_t recv_rows;
+    uint64_t back_addr;     /* [tokens * topk][row_bytes]: rows read back, in (token, k) order */
+    int32_t *table;         /* host [n][nexp] counts (registered: table_lkey / table_rkey) */
+    uint32_t table_lkey;
+    uint32_t table_rkey;
+    uint64_t peer_recv_addr[UGDR_X_VGROUP_MAX_RANKS];
+    uint32_t peer_recv_rkey[UGDR_X_VGROUP_MAX_RANKS];
+    uint64_t peer_table_addr[UGDR_X_VGROUP_MAX_RANKS];
+    uint32_t peer_table_rkey[UGDR_X_VGROUP_MAX_RANKS];
+    /* Filled by dispatch for combine: first receive row of (expert e, source rank r) at the
+     * owner, and how many rows this rank received. */
+    uint64_t *base;         /* host [nexp][n] */
+    uint64_t received;
+} ugdr_x_vmoe;
+
+/* Largest number of data WRs one dispatch or combine posts on one QP for `rows_per_rank`
+ * (token, k) rows (an upper bound for sizing send queues). */
+uint32_t ugdr_x_verbs_moe_wrs(uint64_t rows_per_rank, int nexp, int n) UGDR_VC_NOEXCEPT;
+
+/* Send every (token, k) row to its expert's owner.  `ids` and `pos` (host, tokens x topk int32)
+ * are each row's expert and its position inside this rank's rows of that expert (row order, as
+ * ugdr_x_moe_route gives them); `counts` (host, nexp int32) this rank's rows per expert.  Blocks
+ * until this rank's rows have landed and every peer's rows for this rank's experts have too.
+ * Returns 0, ENOSPC (receive area too small), EINVAL, ETIMEDOUT, EIO or a verbs errno. */
+int ugdr_x_verbs_moe_dispatch(ugdr_x_vgroup *g, ugdr_x_vmoe *m, const int32_t *ids, const int32_t *pos,
+                              const int32_t *counts, uint64_t timeout_ns) UGDR_VC_NOEXCEPT;
+
+/* Read every row this rank dispatched (after the owners' experts worked on them in place) back
+ * into `back` in (token, k) order.  Blocks until all reads completed. */
+int ugdr_x_verbs_moe_combine(ugdr_x_vgroup *g, ugdr_x_vmoe *m, const int32_t *ids, const int32_t *pos,
+                             uint64_t timeout_ns) UGDR_VC_NOEXCEPT;
+
 #ifdef __cplusplus
 }
 #endif

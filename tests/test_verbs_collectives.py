@@ -113,3 +113,120 @@ def test_verbs_allreduce_on_the_executors(world):
     if gpu_count() < world:
         pytest.skip(f"needs {world} GPUs")
     _run(world, True, [(1 << 24) + 40, 3 * 8 * 1000 + 3], 4)
+
+
+# ---- MoE all-to-all on the verbs ------------------------------------------------------------------
+
+
+def _moe_inputs(rank: int, T: int, H: int, K: int, E: int, call: int, dev):
+    from ugdr_b200.models.moe import route
+
+    g = torch.Generator().manual_seed(10_000 * call + 10 + rank)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    ids, w = route(T, E, K, seed=10_000 * call + 20 + rank, device="cpu")
+    return x.to(dev), ids.to(dev), w.to(dev)
+
+
+def _moe_expected_recv(q: int, world: int, T: int, H: int, K: int, E: int, call: int) -> torch.Tensor:
+    """Owner q's receive area: its experts in order, inside each the source ranks in order, inside
+    each source its rows of that expert in (token, k) order."""
+    from ugdr_b200.models.moe import reference_positions
+
+    epr = E // world
+    parts = []
+    srcs = [_moe_inputs(s, T, H, K, E, call, "cpu") for s in range(world)]
+    for e in range(q * epr, (q + 1) * epr):
+        for s in range(world):
+            x, ids, _ = srcs[s]
+            counts, pos = reference_positions(ids, E)
+            flat = ids.reshape(-1)
+            sel = (flat == e).nonzero().reshape(-1)
+            order = sel[torch.argsort(pos.reshape(-1)[sel])]
+            parts.append(x[order // K])
+    return torch.cat(parts) if parts else torch.empty(0, H, dtype=torch.bfloat16)
+
+
+def _moe_worker(rank: int, world: int, port: int, gpu: bool, shape: tuple, calls: int, errq) -> None:
+    import torch.distributed as dist
+
+    T, H, K, E = shape
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    daemon = None
+    try:
+        from ugdr_b200.parallel.verbs_collectives import VerbsMoE, moe_group, shared_daemon
+
+        def bcast(obj):
+            lst = [obj]
+            dist.broadcast_object_list(lst, src=0)
+            return lst[0]
+
+        def exchange(obj):
+            out = [None] * world
+            dist.all_gather_object(out, obj)
+            return out
+
+        dev = f"cuda:{rank}" if gpu else "cpu"
+        if gpu:
+            torch.cuda.set_device(rank)
+        daemon = shared_daemon(rank, world, bcast, gpus=world if gpu else 0)
+        g = moe_group(rank, world, rank if gpu else 0, T, K, E, exchange, device_kind=1 if gpu else 0)
+        moe = VerbsMoE(g, T, H, K, E, recv_rows=T * K * world)
+        try:
+            for call in range(calls):
+                x, ids, w = _moe_inputs(rank, T, H, K, E, call, dev)
+                moe.dispatch(x, ids)
+                got = moe.recv_view().cpu()
+                want = _moe_expected_recv(rank, world, T, H, K, E, call)
+                assert got.shape == want.shape, (got.shape, want.shape)
+                assert torch.equal(got, want), f"rank {rank} call {call}: receive area differs"
+                out = moe.combine(w)
+                if gpu:
+                    torch.cuda.synchronize()
+                back = moe.back.cpu()
+                assert torch.equal(back, x.cpu().repeat_interleave(K, dim=0)), f"rank {rank}: rows read back differ"
+                ref = x.cpu().float() * w.cpu().sum(-1, keepdim=True)
+                assert torch.allclose(out.cpu().float(), ref, atol=2e-2, rtol=1e-2), f"rank {rank}: combine"
+                dist.barrier()
+        finally:
+            moe.close()
+            g.close()
+        dist.barrier()
+    except BaseException as e:
+        errq.put(f"rank {rank}: {type(e).__name__}: {e}")
+        raise
+    finally:
+        if daemon is not None:
+            daemon.stop()
+        dist.destroy_process_group()
+
+
+def _run_moe(world: int, gpu: bool, shape: tuple, calls: int) -> None:
+    ctx = mp.get_context("spawn")
+    errq = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_moe_worker, args=(r, world, port, gpu, shape, calls, errq)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(600)
+    errs = []
+    while not errq.empty():
+        errs.append(errq.get())
+    assert not errs, errs
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+
+
+@pytest.mark.parametrize("world,shape", [(2, (64, 64, 4, 8)), (3, (50, 32, 2, 6))])
+def test_verbs_moe_exact_permutation_on_the_host_engine(world, shape):
+    """Every owner's receive area equals, row for row, the expected expert-grouped permutation of
+    every rank's tokens; combine reads every row back to its (token, k) slot and weights it."""
+    _run_moe(world, False, shape, calls=2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_verbs_moe_exact_permutation_on_the_executors(world):
+    if gpu_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    _run_moe(world, True, (512, 1024, 8, 32), calls=2)

@@ -64,16 +64,18 @@ class VerbsGroup:
     """A rank's QPs, CQ and registered buffers for the verbs collectives (one GPU per rank)."""
 
     def __init__(self, rank: int, world: int, gpu: int, count: int, exchange, pieces: int = 8,
-                 device_kind: int = 1):
+                 device_kind: int = 1, send_depth: int = 0, max_sge: int = 1):
         if not 1 <= world <= MAX_RANKS or not 1 <= pieces <= MAX_PIECES:
             raise ValueError("world must be 1..8 and pieces 1..64")
         self.rank, self.world, self.count, self.pieces = rank, world, count, pieces
+        self.device_kind = device_kind
         L = _lib()
         dev = V.find_device(gpu=gpu) if device_kind == 1 else V.find_device(kind=0)
         self.ctx = V.Context(dev)
         self.pd = self.ctx.alloc_pd()
-        depth = 2 * pieces + 4
-        self.cq = self.ctx.create_cq(2 * pieces * world + pieces + world + 64)
+        depth = max(2 * pieces + 4, send_depth)
+        self.exchange = exchange
+        self.cq = self.ctx.create_cq(2 * pieces * world + pieces + 4 * world + 64)
         stage_bytes = max(int(L.ugdr_x_verbs_allreduce_stage_bytes(count, world)), 16)
         self._host = []
         if device_kind == 1:
@@ -88,13 +90,17 @@ class VerbsGroup:
         acc = N.ACCESS_LOCAL_WRITE | N.ACCESS_REMOTE_WRITE
         self.buf_mr = self.pd.reg_mr(self.buf.data_ptr(), max(2 * count, 2), acc)
         self.stage_mr = self.pd.reg_mr(self.stage.data_ptr(), self.stage.numel(), acc)
-        self.to = {q: self.pd.create_qp(self.cq, max_send_wr=depth, max_recv_wr=4) for q in range(world) if q != rank}
-        self.frm = {q: self.pd.create_qp(self.cq, max_send_wr=4, max_recv_wr=depth) for q in range(world) if q != rank}
-        self.self_to = self.pd.create_qp(self.cq, max_send_wr=depth, max_recv_wr=4, max_send_sge=MAX_RANKS)
+        self.to = {q: self.pd.create_qp(self.cq, max_send_wr=depth, max_recv_wr=4, max_send_sge=max_sge)
+                   for q in range(world) if q != rank}
+        self.frm = {q: self.pd.create_qp(self.cq, max_send_wr=4, max_recv_wr=2 * pieces + 4)
+                    for q in range(world) if q != rank}
+        self.self_to = self.pd.create_qp(self.cq, max_send_wr=depth, max_recv_wr=4,
+                                         max_send_sge=max(MAX_RANKS, max_sge))
         self.self_peer = self.pd.create_qp(self.cq, max_send_wr=4, max_recv_wr=4)
-        V.connect_pair(self.self_to, self.self_peer, access=N.ACCESS_REMOTE_WRITE)
+        remote = N.ACCESS_REMOTE_WRITE | N.ACCESS_REMOTE_READ
+        V.connect_pair(self.self_to, self.self_peer, access=remote)
         for q in list(self.to.values()) + list(self.frm.values()):
-            q.to_init(N.ACCESS_REMOTE_WRITE)
+            q.to_init(remote)
         info = exchange({"to": {q: qp.qpn for q, qp in self.to.items()},
                          "from": {q: qp.qpn for q, qp in self.frm.items()},
                          "buf": (self.buf.data_ptr(), self.buf_mr.rkey),
@@ -134,5 +140,157 @@ class VerbsGroup:
         self.cq.destroy()
         self.pd.dealloc()
         self.ctx.close()
+        for h in self._host:
+            h.free()
+
+
+class _Moe(C.Structure):
+    _fields_ = [("tokens", C.c_int), ("topk", C.c_int), ("nexp", C.c_int), ("row_bytes", C.c_uint32),
+                ("x_addr", C.c_uint64), ("x_lkey", C.c_uint32), ("recv_lkey", C.c_uint32),
+                ("recv_addr", C.c_uint64), ("recv_rkey", C.c_uint32), ("back_lkey", C.c_uint32),
+                ("recv_rows", C.c_uint64), ("back_addr", C.c_uint64), ("table", C.c_void_p),
+                ("table_lkey", C.c_uint32), ("table_rkey", C.c_uint32),
+                ("peer_recv_addr", C.c_uint64 * MAX_RANKS), ("peer_recv_rkey", C.c_uint32 * MAX_RANKS),
+                ("peer_table_addr", C.c_uint64 * MAX_RANKS), ("peer_table_rkey", C.c_uint32 * MAX_RANKS),
+                ("base", C.c_void_p), ("received", C.c_uint64)]
+
+
+def _moe_lib():
+    L = _lib()
+    if not getattr(L, "_vmoe_sigs", False):
+        L.ugdr_x_verbs_moe_wrs.restype = C.c_uint32
+        L.ugdr_x_verbs_moe_wrs.argtypes = [C.c_uint64, C.c_int, C.c_int]
+        for f in (L.ugdr_x_verbs_moe_dispatch,):
+            f.restype = C.c_int
+            f.argtypes = [C.POINTER(_Group), C.POINTER(_Moe), C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint64]
+        L.ugdr_x_verbs_moe_combine.restype = C.c_int
+        L.ugdr_x_verbs_moe_combine.argtypes = [C.POINTER(_Group), C.POINTER(_Moe), C.c_void_p, C.c_void_p,
+                                               C.c_uint64]
+        L.ugdr_x_moe_weighted_sum.restype = C.c_int
+        L.ugdr_x_moe_weighted_sum.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint64, C.c_int, C.c_uint64,
+                                              C.c_int, C.c_void_p]
+        L._vmoe_sigs = True
+    return L
+
+
+def moe_group(rank: int, world: int, gpu: int, tokens: int, topk: int, nexp: int, exchange,
+              device_kind: int = 1) -> VerbsGroup:
+    """A VerbsGroup sized for VerbsMoE: 32-SGE send queues deep enough for one call's WRs."""
+    depth = int(_moe_lib().ugdr_x_verbs_moe_wrs(tokens * topk, nexp, world)) + 8
+    return VerbsGroup(rank, world, gpu, 8, exchange, pieces=1, send_depth=depth, max_sge=32,
+                      device_kind=device_kind)
+
+
+def _host_tensor(nbytes: int, dtype, shape, keep: list):
+    hb = V.HostBuffer(max(nbytes, 16))
+    keep.append(hb)
+    return torch.from_numpy(hb.view()[:nbytes]).view(dtype).view(*shape)
+
+
+class VerbsMoE:
+    """MoE all-to-all on the verbs (ugdr_x_verbs_moe_dispatch / _combine).
+
+    dispatch(x, ids) routes on the GPU (ugdr_x_moe_route), copies the routing to the host and
+    sends every (token, k) row to its expert's owner with WRITEs whose SGE lists are the permute;
+    `recv_view()[:received]` then holds this rank's experts' rows, grouped by expert and source
+    rank.  combine(w) READs every row back into (token, k) order (SGE lists again) and returns
+    sum_k w[t, k] * row(t, k) (ugdr_x_moe_weighted_sum)."""
+
+    def __init__(self, group: VerbsGroup, tokens: int, hidden: int, topk: int, nexp: int, recv_rows: int):
+        if nexp % group.world:
+            raise ValueError("experts must split evenly over ranks")
+        self.g, self.tokens, self.hidden, self.topk, self.nexp = group, tokens, hidden, topk, nexp
+        L = _moe_lib()
+        self.row_bytes = hidden * 2
+        self.gpu = group.device_kind == 1
+        self._host = []
+        if self.gpu:
+            dev = torch.device("cuda", torch.cuda.current_device())
+            self.x = torch.empty(tokens, hidden, dtype=torch.bfloat16, device=dev)
+            self.recv = torch.empty(recv_rows, hidden, dtype=torch.bfloat16, device=dev)
+            self.back = torch.empty(tokens * topk, hidden, dtype=torch.bfloat16, device=dev)
+            torch.cuda.synchronize()
+        else:  # host engine: daemon-shareable host memory, torch on the CPU
+            rb = self.row_bytes
+            self.x = _host_tensor(tokens * rb, torch.bfloat16, (tokens, hidden), self._host)
+            self.recv = _host_tensor(recv_rows * rb, torch.bfloat16, (recv_rows, hidden), self._host)
+            self.back = _host_tensor(tokens * topk * rb, torch.bfloat16, (tokens * topk, hidden), self._host)
+        self.table = V.HostBuffer(group.world * nexp * 4)
+        self.table.view()[:] = 0
+        pd = group.pd
+        lw, rw, rr = N.ACCESS_LOCAL_WRITE, N.ACCESS_REMOTE_WRITE, N.ACCESS_REMOTE_READ
+        self.x_mr = pd.reg_mr(self.x.data_ptr(), self.x.numel() * 2, lw)
+        self.recv_mr = pd.reg_mr(self.recv.data_ptr(), self.recv.numel() * 2, lw | rw | rr)
+        self.back_mr = pd.reg_mr(self.back.data_ptr(), self.back.numel() * 2, lw)
+        self.table_mr = pd.reg_mr(self.table.addr, self.table.length, lw | rw)
+        import numpy as np
+
+        self.base = np.zeros(nexp * group.world, dtype=np.uint64)
+        info = group.exchange({"recv": (self.recv.data_ptr(), self.recv_mr.rkey),
+                               "table": (self.table.addr, self.table_mr.rkey)})
+        m = _Moe()
+        m.tokens, m.topk, m.nexp, m.row_bytes = tokens, topk, nexp, self.row_bytes
+        m.x_addr, m.x_lkey = self.x.data_ptr(), self.x_mr.lkey
+        m.recv_addr, m.recv_lkey, m.recv_rkey, m.recv_rows = (self.recv.data_ptr(), self.recv_mr.lkey,
+                                                              self.recv_mr.rkey, recv_rows)
+        m.back_addr, m.back_lkey = self.back.data_ptr(), self.back_mr.lkey
+        m.table, m.table_lkey, m.table_rkey = self.table.addr, self.table_mr.lkey, self.table_mr.rkey
+        for q in range(group.world):
+            m.peer_recv_addr[q], m.peer_recv_rkey[q] = info[q]["recv"]
+            m.peer_table_addr[q], m.peer_table_rkey[q] = info[q]["table"]
+        m.base = self.base.ctypes.data
+        self._m = m
+        self.ids = self.pos = None
+        self.scratch = None
+
+    def recv_view(self) -> torch.Tensor:
+        return self.recv[: int(self._m.received)]
+
+    def dispatch(self, x: torch.Tensor | None, expert_ids: torch.Tensor, timeout_s: float = 60.0) -> None:
+        if x is not None:
+            self.x.copy_(x)
+        if self.gpu:
+            from .collectives import moe_route
+
+            counts, pos = moe_route(expert_ids, self.nexp)
+        else:
+            from ..models.moe import reference_positions
+
+            counts, pos = reference_positions(expert_ids, self.nexp)
+        ids_h = expert_ids.reshape(-1).to(torch.int32).cpu().contiguous()
+        pos_h = pos.reshape(-1).to(torch.int32).cpu().contiguous()  # synchronises: x and the routing are ready
+        counts_h = counts.to(torch.int32).cpu().contiguous()
+        self.ids, self.pos = ids_h, pos_h
+        rc = _moe_lib().ugdr_x_verbs_moe_dispatch(C.byref(self.g._g), C.byref(self._m), ids_h.data_ptr(),
+                                                   pos_h.data_ptr(), counts_h.data_ptr(), int(timeout_s * 1e9))
+        if rc != 0:
+            raise V.UgdrError(rc, f"ugdr_x_verbs_moe_dispatch: {N.errname(rc)}")
+
+    def combine(self, weights: torch.Tensor, out: torch.Tensor | None = None, timeout_s: float = 60.0) -> torch.Tensor:
+        L = _moe_lib()
+        rc = L.ugdr_x_verbs_moe_combine(C.byref(self.g._g), C.byref(self._m), self.ids.data_ptr(),
+                                        self.pos.data_ptr(), int(timeout_s * 1e9))
+        if rc != 0:
+            raise V.UgdrError(rc, f"ugdr_x_verbs_moe_combine: {N.errname(rc)}")
+        w = weights.reshape(-1).to(torch.float32).contiguous()
+        if not self.gpu:
+            rows = self.back.float().view(self.tokens, self.topk, self.hidden)
+            res = (rows * w.view(self.tokens, self.topk, 1)).sum(1).to(torch.bfloat16)
+            if out is not None:
+                out.copy_(res)
+                return out
+            return res
+        if out is None:
+            out = torch.empty(self.tokens, self.hidden, dtype=torch.bfloat16, device=self.x.device)
+        rc = L.ugdr_x_moe_weighted_sum(out.data_ptr(), self.back.data_ptr(), w.data_ptr(), self.tokens, self.topk,
+                                       self.row_bytes, 0, torch.cuda.current_stream().cuda_stream)
+        if rc != 0:
+            raise RuntimeError(f"ugdr_x_moe_weighted_sum: cudaError {rc}")
+        return out
+
+    def close(self) -> None:
+        for mr in (self.x_mr, self.recv_mr, self.back_mr, self.table_mr):
+            mr.dereg()
+        self.table.free()
         for h in self._host:
             h.free()
