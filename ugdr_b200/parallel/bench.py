@@ -272,6 +272,68 @@ def bench_moe(rank, world, iters, warmup, cfg: MoEConfig) -> dict:
             "speedup_vs_nccl": round(t_nccl / t_ugdr, 3), "correct": bool(ok)}
 
 
+def bench_moe_verbs(rank, world, local, iters, warmup, cfg: MoEConfig) -> dict:
+    """MoE dispatch + combine on the verbs (VerbsMoE): the permutes are the SGE lists of WRITEs
+    and READs that the daemon's executors run; experts are the identity.  Checked against the
+    fp32 reference of the same workload; timed by wall clock per step (routing, the host copy of
+    the routing, both transfers and the weighted sum), max over ranks."""
+    import time
+
+    from . import verbs_collectives as VC
+
+    T, H, K, E = cfg.tokens, cfg.hidden, cfg.topk, cfg.experts
+
+    def exchange(obj):
+        out = [None] * world
+        dist.all_gather_object(out, obj, group=_GLOO)
+        return out
+
+    def bcast(obj):
+        lst = [obj]
+        dist.broadcast_object_list(lst, src=0, group=_GLOO)
+        return lst[0]
+
+    daemon = VC.shared_daemon(rank, world, bcast)
+    g = VC.moe_group(rank, world, local, T, K, E, exchange)
+    moe = VC.VerbsMoE(g, T, H, K, E, recv_rows=int(T * K * 1.25) + 4096)
+    try:
+        gen = torch.Generator(device="cuda").manual_seed(1000 + rank)
+        x = torch.randn(T, H, generator=gen, device="cuda").to(torch.bfloat16)
+        ids, w = route(T, E, K, seed=2000 + rank)
+
+        def step():
+            moe.dispatch(x, ids)
+            return moe.combine(w)
+
+        out = step()
+        torch.cuda.synchronize()
+        ok = torch.allclose(out.float(), x.float() * w.sum(-1, keepdim=True), atol=3e-2, rtol=2e-2)
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        dist.barrier(group=_GLOO)
+        t0 = time.perf_counter()
+        for _ in range(iters):
+            step()
+        torch.cuda.synchronize()
+        ms = (time.perf_counter() - t0) / iters * 1e3
+        t = torch.tensor([ms], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=_GLOO)
+        ms = float(t.item())
+        dist.barrier(group=_GLOO)
+    finally:
+        moe.close()
+        g.close()
+        dist.barrier(group=_GLOO)
+        if daemon is not None:
+            daemon.stop()
+    moved = 2 * T * K * H * 2
+    return {"op": "moe_dispatch_combine_verbs", "n_gpus": world, "tokens": T, "hidden": H, "topk": K, "experts": E,
+            "ugdr_verbs_ms": round(ms, 4), "ugdr_verbs_GBps_per_rank": round(moved / ms / 1e6, 1),
+            "correct": bool(ok), "timing": "wall clock per step (route + host copy of the routing + dispatch WRs + "
+                                           "combine WRs + weighted sum), max over ranks"}
+
+
 def main():
     global _GLOO
     ap = argparse.ArgumentParser()
@@ -311,7 +373,10 @@ def main():
         sizes = [1 << k for k in range(3, 31, 2)]
         results.extend(bench_p2p_nccl(rank, world, sizes, max(args.iters, 20), args.warmup))
     if args.op in ("all", "moe"):
-        results.append(bench_moe(rank, world, args.iters, args.warmup, MoEConfig(tokens=args.tokens)))
+        if args.api in ("peer", "both"):
+            results.append(bench_moe(rank, world, args.iters, args.warmup, MoEConfig(tokens=args.tokens)))
+        if args.api in ("verbs", "both"):
+            results.append(bench_moe_verbs(rank, world, local, args.iters, args.warmup, MoEConfig(tokens=args.tokens)))
     if rank == 0:
         for r in results:
             print(json.dumps(r), flush=True)
