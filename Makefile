@@ -18,7 +18,7 @@ LIB_CXX := \
   csrc/control/rpc.cpp csrc/control/service.cpp csrc/control/client.cpp \
   csrc/api/posting.cpp csrc/api/runtime.cpp csrc/api/memory_export.cpp \
   csrc/engine/cpu_engine.cpp csrc/gpu/cuda_memory.cpp csrc/gpu/gpu_engine.cpp csrc/gpu/diag.cpp \
-  csrc/gpu/visibility.cpp csrc/gpu/trace_writer.cpp \
+  csrc/gpu/visibility.cpp csrc/gpu/trace_writer.cpp csrc/gpu/multicast.cpp \
   csrc/daemon/daemon.cpp csrc/collective/api.cpp csrc/collective/nvls.cpp \
   csrc/collective/verbs_allreduce.cpp csrc/collective/verbs_moe.cpp
 LIB_CU  := csrc/gpu/executor.cu csrc/gpu/bulk_copy.cu csrc/collective/kernels.cu csrc/collective/route_noalloc.cu

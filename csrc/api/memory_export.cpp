@@ -49,6 +49,19 @@ int export_host(const SharedMapping &m, uintptr_t addr, size_t len, std::vector<
 
 }  // namespace
 
+int export_multicast(int fd, uint64_t client_addr, size_t len, std::vector<std::byte> *opaque,
+                     std::vector<Fd> *fds) {
+    if (fd < 0 || client_addr == 0 || len == 0) return EINVAL;
+    Fd dup_fd(::dup(fd));
+    if (!dup_fd.valid()) return errno;
+    ByteWriter w(opaque);
+    const uint8_t pad[3] = {0, 0, 0};
+    w.be(uint8_t(control::MemKind::multicast)).raw(pad, 3).be(uint64_t(client_addr));
+    w.be(uint64_t(len)).be(uint64_t(0));
+    fds->push_back(std::move(dup_fd));
+    return 0;
+}
+
 void *host_alloc(size_t len) {
     if (len == 0) {
         errno = EINVAL;

@@ -17,6 +17,12 @@ namespace ugdr::api {
 // Build the register-MR opaque (and the fd list) for [addr, addr + len).
 int export_memory(void *addr, size_t len, std::vector<std::byte> *opaque, std::vector<Fd> *fds);
 
+// The register-MR opaque for an NVLink multicast object: `fd` is its POSIX shareable handle
+// (duplicated here), `client_addr` the caller's own multicast mapping of it and `len` the bytes
+// registered from offset 0.
+int export_multicast(int fd, uint64_t client_addr, size_t len, std::vector<std::byte> *opaque,
+                     std::vector<Fd> *fds);
+
 // Host buffers.
 void *host_alloc(size_t len);
 int host_free(void *addr);

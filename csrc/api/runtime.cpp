@@ -298,14 +298,17 @@ int ugdr_dealloc_pd(ugdr_pd *pd) noexcept {
     return 0;
 }
 
-ugdr_mr *ugdr_reg_mr(ugdr_pd *pd, void *address, size_t length, int access) noexcept {
+namespace {
+ugdr_mr *register_mr(ugdr_pd *pd, void *address, size_t length, int access, int mc_fd) noexcept {
     if (!rt().live(pd) || address == nullptr || length == 0) return fail_null<ugdr_mr>(EINVAL);
     try {
         Request req = make(kRegisterMr, pd->identity);
         req.length = length;
         req.access = uint32_t(access);
-        if (int rc = ugdr::api::export_memory(address, length, &req.opaque, &req.fds); rc != 0)
-            return fail_null<ugdr_mr>(rc);
+        const int rc0 = mc_fd < 0 ? ugdr::api::export_memory(address, length, &req.opaque, &req.fds)
+                                  : ugdr::api::export_multicast(mc_fd, reinterpret_cast<uint64_t>(address), length,
+                                                                &req.opaque, &req.fds);
+        if (rc0 != 0) return fail_null<ugdr_mr>(rc0);
         Response resp;
         if (int rc = rt().call(std::move(req), &resp); rc != 0) return fail_null<ugdr_mr>(rc);
         ByteReader rd(resp.opaque);
@@ -327,6 +330,16 @@ ugdr_mr *ugdr_reg_mr(ugdr_pd *pd, void *address, size_t length, int access) noex
     } catch (...) {
         return fail_null<ugdr_mr>(ENOMEM);
     }
+}
+}  // namespace
+
+ugdr_mr *ugdr_reg_mr(ugdr_pd *pd, void *address, size_t length, int access) noexcept {
+    return register_mr(pd, address, length, access, -1);
+}
+
+ugdr_mr *ugdr_x_reg_mr_multicast(ugdr_pd *pd, void *address, size_t length, int access, int mc_fd) noexcept {
+    if (mc_fd < 0) return fail_null<ugdr_mr>(EINVAL);
+    return register_mr(pd, address, length, access, mc_fd);
 }
 
 int ugdr_dereg_mr(ugdr_mr *mr) noexcept {

@@ -180,3 +180,95 @@ extern "C" int ugdr_x_verbs_allreduce_bf16(ugdr_x_vgroup *g, uint64_t count, int
     }
     return 0;
 }
+
+extern "C" int ugdr_x_verbs_allreduce_bf16_mc(ugdr_x_vgroup *g, uint64_t mc_addr, uint32_t mc_lkey, uint32_t mc_rkey,
+                                              uint64_t count, uint64_t timeout_ns) noexcept {
+    if (g == nullptr || g->n < 1 || g->n > UGDR_X_VGROUP_MAX_RANKS || g->rank < 0 || g->rank >= g->n ||
+        g->cq == nullptr || g->self_to == nullptr || mc_addr == 0 || (mc_addr & 15) != 0 || count % 8 != 0)
+        return EINVAL;
+    const int n = g->n, r = g->rank;
+    for (int q = 0; q < n; ++q)
+        if (q != r && (g->peer[q].to == nullptr || g->peer[q].from == nullptr)) return EINVAL;
+    const Geometry G = geometry(count, n, 1);
+    const uint32_t epoch = g->epoch++;
+    constexpr int kReady = 7, kDone = 8;
+
+    for (int q = 0; q < n; ++q) {
+        if (q == r) continue;
+        ugdr_recv_wr rw[2] = {};
+        rw[0].next = &rw[1];
+        ugdr_recv_wr *bad = nullptr;
+        if (int rc = ugdr_post_recv(g->peer[q].from, rw, &bad); rc != 0) return rc;
+    }
+    // A zero-length WRITE_WITH_IMM to every peer; with `signal`, its retirement (after every
+    // earlier WR of the QP) is reported here too.
+    auto notify = [&](int phase, bool signal) -> int {
+        for (int k = 1; k < n; ++k) {
+            const int q = (r + k) % n;
+            ugdr_send_wr w{};
+            w.wr_id = signal ? (kTagLast | uint64_t(q)) : 0;
+            w.opcode = UGDR_WR_RDMA_WRITE_WITH_IMM;
+            w.send_flags = signal ? UGDR_SEND_SIGNALED : 0;
+            w.imm_data = imm_of(epoch, phase, 0, r);
+            w.wr.rdma.remote_addr = g->peer[q].buf_addr;
+            w.wr.rdma.rkey = g->peer[q].buf_rkey;
+            ugdr_send_wr *bad = nullptr;
+            if (int rc = ugdr_post_send(g->peer[q].to, &w, &bad); rc != 0) return rc;
+        }
+        return 0;
+    };
+    int ready = 0, done = 0, lasts = 0, sums = 0;
+    const auto deadline = std::chrono::steady_clock::now() + std::chrono::nanoseconds(timeout_ns);
+    auto wait = [&](auto until) -> int {
+        ugdr_wc wc[64];
+        uint32_t idle = 0;
+        while (!until()) {
+            const int k = ugdr_poll_cq(g->cq, 64, wc);
+            if (k < 0) return -k;
+            if (k == 0) {
+                if ((++idle & 1023) == 0 && std::chrono::steady_clock::now() > deadline) return ETIMEDOUT;
+                continue;
+            }
+            idle = 0;
+            for (int i = 0; i < k; ++i) {
+                if (wc[i].status != UGDR_WC_SUCCESS) return EIO;
+                if (wc[i].opcode == UGDR_WC_RECV_RDMA_WITH_IMM) {
+                    const uint32_t imm = wc[i].imm_data;
+                    const int phase = int((imm >> 16) & 0xffu);
+                    if ((imm >> 24) != (epoch & 0xffu)) return EIO;
+                    if (phase == kReady) ++ready;
+                    else if (phase == kDone) ++done;
+                    else return EIO;
+                } else if (wc[i].wr_id & kTagSum) {
+                    ++sums;
+                } else if (wc[i].wr_id & kTagLast) {
+                    ++lasts;
+                }
+            }
+        }
+        return 0;
+    };
+    // 1. Every rank's input is in place.
+    if (int rc = notify(kReady, false); rc != 0) return rc;
+    if (int rc = wait([&] { return ready == n - 1; }); rc != 0) return rc;
+    // 2. This rank's shard: one WRITE_SUM_BF16 from the multicast view (the NVSwitch sums every
+    //    GPU's copy) to the multicast view (every GPU receives the sum).
+    {
+        const uint64_t a = G.lo(r), b = G.hi(r);
+        ugdr_sge sg{mc_addr + a * 2, uint32_t((b - a) * 2), mc_lkey};
+        ugdr_send_wr w{};
+        w.wr_id = kTagSum;
+        w.sg_list = &sg;
+        w.num_sge = 1;
+        w.opcode = UGDR_X_WR_RDMA_WRITE_SUM_BF16;
+        w.send_flags = UGDR_SEND_SIGNALED;
+        w.wr.rdma.remote_addr = mc_addr + a * 2;
+        w.wr.rdma.rkey = mc_rkey;
+        ugdr_send_wr *bad = nullptr;
+        if (int rc = ugdr_post_send(g->self_to, &w, &bad); rc != 0) return rc;
+    }
+    if (int rc = wait([&] { return sums == 1; }); rc != 0) return rc;
+    // 3. Tell every peer this shard is everywhere; done when every shard is.
+    if (int rc = notify(kDone, true); rc != 0) return rc;
+    return wait([&] { return done == n - 1 && lasts == n - 1; });
+}

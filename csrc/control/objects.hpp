@@ -33,7 +33,7 @@ struct DeviceInfo {
 
 // ---- memory --------------------------------------------------------------------------------
 
-enum class MemKind : uint8_t { cuda = 1, host = 2 };
+enum class MemKind : uint8_t { cuda = 1, host = 2, multicast = 3 };
 
 // What a client sends to register memory (decoded from the register-MR opaque).
 struct MemoryDescriptor {
@@ -44,7 +44,8 @@ struct MemoryDescriptor {
     uint64_t allocation_bytes = 0;
     uint64_t allocation_offset = 0;  // registered range start - allocation base
     std::vector<uint8_t> ipc_handle;
-    // host: the memfd region holding the range
+    // host: the memfd region holding the range; multicast: the NVLink multicast object (a CUDA
+    // POSIX-fd shareable handle), mapped from offset 0 over region_bytes
     uint64_t region_bytes = 0;
     uint64_t region_offset = 0;
     Fd region_fd;
@@ -60,6 +61,12 @@ struct OpenedMemory {
     std::vector<void *> bases;  // per-GPU IPC mapping bases to close (device memory)
     void *host_registered = nullptr;  // pinned host region to unregister (host memory)
     SharedMapping host;       // host regions stay mapped while registered
+    // NVLink multicast memory: loads through it are multimem reductions over every GPU bound to
+    // the object, stores reach every one of them.  The executors use it only as the source and
+    // destination of UGDR_X_WR_RDMA_WRITE_SUM_BF16.
+    bool multicast = false;
+    uint64_t mc_handle = 0;  // imported object
+    uint64_t mc_bytes = 0;   // mapped bytes at `address`
 };
 
 class MemoryBackend {

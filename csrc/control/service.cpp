@@ -238,6 +238,12 @@ Response ControlPlane::register_mr(uint64_t s, Request &r) {
         if (desc.region_offset > desc.region_bytes || r.length > desc.region_bytes - desc.region_offset)
             return status(EINVAL);
         desc.region_fd = std::move(r.fds[0]);
+    } else if (kind == uint8_t(MemKind::multicast)) {
+        desc.kind = MemKind::multicast;
+        if (!rd.be(&desc.region_bytes) || !rd.be(&desc.region_offset) || !rd.done()) return status(EPROTO);
+        if (r.fds.size() != 1) return status(EPROTO);
+        if (desc.region_offset != 0 || r.length > desc.region_bytes) return status(EINVAL);
+        desc.region_fd = std::move(r.fds[0]);
     } else {
         return status(EOPNOTSUPP);
     }

@@ -66,7 +66,7 @@ control::DeviceInfo CpuEngine::info() const {
 
 int CpuEngine::attach_mr(control::Mr &mr) {
     MrView v;
-    if (mr.mem.gpu < 0) v.base = static_cast<uint8_t *>(mr.mem.address);  // host only
+    if (mr.mem.gpu == -1 && !mr.mem.multicast) v.base = static_cast<uint8_t *>(mr.mem.address);  // host only
     v.client_base = mr.client_address;
     v.length = mr.length;
     v.access = mr.access;

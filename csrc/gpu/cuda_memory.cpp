@@ -1,4 +1,5 @@
 #include "gpu/cuda_memory.hpp"
+#include "gpu/multicast.hpp"
 
 #include <cuda_runtime_api.h>
 
@@ -52,6 +53,22 @@ int enable_all_peer_access(int n) {
 
 int DaemonMemoryBackend::open(control::MemoryDescriptor &desc, uint64_t length,
                               control::OpenedMemory *out) {
+    if (desc.kind == control::MemKind::multicast) {
+        if (inv_.count <= 0) return EOPNOTSUPP;
+        McMapping m;
+        const int rc = map_multicast(desc.region_fd.get(), desc.region_bytes, inv_.count, &m);
+        desc.region_fd.reset();
+        if (rc != 0) return rc;
+        out->multicast = true;
+        out->mc_handle = m.handle;
+        out->mc_bytes = m.bytes;
+        out->address = m.address;
+        out->gpu = -2;  // no owner: every team GPU reaches it through the same multicast view
+        out->device_address.assign(size_t(inv_.count), nullptr);
+        for (int g = 0; g < inv_.count; ++g)
+            if (m.reachable[size_t(g)]) out->device_address[size_t(g)] = m.address;
+        return 0;
+    }
     if (desc.kind == control::MemKind::host) {
         if (int rc = map_shared_fd(desc.region_fd.release(), 0, &out->host); rc != 0) return rc;
         if (desc.region_offset > out->host.bytes || length > out->host.bytes - desc.region_offset) {
@@ -124,6 +141,17 @@ int DaemonMemoryBackend::open(control::MemoryDescriptor &desc, uint64_t length,
 }
 
 void DaemonMemoryBackend::close(control::OpenedMemory &mem) noexcept {
+    if (mem.multicast) {
+        McMapping m;
+        m.address = mem.address;
+        m.bytes = mem.mc_bytes;
+        m.handle = mem.mc_handle;
+        unmap_multicast(m);
+        mem.address = nullptr;
+        mem.device_address.clear();
+        mem.multicast = false;
+        return;
+    }
     if (mem.gpu < 0) {
         if (mem.host_registered != nullptr) cudaHostUnregister(mem.host_registered);
         mem.host_registered = nullptr;

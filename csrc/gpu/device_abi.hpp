@@ -25,6 +25,9 @@ constexpr uint32_t kMaxSge = 32;
 constexpr uint32_t kJobSlots = 1024;         // chunked-job slots per engine
 constexpr uint32_t kInlineBytes = 4096;      // WRs up to this size are copied by the owner warp
 
+// DevMr::pad bits.
+constexpr uint32_t kMrMulticast = 1;  // an NVLink multicast view: multimem loads reduce, stores broadcast
+
 struct DevMr {
     uint64_t base;         // device-usable address of the first registered byte; 0 = unusable
     uint64_t client_base;  // client address of that byte
@@ -34,7 +37,7 @@ struct DevMr {
     uint32_t lkey;
     uint32_t rkey;
     uint32_t valid;
-    uint32_t pad;
+    uint32_t pad;  // flags (kMrMulticast)
 };
 
 struct DevCqConfig {

@@ -422,8 +422,62 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     return *reinterpret_cast<const uint32_t *>(&v);
 }
 
+// Multicast (NVLS) forms, for WRs whose source or destination MR is an NVLink multicast view:
+// the load has the NVSwitch read the 16 bytes from every GPU bound to the object and return the
+// fp32-accumulated bf16 sums; the store writes 16 bytes to every one of them.
+__device__ __forceinline__ uint4 mc_ld_sum(const uint8_t *p) {
+    uint4 v;
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ void mc_st(uint8_t *p, uint4 v) {
+    asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
+                 "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+// WrRec::pad[0] bits of a WRITE_SUM_BF16 whose MRs are multicast views (stage_wr checks that
+// such a WR has one SGE and 16-byte aligned addresses and length).
+constexpr uint32_t kWrSrcMulticast = 1, kWrDstMulticast = 2;
+
+__device__ __noinline__ void sum_stream_mc(uint32_t mc, const WrRec *rec, uint64_t remote, uint64_t off, uint64_t len, int lane) {
+    const uint8_t *src =
+        reinterpret_cast<const uint8_t *>(__ldcg(reinterpret_cast<const unsigned long long *>(&rec->seg[0].local))) + off;
+    uint8_t *dst = reinterpret_cast<uint8_t *>(remote) + off;
+    // Unicast writes of the inputs (earlier WRs, other GPUs) before the multicast reads.
+    asm volatile("fence.proxy.alias;" ::: "memory");
+    const uint64_t nvec = len >> 4;
+    constexpr int U = 4;
+    for (uint64_t v0 = lane; v0 < nvec; v0 += 32 * U) {
+        uint4 x[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const uint64_t v = v0 + uint64_t(u) * 32;
+            if (v < nvec) x[u] = (mc & kWrSrcMulticast) ? mc_ld_sum(src + v * 16) : ld128(src + v * 16);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const uint64_t v = v0 + uint64_t(u) * 32;
+            if (v >= nvec) continue;
+            if (mc & kWrDstMulticast)
+                mc_st(dst + v * 16, x[u]);
+            else
+                st128(dst + v * 16, x[u]);
+        }
+    }
+    // The multicast stores before the retire's fences and the peers' unicast reads of the result.
+    asm volatile("fence.proxy.alias;" ::: "memory");
+}
+
 __device__ __noinline__ void sum_stream(const WrRec *rec, uint32_t nseg, uint64_t remote, uint64_t off,
                                         uint64_t len, int lane) {
+    if (const uint32_t mc = __ldcg(&rec->pad[0]); mc != 0) {
+        sum_stream_mc(mc, rec, remote, off, len, lane);
+        return;
+    }
     // Lane i holds segment i's source address at `off`; the others come by shuffle.
     const uint64_t mine =
         uint32_t(lane) < nseg
@@ -433,8 +487,11 @@ __device__ __noinline__ void sum_stream(const WrRec *rec, uint32_t nseg, uint64_
     const uint32_t misaligned =
         __ballot_sync(0xffffffffu, (uint32_t(lane) < nseg && (mine & 15) != 0) || (lane == 0 && (uintptr_t(dst) & 15)));
     const uint64_t nvec = misaligned ? 0 : len >> 4;
-    uint64_t v = lane;
-    for (; v + 32 < nvec; v += 64) {  // two vectors per lane in flight
+    // Loop bounds are uniform over the warp, so every lane reaches each shuffle: full groups of
+    // 64 vectors (two per lane in flight), then groups of 32 with the lanes past the end idle.
+    uint64_t base = 0;
+    for (; base + 64 <= nvec; base += 64) {
+        const uint64_t v = base + lane;
         float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, b[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         for (uint32_t i = 0; i < nseg; ++i) {
             const uint8_t *src = reinterpret_cast<const uint8_t *>(__shfl_sync(0xffffffffu, (unsigned long long)mine, i));
@@ -453,18 +510,22 @@ __device__ __noinline__ void sum_stream(const WrRec *rec, uint32_t nseg, uint64_
         st128(dst + (v + 32) * 16, make_uint4(pack_bf16x2(b[0], b[1]), pack_bf16x2(b[2], b[3]),
                                               pack_bf16x2(b[4], b[5]), pack_bf16x2(b[6], b[7])));
     }
-    for (; v < nvec; v += 32) {
+    for (; base < nvec; base += 32) {
+        const uint64_t v = base + lane;
+        const bool in = v < nvec;
         float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         for (uint32_t i = 0; i < nseg; ++i) {
             const uint8_t *src = reinterpret_cast<const uint8_t *>(__shfl_sync(0xffffffffu, (unsigned long long)mine, i));
+            if (!in) continue;
             const uint4 x = ld128(src + v * 16);
             acc_bf16x2(a[0], a[1], x.x);
             acc_bf16x2(a[2], a[3], x.y);
             acc_bf16x2(a[4], a[5], x.z);
             acc_bf16x2(a[6], a[7], x.w);
         }
-        st128(dst + v * 16, make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]), pack_bf16x2(a[4], a[5]),
-                                       pack_bf16x2(a[6], a[7])));
+        if (in)
+            st128(dst + v * 16, make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]), pack_bf16x2(a[4], a[5]),
+                                           pack_bf16x2(a[6], a[7])));
     }
     // Tail, or everything when an address is not 16-byte aligned: 2-byte elements.  The loop
     // bound is uniform over the warp so every lane reaches each shuffle.
@@ -1076,7 +1137,7 @@ __device__ __forceinline__ uint64_t keep_hi(bool on, uint64_t v) {
     return a;
 }
 
-__device__ void stage_wr(Warp &w, const QpView &v, const uint8_t *wqe, WrRec *rec, uint32_t *status_out,
+__device__ __noinline__ void stage_wr(Warp &w, const QpView &v, const uint8_t *wqe, WrRec *rec, uint32_t *status_out,
                          uint64_t *total_out, uint64_t *remote_out, uint64_t *lo_out, uint64_t *hi_out) {
     const queue::SendWqe *h = reinterpret_cast<const queue::SendWqe *>(wqe);
     const uint32_t op = h->opcode;
@@ -1110,7 +1171,7 @@ __device__ void stage_wr(Warp &w, const QpView &v, const uint8_t *wqe, WrRec *re
     }
     // --- then check ---
     uint64_t local = 0;
-    bool bad = false;
+    bool bad = false, lmc = false;
     if (mine && len != 0) {
         const uint64_t base = (uint64_t(l0.y) << 32) | l0.x, cb = (uint64_t(l0.w) << 32) | l0.z;
         const uint64_t ml = (uint64_t(l1.y) << 32) | l1.x;
@@ -1121,6 +1182,7 @@ __device__ void stage_wr(Warp &w, const QpView &v, const uint8_t *wqe, WrRec *re
             bad = true;
         else
             local = base + (sg->address - cb);
+        lmc = valid && (l2.w & kMrMulticast) != 0;
     }
     const bool any_bad = __any_sync(0xffffffffu, bad);
     uint64_t total = len;
@@ -1128,6 +1190,11 @@ __device__ void stage_wr(Warp &w, const QpView &v, const uint8_t *wqe, WrRec *re
     if (status == UGDR_WC_SUCCESS && any_bad) status = UGDR_WC_LOC_PROT_ERR;
     if (status == UGDR_WC_SUCCESS && total > 0xffffffffull) status = UGDR_WC_LOC_LEN_ERR;  // 4 GiB - 1 max
     if (status == UGDR_WC_SUCCESS && is_atomic(op) && total != 8) status = UGDR_WC_LOC_LEN_ERR;
+    // A multicast MR is only the single 16-byte aligned SGE of a WRITE_SUM_BF16.
+    const bool any_lmc = __any_sync(0xffffffffu, lmc);
+    if (status == UGDR_WC_SUCCESS && any_lmc &&
+        (!sum || nsge != 1 || (__shfl_sync(0xffffffffu, (local | len), 0) & 15) != 0))
+        status = UGDR_WC_LOC_QP_OP_ERR;
     if (status == UGDR_WC_SUCCESS && sum && nsge > 0) {
         // Every SGE has the same even length L, at a 2-byte aligned address; the WR moves L bytes.
         const uint64_t l0 = __shfl_sync(0xffffffffu, len, 0);
@@ -1150,6 +1217,7 @@ __device__ void stage_wr(Warp &w, const QpView &v, const uint8_t *wqe, WrRec *re
     }
 
     uint64_t remote = 0;
+    bool rmc = false;
     if (status == UGDR_WC_SUCCESS) {
         if (v.peer == nullptr || v.lost || pstate == UGDR_QPS_RESET || !pactive) {
             status = UGDR_WC_RETRY_EXC_ERR;
@@ -1173,6 +1241,9 @@ __device__ void stage_wr(Warp &w, const QpView &v, const uint8_t *wqe, WrRec *re
                 if (status == UGDR_WC_SUCCESS && is_atomic(op) && (ra & 7) != 0)
                     status = UGDR_WC_REM_INV_REQ_ERR;
                 if (status == UGDR_WC_SUCCESS && sum && (ra & 1) != 0) status = UGDR_WC_REM_INV_REQ_ERR;
+                rmc = valid && (r2.w & kMrMulticast) != 0;
+                if (status == UGDR_WC_SUCCESS && rmc && (!sum || ((remote | total) & 15) != 0))
+                    status = UGDR_WC_REM_INV_REQ_ERR;
             }
         }
     }
@@ -1189,6 +1260,7 @@ __device__ void stage_wr(Warp &w, const QpView &v, const uint8_t *wqe, WrRec *re
         rec->nchunks = 0;
         rec->lo = lo < hi ? lo : 0;
         rec->hi = lo < hi ? hi : 0;
+        rec->pad[0] = (any_lmc ? kWrSrcMulticast : 0u) | (rmc ? kWrDstMulticast : 0u);
     }
     __syncwarp();
     *status_out = status;
@@ -1455,7 +1527,10 @@ __device__ uint32_t issue_fast(Warp &w, DevQp *qp, const QpView &v, const uint8_
     // --- check ---
     uint32_t status = UGDR_WC_SUCCESS;
     uint64_t local = 0, remote = 0;
-    if (act && len != 0) {
+    if (act && len != 0 && ((l2.w | r2.w) & kMrMulticast) != 0) {
+        // Multicast views serve WRITE_SUM_BF16 only.
+        status = (l2.w & kMrMulticast) ? UGDR_WC_LOC_QP_OP_ERR : UGDR_WC_REM_INV_REQ_ERR;
+    } else if (act && len != 0) {
         const uint64_t base = (uint64_t(l0.y) << 32) | l0.x, cb = (uint64_t(l0.w) << 32) | l0.z;
         const uint64_t ml = (uint64_t(l1.y) << 32) | l1.x;
         const bool need_write = op == UGDR_WR_RDMA_READ;

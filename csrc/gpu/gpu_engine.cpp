@@ -212,6 +212,7 @@ int GpuEngine::attach_mr(control::Mr &mr) {
     d.lkey = mr.lkey;
     d.rkey = mr.rkey;
     d.valid = 1;
+    d.pad = mr.mem.multicast ? kMrMulticast : 0u;
     return copy_to_device(&mrs_[mr.table_slot], &d, sizeof(d));
 }
 

@@ -252,6 +252,16 @@ int ugdr_x_query_device(ugdr_device *device, ugdr_x_device_info *info) UGDR_NOEX
 
 /* Host memory that the daemon can reach: a memfd-backed shared mapping.  Only ranges inside
  * such a buffer (or `cudaMalloc` device memory) can be registered with ugdr_reg_mr. */
+/* Register an NVLink multicast object (NVLS; see ugdr_x_nvls_* in ugdr/collective.h) as an MR.
+ * `mc_fd` is the object's POSIX shareable handle, `address` this process's multicast mapping of
+ * it (SGE and remote addresses are given in it) and `length` the bytes registered from offset 0.
+ * The daemon maps the object itself.  Reading through such an MR returns the sum over every GPU
+ * bound to the object (the NVSwitch reduces), writing stores to every one of them; the
+ * executors accept it only as the single SGE and as the remote range of
+ * UGDR_X_WR_RDMA_WRITE_SUM_BF16 (16-byte aligned), so one such WR is an allreduce of its range.
+ * Every rank's physical memory stays bound while the MR exists: deregister before releasing
+ * the object.  GPU contexts only (EOPNOTSUPP elsewhere). */
+ugdr_mr *ugdr_x_reg_mr_multicast(ugdr_pd *pd, void *address, size_t length, int access, int mc_fd) UGDR_NOEXCEPT;
 void *ugdr_x_alloc_host(size_t length) UGDR_NOEXCEPT;
 int ugdr_x_free_host(void *address) UGDR_NOEXCEPT;
 

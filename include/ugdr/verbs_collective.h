@@ -71,6 +71,18 @@ uint64_t ugdr_x_verbs_allreduce_stage_bytes(uint64_t count, int n) UGDR_VC_NOEXC
 int ugdr_x_verbs_allreduce_bf16(ugdr_x_vgroup *g, uint64_t count, int pieces,
                                 uint64_t timeout_ns) UGDR_VC_NOEXCEPT;
 
+/* The same sum through NVLink SHARP: `mc_addr` is this process's multicast view of an NVLS
+ * object holding the data (every rank's unicast copy at the same offsets), registered on this
+ * rank's PD with ugdr_x_reg_mr_multicast (mc_lkey / mc_rkey).  After a ready exchange (zero-length
+ * WRITE_WITH_IMMs), each rank posts ONE UGDR_X_WR_RDMA_WRITE_SUM_BF16 on its loopback QP whose
+ * source and destination are its shard in the multicast view: the executor's multimem loads have
+ * the NVSwitch sum the shard over every GPU (fp32 accumulation) and its multimem stores write the
+ * sum to every GPU; a second exchange tells every rank that every shard is done.  Per GPU about
+ * (1 + 1/n) of the buffer crosses each link direction.  count a multiple of 8, mc_addr 16-byte
+ * aligned.  Returns 0, EINVAL, ETIMEDOUT, EIO or a verbs errno. */
+int ugdr_x_verbs_allreduce_bf16_mc(ugdr_x_vgroup *g, uint64_t mc_addr, uint32_t mc_lkey, uint32_t mc_rkey,
+                                   uint64_t count, uint64_t timeout_ns) UGDR_VC_NOEXCEPT;
+
 /* MoE all-to-all on the verbs.  Experts split evenly over the ranks (rank q owns experts
  * [q * nexp / n, (q + 1) * nexp / n)).  The permutes are the SGE lists of the WRs: dispatch
  * WRITEs gather each expert group's token rows (one SGE per row) into one contiguous range of

@@ -230,3 +230,103 @@ def test_verbs_moe_exact_permutation_on_the_executors(world):
     if gpu_count() < world:
         pytest.skip(f"needs {world} GPUs")
     _run_moe(world, True, (512, 1024, 8, 32), calls=2)
+
+
+# ---- allreduce through NVLink SHARP on the verbs (multicast MR) -----------------------------------
+
+
+def _nvls_worker(rank: int, world: int, port: int, count: int, errq) -> None:
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    daemon = None
+    try:
+        from ugdr_b200.parallel import nvls
+        from ugdr_b200.parallel.verbs_collectives import VerbsGroup, shared_daemon
+
+        def bcast(obj):
+            lst = [obj]
+            dist.broadcast_object_list(lst, src=0)
+            return lst[0]
+
+        def exchange(obj):
+            out = [None] * world
+            dist.all_gather_object(out, obj)
+            return out
+
+        torch.cuda.set_device(rank)
+        daemon = shared_daemon(rank, world, bcast)
+        g = VerbsGroup(rank, world, rank, 8, exchange, pieces=1)
+        buf = nvls.NvlsBuffer(count * 2, rank, world, exchange)
+        try:
+            for call in range(2):
+                v = buf.view(torch.bfloat16, count)
+                v.copy_(_inputs(rank, count, call).cuda())
+                torch.cuda.synchronize()
+                g.allreduce_nvls(buf, count)
+                got = v.cpu()
+                want = _expected(world, count, call).float()
+                # The switch accumulates in fp32 in its own order and rounds once.
+                bad = (got.float() - want).abs() > want.abs() * 2.0 ** -7 + 1e-3
+                assert not bool(bad.any()), f"rank {rank} call {call}: {int(bad.sum())} elements off"
+                del v
+                dist.barrier()
+        finally:
+            g.release_multicast()  # the daemon's mapping goes before any rank unbinds
+            dist.barrier()
+            buf.close()
+            g.close()
+        dist.barrier()
+    except BaseException as e:
+        errq.put(f"rank {rank}: {type(e).__name__}: {e}")
+        raise
+    finally:
+        if daemon is not None:
+            daemon.stop()
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_verbs_nvls_allreduce_on_the_executors(world):
+    """One WRITE_SUM_BF16 per rank from and to its shard of a multicast MR: the executor's
+    multimem loads have the NVSwitch sum, its multimem stores broadcast."""
+    if gpu_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    from ugdr_b200.parallel import nvls
+
+    if not nvls.supported(0):
+        pytest.skip("no NVLS multicast on this box")
+    ctx = mp.get_context("spawn")
+    errq = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_nvls_worker, args=(r, world, port, (1 << 22) + 64, errq)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    errs = []
+    while not errq.empty():
+        errs.append(errq.get())
+    assert not errs, errs
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+
+
+def test_multicast_mr_needs_a_gpu_context(cpu_daemon):
+    """The host engine cannot reach NVLink multicast memory: registration is refused."""
+    from ugdr_b200 import verbs as V
+
+    ctx = V.Context(V.find_device(kind=0))
+    pd = ctx.alloc_pd()
+    r, w = os.pipe()
+    try:
+        with pytest.raises(V.UgdrError):
+            pd.reg_mr_multicast(1 << 21, 1 << 21, 1, r)
+        with pytest.raises(V.UgdrError):
+            pd.reg_mr_multicast(1 << 21, 1 << 21, 1, -1)
+    finally:
+        os.close(r)
+        os.close(w)
+        pd.dealloc()
+        ctx.close()

@@ -260,6 +260,7 @@ def lib() -> C.CDLL:
         "ugdr_post_send": (i, [vp, C.POINTER(SendWr), C.POINTER(C.POINTER(SendWr))]),
         "ugdr_post_recv": (i, [vp, C.POINTER(RecvWr), C.POINTER(C.POINTER(RecvWr))]),
         "ugdr_x_query_device": (i, [vp, C.POINTER(DeviceInfo)]),
+        "ugdr_x_reg_mr_multicast": (C.POINTER(Mr), [vp, vp, sz, i, i]),
         "ugdr_x_alloc_host": (vp, [sz]),
         "ugdr_x_free_host": (i, [vp]),
         "ugdr_x_query_engine_stats": (i, [vp, C.POINTER(EngineStats), i]),

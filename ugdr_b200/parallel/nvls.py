@@ -112,15 +112,20 @@ class NvlsBuffer:
             server.start()
             ready.wait(timeout)
         name = exchange(name)[0]
+        # The object's descriptor stays open: registering the buffer with the verbs daemon
+        # (ugdr_x_reg_mr_multicast) hands the daemon a duplicate of it.
+        self.fd = -1
         if rank != 0:
             got = _fetch_fd(name, timeout)
             try:
                 check(L.ugdr_x_nvls_import(got, world, nbytes, C.byref(self.h)), "ugdr_x_nvls_import")
-            finally:
+            except BaseException:
                 os.close(got)
+                raise
+            self.fd = got
         if server is not None:
             server.join(timeout)
-            os.close(fd.value)
+            self.fd = fd.value
             if errors:
                 raise RuntimeError(f"passing the NVLS descriptor failed: {errors[0]}")
         check(L.ugdr_x_nvls_add_device(C.byref(self.h)), "ugdr_x_nvls_add_device")
@@ -142,6 +147,9 @@ class NvlsBuffer:
             torch.cuda.synchronize()
             self._exchange(None)
             _lib().ugdr_x_nvls_release(C.byref(self.h))
+        if self.fd >= 0:
+            os.close(self.fd)
+            self.fd = -1
 
 
 class _Raw:

@@ -69,6 +69,7 @@ class VerbsGroup:
             raise ValueError("world must be 1..8 and pieces 1..64")
         self.rank, self.world, self.count, self.pieces = rank, world, count, pieces
         self.device_kind = device_kind
+        self._mc = {}
         L = _lib()
         dev = V.find_device(gpu=gpu) if device_kind == 1 else V.find_device(kind=0)
         self.ctx = V.Context(dev)
@@ -132,7 +133,36 @@ class VerbsGroup:
         if rc != 0:
             raise V.UgdrError(rc, f"ugdr_x_verbs_allreduce_bf16: {N.errname(rc)}")
 
+    def allreduce_nvls(self, nvbuf, count: int, timeout_s: float = 60.0) -> None:
+        """In-place bf16 sum of the first `count` elements of an NVLS buffer (parallel.nvls.NvlsBuffer,
+        each rank's data in its unicast view) through NVLink SHARP, on the verbs: the buffer is
+        registered once as a multicast MR and every rank posts one WRITE_SUM_BF16 of its shard
+        (ugdr_x_verbs_allreduce_bf16_mc)."""
+        L = _lib()
+        if not getattr(L, "_vcoll_mc_sig", False):
+            L.ugdr_x_verbs_allreduce_bf16_mc.restype = C.c_int
+            L.ugdr_x_verbs_allreduce_bf16_mc.argtypes = [C.POINTER(_Group), C.c_uint64, C.c_uint32, C.c_uint32,
+                                                         C.c_uint64, C.c_uint64]
+            L._vcoll_mc_sig = True
+        mr = self._mc.get(id(nvbuf))
+        if mr is None:
+            acc = N.ACCESS_LOCAL_WRITE | N.ACCESS_REMOTE_WRITE
+            mr = self.pd.reg_mr_multicast(int(nvbuf.h.mc), nvbuf.nbytes, acc, nvbuf.fd)
+            self._mc[id(nvbuf)] = mr
+        torch.cuda.synchronize()
+        rc = L.ugdr_x_verbs_allreduce_bf16_mc(C.byref(self._g), int(nvbuf.h.mc), mr.lkey, mr.rkey, count,
+                                              int(timeout_s * 1e9))
+        if rc != 0:
+            raise V.UgdrError(rc, f"ugdr_x_verbs_allreduce_bf16_mc: {N.errname(rc)}")
+
+    def release_multicast(self) -> None:
+        """Deregister the multicast MRs; every rank does this before its NVLS buffers close."""
+        for mr in self._mc.values():
+            mr.dereg()
+        self._mc.clear()
+
     def close(self) -> None:
+        self.release_multicast()
         for q in list(self.to.values()) + list(self.frm.values()) + [self.self_to, self.self_peer]:
             q.destroy()
         self.buf_mr.dereg()

@@ -240,6 +240,10 @@ class Pd:
     def reg_mr(self, addr: int, length: int, access: int) -> "MemoryRegion":
         return MemoryRegion(self, addr, length, access)
 
+    def reg_mr_multicast(self, mc_addr: int, length: int, access: int, mc_fd: int) -> "MemoryRegion":
+        """An NVLS multicast object as an MR (see ugdr_x_reg_mr_multicast)."""
+        return MemoryRegion(self, mc_addr, length, access, mc_fd=mc_fd)
+
     def create_qp(self, send_cq: "CompletionQueue", recv_cq: "CompletionQueue | None" = None,
                   max_send_wr: int = 128, max_recv_wr: int = 128, max_send_sge: int = 1,
                   max_recv_sge: int = 1, sq_sig_all: bool = False) -> "QueuePair":
@@ -248,9 +252,13 @@ class Pd:
 
 
 class MemoryRegion:
-    def __init__(self, pd: Pd, addr: int, length: int, access: int):
+    def __init__(self, pd: Pd, addr: int, length: int, access: int, mc_fd: int = -1):
         self.pd = pd
-        self.p = _check_ptr(N.lib().ugdr_reg_mr(pd.h, C.c_void_p(addr), length, access), "ugdr_reg_mr")
+        if mc_fd >= 0:  # an NVLink multicast object (ugdr_x_reg_mr_multicast); addr: its multicast view
+            self.p = _check_ptr(N.lib().ugdr_x_reg_mr_multicast(pd.h, C.c_void_p(addr), length, access, mc_fd),
+                                "ugdr_x_reg_mr_multicast")
+        else:
+            self.p = _check_ptr(N.lib().ugdr_reg_mr(pd.h, C.c_void_p(addr), length, access), "ugdr_reg_mr")
         self.addr = addr
         self.length = length
         self.lkey = self.p.contents.lkey
