@@ -592,7 +592,8 @@ int ugdr_x_query_engine_stats(ugdr_context *ctx, ugdr_x_engine_stats *stats, int
         !rd.be(&stats->inline_runs) || !rd.be(&stats->busy_ns) || !rd.be(&stats->fast_batches) ||
         !rd.be(&stats->fast_fetch_ns) || !rd.be(&stats->fast_exec_ns) || !rd.be(&stats->fast_reserve_ns) ||
         !rd.be(&stats->fast_publish_ns) || !rd.be(&stats->slow_wrs) || !rd.be(&stats->slow_issue_ns) ||
-        !rd.be(&stats->job_slot_misses) || !rd.be(&stats->publish_waits) || !rd.be(&stats->publish_wait_ns))
+        !rd.be(&stats->job_slot_misses) || !rd.be(&stats->publish_waits) || !rd.be(&stats->publish_wait_ns) ||
+        !rd.be(&stats->mr_detach_live) || !rd.be(&stats->mr_detach_quiesced))
         return EPROTO;
     return 0;
 }

@@ -127,6 +127,19 @@ struct DevQp {
     DevQpState st;
 };
 
+// Per QP slot, written by the owner warp at the end of every service pass: the MR epoch the
+// pass started with, and the QP's issue and retire cursors after it.  An MR is deregistered
+// without stopping the executor once every active QP has begun a pass under the new epoch (no
+// later resolution can use the invalidated entry: per-warp MR caches are keyed by epoch) and has
+// retired everything issued until then (no in-flight WR still addresses the memory).
+struct QpProgress {
+    unsigned int seen_epoch;
+    unsigned int pad;
+    unsigned long long issue;
+    unsigned long long head;
+    unsigned long long pad2;
+};
+
 // One chunked job: WRs [first, first + nwr) of one QP's window (indices mod kWindow), cut into
 // `chunk_bytes` chunks numbered across the WRs (WR i owns chunks [start[i], start[i + 1])).
 // `ctl` = generation (high 32) | next unclaimed chunk (low 32); claims are fetch-and-adds on it.
@@ -178,7 +191,8 @@ struct DevStats {
     unsigned int exiting;
     unsigned int error_code;  // first bounded wait that gave up (see ExecError)
     unsigned int qp_slots;
-    unsigned int pad[13];
+    unsigned int mr_epoch;  // bumped by the host when an MR entry is invalidated (see QpProgress)
+    unsigned int pad[12];
 };
 
 enum ExecError : uint32_t {
@@ -228,6 +242,7 @@ struct ExecParams {
     TraceRec *trace;             // null: tracing off
     unsigned int *trace_count;   // one append counter per CTA
     uint32_t trace_cap;          // records per CTA
+    QpProgress *progress;        // one per QP slot
     uint32_t bulk_min;           // chunk pieces of at least this many 16-byte aligned bytes go
                                  // through the TMA bulk-copy engine (0: never)
 };

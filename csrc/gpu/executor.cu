@@ -557,11 +557,11 @@ struct QpView {
     uint32_t pstate, perr, pactive, pacc, ppd;
 };
 
-// Per-warp cache of the two MR entries the fast path used last.  MR table entries change only
-// while the executor is stopped (deregistration quiesces it), and a key's generation bits make a
-// reused slot miss, so a hit is always current within a launch.
+// Per-warp cache of the two MR entries the fast path used last.  An entry hits only under the
+// MR epoch it was cached in: deregistration bumps the epoch after it invalidates the table entry,
+// and a key's generation bits make a reused slot miss.
 struct MrCacheEntry {
-    uint32_t key, pad[3];
+    uint32_t key, epoch, pad[2];  // epoch: DevStats::mr_epoch when cached (a newer one misses)
     uint4 part[3];
 };
 
@@ -601,6 +601,8 @@ struct Warp {
     uint64_t vt, vhead, vissue, vtail, t_reserved;
     QpView *vv;  // cached view of the QP serviced last (shared memory)
     Tma *tma;    // this warp's TMA staging (null for the leader warp, which runs no chunks)
+    volatile uint32_t *mr_epoch;  // the CTA's shared copy of DevStats::mr_epoch
+    uint32_t epoch;               // the MR epoch of the current service pass
 };
 
 // Appends one trace record (lane 0 only; the caller checks that tracing is on).  Not inlined:
@@ -1483,8 +1485,8 @@ __device__ uint32_t issue_fast(Warp &w, DevQp *qp, const QpView &v, const uint8_
     // QP view ---
     uint4 l0{}, l1{}, l2{}, r0{}, r1{}, r2{};
     const MrCacheEntry *lc = &w.mrc[0], *rc = &w.mrc[1];
-    const bool lhit = act && lc->key == sg->lkey && sg->lkey != 0;
-    const bool rhit = act && rc->key == h->rkey && h->rkey != 0;
+    const bool lhit = act && lc->key == sg->lkey && sg->lkey != 0 && lc->epoch == w.epoch;
+    const bool rhit = act && rc->key == h->rkey && h->rkey != 0 && rc->epoch == w.epoch;
     if (act) {
         if (lhit) {
             l0 = lc->part[0];
@@ -1511,12 +1513,14 @@ __device__ uint32_t issue_fast(Warp &w, DevQp *qp, const QpView &v, const uint8_
     if (j == 0 && act) {  // remember lane 0's entries (only valid ones)
         if (!lhit && l2.z && l2.x == sg->lkey) {
             w.mrc[0].key = sg->lkey;
+            w.mrc[0].epoch = w.epoch;
             w.mrc[0].part[0] = l0;
             w.mrc[0].part[1] = l1;
             w.mrc[0].part[2] = l2;
         }
         if (!rhit && r2.z && r2.y == h->rkey) {
             w.mrc[1].key = h->rkey;
+            w.mrc[1].epoch = w.epoch;
             w.mrc[1].part[0] = r0;
             w.mrc[1].part[1] = r1;
             w.mrc[1].part[2] = r2;
@@ -1655,8 +1659,28 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
 
 // Service one QP: retire, flush when in ERR, else issue a batch of WQEs and retire again.
 // Warp-wide; returns the work done.
+__device__ uint32_t service_pass(Warp &w, DevQp *qp, uint8_t *wqe_smem, queue::Cqe *cqe_smem, JobRing *jr,
+                                 uint32_t *bitmap, uint32_t nwarps);
+
+// One service pass over a QP under the current MR epoch, then its progress record (see
+// QpProgress): the epoch the pass started with and the cursors after it.
 __device__ uint32_t service_qp(Warp &w, DevQp *qp, uint8_t *wqe_smem, queue::Cqe *cqe_smem, JobRing *jr,
                                uint32_t *bitmap, uint32_t nwarps) {
+    w.epoch = *w.mr_epoch;
+    __syncwarp();
+    const uint32_t work = service_pass(w, qp, wqe_smem, cqe_smem, jr, bitmap, nwarps);
+    if (w.lane == 0 && w.vq == qp) {
+        QpProgress *pr = &w.p->progress[qp - w.p->qps];
+        pr->issue = w.vissue;
+        pr->head = w.vhead;
+        __threadfence();  // the cursors before the epoch that vouches for them
+        pr->seen_epoch = w.epoch;
+    }
+    return work;
+}
+
+__device__ uint32_t service_pass(Warp &w, DevQp *qp, uint8_t *wqe_smem, queue::Cqe *cqe_smem, JobRing *jr,
+                                 uint32_t *bitmap, uint32_t nwarps) {
     const uint64_t max_ns = w.p->max_wait_ns;
     // The configuration this pass needs: cached per warp for the QP it serviced last and re-read
     // at least every 20 us (a host state change is seen within that; slots are only reused after
@@ -1973,7 +1997,7 @@ __global__ void __launch_bounds__(kThreads, 1) executor_kernel(ExecParams p) {
     __shared__ CqCache cq_cache[kWarps];
     __shared__ QpView qp_view[kWarps];
     __shared__ volatile uint32_t s_bits[32];
-    __shared__ volatile uint32_t s_slots, s_exit, s_work;
+    __shared__ volatile uint32_t s_slots, s_exit, s_work, s_epoch;
     Warp w;
     w.p = &p;
     w.lane = threadIdx.x & 31;
@@ -2015,8 +2039,11 @@ __global__ void __launch_bounds__(kThreads, 1) executor_kernel(ExecParams p) {
     const uint64_t t_launch = gtime();
     const bool leader = w.wi == 0;
     if (threadIdx.x < 32) s_bits[threadIdx.x] = ld_vol32(&bits[threadIdx.x]);
+    w.mr_epoch = &s_epoch;
+    w.epoch = 0;
     if (threadIdx.x == 0) {
         s_slots = ld_vol32(&p.stats->qp_slots);
+        s_epoch = ld_vol32(&p.stats->mr_epoch);
         s_exit = 0;
         s_work = 0;
         if (blockIdx.x == 0) atomicAdd(&p.stats->launches_seen, 1ull);
@@ -2053,6 +2080,7 @@ __global__ void __launch_bounds__(kThreads, 1) executor_kernel(ExecParams p) {
                 int exit_now = 0;
                 if (w.lane == 0) {
                     s_slots = ld_vol32(&p.stats->qp_slots);
+                    s_epoch = ld_vol32(&p.stats->mr_epoch);
                     const bool busy = work != 0 || s_work != 0;
                     s_work = 0;
                     // Activity stamps are rare (one per CTA per 50 us) so the shared word

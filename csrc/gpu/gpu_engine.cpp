@@ -92,6 +92,7 @@ class GpuEngine final : public control::Engine {
     // A stopped kernel has finished every piece it claimed, so with the bitmap clear no copy
     // into any MR is left half done.
     bool copies_pending_locked();
+    bool mr_grace_locked();
     void monitor();
     void fill_qp_config(control::Qp &qp, DevQpConfig *cfg);
 
@@ -101,6 +102,9 @@ class GpuEngine final : public control::Engine {
     cudaEvent_t ev_start_ = nullptr, ev_done_ = nullptr;
     DevMr *mrs_ = nullptr;
     DevQp *qps_ = nullptr;
+    QpProgress *progress_ = nullptr;  // per QP slot, written by the owner warps
+    uint32_t mr_epoch_ = 0;           // last value stored in DevStats::mr_epoch
+    uint64_t mr_fast_detaches_ = 0, mr_slow_detaches_ = 0;
     DevCq *cqs_ = nullptr;
     JobRing *jobs_ = nullptr;
     DevStats *stats_ = nullptr;
@@ -157,6 +161,7 @@ int GpuEngine::init() {
         !ok(cudaEventCreate(&ev_start_)) || !ok(cudaEventCreate(&ev_done_)) ||
         !ok(cudaMalloc(reinterpret_cast<void **>(&mrs_), sizeof(DevMr) * kMaxMrs)) ||
         !ok(cudaMalloc(reinterpret_cast<void **>(&qps_), sizeof(DevQp) * kMaxQpsPerEngine)) ||
+        !ok(cudaMalloc(reinterpret_cast<void **>(&progress_), sizeof(QpProgress) * kMaxQpsPerEngine)) ||
         !ok(cudaMalloc(reinterpret_cast<void **>(&cqs_), sizeof(DevCq) * kMaxCqsPerEngine)) ||
         !ok(cudaMalloc(reinterpret_cast<void **>(&jobs_), job_ring_bytes())) ||
         !ok(cudaMalloc(reinterpret_cast<void **>(&stats_), sizeof(DevStats))) ||
@@ -168,6 +173,7 @@ int GpuEngine::init() {
     std::memset(ctrl_, 0, sizeof(HostCtrl));
     cudaMemsetAsync(mrs_, 0, sizeof(DevMr) * kMaxMrs, ctl_stream_);
     cudaMemsetAsync(qps_, 0, sizeof(DevQp) * kMaxQpsPerEngine, ctl_stream_);
+    cudaMemsetAsync(progress_, 0, sizeof(QpProgress) * kMaxQpsPerEngine, ctl_stream_);
     cudaMemsetAsync(cqs_, 0, sizeof(DevCq) * kMaxCqsPerEngine, ctl_stream_);
     cudaMemsetAsync(jobs_, 0, job_ring_bytes(), ctl_stream_);
     cudaMemsetAsync(stats_, 0, sizeof(DevStats), ctl_stream_);
@@ -218,14 +224,23 @@ int GpuEngine::attach_mr(control::Mr &mr) {
 
 void GpuEngine::detach_mr(control::Mr &mr) noexcept {
     // Clear the entry's `valid` word first (one aligned 4-byte store, so a running warp sees
-    // either the whole old entry or an invalid one): a kernel that quiesce() restarts to finish
-    // pending copies then resolves no new WR against this MR.  Warps of the running kernel may
-    // still hold it in their MR caches, which the stop clears.  The rest of the entry is zeroed
-    // once the kernel is stopped.
+    // either the whole old entry or an invalid one): from then on no WR resolves against it.
+    // Then, without stopping the executor, wait for a grace period (mr_grace_locked): every
+    // active QP has started a service pass under a new MR epoch (so no per-warp cache still
+    // serves the entry) and has retired every WR issued before that (so nothing in flight
+    // still addresses the memory).  Only if that does not happen in time is the executor
+    // quiesced, as for the other destructive operations.
     {
         std::lock_guard<std::mutex> lk(mu_);
         const uint32_t invalid = 0;
         copy_to_device(&mrs_[mr.table_slot].valid, &invalid, sizeof(invalid));
+        if (mr_grace_locked()) {
+            DevMr d{};
+            copy_to_device(&mrs_[mr.table_slot], &d, sizeof(d));
+            mr_fast_detaches_ += 1;
+            return;
+        }
+        mr_slow_detaches_ += 1;
     }
     quiesce();
     {
@@ -447,6 +462,40 @@ bool GpuEngine::kernel_done_locked() {
     return true;
 }
 
+bool GpuEngine::mr_grace_locked() {
+    if (!running_) return !copies_pending_locked();  // no kernel: nothing resolves or copies
+    mr_epoch_ += 1;
+    if (copy_to_device(&stats_->mr_epoch, &mr_epoch_, sizeof(mr_epoch_)) != 0) return false;
+    const uint32_t epoch = mr_epoch_;
+    uint32_t nslots = 0;
+    for (const QpEntry &e : qps_host_) nslots = std::max(nslots, e.slot + 1);
+    if (nslots == 0) return !copies_pending_locked();
+    std::vector<QpProgress> pr(nslots);
+    std::vector<uint64_t> issued(nslots, 0);
+    const auto deadline = Clock::now() + std::chrono::milliseconds(cfg_.max_wait_ms);
+    for (int phase = 0; phase < 2;) {
+        if (copy_from_device(pr.data(), progress_, sizeof(QpProgress) * nslots) != 0) return false;
+        bool all = true;
+        for (const QpEntry &e : qps_host_) {
+            const QpProgress &q = pr[e.slot];
+            if (phase == 0)
+                all &= int32_t(q.seen_epoch - epoch) >= 0;
+            else
+                all &= q.head >= issued[e.slot];
+        }
+        if (all) {
+            if (phase == 0)
+                for (const QpEntry &e : qps_host_) issued[e.slot] = pr[e.slot].issue;
+            ++phase;
+            continue;
+        }
+        if (kernel_done_locked()) return !copies_pending_locked();  // it went idle or stopped
+        if (Clock::now() > deadline) return false;
+        std::this_thread::sleep_for(std::chrono::microseconds(10));
+    }
+    return true;
+}
+
 bool GpuEngine::copies_pending_locked() {
     uint32_t words[32] = {};
     if (copy_from_device(words, reinterpret_cast<uint8_t *>(jobs_) + sizeof(JobRing), sizeof(words)) != 0)
@@ -507,6 +556,7 @@ int GpuEngine::launch_locked(uint32_t mode, uint64_t expected, bool timed) {
     p.trace_count = trace_count_;
     p.trace_cap = trace_cap_;
     p.bulk_min = cfg_.bulk_min_bytes;
+    p.progress = progress_;
     if (vis_.mode() == VisibilityGate::Mode::kFlush && vis_.before_publish() != 0) return EIO;
     if (timed) cudaEventRecord(ev_start_, exec_stream_);
     const int rc = launch_executor(p, cfg_.ctas, exec_stream_);
@@ -673,6 +723,8 @@ int GpuEngine::stats(control::EngineStats *out, bool reset) {
     out->job_slot_misses = st.job_slot_misses;
     out->publish_waits = st.publish_waits;
     out->publish_wait_ns = st.publish_wait_ns;
+    out->mr_detach_live = mr_fast_detaches_;
+    out->mr_detach_quiesced = mr_slow_detaches_;
     if (reset) {
         // Counters only (a running kernel may race a few increments into the fresh window).
         cudaMemsetAsync(stats_, 0, offsetof(DevStats, last_work_ns), ctl_stream_);

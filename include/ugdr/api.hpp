@@ -285,6 +285,9 @@ typedef struct ugdr_x_engine_stats {
      * time; issue attempts that found no free job slot; CQ publishes that had to wait for their turn
      * behind other producers of the same CQ, and the summed wait */
     uint64_t slow_wrs, slow_issue_ns, job_slot_misses, publish_waits, publish_wait_ns;
+    /* MR deregistrations finished while the executor kept running (grace period), and those
+     * that had to stop it (not reset by `reset`) */
+    uint64_t mr_detach_live, mr_detach_quiesced;
 } ugdr_x_engine_stats;
 
 int ugdr_x_query_engine_stats(ugdr_context *context, ugdr_x_engine_stats *stats,

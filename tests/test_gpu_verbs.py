@@ -319,6 +319,53 @@ def test_qp_stats_on_the_executor(gpu_env):
     assert (st.send_retired, st.bytes, st.error_completions, st.state) == (7, sum(sizes), 2, N.QPS_ERR)
 
 
+def test_mr_deregistration_keeps_the_executor_running(gpu_env):
+    """Deregistering an MR that no in-flight WR uses finishes by a grace period while another QP
+    keeps streaming: the executor is not stopped (no extra launch), the stream's bytes are right,
+    and the engine counts the deregistrations as live ones."""
+    V = gpu_env
+    from ugdr_b200 import _native as N
+
+    ctx, pd, cq, a, b = _setup(V, N, depth=512)
+    n = 64 << 20
+    src = torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda")
+    dst = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    spare = torch.zeros(1 << 20, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    ms, md = pd.reg_mr(src.data_ptr(), n, _acc(N)), pd.reg_mr(dst.data_ptr(), n, _acc(N))
+    a.post_write((src.data_ptr(), 4096, ms.lkey), dst.data_ptr(), md.rkey, wr_id=0)
+    assert cq.wait(1, 60)[0].status == N.WC_SUCCESS  # the executor is up
+    st0 = ctx.stats()
+    chunk = 1 << 20
+    posted = 0
+    done = 0
+    deregs = 0
+    while done < 256:
+        while posted < 256 and posted - done < 64:
+            off = (posted % 64) * chunk
+            a.post_write((src.data_ptr() + off, chunk, ms.lkey), dst.data_ptr() + off, md.rkey, wr_id=posted)
+            posted += 1
+        if deregs < 8:  # an unrelated MR comes and goes under the stream
+            pd.reg_mr(spare.data_ptr(), spare.numel(), _acc(N)).dereg()
+            deregs += 1
+        wcs = cq.wait(1, 60)
+        assert all(w.status == N.WC_SUCCESS for w in wcs)
+        done += len(wcs)
+    st1 = ctx.stats()
+    torch.cuda.synchronize()
+    assert torch.equal(dst, src)
+    assert st1.mr_detach_live - st0.mr_detach_live == deregs, (st0.mr_detach_live, st1.mr_detach_live)
+    assert st1.mr_detach_quiesced == st0.mr_detach_quiesced
+    assert st1.launches == st0.launches  # never stopped and relaunched
+    for q in (a, b):
+        q.destroy()
+    ms.dereg()
+    md.dereg()
+    cq.destroy()
+    pd.dealloc()
+    ctx.close()
+
+
 def test_kernel_attributes_report_every_kernel():
     """cudaFuncGetAttributes + occupancy for every kernel of the library: each fits its launch
     block size; the persistent executor keeps one 512-thread CTA per SM without spilling more than

@@ -221,6 +221,8 @@ class EngineStats(C.Structure):
         ("job_slot_misses", C.c_uint64),
         ("publish_waits", C.c_uint64),
         ("publish_wait_ns", C.c_uint64),
+        ("mr_detach_live", C.c_uint64),
+        ("mr_detach_quiesced", C.c_uint64),
     ]
 
 
