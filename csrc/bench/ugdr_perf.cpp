@@ -3,6 +3,7 @@
 //
 //   ugdr_perf latency  --src-gpu A --dst-gpu B --bytes N --iters K        QD1 post_send -> poll_cq
 //   ugdr_perf bw       --src-gpu A --dst-gpu B --op write|read --min 8 --max 1G --qd 64 --bytes-per-size T
+//                      [--trace-size S --trace-out PATH]   device trace of the executor at WR size S
 //   ugdr_perf posting  --batch B --wrs N                                    post_send into the SQ ring
 //   ugdr_perf ring     --batch B --wrs N                                    shared SPSC ring alone (2 threads)
 //   ugdr_perf postcore --batch B --wrs N                                    WR encode + publish path alone
@@ -52,6 +53,8 @@ struct Opts {
     uint64_t min_bytes = 8, max_bytes = 1ull << 30, qd = 64, bytes_per_size = 8ull << 30;
     uint64_t batch = 32, wrs = 4000000;
     uint64_t qps = 64, depth = 128, sges = 16, rounds = 3, seed = 7;
+    uint64_t trace_size = 0;  // bw: keep a device trace of the executor at this WR size
+    std::string trace_out;    // ... written here (Chrome trace JSON)
     std::string sync_dir;  // stress: start / finish barrier shared by concurrent clients
     uint64_t sync_n = 0;
 };
@@ -249,6 +252,8 @@ int run_bw(const Opts &o) {
         std::vector<ugdr_sge> chain_sge(qd);
         ugdr_x_engine_stats es{};
         ugdr_x_query_engine_stats(a.ctx, &es, 1);
+        const bool tracing = o.trace_size == sz && !o.trace_out.empty();
+        if (tracing && ugdr_x_engine_trace(a.ctx, 16384) != 0) die("ugdr_x_engine_trace", EINVAL);
         const auto t0 = Clock::now();
         while (done < wrs) {
             // Bound each size to ~2 s: stop posting and drain what is in flight.
@@ -296,6 +301,14 @@ int run_bw(const Opts &o) {
         }
         const double s = std::chrono::duration<double>(Clock::now() - t0).count();
         const double gbps = double(wrs) * double(sz) / s / 1e9;
+        if (tracing) {
+            uint64_t kept = 0, dropped = 0;
+            if (ugdr_x_engine_trace_dump(a.ctx, o.trace_out.c_str(), &kept, &dropped) != 0)
+                die("ugdr_x_engine_trace_dump", EIO);
+            ugdr_x_engine_trace(a.ctx, 0);
+            std::fprintf(stderr, "trace: %llu events kept, %llu dropped -> %s\n", (unsigned long long)kept,
+                         (unsigned long long)dropped, o.trace_out.c_str());
+        }
         const bool ok = op == UGDR_WR_RDMA_WRITE ? same(a.buf, o.src_gpu, b.buf, o.dst_gpu, sz)
                                                  : same(b.buf, o.dst_gpu, a.buf, o.src_gpu, sz);
         if (!ok) status = 2;
@@ -1025,6 +1038,8 @@ int main(int argc, char **argv) {
         else if (k == "--max") o.max_bytes = parse_size(v);
         else if (k == "--qd") o.qd = parse_size(v);
         else if (k == "--bytes-per-size") o.bytes_per_size = parse_size(v);
+        else if (k == "--trace-size") o.trace_size = parse_size(v);
+        else if (k == "--trace-out") o.trace_out = v;
         else if (k == "--batch") o.batch = parse_size(v);
         else if (k == "--wrs") o.wrs = parse_size(v);
         else if (k == "--qps") o.qps = parse_size(v);
