@@ -175,13 +175,48 @@ def bench_allreduce_verbs(rank, world, local, iters, warmup, nbytes=1 << 30, pie
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=_GLOO)
         wall, dev = float(t[0]), float(t[1])
         dist.barrier(group=_GLOO)
+        # The same sum through NVLink SHARP on the verbs: one WRITE_SUM_BF16 per rank over its shard
+        # of a multicast MR (ugdr_x_verbs_allreduce_bf16_mc).
+        mc = {}
+        if world >= 2 and nvls.supported():
+            nvbuf = nvls.NvlsBuffer(nbytes, rank, world, exchange)
+            try:
+                xv = nvbuf.view(torch.bfloat16, count)
+                xv.copy_(torch.randn(count, generator=torch.Generator(device="cuda").manual_seed(rank),
+                                     device="cuda", dtype=torch.float32).to(torch.bfloat16))
+                torch.cuda.synchronize()
+                dist.barrier(group=_GLOO)
+                g.allreduce_nvls(nvbuf, count)
+                torch.cuda.synchronize()
+                err = (xv[lo:lo + (1 << 20)].float() - ref).abs()
+                mc_ok = bool((err <= ref.abs() * 2.0 ** -7 + 1e-3).all())
+                for _ in range(warmup):
+                    g.allreduce_nvls(nvbuf, count)
+                dist.barrier(group=_GLOO)
+                g.allreduce_nvls(nvbuf, count)
+                s0 = g.ctx.stats()
+                t1 = time.perf_counter()
+                for _ in range(iters):
+                    g.allreduce_nvls(nvbuf, count)
+                mwall = (time.perf_counter() - t1) / iters * 1e3
+                s1 = g.ctx.stats()
+                mdev = (int(s1.last_end_ns) - int(s0.last_end_ns)) / 1e6 / iters
+                tt = torch.tensor([mwall, mdev], dtype=torch.float64)
+                dist.all_reduce(tt, op=dist.ReduceOp.MAX, group=_GLOO)
+                mc = {"ugdr_verbs_nvls_ms": round(float(tt[1]), 4), "ugdr_verbs_nvls_wall_ms": round(float(tt[0]), 4),
+                      "ugdr_verbs_nvls_algbw_GBps": round(nbytes / float(tt[1]) / 1e6, 1), "nvls_correct": mc_ok}
+                del xv
+            finally:
+                g.release_multicast()
+                dist.barrier(group=_GLOO)
+                nvbuf.close()
     finally:
         g.close()
         dist.barrier(group=_GLOO)
         if daemon is not None:
             daemon.stop()
     bus = 2 * (world - 1) / world if world > 1 else 1.0
-    return {"op": "allreduce_bf16_verbs", "n_gpus": world, "bytes": nbytes, "pieces": pieces,
+    return {"op": "allreduce_bf16_verbs", "n_gpus": world, "bytes": nbytes, "pieces": pieces, **mc,
             "ugdr_verbs_ms": round(dev, 4), "ugdr_verbs_wall_ms": round(wall, 4),
             "ugdr_verbs_algbw_GBps": round(nbytes / dev / 1e6, 1),
             "ugdr_verbs_busbw_GBps": round(bus * nbytes / dev / 1e6, 1),
@@ -366,8 +401,11 @@ def main():
             if args.api == "verbs":  # the NCCL figure beside it
                 y = torch.randn((args.ar_mib << 20) // 2, device="cuda").to(torch.bfloat16)
                 t_nccl = _timed(lambda: dist.all_reduce(y), args.iters, args.warmup)
-                results[-1]["nccl_ms"] = round(t_nccl, 4)
-                results[-1]["speedup_vs_nccl"] = round(t_nccl / results[-1]["ugdr_verbs_ms"], 3)
+                r = results[-1]
+                r["nccl_ms"] = round(t_nccl, 4)
+                best = min(v for v in (r["ugdr_verbs_ms"], r.get("ugdr_verbs_nvls_ms")) if v is not None)
+                r["ugdr_verbs_best_ms"] = best
+                r["speedup_vs_nccl"] = round(t_nccl / best, 3)
                 del y
     if args.op == "p2p":
         sizes = [1 << k for k in range(3, 31, 2)]
