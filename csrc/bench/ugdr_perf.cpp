@@ -213,7 +213,9 @@ int run_latency(const Opts &o) {
     fill(a.buf, o.bytes, 1, o.src_gpu);
     std::vector<double> us;
     us.reserve(o.iters);
+    ugdr_x_engine_stats es{};
     for (uint64_t i = 0; i < o.warmup + o.iters; ++i) {
+        if (i == o.warmup) ugdr_x_query_engine_stats(a.ctx, &es, 1);
         const auto t0 = Clock::now();
         post(a.qp, UGDR_WR_RDMA_WRITE, a.buf, a.mr->lkey, o.bytes, b.buf, b.mr->rkey, i);
         wait_cq(a.cq, 1);
@@ -225,6 +227,13 @@ int run_latency(const Opts &o) {
                 "p99_us=%.3f p999_us=%.3f min_us=%.3f correct=%d\n",
                 (unsigned long long)o.bytes, o.src_gpu, o.dst_gpu, (unsigned long long)o.iters, pct(us, 0.5),
                 pct(us, 0.99), pct(us, 0.999), pct(us, 0.0), int(ok));
+    // Executor side of the same WRs (GPU contexts): mean time per fast batch in each phase.
+    if (ugdr_x_query_engine_stats(a.ctx, &es, 0) == 0 && es.fast_batches > 0) {
+        const double nb = double(es.fast_batches) * 1e3;
+        std::printf("executor: batches=%llu fetch_us=%.3f exec_us=%.3f reserve_us=%.3f publish_us=%.3f\n",
+                    (unsigned long long)es.fast_batches, es.fast_fetch_ns / nb, es.fast_exec_ns / nb,
+                    es.fast_reserve_ns / nb, es.fast_publish_ns / nb);
+    }
     std::printf("{\"benchmark\": \"ugdr_latency\", \"bytes\": %llu, \"src_gpu\": %d, \"dst_gpu\": %d, "
                 "\"p50_us\": %.3f, \"p99_us\": %.3f, \"correct\": %s}\n",
                 (unsigned long long)o.bytes, o.src_gpu, o.dst_gpu, pct(us, 0.5), pct(us, 0.99),
