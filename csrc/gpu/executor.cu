@@ -238,7 +238,7 @@ __device__ void warp_copy(uint8_t *dst, const uint8_t *src, uint64_t n, int lane
         const uint4 *sa = reinterpret_cast<const uint4 *>(src - r);
         uint4 *dv = reinterpret_cast<uint4 *>(dst);
         const uint64_t nvec = n >> 4;
-        constexpr int U = 2;
+        constexpr int U = 4;  // 2 KiB in flight per warp: misaligned gathers are latency-bound
         for (uint64_t j0 = 0; j0 < nvec; j0 += 32 * U) {
             uint4 v[U], nx[U];
 #pragma unroll
