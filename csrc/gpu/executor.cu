@@ -2056,6 +2056,7 @@ __global__ void __launch_bounds__(kThreads, 1) executor_kernel(ExecParams p) {
         // Owned QPs: q = cta + grid * (wi + warps * k).
         const uint32_t slots = s_slots;
         const bool owner = blockIdx.x + gridDim.x * w.wi < slots;
+        bool in_flight = false;  // an owned QP waits for WRs to finish: come back to it soon
         for (uint32_t q = blockIdx.x + gridDim.x * w.wi; q < slots; q += gridDim.x * kWarps) {
             work += service_qp(w, &p.qps[q], wqe_buf[w.wi], cqe_buf[w.wi], jr, bits, nwarps);
             if (w.abort) {
@@ -2063,9 +2064,13 @@ __global__ void __launch_bounds__(kThreads, 1) executor_kernel(ExecParams p) {
                 flush_counters(w);
                 return;
             }
+            in_flight |= w.vq == &p.qps[q] && w.vhead != w.vissue;
         }
         if (!leader) {
-            for (int k = 0; k < 8; ++k) {
+            // A warp whose QPs have WRs in flight takes one chunk per round, so it notices their
+            // completion (and retires them) within one chunk's time rather than eight.
+            const int max_chunks = in_flight ? 1 : 8;
+            for (int k = 0; k < max_chunks; ++k) {
                 Claim cl;
                 if (!claim_chunk(w, jr, bits, s_bits, &cl)) break;
                 run_chunk(w, cl);
