@@ -132,12 +132,11 @@ struct DevQp {
 // without stopping the executor once every active QP has begun a pass under the new epoch (no
 // later resolution can use the invalidated entry: per-warp MR caches are keyed by epoch) and has
 // retired everything issued until then (no in-flight WR still addresses the memory).
+// The epoch and the issue cursor share one 8-byte word, written by one store, so the host never
+// pairs an epoch with an older cursor and the owner needs no fence between them.
 struct QpProgress {
-    unsigned int seen_epoch;
-    unsigned int pad;
-    unsigned long long issue;
-    unsigned long long head;
-    unsigned long long pad2;
+    unsigned long long epoch_issue;  // seen epoch << 32 | issue cursor mod 2^32
+    unsigned long long head;         // retire cursor
 };
 
 // One chunked job: WRs [first, first + nwr) of one QP's window (indices mod kWindow), cut into

@@ -1671,10 +1671,8 @@ __device__ uint32_t service_qp(Warp &w, DevQp *qp, uint8_t *wqe_smem, queue::Cqe
     const uint32_t work = service_pass(w, qp, wqe_smem, cqe_smem, jr, bitmap, nwarps);
     if (w.lane == 0 && w.vq == qp) {
         QpProgress *pr = &w.p->progress[qp - w.p->qps];
-        pr->issue = w.vissue;
-        pr->head = w.vhead;
-        __threadfence();  // the cursors before the epoch that vouches for them
-        pr->seen_epoch = w.epoch;
+        st_vol64(&pr->epoch_issue, (uint64_t(w.epoch) << 32) | (w.vissue & 0xffffffffull));
+        st_vol64(&pr->head, w.vhead);
     }
     return work;
 }

@@ -471,7 +471,7 @@ bool GpuEngine::mr_grace_locked() {
     for (const QpEntry &e : qps_host_) nslots = std::max(nslots, e.slot + 1);
     if (nslots == 0) return !copies_pending_locked();
     std::vector<QpProgress> pr(nslots);
-    std::vector<uint64_t> issued(nslots, 0);
+    std::vector<uint32_t> issued(nslots, 0);
     const auto deadline = Clock::now() + std::chrono::milliseconds(cfg_.max_wait_ms);
     for (int phase = 0; phase < 2;) {
         if (copy_from_device(pr.data(), progress_, sizeof(QpProgress) * nslots) != 0) return false;
@@ -479,13 +479,13 @@ bool GpuEngine::mr_grace_locked() {
         for (const QpEntry &e : qps_host_) {
             const QpProgress &q = pr[e.slot];
             if (phase == 0)
-                all &= int32_t(q.seen_epoch - epoch) >= 0;
+                all &= int32_t(uint32_t(q.epoch_issue >> 32) - epoch) >= 0;
             else
-                all &= q.head >= issued[e.slot];
+                all &= int32_t(uint32_t(q.head) - issued[e.slot]) >= 0;
         }
         if (all) {
             if (phase == 0)
-                for (const QpEntry &e : qps_host_) issued[e.slot] = pr[e.slot].issue;
+                for (const QpEntry &e : qps_host_) issued[e.slot] = uint32_t(pr[e.slot].epoch_issue);
             ++phase;
             continue;
         }
