@@ -185,6 +185,7 @@ struct DevStats {
     unsigned long long fast_batches, fast_fetch_ns, fast_exec_ns, fast_reserve_ns, fast_publish_ns;
     // One-per-round issue path and CQ publish waits (see ugdr_x_engine_stats).
     unsigned long long slow_wrs, slow_issue_ns, job_slot_misses, publish_waits, publish_wait_ns;
+    unsigned long long order_waits;  // issue passes cut short by the per-QP ordering rule
     unsigned long long last_work_ns;
     unsigned long long retired;  // WRs retired since the last reset (drain mode exit test)
     unsigned int exiting;

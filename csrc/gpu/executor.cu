@@ -1574,6 +1574,7 @@ __device__ uint32_t issue_fast(Warp &w, DevQp *qp, const QpView &v, const uint8_
         const bool f = clashes_in_flight(w, qp, head, issue0, sp);
         const uint32_t clash_mask = __ballot_sync(0xffffffffu, j < count && (c || f));
         if (clash_mask) {
+            if (w.lane == 0) atomicAdd(&w.p->stats->order_waits, 1ull);
             count = __ffs(clash_mask) - 1;
             if (count == 0) return 0;
         }
@@ -1847,8 +1848,10 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
         // Ordering: wait (a later pass) while an earlier WR still in flight touches its bytes.
         if (__any_sync(0xffffffffu,
                        clashes_in_flight(w, qp, head, issue,
-                                         span_of(op, remote, total, lo, hi, status == UGDR_WC_SUCCESS))))
+                                         span_of(op, remote, total, lo, hi, status == UGDR_WC_SUCCESS)))) {
+            if (w.lane == 0) atomicAdd(&w.p->stats->order_waits, 1ull);
             break;
+        }
 
         // A WR that becomes a job takes its job slot first: with no slot free the WR waits for a
         // later pass before anything (an RQ claim, a copy) has been done for it.

@@ -725,6 +725,7 @@ int GpuEngine::stats(control::EngineStats *out, bool reset) {
     out->publish_wait_ns = st.publish_wait_ns;
     out->mr_detach_live = mr_fast_detaches_;
     out->mr_detach_quiesced = mr_slow_detaches_;
+    out->order_waits = st.order_waits;
     if (reset) {
         // Counters only (a running kernel may race a few increments into the fresh window).
         cudaMemsetAsync(stats_, 0, offsetof(DevStats, last_work_ns), ctl_stream_);

@@ -288,6 +288,9 @@ typedef struct ugdr_x_engine_stats {
     /* MR deregistrations finished while the executor kept running (grace period), and those
      * that had to stop it (not reset by `reset`) */
     uint64_t mr_detach_live, mr_detach_quiesced;
+    /* issue passes that stopped before a WR touching bytes an earlier in-flight WR of its QP
+     * still moves (the per-QP ordering rule) */
+    uint64_t order_waits;
 } ugdr_x_engine_stats;
 
 int ugdr_x_query_engine_stats(ugdr_context *context, ugdr_x_engine_stats *stats,

@@ -223,6 +223,7 @@ class EngineStats(C.Structure):
         ("publish_wait_ns", C.c_uint64),
         ("mr_detach_live", C.c_uint64),
         ("mr_detach_quiesced", C.c_uint64),
+        ("order_waits", C.c_uint64),
     ]
 
 
