@@ -593,7 +593,8 @@ int ugdr_x_query_engine_stats(ugdr_context *ctx, ugdr_x_engine_stats *stats, int
         !rd.be(&stats->fast_fetch_ns) || !rd.be(&stats->fast_exec_ns) || !rd.be(&stats->fast_reserve_ns) ||
         !rd.be(&stats->fast_publish_ns) || !rd.be(&stats->slow_wrs) || !rd.be(&stats->slow_issue_ns) ||
         !rd.be(&stats->job_slot_misses) || !rd.be(&stats->publish_waits) || !rd.be(&stats->publish_wait_ns) ||
-        !rd.be(&stats->mr_detach_live) || !rd.be(&stats->mr_detach_quiesced) || !rd.be(&stats->order_waits))
+        !rd.be(&stats->mr_detach_live) || !rd.be(&stats->mr_detach_quiesced) || !rd.be(&stats->order_waits) ||
+        !rd.be(&stats->overlap_issues))
         return EPROTO;
     return 0;
 }

@@ -323,12 +323,13 @@ int run_bw(const Opts &o) {
         if (!ok) status = 2;
         if (ugdr_x_query_engine_stats(a.ctx, &es, 0) == 0)
             std::printf("engine bytes=%llu wrs=%llu jobs=%llu chunks=%llu claim_misses=%llu busy_us=%.1f "
-                        "fast_batches=%llu slow_wrs=%llu publish_waits=%llu order_waits=%llu slot_misses=%llu\n",
+                        "fast_batches=%llu slow_wrs=%llu publish_waits=%llu order_waits=%llu slot_misses=%llu overlap_issues=%llu\n",
                         (unsigned long long)sz, (unsigned long long)es.wrs_completed,
                         (unsigned long long)es.jobs_published, (unsigned long long)es.chunks_run,
                         (unsigned long long)es.claim_misses, double(es.busy_ns) / 1e3,
                         (unsigned long long)es.fast_batches, (unsigned long long)es.slow_wrs,
-                        (unsigned long long)es.publish_waits, (unsigned long long)es.order_waits, (unsigned long long)es.job_slot_misses);
+                        (unsigned long long)es.publish_waits, (unsigned long long)es.order_waits, (unsigned long long)es.job_slot_misses,
+                        (unsigned long long)es.overlap_issues);
         std::printf("benchmark=ugdr_bw op=%s bytes=%llu qd=%u src_gpu=%d dst_gpu=%d wrs=%llu seconds=%.6f "
                     "GB_per_s=%.3f MWR_per_s=%.4f correct=%d\n",
                     o.op.c_str(), (unsigned long long)sz, qd, o.src_gpu, o.dst_gpu, (unsigned long long)wrs, s,

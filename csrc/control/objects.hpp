@@ -146,7 +146,7 @@ struct EngineStats {
              jobs_published = 0, inline_runs = 0, busy_ns = 0, fast_batches = 0, fast_fetch_ns = 0,
              fast_exec_ns = 0, fast_reserve_ns = 0, fast_publish_ns = 0, slow_wrs = 0, slow_issue_ns = 0,
              job_slot_misses = 0, publish_waits = 0, publish_wait_ns = 0, mr_detach_live = 0,
-             mr_detach_quiesced = 0, order_waits = 0;
+             mr_detach_quiesced = 0, order_waits = 0, overlap_issues = 0;
 };
 
 // Per-QP counters an engine keeps on top of the ring cursors (which the control plane reads

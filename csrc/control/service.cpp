@@ -561,7 +561,7 @@ Response ControlPlane::engine_stats(uint64_t s, const Request &r) {
     w.be(st.chunks_run).be(st.claim_misses).be(st.jobs_published).be(st.inline_runs).be(st.busy_ns);
     w.be(st.fast_batches).be(st.fast_fetch_ns).be(st.fast_exec_ns).be(st.fast_reserve_ns).be(st.fast_publish_ns);
     w.be(st.slow_wrs).be(st.slow_issue_ns).be(st.job_slot_misses).be(st.publish_waits).be(st.publish_wait_ns);
-    w.be(st.mr_detach_live).be(st.mr_detach_quiesced).be(st.order_waits);
+    w.be(st.mr_detach_live).be(st.mr_detach_quiesced).be(st.order_waits).be(st.overlap_issues);
     return out;
 }
 

@@ -186,6 +186,7 @@ struct DevStats {
     // One-per-round issue path and CQ publish waits (see ugdr_x_engine_stats).
     unsigned long long slow_wrs, slow_issue_ns, job_slot_misses, publish_waits, publish_wait_ns;
     unsigned long long order_waits;  // issue passes cut short by the per-QP ordering rule
+    unsigned long long overlap_issues;  // issue passes that found earlier WRs of the QP in flight
     unsigned long long last_work_ns;
     unsigned long long retired;  // WRs retired since the last reset (drain mode exit test)
     unsigned int exiting;

@@ -1829,6 +1829,7 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
                                  &fast_chunked);
     const uint32_t fast_n = uint32_t(issued);
     if (issued > 0) {
+        if (w.lane == 0 && head != issue0) atomicAdd(&w.p->stats->overlap_issues, 1ull);
         inline_ran += uint32_t(issued);
         if (w.lane == 0 && !w.started) atomicCAS(&w.p->stats->first_start_ns, 0ull, (unsigned long long)gtime());
         w.started = true;

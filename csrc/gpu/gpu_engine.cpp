@@ -726,6 +726,7 @@ int GpuEngine::stats(control::EngineStats *out, bool reset) {
     out->mr_detach_live = mr_fast_detaches_;
     out->mr_detach_quiesced = mr_slow_detaches_;
     out->order_waits = st.order_waits;
+    out->overlap_issues = st.overlap_issues;
     if (reset) {
         // Counters only (a running kernel may race a few increments into the fresh window).
         cudaMemsetAsync(stats_, 0, offsetof(DevStats, last_work_ns), ctl_stream_);

@@ -291,6 +291,8 @@ typedef struct ugdr_x_engine_stats {
     /* issue passes that stopped before a WR touching bytes an earlier in-flight WR of its QP
      * still moves (the per-QP ordering rule) */
     uint64_t order_waits;
+    /* issue passes that found earlier WRs of the QP still in flight (pipelining depth) */
+    uint64_t overlap_issues;
 } ugdr_x_engine_stats;
 
 int ugdr_x_query_engine_stats(ugdr_context *context, ugdr_x_engine_stats *stats,

@@ -224,6 +224,7 @@ class EngineStats(C.Structure):
         ("mr_detach_live", C.c_uint64),
         ("mr_detach_quiesced", C.c_uint64),
         ("order_waits", C.c_uint64),
+        ("overlap_issues", C.c_uint64),
     ]
 
 
