@@ -220,6 +220,7 @@ enum TraceEvent : uint32_t {
     kTraceRetire = 2,     // in-order retire of staged / chunked WRs; value = WRs retired
     kTraceChunk = 3,      // one chunk copied by a worker warp; value = bytes
     kTraceError = 4,      // a bounded wait ran out; value = error code
+    kTraceIssue = 5,      // an issue pass: WQE fetch .. fast-path issue; value = see executor.cu
 };
 
 struct TraceRec {

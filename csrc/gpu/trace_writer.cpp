@@ -10,7 +10,7 @@ int write_chrome_trace(const std::string &path, const std::vector<TraceRec> &rec
                        const std::vector<unsigned int> &counts, uint32_t cap, int gpu, uint64_t *kept,
                        uint64_t *dropped) {
     if (recs.size() < counts.size() * size_t(cap)) return EINVAL;
-    static const char *names[] = {"?", "fast_batch", "retire", "chunk", "error"};
+    static const char *names[] = {"?", "fast_batch", "retire", "chunk", "error", "issue"};
     uint64_t t_min = ~0ull, n_kept = 0, n_drop = 0;
     for (size_t c = 0; c < counts.size(); ++c) {
         const uint32_t k = std::min<uint32_t>(counts[c], cap);
