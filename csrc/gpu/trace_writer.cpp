@@ -32,7 +32,7 @@ int write_chrome_trace(const std::string &path, const std::vector<TraceRec> &rec
             std::fprintf(f,
                          "%s\n{\"name\": \"%s\", \"ph\": \"X\", \"pid\": %u, \"tid\": %u, \"ts\": %.3f, "
                          "\"dur\": %.3f, \"args\": {\"qp\": %d, \"value\": %u}}",
-                         first ? "" : ",", ev < 5 ? names[ev] : "?", r.cta, r.event & 0xffffu,
+                         first ? "" : ",", ev < 6 ? names[ev] : "?", r.cta, r.event & 0xffffu,
                          double(r.t0 - t_min) / 1000.0, double(dur) / 1000.0,
                          r.qp == 0xffffffffu ? -1 : int(r.qp), r.value);
             first = false;
