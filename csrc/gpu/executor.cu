@@ -1315,7 +1315,7 @@ __device__ void run_inline(Warp &w, WrRec *rec, const uint8_t *wqe, uint32_t op,
 // Commit the retirement of WRs [head, head + p): lane i (< p) holds WR head + i's completion
 // fields.  Send CQEs go out with one reservation and one publish; the head then moves past every
 // WR whose CQE found a slot.  Returns WRs retired (>= 0) or -1 when the publish wait ran out.
-__device__ __noinline__ int retire_commit(Warp &w, DevQp *qp, const QpView &v, queue::Cqe *cqe_buf, uint64_t head, uint32_t p,
+__device__ int retire_commit(Warp &w, DevQp *qp, const QpView &v, queue::Cqe *cqe_buf, uint64_t head, uint32_t p,
                              uint32_t err_mask, uint64_t wr_id, uint32_t status, uint32_t op, uint32_t signaled,
                              uint64_t total) {
     const uint64_t max_ns = w.p->max_wait_ns;
@@ -1379,7 +1379,7 @@ __device__ __noinline__ int retire_commit(Warp &w, DevQp *qp, const QpView &v, q
     return verdict;
 }
 
-__device__ __noinline__ int retire(Warp &w, DevQp *qp, const QpView &v, queue::Cqe *cqe_buf) {
+__device__ int retire(Warp &w, DevQp *qp, const QpView &v, queue::Cqe *cqe_buf) {
     const uint64_t max_ns = w.p->max_wait_ns;
     const uint64_t head = ld_vol(&qp->st.sq_head), issue = ld_vol(&qp->st.sq_issue);
     const uint32_t m = uint32_t(issue - head);  // <= kWindow <= 32
@@ -1464,7 +1464,7 @@ struct LaneWr {
     uint32_t status, op, signaled;
 };
 
-__device__ __noinline__ uint32_t issue_fast(Warp &w, DevQp *qp, const QpView &v, const uint8_t *wqe_smem, uint64_t head,
+__device__ uint32_t issue_fast(Warp &w, DevQp *qp, const QpView &v, const uint8_t *wqe_smem, uint64_t head,
                                uint64_t issue0, uint32_t avail, LaneWr *out, JobRing *jr, uint32_t *bitmap,
                                uint32_t nwarps, bool *chunked_out) {
     *chunked_out = false;
@@ -1797,203 +1797,189 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
     }
     if (v.state != UGDR_QPS_RTS) return work;
 
-    // Up to two issue rounds per pass (the window holds two staging buffers' worth), so the
-    // pass's fixed costs (retire, cursor reads) are shared by up to 32 WRs.
-    for (int round = 0; round < 2; ++round) {
-        // Issue: one lane-parallel fetch of every WQE that fits the window and the staging buffer.
-        // The SQ tail (a PCIe read) is read only when the window has room and the tail seen last
-        // does not already cover it: WQEs below a tail acquired earlier are as valid now.
-        const uint64_t head = w.vhead, issue0 = w.vissue;
-        uint64_t room = kWindow - (issue0 - head);
-        if (room > kWqeStage / v.sq_stride) room = kWqeStage / v.sq_stride;
-        if (room == 0) return work;
-        if (w.vtail < issue0 + room) {
-            uint64_t tail = 0;
-            if (w.lane == 0) tail = ld_acq_sys(&v.sq->tail.value);
-            w.vtail = bcast64(tail);
+    // Issue: one lane-parallel fetch of every WQE that fits the window and the staging buffer.
+    // The SQ tail (a PCIe read) is read only when the window has room and the tail seen last
+    // does not already cover it: WQEs below a tail acquired earlier are as valid now.
+    const uint64_t head = w.vhead, issue0 = w.vissue;
+    uint64_t room = kWindow - (issue0 - head);
+    if (room > kWqeStage / v.sq_stride) room = kWqeStage / v.sq_stride;
+    if (room == 0) return work;
+    if (w.vtail < issue0 + room) {
+        uint64_t tail = 0;
+        if (w.lane == 0) tail = ld_acq_sys(&v.sq->tail.value);
+        w.vtail = bcast64(tail);
+    }
+    const uint64_t tail = w.vtail;
+    uint64_t avail = tail > issue0 ? tail - issue0 : 0;
+    if (avail > room) avail = room;
+    if (avail == 0) return work;
+    const uint64_t t_fetch0 = gtime();
+    const uint32_t nbytes = uint32_t(avail) * v.sq_stride;
+    for (uint32_t o = w.lane * 16; o < nbytes; o += 32 * 16) {
+        const uint64_t s = issue0 + o / v.sq_stride;
+        const uint8_t *src = v.sq_slots + (s % v.sq_cap) * v.sq_stride + (o % v.sq_stride);
+        *reinterpret_cast<uint4 *>(wqe_smem + o) = ld_vol128(src);
+    }
+    __syncwarp();
+    uint32_t inline_ran = 0;
+    const uint64_t t_fetch1 = gtime();
+    LaneWr lw{0, 0, 0, 0, 0};
+    bool fast_chunked = false;
+    uint64_t issued = issue_fast(w, qp, v, wqe_smem, head, issue0, uint32_t(avail), &lw, jr, bitmap, nwarps,
+                                 &fast_chunked);
+    const uint32_t fast_n = uint32_t(issued);
+    if (issued > 0) {
+        if (w.lane == 0 && head != issue0) atomicAdd(&w.p->stats->overlap_issues, 1ull);
+        inline_ran += uint32_t(issued);
+        if (w.lane == 0 && !w.started) atomicCAS(&w.p->stats->first_start_ns, 0ull, (unsigned long long)gtime());
+        w.started = true;
+    }
+    const uint32_t fast_err = __ballot_sync(0xffffffffu, uint32_t(w.lane) < fast_n && lw.status != 0);
+    for (uint64_t j = fast_err ? avail : issued; j < avail; ++j) {
+        const uint64_t issue = issue0 + j;
+        const uint8_t *wqe = wqe_smem + j * v.sq_stride;
+        WrRec *rec = &qp->st.win[issue % kWindow];
+        uint32_t status;
+        uint64_t total, remote, lo, hi;
+        const uint64_t t_stage = gtime();
+        stage_wr(w, v, wqe, rec, &status, &total, &remote, &lo, &hi);
+        const queue::SendWqe *h = reinterpret_cast<const queue::SendWqe *>(wqe);
+        const uint32_t op = h->opcode;
+        const bool signaled = v.sig_all || (h->send_flags & UGDR_SEND_SIGNALED) != 0;
+        // Ordering: wait (a later pass) while an earlier WR still in flight touches its bytes.
+        if (__any_sync(0xffffffffu,
+                       clashes_in_flight(w, qp, head, issue,
+                                         span_of(op, remote, total, lo, hi, status == UGDR_WC_SUCCESS)))) {
+            if (w.lane == 0) atomicAdd(&w.p->stats->order_waits, 1ull);
+            break;
         }
-        const uint64_t tail = w.vtail;
-        uint64_t avail = tail > issue0 ? tail - issue0 : 0;
-        if (avail > room) avail = room;
-        if (avail == 0) return work;
-        const uint64_t t_fetch0 = gtime();
-        const uint32_t nbytes = uint32_t(avail) * v.sq_stride;
-        for (uint32_t o = w.lane * 16; o < nbytes; o += 32 * 16) {
-            const uint64_t s = issue0 + o / v.sq_stride;
-            const uint8_t *src = v.sq_slots + (s % v.sq_cap) * v.sq_stride + (o % v.sq_stride);
-            *reinterpret_cast<uint4 *>(wqe_smem + o) = ld_vol128(src);
-        }
-        __syncwarp();
-        uint32_t inline_ran = 0;
-        const uint64_t t_fetch1 = gtime();
-        LaneWr lw{0, 0, 0, 0, 0};
-        bool fast_chunked = false;
-        uint64_t issued = issue_fast(w, qp, v, wqe_smem, head, issue0, uint32_t(avail), &lw, jr, bitmap, nwarps,
-                                     &fast_chunked);
-        const uint32_t fast_n = uint32_t(issued);
-        if (w.lane == 0 && w.p->trace != nullptr) {
-            // Issue pass: WRs issued by the fast path | in flight before << 8 | fetched << 16 |
-            // unissued WQEs seen (capped) << 24.
-            const uint64_t seen = tail - issue0 < 255 ? tail - issue0 : 255;
-            trace_event(w.p, kTraceIssue, w.gwarp, uint32_t(qp - w.p->qps),
-                        fast_n | uint32_t(issue0 - head) << 8 | uint32_t(avail) << 16 | uint32_t(seen) << 24, t_fetch0,
-                        gtime());
-        }
-        if (issued > 0) {
-            if (w.lane == 0 && head != issue0) atomicAdd(&w.p->stats->overlap_issues, 1ull);
-            inline_ran += uint32_t(issued);
-            if (w.lane == 0 && !w.started) atomicCAS(&w.p->stats->first_start_ns, 0ull, (unsigned long long)gtime());
-            w.started = true;
-        }
-        const uint32_t fast_err = __ballot_sync(0xffffffffu, uint32_t(w.lane) < fast_n && lw.status != 0);
-        for (uint64_t j = fast_err ? avail : issued; j < avail; ++j) {
-            const uint64_t issue = issue0 + j;
-            const uint8_t *wqe = wqe_smem + j * v.sq_stride;
-            WrRec *rec = &qp->st.win[issue % kWindow];
-            uint32_t status;
-            uint64_t total, remote, lo, hi;
-            const uint64_t t_stage = gtime();
-            stage_wr(w, v, wqe, rec, &status, &total, &remote, &lo, &hi);
-            const queue::SendWqe *h = reinterpret_cast<const queue::SendWqe *>(wqe);
-            const uint32_t op = h->opcode;
-            const bool signaled = v.sig_all || (h->send_flags & UGDR_SEND_SIGNALED) != 0;
-            // Ordering: wait (a later pass) while an earlier WR still in flight touches its bytes.
-            if (__any_sync(0xffffffffu,
-                           clashes_in_flight(w, qp, head, issue,
-                                             span_of(op, remote, total, lo, hi, status == UGDR_WC_SUCCESS)))) {
-                if (w.lane == 0) atomicAdd(&w.p->stats->order_waits, 1ull);
+
+        // A WR that becomes a job takes its job slot first: with no slot free the WR waits for a
+        // later pass before anything (an RQ claim, a copy) has been done for it.
+        int slot = -1;
+        unsigned long long gen = 0;
+        const bool needs_job = status == UGDR_WC_SUCCESS && !is_atomic(op) && total > kInlineBytes;
+        if (needs_job) {
+            if (w.lane == 0) slot = take_job_slot(jr, w.gwarp + uint32_t(issue), &gen);
+            slot = bcast(slot);
+            gen = bcast64(gen);
+            if (slot < 0) {  // no job slot: retry on a later pass
+                if (w.lane == 0) w.ctr->n_slot_miss += 1;
                 break;
             }
+        }
 
-            // A WR that becomes a job takes its job slot first: with no slot free the WR waits for a
-            // later pass before anything (an RQ claim, a copy) has been done for it.
-            int slot = -1;
-            unsigned long long gen = 0;
-            const bool needs_job = status == UGDR_WC_SUCCESS && !is_atomic(op) && total > kInlineBytes;
-            if (needs_job) {
-                if (w.lane == 0) slot = take_job_slot(jr, w.gwarp + uint32_t(issue), &gen);
-                slot = bcast(slot);
-                gen = bcast64(gen);
-                if (slot < 0) {  // no job slot: retry on a later pass
-                    if (w.lane == 0) w.ctr->n_slot_miss += 1;
-                    break;
-                }
-            }
-
-            // Responder RQ for WRITE_WITH_IMM (RNR when empty).
-            int rnr = 0;  // 0 go, 1 wait, 2 retry budget exhausted
-            if (status == UGDR_WC_SUCCESS && op == UGDR_WR_RDMA_WRITE_WITH_IMM) {
-                if (w.lane == 0) {
-                    uint64_t claim = 0, wr_id = 0;
-                    if (claim_rq(v.peer, &claim, &wr_id)) {
-                        rec->recv_claim = claim;
-                        rec->recv_wr_id = wr_id;
-                        qp->st.rnr_attempts = 0;
-                        qp->st.rnr_next_ns = 0;
+        // Responder RQ for WRITE_WITH_IMM (RNR when empty).
+        int rnr = 0;  // 0 go, 1 wait, 2 retry budget exhausted
+        if (status == UGDR_WC_SUCCESS && op == UGDR_WR_RDMA_WRITE_WITH_IMM) {
+            if (w.lane == 0) {
+                uint64_t claim = 0, wr_id = 0;
+                if (claim_rq(v.peer, &claim, &wr_id)) {
+                    rec->recv_claim = claim;
+                    rec->recv_wr_id = wr_id;
+                    qp->st.rnr_attempts = 0;
+                    qp->st.rnr_next_ns = 0;
+                } else {
+                    const uint8_t rnr_retry = uint8_t(v.retry_word >> 16);
+                    if (rnr_retry == 7) {
+                        rnr = 1;
                     } else {
-                        const uint8_t rnr_retry = uint8_t(v.retry_word >> 16);
-                        if (rnr_retry == 7) {
-                            rnr = 1;
-                        } else {
-                            const uint64_t now = gtime();
-                            if (qp->st.rnr_next_ns == 0 || now >= qp->st.rnr_next_ns) {
-                                if (qp->st.rnr_next_ns != 0) qp->st.rnr_attempts += 1;
-                                if (qp->st.rnr_attempts >= rnr_retry) {
-                                    rnr = 2;
-                                } else {
-                                    const uint32_t code = ld_vol32(&v.peer->cfg.timeout) >> 24;
-                                    qp->st.rnr_next_ns = now + rnr_ns(code);
-                                    rnr = 1;
-                                }
+                        const uint64_t now = gtime();
+                        if (qp->st.rnr_next_ns == 0 || now >= qp->st.rnr_next_ns) {
+                            if (qp->st.rnr_next_ns != 0) qp->st.rnr_attempts += 1;
+                            if (qp->st.rnr_attempts >= rnr_retry) {
+                                rnr = 2;
                             } else {
+                                const uint32_t code = ld_vol32(&v.peer->cfg.timeout) >> 24;
+                                qp->st.rnr_next_ns = now + rnr_ns(code);
                                 rnr = 1;
                             }
+                        } else {
+                            rnr = 1;
                         }
                     }
                 }
-                rnr = bcast(rnr);
-                if (rnr != 0 && slot >= 0) {
-                    // No job after all: hand the taken slot back (its sequence becomes even again).
-                    if (w.lane == 0) atomicAdd(&jr->slots[slot].seq, 1ull);
-                    slot = -1;
-                }
-                if (rnr == 1) break;
-                if (rnr == 2) {
-                    status = UGDR_WC_RNR_RETRY_EXC_ERR;
-                    if (w.lane == 0) {
-                        rec->status = status;
-                        qp->st.rnr_attempts = 0;
-                        qp->st.rnr_next_ns = 0;
-                    }
-                }
             }
-            if (w.lane == 0) {
-                rec->signaled = signaled ? 1u : 0u;
-                if (!w.started) atomicCAS(&w.p->stats->first_start_ns, 0ull, (unsigned long long)gtime());
+            rnr = bcast(rnr);
+            if (rnr != 0 && slot >= 0) {
+                // No job after all: hand the taken slot back (its sequence becomes even again).
+                if (w.lane == 0) atomicAdd(&jr->slots[slot].seq, 1ull);
+                slot = -1;
             }
-            w.started = true;
-            if (status == UGDR_WC_SUCCESS) {
-                if (slot < 0) {
-                    run_inline(w, rec, wqe, op, total, remote);
-                    ++inline_ran;
-                } else {
-                    const uint32_t chunk = chunk_for(total, nwarps);
-                    const uint32_t n = uint32_t((total + chunk - 1) / chunk);
-                    if (w.lane == 0) rec->nchunks = n;
-                    publish_job(w, jr, bitmap, slot, gen, qp->st.win, uint32_t(issue % kWindow), 1u, 0u, n, chunk);
-                }
-            }
-            if (w.lane == 0) w.ctr->n_slow += 1;
-            if (w.lane == 0) w.ctr->t_slow += gtime() - t_stage;
-            ++issued;
-            if (status != UGDR_WC_SUCCESS) break;  // stop issuing behind an error
-        }
-        if (issued > 0) {
-            __syncwarp();
-            if (w.lane == 0) {
-                // No fence: the issue cursor is private to this warp, and the publish path's system
-                // fence orders these inline payload stores before any of their CQEs.
-                qp->st.sq_issue = issue0 + issued;
-            }
-            __syncwarp();
-            w.vissue = issue0 + issued;
-            if (w.lane == 0) w.ctr->n_inline += inline_ran;
-            work += uint32_t(issued);
-            if (head == issue0 && issued == fast_n && !fast_chunked) {
-                // Only this fast batch is in flight and every lane still holds its WR: retire it
-                // without reading anything back.
-                const uint32_t err_mask = __ballot_sync(0xffffffffu, uint32_t(w.lane) < fast_n && lw.status != 0);
-                const uint64_t t_exec1 = gtime();
-                r = retire_commit(w, qp, v, cqe_smem, head, fast_n, err_mask, lw.wr_id, lw.status, lw.op, lw.signaled,
-                                  lw.total);
+            if (rnr == 1) break;
+            if (rnr == 2) {
+                status = UGDR_WC_RNR_RETRY_EXC_ERR;
                 if (w.lane == 0) {
-                    const uint64_t t_end = gtime();
-                    const uint64_t t_res = w.t_reserved > t_exec1 ? w.t_reserved : t_exec1;
-                    atomicAdd(&w.p->stats->fast_batches, 1ull);
-                    atomicAdd(&w.p->stats->fast_fetch_ns, (unsigned long long)(t_fetch1 - t_fetch0));
-                    atomicAdd(&w.p->stats->fast_exec_ns, (unsigned long long)(t_exec1 - t_fetch1));
-                    atomicAdd(&w.p->stats->fast_reserve_ns, (unsigned long long)(t_res - t_exec1));
-                    atomicAdd(&w.p->stats->fast_publish_ns, (unsigned long long)(t_end - t_res));
-                    if (w.p->trace != nullptr)
-                        trace_event(w.p, kTraceFastBatch, w.gwarp, uint32_t(qp - w.p->qps), fast_n, t_fetch0, t_end);
+                    rec->status = status;
+                    qp->st.rnr_attempts = 0;
+                    qp->st.rnr_next_ns = 0;
                 }
-            } else {
-                const uint64_t t_r0 = gtime();
-                // A batch that went to a chunked job cannot be finished yet: retire it next pass.
-                r = fast_chunked && issued == fast_n ? 0 : retire(w, qp, v, cqe_smem);
-                if (r > 0 && w.lane == 0 && w.p->trace != nullptr)
-                    trace_event(w.p, kTraceRetire, w.gwarp, uint32_t(qp - w.p->qps), uint32_t(r), t_r0, gtime());
             }
-            if (r < 0) {
-                record_error(w, r == -1 ? kErrCqPublishTimeout : kErrRqReleaseTimeout);
-                return work;
-            }
-            w.vhead += uint64_t(r);
-            work += uint32_t(r);
-            if (r > 0 && ld_vol32(&qp->st.err) != 0) v.err = 1;
         }
-        // Another round only after a full staging buffer: the QP may have more WQEs queued.
-        if (issued < kWqeStage / v.sq_stride) break;
+        if (w.lane == 0) {
+            rec->signaled = signaled ? 1u : 0u;
+            if (!w.started) atomicCAS(&w.p->stats->first_start_ns, 0ull, (unsigned long long)gtime());
+        }
+        w.started = true;
+        if (status == UGDR_WC_SUCCESS) {
+            if (slot < 0) {
+                run_inline(w, rec, wqe, op, total, remote);
+                ++inline_ran;
+            } else {
+                const uint32_t chunk = chunk_for(total, nwarps);
+                const uint32_t n = uint32_t((total + chunk - 1) / chunk);
+                if (w.lane == 0) rec->nchunks = n;
+                publish_job(w, jr, bitmap, slot, gen, qp->st.win, uint32_t(issue % kWindow), 1u, 0u, n, chunk);
+            }
+        }
+        if (w.lane == 0) w.ctr->n_slow += 1;
+        if (w.lane == 0) w.ctr->t_slow += gtime() - t_stage;
+        ++issued;
+        if (status != UGDR_WC_SUCCESS) break;  // stop issuing behind an error
+    }
+    if (issued > 0) {
+        __syncwarp();
+        if (w.lane == 0) {
+            // No fence: the issue cursor is private to this warp, and the publish path's system
+            // fence orders these inline payload stores before any of their CQEs.
+            qp->st.sq_issue = issue0 + issued;
+        }
+        __syncwarp();
+        w.vissue = issue0 + issued;
+        if (w.lane == 0) w.ctr->n_inline += inline_ran;
+        work += uint32_t(issued);
+        if (head == issue0 && issued == fast_n && !fast_chunked) {
+            // Only this fast batch is in flight and every lane still holds its WR: retire it
+            // without reading anything back.
+            const uint32_t err_mask = __ballot_sync(0xffffffffu, uint32_t(w.lane) < fast_n && lw.status != 0);
+            const uint64_t t_exec1 = gtime();
+            r = retire_commit(w, qp, v, cqe_smem, head, fast_n, err_mask, lw.wr_id, lw.status, lw.op, lw.signaled,
+                              lw.total);
+            if (w.lane == 0) {
+                const uint64_t t_end = gtime();
+                const uint64_t t_res = w.t_reserved > t_exec1 ? w.t_reserved : t_exec1;
+                atomicAdd(&w.p->stats->fast_batches, 1ull);
+                atomicAdd(&w.p->stats->fast_fetch_ns, (unsigned long long)(t_fetch1 - t_fetch0));
+                atomicAdd(&w.p->stats->fast_exec_ns, (unsigned long long)(t_exec1 - t_fetch1));
+                atomicAdd(&w.p->stats->fast_reserve_ns, (unsigned long long)(t_res - t_exec1));
+                atomicAdd(&w.p->stats->fast_publish_ns, (unsigned long long)(t_end - t_res));
+                if (w.p->trace != nullptr)
+                    trace_event(w.p, kTraceFastBatch, w.gwarp, uint32_t(qp - w.p->qps), fast_n, t_fetch0, t_end);
+            }
+        } else {
+            const uint64_t t_r0 = gtime();
+            // A batch that went to a chunked job cannot be finished yet: retire it next pass.
+            r = fast_chunked && issued == fast_n ? 0 : retire(w, qp, v, cqe_smem);
+            if (r > 0 && w.lane == 0 && w.p->trace != nullptr)
+                trace_event(w.p, kTraceRetire, w.gwarp, uint32_t(qp - w.p->qps), uint32_t(r), t_r0, gtime());
+        }
+        if (r < 0) {
+            record_error(w, r == -1 ? kErrCqPublishTimeout : kErrRqReleaseTimeout);
+            return work;
+        }
+        w.vhead += uint64_t(r);
+        work += uint32_t(r);
+        if (r > 0 && ld_vol32(&qp->st.err) != 0) v.err = 1;
     }
     return work;
 }
@@ -2087,9 +2073,9 @@ __global__ void __launch_bounds__(kThreads, 1) executor_kernel(ExecParams p) {
             in_flight |= w.vq == &p.qps[q] && w.vhead != w.vissue;
         }
         if (!leader) {
-            // A warp whose QPs have WRs in flight copies no chunk: a chunk costs microseconds, and
-            // its QPs' completions (and their next WRs) wait for it.  The other warps copy.
-            const int max_chunks = in_flight ? 0 : 8;
+            // A warp whose QPs have WRs in flight takes one chunk per round, so it notices their
+            // completion (and retires them) within one chunk's time rather than eight.
+            const int max_chunks = in_flight ? 1 : 8;
             for (int k = 0; k < max_chunks; ++k) {
                 Claim cl;
                 if (!claim_chunk(w, jr, bits, s_bits, &cl)) break;
