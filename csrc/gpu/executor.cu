@@ -2058,12 +2058,9 @@ __global__ void __launch_bounds__(kThreads, 1) executor_kernel(ExecParams p) {
         uint32_t work = 0;
         // Owned QPs: q = cta + grid * (wi + warps * k).
         const uint32_t slots = s_slots;
-        // QP slot q belongs to CTA q % grid, warp 1 + (q / grid) % 15: the leader (warp 0) owns
-        // none, so its refresh duties never delay an owner's pass.
-        const uint32_t first_q = blockIdx.x + gridDim.x * (w.wi - 1);
-        const bool owner = !leader && first_q < slots;
+        const bool owner = blockIdx.x + gridDim.x * w.wi < slots;
         bool in_flight = false;  // an owned QP waits for WRs to finish: come back to it soon
-        for (uint32_t q = first_q; owner && q < slots; q += gridDim.x * (kWarps - 1)) {
+        for (uint32_t q = blockIdx.x + gridDim.x * w.wi; q < slots; q += gridDim.x * kWarps) {
             work += service_qp(w, &p.qps[q], wqe_buf[w.wi], cqe_buf[w.wi], jr, bits, nwarps);
             if (w.abort) {
                 s_exit = 1;
