@@ -1828,6 +1828,14 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
     uint64_t issued = issue_fast(w, qp, v, wqe_smem, head, issue0, uint32_t(avail), &lw, jr, bitmap, nwarps,
                                  &fast_chunked);
     const uint32_t fast_n = uint32_t(issued);
+    if (w.lane == 0 && w.p->trace != nullptr) {
+        // Issue pass: WRs issued by the fast path | in flight before << 8 | fetched << 16 |
+        // unissued WQEs seen (capped) << 24.
+        const uint64_t seen = tail - issue0 < 255 ? tail - issue0 : 255;
+        trace_event(w.p, kTraceIssue, w.gwarp, uint32_t(qp - w.p->qps),
+                    fast_n | uint32_t(issue0 - head) << 8 | uint32_t(avail) << 16 | uint32_t(seen) << 24, t_fetch0,
+                    gtime());
+    }
     if (issued > 0) {
         if (w.lane == 0 && head != issue0) atomicAdd(&w.p->stats->overlap_issues, 1ull);
         inline_ran += uint32_t(issued);
@@ -1968,8 +1976,7 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
             }
         } else {
             const uint64_t t_r0 = gtime();
-            // A batch that went to a chunked job cannot be finished yet: retire it next pass.
-            r = fast_chunked && issued == fast_n ? 0 : retire(w, qp, v, cqe_smem);
+            r = retire(w, qp, v, cqe_smem);
             if (r > 0 && w.lane == 0 && w.p->trace != nullptr)
                 trace_event(w.p, kTraceRetire, w.gwarp, uint32_t(qp - w.p->qps), uint32_t(r), t_r0, gtime());
         }
