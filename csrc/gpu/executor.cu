@@ -279,7 +279,11 @@ __device__ void warp_copy(uint8_t *dst, const uint8_t *src, uint64_t n, int lane
 // far more bytes in flight per warp than the vector core, which is what an NVLink round trip
 // wants.  Every mbarrier wait is bounded; when one runs out the copy waits (bounded) for its other
 // loads, reports failure and the kernel exits with kErrBulkCopyTimeout.
-constexpr uint32_t kTmaStages = 3;
+#ifndef UGDR_TMA_STAGES
+#define UGDR_TMA_STAGES 3  // 0 builds the executor without the bulk-copy path (no dynamic smem)
+#endif
+constexpr uint32_t kTmaStages = UGDR_TMA_STAGES > 0 ? UGDR_TMA_STAGES : 1;
+constexpr bool kTmaBuilt = UGDR_TMA_STAGES > 0;
 constexpr uint32_t kTmaPiece = 4096;
 
 struct Tma {
@@ -2033,7 +2037,7 @@ __global__ void __launch_bounds__(kThreads, 1) executor_kernel(ExecParams p) {
             t.buf = tma_smem + size_t(w.wi - 1) * kTmaStages * kTmaPiece;
             t.bar = tma_bar[w.wi];
             t.phase = 0;
-            t.min = p.bulk_min < kTmaPiece && p.bulk_min != 0 ? kTmaPiece : p.bulk_min;
+            t.min = !kTmaBuilt ? 0u : p.bulk_min < kTmaPiece && p.bulk_min != 0 ? kTmaPiece : p.bulk_min;
             t.failed = 0;
             t.max_ns = p.max_wait_ns;
             for (uint32_t s = 0; s < kTmaStages; ++s)
@@ -2174,15 +2178,16 @@ int launch_grid_copy(void *dst, const void *src, uint64_t n, int ctas, cudaStrea
 size_t job_ring_bytes() { return sizeof(JobRing) + 32 * sizeof(uint32_t); }
 int executor_threads() { return kThreads; }
 
-constexpr size_t kTmaSmemBytes = size_t(kWarps - 1) * kTmaStages * kTmaPiece;
+constexpr size_t kTmaSmemBytes = kTmaBuilt ? size_t(kWarps - 1) * kTmaStages * kTmaPiece : 0;
 
 int launch_executor(const ExecParams &p, int ctas, cudaStream_t stream) {
     // The dynamic shared memory (TMA staging) is above the 48 KiB default: opt in (cheap, and
     // per device, so it is set on every launch).
-    if (cudaError_t e = cudaFuncSetAttribute(executor_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             int(kTmaSmemBytes));
-        e != cudaSuccess)
-        return int(e);
+    if (kTmaSmemBytes > 0)
+        if (cudaError_t e = cudaFuncSetAttribute(executor_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 int(kTmaSmemBytes));
+            e != cudaSuccess)
+            return int(e);
     executor_kernel<<<ctas, kThreads, kTmaSmemBytes, stream>>>(p);
     return int(cudaGetLastError());
 }
