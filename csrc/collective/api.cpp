@@ -167,4 +167,14 @@ int ugdr_x_moe_weighted_sum(void *out, const void *rows, const float *weights, u
                                             ctas > 0 ? ctas : default_ctas(), static_cast<cudaStream_t>(stream));
 }
 
+int ugdr_x_moe_weighted_sum_grouped(void *out, const void *rows, const int32_t *ids, const int32_t *pos,
+                                    const int64_t *start, const float *weights, uint64_t tokens, int topk,
+                                    uint64_t row_bytes, int ctas, void *stream) {
+    if (out == nullptr || rows == nullptr || weights == nullptr || ids == nullptr || pos == nullptr || start == nullptr)
+        return int(cudaErrorInvalidValue);
+    return ugdr::coll::launch_weighted_rows(out, rows, weights, tokens, topk, row_bytes,
+                                            ctas > 0 ? ctas : default_ctas(), static_cast<cudaStream_t>(stream), ids,
+                                            pos, start);
+}
+
 }  // extern "C"

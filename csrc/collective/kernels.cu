@@ -445,7 +445,9 @@ __global__ void __launch_bounds__(512) combine_kernel(PeerSet ps, uint8_t *out, 
 // flight before the sum.
 template <int TOPK>
 __global__ void __launch_bounds__(512) weighted_rows_kernel(uint8_t *out, const uint8_t *rows, const float *w,
-                                                            uint64_t ntok, int topk, uint64_t row_bytes) {
+                                                            uint64_t ntok, int topk, uint64_t row_bytes,
+                                                            const int32_t *ids, const int32_t *pos,
+                                                            const int64_t *start) {
     const int lane = threadIdx.x & 31;
     const uint64_t warp = (uint64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const uint64_t nwarps = (uint64_t(gridDim.x) * blockDim.x) >> 5;
@@ -454,13 +456,20 @@ __global__ void __launch_bounds__(512) weighted_rows_kernel(uint8_t *out, const 
         float wk[TOPK];
 #pragma unroll
         for (int k = 0; k < TOPK; ++k) wk[k] = k < topk ? __ldg(w + t * topk + k) : 0.f;
-        const uint8_t *base = rows + t * uint64_t(topk) * row_bytes;
+        // Row (t, k): at t * topk + k, or (grouped) at start[expert] + position.
+        const uint8_t *rk[TOPK];
+#pragma unroll
+        for (int k = 0; k < TOPK; ++k) {
+            uint64_t row = t * uint64_t(topk) + uint64_t(k);
+            if (ids != nullptr && k < topk) row = uint64_t(__ldg(start + __ldg(ids + row))) + uint64_t(__ldg(pos + row));
+            rk[k] = rows + row * row_bytes;
+        }
         uint8_t *orow = out + t * row_bytes;
         for (uint64_t i = lane; i < nv; i += 32) {
             uint4 v[TOPK];
 #pragma unroll
             for (int k = 0; k < TOPK; ++k)
-                if (k < topk) v[k] = ld128(base + uint64_t(k) * row_bytes + i * 16);
+                if (k < topk) v[k] = ld128(rk[k] + i * 16);
             float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
             for (int k = 0; k < TOPK; ++k) {
@@ -620,18 +629,18 @@ int launch_combine(const PeerSet &ps, void *out, uint64_t row_bytes, const int32
 }
 
 int launch_weighted_rows(void *out, const void *rows, const float *w, uint64_t ntok, int topk, uint64_t row_bytes,
-                         int ctas, cudaStream_t s) {
+                         int ctas, cudaStream_t s, const int32_t *ids, const int32_t *pos, const int64_t *start) {
     if (row_bytes % 16 != 0 || topk <= 0 || topk > 16) return int(cudaErrorInvalidValue);
     uint8_t *o = static_cast<uint8_t *>(out);
     const uint8_t *r = static_cast<const uint8_t *>(rows);
     if (topk <= 2)
-        weighted_rows_kernel<2><<<ctas, 512, 0, s>>>(o, r, w, ntok, topk, row_bytes);
+        weighted_rows_kernel<2><<<ctas, 512, 0, s>>>(o, r, w, ntok, topk, row_bytes, ids, pos, start);
     else if (topk <= 4)
-        weighted_rows_kernel<4><<<ctas, 512, 0, s>>>(o, r, w, ntok, topk, row_bytes);
+        weighted_rows_kernel<4><<<ctas, 512, 0, s>>>(o, r, w, ntok, topk, row_bytes, ids, pos, start);
     else if (topk <= 8)
-        weighted_rows_kernel<8><<<ctas, 512, 0, s>>>(o, r, w, ntok, topk, row_bytes);
+        weighted_rows_kernel<8><<<ctas, 512, 0, s>>>(o, r, w, ntok, topk, row_bytes, ids, pos, start);
     else
-        weighted_rows_kernel<16><<<ctas, 512, 0, s>>>(o, r, w, ntok, topk, row_bytes);
+        weighted_rows_kernel<16><<<ctas, 512, 0, s>>>(o, r, w, ntok, topk, row_bytes, ids, pos, start);
     return int(cudaGetLastError());
 }
 

@@ -47,7 +47,8 @@ int launch_dispatch(const PeerSet &ps, const void *x, uint64_t row_bytes, const 
                     const int64_t *gbase, uint64_t ntok, int topk, int exp_per_rank, uint64_t recv_off,
                     uint64_t recv_rows, uint64_t epoch, int ctas, uint64_t max_ns, cudaStream_t s);
 int launch_weighted_rows(void *out, const void *rows, const float *w, uint64_t ntok, int topk, uint64_t row_bytes,
-                         int ctas, cudaStream_t s);
+                         int ctas, cudaStream_t s, const int32_t *ids = nullptr, const int32_t *pos = nullptr,
+                         const int64_t *start = nullptr);
 int launch_combine(const PeerSet &ps, void *out, uint64_t row_bytes, const int32_t *idx, const int32_t *pos,
                    const int64_t *gbase, const float *w, uint64_t ntok, int topk, int exp_per_rank,
                    uint64_t recv_off, uint64_t recv_rows, uint64_t epoch, int ctas, uint64_t max_ns,

@@ -250,14 +250,21 @@ extern "C" int ugdr_x_verbs_moe_dispatch(ugdr_x_vgroup *g, ugdr_x_vmoe *m, const
     return drive(g, chains, timeout_ns, [&] { return rows_in == n - 1 && lasts == n; }, on);
 }
 
-extern "C" int ugdr_x_verbs_moe_combine(ugdr_x_vgroup *g, ugdr_x_vmoe *m, const int32_t *ids, const int32_t *pos,
-                                        uint64_t timeout_ns) noexcept {
-    if (!valid(g, m) || ids == nullptr || pos == nullptr) return EINVAL;
+extern "C" int ugdr_x_verbs_moe_combine(ugdr_x_vgroup *g, ugdr_x_vmoe *m, uint64_t timeout_ns) noexcept {
+    if (!valid(g, m)) return EINVAL;
     const int n = g->n, r = g->rank, E = m->nexp, epr = E / n;
     const int32_t *counts = m->table + size_t(r) * size_t(E);
-    Buckets b;
-    if (int rc = bucket(m, ids, pos, counts, &b); rc != 0) return rc;
     const uint64_t rb = m->row_bytes;
+    // `back` holds this rank's rows grouped by expert (expert e's rows from row start(e) on, in
+    // position order), the same order dispatch read them in, so every (owner, expert) group
+    // comes back with ONE contiguous READ; the unpermute to (token, k) order is done by the
+    // weighted sum that consumes them (ugdr_x_moe_weighted_sum_grouped).
+    std::vector<uint64_t> start(size_t(E) + 1, 0);
+    for (int e = 0; e < E; ++e) {
+        if (counts[e] < 0) return EINVAL;
+        start[e + 1] = start[e] + uint64_t(counts[e]);
+    }
+    if (start[E] != uint64_t(m->tokens) * uint64_t(m->topk)) return EINVAL;
     std::vector<Chain> chains(static_cast<size_t>(n));
     for (int k = 0; k < n; ++k) {
         const int q = (r + 1 + k) % n;
@@ -265,26 +272,20 @@ extern "C" int ugdr_x_verbs_moe_combine(ugdr_x_vgroup *g, ugdr_x_vmoe *m, const 
         c.qp = qp_to(g, q);
         const uint64_t src0 = q == r ? m->recv_addr : m->peer_recv_addr[q];
         const uint32_t rkey = q == r ? m->recv_rkey : m->peer_recv_rkey[q];
-        uint64_t nrows = 0;
-        for (int e = q * epr; e < (q + 1) * epr; ++e) nrows += uint64_t(counts[e]);
-        c.sge.reserve(size_t(nrows));
-        c.wr.reserve(size_t(nrows / kSgePerWr + epr + 2));
+        c.sge.reserve(size_t(epr));
+        c.wr.reserve(size_t(epr + 1));
         for (int e = q * epr; e < (q + 1) * epr; ++e) {
             const uint64_t ce = uint64_t(counts[e]);
-            for (uint64_t j = 0; j < ce; j += kSgePerWr) {
-                const uint64_t take = ce - j < uint64_t(kSgePerWr) ? ce - j : uint64_t(kSgePerWr);
-                const size_t first = c.sge.size();
-                for (uint64_t p = j; p < j + take; ++p)
-                    c.sge.push_back(
-                        ugdr_sge{m->back_addr + uint64_t(b.order[b.start[e] + p]) * rb, uint32_t(rb), m->back_lkey});
-                ugdr_send_wr w{};
-                w.sg_list = &c.sge[first];
-                w.num_sge = int(take);
-                w.opcode = UGDR_WR_RDMA_READ;
-                w.wr.rdma.remote_addr = src0 + (m->base[size_t(e) * size_t(n) + size_t(r)] + j) * rb;
-                w.wr.rdma.rkey = rkey;
-                c.wr.push_back(w);
-            }
+            if (ce == 0) continue;
+            if (ce * rb > 0xffffffffull) return EINVAL;  // one SGE per group
+            c.sge.push_back(ugdr_sge{m->back_addr + start[e] * rb, uint32_t(ce * rb), m->back_lkey});
+            ugdr_send_wr w{};
+            w.sg_list = &c.sge.back();
+            w.num_sge = 1;
+            w.opcode = UGDR_WR_RDMA_READ;
+            w.wr.rdma.remote_addr = src0 + m->base[size_t(e) * size_t(n) + size_t(r)] * rb;
+            w.wr.rdma.rkey = rkey;
+            c.wr.push_back(w);
         }
         // A zero-length signalled READ closes the QP's list (its WRs retire in order).
         ugdr_send_wr w{};

@@ -125,6 +125,12 @@ int ugdr_x_moe_dispatch(const ugdr_x_peerset *ps, const void *x, uint64_t row_by
  * MoE combine on the verbs, after its READs brought the rows back.  row_bytes a multiple of 16. */
 int ugdr_x_moe_weighted_sum(void *out, const void *rows, const float *weights, uint64_t tokens, int topk,
                             uint64_t row_bytes, int ctas, void *stream);
+/* The same from rows grouped by expert: row (t, k) is rows[start[ids[t * topk + k]] +
+ * pos[t * topk + k]], with ids / pos as ugdr_x_moe_route gives them and start[e] the first row
+ * of expert e (all on the device).  The gather is the combine's unpermute. */
+int ugdr_x_moe_weighted_sum_grouped(void *out, const void *rows, const int32_t *ids, const int32_t *pos,
+                                    const int64_t *start, const float *weights, uint64_t tokens, int topk,
+                                    uint64_t row_bytes, int ctas, void *stream);
 int ugdr_x_moe_combine(const ugdr_x_peerset *ps, void *out, uint64_t row_bytes, const int32_t *expert_ids,
                        const int32_t *positions, const int64_t *group_base, const float *weights,
                        uint64_t tokens, int topk, int experts_per_rank, uint64_t recv_offset, uint64_t recv_rows,

@@ -86,8 +86,7 @@ int ugdr_x_verbs_allreduce_bf16_mc(ugdr_x_vgroup *g, uint64_t mc_addr, uint32_t 
 /* MoE all-to-all on the verbs.  Experts split evenly over the ranks (rank q owns experts
  * [q * nexp / n, (q + 1) * nexp / n)).  The permutes are the SGE lists of the WRs: dispatch
  * WRITEs gather each expert group's token rows (one SGE per row) into one contiguous range of
- * the owner's receive area; combine READs each group back and scatters it (one SGE per row)
- * into the (token, k) row order of `back`.  The group's `to` QPs and `self_to` need
+ * the owner's receive area; combine READs each group back in one piece.  The group's `to` QPs and `self_to` need
  * max_send_sge >= 32 and send queues of at least ugdr_x_verbs_moe_wrs(...) WRs; `from` QPs need
  * 2 receives per call.  Counts travel as WRITE_WITH_IMM into every rank's count table (a host
  * buffer), which also orders calls: a rank's next dispatch writes nothing before every rank has
@@ -104,7 +103,7 @@ typedef struct ugdr_x_vmoe {
     uint32_t recv_rkey;
     uint32_t back_lkey;
     uint64_t recv_rows;
-    uint64_t back_addr;     /* [tokens * topk][row_bytes]: rows read back, in (token, k) order */
+    uint64_t back_addr;     /* [tokens * topk][row_bytes]: rows read back, grouped by expert */
     int32_t *table;         /* host [n][nexp] counts (registered: table_lkey / table_rkey) */
     uint32_t table_lkey;
     uint32_t table_rkey;
@@ -131,9 +130,11 @@ int ugdr_x_verbs_moe_dispatch(ugdr_x_vgroup *g, ugdr_x_vmoe *m, const int32_t *i
                               const int32_t *counts, uint64_t timeout_ns) UGDR_VC_NOEXCEPT;
 
 /* Read every row this rank dispatched (after the owners' experts worked on them in place) back
- * into `back` in (token, k) order.  Blocks until all reads completed. */
-int ugdr_x_verbs_moe_combine(ugdr_x_vgroup *g, ugdr_x_vmoe *m, const int32_t *ids, const int32_t *pos,
-                             uint64_t timeout_ns) UGDR_VC_NOEXCEPT;
+ * into `back`, grouped by expert in the order dispatch sent them: expert e's rows start at row
+ * sum_{e' < e} counts[e'], in position order.  Each (owner, expert) group is ONE contiguous READ;
+ * ugdr_x_moe_weighted_sum_grouped then unpermutes and weights them in one pass.  Blocks until
+ * all reads completed. */
+int ugdr_x_verbs_moe_combine(ugdr_x_vgroup *g, ugdr_x_vmoe *m, uint64_t timeout_ns) UGDR_VC_NOEXCEPT;
 
 #ifdef __cplusplus
 }

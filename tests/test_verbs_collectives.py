@@ -183,7 +183,9 @@ def _moe_worker(rank: int, world: int, port: int, gpu: bool, shape: tuple, calls
                 out = moe.combine(w)
                 if gpu:
                     torch.cuda.synchronize()
-                back = moe.back.cpu()
+                # Rows read back, grouped by expert in position order: row (t, k) at start[e] + pos.
+                idx = (moe.start_d[moe.ids_d.long()] + moe.pos_d.long()).cpu()
+                back = moe.back.cpu()[idx]
                 assert torch.equal(back, x.cpu().repeat_interleave(K, dim=0)), f"rank {rank}: rows read back differ"
                 ref = x.cpu().float() * w.cpu().sum(-1, keepdim=True)
                 assert torch.allclose(out.cpu().float(), ref, atol=2e-2, rtol=1e-2), f"rank {rank}: combine"

@@ -194,8 +194,11 @@ def _moe_lib():
             f.restype = C.c_int
             f.argtypes = [C.POINTER(_Group), C.POINTER(_Moe), C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint64]
         L.ugdr_x_verbs_moe_combine.restype = C.c_int
-        L.ugdr_x_verbs_moe_combine.argtypes = [C.POINTER(_Group), C.POINTER(_Moe), C.c_void_p, C.c_void_p,
-                                               C.c_uint64]
+        L.ugdr_x_verbs_moe_combine.argtypes = [C.POINTER(_Group), C.POINTER(_Moe), C.c_uint64]
+        L.ugdr_x_moe_weighted_sum_grouped.restype = C.c_int
+        L.ugdr_x_moe_weighted_sum_grouped.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                                      C.c_void_p, C.c_uint64, C.c_int, C.c_uint64, C.c_int,
+                                                      C.c_void_p]
         L.ugdr_x_moe_weighted_sum.restype = C.c_int
         L.ugdr_x_moe_weighted_sum.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint64, C.c_int, C.c_uint64,
                                               C.c_int, C.c_void_p]
@@ -223,8 +226,9 @@ class VerbsMoE:
     dispatch(x, ids) routes on the GPU (ugdr_x_moe_route), copies the routing to the host and
     sends every (token, k) row to its expert's owner with WRITEs whose SGE lists are the permute;
     `recv_view()[:received]` then holds this rank's experts' rows, grouped by expert and source
-    rank.  combine(w) READs every row back into (token, k) order (SGE lists again) and returns
-    sum_k w[t, k] * row(t, k) (ugdr_x_moe_weighted_sum)."""
+    rank.  combine(w) READs every (owner, expert) group back in one piece into `back` (grouped by
+    expert) and returns sum_k w[t, k] * row(t, k), the unpermute being the gather of the
+    weighted sum (ugdr_x_moe_weighted_sum_grouped)."""
 
     def __init__(self, group: VerbsGroup, tokens: int, hidden: int, topk: int, nexp: int, recv_rows: int):
         if nexp % group.world:
@@ -291,6 +295,14 @@ class VerbsMoE:
         pos_h = pos.reshape(-1).to(torch.int32).cpu().contiguous()  # synchronises: x and the routing are ready
         counts_h = counts.to(torch.int32).cpu().contiguous()
         self.ids, self.pos = ids_h, pos_h
+        # For the combine's grouped weighted sum: the routing on the rows' device and each
+        # expert's first row in the expert-grouped area.
+        start = torch.zeros(self.nexp, dtype=torch.int64)
+        start[1:] = torch.cumsum(counts_h.to(torch.int64), 0)[:-1]
+        dev = self.x.device
+        self.ids_d = expert_ids.reshape(-1).to(device=dev, dtype=torch.int32).contiguous()
+        self.pos_d = pos.reshape(-1).to(device=dev, dtype=torch.int32).contiguous()
+        self.start_d = start.to(dev)
         rc = _moe_lib().ugdr_x_verbs_moe_dispatch(C.byref(self.g._g), C.byref(self._m), ids_h.data_ptr(),
                                                    pos_h.data_ptr(), counts_h.data_ptr(), int(timeout_s * 1e9))
         if rc != 0:
@@ -298,13 +310,13 @@ class VerbsMoE:
 
     def combine(self, weights: torch.Tensor, out: torch.Tensor | None = None, timeout_s: float = 60.0) -> torch.Tensor:
         L = _moe_lib()
-        rc = L.ugdr_x_verbs_moe_combine(C.byref(self.g._g), C.byref(self._m), self.ids.data_ptr(),
-                                        self.pos.data_ptr(), int(timeout_s * 1e9))
+        rc = L.ugdr_x_verbs_moe_combine(C.byref(self.g._g), C.byref(self._m), int(timeout_s * 1e9))
         if rc != 0:
             raise V.UgdrError(rc, f"ugdr_x_verbs_moe_combine: {N.errname(rc)}")
-        w = weights.reshape(-1).to(torch.float32).contiguous()
+        w = weights.reshape(-1).to(device=self.x.device, dtype=torch.float32).contiguous()
         if not self.gpu:
-            rows = self.back.float().view(self.tokens, self.topk, self.hidden)
+            idx = (self.start_d[self.ids_d.long()] + self.pos_d.long())
+            rows = self.back[idx].float().view(self.tokens, self.topk, self.hidden)
             res = (rows * w.view(self.tokens, self.topk, 1)).sum(1).to(torch.bfloat16)
             if out is not None:
                 out.copy_(res)
@@ -312,10 +324,12 @@ class VerbsMoE:
             return res
         if out is None:
             out = torch.empty(self.tokens, self.hidden, dtype=torch.bfloat16, device=self.x.device)
-        rc = L.ugdr_x_moe_weighted_sum(out.data_ptr(), self.back.data_ptr(), w.data_ptr(), self.tokens, self.topk,
-                                       self.row_bytes, 0, torch.cuda.current_stream().cuda_stream)
+        rc = L.ugdr_x_moe_weighted_sum_grouped(out.data_ptr(), self.back.data_ptr(), self.ids_d.data_ptr(),
+                                               self.pos_d.data_ptr(), self.start_d.data_ptr(), w.data_ptr(),
+                                               self.tokens, self.topk, self.row_bytes, 0,
+                                               torch.cuda.current_stream().cuda_stream)
         if rc != 0:
-            raise RuntimeError(f"ugdr_x_moe_weighted_sum: cudaError {rc}")
+            raise RuntimeError(f"ugdr_x_moe_weighted_sum_grouped: cudaError {rc}")
         return out
 
     def close(self) -> None:
