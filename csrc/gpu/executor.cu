@@ -1847,6 +1847,13 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
         w.started = true;
     }
     const uint32_t fast_err = __ballot_sync(0xffffffffu, uint32_t(w.lane) < fast_n && lw.status != 0);
+    // Staged WRs that need chunk copies share ONE job: the first takes the slot, each adds its
+    // chunks (lane i holds WR i's first chunk index), staged inline WRs after it join with zero
+    // chunks so the job's WRs stay consecutive in the window, and the job is published once,
+    // when the loop ends for whatever reason.
+    int bslot = -1;
+    unsigned long long bgen = 0;
+    uint32_t bfirst = 0, bn = 0, bchunks = 0, bcb = 0, my_start = 0;
     for (uint64_t j = fast_err ? avail : issued; j < avail; ++j) {
         const uint64_t issue = issue0 + j;
         const uint8_t *wqe = wqe_smem + j * v.sq_stride;
@@ -1868,17 +1875,20 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
 
         // A WR that becomes a job takes its job slot first: with no slot free the WR waits for a
         // later pass before anything (an RQ claim, a copy) has been done for it.
-        int slot = -1;
-        unsigned long long gen = 0;
         const bool needs_job = status == UGDR_WC_SUCCESS && !is_atomic(op) && total > kInlineBytes;
-        if (needs_job) {
+        bool took = false;  // this WR took the batch's job slot
+        if (needs_job && bslot < 0) {
+            int slot = -1;
+            unsigned long long gen = 0;
             if (w.lane == 0) slot = take_job_slot(jr, w.gwarp + uint32_t(issue), &gen);
             slot = bcast(slot);
-            gen = bcast64(gen);
             if (slot < 0) {  // no job slot: retry on a later pass
                 if (w.lane == 0) w.ctr->n_slot_miss += 1;
                 break;
             }
+            bslot = slot;
+            bgen = bcast64(gen);
+            took = true;
         }
 
         // Responder RQ for WRITE_WITH_IMM (RNR when empty).
@@ -1913,10 +1923,10 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
                 }
             }
             rnr = bcast(rnr);
-            if (rnr != 0 && slot >= 0) {
+            if (rnr != 0 && took) {
                 // No job after all: hand the taken slot back (its sequence becomes even again).
-                if (w.lane == 0) atomicAdd(&jr->slots[slot].seq, 1ull);
-                slot = -1;
+                if (w.lane == 0) atomicAdd(&jr->slots[bslot].seq, 1ull);
+                bslot = -1;
             }
             if (rnr == 1) break;
             if (rnr == 2) {
@@ -1934,20 +1944,37 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
         }
         w.started = true;
         if (status == UGDR_WC_SUCCESS) {
-            if (slot < 0) {
+            if (!(needs_job && bslot >= 0)) {
                 run_inline(w, rec, wqe, op, total, remote);
                 ++inline_ran;
+                if (bn > 0) {  // inside the job's range, with no chunks
+                    if (uint32_t(w.lane) == bn) my_start = bchunks;
+                    ++bn;
+                }
             } else {
-                const uint32_t chunk = chunk_for(total, nwarps);
-                const uint32_t n = uint32_t((total + chunk - 1) / chunk);
+                if (bn == 0) {
+                    bfirst = uint32_t(issue % kWindow);
+                    bcb = chunk_for(total, nwarps);
+                }
+                const uint32_t n = uint32_t((total + bcb - 1) / bcb);
                 if (w.lane == 0) rec->nchunks = n;
-                publish_job(w, jr, bitmap, slot, gen, qp->st.win, uint32_t(issue % kWindow), 1u, 0u, n, chunk);
+                if (uint32_t(w.lane) == bn) my_start = bchunks;
+                ++bn;
+                bchunks += n;
             }
         }
         if (w.lane == 0) w.ctr->n_slow += 1;
         if (w.lane == 0) w.ctr->t_slow += gtime() - t_stage;
         ++issued;
         if (status != UGDR_WC_SUCCESS) break;  // stop issuing behind an error
+    }
+    if (bslot >= 0) {
+        if (bchunks > 0) {
+            __syncwarp();
+            publish_job(w, jr, bitmap, bslot, bgen, qp->st.win, bfirst, bn, my_start, bchunks, bcb);
+        } else if (w.lane == 0) {
+            atomicAdd(&jr->slots[bslot].seq, 1ull);  // nothing to copy after all: free the slot
+        }
     }
     if (issued > 0) {
         __syncwarp();
