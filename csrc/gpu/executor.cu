@@ -280,7 +280,7 @@ __device__ void warp_copy(uint8_t *dst, const uint8_t *src, uint64_t n, int lane
 // wants.  Every mbarrier wait is bounded; when one runs out the copy waits (bounded) for its other
 // loads, reports failure and the kernel exits with kErrBulkCopyTimeout.
 #ifndef UGDR_TMA_STAGES
-#define UGDR_TMA_STAGES 3  // 0 builds the executor without the bulk-copy path (no dynamic smem)
+#define UGDR_TMA_STAGES 2  // 0 builds the executor without the bulk-copy path (no dynamic smem)
 #endif
 constexpr uint32_t kTmaStages = UGDR_TMA_STAGES > 0 ? UGDR_TMA_STAGES : 1;
 constexpr bool kTmaBuilt = UGDR_TMA_STAGES > 0;
