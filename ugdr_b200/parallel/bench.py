@@ -348,10 +348,22 @@ def bench_moe_verbs(rank, world, local, iters, warmup, cfg: MoEConfig) -> dict:
         torch.cuda.synchronize()
         dist.barrier(group=_GLOO)
         t0 = time.perf_counter()
+        td = tc = 0.0
+        st0 = g.ctx.stats()
         for _ in range(iters):
-            step()
-        torch.cuda.synchronize()
+            a = time.perf_counter()
+            moe.dispatch(x, ids)
+            b = time.perf_counter()
+            moe.combine(w)
+            torch.cuda.synchronize()
+            td += b - a
+            tc += time.perf_counter() - b
         ms = (time.perf_counter() - t0) / iters * 1e3
+        st1 = g.ctx.stats()
+        split = {"dispatch_ms": round(td / iters * 1e3, 3), "combine_ms": round(tc / iters * 1e3, 3),
+                 "slow_wrs_per_step": (int(st1.slow_wrs) - int(st0.slow_wrs)) // iters,
+                 "jobs_per_step": (int(st1.jobs_published) - int(st0.jobs_published)) // iters,
+                 "order_waits_per_step": (int(st1.order_waits) - int(st0.order_waits)) // iters}
         t = torch.tensor([ms], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=_GLOO)
         ms = float(t.item())
@@ -364,7 +376,7 @@ def bench_moe_verbs(rank, world, local, iters, warmup, cfg: MoEConfig) -> dict:
             daemon.stop()
     moved = 2 * T * K * H * 2
     return {"op": "moe_dispatch_combine_verbs", "n_gpus": world, "tokens": T, "hidden": H, "topk": K, "experts": E,
-            "ugdr_verbs_ms": round(ms, 4), "ugdr_verbs_GBps_per_rank": round(moved / ms / 1e6, 1),
+            "ugdr_verbs_ms": round(ms, 4), "ugdr_verbs_GBps_per_rank": round(moved / ms / 1e6, 1), **split,
             "correct": bool(ok), "timing": "wall clock per step (route + host copy of the routing + dispatch WRs + "
                                            "combine WRs + weighted sum), max over ranks"}
 
