@@ -177,4 +177,12 @@ int ugdr_x_moe_weighted_sum_grouped(void *out, const void *rows, const int32_t *
                                             pos, start);
 }
 
+int ugdr_x_moe_pack_grouped(void *rows, const void *x, const int32_t *ids, const int32_t *pos, const int64_t *start,
+                            uint64_t tokens, int topk, uint64_t row_bytes, int ctas, void *stream) {
+    if (rows == nullptr || x == nullptr || ids == nullptr || pos == nullptr || start == nullptr)
+        return int(cudaErrorInvalidValue);
+    return ugdr::coll::launch_pack_rows(rows, x, tokens, topk, row_bytes, ids, pos, start,
+                                        ctas > 0 ? ctas : default_ctas(), static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

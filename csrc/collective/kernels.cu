@@ -484,6 +484,38 @@ __global__ void __launch_bounds__(512) weighted_rows_kernel(uint8_t *out, const 
     }
 }
 
+// Pack for the MoE dispatch on the verbs: row (t, k) of x goes to rows[start[ids[t, k]] +
+// pos[t, k]], so every expert's rows are contiguous and each (owner, expert) group leaves in ONE
+// WRITE.  One warp per token: its row is loaded once (16 B per lane per step) and stored to its
+// top-k destinations.
+template <int TOPK>
+__global__ void __launch_bounds__(512) pack_rows_kernel(uint8_t *rows, const uint8_t *x, uint64_t ntok, int topk,
+                                                        uint64_t row_bytes, const int32_t *ids, const int32_t *pos,
+                                                        const int64_t *start) {
+    const int lane = threadIdx.x & 31;
+    const uint64_t warp = (uint64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const uint64_t nwarps = (uint64_t(gridDim.x) * blockDim.x) >> 5;
+    const uint64_t nv = row_bytes / 16;
+    for (uint64_t t = warp; t < ntok; t += nwarps) {
+        uint8_t *dk[TOPK];
+#pragma unroll
+        for (int k = 0; k < TOPK; ++k) {
+            dk[k] = nullptr;
+            if (k < topk) {
+                const uint64_t r = t * uint64_t(topk) + uint64_t(k);
+                dk[k] = rows + (uint64_t(__ldg(start + __ldg(ids + r))) + uint64_t(__ldg(pos + r))) * row_bytes;
+            }
+        }
+        const uint8_t *xr = x + t * row_bytes;
+        for (uint64_t i = lane; i < nv; i += 32) {
+            const uint4 v = ld128(xr + i * 16);
+#pragma unroll
+            for (int k = 0; k < TOPK; ++k)
+                if (k < topk) st128(dk[k] + i * 16, v);
+        }
+    }
+}
+
 // Counts exchange: this rank's per-expert counts stored into every rank's table
 // (table[rank * nexp + e], int32, at byte `table_off` of each buffer), then the end barrier.
 __global__ void counts_exchange_kernel(PeerSet ps, const int32_t *counts, int nexp, uint64_t table_off,
@@ -575,6 +607,7 @@ int collective_kernels(const KernelRef **out) {
         {"dispatch_kernel", reinterpret_cast<const void *>(&dispatch_kernel), 512},
         {"combine_kernel<8>", reinterpret_cast<const void *>(&combine_kernel<8>), 512},
         {"weighted_rows_kernel<8>", reinterpret_cast<const void *>(&weighted_rows_kernel<8>), 512},
+        {"pack_rows_kernel<8>", reinterpret_cast<const void *>(&pack_rows_kernel<8>), 512},
     };
     *out = refs;
     return int(sizeof(refs) / sizeof(refs[0]));
@@ -641,6 +674,22 @@ int launch_weighted_rows(void *out, const void *rows, const float *w, uint64_t n
         weighted_rows_kernel<8><<<ctas, 512, 0, s>>>(o, r, w, ntok, topk, row_bytes, ids, pos, start);
     else
         weighted_rows_kernel<16><<<ctas, 512, 0, s>>>(o, r, w, ntok, topk, row_bytes, ids, pos, start);
+    return int(cudaGetLastError());
+}
+
+int launch_pack_rows(void *rows, const void *x, uint64_t ntok, int topk, uint64_t row_bytes, const int32_t *ids,
+                     const int32_t *pos, const int64_t *start, int ctas, cudaStream_t s) {
+    if (row_bytes % 16 != 0 || topk <= 0 || topk > 16) return int(cudaErrorInvalidValue);
+    uint8_t *o = static_cast<uint8_t *>(rows);
+    const uint8_t *r = static_cast<const uint8_t *>(x);
+    if (topk <= 2)
+        pack_rows_kernel<2><<<ctas, 512, 0, s>>>(o, r, ntok, topk, row_bytes, ids, pos, start);
+    else if (topk <= 4)
+        pack_rows_kernel<4><<<ctas, 512, 0, s>>>(o, r, ntok, topk, row_bytes, ids, pos, start);
+    else if (topk <= 8)
+        pack_rows_kernel<8><<<ctas, 512, 0, s>>>(o, r, ntok, topk, row_bytes, ids, pos, start);
+    else
+        pack_rows_kernel<16><<<ctas, 512, 0, s>>>(o, r, ntok, topk, row_bytes, ids, pos, start);
     return int(cudaGetLastError());
 }
 

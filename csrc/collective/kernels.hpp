@@ -49,6 +49,9 @@ int launch_dispatch(const PeerSet &ps, const void *x, uint64_t row_bytes, const 
 int launch_weighted_rows(void *out, const void *rows, const float *w, uint64_t ntok, int topk, uint64_t row_bytes,
                          int ctas, cudaStream_t s, const int32_t *ids = nullptr, const int32_t *pos = nullptr,
                          const int64_t *start = nullptr);
+// rows[start[ids[t, k]] + pos[t, k]] = x[t] for every (t, k): x's rows grouped by expert.
+int launch_pack_rows(void *rows, const void *x, uint64_t ntok, int topk, uint64_t row_bytes, const int32_t *ids,
+                     const int32_t *pos, const int64_t *start, int ctas, cudaStream_t s);
 int launch_combine(const PeerSet &ps, void *out, uint64_t row_bytes, const int32_t *idx, const int32_t *pos,
                    const int64_t *gbase, const float *w, uint64_t ntok, int topk, int exp_per_rank,
                    uint64_t recv_off, uint64_t recv_rows, uint64_t epoch, int ctas, uint64_t max_ns,

@@ -7,7 +7,9 @@
 // rank) group starts in each owner's receive area.  Then, per owner and expert, WRITEs of up to
 // 32 SGEs gather this rank's rows of that expert (one SGE per token row) into the group's
 // contiguous range; the last WR to each owner carries an immediate that tells the owner this
-// rank's rows have all landed (the owner's QP retires WRs in order).
+// rank's rows have all landed (the owner's QP retires WRs in order).  The packed form takes the
+// rows already grouped by expert (ugdr_x_moe_pack_grouped on the GPU) and sends each
+// (owner, expert) group as one contiguous WRITE.
 // Combine: per owner and expert, READs of up to 32 SGEs bring the group back and scatter it
 // (one SGE per row) into (token, k) order.
 //
@@ -130,12 +132,28 @@ extern "C" uint32_t ugdr_x_verbs_moe_wrs(uint64_t rows_per_rank, int nexp, int n
     return uint32_t((rows_per_rank + kSgePerWr - 1) / kSgePerWr + uint64_t(nexp / n) + 2);
 }
 
-extern "C" int ugdr_x_verbs_moe_dispatch(ugdr_x_vgroup *g, ugdr_x_vmoe *m, const int32_t *ids, const int32_t *pos,
-                                         const int32_t *counts, uint64_t timeout_ns) noexcept {
-    if (!valid(g, m) || ids == nullptr || pos == nullptr || counts == nullptr) return EINVAL;
+namespace {
+
+// Both dispatch forms.  Gathered (`ids` / `pos` given): per owner and expert, WRs of up to 32
+// row SGEs straight from x.  Packed (`ids` null): `back` already holds this rank's rows grouped
+// by expert, and each (owner, expert) group leaves as ONE contiguous WRITE, so the executors
+// chunk it over all their warps instead of staging one 32-SGE WR per pass.
+int dispatch(ugdr_x_vgroup *g, ugdr_x_vmoe *m, const int32_t *ids, const int32_t *pos, const int32_t *counts,
+             uint64_t timeout_ns) {
     const int n = g->n, r = g->rank, E = m->nexp, epr = E / n;
+    const bool packed = ids == nullptr;
     Buckets b;
-    if (int rc = bucket(m, ids, pos, counts, &b); rc != 0) return rc;
+    if (packed) {
+        b.start.assign(size_t(E) + 1, 0);
+        for (int e = 0; e < E; ++e) {
+            if (counts[e] < 0) return EINVAL;
+            b.start[e + 1] = b.start[e] + uint64_t(counts[e]);
+        }
+        if (b.start[E] != uint64_t(m->tokens) * uint64_t(m->topk)) return EINVAL;
+        if (m->back_addr == 0) return EINVAL;
+    } else if (int rc = bucket(m, ids, pos, counts, &b); rc != 0) {
+        return rc;
+    }
     const uint32_t epoch = g->epoch++;
 
     // Receives: one count-table write and one rows-landed immediate from every peer.
@@ -213,6 +231,21 @@ extern "C" int ugdr_x_verbs_moe_dispatch(ugdr_x_vgroup *g, ugdr_x_vmoe *m, const
         c.wr.reserve(size_t(nrows / kSgePerWr + epr + 2));
         for (int e = q * epr; e < (q + 1) * epr; ++e) {
             const uint64_t ce = uint64_t(counts[e]);
+            if (packed) {
+                // One WRITE per group, split only where an SGE's 32-bit length would overflow.
+                const uint64_t per = 0xffffffffull / rb;  // >= 1: row_bytes is 32-bit
+                for (uint64_t j = 0; j < ce; j += per) {
+                    const uint64_t take = ce - j < per ? ce - j : per;
+                    c.sge.push_back(ugdr_sge{m->back_addr + (b.start[e] + j) * rb, uint32_t(take * rb), m->back_lkey});
+                    ugdr_send_wr w{};
+                    w.num_sge = 1;
+                    w.opcode = UGDR_WR_RDMA_WRITE;
+                    w.wr.rdma.remote_addr = dst0 + (m->base[size_t(e) * size_t(n) + size_t(r)] + j) * rb;
+                    w.wr.rdma.rkey = rkey;
+                    c.wr.push_back(w);
+                }
+                continue;
+            }
             for (uint64_t j = 0; j < ce; j += kSgePerWr) {
                 const uint64_t take = ce - j < uint64_t(kSgePerWr) ? ce - j : uint64_t(kSgePerWr);
                 const size_t first = c.sge.size();
@@ -245,9 +278,25 @@ extern "C" int ugdr_x_verbs_moe_dispatch(ugdr_x_vgroup *g, ugdr_x_vmoe *m, const
             w.wr.rdma.rkey = rkey;
         }
         c.wr.push_back(w);
+        if (packed)  // sg_list of WR i is SGE i (the closing WR has none)
+            for (size_t i = 0; i + 1 < c.wr.size(); ++i) c.wr[i].sg_list = &c.sge[i];
         c.link();
     }
     return drive(g, chains, timeout_ns, [&] { return rows_in == n - 1 && lasts == n; }, on);
+}
+
+}  // namespace
+
+extern "C" int ugdr_x_verbs_moe_dispatch(ugdr_x_vgroup *g, ugdr_x_vmoe *m, const int32_t *ids, const int32_t *pos,
+                                         const int32_t *counts, uint64_t timeout_ns) noexcept {
+    if (!valid(g, m) || ids == nullptr || pos == nullptr || counts == nullptr) return EINVAL;
+    return dispatch(g, m, ids, pos, counts, timeout_ns);
+}
+
+extern "C" int ugdr_x_verbs_moe_dispatch_packed(ugdr_x_vgroup *g, ugdr_x_vmoe *m, const int32_t *counts,
+                                                uint64_t timeout_ns) noexcept {
+    if (!valid(g, m) || counts == nullptr) return EINVAL;
+    return dispatch(g, m, nullptr, nullptr, counts, timeout_ns);
 }
 
 extern "C" int ugdr_x_verbs_moe_combine(ugdr_x_vgroup *g, ugdr_x_vmoe *m, uint64_t timeout_ns) noexcept {

@@ -131,6 +131,12 @@ int ugdr_x_moe_weighted_sum(void *out, const void *rows, const float *weights, u
 int ugdr_x_moe_weighted_sum_grouped(void *out, const void *rows, const int32_t *ids, const int32_t *pos,
                                     const int64_t *start, const float *weights, uint64_t tokens, int topk,
                                     uint64_t row_bytes, int ctas, void *stream);
+/* The inverse gather: rows[start[ids[t * topk + k]] + pos[t * topk + k]] = x[t] for every (t, k)
+ * (all on the device), so every expert's rows are contiguous: the pack before the MoE dispatch on
+ * the verbs (ugdr_x_verbs_moe_dispatch_packed).  Each x row is read once.  row_bytes a multiple
+ * of 16. */
+int ugdr_x_moe_pack_grouped(void *rows, const void *x, const int32_t *ids, const int32_t *pos, const int64_t *start,
+                            uint64_t tokens, int topk, uint64_t row_bytes, int ctas, void *stream);
 int ugdr_x_moe_combine(const ugdr_x_peerset *ps, void *out, uint64_t row_bytes, const int32_t *expert_ids,
                        const int32_t *positions, const int64_t *group_base, const float *weights,
                        uint64_t tokens, int topk, int experts_per_rank, uint64_t recv_offset, uint64_t recv_rows,

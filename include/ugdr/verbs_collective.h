@@ -129,6 +129,13 @@ uint32_t ugdr_x_verbs_moe_wrs(uint64_t rows_per_rank, int nexp, int n) UGDR_VC_N
 int ugdr_x_verbs_moe_dispatch(ugdr_x_vgroup *g, ugdr_x_vmoe *m, const int32_t *ids, const int32_t *pos,
                               const int32_t *counts, uint64_t timeout_ns) UGDR_VC_NOEXCEPT;
 
+/* The same from rows already grouped by expert: `back` holds this rank's tokens * topk rows,
+ * expert e's from row sum_{e' < e} counts[e'] on (as ugdr_x_moe_pack_grouped writes them), and
+ * each (owner, expert) group leaves as ONE contiguous WRITE, which the executors split into
+ * chunks over all their warps.  Same result, completions and errors as the gathering form. */
+int ugdr_x_verbs_moe_dispatch_packed(ugdr_x_vgroup *g, ugdr_x_vmoe *m, const int32_t *counts,
+                                     uint64_t timeout_ns) UGDR_VC_NOEXCEPT;
+
 /* Read every row this rank dispatched (after the owners' experts worked on them in place) back
  * into `back`, grouped by expert in the order dispatch sent them: expert e's rows start at row
  * sum_{e' < e} counts[e'], in position order.  Each (owner, expert) group is ONE contiguous READ;

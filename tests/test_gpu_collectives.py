@@ -40,6 +40,39 @@ def test_moe_route_rejects_out_of_range_ids(one_gpu):
     assert pos.tolist() == [[0, 0], [-1, 0], [-1, 1]]
 
 
+@pytest.mark.parametrize("tokens,hidden,experts,topk", [(1, 8, 4, 1), (777, 1024, 64, 8), (300, 7168, 256, 3)])
+def test_pack_grouped_and_grouped_weighted_sum(one_gpu, tokens, hidden, experts, topk):
+    """ugdr_x_moe_pack_grouped places row (t, k) at start[e] + pos exactly (a permutation, bit for
+    bit), and ugdr_x_moe_weighted_sum_grouped on that layout matches an fp32 torch weighted sum."""
+    from ugdr_b200.models.moe import route
+    from ugdr_b200.parallel.collectives import moe_route
+    from ugdr_b200.parallel.verbs_collectives import _moe_lib
+
+    L = _moe_lib()
+    ids, w = route(tokens, experts, topk, seed=tokens + hidden)
+    counts, pos = moe_route(ids, experts)
+    x = torch.randn(tokens, hidden, device="cuda").to(torch.bfloat16)
+    ids_d = ids.reshape(-1).to(torch.int32).contiguous()
+    pos_d = pos.reshape(-1).to(torch.int32).contiguous()
+    c64 = counts.to(torch.int64)
+    start = torch.cumsum(c64, 0) - c64
+    rows = torch.full((tokens * topk, hidden), float("nan"), device="cuda", dtype=torch.bfloat16)
+    s = torch.cuda.current_stream().cuda_stream
+    assert L.ugdr_x_moe_pack_grouped(rows.data_ptr(), x.data_ptr(), ids_d.data_ptr(), pos_d.data_ptr(),
+                                     start.data_ptr(), tokens, topk, hidden * 2, 0, s) == 0
+    torch.cuda.synchronize()
+    idx = start[ids_d.long()] + pos_d.long()
+    assert torch.equal(torch.sort(idx).values, torch.arange(tokens * topk, device="cuda"))
+    assert torch.equal(rows[idx], x.repeat_interleave(topk, dim=0))
+    wf = w.reshape(-1).to(device="cuda", dtype=torch.float32).contiguous()
+    out = torch.empty(tokens, hidden, device="cuda", dtype=torch.bfloat16)
+    assert L.ugdr_x_moe_weighted_sum_grouped(out.data_ptr(), rows.data_ptr(), ids_d.data_ptr(), pos_d.data_ptr(),
+                                             start.data_ptr(), wf.data_ptr(), tokens, topk, hidden * 2, 0, s) == 0
+    torch.cuda.synchronize()
+    ref = (x.float().unsqueeze(1) * wf.view(tokens, topk, 1)).sum(1)
+    assert torch.allclose(out.float(), ref, atol=1e-2, rtol=1e-2)
+
+
 def _single_rank_group(nbytes):
     from ugdr_b200.parallel.peers import PeerGroup
 

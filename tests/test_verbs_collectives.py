@@ -175,7 +175,8 @@ def _moe_worker(rank: int, world: int, port: int, gpu: bool, shape: tuple, calls
         try:
             for call in range(calls):
                 x, ids, w = _moe_inputs(rank, T, H, K, E, call, dev)
-                moe.dispatch(x, ids)
+                # On the GPU the calls alternate the packed dispatch (the default) and the 32-SGE gathers.
+                moe.dispatch(x, ids, packed=(call % 2 == 0) if gpu else None)
                 got = moe.recv_view().cpu()
                 want = _moe_expected_recv(rank, world, T, H, K, E, call)
                 assert got.shape == want.shape, (got.shape, want.shape)

@@ -190,9 +190,14 @@ def _moe_lib():
     if not getattr(L, "_vmoe_sigs", False):
         L.ugdr_x_verbs_moe_wrs.restype = C.c_uint32
         L.ugdr_x_verbs_moe_wrs.argtypes = [C.c_uint64, C.c_int, C.c_int]
-        for f in (L.ugdr_x_verbs_moe_dispatch,):
-            f.restype = C.c_int
-            f.argtypes = [C.POINTER(_Group), C.POINTER(_Moe), C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint64]
+        L.ugdr_x_verbs_moe_dispatch.restype = C.c_int
+        L.ugdr_x_verbs_moe_dispatch.argtypes = [C.POINTER(_Group), C.POINTER(_Moe), C.c_void_p, C.c_void_p,
+                                                C.c_void_p, C.c_uint64]
+        L.ugdr_x_verbs_moe_dispatch_packed.restype = C.c_int
+        L.ugdr_x_verbs_moe_dispatch_packed.argtypes = [C.POINTER(_Group), C.POINTER(_Moe), C.c_void_p, C.c_uint64]
+        L.ugdr_x_moe_pack_grouped.restype = C.c_int
+        L.ugdr_x_moe_pack_grouped.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                              C.c_uint64, C.c_int, C.c_uint64, C.c_int, C.c_void_p]
         L.ugdr_x_verbs_moe_combine.restype = C.c_int
         L.ugdr_x_verbs_moe_combine.argtypes = [C.POINTER(_Group), C.POINTER(_Moe), C.c_uint64]
         L.ugdr_x_moe_weighted_sum_grouped.restype = C.c_int
@@ -223,8 +228,9 @@ def _host_tensor(nbytes: int, dtype, shape, keep: list):
 class VerbsMoE:
     """MoE all-to-all on the verbs (ugdr_x_verbs_moe_dispatch / _combine).
 
-    dispatch(x, ids) routes on the GPU (ugdr_x_moe_route), copies the routing to the host and
-    sends every (token, k) row to its expert's owner with WRITEs whose SGE lists are the permute;
+    dispatch(x, ids) routes on the GPU (ugdr_x_moe_route), groups the rows by expert into `back`
+    (ugdr_x_moe_pack_grouped) and sends each (owner, expert) group with one WRITE (on the host
+    engine, or with packed=False, WRITEs whose 32-SGE lists gather the rows are the permute);
     `recv_view()[:received]` then holds this rank's experts' rows, grouped by expert and source
     rank.  combine(w) READs every (owner, expert) group back in one piece into `back` (grouped by
     expert) and returns sum_k w[t, k] * row(t, k), the unpermute being the gather of the
@@ -274,15 +280,28 @@ class VerbsMoE:
             m.peer_table_addr[q], m.peer_table_rkey[q] = info[q]["table"]
         m.base = self.base.ctypes.data
         self._m = m
-        self.ids = self.pos = None
         self.scratch = None
 
     def recv_view(self) -> torch.Tensor:
         return self.recv[: int(self._m.received)]
 
-    def dispatch(self, x: torch.Tensor | None, expert_ids: torch.Tensor, timeout_s: float = 60.0) -> None:
+    def dispatch(self, x: torch.Tensor | None, expert_ids: torch.Tensor, timeout_s: float = 60.0,
+                 packed: bool | None = None) -> None:
+        """Send every (token, k) row of x to its expert's owner.  On the GPU the default is the
+        packed form: ugdr_x_moe_pack_grouped groups the rows by expert into `back` (each x row
+        read once, straight from the caller's tensor) and every (owner, expert) group leaves as
+        one contiguous WRITE.  packed=False (and the host engine) gathers the rows with 32-SGE
+        WRITEs from the registered x instead."""
+        packed = self.gpu if packed is None else packed
+        if packed and not self.gpu:
+            raise ValueError("the packed dispatch needs GPU memory")
+        src = self.x
         if x is not None:
-            self.x.copy_(x)
+            if packed and x.is_contiguous() and x.dtype == torch.bfloat16 and x.shape == self.x.shape \
+                    and x.device == self.x.device:
+                src = x
+            else:
+                self.x.copy_(x)
         if self.gpu:
             from .collectives import moe_route
 
@@ -291,22 +310,33 @@ class VerbsMoE:
             from ..models.moe import reference_positions
 
             counts, pos = reference_positions(expert_ids, self.nexp)
-        ids_h = expert_ids.reshape(-1).to(torch.int32).cpu().contiguous()
-        pos_h = pos.reshape(-1).to(torch.int32).cpu().contiguous()  # synchronises: x and the routing are ready
-        counts_h = counts.to(torch.int32).cpu().contiguous()
-        self.ids, self.pos = ids_h, pos_h
-        # For the combine's grouped weighted sum: the routing on the rows' device and each
-        # expert's first row in the expert-grouped area.
-        start = torch.zeros(self.nexp, dtype=torch.int64)
-        start[1:] = torch.cumsum(counts_h.to(torch.int64), 0)[:-1]
         dev = self.x.device
+        # The routing on the rows' device and each expert's first row in the expert-grouped area
+        # (`back`): the pack, and the combine's grouped weighted sum, gather through them.
         self.ids_d = expert_ids.reshape(-1).to(device=dev, dtype=torch.int32).contiguous()
         self.pos_d = pos.reshape(-1).to(device=dev, dtype=torch.int32).contiguous()
-        self.start_d = start.to(dev)
-        rc = _moe_lib().ugdr_x_verbs_moe_dispatch(C.byref(self.g._g), C.byref(self._m), ids_h.data_ptr(),
-                                                   pos_h.data_ptr(), counts_h.data_ptr(), int(timeout_s * 1e9))
+        c64 = counts.to(device=dev, dtype=torch.int64)
+        self.start_d = torch.cumsum(c64, 0) - c64
+        L = _moe_lib()
+        if packed:
+            rc = L.ugdr_x_moe_pack_grouped(self.back.data_ptr(), src.data_ptr(), self.ids_d.data_ptr(),
+                                           self.pos_d.data_ptr(), self.start_d.data_ptr(), self.tokens, self.topk,
+                                           self.row_bytes, 0, torch.cuda.current_stream().cuda_stream)
+            if rc != 0:
+                raise RuntimeError(f"ugdr_x_moe_pack_grouped: cudaError {rc}")
+        counts_h = counts.to(torch.int32).cpu().contiguous()  # synchronises: the rows and the routing are ready
+        if packed:
+            rc = L.ugdr_x_verbs_moe_dispatch_packed(C.byref(self.g._g), C.byref(self._m), counts_h.data_ptr(),
+                                                    int(timeout_s * 1e9))
+            name = "ugdr_x_verbs_moe_dispatch_packed"
+        else:
+            ids_h = expert_ids.reshape(-1).to(torch.int32).cpu().contiguous()
+            pos_h = pos.reshape(-1).to(torch.int32).cpu().contiguous()
+            rc = L.ugdr_x_verbs_moe_dispatch(C.byref(self.g._g), C.byref(self._m), ids_h.data_ptr(),
+                                             pos_h.data_ptr(), counts_h.data_ptr(), int(timeout_s * 1e9))
+            name = "ugdr_x_verbs_moe_dispatch"
         if rc != 0:
-            raise V.UgdrError(rc, f"ugdr_x_verbs_moe_dispatch: {N.errname(rc)}")
+            raise V.UgdrError(rc, f"{name}: {N.errname(rc)}")
 
     def combine(self, weights: torch.Tensor, out: torch.Tensor | None = None, timeout_s: float = 60.0) -> torch.Tensor:
         L = _moe_lib()
