@@ -41,7 +41,7 @@ namespace {
 
 constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
-constexpr uint32_t kWqeStage = 1024;  // per-warp WQE staging: 16 slots of 64 B, or one of 576
+constexpr uint32_t kWqeStage = 1024;  // per-warp WQE staging: 16 WQEs of 64 B, or one wide one of up to 576
 constexpr uint32_t kChunkMin = 16384;
 constexpr uint32_t kChunkMax = 262144;
 
@@ -1468,14 +1468,14 @@ struct LaneWr {
     uint32_t status, op, signaled;
 };
 
-__device__ uint32_t issue_fast(Warp &w, DevQp *qp, const QpView &v, const uint8_t *wqe_smem, uint64_t head,
+__device__ uint32_t issue_fast(Warp &w, DevQp *qp, const QpView &v, const uint8_t *wqe_smem, uint32_t st, uint64_t head,
                                uint64_t issue0, uint32_t avail, LaneWr *out, JobRing *jr, uint32_t *bitmap,
                                uint32_t nwarps, bool *chunked_out) {
     *chunked_out = false;
     const uint32_t j = uint32_t(w.lane);
     const bool in = j < avail;
-    const queue::SendWqe *h = reinterpret_cast<const queue::SendWqe *>(wqe_smem + (in ? j : 0) * v.sq_stride);
-    const queue::Sge *sg = reinterpret_cast<const queue::Sge *>(wqe_smem + (in ? j : 0) * v.sq_stride +
+    const queue::SendWqe *h = reinterpret_cast<const queue::SendWqe *>(wqe_smem + (in ? j : 0) * st);
+    const queue::Sge *sg = reinterpret_cast<const queue::Sge *>(wqe_smem + (in ? j : 0) * st +
                                                                 queue::kSendSgeOffset);
     const uint32_t op = h->opcode;
     const bool fast = in && (op == UGDR_WR_RDMA_WRITE || op == UGDR_WR_RDMA_READ) && h->sge_count == 1 &&
@@ -1804,9 +1804,15 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
     // Issue: one lane-parallel fetch of every WQE that fits the window and the staging buffer.
     // The SQ tail (a PCIe read) is read only when the window has room and the tail seen last
     // does not already cover it: WQEs below a tail acquired earlier are as valid now.
+    // On a queue whose slots are wider than 64 B (max_send_sge > 1) only each slot's first 64 B
+    // are fetched at first: a WQE of at most one SGE (atomics included) lies wholly inside them,
+    // so up to 16 such WQEs are staged per pass, as on a one-SGE queue.  The batch ends before
+    // the first wider WQE; when that is the first one, it alone is fetched in full.
     const uint64_t head = w.vhead, issue0 = w.vissue;
+    const uint32_t wide = v.sq_stride > 64 ? 1u : 0u;
+    uint32_t st = wide ? 64u : v.sq_stride;  // stage stride: bytes per staged WQE
     uint64_t room = kWindow - (issue0 - head);
-    if (room > kWqeStage / v.sq_stride) room = kWqeStage / v.sq_stride;
+    if (room > kWqeStage / st) room = kWqeStage / st;
     if (room == 0) return work;
     if (w.vtail < issue0 + room) {
         uint64_t tail = 0;
@@ -1818,18 +1824,35 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
     if (avail > room) avail = room;
     if (avail == 0) return work;
     const uint64_t t_fetch0 = gtime();
-    const uint32_t nbytes = uint32_t(avail) * v.sq_stride;
+    const uint32_t nbytes = uint32_t(avail) * st;
     for (uint32_t o = w.lane * 16; o < nbytes; o += 32 * 16) {
-        const uint64_t s = issue0 + o / v.sq_stride;
-        const uint8_t *src = v.sq_slots + (s % v.sq_cap) * v.sq_stride + (o % v.sq_stride);
+        const uint64_t s = issue0 + o / st;
+        const uint8_t *src = v.sq_slots + (s % v.sq_cap) * v.sq_stride + (o % st);
         *reinterpret_cast<uint4 *>(wqe_smem + o) = ld_vol128(src);
     }
     __syncwarp();
+    if (wide) {
+        const bool in = uint32_t(w.lane) < avail;
+        const uint32_t nsge = in ? reinterpret_cast<const queue::SendWqe *>(wqe_smem + w.lane * 64)->sge_count : 0;
+        const uint32_t narrow = __ballot_sync(0xffffffffu, in && nsge <= 1);
+        const uint32_t p = __ffs(~narrow) - 1;  // WQEs before the first wide one
+        __syncwarp();
+        if (p > 0) {
+            avail = p;
+        } else {  // the first WQE is wide: it alone, in full
+            avail = 1;
+            st = v.sq_stride;
+            const uint8_t *src = v.sq_slots + (issue0 % v.sq_cap) * v.sq_stride;
+            for (uint32_t o = w.lane * 16; o < st; o += 32 * 16)
+                *reinterpret_cast<uint4 *>(wqe_smem + o) = ld_vol128(src + o);
+            __syncwarp();
+        }
+    }
     uint32_t inline_ran = 0;
     const uint64_t t_fetch1 = gtime();
     LaneWr lw{0, 0, 0, 0, 0};
     bool fast_chunked = false;
-    uint64_t issued = issue_fast(w, qp, v, wqe_smem, head, issue0, uint32_t(avail), &lw, jr, bitmap, nwarps,
+    uint64_t issued = issue_fast(w, qp, v, wqe_smem, st, head, issue0, uint32_t(avail), &lw, jr, bitmap, nwarps,
                                  &fast_chunked);
     const uint32_t fast_n = uint32_t(issued);
     if (w.lane == 0 && w.p->trace != nullptr) {
@@ -1856,7 +1879,7 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
     uint32_t bfirst = 0, bn = 0, bchunks = 0, bcb = 0, my_start = 0;
     for (uint64_t j = fast_err ? avail : issued; j < avail; ++j) {
         const uint64_t issue = issue0 + j;
-        const uint8_t *wqe = wqe_smem + j * v.sq_stride;
+        const uint8_t *wqe = wqe_smem + j * st;
         WrRec *rec = &qp->st.win[issue % kWindow];
         uint32_t status;
         uint64_t total, remote, lo, hi;
