@@ -117,6 +117,10 @@ struct DevQpState {
     unsigned long long rnr_next_ns;
     uint32_t rnr_attempts;
     uint32_t err;  // executor-detected error: the QP is in ERR
+    // A WR that completes in error has been issued but not yet retired: nothing behind it may
+    // be issued (RC semantics: every later WR is flushed once it retires).  Owner warp only.
+    uint32_t err_issued;
+    uint32_t pad0;
     unsigned long long bytes;   // payload bytes of retired successful send WRs (owner warp writes)
     unsigned long long errors;  // error and flush completions of this QP (owner warp writes)
     WrRec win[kWindow];

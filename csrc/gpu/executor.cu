@@ -39,7 +39,10 @@
 namespace ugdr::gpu {
 namespace {
 
-constexpr int kWarps = 16;
+#ifndef UGDR_EXEC_WARPS
+#define UGDR_EXEC_WARPS 8  // warps per executor CTA (one CTA per SM); 8 keeps every thread under 255 registers with no spills
+#endif
+constexpr int kWarps = UGDR_EXEC_WARPS;
 constexpr int kThreads = kWarps * 32;
 constexpr uint32_t kWqeStage = 1024;  // per-warp WQE staging: 16 WQEs of 64 B, or one wide one of up to 576
 constexpr uint32_t kChunkMin = 16384;
@@ -280,7 +283,7 @@ __device__ void warp_copy(uint8_t *dst, const uint8_t *src, uint64_t n, int lane
 // wants.  Every mbarrier wait is bounded; when one runs out the copy waits (bounded) for its other
 // loads, reports failure and the kernel exits with kErrBulkCopyTimeout.
 #ifndef UGDR_TMA_STAGES
-#define UGDR_TMA_STAGES 2  // 0 builds the executor without the bulk-copy path (no dynamic smem)
+#define UGDR_TMA_STAGES 4  // 0 builds the executor without the bulk-copy path (no dynamic smem)
 #endif
 constexpr uint32_t kTmaStages = UGDR_TMA_STAGES > 0 ? UGDR_TMA_STAGES : 1;
 constexpr bool kTmaBuilt = UGDR_TMA_STAGES > 0;
@@ -556,7 +559,7 @@ struct QpView {
     const uint8_t *sq_slots;
     DevQp *peer;
     DevCq *send_cq;
-    uint32_t sq_cap, sq_stride, qpn, state, pd, max_sge, sig_all, lost, err, retry_word;
+    uint32_t sq_cap, sq_stride, qpn, state, pd, max_sge, sig_all, lost, err, err_issued, retry_word;
     // Responder configuration as of the last refresh (at most 20 us old).
     uint32_t pstate, perr, pactive, pacc, ppd;
 };
@@ -1711,6 +1714,7 @@ __device__ uint32_t service_pass(Warp &w, DevQp *qp, uint8_t *wqe_smem, queue::C
     v.sig_all = ld_vol32(&qp->cfg.sq_sig_all);
     v.lost = ld_vol32(&qp->cfg.peer_lost);
     v.err = ld_vol32(&qp->st.err);
+    v.err_issued = ld_vol32(&qp->st.err_issued);
     v.retry_word = ld_vol32(&qp->cfg.timeout);  // timeout, retry_cnt, rnr_retry, min_rnr_timer
     v.pstate = v.perr = v.pactive = v.pacc = v.ppd = 0;
     if (v.peer != nullptr) {
@@ -1729,6 +1733,17 @@ __device__ uint32_t service_pass(Warp &w, DevQp *qp, uint8_t *wqe_smem, queue::C
     __syncwarp();
     w.vt = now0;
     return service_cached(w, qp, *w.vv, wqe_smem, cqe_smem, jr, bitmap, nwarps);
+}
+
+// An error WR was issued: later passes issue nothing on this QP until it retires and the QP
+// enters ERR (whose flush then completes every WR behind it).
+__device__ void mark_err_issued(Warp &w, DevQp *qp, QpView &v) {
+    __syncwarp();
+    if (w.lane == 0) {
+        *reinterpret_cast<volatile uint32_t *>(&qp->st.err_issued) = 1u;
+        v.err_issued = 1;
+    }
+    __syncwarp();
 }
 
 __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_smem, queue::Cqe *cqe_smem,
@@ -1799,7 +1814,7 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
         w.vissue = ld_vol(&qp->st.sq_issue);
         return work + (flushed > 0 ? flushed : 0);
     }
-    if (v.state != UGDR_QPS_RTS) return work;
+    if (v.state != UGDR_QPS_RTS || v.err_issued) return work;  // an error WR in flight: wait for its retire
 
     // Issue: one lane-parallel fetch of every WQE that fits the window and the staging buffer.
     // The SQ tail (a PCIe read) is read only when the window has room and the tail seen last
@@ -1870,6 +1885,7 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
         w.started = true;
     }
     const uint32_t fast_err = __ballot_sync(0xffffffffu, uint32_t(w.lane) < fast_n && lw.status != 0);
+    if (fast_err) mark_err_issued(w, qp, v);
     // Staged WRs that need chunk copies share ONE job: the first takes the slot, each adds its
     // chunks (lane i holds WR i's first chunk index), staged inline WRs after it join with zero
     // chunks so the job's WRs stay consecutive in the window, and the job is published once,
@@ -1989,7 +2005,10 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
         if (w.lane == 0) w.ctr->n_slow += 1;
         if (w.lane == 0) w.ctr->t_slow += gtime() - t_stage;
         ++issued;
-        if (status != UGDR_WC_SUCCESS) break;  // stop issuing behind an error
+        if (status != UGDR_WC_SUCCESS) {  // stop issuing behind an error
+            mark_err_issued(w, qp, v);
+            break;
+        }
     }
     if (bslot >= 0) {
         if (bchunks > 0) {
@@ -2047,7 +2066,7 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
 
 // Warp 0 of every CTA is its leader: it services its own QPs and, about every microsecond,
 // mirrors the global control words (job bitmap, QP-slot bound, exit / stop / drain state) into
-// shared memory.  Warps 1..15 service their QPs and copy chunks, reading only the mirror when
+// shared memory.  The other warps service their QPs and copy chunks, reading only the mirror when
 // idle.  Without the mirror every warp of the grid polled the same few L2 lines and every
 // data access hashing to those slices queued behind the polls.
 __global__ void __launch_bounds__(kThreads, 1) executor_kernel(ExecParams p) {
