@@ -51,6 +51,53 @@ int enable_all_peer_access(int n) {
     return failures;
 }
 
+namespace {
+std::mutex g_backend_mu;
+DaemonMemoryBackend *g_backend = nullptr;  // the daemon's one backend (reap_ipc_closes)
+}  // namespace
+
+DaemonMemoryBackend::DaemonMemoryBackend(GpuInventory inv) : inv_(std::move(inv)) {
+    std::lock_guard<std::mutex> lk(g_backend_mu);
+    g_backend = this;
+}
+
+DaemonMemoryBackend::~DaemonMemoryBackend() {
+    {
+        std::lock_guard<std::mutex> lk(g_backend_mu);
+        if (g_backend == this) g_backend = nullptr;
+    }
+    for (int d = 0; d < inv_.count; ++d) reap(d);
+}
+
+void reap_ipc_closes(int device) noexcept {
+    std::lock_guard<std::mutex> lk(g_backend_mu);
+    if (g_backend != nullptr) g_backend->reap(device);
+}
+
+void DaemonMemoryBackend::reap(int device) noexcept {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (device < 0 || device >= inv_.count) return;
+    int prev = -1;
+    for (auto it = open_.begin(); it != open_.end();) {
+        Mapping &m = it->second;
+        if (m.refs == 0 && m.bases[size_t(device)] != nullptr) {
+            if (prev < 0) cudaGetDevice(&prev);
+            cudaSetDevice(device);
+            cudaIpcCloseMemHandle(m.bases[size_t(device)]);
+            m.bases[size_t(device)] = nullptr;
+            m.closed[size_t(device)] = 1;
+        }
+        bool any = false;
+        for (void *b : m.bases) any |= b != nullptr;
+        if (m.refs == 0 && !any)
+            it = open_.erase(it);
+        else
+            ++it;
+    }
+    if (prev >= 0) cudaSetDevice(prev);
+    (void)cudaGetLastError();
+}
+
 int DaemonMemoryBackend::open(control::MemoryDescriptor &desc, uint64_t length,
                               control::OpenedMemory *out) {
     if (desc.kind == control::MemKind::multicast) {
@@ -108,6 +155,7 @@ int DaemonMemoryBackend::open(control::MemoryDescriptor &desc, uint64_t length,
         Mapping m;
         m.gpu = gpu;
         m.bases.assign(size_t(inv_.count), nullptr);
+        m.closed.assign(size_t(inv_.count), 0);
         bool ok = true;
         for (int d = 0; d < inv_.count && ok; ++d) {
             cudaSetDevice(d);
@@ -128,6 +176,26 @@ int DaemonMemoryBackend::open(control::MemoryDescriptor &desc, uint64_t length,
         }
         cudaSetDevice(prev);
         it = open_.emplace(desc.ipc_handle, std::move(m)).first;
+    } else if (it->second.refs == 0) {
+        // Unused and partly reaped: map it again on the GPUs that already closed it.
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, desc.ipc_handle.data(), sizeof(h));
+        int prev = 0;
+        cudaGetDevice(&prev);
+        for (int d = 0; d < inv_.count; ++d) {
+            if (!it->second.closed[size_t(d)]) continue;
+            cudaSetDevice(d);
+            if (cudaIpcOpenMemHandle(&it->second.bases[size_t(d)], h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                (void)cudaGetLastError();
+                it->second.bases[size_t(d)] = nullptr;
+                if (d == gpu) {
+                    cudaSetDevice(prev);
+                    return EACCES;
+                }
+            }
+            it->second.closed[size_t(d)] = 0;
+        }
+        cudaSetDevice(prev);
     }
     it->second.refs += 1;
     out->gpu = gpu;
@@ -163,17 +231,7 @@ void DaemonMemoryBackend::close(control::OpenedMemory &mem) noexcept {
     std::lock_guard<std::mutex> lk(mu_);
     for (auto it = open_.begin(); it != open_.end(); ++it) {
         if (it->second.bases != mem.bases) continue;
-        if (--it->second.refs == 0) {
-            int prev = 0;
-            cudaGetDevice(&prev);
-            for (size_t d = 0; d < it->second.bases.size(); ++d) {
-                if (it->second.bases[d] == nullptr) continue;
-                cudaSetDevice(int(d));
-                cudaIpcCloseMemHandle(it->second.bases[d]);
-            }
-            cudaSetDevice(prev);
-            open_.erase(it);
-        }
+        it->second.refs -= 1;  // at 0 the mappings close in reap(), while no executor runs
         break;
     }
     mem.address = nullptr;

@@ -30,18 +30,30 @@ GpuInventory probe_gpus(int limit);
 // pairs that could not be enabled.
 int enable_all_peer_access(int n);
 
+// Close the IPC mappings on GPU `device` whose last MR went away.  cudaIpcCloseMemHandle waits
+// for the kernels running in that GPU's context, and the executor is persistent, so closing at
+// deregistration would stall the caller until the executor's idle exit.  Deregistration only
+// marks the mapping unused (the MR entry is already invalid and no WR can reach it); each GPU's
+// engine calls this while its executor is not running.  A handle registered again before then
+// reuses its open mapping.
+void reap_ipc_closes(int device) noexcept;
+
 class DaemonMemoryBackend : public control::MemoryBackend {
   public:
-    explicit DaemonMemoryBackend(GpuInventory inv) : inv_(std::move(inv)) {}
+    explicit DaemonMemoryBackend(GpuInventory inv);
+    ~DaemonMemoryBackend() override;
     int open(control::MemoryDescriptor &desc, uint64_t length, control::OpenedMemory *out) override;
     void close(control::OpenedMemory &mem) noexcept override;
 
   private:
     struct Mapping {
         std::vector<void *> bases;  // one mapping per daemon GPU (index = CUDA ordinal)
+        std::vector<uint8_t> closed;  // per GPU: unused and already closed by reap()
         int gpu = -1;               // owner
-        int refs = 0;
+        int refs = 0;               // 0: unused, waiting for reap() on every GPU
     };
+    friend void reap_ipc_closes(int device) noexcept;
+    void reap(int device) noexcept;
     GpuInventory inv_;
     std::mutex mu_;
     std::map<std::vector<uint8_t>, Mapping> open_;  // handle bytes -> mapping

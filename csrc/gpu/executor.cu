@@ -44,7 +44,22 @@ namespace {
 #endif
 constexpr int kWarps = UGDR_EXEC_WARPS;
 constexpr int kThreads = kWarps * 32;
-constexpr uint32_t kWqeStage = 1024;  // per-warp WQE staging: 16 WQEs of 64 B, or one wide one of up to 576
+#ifndef UGDR_WQE_STAGE
+#define UGDR_WQE_STAGE 2048
+#endif
+constexpr uint32_t kWqeStage = UGDR_WQE_STAGE;  // per-warp WQE staging: kWqeStage / 64 WQEs, or one wide one
+#ifndef UGDR_LEADER_OWNS_LAST
+#define UGDR_LEADER_OWNS_LAST 1
+#endif
+// Owner rank of warp `wi` among its CTA's warps: QP q belongs to CTA q % grid and to the warp of
+// rank (q / grid) % kWarps.  With UGDR_LEADER_OWNS_LAST the leader (warp 0, which also mirrors
+// the control words) takes the last rank, so it owns a QP only when every other warp has one.
+// Number of consecutive set bits from bit 0: 0..32 (`__ffs(~m) - 1` alone wraps when m is all ones).
+__device__ __forceinline__ uint32_t ones_prefix(uint32_t m) { return m == 0xffffffffu ? 32u : uint32_t(__ffs(~m) - 1); }
+
+__device__ __forceinline__ uint32_t owner_rank(uint32_t wi) {
+    return UGDR_LEADER_OWNS_LAST ? (wi + kWarps - 1) % kWarps : wi;
+}
 constexpr uint32_t kChunkMin = 16384;
 constexpr uint32_t kChunkMax = 262144;
 
@@ -1406,7 +1421,7 @@ __device__ int retire(Warp &w, DevQp *qp, const QpView &v, queue::Cqe *cqe_buf) 
         total = ld_vol(&rec->total);
     }
     const uint32_t ready_mask = __ballot_sync(0xffffffffu, mine && (n == 0 || done >= n));
-    uint32_t p = __ffs(~ready_mask) - 1;  // ready prefix length
+    uint32_t p = ones_prefix(ready_mask);  // ready prefix length
     if (p == 0) return 0;
     const uint32_t err_mask = __ballot_sync(0xffffffffu, uint32_t(w.lane) < p && status != UGDR_WC_SUCCESS);
     if (err_mask) p = __ffs(err_mask);  // retire up to and including the first error
@@ -1484,7 +1499,7 @@ __device__ uint32_t issue_fast(Warp &w, DevQp *qp, const QpView &v, const uint8_
     const bool fast = in && (op == UGDR_WR_RDMA_WRITE || op == UGDR_WR_RDMA_READ) && h->sge_count == 1 &&
                       sg->length <= 0x80000000u && v.max_sge >= 1;
     const uint32_t fast_mask = __ballot_sync(0xffffffffu, fast);
-    const uint32_t p = __ffs(~fast_mask) - 1;
+    const uint32_t p = ones_prefix(fast_mask);
     if (p == 0) return 0;
     const bool act = j < p;
     const uint64_t len = act ? sg->length : 0;
@@ -1850,7 +1865,7 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
         const bool in = uint32_t(w.lane) < avail;
         const uint32_t nsge = in ? reinterpret_cast<const queue::SendWqe *>(wqe_smem + w.lane * 64)->sge_count : 0;
         const uint32_t narrow = __ballot_sync(0xffffffffu, in && nsge <= 1);
-        const uint32_t p = __ffs(~narrow) - 1;  // WQEs before the first wide one
+        const uint32_t p = ones_prefix(narrow);  // WQEs before the first wide one
         __syncwarp();
         if (p > 0) {
             avail = p;
@@ -2138,9 +2153,10 @@ __global__ void __launch_bounds__(kThreads, 1) executor_kernel(ExecParams p) {
         uint32_t work = 0;
         // Owned QPs: q = cta + grid * (wi + warps * k).
         const uint32_t slots = s_slots;
-        const bool owner = blockIdx.x + gridDim.x * w.wi < slots;
+        const uint32_t orank = owner_rank(w.wi);
+        const bool owner = blockIdx.x + gridDim.x * orank < slots;
         bool in_flight = false;  // an owned QP waits for WRs to finish: come back to it soon
-        for (uint32_t q = blockIdx.x + gridDim.x * w.wi; q < slots; q += gridDim.x * kWarps) {
+        for (uint32_t q = blockIdx.x + gridDim.x * orank; q < slots; q += gridDim.x * kWarps) {
             work += service_qp(w, &p.qps[q], wqe_buf[w.wi], cqe_buf[w.wi], jr, bits, nwarps);
             if (w.abort) {
                 s_exit = 1;

@@ -1,4 +1,5 @@
 #include "gpu/gpu_engine.hpp"
+#include "gpu/cuda_memory.hpp"
 
 #include "control/service.hpp"
 #include "gpu/device_abi.hpp"
@@ -103,6 +104,12 @@ class GpuEngine final : public control::Engine {
     DevMr *mrs_ = nullptr;
     DevQp *qps_ = nullptr;
     QpProgress *progress_ = nullptr;  // per QP slot, written by the owner warps
+    // Pinned staging for the control copies.  A copy between device memory and pageable host
+    // memory can wait for the running executor to exit (measured: a 16 B device-to-host read
+    // took until the 200 ms idle exit), so every control copy goes through this buffer.
+    static constexpr size_t kStageBytes = 128 << 10;
+    uint8_t *stage_ = nullptr;
+    std::mutex stage_mu_;
     uint32_t mr_epoch_ = 0;           // last value stored in DevStats::mr_epoch
     uint64_t mr_fast_detaches_ = 0, mr_slow_detaches_ = 0;
     DevCq *cqs_ = nullptr;
@@ -151,6 +158,7 @@ GpuEngine::~GpuEngine() {
     cudaFree(trace_);
     cudaFree(trace_count_);
     if (ctrl_) cudaFreeHost(ctrl_);
+    if (stage_) cudaFreeHost(stage_);
 }
 
 int GpuEngine::init() {
@@ -166,6 +174,7 @@ int GpuEngine::init() {
         !ok(cudaMalloc(reinterpret_cast<void **>(&jobs_), job_ring_bytes())) ||
         !ok(cudaMalloc(reinterpret_cast<void **>(&stats_), sizeof(DevStats))) ||
         !ok(cudaHostAlloc(reinterpret_cast<void **>(&ctrl_), sizeof(HostCtrl), cudaHostAllocMapped | cudaHostAllocPortable)) ||
+        !ok(cudaHostAlloc(reinterpret_cast<void **>(&stage_), kStageBytes, cudaHostAllocPortable)) ||
         !ok(cudaHostGetDevicePointer(reinterpret_cast<void **>(&ctrl_dev_), ctrl_, 0))) {
         (void)cudaGetLastError();
         return ENODEV;
@@ -187,20 +196,32 @@ int GpuEngine::init() {
 
 int GpuEngine::copy_to_device(void *dst, const void *src, size_t n) {
     set_device();
-    if (cudaMemcpyAsync(dst, src, n, cudaMemcpyHostToDevice, ctl_stream_) != cudaSuccess ||
-        cudaStreamSynchronize(ctl_stream_) != cudaSuccess) {
-        (void)cudaGetLastError();
-        return EIO;
+    std::lock_guard<std::mutex> lk(stage_mu_);
+    for (size_t o = 0; o < n; o += kStageBytes) {
+        const size_t k = n - o < kStageBytes ? n - o : kStageBytes;
+        std::memcpy(stage_, static_cast<const uint8_t *>(src) + o, k);
+        if (cudaMemcpyAsync(static_cast<uint8_t *>(dst) + o, stage_, k, cudaMemcpyHostToDevice, ctl_stream_) !=
+                cudaSuccess ||
+            cudaStreamSynchronize(ctl_stream_) != cudaSuccess) {
+            (void)cudaGetLastError();
+            return EIO;
+        }
     }
     return 0;
 }
 
 int GpuEngine::copy_from_device(void *dst, const void *src, size_t n) {
     set_device();
-    if (cudaMemcpyAsync(dst, src, n, cudaMemcpyDeviceToHost, ctl_stream_) != cudaSuccess ||
-        cudaStreamSynchronize(ctl_stream_) != cudaSuccess) {
-        (void)cudaGetLastError();
-        return EIO;
+    std::lock_guard<std::mutex> lk(stage_mu_);
+    for (size_t o = 0; o < n; o += kStageBytes) {
+        const size_t k = n - o < kStageBytes ? n - o : kStageBytes;
+        if (cudaMemcpyAsync(stage_, static_cast<const uint8_t *>(src) + o, k, cudaMemcpyDeviceToHost, ctl_stream_) !=
+                cudaSuccess ||
+            cudaStreamSynchronize(ctl_stream_) != cudaSuccess) {
+            (void)cudaGetLastError();
+            return EIO;
+        }
+        std::memcpy(static_cast<uint8_t *>(dst) + o, stage_, k);
     }
     return 0;
 }
@@ -578,6 +599,7 @@ void GpuEngine::monitor() {
         {
             std::lock_guard<std::mutex> lk(mu_);
             kernel_done_locked();
+            if (!running_) reap_ipc_closes(cfg_.ordinal);  // unused IPC mappings close only now
             if (!running_ && !held_ && paused_ == 0 && has_work_locked()) {
                 launch_locked(kPersistent, 0, false);
                 idle = false;
