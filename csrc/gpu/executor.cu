@@ -1836,8 +1836,9 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
     // does not already cover it: WQEs below a tail acquired earlier are as valid now.
     // On a queue whose slots are wider than 64 B (max_send_sge > 1) only each slot's first 64 B
     // are fetched at first: a WQE of at most one SGE (atomics included) lies wholly inside them,
-    // so up to 16 such WQEs are staged per pass, as on a one-SGE queue.  The batch ends before
-    // the first wider WQE; when that is the first one, it alone is fetched in full.
+    // so up to kWqeStage / 64 such WQEs are staged per pass, as on a one-SGE queue.  The batch
+    // ends before the first wider WQE; when that is the first one, the pass fetches as many
+    // whole slots as the staging buffer holds.
     const uint64_t head = w.vhead, issue0 = w.vissue;
     const uint32_t wide = v.sq_stride > 64 ? 1u : 0u;
     uint32_t st = wide ? 64u : v.sq_stride;  // stage stride: bytes per staged WQE
@@ -1869,12 +1870,15 @@ __device__ uint32_t service_cached(Warp &w, DevQp *qp, QpView &v, uint8_t *wqe_s
         __syncwarp();
         if (p > 0) {
             avail = p;
-        } else {  // the first WQE is wide: it alone, in full
-            avail = 1;
+        } else {  // the first WQE is wide: as many as fit, in full
+            const uint64_t fit = kWqeStage / v.sq_stride;
+            avail = avail < fit ? avail : fit;
             st = v.sq_stride;
-            const uint8_t *src = v.sq_slots + (issue0 % v.sq_cap) * v.sq_stride;
-            for (uint32_t o = w.lane * 16; o < st; o += 32 * 16)
-                *reinterpret_cast<uint4 *>(wqe_smem + o) = ld_vol128(src + o);
+            const uint32_t nb = uint32_t(avail) * st;
+            for (uint32_t o = w.lane * 16; o < nb; o += 32 * 16) {
+                const uint64_t s = issue0 + o / st;
+                *reinterpret_cast<uint4 *>(wqe_smem + o) = ld_vol128(v.sq_slots + (s % v.sq_cap) * st + (o % st));
+            }
             __syncwarp();
         }
     }
