@@ -20,7 +20,8 @@ namespace ugdr::gpu {
 constexpr uint32_t kMaxMrs = 1u << 16;       // key slots (matches the control plane's keys)
 constexpr uint32_t kMaxQpsPerEngine = 4096;
 constexpr uint32_t kMaxCqsPerEngine = 4096;
-constexpr uint32_t kWindow = 32;             // in-flight WRs per QP (one per lane of the owner warp)
+constexpr uint32_t kBatch = 32;              // WRs one owner pass issues or retires (one per lane)
+constexpr uint32_t kWindow = 64;             // in-flight WRs per QP: two batches
 constexpr uint32_t kMaxSge = 32;
 constexpr uint32_t kJobSlots = 1024;         // chunked-job slots per engine
 constexpr uint32_t kInlineBytes = 4096;      // WRs up to this size are copied by the owner warp
@@ -159,7 +160,7 @@ struct alignas(64) Job {
     uint32_t done;
     uint32_t pad0;
     uint32_t pad1[4];
-    uint32_t start[kWindow];
+    uint32_t start[kBatch];
 };
 
 struct JobRing {

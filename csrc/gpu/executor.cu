@@ -883,24 +883,28 @@ __device__ __forceinline__ void span_box(const Span &s, uint64_t *lo, uint64_t *
 // Warp-wide: true on the lanes whose span clashes with a WR of `qp` in [head, issue) (issued,
 // not yet retired; such a WR may still be copying).  Lane k loads WR head + k's record.
 __device__ bool clashes_in_flight(const Warp &w, DevQp *qp, uint64_t head, uint64_t issue, const Span &mine) {
-    const uint32_t m = uint32_t(issue - head);
-    if (m == 0 || __all_sync(0xffffffffu, mine.w == 0)) return false;
-    Span f{0, 0, 0, 0, 0};
-    if (uint32_t(w.lane) < m) {
-        const WrRec *r = &qp->st.win[(head + w.lane) % kWindow];
-        if (ld_vol32(&r->status) == UGDR_WC_SUCCESS)
-            f = span_of(ld_vol32(&r->opcode), ld_vol(&r->remote), ld_vol(&r->total), ld_vol(&r->lo), ld_vol(&r->hi),
-                        true);
-    }
-    // Cheap filter: nothing in flight reaches the addresses this warp's spans touch.
-    uint64_t blo, bhi;
-    span_box(f, &blo, &bhi);
-    const bool near = mine.w != 0 && (overlap(mine.rl, mine.rh, blo, bhi) || overlap(mine.ll, mine.lh, blo, bhi));
-    if (!__any_sync(0xffffffffu, near)) return false;
+    const uint32_t all = uint32_t(issue - head);
+    if (all == 0 || __all_sync(0xffffffffu, mine.w == 0)) return false;
     bool hit = false;
-    for (uint32_t k = 0; k < m; ++k) {
-        const Span s = shfl_span(f, int(k));
-        hit |= mine.w != 0 && clash(s, mine);
+    for (uint32_t base = 0; base < all; base += 32) {  // in-flight WRs, 32 at a time (lane k: WR base + k)
+        const uint32_t m = all - base < 32 ? all - base : 32u;
+        Span f{0, 0, 0, 0, 0};
+        if (uint32_t(w.lane) < m) {
+            const WrRec *r = &qp->st.win[(head + base + w.lane) % kWindow];
+            if (ld_vol32(&r->status) == UGDR_WC_SUCCESS)
+                f = span_of(ld_vol32(&r->opcode), ld_vol(&r->remote), ld_vol(&r->total), ld_vol(&r->lo),
+                            ld_vol(&r->hi), true);
+        }
+        // Cheap filter: nothing of these reaches the addresses this warp's spans touch.
+        uint64_t blo, bhi;
+        span_box(f, &blo, &bhi);
+        const bool near =
+            mine.w != 0 && (overlap(mine.rl, mine.rh, blo, bhi) || overlap(mine.ll, mine.lh, blo, bhi));
+        if (!__any_sync(0xffffffffu, near)) continue;
+        for (uint32_t k = 0; k < m; ++k) {
+            const Span s = shfl_span(f, int(k));
+            hit |= mine.w != 0 && clash(s, mine);
+        }
     }
     return hit;
 }
@@ -1404,7 +1408,8 @@ __device__ int retire_commit(Warp &w, DevQp *qp, const QpView &v, queue::Cqe *cq
 __device__ int retire(Warp &w, DevQp *qp, const QpView &v, queue::Cqe *cqe_buf) {
     const uint64_t max_ns = w.p->max_wait_ns;
     const uint64_t head = ld_vol(&qp->st.sq_head), issue = ld_vol(&qp->st.sq_issue);
-    const uint32_t m = uint32_t(issue - head);  // <= kWindow <= 32
+    // The oldest batch's worth at most; a later pass retires the rest.
+    const uint32_t m = issue - head < kBatch ? uint32_t(issue - head) : kBatch;
     if (m == 0) return 0;
     const bool mine = uint32_t(w.lane) < m;
     WrRec *rec = &qp->st.win[(head + (mine ? w.lane : 0)) % kWindow];
@@ -2093,7 +2098,7 @@ __global__ void __launch_bounds__(kThreads, 1) executor_kernel(ExecParams p) {
     __shared__ __align__(8) uint64_t tma_bar[kWarps][kTmaStages];
     __shared__ Tma tma_state[kWarps];
     __shared__ __align__(16) uint8_t wqe_buf[kWarps][kWqeStage];
-    __shared__ __align__(16) queue::Cqe cqe_buf[kWarps][kWindow];
+    __shared__ __align__(16) queue::Cqe cqe_buf[kWarps][kBatch];
     __shared__ __align__(16) MrCacheEntry mr_cache[kWarps][2];
     __shared__ WarpCounters counters[kWarps];
     __shared__ CqCache cq_cache[kWarps];

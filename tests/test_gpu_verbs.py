@@ -324,8 +324,13 @@ def test_mr_deregistration_keeps_the_executor_running(gpu_env):
     keeps streaming: the executor is not stopped (no extra launch), the stream's bytes are right,
     and the engine counts the deregistrations as live ones."""
     V = gpu_env
+    import gc
+
     from ugdr_b200 import _native as N
 
+    # Objects of earlier tests on this daemon are released now, not mid-test: destroying a QP or
+    # a CQ still stops the executor, which would show up as a relaunch below.
+    gc.collect()
     ctx, pd, cq, a, b = _setup(V, N, depth=512)
     n = 64 << 20
     src = torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda")
