@@ -176,6 +176,10 @@ class Engine {
     virtual void quiesce() = 0;
     // Allow execution again after quiesce().
     virtual void resume() = 0;
+    // True when this engine's detach_qp / detach_cq / update_qp are safe while it runs, for
+    // objects that only this engine's own execution may still touch (it keeps their memory
+    // until it is not running).  The control plane then stops it only for peers on other engines.
+    virtual bool detaches_live() const noexcept { return false; }
 
     virtual int stats(EngineStats *out, bool reset) = 0;
     // Device trace: keep up to `records_per_unit` events per execution unit from the next launch

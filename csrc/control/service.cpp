@@ -430,11 +430,15 @@ void ControlPlane::erase_qp(uint64_t id) noexcept {
     // engines may be on other GPUs and may be executing a WRITE_WITH_IMM into this QP's receive
     // ring at this moment, so each is stopped before the binding changes and stays stopped until
     // this QP's rings are gone from its own engine.
+    // An engine that detaches live keeps the QP's memory until it is not running, which covers
+    // its own requesters; requesters on other engines are stopped as before.
     std::vector<Engine *> held;
+    Engine *own = engines_[qp->device];
     qps_.for_each([&](uint64_t, uint64_t, Qp &other) {
         if (other.peer != qp) return;
         Engine *e = engines_[other.device];
-        if (std::find(held.begin(), held.end(), e) == held.end()) {
+        const bool live = e == own && e->detaches_live();
+        if (!live && std::find(held.begin(), held.end(), e) == held.end()) {
             e->quiesce();
             held.push_back(e);
         }

@@ -64,6 +64,7 @@ class GpuEngine final : public control::Engine {
     void update_qp(control::Qp &qp) override;
     void detach_qp(control::Qp &qp) noexcept override;
     void quiesce() override;
+    bool detaches_live() const noexcept override { return true; }
     void resume() override;
     int stats(control::EngineStats *out, bool reset) override;
     int qp_counters(control::Qp &qp, control::QpCounters *out) override;
@@ -131,6 +132,16 @@ class GpuEngine final : public control::Engine {
     unsigned int *trace_count_ = nullptr;
     uint32_t trace_cap_ = 0;
     std::vector<queue::Ring> graveyard_;  // rings of objects destroyed while wedged (kept mapped)
+    // Destroyed while the executor ran: a warp's cached view may still reach the rings, the CQ
+    // `ready` arrays and the slots, so they are released (and the slots reused) only while no
+    // executor runs and no chunk job is pending (reap_locked).  cudaHostUnregister and cudaFree
+    // would also wait for the persistent kernel.
+    std::vector<queue::Ring> deferred_rings_;
+    std::vector<unsigned long long *> deferred_ready_;
+    std::vector<uint32_t> cooling_qp_slots_, cooling_cq_slots_;
+    void reap_locked();
+    // All slots in use and some cooling: stop the executor once so that they can be reused.
+    void reclaim_slots(bool qp);
     uint64_t launches_ = 0;
     std::atomic<bool> stop_monitor_{false};
     std::thread monitor_;
@@ -144,6 +155,11 @@ GpuEngine::~GpuEngine() {
     std::lock_guard<std::mutex> lk(mu_);
     set_device();
     stop_kernel_locked(5000);
+    for (queue::Ring &r : deferred_rings_) cudaHostUnregister(r.mapping());
+    deferred_rings_.clear();
+    for (unsigned long long *p : deferred_ready_)
+        if (p) cudaFree(p);
+    deferred_ready_.clear();
     if (exec_stream_) cudaStreamDestroy(exec_stream_);
     if (ctl_stream_) cudaStreamDestroy(ctl_stream_);
     if (ev_start_) cudaEventDestroy(ev_start_);
@@ -274,7 +290,24 @@ void GpuEngine::detach_mr(control::Mr &mr) noexcept {
 
 // ---- CQs --------------------------------------------------------------------------------------
 
+void GpuEngine::reclaim_slots(bool qp) {
+    {
+        std::lock_guard<std::mutex> lk(mu_);
+        const bool full = qp ? free_qp_slots_.empty() && next_qp_slot_ >= kMaxQpsPerEngine
+                             : free_cq_slots_.empty() && next_cq_slot_ >= kMaxCqsPerEngine;
+        const bool cooling = qp ? !cooling_qp_slots_.empty() : !cooling_cq_slots_.empty();
+        if (!full || !cooling) return;
+    }
+    quiesce();
+    {
+        std::lock_guard<std::mutex> lk(mu_);
+        reap_locked();
+    }
+    resume();
+}
+
 int GpuEngine::attach_cq(control::Cq &cq) {
+    reclaim_slots(false);
     std::lock_guard<std::mutex> lk(mu_);
     uint32_t slot;
     if (!free_cq_slots_.empty()) {
@@ -320,25 +353,21 @@ int GpuEngine::attach_cq(control::Cq &cq) {
 
 void GpuEngine::detach_cq(control::Cq &cq) noexcept {
     if (cq.engine_block == nullptr) return;
-    quiesce();
-    {
-        std::lock_guard<std::mutex> lk(mu_);
-        DevCq *d = static_cast<DevCq *>(cq.engine_block);
-        DevCq zero{};
-        copy_to_device(d, &zero, sizeof(zero));
-        set_device();
-        const uint32_t slot = uint32_t(d - cqs_);
-        if (!wedged_) {
-            cudaHostUnregister(cq.ring.mapping());
-            cudaFree(cq_ready_[slot]);
-            cq_ready_[slot] = nullptr;
-            free_cq_slots_.push_back(slot);
-        } else {
-            graveyard_.push_back(std::move(cq.ring));
-        }
-        cq.engine_block = nullptr;
+    // No QP uses the CQ any more (the control plane refuses otherwise), but a warp that retired a
+    // destroyed QP's WRs a moment ago may still hold it in its CQ cache: its device entry stays as
+    // it is, and the ring, the `ready` array and the slot go only in reap_locked().
+    std::lock_guard<std::mutex> lk(mu_);
+    DevCq *d = static_cast<DevCq *>(cq.engine_block);
+    const uint32_t slot = uint32_t(d - cqs_);
+    if (!wedged_) {
+        deferred_rings_.push_back(std::move(cq.ring));
+        deferred_ready_.push_back(cq_ready_[slot]);
+        cq_ready_[slot] = nullptr;
+        cooling_cq_slots_.push_back(slot);
+    } else {
+        graveyard_.push_back(std::move(cq.ring));
     }
-    resume();
+    cq.engine_block = nullptr;
 }
 
 // ---- QPs --------------------------------------------------------------------------------------
@@ -374,6 +403,7 @@ void GpuEngine::fill_qp_config(control::Qp &qp, DevQpConfig *c) {
 }
 
 int GpuEngine::attach_qp(control::Qp &qp) {
+    reclaim_slots(true);
     std::lock_guard<std::mutex> lk(mu_);
     uint32_t slot;
     if (!free_qp_slots_.empty()) {
@@ -439,30 +469,46 @@ void GpuEngine::update_qp(control::Qp &qp) {
 
 void GpuEngine::detach_qp(control::Qp &qp) noexcept {
     if (qp.engine_block == nullptr) return;
-    quiesce();
-    {
-        std::lock_guard<std::mutex> lk(mu_);
-        DevQp *d = static_cast<DevQp *>(qp.engine_block);
-        const uint32_t zero = 0;
-        copy_to_device(&d->cfg.active, &zero, sizeof(zero));
-        set_device();
-        for (size_t i = 0; i < qps_host_.size(); ++i) {
-            if (qps_host_[i].qp != &qp) continue;
-            if (!wedged_) {
-                cudaHostUnregister(qp.sq.mapping());
-                cudaHostUnregister(qp.rq.mapping());
-                free_qp_slots_.push_back(qps_host_[i].slot);
-            } else {
-                graveyard_.push_back(std::move(qp.sq));
-                graveyard_.push_back(std::move(qp.rq));
-            }
-            qps_host_[i] = qps_host_.back();
-            qps_host_.pop_back();
-            break;
+    // The owner warp stops servicing the slot at its next configuration refresh (within 20 us);
+    // until the executor is not running its cached view may still read the rings, so they and
+    // the slot are released only in reap_locked().  WRs still in flight are discarded.
+    std::lock_guard<std::mutex> lk(mu_);
+    DevQp *d = static_cast<DevQp *>(qp.engine_block);
+    const uint32_t zero = 0;
+    copy_to_device(&d->cfg.active, &zero, sizeof(zero));
+    for (size_t i = 0; i < qps_host_.size(); ++i) {
+        if (qps_host_[i].qp != &qp) continue;
+        if (!wedged_) {
+            deferred_rings_.push_back(std::move(qp.sq));
+            deferred_rings_.push_back(std::move(qp.rq));
+            cooling_qp_slots_.push_back(qps_host_[i].slot);
+        } else {
+            graveyard_.push_back(std::move(qp.sq));
+            graveyard_.push_back(std::move(qp.rq));
         }
-        qp.engine_block = nullptr;
+        qps_host_[i] = qps_host_.back();
+        qps_host_.pop_back();
+        break;
     }
-    resume();
+    qp.engine_block = nullptr;
+}
+
+void GpuEngine::reap_locked() {
+    if (running_ || (deferred_rings_.empty() && deferred_ready_.empty() && cooling_qp_slots_.empty() &&
+                     cooling_cq_slots_.empty()))
+        return;
+    if (copies_pending_locked()) return;  // a relaunch finishes them first
+    set_device();
+    for (queue::Ring &r : deferred_rings_) cudaHostUnregister(r.mapping());
+    (void)cudaGetLastError();
+    deferred_rings_.clear();  // unmaps
+    for (unsigned long long *p : deferred_ready_)
+        if (p) cudaFree(p);
+    deferred_ready_.clear();
+    free_qp_slots_.insert(free_qp_slots_.end(), cooling_qp_slots_.begin(), cooling_qp_slots_.end());
+    free_cq_slots_.insert(free_cq_slots_.end(), cooling_cq_slots_.begin(), cooling_cq_slots_.end());
+    cooling_qp_slots_.clear();
+    cooling_cq_slots_.clear();
 }
 
 // ---- kernel life cycle ------------------------------------------------------------------------
@@ -599,7 +645,10 @@ void GpuEngine::monitor() {
         {
             std::lock_guard<std::mutex> lk(mu_);
             kernel_done_locked();
-            if (!running_) reap_ipc_closes(cfg_.ordinal);  // unused IPC mappings close only now
+            if (!running_) {  // what destroyed objects left behind is released only now
+                reap_ipc_closes(cfg_.ordinal);
+                reap_locked();
+            }
             if (!running_ && !held_ && paused_ == 0 && has_work_locked()) {
                 launch_locked(kPersistent, 0, false);
                 idle = false;

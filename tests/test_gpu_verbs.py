@@ -371,6 +371,67 @@ def test_mr_deregistration_keeps_the_executor_running(gpu_env):
     ctx.close()
 
 
+def test_qp_and_cq_destruction_keeps_the_executor_running(gpu_env):
+    """QPs and CQs created, used and destroyed while another QP streams: the executor is never
+    stopped (no relaunch), every short-lived pair's WRs complete correctly, and the stream's bytes
+    are right.  The destroyed objects' rings and slots are released once the executor is idle."""
+    V = gpu_env
+    import gc
+
+    from ugdr_b200 import _native as N
+
+    gc.collect()
+    ctx, pd, cq, a, b = _setup(V, N, depth=512)
+    n = 64 << 20
+    src = torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda")
+    dst = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    small = torch.randint(0, 256, (1 << 16,), dtype=torch.uint8, device="cuda")
+    small_dst = torch.zeros_like(small)
+    torch.cuda.synchronize()
+    ms, md = pd.reg_mr(src.data_ptr(), n, _acc(N)), pd.reg_mr(dst.data_ptr(), n, _acc(N))
+    ss, sd = pd.reg_mr(small.data_ptr(), small.numel(), _acc(N)), pd.reg_mr(small_dst.data_ptr(), small.numel(), _acc(N))
+    a.post_write((src.data_ptr(), 4096, ms.lkey), dst.data_ptr(), md.rkey, wr_id=0)
+    assert cq.wait(1, 60)[0].status == N.WC_SUCCESS  # the executor is up
+    st0 = ctx.stats()
+    chunk = 1 << 20
+    posted = done = cycles = 0
+    while done < 256:
+        while posted < 256 and posted - done < 64:
+            off = (posted % 64) * chunk
+            a.post_write((src.data_ptr() + off, chunk, ms.lkey), dst.data_ptr() + off, md.rkey, wr_id=posted)
+            posted += 1
+        if cycles < 6:  # a short-lived pair with its own CQ comes and goes under the stream
+            cq2 = ctx.create_cq(64)
+            c = pd.create_qp(cq2, max_send_wr=16, max_recv_wr=16)
+            d = pd.create_qp(cq2, max_send_wr=16, max_recv_wr=16)
+            V.connect_pair(c, d, access=N.ACCESS_REMOTE_WRITE | N.ACCESS_REMOTE_READ)
+            k = 4096 * (cycles + 1)
+            c.post_write((small.data_ptr(), k, ss.lkey), small_dst.data_ptr(), sd.rkey, wr_id=1000 + cycles)
+            wc = cq2.wait(1, 60)[0]
+            assert (wc.wr_id, wc.status) == (1000 + cycles, N.WC_SUCCESS), wc
+            torch.cuda.synchronize()
+            assert torch.equal(small_dst[:k], small[:k])
+            c.destroy()
+            d.destroy()
+            cq2.destroy()
+            cycles += 1
+        wcs = cq.wait(1, 60)
+        assert all(w.status == N.WC_SUCCESS for w in wcs)
+        done += len(wcs)
+    st1 = ctx.stats()
+    torch.cuda.synchronize()
+    assert cycles == 6
+    assert torch.equal(dst, src)
+    assert st1.launches == st0.launches, (st0.launches, st1.launches)  # never stopped and relaunched
+    for q in (a, b):
+        q.destroy()
+    for m in (ms, md, ss, sd):
+        m.dereg()
+    cq.destroy()
+    pd.dealloc()
+    ctx.close()
+
+
 def test_kernel_attributes_report_every_kernel():
     """cudaFuncGetAttributes + occupancy for every kernel of the library: each fits its launch
     block size; the persistent executor keeps one 256-thread CTA (8 warps) per SM, whose register
