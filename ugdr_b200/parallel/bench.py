@@ -328,7 +328,7 @@ def bench_moe_verbs(rank, world, local, iters, warmup, cfg: MoEConfig) -> dict:
         dist.broadcast_object_list(lst, src=0, group=_GLOO)
         return lst[0]
 
-    daemon = VC.shared_daemon(rank, world, bcast)
+    daemon = VC.shared_daemon(rank, world, bcast, idle_exit_us=50)  # see VerbsMoE
     g = VC.moe_group(rank, world, local, T, K, E, exchange)
     moe = VC.VerbsMoE(g, T, H, K, E, recv_rows=int(T * K * 1.25) + 4096)
     try:
