@@ -175,8 +175,9 @@ def _moe_worker(rank: int, world: int, port: int, gpu: bool, shape: tuple, calls
         try:
             for call in range(calls):
                 x, ids, w = _moe_inputs(rank, T, H, K, E, call, dev)
-                # On the GPU the calls alternate the packed dispatch (the default) and the 32-SGE gathers.
-                moe.dispatch(x, ids, packed=(call % 2 == 0) if gpu else None)
+                # The calls alternate the packed dispatch (one WRITE per expert group) and the
+                # 32-SGE gathers, on the host engine and on the executors.
+                moe.dispatch(x, ids, packed=call % 2 == 0)
                 got = moe.recv_view().cpu()
                 want = _moe_expected_recv(rank, world, T, H, K, E, call)
                 assert got.shape == want.shape, (got.shape, want.shape)

@@ -301,11 +301,10 @@ class VerbsMoE:
         """Send every (token, k) row of x to its expert's owner.  On the GPU the default is the
         packed form: ugdr_x_moe_pack_grouped groups the rows by expert into `back` (each x row
         read once, straight from the caller's tensor) and every (owner, expert) group leaves as
-        one contiguous WRITE.  packed=False (and the host engine) gathers the rows with 32-SGE
-        WRITEs from the registered x instead."""
+        one contiguous WRITE.  packed=False gathers the rows with 32-SGE WRITEs from the
+        registered x instead (the default on the host engine, where packed=True groups the rows
+        with torch)."""
         packed = self.gpu if packed is None else packed
-        if packed and not self.gpu:
-            raise ValueError("the packed dispatch needs GPU memory")
         src = self.x
         if x is not None:
             if packed and x.is_contiguous() and x.dtype == torch.bfloat16 and x.shape == self.x.shape \
@@ -329,7 +328,9 @@ class VerbsMoE:
         c64 = counts.to(device=dev, dtype=torch.int64)
         self.start_d = torch.cumsum(c64, 0) - c64
         L = _moe_lib()
-        if packed:
+        if packed and not self.gpu:  # host engine: the same grouping with torch
+            self.back[self.start_d[self.ids_d.long()] + self.pos_d.long()] = src.repeat_interleave(self.topk, 0)
+        elif packed:
             rc = L.ugdr_x_moe_pack_grouped(self.back.data_ptr(), src.data_ptr(), self.ids_d.data_ptr(),
                                            self.pos_d.data_ptr(), self.start_d.data_ptr(), self.tokens, self.topk,
                                            self.row_bytes, 0, torch.cuda.current_stream().cuda_stream)
