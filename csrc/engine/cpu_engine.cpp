@@ -201,10 +201,27 @@ size_t CpuEngine::progress_qp(QpView &v) {
     }
     if (qp.state != UGDR_QPS_RTS) return 0;
 
-    for (uint32_t budget = 0; budget < 64; ++budget) {
-        queue::SlotRun run = qp.sq.peek(1);
-        if (run.count() == 0) break;
-        const uint8_t *slot = run.first;
+    // One batch per pass: the SQ slots are peeked together, send-CQ slots reserved together, and
+    // both cursors move once at the end (SQ head first, then the CQ tail), so the client's
+    // polled cache lines are written once per batch instead of once per WR.
+    const queue::SlotRun run = qp.sq.peek(64);
+    const uint32_t k = run.count();
+    if (k == 0) return 0;
+    const uint32_t sq_stride = qp.sq.geometry().stride;
+    queue::Ring &scq = qp.send_cq->ring;
+    const uint32_t cq_stride = scq.geometry().stride;
+    queue::SlotRun cq_run = scq.reserve(k);
+    uint32_t consumed = 0, ncqe = 0;
+    auto cq_slot = [&](uint32_t j) {
+        return j < cq_run.first_count ? cq_run.first + j * cq_stride : cq_run.second + (j - cq_run.first_count) * cq_stride;
+    };
+    auto finish = [&]() {  // SQ slots back before their completions become visible
+        qp.sq.release(consumed);
+        scq.publish(ncqe);
+        ncqe = 0;
+    };
+    for (uint32_t i = 0; i < k; ++i) {
+        const uint8_t *slot = i < run.first_count ? run.first + i * sq_stride : run.second + (i - run.first_count) * sq_stride;
         queue::SendWqe h;
         std::memcpy(&h, slot, sizeof(h));
         const uint32_t op = h.opcode;
@@ -301,12 +318,19 @@ size_t CpuEngine::progress_qp(QpView &v) {
                 queue::RecvWqe rh;
                 std::memcpy(&rh, rq.first, sizeof(rh));
                 recv_wr_id = rh.wr_id;
+                // The receive CQ may be this batch's send CQ: publish what the batch has so far
+                // (earlier WRs complete first), then check the responder's slot afresh.
+                if (ncqe > 0) {
+                    scq.publish(ncqe);
+                    ncqe = 0;
+                    cq_run = scq.reserve(k - i);
+                }
                 if (peer->recv_cq->ring.reserve(1).count() == 0) break;  // responder CQ full: wait
             }
         }
         // Requester CQ slot (signaled successes and every error).
         const bool need_cqe = signaled || status != UGDR_WC_SUCCESS;
-        if (need_cqe && qp.send_cq->ring.reserve(1).count() == 0) break;
+        if (need_cqe && ncqe >= cq_run.count()) break;
 
         if (status == UGDR_WC_SUCCESS) {
             if (op_sum(op)) {
@@ -356,6 +380,7 @@ size_t CpuEngine::progress_qp(QpView &v) {
                 queue::Cqe rc{recv_wr_id, UGDR_WC_SUCCESS, UGDR_WC_RECV_RDMA_WITH_IMM,
                               uint32_t(total), h.immediate_data, peer->qpn, UGDR_WC_WITH_IMM};
                 produce(peer->recv_cq, &rc);
+                if (peer->recv_cq == qp.send_cq) cq_run = scq.reserve(k - i);  // produce() used the ring
             }
             v.rnr_attempts = 0;
             v.rnr_next_ns = 0;
@@ -363,14 +388,15 @@ size_t CpuEngine::progress_qp(QpView &v) {
             stats_.bytes_moved += op_atomic(op) ? 8 : total;
             v.c.bytes += op_atomic(op) ? 8 : total;
         }
-        // The SQ slot is returned before the completion is visible: a client that sees the CQE
-        // may post into that slot at once (an HCA retires the WQE before it reports it).
-        qp.sq.peek(1);
-        qp.sq.release(1);
+        // The SQ slot is returned before the completion is visible (finish() releases first): a
+        // client that sees the CQE may post into that slot at once (an HCA retires the WQE before
+        // it reports it).
+        ++consumed;
         if (need_cqe) {
             queue::Cqe c{h.wr_id, status, wc_opcode(op), uint32_t(total), 0, qp.qpn, 0};
             if (status != UGDR_WC_SUCCESS) c.byte_length = 0;
-            produce(qp.send_cq, &c);
+            std::memcpy(cq_slot(ncqe), &c, sizeof(c));
+            ++ncqe;
         }
         ++retired;
         stats_.wrs_completed += 1;
@@ -379,10 +405,12 @@ size_t CpuEngine::progress_qp(QpView &v) {
             v.c.error_completions += 1;
             v.rnr_attempts = 0;
             v.rnr_next_ns = 0;
+            finish();
             enter_error(qp);
             return retired + progress_qp(v);  // flush what remains
         }
     }
+    finish();
     return retired;
 }
 
