@@ -474,7 +474,9 @@ namespace {
 // An engine that records the calls the control plane makes, for ordering checks.
 class RecordingEngine : public Engine {
   public:
-    RecordingEngine(std::vector<std::string> *log, std::string name) : log_(log), name_(std::move(name)) {}
+    RecordingEngine(std::vector<std::string> *log, std::string name, bool live = false)
+        : log_(log), name_(std::move(name)), live_(live) {}
+    bool detaches_live() const noexcept override { return live_; }
     DeviceInfo info() const override {
         DeviceInfo d;
         d.name = name_;
@@ -496,6 +498,7 @@ class RecordingEngine : public Engine {
   private:
     std::vector<std::string> *log_;
     std::string name_;
+    bool live_ = false;
 };
 
 }  // namespace
@@ -551,6 +554,66 @@ TEST(control_destroying_a_qp_stops_its_peers_engine_first) {
     log.clear();
     CHECK_EQ(call(kDestroyQp, qp[1]).status, 0);
     const std::vector<std::string> want = {"e1.quiesce", "e1.update_qp(" + std::to_string(qpn[0]) + ")",
+                                           "e2.detach_qp(" + std::to_string(qpn[1]) + ")", "e1.resume"};
+    CHECK(log == want);
+    if (log != want)
+        for (const std::string &l : log) std::fprintf(stderr, "    got %s\n", l.c_str());
+}
+
+TEST(control_live_detach_stops_only_other_engines_requesters) {
+    // QP b on engine 2 has two requesters: a on engine 1 and c on engine 2.  Both engines detach
+    // live.  Destroying b stops engine 1 only (its kernel is not covered by engine 2's idle
+    // point), unbinds a and c, and drops b from engine 2 without stopping engine 2.
+    std::vector<std::string> log;
+    RecordingEngine e1(&log, "e1", true), e2(&log, "e2", true);
+    HostBackend mem;
+    ControlPlane cp{{&e1, &e2}, mem};
+    auto call = [&](uint32_t method, uint64_t id, uint64_t length = 0, uint32_t access = 0,
+                    std::vector<std::byte> opaque = {}) {
+        Request r;
+        r.method = method;
+        r.identity = id;
+        r.length = length;
+        r.access = access;
+        r.opaque = std::move(opaque);
+        return cp.dispatch(1, std::move(r));
+    };
+    const int device_of[3] = {1, 2, 2};  // a, b, c
+    uint64_t qp[3];
+    uint32_t qpn[3];
+    for (int i = 0; i < 3; ++i) {
+        const uint64_t ctx = call(kCreateContext, uint64_t(device_of[i])).identity;
+        const uint64_t pd = call(kCreatePd, ctx).identity;
+        const uint64_t cq = call(kCreateCq, ctx, 16).identity;
+        std::vector<std::byte> o;
+        ByteWriter w(&o);
+        w.be(cq).be(cq).be(uint32_t(16)).be(uint32_t(16)).be(uint32_t(1)).be(uint32_t(1)).be(uint32_t(UGDR_QPT_RC));
+        w.be(uint32_t(0));
+        Response q = call(kCreateQp, pd, 0, 0, std::move(o));
+        CHECK_EQ(q.status, 0);
+        qp[i] = q.identity;
+        qpn[i] = qpn_of(q);
+        std::vector<std::byte> m;
+        ByteWriter mw(&m);
+        mw.be(uint32_t(UGDR_QPS_INIT)).be(uint32_t(0)).be(uint32_t(UGDR_ACCESS_REMOTE_WRITE));
+        mw.be(uint8_t(14)).be(uint8_t(7)).be(uint8_t(7)).be(uint8_t(12));
+        CHECK_EQ(call(kModifyQp, qp[i], 0, UGDR_QP_STATE | UGDR_QP_ACCESS_FLAGS, std::move(m)).status, 0);
+    }
+    const int target[3] = {1, 0, 1};  // a -> b, b -> a, c -> b
+    for (int i = 0; i < 3; ++i) {
+        std::vector<std::byte> o;
+        ByteWriter w(&o);
+        w.be(qpn[target[i]]).be(uint32_t(0)).be(uint32_t(0)).be(uint32_t(0)).be(uint8_t(14)).be(uint8_t(7));
+        w.be(uint8_t(7)).be(uint8_t(1));
+        CHECK_EQ(call(kConnectQp, qp[i], 0,
+                      UGDR_QP_TIMEOUT | UGDR_QP_RETRY_CNT | UGDR_QP_RNR_RETRY | UGDR_QP_MIN_RNR_TIMER, std::move(o))
+                     .status,
+                 0);
+    }
+    log.clear();
+    CHECK_EQ(call(kDestroyQp, qp[1]).status, 0);
+    const std::vector<std::string> want = {"e1.quiesce", "e1.update_qp(" + std::to_string(qpn[0]) + ")",
+                                           "e2.update_qp(" + std::to_string(qpn[2]) + ")",
                                            "e2.detach_qp(" + std::to_string(qpn[1]) + ")", "e1.resume"};
     CHECK(log == want);
     if (log != want)
