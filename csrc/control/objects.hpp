@@ -180,6 +180,13 @@ class Engine {
     // objects that only this engine's own execution may still touch (it keeps their memory
     // until it is not running).  The control plane then stops it only for peers on other engines.
     virtual bool detaches_live() const noexcept { return false; }
+    // Forget cached object views: the engine's execution reloads them before using any object
+    // again (a CQ slot of another engine may be reused later).  No wait.
+    virtual void invalidate_caches() noexcept {}
+    // Wait until everything running on this engine has seen the objects' current bindings and
+    // retired the WRs issued under the old ones.  False when that did not happen in time (or is
+    // not supported): the caller then stops the engine instead.
+    virtual bool settle() noexcept { return false; }
 
     virtual int stats(EngineStats *out, bool reset) = 0;
     // Device trace: keep up to `records_per_unit` events per execution unit from the next launch

@@ -347,6 +347,9 @@ Response ControlPlane::create_cq(uint64_t s, const Request &r) {
 void ControlPlane::erase_cq(uint64_t id) noexcept {
     Cq *cq = cqs_.find_any(id);
     if (cq == nullptr) return;
+    // Other engines' executors may cache this CQ (they produce receive completions into it).
+    for (Engine *e : engines_)
+        if (e != engines_[cq->device]) e->invalidate_caches();
     engines_[cq->device]->detach_cq(*cq);
     if (Context *ctx = contexts_.find_any(cq->context_id)) ctx->children -= 1;
     cqs_.erase(id);
@@ -431,13 +434,15 @@ void ControlPlane::erase_qp(uint64_t id) noexcept {
     // ring at this moment, so each is stopped before the binding changes and stays stopped until
     // this QP's rings are gone from its own engine.
     // An engine that detaches live keeps the QP's memory until it is not running, which covers
-    // its own requesters; requesters on other engines are stopped as before.
-    std::vector<Engine *> held;
+    // its own requesters.  Requesters on other live engines are unbound while they run, and
+    // their engine then settles (every QP re-reads its binding and retires what it issued under
+    // the old one); an engine that cannot settle in time, or does not detach live, is stopped.
+    std::vector<Engine *> held, settle;
     Engine *own = engines_[qp->device];
     qps_.for_each([&](uint64_t, uint64_t, Qp &other) {
         if (other.peer != qp) return;
         Engine *e = engines_[other.device];
-        const bool live = e == own && e->detaches_live();
+        const bool live = e->detaches_live();
         if (!live && std::find(held.begin(), held.end(), e) == held.end()) {
             e->quiesce();
             held.push_back(e);
@@ -445,7 +450,14 @@ void ControlPlane::erase_qp(uint64_t id) noexcept {
         other.peer = nullptr;
         other.peer_lost = true;
         e->update_qp(other);
+        if (live && e != own && std::find(settle.begin(), settle.end(), e) == settle.end()) settle.push_back(e);
     });
+    for (Engine *e : settle) {
+        if (!e->settle()) {
+            e->quiesce();
+            held.push_back(e);
+        }
+    }
     engines_[qp->device]->detach_qp(*qp);
     for (Engine *e : held) e->resume();
     qpn_index_.erase(qp->qpn);

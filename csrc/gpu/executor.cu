@@ -596,6 +596,7 @@ struct CqCache {
     uint32_t cap, stride;
     unsigned long long *ready;
     uint64_t reserve, head, published;
+    uint32_t epoch;  // MR epoch when filled: a CQ slot is reused only under a newer one
 };
 
 // A warp's private statistics, folded into DevStats now and then (hot shared counters would
@@ -621,6 +622,7 @@ struct Warp {
     // Cached view of the QP this warp serviced last (see service_qp).
     DevQp *vq;
     uint64_t vt, vhead, vissue, vtail, t_reserved;
+    uint32_t vepoch;  // MR epoch the view was read under: a newer epoch forces a re-read
     QpView *vv;  // cached view of the QP serviced last (shared memory)
     Tma *tma;    // this warp's TMA staging (null for the leader warp, which runs no chunks)
     volatile uint32_t *mr_epoch;  // the CTA's shared copy of DevStats::mr_epoch
@@ -668,8 +670,9 @@ __device__ bool wait_eq_sys(const unsigned long long *p, uint64_t want, uint64_t
 // CQ's configuration and its last view of the cursors, so an uncontended reservation is one CAS.
 __device__ uint32_t reserve_cq(Warp &w, DevCq *cq, uint32_t want, uint64_t *first) {
     CqCache &c = *w.cq;
-    if (c.cq != cq) {
+    if (c.cq != cq || c.epoch != w.epoch) {
         c.cq = cq;
+        c.epoch = w.epoch;
         c.cap = ld_vol32(&cq->cfg.capacity);
         c.stride = ld_vol32(&cq->cfg.stride);
         c.ring = reinterpret_cast<queue::RingHeader *>(ld_vol(&cq->cfg.ring));
@@ -1709,11 +1712,12 @@ __device__ uint32_t service_pass(Warp &w, DevQp *qp, uint8_t *wqe_smem, queue::C
                                  uint32_t *bitmap, uint32_t nwarps) {
     const uint64_t max_ns = w.p->max_wait_ns;
     // The configuration this pass needs: cached per warp for the QP it serviced last and re-read
-    // at least every 20 us (a host state change is seen within that; slots are only reused after
-    // the kernel was stopped, so a cache never outlives its QP).  The owner warp is the only
-    // writer of the QP's cursors, so the cached head / issue are authoritative.
+    // at least every 20 us, and at once under a new MR epoch: the host bumps the epoch and waits
+    // for every QP's next pass when a change must be seen by a deadline (a peer unbound before
+    // its QP goes away).  The owner warp is the only writer of the QP's cursors, so the cached
+    // head / issue are authoritative.
     const uint64_t now0 = gtime();
-    if (w.vq == qp && now0 - w.vt < 20000) {
+    if (w.vq == qp && now0 - w.vt < 20000 && w.vepoch == w.epoch) {
         return service_cached(w, qp, *w.vv, wqe_smem, cqe_smem, jr, bitmap, nwarps);
     }
     if (!ld_vol32(&qp->cfg.active)) {
@@ -1752,6 +1756,7 @@ __device__ uint32_t service_pass(Warp &w, DevQp *qp, uint8_t *wqe_smem, queue::C
     if (w.lane == 0) *w.vv = v;
     __syncwarp();
     w.vt = now0;
+    w.vepoch = w.epoch;
     return service_cached(w, qp, *w.vv, wqe_smem, cqe_smem, jr, bitmap, nwarps);
 }
 
@@ -2119,6 +2124,7 @@ __global__ void __launch_bounds__(kThreads, 1) executor_kernel(ExecParams p) {
     w.vv = &qp_view[w.wi];
     if (w.lane == 0) w.cq->cq = nullptr;
     w.vq = nullptr;
+    w.vepoch = 0;
     w.mrc = mr_cache[w.wi];
     w.mirror = s_bits;
     if (w.lane < 2) w.mrc[w.lane].key = 0;

@@ -65,6 +65,8 @@ class GpuEngine final : public control::Engine {
     void detach_qp(control::Qp &qp) noexcept override;
     void quiesce() override;
     bool detaches_live() const noexcept override { return true; }
+    void invalidate_caches() noexcept override;
+    bool settle() noexcept override;
     void resume() override;
     int stats(control::EngineStats *out, bool reset) override;
     int qp_counters(control::Qp &qp, control::QpCounters *out) override;
@@ -491,6 +493,17 @@ void GpuEngine::detach_qp(control::Qp &qp) noexcept {
         break;
     }
     qp.engine_block = nullptr;
+}
+
+void GpuEngine::invalidate_caches() noexcept {
+    std::lock_guard<std::mutex> lk(mu_);
+    mr_epoch_ += 1;  // every warp reloads its MR, QP-view and CQ caches at its next pass
+    copy_to_device(&stats_->mr_epoch, &mr_epoch_, sizeof(mr_epoch_));
+}
+
+bool GpuEngine::settle() noexcept {
+    std::lock_guard<std::mutex> lk(mu_);
+    return mr_grace_locked();
 }
 
 void GpuEngine::reap_locked() {

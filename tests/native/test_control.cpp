@@ -474,9 +474,13 @@ namespace {
 // An engine that records the calls the control plane makes, for ordering checks.
 class RecordingEngine : public Engine {
   public:
-    RecordingEngine(std::vector<std::string> *log, std::string name, bool live = false)
-        : log_(log), name_(std::move(name)), live_(live) {}
+    RecordingEngine(std::vector<std::string> *log, std::string name, bool live = false, bool settles = true)
+        : log_(log), name_(std::move(name)), live_(live), settles_(settles) {}
     bool detaches_live() const noexcept override { return live_; }
+    bool settle() noexcept override {
+        log_->push_back(name_ + ".settle");
+        return settles_;
+    }
     DeviceInfo info() const override {
         DeviceInfo d;
         d.name = name_;
@@ -498,7 +502,7 @@ class RecordingEngine : public Engine {
   private:
     std::vector<std::string> *log_;
     std::string name_;
-    bool live_ = false;
+    bool live_ = false, settles_ = true;
 };
 
 }  // namespace
@@ -560,12 +564,14 @@ TEST(control_destroying_a_qp_stops_its_peers_engine_first) {
         for (const std::string &l : log) std::fprintf(stderr, "    got %s\n", l.c_str());
 }
 
-TEST(control_live_detach_stops_only_other_engines_requesters) {
-    // QP b on engine 2 has two requesters: a on engine 1 and c on engine 2.  Both engines detach
-    // live.  Destroying b stops engine 1 only (its kernel is not covered by engine 2's idle
-    // point), unbinds a and c, and drops b from engine 2 without stopping engine 2.
+namespace {
+
+// QP b on engine 2 has two requesters: a on engine 1 and c on engine 2, and both engines detach
+// live.  Destroying b unbinds a and c while their engines run; engine 1 (whose kernel engine 2's
+// idle point does not cover) then settles, or is stopped when it cannot; engine 2 never stops.
+std::vector<std::string> destroy_shared_responder(bool e1_settles, uint32_t qpn_out[3]) {
     std::vector<std::string> log;
-    RecordingEngine e1(&log, "e1", true), e2(&log, "e2", true);
+    RecordingEngine e1(&log, "e1", true, e1_settles), e2(&log, "e2", true);
     HostBackend mem;
     ControlPlane cp{{&e1, &e2}, mem};
     auto call = [&](uint32_t method, uint64_t id, uint64_t length = 0, uint32_t access = 0,
@@ -612,9 +618,31 @@ TEST(control_live_detach_stops_only_other_engines_requesters) {
     }
     log.clear();
     CHECK_EQ(call(kDestroyQp, qp[1]).status, 0);
-    const std::vector<std::string> want = {"e1.quiesce", "e1.update_qp(" + std::to_string(qpn[0]) + ")",
-                                           "e2.update_qp(" + std::to_string(qpn[2]) + ")",
-                                           "e2.detach_qp(" + std::to_string(qpn[1]) + ")", "e1.resume"};
+    for (int i = 0; i < 3; ++i) qpn_out[i] = qpn[i];
+    std::vector<std::string> out = log;  // the teardown below logs more
+    return out;
+}
+
+}  // namespace
+
+TEST(control_live_detach_settles_other_engines_instead_of_stopping_them) {
+    uint32_t qpn[3];
+    const std::vector<std::string> log = destroy_shared_responder(true, qpn);
+    const std::vector<std::string> want = {"e1.update_qp(" + std::to_string(qpn[0]) + ")",
+                                           "e2.update_qp(" + std::to_string(qpn[2]) + ")", "e1.settle",
+                                           "e2.detach_qp(" + std::to_string(qpn[1]) + ")"};
+    CHECK(log == want);
+    if (log != want)
+        for (const std::string &l : log) std::fprintf(stderr, "    got %s\n", l.c_str());
+}
+
+TEST(control_live_detach_stops_an_engine_that_does_not_settle) {
+    uint32_t qpn[3];
+    const std::vector<std::string> log = destroy_shared_responder(false, qpn);
+    const std::vector<std::string> want = {"e1.update_qp(" + std::to_string(qpn[0]) + ")",
+                                           "e2.update_qp(" + std::to_string(qpn[2]) + ")", "e1.settle",
+                                           "e1.quiesce", "e2.detach_qp(" + std::to_string(qpn[1]) + ")",
+                                           "e1.resume"};
     CHECK(log == want);
     if (log != want)
         for (const std::string &l : log) std::fprintf(stderr, "    got %s\n", l.c_str());

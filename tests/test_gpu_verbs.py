@@ -432,6 +432,88 @@ def test_qp_and_cq_destruction_keeps_the_executor_running(gpu_env):
     ctx.close()
 
 
+def test_cross_gpu_qp_destruction_keeps_both_executors_running(gpu2_env):
+    """A cross-GPU pair (requester on GPU 0, responder on GPU 1, WRITE_WITH_IMM into GPU 1's RQ and
+    receive CQ) is created, used and destroyed six times while a GPU 0 loopback stream runs.  The
+    responder's destruction unbinds the GPU 0 requester while GPU 0's executor runs and waits for
+    its grace period: neither executor is stopped, and every byte and completion is right."""
+    V = gpu2_env
+    import gc
+
+    from ugdr_b200 import _native as N
+
+    gc.collect()
+    acc = _acc(N)
+    c0, c1 = V.Context(V.find_device(gpu=0)), V.Context(V.find_device(gpu=1))
+    p0, p1 = c0.alloc_pd(), c1.alloc_pd()
+    cq0 = c0.create_cq(1024)
+    a = p0.create_qp(cq0, max_send_wr=512)
+    b = p0.create_qp(cq0, max_send_wr=512)
+    V.connect_pair(a, b, access=N.ACCESS_REMOTE_WRITE | N.ACCESS_REMOTE_READ)
+    n = 64 << 20
+    src = torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda:0")
+    dst = torch.zeros(n, dtype=torch.uint8, device="cuda:0")
+    small = torch.randint(0, 256, (1 << 16,), dtype=torch.uint8, device="cuda:0")
+    far = torch.zeros(1 << 16, dtype=torch.uint8, device="cuda:1")
+    torch.cuda.synchronize(0)
+    torch.cuda.synchronize(1)
+    ms, md, ss = (p0.reg_mr(t.data_ptr(), t.numel(), acc) for t in (src, dst, small))
+    mf = p1.reg_mr(far.data_ptr(), far.numel(), acc)
+    a.post_write((src.data_ptr(), 4096, ms.lkey), dst.data_ptr(), md.rkey, wr_id=0)
+    assert cq0.wait(1, 60)[0].status == N.WC_SUCCESS  # GPU 0's executor is up
+    cqx, cqy = c0.create_cq(64), c1.create_cq(64)
+    x0 = p0.create_qp(cqx, max_send_wr=16)
+    y0 = p1.create_qp(cqy, max_send_wr=16)
+    V.connect_pair(x0, y0, access=N.ACCESS_REMOTE_WRITE)
+    y0.post_recv(wr_id=7)
+    x0.post_send(N.WR_RDMA_WRITE_WITH_IMM, [(small.data_ptr(), 4096, ss.lkey)], remote_addr=far.data_ptr(),
+                 rkey=mf.rkey, wr_id=7, imm=7)
+    assert cqx.wait(1, 60)[0].status == N.WC_SUCCESS and cqy.wait(1, 60)[0].status == N.WC_SUCCESS  # GPU 1's too
+    s0, s1 = c0.stats(), c1.stats()
+    chunk = 1 << 20
+    posted = done = cycles = 0
+    while done < 256:
+        while posted < 256 and posted - done < 64:
+            off = (posted % 64) * chunk
+            a.post_write((src.data_ptr() + off, chunk, ms.lkey), dst.data_ptr() + off, md.rkey, wr_id=posted)
+            posted += 1
+        if cycles < 6:
+            x = p0.create_qp(cqx, max_send_wr=16)
+            y = p1.create_qp(cqy, max_send_wr=16)
+            V.connect_pair(x, y, access=N.ACCESS_REMOTE_WRITE)
+            k = 4096 * (cycles + 1)
+            y.post_recv(wr_id=100 + cycles)
+            x.post_send(N.WR_RDMA_WRITE_WITH_IMM, [(small.data_ptr(), k, ss.lkey)], remote_addr=far.data_ptr(),
+                        rkey=mf.rkey, wr_id=100 + cycles, imm=cycles)
+            w = cqx.wait(1, 60)[0]
+            r = cqy.wait(1, 60)[0]
+            assert (w.wr_id, w.status) == (100 + cycles, N.WC_SUCCESS), w
+            assert (r.wr_id, r.status, r.imm_data, r.byte_len) == (100 + cycles, N.WC_SUCCESS, cycles, k), r
+            torch.cuda.synchronize(1)
+            assert torch.equal(far[:k].cpu(), small[:k].cpu())
+            y.destroy()  # the responder first: its GPU 0 requester is unbound live
+            x.destroy()
+            cycles += 1
+        wcs = cq0.wait(1, 60)
+        assert all(wc.status == N.WC_SUCCESS for wc in wcs)
+        done += len(wcs)
+    t0, t1 = c0.stats(), c1.stats()
+    torch.cuda.synchronize(0)
+    assert cycles == 6
+    assert torch.equal(dst, src)
+    assert (t0.launches, t1.launches) == (s0.launches, s1.launches), (s0.launches, t0.launches, s1.launches, t1.launches)
+    for q in (a, b, x0, y0):
+        q.destroy()
+    for m in (ms, md, ss, mf):
+        m.dereg()
+    for c in (cq0, cqx, cqy):
+        c.destroy()
+    p0.dealloc()
+    p1.dealloc()
+    c0.close()
+    c1.close()
+
+
 def test_kernel_attributes_report_every_kernel():
     """cudaFuncGetAttributes + occupancy for every kernel of the library: each fits its launch
     block size; the persistent executor keeps one 256-thread CTA (8 warps) per SM, whose register
