@@ -334,3 +334,17 @@ def test_multicast_mr_needs_a_gpu_context(cpu_daemon):
         os.close(w)
         pd.dealloc()
         ctx.close()
+
+
+def test_verbs_collectives_example_on_host_memory():
+    """examples/verbs_collectives.py runs end to end on the host-memory device (2 ranks, torchrun)."""
+    import subprocess
+    import sys
+
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                        "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+                        os.path.join(repo, "examples", "verbs_collectives.py"), "--cpu"],
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    assert "verbs collectives ok on 2 ranks (host memory)" in r.stdout
