@@ -12,6 +12,8 @@
 #include <unistd.h>
 
 #include <cstring>
+#include <map>
+#include <set>
 #include <memory>
 #include <mutex>
 #include <random>
@@ -646,4 +648,131 @@ TEST(control_live_detach_stops_an_engine_that_does_not_settle) {
     CHECK(log == want);
     if (log != want)
         for (const std::string &l : log) std::fprintf(stderr, "    got %s\n", l.c_str());
+}
+
+namespace {
+
+// An engine that checks, call by call, what the control plane asks of it during random
+// create / connect / destroy sequences: no call names a QP it already detached, stops and resumes
+// pair up, and when a QP is detached no QP still bound to it is left on any engine.
+struct Bindings {
+    std::map<uint32_t, uint32_t> peer_of;  // live QP -> the QPN it is bound to (0: none)
+    std::set<uint32_t> detached;
+    int violations = 0;
+};
+
+class CheckingEngine : public Engine {
+  public:
+    CheckingEngine(Bindings *b, bool live, bool settles) : b_(b), live_(live), settles_(settles) {}
+    DeviceInfo info() const override {
+        DeviceInfo d;
+        d.name = "checking";
+        d.kind = DeviceKind::gpu;
+        return d;
+    }
+    int attach_mr(Mr &) override { return 0; }
+    void detach_mr(Mr &) noexcept override {}
+    int attach_cq(Cq &) override { return 0; }
+    void detach_cq(Cq &) noexcept override {}
+    int attach_qp(Qp &q) override {
+        b_->peer_of[q.qpn] = 0;
+        return 0;
+    }
+    void update_qp(Qp &q) override {
+        if (b_->detached.count(q.qpn)) ++b_->violations;
+        b_->peer_of[q.qpn] = q.peer != nullptr ? q.peer->qpn : 0;
+    }
+    void detach_qp(Qp &q) noexcept override {
+        if (b_->detached.count(q.qpn)) ++b_->violations;
+        for (const auto &[qpn, peer] : b_->peer_of)
+            if (peer == q.qpn && qpn != q.qpn) ++b_->violations;  // a requester still bound to it
+        b_->peer_of.erase(q.qpn);
+        b_->detached.insert(q.qpn);
+    }
+    void quiesce() override { ++depth; }
+    void resume() override {
+        if (--depth < 0) ++b_->violations;
+    }
+    bool detaches_live() const noexcept override { return live_; }
+    bool settle() noexcept override { return settles_; }
+    int stats(EngineStats *, bool) override { return 0; }
+    int hold(bool) override { return 0; }
+    int depth = 0;
+
+  private:
+    Bindings *b_;
+    bool live_, settles_;
+};
+
+}  // namespace
+
+TEST(control_random_qp_lifecycles_never_leave_a_dangling_binding) {
+    for (uint32_t seed = 1; seed <= 40; ++seed) {
+        std::mt19937 rng(seed);
+        Bindings b;
+        CheckingEngine e1(&b, rng() % 2 == 0, rng() % 2 == 0), e2(&b, rng() % 2 == 0, rng() % 2 == 0);
+        HostBackend mem;
+        ControlPlane cp{{&e1, &e2}, mem};
+        auto call = [&](uint32_t method, uint64_t id, uint64_t length = 0, uint32_t access = 0,
+                        std::vector<std::byte> opaque = {}) {
+            Request r;
+            r.method = method;
+            r.identity = id;
+            r.length = length;
+            r.access = access;
+            r.opaque = std::move(opaque);
+            return cp.dispatch(1, std::move(r));
+        };
+        uint64_t pd[2], cq[2];
+        for (int d = 0; d < 2; ++d) {
+            const uint64_t ctx = call(kCreateContext, uint64_t(d + 1)).identity;
+            pd[d] = call(kCreatePd, ctx).identity;
+            cq[d] = call(kCreateCq, ctx, 64).identity;
+        }
+        struct Live {
+            uint64_t id;
+            uint32_t qpn;
+            bool connected;
+        };
+        std::vector<Live> qps;
+        for (int op = 0; op < 60; ++op) {
+            const uint32_t what = rng() % 3;
+            if (what == 0 || qps.size() < 2) {  // create (and move to INIT) on a random engine
+                const int d = int(rng() % 2);
+                std::vector<std::byte> o;
+                ByteWriter w(&o);
+                w.be(cq[d]).be(cq[d]).be(uint32_t(8)).be(uint32_t(8)).be(uint32_t(1)).be(uint32_t(1));
+                w.be(uint32_t(UGDR_QPT_RC)).be(uint32_t(0));
+                Response q = call(kCreateQp, pd[d], 0, 0, std::move(o));
+                CHECK_EQ(q.status, 0);
+                std::vector<std::byte> m;
+                ByteWriter mw(&m);
+                mw.be(uint32_t(UGDR_QPS_INIT)).be(uint32_t(0)).be(uint32_t(UGDR_ACCESS_REMOTE_WRITE));
+                mw.be(uint8_t(14)).be(uint8_t(7)).be(uint8_t(7)).be(uint8_t(12));
+                CHECK_EQ(call(kModifyQp, q.identity, 0, UGDR_QP_STATE | UGDR_QP_ACCESS_FLAGS, std::move(m)).status, 0);
+                qps.push_back({q.identity, qpn_of(q), false});
+            } else if (what == 1) {  // connect an unconnected QP to any live QP
+                Live &x = qps[rng() % qps.size()];
+                const Live &y = qps[rng() % qps.size()];
+                if (x.connected) continue;
+                std::vector<std::byte> o;
+                ByteWriter w(&o);
+                w.be(y.qpn).be(uint32_t(0)).be(uint32_t(0)).be(uint32_t(0)).be(uint8_t(14)).be(uint8_t(7));
+                w.be(uint8_t(7)).be(uint8_t(1));
+                const int rc = call(kConnectQp, x.id, 0,
+                                    UGDR_QP_TIMEOUT | UGDR_QP_RETRY_CNT | UGDR_QP_RNR_RETRY | UGDR_QP_MIN_RNR_TIMER,
+                                    std::move(o))
+                                   .status;
+                if (rc == 0) x.connected = true;
+            } else {  // destroy a random QP
+                const size_t i = rng() % qps.size();
+                CHECK_EQ(call(kDestroyQp, qps[i].id).status, 0);
+                qps.erase(qps.begin() + long(i));
+            }
+            CHECK_EQ(e1.depth, 0);
+            CHECK_EQ(e2.depth, 0);
+        }
+        CHECK_EQ(b.violations, 0);
+        if (b.violations != 0) std::fprintf(stderr, "    seed %u: %d violations\n", seed, b.violations);
+    }
 }
