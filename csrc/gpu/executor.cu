@@ -8,16 +8,16 @@
 // reference's kernel is one CTA fed 8 KiB copy tasks by a host thread; here the host is off the
 // data path entirely:
 //
-//  * Ownership.  QP slot q belongs to exactly one warp of the grid (CTA q % grid, warp
-//    (q / grid) % warps), so each QP's WRs are fetched, validated and retired in posting order by
-//    one warp, and QPs spread over all SMs.
-//  * Issue.  The owner warp reads up to 16 WQEs (host-mapped ring) lane-parallel into shared
-//    memory.  Single-SGE WRITE / READ are validated lane-parallel (lane j checks WQE j against
-//    the device MR table); payloads up to 64 B are copied by their lane, larger ones become one
-//    chunked job for the whole batch.  Other WRs (multi-SGE, WRITE_WITH_IMM, atomics) are staged
-//    one per round and run inline (<= 4 KiB, atomics) or as a one-WR job.  Any warp of the GPU
-//    claims job chunks with a fetch-and-add on the job's counter, so one large WR spreads over
-//    every SM.
+//  * Ownership.  QP slot q belongs to exactly one warp of the grid (CTA q % grid, owner rank
+//    (q / grid) % warps, the CTA's leader warp ranked last; see owner_rank), so each QP's WRs are
+//    fetched, validated and retired in posting order by one warp, and QPs spread over all SMs.
+//  * Issue.  The owner warp reads up to 32 WQEs (host-mapped ring) lane-parallel into shared
+//    memory, with up to 64 WRs of a QP in flight (two batches).  Single-SGE WRITE / READ are
+//    validated lane-parallel (lane j checks WQE j against the device MR table); payloads up to
+//    64 B are copied by their lane, larger ones become one chunked job for the whole batch.
+//    Other WRs (multi-SGE, WRITE_WITH_IMM, atomics) are staged one after another and run inline
+//    (<= 4 KiB, atomics) or join the pass's job.  Any warp of the GPU claims job chunks with a
+//    fetch-and-add on the job's counter, so one large WR spreads over every SM.
 //  * Retire.  When all chunks of the oldest in-flight WRs are done the owner produces the
 //    receive CQEs (WRITE_WITH_IMM), the send CQEs (signaled or error) and advances the ring
 //    head.  CQs are multi-producer (several warps, several GPUs): slots are reserved by CAS and
