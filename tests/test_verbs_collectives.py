@@ -124,6 +124,9 @@ def _moe_inputs(rank: int, T: int, H: int, K: int, E: int, call: int, dev):
     g = torch.Generator().manual_seed(10_000 * call + 10 + rank)
     x = torch.randn(T, H, generator=g).to(torch.bfloat16)
     ids, w = route(T, E, K, seed=10_000 * call + 20 + rank, device="cpu")
+    if call >= 2:  # skewed: every token picks among K experts only, so most expert groups are empty
+        allowed = torch.tensor([e * E // K for e in range(K - 1)] + [E - 1], dtype=torch.int32)
+        ids = allowed[torch.argsort(torch.rand(T, K, generator=g), dim=1)]
     return x.to(dev), ids.to(dev), w.to(dev)
 
 
@@ -224,8 +227,9 @@ def _run_moe(world: int, gpu: bool, shape: tuple, calls: int) -> None:
 @pytest.mark.parametrize("world,shape", [(2, (64, 64, 4, 8)), (3, (50, 32, 2, 6))])
 def test_verbs_moe_exact_permutation_on_the_host_engine(world, shape):
     """Every owner's receive area equals, row for row, the expected expert-grouped permutation of
-    every rank's tokens; combine reads every row back to its (token, k) slot and weights it."""
-    _run_moe(world, False, shape, calls=2)
+    every rank's tokens; combine reads every row back to its (token, k) slot and weights it.
+    Calls 2 and 3 route to a few experts only (most groups empty), packed and gathered."""
+    _run_moe(world, False, shape, calls=4)
 
 
 @pytest.mark.gpu
