@@ -352,3 +352,15 @@ def test_verbs_collectives_example_on_host_memory():
                        capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
     assert "verbs collectives ok on 2 ranks (host memory)" in r.stdout
+
+
+def test_packed_dispatch_and_pack_reject_missing_arguments():
+    """The packed dispatch refuses a missing group, descriptor or count table (EINVAL) and the
+    pack refuses missing pointers (cudaErrorInvalidValue) before touching any device."""
+    import errno
+
+    from ugdr_b200.parallel.verbs_collectives import _moe_lib
+
+    L = _moe_lib()
+    assert L.ugdr_x_verbs_moe_dispatch_packed(None, None, None, 0) == errno.EINVAL
+    assert L.ugdr_x_moe_pack_grouped(None, None, None, None, None, 16, 2, 32, 0, None) == 1
